@@ -1,0 +1,143 @@
+/*
+ * libstrata_cuda — B200 (sm_100a) backend for StrataCuda's mixture-of-experts path.
+ *
+ * A C ABI (plain pointers, sizes and opaque 64-bit buffer handles; no CUDA or torch types)
+ * that a host language binds through its FFI. It replaces the reference's backend object
+ * protocol (src/backend.js:58-206: kind, alloc, write, read, copy, zero, run, free, idle,
+ * flush, info, dispose) with one context per device, and adds fused entry points for the
+ * whole MoE layer so that no routing result crosses to the host.
+ *
+ * Conventions
+ *  - Every call returns a status (STRATA_OK = 0). The message of the last failure on a
+ *    context is available from strata_last_error().
+ *  - Buffers hold 4-byte elements (src/backend.js:84-92, 128-134): lengths and offsets are
+ *    counted in elements, never bytes.
+ *  - Calls on one context are stream-ordered and asynchronous; strata_read and strata_idle
+ *    synchronise (src/backend.js:94, 117). One thread drives a context at a time.
+ *  - Host memory passed in is borrowed only for the duration of the call.
+ *  - Kernels never fault on bad indices: a data-dependent index outside its buffer is
+ *    skipped and recorded, and the next synchronising call returns STRATA_ERR_DEVICE.
+ */
+#ifndef STRATA_CUDA_H
+#define STRATA_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define STRATA_OK 0
+#define STRATA_ERR_RANGE 1   /* argument outside the supported range: RangeError, src/backend.js:6-9 */
+#define STRATA_ERR_LAYOUT 2  /* buffer/shape layout violated: Error, src/backend.js:22-36 */
+#define STRATA_ERR_UNKNOWN 3 /* unknown kernel or missing argument: src/backend.js:102; wasm/runtime.js:12 */
+#define STRATA_ERR_HANDLE 4  /* not a live buffer of this context: src/backend.js:138-143 */
+#define STRATA_ERR_ALLOC 5   /* device allocation failed: wasm/runtime.js:7 "WASM allocation failed" */
+#define STRATA_ERR_CUDA 6    /* CUDA runtime error (the message names it) */
+#define STRATA_ERR_DEVICE 7  /* a kernel recorded an out-of-range index, an invalid routing or a timed-out wait */
+
+#define STRATA_F32 0
+#define STRATA_I32 1
+#define STRATA_U32 2
+
+#define STRATA_ARG_BUF 0
+#define STRATA_ARG_I32 1
+#define STRATA_ARG_F32 2
+
+typedef struct strata_ctx strata_ctx;
+typedef uint64_t strata_buf; /* opaque; 0 is never a valid handle */
+
+/* One named argument of strata_run: the reference passes buffers and numbers in one object
+ * keyed by the kernel's parameter names (src/backend.js:101-113). */
+typedef struct {
+    const char *name;
+    int32_t kind; /* STRATA_ARG_* */
+    int32_t i32;
+    float f32;
+    strata_buf buf;
+} strata_arg;
+
+/* ---- context (GpuBackend.create / dispose, src/backend.js:59-71, 121) ---- */
+int strata_create(int device, strata_ctx **out);
+int strata_destroy(strata_ctx *ctx);
+/* Copies the last error message (NUL-terminated, truncated to cap). Returns its full length. */
+int strata_last_error(strata_ctx *ctx, char *buf, size_t cap);
+/* The CUDA stream the context issues work on (a cudaStream_t, as an opaque pointer). */
+int strata_stream(strata_ctx *ctx, void **stream);
+
+/* ---- buffers (src/backend.js:84-100, 114-118) ---- */
+/* alloc(length, type, {zero}); length in 4-byte elements, >= 1. */
+int strata_alloc(strata_ctx *ctx, uint64_t length, int type, int zero, strata_buf *out);
+int strata_free(strata_ctx *ctx, strata_buf buf);
+/* write(buffer, data, offset): count elements from host memory at element offset. */
+int strata_write(strata_ctx *ctx, strata_buf buf, const void *data, uint64_t count, uint64_t offset);
+/* read(buffer): count elements from element offset into host memory; synchronises. */
+int strata_read(strata_ctx *ctx, strata_buf buf, void *out, uint64_t count, uint64_t offset);
+/* copy(source, destination, count, sourceOffset, destinationOffset), stream-ordered. */
+int strata_copy(strata_ctx *ctx, strata_buf src, strata_buf dst, uint64_t count, uint64_t src_offset, uint64_t dst_offset);
+/* zero(buffer), stream-ordered (src/backend.js:93). */
+int strata_zero(strata_ctx *ctx, strata_buf buf);
+/* Length (elements), type and device address of a live buffer. */
+int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *type, void **device_ptr);
+
+/* ---- dispatch (run, src/backend.js:101-113; validateDispatch :10-56) ----
+ * Runs one reference entry of kernels/strata.cu by name with the reference's grid of 64-lane
+ * workgroups. Supported names: strata_unpack_half, strata_expert_scales, strata_q2_gate_up,
+ * strata_q2_down, strata_project, strata_bf16_project, strata_q2_project, strata_quant_project,
+ * strata_elementwise, strata_router, strata_router_batch, strata_moe_combine,
+ * strata_moe_combine_batch, strata_gather_rows, strata_scatter_rows. Results are bit-identical
+ * to the reference's F32 CPU path. */
+int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int nargs, const uint32_t groups[3]);
+
+/* ---- synchronisation and introspection (idle, flush, info: src/backend.js:119-120) ---- */
+int strata_idle(strata_ctx *ctx);
+int strata_flush(strata_ctx *ctx);
+/* JSON object: device, SMs, bytes resident, buffers, dispatches, fused calls. */
+int strata_info(strata_ctx *ctx, char *json, size_t cap);
+
+/* ---- fused mixture-of-experts layer ----
+ * One layer's weights, as resident buffers. The routed experts are the layer's slice of
+ * experts.bin: `experts` consecutive Q2 blobs (vendor/strata/tools/pack_layer.py:54-65 with
+ * H = width, FF = ff: gate/up codes with rows interleaved g0,u0,g1,..., down codes,
+ * gate/up FP16 scales, down FP16 scales; 3*ff*width*9/32 bytes per blob), read by
+ * src/model.js:160-167. Replaces the per-layer sequence of src/engine.js:133-156 (decode)
+ * and src/prefill.js:52-78 (prompt batches). */
+typedef struct {
+    int32_t width;           /* hidden size H; multiple of 64 */
+    int32_t ff;              /* expert intermediate size; multiple of 64 */
+    int32_t experts;         /* 1..512 */
+    int32_t top_k;           /* 1..min(experts, 32) */
+    strata_buf router;       /* f32 [experts * width]: blk.L.ffn_gate_inp.weight, row-major */
+    strata_buf router_bias;  /* 0, or f32 [experts] added to the logits (strata_elementwise mode 5) */
+    strata_buf experts_blob; /* u32 [experts * blob_bytes / 4] */
+    strata_buf shared_blob;  /* u32 [blob_bytes / 4]: the shared expert as one Q2 blob */
+    strata_buf shared_gate;  /* f32 [width]: blk.L.ffn_gate_inp_shexp.weight */
+} strata_moe_layer;
+
+/* Whole layer for `tokens` rows of x (f32 [tokens * width]) into y (f32 [tokens * width]),
+ * routed ids (i32 [tokens * top_k]) and weights (f32 [tokens * top_k]). Routing is
+ * bit-identical to strata_router_batch; y follows the reference's combine order.
+ *   mode 0: exact — every dot product in the reference's reduction order (bit-identical y).
+ * Stream-ordered; does not synchronise. */
+#define STRATA_MOE_EXACT 0
+int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
+                       strata_buf weights, int32_t mode);
+
+/* ---- seeded synthetic workload (device generator; same bytes as stratacuda_b200/synth.py) ---- */
+/* `count` expert blobs of one layer starting at `first_expert` into buf at element offset. */
+int strata_synth_blobs(strata_ctx *ctx, strata_buf buf, uint64_t offset, uint64_t seed, int32_t layer, int32_t first_expert,
+                       int32_t count, int32_t width, int32_t ff, int32_t shared);
+/* `count` normals N(0,1)*scale of stream (seed, tag, sub) from draw `start` into buf at offset. */
+int strata_synth_normals(strata_ctx *ctx, strata_buf buf, uint64_t offset, uint64_t seed, uint64_t tag, uint64_t sub, uint64_t start,
+                         uint64_t count, double scale);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,392 @@
+/*
+ * TEST INFRASTRUCTURE (oracle). A CPU restatement of the reference's mixture-of-experts
+ * kernels, used only by tests/, bench.py's cpu_baseline / --impl reference legs and
+ * __graft_entry__.smoke() as the checker. The product never links or calls it.
+ *
+ * Every entry keeps the reference's workgroup semantics (kernels/strata.cu:3: 64 lanes per
+ * workgroup, lane-strided F32 accumulation, then a shared-memory tree s = 32..1) and its
+ * dispatch convention: a grid (gx, gy, gz) of workgroups followed by the kernel's own
+ * parameters, exactly as vendor/webcuda/src/wasm/compile.mjs:39 wraps each entry as
+ * cw_<entry>(gx, gy, gz, params...). Arithmetic is F32 with no contraction (build with
+ * -ffp-contract=off), so results are bit-identical to the reference's CPU path whenever
+ * the same expf is used (strata_expf.h).
+ *
+ * Return value: 0, like cw_parallel (thread-pool.hpp:61) when no barrier diverged.
+ */
+#include <stdint.h>
+#include <string.h>
+#include <math.h>
+#include <stdlib.h>
+#include "strata_expf.h"
+
+#define LANES 64
+
+/* kernels/strata.cu:7-8 */
+static inline float o_sigmoid(float x) { return 1.0f / (1.0f + strata_oracle_expf(-x)); }
+static inline float o_silu(float x) { return x * o_sigmoid(x); }
+
+/* kernels/strata.cu:9-12 */
+static inline int o_group(int index, int size) {
+    if (size == 16) return index >> 4;
+    if (size == 32) return index >> 5;
+    if (size == 64) return index >> 6;
+    return index / size;
+}
+
+/* kernels/strata.cu:13-18 — FP16 bits to float, subnormals by a multiply with 2^-24. */
+float oracle_half_bits(unsigned int h) {
+    unsigned int sign = (h & 32768u) << 16;
+    unsigned int exponent = (h >> 10) & 31u;
+    unsigned int fraction = h & 1023u;
+    if (exponent == 0u) {
+        if (fraction == 0u) return strata_o_u2f(sign);
+        float v = (float)fraction * 0.000000059604644775390625f;
+        return sign != 0u ? -v : v;
+    }
+    if (exponent == 31u) return strata_o_u2f(sign | 2139095040u | (fraction << 13));
+    return strata_o_u2f(sign | ((exponent + 112u) << 23) | (fraction << 13));
+}
+
+/* kernels/strata.cu:22-31 */
+static float o_iq4(int c) {
+    static const float t[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+    return (c >= 0 && c < 15) ? t[c] : 113.0f;
+}
+
+float oracle_expf(float x) { return strata_oracle_expf(x); }
+
+/* The reference's reduction: partial[lane] += partial[lane + s] for s = 32..1. */
+static float tree_sum(float *p) {
+    for (int s = 32; s > 0; s >>= 1)
+        for (int l = 0; l < s; ++l) p[l] += p[l + s];
+    return p[0];
+}
+
+static inline float half_at(const unsigned int *words, int halfIndex) {
+    return oracle_half_bits((words[halfIndex / 2] >> ((halfIndex % 2) * 16)) & 65535u);
+}
+static inline int code_at(const unsigned int *words, int codeOffset, int index) {
+    return (int)((words[codeOffset + index / 16] >> ((index % 16) * 2)) & 3u) - 1;
+}
+
+/* kernels/strata.cu:19-21 */
+int oracle_strata_unpack_half(unsigned gx, unsigned gy, unsigned gz, const unsigned int *Packed, float *Values, int count) {
+    (void)gy; (void)gz; /* blockIdx.y/z do not enter i: extra workgroups rewrite the same values */
+    for (long i = 0; i < (long)gx * LANES && i < count; ++i) Values[i] = half_at(Packed, (int)i);
+    return 0;
+}
+
+/* kernels/strata.cu:35-37 */
+int oracle_strata_expert_scales(unsigned gx, unsigned gy, unsigned gz, const unsigned int *Blob, float *Scales, int offset, int count) {
+    (void)gy; (void)gz;
+    for (long i = 0; i < (long)gx * LANES; ++i)
+        if (i < count) { int at = offset + (int)i; Scales[i] = half_at(Blob, at); }
+    return 0;
+}
+
+/* kernels/strata.cu:38-55 — fused gate/up/SiLU over interleaved rows 2r (gate), 2r+1 (up). */
+int oracle_strata_q2_gate_up(unsigned gx, unsigned gy, unsigned gz, const float *X, const unsigned int *Blob, const float *Scales,
+                             const int *Mapping, float *Hidden, int width, int ff, int tokens, int mapped, int expanded,
+                             int codeOffset, int scaleOffset) {
+    (void)gz;
+    float gate[LANES], up[LANES];
+    for (unsigned token = 0; token < gy; ++token)
+        for (unsigned row = 0; row < gx; ++row) {
+            if (!((int)row < ff && (int)token < tokens)) continue;
+            int inputRow = mapped != 0 ? Mapping[2 * token] : (int)token;
+            for (int lane = 0; lane < LANES; ++lane) {
+                float g = 0.0f, u = 0.0f;
+                for (int i = lane; i < width; i += LANES) {
+                    int gi = (int)row * 2 * width + i, ui = gi + width;
+                    int gc = code_at(Blob, codeOffset, gi), uc = code_at(Blob, codeOffset, ui);
+                    int gs = scaleOffset + gi / 64, us = scaleOffset + ui / 64;
+                    float gw = (float)gc * (expanded != 0 ? Scales[gs] : half_at(Blob, gs));
+                    float uw = (float)uc * (expanded != 0 ? Scales[us] : half_at(Blob, us));
+                    float x = X[inputRow * width + i];
+                    g += gw * x; u += uw * x;
+                }
+                gate[lane] = g; up[lane] = u;
+            }
+            for (int s = 32; s > 0; s >>= 1)
+                for (int l = 0; l < s; ++l) { gate[l] += gate[l + s]; up[l] += up[l + s]; }
+            Hidden[token * ff + row] = o_silu(gate[0]) * up[0];
+        }
+    return 0;
+}
+
+/* kernels/strata.cu:56-69 — down projection scattered to Y[outputOffset + Mapping[2t+1]*width + row]. */
+int oracle_strata_q2_down(unsigned gx, unsigned gy, unsigned gz, const float *Hidden, const unsigned int *Blob, const float *Scales,
+                          const int *Mapping, float *Y, int width, int ff, int tokens, int mapped, int expanded, int outputOffset,
+                          int codeOffset, int scaleOffset) {
+    (void)gz;
+    float partial[LANES];
+    for (unsigned token = 0; token < gy; ++token)
+        for (unsigned row = 0; row < gx; ++row) {
+            if (!((int)row < width && (int)token < tokens)) continue;
+            for (int lane = 0; lane < LANES; ++lane) {
+                float sum = 0.0f;
+                for (int i = lane; i < ff; i += LANES) {
+                    int index = (int)row * ff + i;
+                    int code = code_at(Blob, codeOffset, index);
+                    int si = scaleOffset + index / 64;
+                    float w = (float)code * (expanded != 0 ? Scales[si] : half_at(Blob, si));
+                    sum += w * Hidden[token * ff + i];
+                }
+                partial[lane] = sum;
+            }
+            float r = tree_sum(partial);
+            int destination = mapped != 0 ? Mapping[2 * token + 1] : (int)token;
+            Y[outputOffset + destination * width + row] = r;
+        }
+    return 0;
+}
+
+/* kernels/strata.cu:156-165 — F32 projection (router logits, shared-expert gate logit). */
+int oracle_strata_project(unsigned gx, unsigned gy, unsigned gz, const float *X, const float *W, float *Y, int cols, int rows,
+                          int tokens, int outputStride, int outputOffset) {
+    (void)gz;
+    float partial[LANES];
+    for (unsigned token = 0; token < gy; ++token)
+        for (unsigned row = 0; row < gx; ++row) {
+            if (!((int)row < rows && (int)token < tokens)) continue;
+            for (int lane = 0; lane < LANES; ++lane) {
+                float sum = 0.0f;
+                for (int i = lane; i < cols; i += LANES) sum += W[(long)row * cols + i] * X[(long)token * cols + i];
+                partial[lane] = sum;
+            }
+            Y[(long)token * outputStride + outputOffset + row] = tree_sum(partial);
+        }
+    return 0;
+}
+
+/* kernels/strata.cu:168-176 — BF16 weight words, F32 math. */
+int oracle_strata_bf16_project(unsigned gx, unsigned gy, unsigned gz, const float *X, const unsigned int *Codes, float *Y, int cols,
+                               int rows, int tokens, int outputStride, int outputOffset) {
+    (void)gz;
+    float partial[LANES];
+    for (unsigned token = 0; token < gy; ++token)
+        for (unsigned row = 0; row < gx; ++row) {
+            if (!((int)row < rows && (int)token < tokens)) continue;
+            for (int lane = 0; lane < LANES; ++lane) {
+                float sum = 0.0f;
+                for (int i = lane; i < cols; i += LANES) {
+                    int ix = (int)row * cols + i;
+                    unsigned int bits = (Codes[ix / 2] >> ((ix % 2) * 16)) & 65535u;
+                    sum += strata_o_u2f(bits << 16) * X[token * cols + i];
+                }
+                partial[lane] = sum;
+            }
+            Y[token * outputStride + outputOffset + row] = tree_sum(partial);
+        }
+    return 0;
+}
+
+/* kernels/strata.cu:179-192 — one role of a resident Q2 blob (weightRow, rowStride 1 or 2). */
+int oracle_strata_q2_project(unsigned gx, unsigned gy, unsigned gz, const float *X, const unsigned int *Blob, float *Y, int cols, int rows,
+                             int tokens, int outputStride, int outputOffset, int codeOffset, int scaleOffset, int weightRow,
+                             int rowStride) {
+    (void)gz;
+    float partial[LANES];
+    for (unsigned token = 0; token < gy; ++token)
+        for (unsigned row = 0; row < gx; ++row) {
+            if (!((int)row < rows && (int)token < tokens)) continue;
+            for (int lane = 0; lane < LANES; ++lane) {
+                float sum = 0.0f;
+                for (int i = lane; i < cols; i += LANES) {
+                    int ix = (weightRow + (int)row * rowStride) * cols + i;
+                    int code = code_at(Blob, codeOffset, ix);
+                    int si = scaleOffset + ix / 64;
+                    float weight = (float)code * half_at(Blob, si);
+                    sum += weight * X[token * cols + i];
+                }
+                partial[lane] = sum;
+            }
+            Y[token * outputStride + outputOffset + row] = tree_sum(partial);
+        }
+    return 0;
+}
+
+/* kernels/strata.cu:193-211 — generic S2/S4/S8 projection; the WASM expert path (bits 2, group 64, bias -1). */
+int oracle_strata_quant_project(unsigned gx, unsigned gy, unsigned gz, const float *X, const unsigned int *Codes, const float *Scales,
+                                const float *Offsets, float *Y, int cols, int rows, int tokens, int outputStride, int outputOffset,
+                                int bits, int groupSize, int bias, int codebook, int hasOffset) {
+    (void)gz;
+    float partial[LANES];
+    for (unsigned token = 0; token < gy; ++token)
+        for (unsigned row = 0; row < gx; ++row) {
+            if (!((int)row < rows && (int)token < tokens)) continue;
+            for (int lane = 0; lane < LANES; ++lane) {
+                float sum = 0.0f;
+                for (int i = lane; i < cols; i += LANES) {
+                    int index = (int)row * cols + i, bit = index * bits;
+                    int code = (int)((Codes[bit / 32] >> (bit % 32)) & ((1u << bits) - 1u));
+                    float value = codebook == 1 ? o_iq4(code) : (float)(code + bias);
+                    int group = o_group(index, groupSize);
+                    float weight = value * Scales[group];
+                    if (hasOffset != 0) weight += Offsets[group];
+                    sum += weight * X[token * cols + i];
+                }
+                partial[lane] = sum;
+            }
+            Y[token * outputStride + outputOffset + row] = tree_sum(partial);
+        }
+    return 0;
+}
+
+/* kernels/strata.cu:229-236 — 0 copy/scale; 1 SiLU; 2 sigmoid; 3 SiLU(A)*B; 4 A*sigmoid(B); 5 add. */
+int oracle_strata_elementwise(unsigned gx, unsigned gy, unsigned gz, const float *A, const float *B, float *Y, int n, int mode, float scale) {
+    (void)gy; (void)gz;
+    for (long i = 0; i < (long)gx * LANES && i < n; ++i) {
+        float a = A[i] * scale, v = a;
+        if (mode == 1) v = o_silu(a);
+        if (mode == 2) v = o_sigmoid(a);
+        if (mode == 3) v = o_silu(a) * B[i];
+        if (mode == 4) v = a * o_sigmoid(B[i]);
+        if (mode == 5) v = a + B[i];
+        Y[i] = v;
+    }
+    return 0;
+}
+
+/* kernels/strata.cu:238-270 (router) and :478-509 (router_batch): softmax over all experts,
+ * k rounds of lane-strided argmax with lower-ID tie-break, weights sel/max(sum, 2^-14). */
+static void router_token(const float *Logits, int *Ids, float *Weights, int experts, int topK) {
+    float prob[512], reduce[LANES], selected[32];
+    int winner[LANES];
+    for (int lane = 0; lane < LANES; ++lane) {
+        float mx = -3.402823e38f;
+        for (int e = lane; e < experts; e += LANES) mx = fmaxf(mx, Logits[e]);
+        reduce[lane] = mx;
+    }
+    for (int s = 32; s > 0; s >>= 1)
+        for (int l = 0; l < s; ++l) reduce[l] = fmaxf(reduce[l], reduce[l + s]);
+    float mx = reduce[0];
+    for (int lane = 0; lane < LANES; ++lane) {
+        float sum = 0.0f;
+        for (int e = lane; e < experts; e += LANES) { prob[e] = strata_oracle_expf(Logits[e] - mx); sum += prob[e]; }
+        reduce[lane] = sum;
+    }
+    float inv = 1.0f / tree_sum(reduce);
+    for (int e = 0; e < experts; ++e) prob[e] *= inv;
+    for (int k = 0; k < topK; ++k) {
+        for (int lane = 0; lane < LANES; ++lane) {
+            float best = -1.0f; int id = experts;
+            for (int e = lane; e < experts; e += LANES)
+                if (prob[e] > best || (prob[e] == best && e < id)) { best = prob[e]; id = e; }
+            reduce[lane] = best; winner[lane] = id;
+        }
+        for (int s = 32; s > 0; s >>= 1)
+            for (int l = 0; l < s; ++l) {
+                float v = reduce[l + s]; int j = winner[l + s];
+                if (v > reduce[l] || (v == reduce[l] && j < winner[l])) { reduce[l] = v; winner[l] = j; }
+            }
+        Ids[k] = winner[0]; selected[k] = reduce[0]; prob[winner[0]] = -1.0f;
+    }
+    float denom = 0.0f;
+    for (int k = 0; k < topK; ++k) denom += selected[k];
+    denom = fmaxf(denom, 0.00006103515625f);
+    for (int k = 0; k < topK; ++k) Weights[k] = selected[k] / denom;
+}
+
+int oracle_strata_router(unsigned gx, unsigned gy, unsigned gz, const float *Logits, int *Ids, float *Weights, int experts, int topK) {
+    (void)gx; (void)gy; (void)gz;
+    router_token(Logits, Ids, Weights, experts, topK);
+    return 0;
+}
+
+int oracle_strata_router_batch(unsigned gx, unsigned gy, unsigned gz, const float *Logits, int *Ids, float *Weights, int experts, int topK) {
+    (void)gy; (void)gz;
+    for (unsigned t = 0; t < gx; ++t)
+        router_token(Logits + (long)t * experts, Ids + (long)t * topK, Weights + (long)t * topK, experts, topK);
+    return 0;
+}
+
+/* kernels/strata.cu:360-365 — y = shared*sigmoid(sg) + sum_k parts[k]*w[k], in this order. */
+int oracle_strata_moe_combine(unsigned gx, unsigned gy, unsigned gz, const float *Parts, const float *Weights, const float *Shared,
+                              const float *SharedGate, float *Y, int width, int count) {
+    (void)gy; (void)gz;
+    for (long i = 0; i < (long)gx * LANES && i < width; ++i) {
+        float value = Shared[i] * o_sigmoid(SharedGate[0]);
+        for (int k = 0; k < count; ++k) value += Parts[k * width + i] * Weights[k];
+        Y[i] = value;
+    }
+    return 0;
+}
+
+/* kernels/strata.cu:470-476 */
+int oracle_strata_moe_combine_batch(unsigned gx, unsigned gy, unsigned gz, const float *Parts, const float *Weights, const float *Shared,
+                                    const float *SharedGate, float *Y, int width, int count, int tokens) {
+    (void)gy; (void)gz;
+    for (long i = 0; i < (long)gx * LANES && i < (long)width * tokens; ++i) {
+        int token = (int)(i / width), d = (int)(i % width);
+        float value = Shared[i] * o_sigmoid(SharedGate[token]);
+        for (int k = 0; k < count; ++k) value += Parts[(long)(token * count + k) * width + d] * Weights[token * count + k];
+        Y[i] = value;
+    }
+    return 0;
+}
+
+/* kernels/strata.cu:464-469 */
+int oracle_strata_gather_rows(unsigned gx, unsigned gy, unsigned gz, const float *X, const int *Indices, float *Y, int width, int rows) {
+    (void)gy; (void)gz;
+    for (long i = 0; i < (long)gx * LANES && i < (long)width * rows; ++i) Y[i] = X[(long)Indices[i / width] * width + i % width];
+    return 0;
+}
+int oracle_strata_scatter_rows(unsigned gx, unsigned gy, unsigned gz, const float *X, const int *Indices, float *Y, int width, int rows) {
+    (void)gy; (void)gz;
+    for (long i = 0; i < (long)gx * LANES && i < (long)width * rows; ++i) Y[(long)Indices[i / width] * width + i % width] = X[i];
+    return 0;
+}
+
+/* ---------------------------------------------------------------------------------------
+ * One MoE layer for one token, in the order of src/engine.js:133-156 on the WASM backend:
+ *   logits = mat(ffn_gate_inp, x)                     (strata_project, src/ops.js:105)
+ *   [logits += bias]                                  (strata_elementwise mode 5; synthetic Zipf offset)
+ *   ids, w = strata_router(logits)                    (src/engine.js:136)
+ *   for k: gate = mat(expert.gate, x); up = mat(expert.up, x)   (strata_quant_project with scales
+ *          act = elementwise(gate, up, 3); down = mat(expert.down, act)   expanded by strata_expert_scales,
+ *          parts[k] = down                            src/engine.js:129-131,148; src/ops.js:32-35,108)
+ *   shared = expert(shared); sg = mat(ffn_gate_inp_shexp, x)    (src/engine.js:154)
+ *   y = strata_moe_combine(parts, w, shared, sg)      (src/engine.js:155)
+ * The quant projection with pre-expanded scales computes the same floats, in the same order, as
+ * the fused strata_q2_gate_up/strata_q2_down entries, so this routine uses the Q2 blob directly.
+ * Blob layout (vendor/strata/tools/pack_layer.py:54-65): gate/up codes (rows interleaved
+ * g0,u0,g1,...), down codes, gate/up FP16 scales, down FP16 scales.
+ * ------------------------------------------------------------------------------------- */
+static void expert_token(const float *x, const unsigned int *blob, int width, int ff, float *hidden, float *out) {
+    const int gu_codes = 0, d_codes = 2 * ff * width / 16, gu_scales = 2 * (3 * ff * width / 16), d_scales = gu_scales + 2 * ff * width / 64;
+    (void)gu_codes;
+    oracle_strata_q2_gate_up((unsigned)ff, 1, 1, x, blob, NULL, NULL, hidden, width, ff, 1, 0, 0, 0, gu_scales);
+    oracle_strata_q2_down((unsigned)width, 1, 1, hidden, blob, NULL, NULL, out, width, ff, 1, 0, 0, 0, d_codes, d_scales);
+}
+
+/* x: [width]; router: [experts x width]; sharedGate: [width]; blobs: experts blobs of blobWords words;
+ * bias: optional [experts] logit offsets. Writes y [width], ids/weights [topK]. */
+int oracle_moe_token(const float *x, const float *router, const float *bias, const float *sharedGate, const unsigned int *blobs,
+                     const unsigned int *sharedBlob, long blobWords, int width, int ff, int experts, int topK, float *y, int *ids,
+                     float *weights) {
+    float *logits = (float *)malloc(sizeof(float) * experts);
+    float *parts = (float *)malloc(sizeof(float) * (size_t)width * topK);
+    float *shared = (float *)malloc(sizeof(float) * width);
+    float *hidden = (float *)malloc(sizeof(float) * ff);
+    float sg;
+    if (!logits || !parts || !shared || !hidden) { free(logits); free(parts); free(shared); free(hidden); return 1; }
+    oracle_strata_project((unsigned)experts, 1, 1, x, router, logits, width, experts, 1, experts, 0);
+    if (bias) oracle_strata_elementwise((unsigned)((experts + 63) / 64), 1, 1, logits, bias, logits, experts, 5, 1.0f);
+    router_token(logits, ids, weights, experts, topK);
+    for (int k = 0; k < topK; ++k) expert_token(x, blobs + (long)ids[k] * blobWords, width, ff, hidden, parts + (long)k * width);
+    expert_token(x, sharedBlob, width, ff, hidden, shared);
+    oracle_strata_project(1, 1, 1, x, sharedGate, &sg, width, 1, 1, 1, 0);
+    oracle_strata_moe_combine((unsigned)((width + 63) / 64), 1, 1, parts, weights, shared, &sg, y, width, topK);
+    free(logits); free(parts); free(shared); free(hidden);
+    return 0;
+}
+
+/* Router logits only (for the routing-exactness checks at full batch sizes). */
+int oracle_route_token(const float *x, const float *router, const float *bias, int width, int experts, int topK, float *logits, int *ids,
+                       float *weights) {
+    oracle_strata_project((unsigned)experts, 1, 1, x, router, logits, width, experts, 1, experts, 0);
+    if (bias) oracle_strata_elementwise((unsigned)((experts + 63) / 64), 1, 1, logits, bias, logits, experts, 5, 1.0f);
+    router_token(logits, ids, weights, experts, topK);
+    return 0;
+}

@@ -1,0 +1,478 @@
+// C-ABI of libstrata_cuda (include/strata_cuda.h): contexts, stream-ordered buffers,
+// by-name dispatch of the reference entries with the reference's argument validation, the
+// fused mixture-of-experts layer and the synthetic-workload generator.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/strata_cuda.h"
+#include "kernels.h"
+
+using namespace strata;
+
+struct Buffer {
+    void *ptr;
+    uint64_t length;  // elements of 4 bytes
+    int type;
+};
+
+struct strata_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::unordered_map<uint64_t, Buffer> buffers;
+    uint64_t next_handle = 1;
+    uint64_t bytes_resident = 0;
+    unsigned *err_dev = nullptr;   // device error word (kErr* bits)
+    unsigned *err_host = nullptr;  // pinned mirror
+    void *workspace = nullptr;
+    size_t workspace_bytes = 0;
+    uint64_t dispatches = 0, fused_calls = 0;
+    std::string last_error;
+    char device_name[256] = {0};
+    int sms = 0;
+};
+
+namespace {
+
+int fail(strata_ctx *ctx, int code, const char *fmt, ...) {
+    char msg[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(msg, sizeof msg, fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->last_error = msg;
+    return code;
+}
+
+int cuda_fail(strata_ctx *ctx, cudaError_t e, const char *what) {
+    return fail(ctx, STRATA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define CUDA_OR_FAIL(ctx, expr, what)                           \
+    do {                                                        \
+        cudaError_t _e = (expr);                                \
+        if (_e != cudaSuccess) return cuda_fail(ctx, _e, what); \
+    } while (0)
+
+int use_device(strata_ctx *ctx) {
+    cudaError_t e = cudaSetDevice(ctx->device);
+    return e == cudaSuccess ? STRATA_OK : cuda_fail(ctx, e, "cudaSetDevice");
+}
+
+Buffer *find(strata_ctx *ctx, strata_buf h) {
+    auto it = ctx->buffers.find(h);
+    return it == ctx->buffers.end() ? nullptr : &it->second;
+}
+
+// Reads back and clears the device error word; the stream must already be synchronised.
+int check_device_errors(strata_ctx *ctx) {
+    unsigned e = *ctx->err_host;
+    if (!e) return STRATA_OK;
+    *ctx->err_host = 0;
+    cudaMemsetAsync(ctx->err_dev, 0, sizeof(unsigned), ctx->stream);
+    std::string what;
+    if (e & kErrIndex) what += "an index outside its buffer was skipped; ";
+    if (e & kErrRouting) what += "invalid expert routing result; ";
+    if (e & kErrWaitTimeout) what += "a bounded device wait timed out; ";
+    return fail(ctx, STRATA_ERR_DEVICE, "device check failed: %s", what.c_str());
+}
+
+int sync(strata_ctx *ctx) {
+    CUDA_OR_FAIL(ctx, cudaMemcpyAsync(ctx->err_host, ctx->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx->stream),
+                 "error word readback");
+    CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return check_device_errors(ctx);
+}
+
+// ---- reference dispatch table (parsed once from kernels.h specs)
+struct Param {
+    std::string name;
+    char kind;
+};
+struct Entry {
+    const KernelSpec *spec;
+    std::vector<Param> params;
+};
+std::vector<Entry> &entries() {
+    static std::vector<Entry> table;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        for (int k = 0; k < kNumKernels; ++k) {
+            Entry e{&kKernels[k], {}};
+            const char *p = kKernels[k].params;
+            while (*p) {
+                while (*p == ' ') ++p;
+                const char *c = strchr(p, ':');
+                if (!c) break;
+                e.params.push_back(Param{std::string(p, c - p), c[1]});
+                p = c + 2;
+            }
+            table.push_back(std::move(e));
+        }
+    });
+    return table;
+}
+
+// src/backend.js:5-8 requireInteger(n, label, min=1, max=2^31-1)
+bool int_in(long long v, long long lo = 1, long long hi = 0x7fffffff) { return v >= lo && v <= hi; }
+
+// src/backend.js:10-56 for the entries this library serves. Returns 0 or an error code.
+int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params, const std::vector<KArg> &a) {
+    auto idx = [&](const char *p) {
+        for (size_t i = 0; i < params.size(); ++i)
+            if (params[i].name == p) return (int)i;
+        return -1;
+    };
+    auto I = [&](const char *p) { return (long long)a[idx(p)].i; };
+    auto len = [&](const char *p) { return a[idx(p)].len; };
+    const std::string n(name);
+    if (n == "strata_router" || n == "strata_router_batch") {
+        if (!int_in(I("experts")) || !int_in(I("topK")))
+            return fail(ctx, STRATA_ERR_RANGE, "%s.experts and %s.topK must be integers in [1, 2147483647]", name, name);
+        if (I("experts") > 512 || I("topK") > std::min(I("experts"), 32LL))
+            return fail(ctx, STRATA_ERR_RANGE, "Router supports 1-512 experts and topK <= min(experts,32)");
+    }
+    if (n == "strata_quant_project") {
+        long long bits = I("bits");
+        if (bits != 2 && bits != 4 && bits != 8) return fail(ctx, STRATA_ERR_RANGE, "Canonical code width must be 2, 4 or 8");
+        if (!int_in(I("cols")) || !int_in(I("groupSize")))
+            return fail(ctx, STRATA_ERR_RANGE, "%s.cols and groupSize must be positive integers", name);
+        if (I("cols") % I("groupSize") || I("cols") * I("rows") * bits > 0x7fffffffLL)
+            return fail(ctx, STRATA_ERR_RANGE, "Quantized rows must contain whole groups and fit 31-bit indexing");
+    }
+    if (n == "strata_project" || n == "strata_quant_project" || n == "strata_bf16_project" || n == "strata_q2_project") {
+        for (const char *p : {"tokens", "rows", "cols", "outputStride"})
+            if (!int_in(I(p))) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p);
+        if (!int_in(I("outputOffset"), 0)) return fail(ctx, STRATA_ERR_RANGE, "projection output offset must be an integer >= 0");
+        if (I("outputOffset") + I("rows") > I("outputStride") || I("tokens") * I("outputStride") > len("Y") ||
+            I("tokens") * I("cols") > len("X"))
+            return fail(ctx, STRATA_ERR_LAYOUT, "Projection batch exceeds buffer layout");
+    }
+    if (n == "strata_q2_project") {
+        if (I("cols") % 64) return fail(ctx, STRATA_ERR_LAYOUT, "Q2 expert columns must contain complete groups");
+        for (const char *p : {"codeOffset", "scaleOffset", "weightRow"})
+            if (!int_in(I(p), 0)) return fail(ctx, STRATA_ERR_RANGE, "%s must be an integer >= 0", p);
+        if (!int_in(I("rowStride"), 1, 2)) return fail(ctx, STRATA_ERR_RANGE, "expert row stride must be an integer in [1, 2]");
+    }
+    if (n == "strata_q2_gate_up" || n == "strata_q2_down") {
+        if (!int_in(I("width")) || !int_in(I("ff")))
+            return fail(ctx, STRATA_ERR_RANGE, "%s.width and ff must be positive integers", name);
+        if (I("width") % 64 || I("ff") % 64) return fail(ctx, STRATA_ERR_LAYOUT, "Packed expert dimensions must contain complete groups");
+        if (!int_in(I("tokens"))) return fail(ctx, STRATA_ERR_RANGE, "%s.tokens must be an integer in [1, 2147483647]", name);
+        if (len("Hidden") < I("tokens") * I("ff") || (I("mapped") && len("Mapping") < I("tokens") * 2))
+            return fail(ctx, STRATA_ERR_LAYOUT, "Packed expert batch exceeds buffer layout");
+        if (n == "strata_q2_down" && !int_in(I("outputOffset"), 0))
+            return fail(ctx, STRATA_ERR_RANGE, "expert output offset must be an integer >= 0");
+    }
+    return STRATA_OK;
+}
+
+bool blob_geometry_ok(int width, int ff) { return width > 0 && ff > 0 && width % 64 == 0 && ff % 64 == 0; }
+long long blob_words_of(int width, int ff) { return 3LL * ff * width / 16 + 3LL * ff * width / 128; }
+
+}  // namespace
+
+extern "C" {
+
+int strata_create(int device, strata_ctx **out) {
+    if (!out) return STRATA_ERR_RANGE;
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) return STRATA_ERR_CUDA;
+    if (device < 0 || device >= count) return STRATA_ERR_RANGE;
+    auto *ctx = new strata_ctx();
+    ctx->device = device;
+    if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&ctx->err_dev, sizeof(unsigned)) != cudaSuccess ||
+        cudaHostAlloc(&ctx->err_host, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess ||
+        cudaMemset(ctx->err_dev, 0, sizeof(unsigned)) != cudaSuccess) {
+        strata_destroy(ctx);
+        return STRATA_ERR_CUDA;
+    }
+    *ctx->err_host = 0;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) {
+        snprintf(ctx->device_name, sizeof ctx->device_name, "%s", prop.name);
+        ctx->sms = prop.multiProcessorCount;
+    }
+    *out = ctx;
+    return STRATA_OK;
+}
+
+int strata_destroy(strata_ctx *ctx) {
+    if (!ctx) return STRATA_OK;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    for (auto &kv : ctx->buffers) cudaFree(kv.second.ptr);
+    ctx->buffers.clear();
+    if (ctx->workspace) cudaFree(ctx->workspace);
+    if (ctx->err_dev) cudaFree(ctx->err_dev);
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return STRATA_OK;
+}
+
+int strata_last_error(strata_ctx *ctx, char *buf, size_t cap) {
+    if (!ctx) return 0;
+    if (buf && cap) snprintf(buf, cap, "%s", ctx->last_error.c_str());
+    return (int)ctx->last_error.size();
+}
+
+int strata_stream(strata_ctx *ctx, void **stream) {
+    if (!ctx || !stream) return STRATA_ERR_RANGE;
+    *stream = (void *)ctx->stream;
+    return STRATA_OK;
+}
+
+int strata_alloc(strata_ctx *ctx, uint64_t length, int type, int zero, strata_buf *out) {
+    if (!ctx || !out) return STRATA_ERR_RANGE;
+    if (type != STRATA_F32 && type != STRATA_I32 && type != STRATA_U32) return fail(ctx, STRATA_ERR_RANGE, "Unsupported buffer type %d", type);
+    if (length < 1 || length > (1ull << 40)) return fail(ctx, STRATA_ERR_RANGE, "allocation must be an integer in [1, 2^40] elements");
+    if (int r = use_device(ctx)) return r;
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, length * 4);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(ctx, STRATA_ERR_ALLOC, "device allocation of %llu bytes failed: %s", (unsigned long long)(length * 4),
+                    cudaGetErrorString(e));
+    }
+    if (zero) CUDA_OR_FAIL(ctx, cudaMemsetAsync(p, 0, length * 4, ctx->stream), "cudaMemsetAsync");
+    uint64_t h = ctx->next_handle++;
+    ctx->buffers[h] = Buffer{p, length, type};
+    ctx->bytes_resident += length * 4;
+    *out = h;
+    return STRATA_OK;
+}
+
+int strata_free(strata_ctx *ctx, strata_buf buf) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    Buffer *b = find(ctx, buf);
+    if (!b) return STRATA_OK;  // src/backend.js:115 ignores unknown buffers
+    if (int r = use_device(ctx)) return r;
+    cudaStreamSynchronize(ctx->stream);  // work that still reads the buffer completes first
+    cudaFree(b->ptr);
+    ctx->bytes_resident -= b->length * 4;
+    ctx->buffers.erase(buf);
+    return STRATA_OK;
+}
+
+int strata_write(strata_ctx *ctx, strata_buf buf, const void *data, uint64_t count, uint64_t offset) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    Buffer *b = find(ctx, buf);
+    if (!b) return fail(ctx, STRATA_ERR_HANDLE, "Invalid write: unknown buffer");
+    if (offset + count > b->length || offset + count < offset) return fail(ctx, STRATA_ERR_LAYOUT, "Invalid write: exceeds buffer");
+    if (!count) return STRATA_OK;
+    if (!data) return fail(ctx, STRATA_ERR_RANGE, "Invalid write: null data");
+    if (int r = use_device(ctx)) return r;
+    // Pageable memory is staged before this returns; page-locked memory is read later by the
+    // stream and must stay unchanged until the next synchronising call.
+    CUDA_OR_FAIL(ctx, cudaMemcpyAsync((char *)b->ptr + offset * 4, data, count * 4, cudaMemcpyHostToDevice, ctx->stream),
+                 "host-to-device copy");
+    return STRATA_OK;
+}
+
+int strata_read(strata_ctx *ctx, strata_buf buf, void *out, uint64_t count, uint64_t offset) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    Buffer *b = find(ctx, buf);
+    if (!b) return fail(ctx, STRATA_ERR_HANDLE, "Invalid read: unknown buffer");
+    if (offset + count > b->length || offset + count < offset) return fail(ctx, STRATA_ERR_LAYOUT, "Invalid read: exceeds buffer");
+    if (int r = use_device(ctx)) return r;
+    if (count) {
+        if (!out) return fail(ctx, STRATA_ERR_RANGE, "Invalid read: null destination");
+        CUDA_OR_FAIL(ctx, cudaMemcpyAsync(out, (const char *)b->ptr + offset * 4, count * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                     "device-to-host copy");
+    }
+    return sync(ctx);
+}
+
+int strata_copy(strata_ctx *ctx, strata_buf src, strata_buf dst, uint64_t count, uint64_t src_offset, uint64_t dst_offset) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    Buffer *a = find(ctx, src), *b = find(ctx, dst);
+    if (!a || !b) return fail(ctx, STRATA_ERR_HANDLE, "Invalid copy: unknown buffer");
+    if (count + src_offset > a->length || count + dst_offset > b->length) return fail(ctx, STRATA_ERR_LAYOUT, "Invalid copy: exceeds buffer");
+    if (!count) return STRATA_OK;
+    if (int r = use_device(ctx)) return r;
+    CUDA_OR_FAIL(ctx, cudaMemcpyAsync((char *)b->ptr + dst_offset * 4, (const char *)a->ptr + src_offset * 4, count * 4,
+                                      cudaMemcpyDeviceToDevice, ctx->stream),
+                 "device copy");
+    return STRATA_OK;
+}
+
+int strata_zero(strata_ctx *ctx, strata_buf buf) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    Buffer *b = find(ctx, buf);
+    if (!b) return fail(ctx, STRATA_ERR_HANDLE, "Invalid zero: unknown buffer");
+    if (int r = use_device(ctx)) return r;
+    CUDA_OR_FAIL(ctx, cudaMemsetAsync(b->ptr, 0, b->length * 4, ctx->stream), "cudaMemsetAsync");
+    return STRATA_OK;
+}
+
+int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *type, void **device_ptr) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    Buffer *b = find(ctx, buf);
+    if (!b) return fail(ctx, STRATA_ERR_HANDLE, "unknown buffer");
+    if (length) *length = b->length;
+    if (type) *type = b->type;
+    if (device_ptr) *device_ptr = b->ptr;
+    return STRATA_OK;
+}
+
+int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int nargs, const uint32_t groups[3]) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!name) return fail(ctx, STRATA_ERR_UNKNOWN, "Unknown kernel (null)");
+    const Entry *entry = nullptr;
+    for (const Entry &e : entries())
+        if (!strcmp(e.spec->name, name)) entry = &e;
+    if (!entry) return fail(ctx, STRATA_ERR_UNKNOWN, "Unknown kernel %s", name);
+    // vendor/webcuda/src/wasm/runtime.js:11: three positive integers, at most 1e8 workgroups.
+    if (!groups || !groups[0] || !groups[1] || !groups[2] || (double)groups[0] * groups[1] * groups[2] > 1e8)
+        return fail(ctx, STRATA_ERR_RANGE, "Invalid dispatch size");
+    std::vector<KArg> vals(entry->params.size());
+    for (size_t i = 0; i < entry->params.size(); ++i) {
+        const Param &p = entry->params[i];
+        const strata_arg *found = nullptr;
+        for (int j = 0; j < nargs; ++j)
+            if (args[j].name && p.name == args[j].name) found = &args[j];
+        if (!found) return fail(ctx, STRATA_ERR_UNKNOWN, "Missing %s.%s", name, p.name.c_str());
+        KArg v{nullptr, 0, 0, 0.0f};
+        if (p.kind == 'f' || p.kind == 'u' || p.kind == 'i') {
+            if (found->kind != STRATA_ARG_BUF) return fail(ctx, STRATA_ERR_LAYOUT, "%s.%s must be a buffer", name, p.name.c_str());
+            Buffer *b = find(ctx, found->buf);
+            if (!b) return fail(ctx, STRATA_ERR_HANDLE, "%s.%s is not a live buffer", name, p.name.c_str());
+            v.ptr = b->ptr;
+            v.len = (long long)b->length;
+        } else if (p.kind == 'I') {
+            if (found->kind != STRATA_ARG_I32) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer", name, p.name.c_str());
+            v.i = found->i32;
+        } else {
+            if (found->kind == STRATA_ARG_F32) v.f = found->f32;
+            else if (found->kind == STRATA_ARG_I32) v.f = (float)found->i32;
+            else return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be a number", name, p.name.c_str());
+        }
+        vals[i] = v;
+    }
+    if (int r = validate(ctx, name, entry->params, vals)) return r;
+    if (int r = use_device(ctx)) return r;
+    const unsigned g[3] = {groups[0], groups[1], groups[2]};
+    cudaError_t e = entry->spec->launch(vals.data(), g, ctx->stream, ctx->err_dev);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, name);
+    ++ctx->dispatches;
+    return STRATA_OK;
+}
+
+int strata_idle(strata_ctx *ctx) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (int r = use_device(ctx)) return r;
+    return sync(ctx);
+}
+
+int strata_flush(strata_ctx *ctx) { return ctx ? STRATA_OK : STRATA_ERR_RANGE; }
+
+int strata_info(strata_ctx *ctx, char *json, size_t cap) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    char buf[1024];
+    int n = snprintf(buf, sizeof buf,
+                     "{\"backend\":\"cuda\",\"device\":\"%s\",\"ordinal\":%d,\"sms\":%d,\"buffers\":%zu,\"bytesResident\":%llu,"
+                     "\"workspaceBytes\":%zu,\"dispatches\":%llu,\"fusedCalls\":%llu}",
+                     ctx->device_name, ctx->device, ctx->sms, ctx->buffers.size(), (unsigned long long)ctx->bytes_resident,
+                     ctx->workspace_bytes, (unsigned long long)ctx->dispatches, (unsigned long long)ctx->fused_calls);
+    if (json && cap) snprintf(json, cap, "%s", buf);
+    return n;
+}
+
+int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
+                       strata_buf weights, int32_t mode) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!layer) return fail(ctx, STRATA_ERR_RANGE, "null layer");
+    const strata_moe_layer &l = *layer;
+    if (!blob_geometry_ok(l.width, l.ff)) return fail(ctx, STRATA_ERR_LAYOUT, "Packed expert dimensions must contain complete groups");
+    if (l.experts < 1 || l.experts > 512 || l.top_k < 1 || l.top_k > std::min(l.experts, 32))
+        return fail(ctx, STRATA_ERR_RANGE, "Router supports 1-512 experts and topK <= min(experts,32)");
+    if (tokens < 1) return fail(ctx, STRATA_ERR_RANGE, "tokens must be an integer >= 1");
+    if (mode != STRATA_MOE_EXACT) return fail(ctx, STRATA_ERR_RANGE, "unknown mode %d", mode);
+    const long long bw = blob_words_of(l.width, l.ff);
+    struct Need {
+        strata_buf h;
+        long long n;
+        const char *what;
+        bool optional;
+    } need[] = {{l.router, (long long)l.experts * l.width, "router", false},
+                {l.router_bias, l.experts, "router_bias", true},
+                {l.experts_blob, bw * l.experts, "experts_blob", false},
+                {l.shared_blob, bw, "shared_blob", false},
+                {l.shared_gate, l.width, "shared_gate", false},
+                {x, (long long)tokens * l.width, "x", false},
+                {y, (long long)tokens * l.width, "y", false},
+                {ids, (long long)tokens * l.top_k, "ids", false},
+                {weights, (long long)tokens * l.top_k, "weights", false}};
+    void *ptr[9];
+    for (int i = 0; i < 9; ++i) {
+        ptr[i] = nullptr;
+        if (need[i].optional && need[i].h == 0) continue;
+        Buffer *b = find(ctx, need[i].h);
+        if (!b) return fail(ctx, STRATA_ERR_HANDLE, "moe layer: %s is not a live buffer", need[i].what);
+        if ((long long)b->length < need[i].n)
+            return fail(ctx, STRATA_ERR_LAYOUT, "moe layer: %s holds %llu elements, needs %lld", need[i].what,
+                        (unsigned long long)b->length, need[i].n);
+        ptr[i] = b->ptr;
+    }
+    if (int r = use_device(ctx)) return r;
+    const size_t ws = moe_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k);
+    if (ws > ctx->workspace_bytes) {
+        CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "workspace resize");
+        if (ctx->workspace) cudaFree(ctx->workspace);
+        ctx->workspace = nullptr;
+        ctx->workspace_bytes = 0;
+        cudaError_t e = cudaMalloc(&ctx->workspace, ws);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(ctx, STRATA_ERR_ALLOC, "workspace allocation of %zu bytes failed", ws);
+        }
+        ctx->workspace_bytes = ws;
+    }
+    MoeLayerDev L{l.width, l.ff, l.experts, l.top_k, (const float *)ptr[0], (const float *)ptr[1], (const unsigned *)ptr[2], bw,
+                  (const unsigned *)ptr[3], (const float *)ptr[4]};
+    MoeScratch s = moe_scratch_carve(ctx->workspace, tokens, l.width, l.ff, l.experts, l.top_k);
+    cudaError_t e = moe_forward_exact(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], s, ctx->stream,
+                                      ctx->err_dev);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "strata_moe_forward");
+    ++ctx->fused_calls;
+    return STRATA_OK;
+}
+
+int strata_synth_blobs(strata_ctx *ctx, strata_buf buf, uint64_t offset, uint64_t seed, int32_t layer, int32_t first_expert,
+                       int32_t count, int32_t width, int32_t ff, int32_t shared) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!blob_geometry_ok(width, ff) || count < 1 || first_expert < 0 || layer < 0)
+        return fail(ctx, STRATA_ERR_RANGE, "synth blobs: invalid geometry");
+    Buffer *b = find(ctx, buf);
+    if (!b) return fail(ctx, STRATA_ERR_HANDLE, "synth blobs: unknown buffer");
+    const long long n = blob_words_of(width, ff) * count;
+    if ((long long)(offset + n) > (long long)b->length) return fail(ctx, STRATA_ERR_LAYOUT, "synth blobs: exceeds buffer");
+    if (int r = use_device(ctx)) return r;
+    cudaError_t e = synth_expert_blobs((unsigned *)b->ptr + offset, seed, layer, first_expert, count, width, ff, shared, ctx->stream);
+    return e == cudaSuccess ? STRATA_OK : cuda_fail(ctx, e, "synth blobs");
+}
+
+int strata_synth_normals(strata_ctx *ctx, strata_buf buf, uint64_t offset, uint64_t seed, uint64_t tag, uint64_t sub, uint64_t start,
+                         uint64_t count, double scale) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    Buffer *b = find(ctx, buf);
+    if (!b) return fail(ctx, STRATA_ERR_HANDLE, "synth normals: unknown buffer");
+    if (offset + count > b->length) return fail(ctx, STRATA_ERR_LAYOUT, "synth normals: exceeds buffer");
+    if (!count) return STRATA_OK;
+    if (int r = use_device(ctx)) return r;
+    cudaError_t e = synth_normals_f32((float *)b->ptr + offset, synth_stream_key(seed, tag, sub), (long long)start, (long long)count, scale,
+                                      ctx->stream);
+    return e == cudaSuccess ? STRATA_OK : cuda_fail(ctx, e, "synth normals");
+}
+
+}  // extern "C"

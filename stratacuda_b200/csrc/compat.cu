@@ -1,0 +1,393 @@
+// Reference-compatible entries for strata_run(): the kernels that src/ops.js, src/engine.js
+// and src/prefill.js dispatch by name (kernels/strata.cu), with the same parameter names,
+// the same dispatch grid of 64-lane workgroups and bit-identical F32 results.
+//
+// B200 shape: a reference workgroup is one warp (thread t owns virtual lanes t and t+32, the
+// s=32 tree step is in-thread, the rest are shuffles), four workgroups per 128-thread block.
+// Every global access is bounds-checked against the buffer it came from: an index outside
+// the buffer reads 0 / skips the write and sets the context's device error word, which the
+// host reports at the next synchronisation. No argument can make these kernels fault.
+#include "common.cuh"
+#include "kernels.h"
+#include "route.cuh"
+
+namespace strata {
+namespace {
+
+template <typename T>
+struct Buf {
+    T *p;
+    long long n;
+    __device__ __forceinline__ T get(long long i, unsigned *err) const {
+        if (i < 0 || i >= n) { raise_error(err, kErrIndex); return T(0); }
+        return p[i];
+    }
+    __device__ __forceinline__ void set(long long i, T v, unsigned *err) const {
+        if (i < 0 || i >= n) { raise_error(err, kErrIndex); return; }
+        p[i] = v;
+    }
+};
+using FB = Buf<float>;
+using UB = Buf<unsigned>;
+using IB = Buf<int>;
+
+__device__ __forceinline__ float half_of(const UB &b, long long h, unsigned *err) {
+    return half_bits((b.get(h / 2, err) >> ((h % 2) * 16)) & 65535u);
+}
+__device__ __forceinline__ int code_of(const UB &b, long long codeOffset, long long index, unsigned *err) {
+    return (int)((b.get(codeOffset + index / 16, err) >> ((index % 16) * 2)) & 3u) - 1;
+}
+
+struct Grid {
+    unsigned x, y, z;
+};
+constexpr int kWarpsPerBlock = 4;
+
+// Workgroup (x, y, z) handled by this warp, or false when past the dispatch grid.
+__device__ __forceinline__ bool my_group(const Grid g, unsigned &gx, unsigned &gy, unsigned &gz) {
+    unsigned long long w = (unsigned long long)blockIdx.x * kWarpsPerBlock + threadIdx.x / 32;
+    unsigned long long total = (unsigned long long)g.x * g.y * g.z;
+    if (w >= total) return false;
+    gx = (unsigned)(w % g.x);
+    gy = (unsigned)((w / g.x) % g.y);
+    gz = (unsigned)(w / ((unsigned long long)g.x * g.y));
+    return true;
+}
+
+// ---------------------------------------------------------------- element kernels
+// (one reference lane per thread: i = blockIdx.x * 64 + threadIdx.x over the x extent)
+
+__global__ void k_unpack_half(Grid g, UB Packed, FB Values, int count, unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (long long)g.x * STRATA_LANES && i < count) Values.set(i, half_of(Packed, i, err), err);
+}
+
+__global__ void k_expert_scales(Grid g, UB Blob, FB Scales, int offset, int count, unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (long long)g.x * STRATA_LANES && i < count) Scales.set(i, half_of(Blob, offset + i, err), err);
+}
+
+__global__ void k_elementwise(Grid g, FB A, FB B, FB Y, int n, int mode, float scale, unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)g.x * STRATA_LANES || i >= n) return;
+    float a = __fmul_rn(A.get(i, err), scale), v = a;
+    if (mode == 1) v = ref_silu(a);
+    if (mode == 2) v = ref_sigmoid(a);
+    if (mode == 3) v = __fmul_rn(ref_silu(a), B.get(i, err));
+    if (mode == 4) v = __fmul_rn(a, ref_sigmoid(B.get(i, err)));
+    if (mode == 5) v = __fadd_rn(a, B.get(i, err));
+    Y.set(i, v, err);
+}
+
+__global__ void k_moe_combine(Grid g, FB Parts, FB Weights, FB Shared, FB SharedGate, FB Y, int width, int count, unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)g.x * STRATA_LANES || i >= width) return;
+    float value = __fmul_rn(Shared.get(i, err), ref_sigmoid(SharedGate.get(0, err)));
+    for (int k = 0; k < count; ++k) value = __fadd_rn(value, __fmul_rn(Parts.get((long long)k * width + i, err), Weights.get(k, err)));
+    Y.set(i, value, err);
+}
+
+__global__ void k_moe_combine_batch(Grid g, FB Parts, FB Weights, FB Shared, FB SharedGate, FB Y, int width, int count, int tokens,
+                                    unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)g.x * STRATA_LANES || i >= (long long)width * tokens) return;
+    long long token = i / width, d = i % width;
+    float value = __fmul_rn(Shared.get(i, err), ref_sigmoid(SharedGate.get(token, err)));
+    for (int k = 0; k < count; ++k)
+        value = __fadd_rn(value, __fmul_rn(Parts.get((token * count + k) * width + d, err), Weights.get(token * count + k, err)));
+    Y.set(i, value, err);
+}
+
+__global__ void k_gather_rows(Grid g, FB X, IB Indices, FB Y, int width, int rows, unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)g.x * STRATA_LANES || i >= (long long)width * rows) return;
+    Y.set(i, X.get((long long)Indices.get(i / width, err) * width + i % width, err), err);
+}
+
+__global__ void k_scatter_rows(Grid g, FB X, IB Indices, FB Y, int width, int rows, unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)g.x * STRATA_LANES || i >= (long long)width * rows) return;
+    Y.set((long long)Indices.get(i / width, err) * width + i % width, X.get(i, err), err);
+}
+
+// ---------------------------------------------------------------- workgroup kernels
+
+// kernels/strata.cu:156-165
+__global__ void k_project(Grid g, FB X, FB W, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset, unsigned *err) {
+    unsigned row, token, z;
+    if (!my_group(g, row, token, z)) return;
+    if (!((int)row < rows && (int)token < tokens)) return;
+    int t = threadIdx.x & 31;
+    float lo = 0.0f, hi = 0.0f;
+    for (int i = t; i < cols; i += STRATA_LANES) {
+        lo = __fadd_rn(lo, __fmul_rn(W.get((long long)row * cols + i, err), X.get((long long)token * cols + i, err)));
+        if (i + 32 < cols)
+            hi = __fadd_rn(hi, __fmul_rn(W.get((long long)row * cols + i + 32, err), X.get((long long)token * cols + i + 32, err)));
+    }
+    float r = tree64(lo, hi);
+    if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
+}
+
+// kernels/strata.cu:168-176
+__global__ void k_bf16_project(Grid g, FB X, UB Codes, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset,
+                               unsigned *err) {
+    unsigned row, token, z;
+    if (!my_group(g, row, token, z)) return;
+    if (!((int)row < rows && (int)token < tokens)) return;
+    int t = threadIdx.x & 31;
+    float acc[2] = {0.0f, 0.0f};
+    for (int i0 = t; i0 < cols; i0 += STRATA_LANES)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int i = i0 + 32 * h;
+            if (i >= cols) continue;
+            long long ix = (long long)row * cols + i;
+            unsigned bits = (Codes.get(ix / 2, err) >> ((ix % 2) * 16)) & 65535u;
+            acc[h] = __fadd_rn(acc[h], __fmul_rn(__uint_as_float(bits << 16), X.get((long long)token * cols + i, err)));
+        }
+    float r = tree64(acc[0], acc[1]);
+    if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
+}
+
+// kernels/strata.cu:179-192
+__global__ void k_q2_project(Grid g, FB X, UB Blob, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset,
+                             int codeOffset, int scaleOffset, int weightRow, int rowStride, unsigned *err) {
+    unsigned row, token, z;
+    if (!my_group(g, row, token, z)) return;
+    if (!((int)row < rows && (int)token < tokens)) return;
+    int t = threadIdx.x & 31;
+    float acc[2] = {0.0f, 0.0f};
+    for (int i0 = t; i0 < cols; i0 += STRATA_LANES)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int i = i0 + 32 * h;
+            if (i >= cols) continue;
+            long long ix = ((long long)weightRow + (long long)row * rowStride) * cols + i;
+            float weight = __fmul_rn((float)code_of(Blob, codeOffset, ix, err), half_of(Blob, scaleOffset + ix / 64, err));
+            acc[h] = __fadd_rn(acc[h], __fmul_rn(weight, X.get((long long)token * cols + i, err)));
+        }
+    float r = tree64(acc[0], acc[1]);
+    if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
+}
+
+__device__ __forceinline__ float iq4(int c) {
+    const float t[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f, 1.f, 13.f, 25.f, 38.f, 53.f, 69.f, 89.f, 113.f};
+    return (c >= 0 && c < 15) ? t[c] : 113.0f;
+}
+__device__ __forceinline__ long long group_of(long long index, int size) {
+    if (size == 16) return index >> 4;
+    if (size == 32) return index >> 5;
+    if (size == 64) return index >> 6;
+    return index / size;
+}
+
+// kernels/strata.cu:193-211
+__global__ void k_quant_project(Grid g, FB X, UB Codes, FB Scales, FB Offsets, FB Y, int cols, int rows, int tokens, int outputStride,
+                                int outputOffset, int bits, int groupSize, int bias, int codebook, int hasOffset, unsigned *err) {
+    unsigned row, token, z;
+    if (!my_group(g, row, token, z)) return;
+    if (!((int)row < rows && (int)token < tokens)) return;
+    int t = threadIdx.x & 31;
+    float acc[2] = {0.0f, 0.0f};
+    for (int i0 = t; i0 < cols; i0 += STRATA_LANES)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int i = i0 + 32 * h;
+            if (i >= cols) continue;
+            long long index = (long long)row * cols + i, bit = index * bits;
+            int code = (int)((Codes.get(bit / 32, err) >> (bit % 32)) & ((1u << bits) - 1u));
+            float value = codebook == 1 ? iq4(code) : (float)(code + bias);
+            long long grp = group_of(index, groupSize);
+            float weight = __fmul_rn(value, Scales.get(grp, err));
+            if (hasOffset != 0) weight = __fadd_rn(weight, Offsets.get(grp, err));
+            acc[h] = __fadd_rn(acc[h], __fmul_rn(weight, X.get((long long)token * cols + i, err)));
+        }
+    float r = tree64(acc[0], acc[1]);
+    if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
+}
+
+// kernels/strata.cu:38-55
+__global__ void k_q2_gate_up(Grid g, FB X, UB Blob, FB Scales, IB Mapping, FB Hidden, int width, int ff, int tokens, int mapped,
+                             int expanded, int codeOffset, int scaleOffset, unsigned *err) {
+    unsigned row, token, z;
+    if (!my_group(g, row, token, z)) return;
+    if (!((int)row < ff && (int)token < tokens)) return;
+    int t = threadIdx.x & 31;
+    long long inputRow = mapped != 0 ? Mapping.get(2LL * token, err) : (long long)token;
+    float ga[2] = {0.0f, 0.0f}, ua[2] = {0.0f, 0.0f};
+    for (int i0 = t; i0 < width; i0 += STRATA_LANES)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int i = i0 + 32 * h;
+            if (i >= width) continue;
+            long long gi = (long long)row * 2 * width + i, ui = gi + width;
+            int gc = code_of(Blob, codeOffset, gi, err), uc = code_of(Blob, codeOffset, ui, err);
+            long long gs = scaleOffset + gi / 64, us = scaleOffset + ui / 64;
+            float gw = __fmul_rn((float)gc, expanded != 0 ? Scales.get(gs, err) : half_of(Blob, gs, err));
+            float uw = __fmul_rn((float)uc, expanded != 0 ? Scales.get(us, err) : half_of(Blob, us, err));
+            float x = X.get(inputRow * width + i, err);
+            ga[h] = __fadd_rn(ga[h], __fmul_rn(gw, x));
+            ua[h] = __fadd_rn(ua[h], __fmul_rn(uw, x));
+        }
+    float gsum = tree64(ga[0], ga[1]);
+    float usum = tree64(ua[0], ua[1]);
+    if (t == 0) Hidden.set((long long)token * ff + row, __fmul_rn(ref_silu(gsum), usum), err);
+}
+
+// kernels/strata.cu:56-69
+__global__ void k_q2_down(Grid g, FB Hidden, UB Blob, FB Scales, IB Mapping, FB Y, int width, int ff, int tokens, int mapped,
+                          int expanded, int outputOffset, int codeOffset, int scaleOffset, unsigned *err) {
+    unsigned row, token, z;
+    if (!my_group(g, row, token, z)) return;
+    if (!((int)row < width && (int)token < tokens)) return;
+    int t = threadIdx.x & 31;
+    float acc[2] = {0.0f, 0.0f};
+    for (int i0 = t; i0 < ff; i0 += STRATA_LANES)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int i = i0 + 32 * h;
+            if (i >= ff) continue;
+            long long index = (long long)row * ff + i;
+            int code = code_of(Blob, codeOffset, index, err);
+            long long si = scaleOffset + index / 64;
+            float w = __fmul_rn((float)code, expanded != 0 ? Scales.get(si, err) : half_of(Blob, si, err));
+            acc[h] = __fadd_rn(acc[h], __fmul_rn(w, Hidden.get((long long)token * ff + i, err)));
+        }
+    float r = tree64(acc[0], acc[1]);
+    long long destination = mapped != 0 ? Mapping.get(2LL * token + 1, err) : (long long)token;
+    if (t == 0) Y.set(outputOffset + destination * width + row, r, err);
+}
+
+}  // namespace
+
+namespace {
+// kernels/strata.cu:238-270 and :478-509. Logits are staged in shared memory per warp.
+__global__ void k_router_batch(Grid g, FB Logits, IB Ids, FB Weights, int experts, int topK, int batch, unsigned *err) {
+    __shared__ float lg[kWarpsPerBlock][512];
+    __shared__ float sel[kWarpsPerBlock][32];
+    __shared__ int ids[kWarpsPerBlock][32];
+    __shared__ float wts[kWarpsPerBlock][32];
+    unsigned token, y, z;
+    if (!my_group(g, token, y, z)) return;
+    if (!batch && (token | y | z)) return;  // strata_router: every workgroup computes token 0 (one is enough)
+    if (batch && (y | z)) return;           // strata_router_batch: blockIdx.x is the token
+    int w = (threadIdx.x / 32) % kWarpsPerBlock, t = threadIdx.x & 31;
+    for (int e = t; e < experts; e += 32) lg[w][e] = Logits.get((long long)token * experts + e, err);
+    __syncwarp();
+    route_warp(lg[w], experts, topK, ids[w], wts[w], sel[w]);
+    for (int k = t; k < topK; k += 32) {
+        Ids.set((long long)token * topK + k, ids[w][k], err);
+        Weights.set((long long)token * topK + k, wts[w][k], err);
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+
+inline Grid grid_of(const unsigned g[3]) { return Grid{g[0], g[1], g[2]}; }
+inline unsigned group_blocks(const unsigned g[3]) {
+    unsigned long long total = (unsigned long long)g[0] * g[1] * g[2];
+    return (unsigned)((total + kWarpsPerBlock - 1) / kWarpsPerBlock);
+}
+inline unsigned lane_blocks(const unsigned g[3]) { return (unsigned)(((unsigned long long)g[0] * STRATA_LANES + 255) / 256); }
+
+#define F(i) FB{(float *)a[i].ptr, a[i].len}
+#define U(i) UB{(unsigned *)a[i].ptr, a[i].len}
+#define I(i) IB{(int *)a[i].ptr, a[i].len}
+#define GROUPS group_blocks(g), kWarpsPerBlock * 32, 0, s
+#define LANESL lane_blocks(g), 256, 0, s
+
+cudaError_t L_unpack_half(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_unpack_half<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_expert_scales(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_expert_scales<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, a[3].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_q2_gate_up(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_q2_gate_up<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_q2_down(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_q2_down<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, a[12].i,
+                          err);
+    return cudaGetLastError();
+}
+cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_project<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_bf16_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_bf16_project<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_q2_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_q2_project<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i,
+                             err);
+    return cudaGetLastError();
+}
+cudaError_t L_quant_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_quant_project<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i,
+                                a[12].i, a[13].i, a[14].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_elementwise(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_elementwise<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].f, err);
+    return cudaGetLastError();
+}
+cudaError_t L_router(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_router_batch<<<1, kWarpsPerBlock * 32, 0, s>>>(Grid{1, 1, 1}, F(0), I(1), F(2), a[3].i, a[4].i, 0, err);
+    return cudaGetLastError();
+}
+cudaError_t L_router_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_router_batch<<<GROUPS>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, 1, err);
+    return cudaGetLastError();
+}
+cudaError_t L_moe_combine(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_moe_combine<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), a[5].i, a[6].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_moe_combine_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_moe_combine_batch<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_gather_rows(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_gather_rows<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_scatter_rows(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_scatter_rows<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, err);
+    return cudaGetLastError();
+}
+}  // namespace
+
+// Parameter lists in kernels/strata.cu order and spelling. Kinds: 'f' float buffer, 'u' u32
+// buffer, 'i' i32 buffer, 'I' i32 scalar, 'F' f32 scalar.
+const KernelSpec kKernels[] = {
+    {"strata_unpack_half", "Packed:u Values:f count:I", L_unpack_half},
+    {"strata_expert_scales", "Blob:u Scales:f offset:I count:I", L_expert_scales},
+    {"strata_q2_gate_up",
+     "X:f Blob:u Scales:f Mapping:i Hidden:f width:I ff:I tokens:I mapped:I expanded:I codeOffset:I scaleOffset:I", L_q2_gate_up},
+    {"strata_q2_down",
+     "Hidden:f Blob:u Scales:f Mapping:i Y:f width:I ff:I tokens:I mapped:I expanded:I outputOffset:I codeOffset:I scaleOffset:I",
+     L_q2_down},
+    {"strata_project", "X:f W:f Y:f cols:I rows:I tokens:I outputStride:I outputOffset:I", L_project},
+    {"strata_bf16_project", "X:f Codes:u Y:f cols:I rows:I tokens:I outputStride:I outputOffset:I", L_bf16_project},
+    {"strata_q2_project",
+     "X:f Blob:u Y:f cols:I rows:I tokens:I outputStride:I outputOffset:I codeOffset:I scaleOffset:I weightRow:I rowStride:I",
+     L_q2_project},
+    {"strata_quant_project",
+     "X:f Codes:u Scales:f Offsets:f Y:f cols:I rows:I tokens:I outputStride:I outputOffset:I bits:I groupSize:I bias:I codebook:I "
+     "hasOffset:I",
+     L_quant_project},
+    {"strata_elementwise", "A:f B:f Y:f n:I mode:I scale:F", L_elementwise},
+    {"strata_router", "Logits:f Ids:i Weights:f experts:I topK:I", L_router},
+    {"strata_router_batch", "Logits:f Ids:i Weights:f experts:I topK:I", L_router_batch},
+    {"strata_moe_combine", "Parts:f Weights:f Shared:f SharedGate:f Y:f width:I count:I", L_moe_combine},
+    {"strata_moe_combine_batch", "Parts:f Weights:f Shared:f SharedGate:f Y:f width:I count:I tokens:I", L_moe_combine_batch},
+    {"strata_gather_rows", "X:f Indices:i Y:f width:I rows:I", L_gather_rows},
+    {"strata_scatter_rows", "X:f Indices:i Y:f width:I rows:I", L_scatter_rows},
+};
+const int kNumKernels = sizeof(kKernels) / sizeof(kKernels[0]);
+
+}  // namespace strata

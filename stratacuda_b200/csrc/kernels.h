@@ -1,0 +1,70 @@
+// Internal interface between the C-ABI layer (api.cu) and the kernel files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace strata {
+
+// Device-side error word bits (set with atomicOr, read by the host at the next sync).
+enum : unsigned {
+    kErrIndex = 1u,        // a data-dependent index (mapping, gather index, expert id) was out of range
+    kErrWaitTimeout = 2u,  // a bounded spin-wait gave up
+    kErrRouting = 4u,      // a routed expert id was invalid or repeated (src/engine.js:138)
+};
+
+// One resolved argument of a reference-compatible dispatch: a device buffer (ptr, length in
+// 4-byte elements) or a scalar.
+struct KArg {
+    void *ptr;
+    long long len;
+    int i;
+    float f;
+};
+using Launcher = cudaError_t (*)(const KArg *args, const unsigned groups[3], cudaStream_t s, unsigned *err);
+struct KernelSpec {
+    const char *name;
+    const char *params;  // "Name:kind ..." with kind f/u/i (buffers) or I/F (scalars)
+    Launcher launch;
+};
+extern const KernelSpec kKernels[];
+extern const int kNumKernels;
+
+// Device view of one mixture-of-experts layer (see strata_moe_layer in include/strata_cuda.h).
+struct MoeLayerDev {
+    int width, ff, experts, topK;
+    const float *router;       // [experts][width] f32
+    const float *bias;         // [experts] f32 or null
+    const unsigned *blobs;     // experts x blob_words
+    long long blob_words;
+    const unsigned *shared_blob;  // blob_words
+    const float *shared_gate;     // [width] f32
+};
+
+// Scratch for one fused call, carved from the context's workspace.
+struct MoeScratch {
+    float *logits;      // [tokens][experts]
+    float *sg;          // [tokens]
+    int *counts;        // [experts]
+    int *active;        // [experts]
+    int *n_active;      // [1]
+    int *begin;         // [experts + 1]
+    int *pair_token;    // [tokens * topK]
+    int *pair_slot;     // [tokens * topK]
+    float *hidden;      // [(tokens * topK + tokens) * ff]
+    float *parts;       // [tokens * topK * width]
+    float *shared_out;  // [tokens * width]
+};
+size_t moe_scratch_bytes(int tokens, int width, int ff, int experts, int topK);
+MoeScratch moe_scratch_carve(void *base, int tokens, int width, int ff, int experts, int topK);
+
+// Fused layer: y[tokens][width], ids/weights[tokens][topK]. Exact reduction order everywhere.
+cudaError_t moe_forward_exact(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights,
+                              const MoeScratch &ws, cudaStream_t s, unsigned *err);
+
+// Device synthetic generator (csrc/synth.cu), same bytes as stratacuda_b200/synth.py.
+cudaError_t synth_expert_blobs(unsigned *out, unsigned long long seed, int layer, int first_expert, int count, int width, int ff,
+                               int shared, cudaStream_t s);
+cudaError_t synth_normals_f32(float *out, unsigned long long key, long long start, long long count, double scale, cudaStream_t s);
+unsigned long long synth_stream_key(unsigned long long seed, unsigned long long tag, unsigned long long sub);
+
+}  // namespace strata
