@@ -126,6 +126,33 @@ typedef struct {
 int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                        strata_buf weights, int32_t mode);
 
+/* ---- allocation-free fused layer ----
+ * No counterpart in the reference. For callers that must not allocate device memory: a host
+ * engine that has already carved HBM into its own arenas and forbids allocations behind its
+ * accounting; code running during CUDA stream capture, where cudaMalloc is not allowed;
+ * processes that may not grow their device footprint. strata_moe_forward grows a workspace
+ * with cudaMalloc. This variant takes caller-owned device pointers and a stream (a
+ * cudaStream_t as void*; NULL = the default stream), computes exactly what
+ * strata_moe_forward computes in mode STRATA_MOE_EXACT, and keeps all temporaries in one
+ * static device array of STRATA_NOALLOC_SCRATCH_BYTES compiled into the library.
+ *  - Calls needing more scratch are rejected with STRATA_ERR_RANGE (up to 73 tokens at
+ *    H 2048 / E 512 / k 10 / F 512).
+ *  - The first call on each device looks the array's address up, so make it before any
+ *    stream capture.
+ *  - Calls share the array: calls that overlap on the GPU race, so order them on one stream.
+ *  - Never allocates or frees. `msg` (optional) receives the reason for a non-zero status. */
+#define STRATA_NOALLOC_SCRATCH_BYTES (8u << 20)
+typedef struct {
+    int32_t width, ff, experts, top_k;   /* as in strata_moe_layer */
+    const float *router;                 /* device f32 [experts * width] */
+    const float *router_bias;            /* device f32 [experts], or NULL */
+    const uint32_t *experts_blob;        /* device u32: experts Q2 blobs */
+    const uint32_t *shared_blob;         /* device u32: one Q2 blob */
+    const float *shared_gate;            /* device f32 [width] */
+} strata_moe_layer_dev;
+int strata_moe_forward_noalloc(const strata_moe_layer_dev *layer, const float *x, int32_t tokens, float *y, int32_t *ids,
+                               float *weights, void *stream, char *msg, size_t msg_cap);
+
 /* ---- seeded synthetic workload (device generator; same bytes as stratacuda_b200/synth.py) ---- */
 /* `count` expert blobs of one layer starting at `first_expert` into buf at element offset. */
 int strata_synth_blobs(strata_ctx *ctx, strata_buf buf, uint64_t offset, uint64_t seed, int32_t layer, int32_t first_expert,

@@ -30,6 +30,12 @@ class StrataMoeLayer(C.Structure):
                 ("shared_blob", C.c_uint64), ("shared_gate", C.c_uint64)]
 
 
+class StrataMoeLayerDev(C.Structure):
+    _fields_ = [("width", C.c_int32), ("ff", C.c_int32), ("experts", C.c_int32), ("top_k", C.c_int32),
+                ("router", C.c_void_p), ("router_bias", C.c_void_p), ("experts_blob", C.c_void_p),
+                ("shared_blob", C.c_void_p), ("shared_gate", C.c_void_p)]
+
+
 SIGNATURES = {
     "strata_create": ([_i, C.POINTER(_vp)], _i),
     "strata_destroy": ([_vp], _i),
@@ -47,6 +53,7 @@ SIGNATURES = {
     "strata_flush": ([_vp], _i),
     "strata_info": ([_vp, C.c_char_p, _sz], _i),
     "strata_moe_forward": ([_vp, C.POINTER(StrataMoeLayer), _u64, C.c_int32, _u64, _u64, _u64, C.c_int32], _i),
+    "strata_moe_forward_noalloc": ([C.POINTER(StrataMoeLayerDev), _vp, C.c_int32, _vp, _vp, _vp, _vp, C.c_char_p, _sz], _i),
     "strata_synth_blobs": ([_vp, _u64, _u64, _u64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32], _i),
     "strata_synth_normals": ([_vp, _u64, _u64, _u64, _u64, _u64, _u64, _u64, _d], _i),
 }

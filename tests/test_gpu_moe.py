@@ -1,0 +1,192 @@
+"""The fused mixture-of-experts layer (strata_moe_forward) on the GPU against the reference:
+golden layers from the reference's compiled kernels, the oracle on seeded BASELINE-shaped
+inputs (decode B = 1, 8, 64; prefill T = 4096 with Zipf skew on sampled tokens), and the
+reference's own host dispatch order through strata_run."""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+WIDTH, FF, EXPERTS, TOPK = 2048, 512, 512, 10
+
+
+@pytest.fixture(scope="module")
+def b():
+    from stratacuda_b200.backend import CudaBackend
+    be = CudaBackend(0)
+    yield be
+    be.dispose()
+
+
+@pytest.fixture(scope="module")
+def layer(b):
+    from stratacuda_b200.moe import MoeLayer
+    L = MoeLayer.synthesize(b, seed=1, layer=0, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK)
+    yield L
+    L.free()
+
+
+def bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+def run_fused(b, L, x_host=None, x_buf=None, tokens=None):
+    x = x_buf if x_buf is not None else b.alloc(np.ascontiguousarray(x_host, np.float32).reshape(-1))
+    T = tokens if tokens is not None else x_host.shape[0]
+    y, ids, w = b.alloc(T * L.width), b.alloc(T * L.top_k, "i32"), b.alloc(T * L.top_k)
+    L.forward(x, T, y, ids, w)
+    out = b.read(y).reshape(T, L.width), b.read(ids).reshape(T, L.top_k), b.read(w).reshape(T, L.top_k)
+    for buf in (y, ids, w) + (() if x_buf is not None else (x,)):
+        b.free(buf)
+    return out
+
+
+def test_device_generator_matches_numpy(b, layer):
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import synth_activations
+    words = layer.blob_words
+    for e in (0, 3, 511):
+        got = b.read(layer.experts_blob, count=words, offset=e * words)
+        assert np.array_equal(got, synth.expert_blob(1, 0, e, WIDTH, FF)), e
+    assert np.array_equal(b.read(layer.shared_blob), synth.expert_blob(1, 0, 0, WIDTH, FF, shared=True))
+    assert np.array_equal(bits(b.read(layer.router)), bits(synth.router_weights(1, 0, EXPERTS, WIDTH).reshape(-1)))
+    assert np.array_equal(bits(b.read(layer.shared_gate)), bits(synth.shared_gate(1, 0, WIDTH)))
+    x = synth_activations(b, 2, 3, WIDTH, start_token=5)
+    assert np.array_equal(bits(b.read(x)), bits(synth.activations(2, 3, WIDTH, start_token=5).reshape(-1)))
+
+
+def test_fused_small_layer_bit_exact(b, golden):
+    from stratacuda_b200.moe import MoeLayer
+    g = golden["moe_small"]
+    L = MoeLayer.upload(b, g["router"], g["blobs"], g["shared_blob"], g["shared_gate"], int(g["top_k"]), g["bias"])
+    y, ids, w = run_fused(b, L, g["x"])
+    assert np.array_equal(ids, g["ids_ref"])
+    assert np.array_equal(bits(w), bits(g["weights_ref"]))
+    assert np.array_equal(bits(y), bits(g["y_ref"]))
+    L.free()
+
+
+@pytest.mark.parametrize("name", ["decode", "prefill"])
+def test_fused_config_geometry_bit_exact(b, layer, golden, name):
+    from stratacuda_b200 import synth
+    g = golden["moe_config"]
+    x = synth.activations(int(g[f"{name}_xseed"]), 2, WIDTH)
+    zipf = float(g[f"{name}_zipf"])
+    bias = None
+    if zipf > 0:
+        bias = b.alloc(synth.zipf_bias(1, EXPERTS, zipf))
+        layer.router_bias = bias
+    try:
+        y, ids, w = run_fused(b, layer, x)
+    finally:
+        layer.router_bias = None
+        if bias is not None:
+            b.free(bias)
+    assert np.array_equal(ids, g[f"{name}_ids_ref"])
+    assert np.array_equal(bits(w), bits(g[f"{name}_weights_ref"]))
+    assert np.array_equal(bits(y), bits(g[f"{name}_y_ref"]))
+
+
+@pytest.mark.parametrize("B", [1, 8, 64])
+def test_fused_decode_batches_vs_oracle(b, layer, port, B):
+    from oracle.oracle import moe_layer_port, route_port
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import synth_activations
+    x_buf = synth_activations(b, 2 + B, B, WIDTH)
+    y, ids, w = run_fused(b, layer, x_buf=x_buf, tokens=B)
+    x = synth.activations(2 + B, B, WIDTH)
+    router = synth.router_weights(1, 0, EXPERTS, WIDTH)
+    _, ids_o, w_o = route_port(port, x, router, TOPK)
+    assert np.array_equal(ids, ids_o)  # routing bit-exact for every token
+    assert np.array_equal(bits(w), bits(w_o))
+    sample = sorted(set([0, B - 1, B // 2]))
+    words = layer.blob_words
+    blobs = np.zeros((EXPERTS, words), np.uint32)
+    for e in sorted(set(ids_o[sample].reshape(-1).tolist())):
+        blobs[e] = synth.expert_blob(1, 0, e, WIDTH, FF)
+    y_o, _, _ = moe_layer_port(port, x, router, synth.shared_gate(1, 0, WIDTH), blobs, synth.expert_blob(1, 0, 0, WIDTH, FF, True),
+                               TOPK, tokens=sample)
+    assert np.array_equal(bits(y[sample]), bits(y_o[sample]))
+    assert rel_l2(y[sample], y_o[sample]) <= 1e-5  # the decode-path tolerance, met with margin (0)
+    b.free(x_buf)
+
+
+def test_reference_dispatch_order_equals_fused(b, golden):
+    """src/engine.js:133-156 and src/prefill.js:52-78 issued through strata_run give the same bits."""
+    from stratacuda_b200.moe import MoeLayer, moe_decode_reference_order, moe_prompt_reference_order
+    g = golden["moe_small"]
+    L = MoeLayer.upload(b, g["router"], g["blobs"], g["shared_blob"], g["shared_gate"], int(g["top_k"]), g["bias"])
+    x = g["x"]
+    for t in range(x.shape[0]):
+        xb = b.alloc(x[t].copy())
+        y, ids, w = moe_decode_reference_order(b, L, xb)
+        assert np.array_equal(b.read(ids), g["ids_ref"][t])
+        assert np.array_equal(bits(b.read(y)), bits(g["y_ref"][t]))
+        for buf in (xb, y, ids, w):
+            b.free(buf)
+    xb = b.alloc(x.reshape(-1).copy())
+    y, ids, w = moe_prompt_reference_order(b, L, xb, x.shape[0])
+    assert np.array_equal(b.read(ids).reshape(x.shape[0], -1), g["ids_ref"])
+    assert np.array_equal(bits(b.read(w)), bits(g["weights_ref"].reshape(-1)))
+    assert np.array_equal(bits(b.read(y)), bits(g["y_ref"].reshape(-1)))
+    L.free()
+
+
+def test_fused_prefill_4096_zipf_sampled(b, layer, port):
+    """BASELINE config 3 (T = 4096, Zipf(1.1) offsets): every token's routing against the oracle
+    on a sample, outputs on a smaller sample, and size-independent properties for all tokens."""
+    from oracle.oracle import moe_layer_port, route_port
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import synth_activations
+    T = 4096
+    bias_h = synth.zipf_bias(1, EXPERTS, 1.1)
+    layer.router_bias = b.alloc(bias_h)
+    try:
+        x_buf = synth_activations(b, 3, T, WIDTH)
+        y, ids, w = run_fused(b, layer, x_buf=x_buf, tokens=T)
+        b.free(x_buf)
+    finally:
+        b.free(layer.router_bias)
+        layer.router_bias = None
+    # properties over all tokens: distinct ids in range, weights renormalised to 1
+    assert ((ids >= 0) & (ids < EXPERTS)).all()
+    assert all(len(set(r)) == TOPK for r in ids.tolist())
+    assert np.allclose(w.sum(1), 1.0, atol=1e-5)
+    assert np.isfinite(y).all()
+    # skew: the most loaded expert carries far more than the uniform share
+    counts = np.bincount(ids.reshape(-1), minlength=EXPERTS)
+    assert counts.max() > 8 * T * TOPK / EXPERTS
+    rng = np.random.default_rng(0)
+    sample = sorted(rng.choice(T, 24, replace=False).tolist())
+    x = synth.activations(3, T, WIDTH)
+    router = synth.router_weights(1, 0, EXPERTS, WIDTH)
+    _, ids_o, w_o = route_port(port, x, router, TOPK, bias_h, tokens=sample)
+    assert np.array_equal(ids[sample], ids_o[sample])
+    assert np.array_equal(bits(w[sample]), bits(w_o[sample]))
+    few = sample[:4]
+    blobs = np.zeros((EXPERTS, layer.blob_words), np.uint32)
+    for e in sorted(set(ids_o[few].reshape(-1).tolist())):
+        blobs[e] = synth.expert_blob(1, 0, e, WIDTH, FF)
+    y_o, _, _ = moe_layer_port(port, x, router, synth.shared_gate(1, 0, WIDTH), blobs, synth.expert_blob(1, 0, 0, WIDTH, FF, True),
+                               TOPK, bias_h, tokens=few)
+    assert np.array_equal(bits(y[few]), bits(y_o[few]))
+
+
+def test_fused_rejects_bad_layouts(b, layer):
+    from stratacuda_b200.backend import StrataError, StrataRangeError
+    x, y = b.alloc(WIDTH), b.alloc(WIDTH)
+    ids, w = b.alloc(TOPK, "i32"), b.alloc(TOPK)
+    with pytest.raises(StrataError, match="x holds"):
+        layer.forward(x, 2, y, ids, w)
+    with pytest.raises(StrataRangeError, match="tokens"):
+        layer.forward(x, 0, y, ids, w)
+    k = layer.top_k
+    layer.top_k = 33
+    with pytest.raises(StrataRangeError, match="topK"):
+        layer.forward(x, 1, y, ids, w)
+    layer.top_k = k
+    for buf in (x, y, ids, w):
+        b.free(buf)
+    b.idle()
