@@ -1,0 +1,335 @@
+"""Benchmark of the mixture-of-experts hot path on B200 (driver contract: one JSON line).
+
+Workload (the metric's decode b=1 case): one MoE layer, H 2048, 512
+routed experts, top-10 renormalised routing, one shared expert, expert intermediate 512,
+Q2 packed blobs (uniform 2-bit codes, FP16 scales |N(0,0.02)|), F32 router N(0,0.02),
+F32 activations N(0,1); seeded synthetic data. A step is one pass of the fused layer over
+one batch. Steps cycle over `--layers` distinct layer replicas (default 24: every layer's
+routed weights are evicted from the 126 MB L2 before the layer comes round again) with a
+fresh activation batch per step, so no step reads weights left in L2 by the previous one.
+
+  value   device time (CUDA events on the library's stream) of K fused steps, inputs
+          resident in HBM; whole-job tokens/s (sum over ranks / max time over ranks).
+  e2e     the same steps through the C-ABI with host buffers: strata_write of the batch
+          from pinned memory, strata_moe_forward, strata_read of y, host-timed.
+  roofline  algorithmic bytes of each step (the U+1 distinct expert blobs actually routed,
+          router rows, shared gate, activations in and out) over the measured step time,
+          against the measured HBM copy bandwidth.
+  cpu_baseline / --impl reference  the reference's own kernels/strata.cu compiled natively
+          (oracle/_ref, WASM-path host order, 8 threads) on a bounded sample of the same
+          workload; falls back to the C restatement when the native build is absent.
+
+Multi-GPU: every rank runs its own replica of the layer stack (the reference has no
+multi-GPU path; see DESIGN.md for the expert-parallel plan); scaling is weak.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s (decode b=1 %HBM BW; prefill %TC peak) at 1/2/4/8 B200"
+WIDTH, FF, EXPERTS, TOPK = 2048, 512, 512, 10
+BLOB_BYTES = 884_736
+ROUTER_BYTES = EXPERTS * WIDTH * 4
+GATE_BYTES = WIDTH * 4
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        rows = [l.split(", ") for l in self.lines if l.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def dist_max(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dist_barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------- CPU reference leg
+
+def cpu_reference_sample(budget_s: float = 12.0, max_tokens: int = 64):
+    """Time the reference's CPU path (oracle/_ref, WASM-path order, 8 threads) on decode tokens
+    of the bench's own layer 0 until the time budget is spent. Returns (tokens/s, info)."""
+    from oracle.oracle import Oracle, moe_layer_port, moe_layer_wasm_path, route_port
+    from stratacuda_b200 import synth
+    try:
+        o = Oracle("reference", threads=8)
+        kind, cores = "reference", 8
+    except (FileNotFoundError, OSError):
+        o = Oracle("port")
+        kind, cores = "port", 1
+    router = synth.router_weights(1, 0, EXPERTS, WIDTH)
+    gate = synth.shared_gate(1, 0, WIDTH)
+    shared = synth.expert_blob(1, 0, 0, WIDTH, FF, shared=True)
+    words = shared.size
+    blobs = np.zeros((EXPERTS, words), np.uint32)
+    filled = set()
+    port = Oracle("port")
+    done, spent = 0, 0.0
+    while done < max_tokens and spent < budget_s:
+        x = synth.activations(2, 1, WIDTH, start_token=done)
+        _, ids, _ = route_port(port, x, router, TOPK)
+        for e in set(ids.reshape(-1).tolist()) - filled:
+            blobs[e] = synth.expert_blob(1, 0, e, WIDTH, FF)
+            filled.add(e)
+        t0 = time.perf_counter()
+        if kind == "reference":
+            moe_layer_wasm_path(o, x, router, gate, blobs, shared, TOPK)
+        else:
+            moe_layer_port(o, x, router, gate, blobs, shared, TOPK)
+        spent += time.perf_counter() - t0
+        done += 1
+    return done / spent, {"kind": kind, "cores": cores, "tokens": done, "seconds": round(spent, 3)}
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    steps, warm = args.steps, args.warmup
+    # a step is one decode token through the reference's CPU path; bound the whole run
+    per_step_budget = max(0.5, min(4.0, 150.0 / max(1, steps + warm)))
+    rate_w, _ = cpu_reference_sample(budget_s=per_step_budget * warm, max_tokens=max(1, warm))
+    rate, info = cpu_reference_sample(budget_s=per_step_budget * steps, max_tokens=max(1, steps))
+    line = {"metric": METRIC, "value": rate, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus, "steps": info["tokens"],
+            "warmup": warm, "ms_per_step": 1000.0 / rate, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded)", "config": workload_config(1, args.layers),
+            "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": info["cores"], "kind": info["kind"],
+                             "sample": f"{info['tokens']} decode tokens (B=1) of layer 0, WASM-path order, {info['seconds']} s"},
+            "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(batch: int, layers: int):
+    return {"workload": f"MoE layer decode b={batch} (H2048, E512 top-10, F512, Q2 experts + shared expert)", "batch": batch,
+            "hidden": WIDTH, "experts": EXPERTS, "top_k": TOPK, "ff": FF, "layers_cycled": layers,
+            "l2": "inputs larger than L2: distinct layer replicas cycled, fresh activations per step", "parallelism": "replicas"}
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def run_gpu_arm(args, world, rank, local):
+    import torch
+
+    from stratacuda_b200.backend import CudaBackend
+    from stratacuda_b200.moe import MoeLayer, synth_activations
+
+    torch.cuda.set_device(local)
+    b = CudaBackend(local)
+    B, K, W, NL = args.batch, args.steps, args.warmup, args.layers
+    layers = [MoeLayer.synthesize(b, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK) for l in range(NL)]
+    n_x = K + W
+    x_all = synth_activations(b, 2 + rank, n_x * B, WIDTH)
+    y_all = b.alloc(n_x * B * WIDTH, zero=False)
+    ids_all = b.alloc(n_x * B * TOPK, "i32")
+    w_all = b.alloc(n_x * B * TOPK, zero=False)
+    b.idle()
+
+    # views into the per-step slices: the fused call takes whole buffers, so give it
+    # per-step buffers that alias nothing (copy-free: a dedicated buffer per step)
+    xs = [b.alloc(B * WIDTH, zero=False) for _ in range(n_x)]
+    for s in range(n_x):
+        b.copy(x_all, xs[s], B * WIDTH, s * B * WIDTH, 0)
+    ys = [b.alloc(B * WIDTH, zero=False) for _ in range(n_x)]
+    idss = [b.alloc(B * TOPK, "i32") for _ in range(n_x)]
+    wss = [b.alloc(B * TOPK, zero=False) for _ in range(n_x)]
+    b.idle()
+
+    stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", local))
+    from stratacuda_b200 import _lib as LL
+    mode = LL.MOE_FAST if args.mode == "fast" else LL.MOE_EXACT
+    launches = 1 if (mode == LL.MOE_FAST and B <= 8) else 6
+    for s in range(W):
+        layers[s % NL].forward(xs[s], B, ys[s], idss[s], wss[s], mode=mode)
+    b.idle()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for s in range(W, W + K):
+            layers[s % NL].forward(xs[s], B, ys[s], idss[s], wss[s], mode=mode)
+        end.record(stream)
+        b.idle()
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    ms = start.elapsed_time(end)
+    ms_max = dist_max(ms, world)
+    # algorithmic bytes per step from the routing that actually happened
+    bytes_steps = []
+    for s in range(W, W + K):
+        ids = b.read(idss[s])
+        U = len(set(ids.tolist()))
+        bytes_steps.append((U + 1) * BLOB_BYTES + ROUTER_BYTES + GATE_BYTES + 2 * B * WIDTH * 4)
+    alg_bytes = float(np.mean(bytes_steps))
+    step_s = ms / 1000.0 / K
+    hbm_peak, peak_kind = peaks()
+    achieved = alg_bytes / step_s / 1e9
+
+    # end to end through the C-ABI with host buffers (pinned), host-timed
+    e2e_steps = min(K, max(20, K // 2))
+    hx = torch.empty(e2e_steps, B * WIDTH, dtype=torch.float32, pin_memory=True)
+    hx.copy_(torch.from_numpy(b.read(x_all, count=e2e_steps * B * WIDTH).reshape(e2e_steps, B * WIDTH)))
+    hy = torch.empty(B * WIDTH, dtype=torch.float32, pin_memory=True)
+    hx_np, hy_np = hx.numpy(), hy.numpy()
+    lib, ctx = b.lib, b.ctx
+    xbuf, ybuf = xs[0], ys[0]
+    for s in range(3):
+        b.write(xbuf, hx_np[s])
+        layers[s % NL].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
+        b._check(lib.strata_read(ctx, ybuf.handle, hy_np.ctypes.data, B * WIDTH, 0))
+    dist_barrier(world)
+    t0 = time.perf_counter()
+    for s in range(e2e_steps):
+        b.write(xbuf, hx_np[s])
+        layers[s % NL].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
+        b._check(lib.strata_read(ctx, ybuf.handle, hy_np.ctypes.data, B * WIDTH, 0))
+    e2e_s = time.perf_counter() - t0
+    e2e_s = dist_max(e2e_s, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, info = cpu_reference_sample(budget_s=args.cpu_seconds)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": info["cores"], "kind": info["kind"],
+               "sample": f"{info['tokens']} decode tokens (B=1) of layer 0 through the reference's WASM-path order, "
+                         f"{info['seconds']} s on {info['cores']} host threads"}
+
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get(f"decode_b{B}")
+
+    total_tokens = B * K * world
+    line = {"metric": METRIC, "value": total_tokens / (ms_max / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded SplitMix64; BASELINE config 2 distributions)",
+            "config": workload_config(B, NL),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                         "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": ("k_moe_fast (one persistent launch per step)" if launches == 1
+                                    else "fused exact MoE layer (6 launches per step)"),
+                         "algorithmic_bytes_per_step": alg_bytes},
+            "e2e": {"value": B * e2e_steps * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * WIDTH * 4,
+                    "d2h_bytes_per_step": B * WIDTH * 4},
+            "gpu_launches": launches * K,
+            "clocks": clocks.summary()}
+    if cpu:
+        line["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for L in layers:
+        L.free()
+    b.dispose()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="strata", choices=["strata", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=24)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", default="fast", choices=["fast", "exact"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference_arm(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_gpu_arm(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

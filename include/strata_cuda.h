@@ -121,8 +121,13 @@ typedef struct {
  * routed ids (i32 [tokens * top_k]) and weights (f32 [tokens * top_k]). Routing is
  * bit-identical to strata_router_batch; y follows the reference's combine order.
  *   mode 0: exact — every dot product in the reference's reduction order (bit-identical y).
+ *   mode 1: fast — one persistent tensor-core launch for decode batches (tokens <= 8 at
+ *           H/F = 2048/512 or 2560/640; other shapes run the exact mode). Routing is still
+ *           bit-identical; y is within 1e-5 relative L2 and, being accumulated with atomics,
+ *           not bit-reproducible from run to run.
  * Stream-ordered; does not synchronise. */
 #define STRATA_MOE_EXACT 0
+#define STRATA_MOE_FAST 1
 int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                        strata_buf weights, int32_t mode);
 

@@ -14,7 +14,7 @@ LIB_PATH = pathlib.Path(os.environ.get("STRATA_CUDA_LIB", PKG / "libstrata_cuda.
 OK, ERR_RANGE, ERR_LAYOUT, ERR_UNKNOWN, ERR_HANDLE, ERR_ALLOC, ERR_CUDA, ERR_DEVICE = range(8)
 F32, I32, U32 = 0, 1, 2
 ARG_BUF, ARG_I32, ARG_F32 = 0, 1, 2
-MOE_EXACT = 0
+MOE_EXACT, MOE_FAST = 0, 1
 
 # Every symbol the header declares, with its ctypes signature.
 _vp, _i, _u64, _sz, _d = C.c_void_p, C.c_int, C.c_uint64, C.c_size_t, C.c_double

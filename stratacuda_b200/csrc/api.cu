@@ -30,6 +30,7 @@ struct strata_ctx {
     uint64_t bytes_resident = 0;
     unsigned *err_dev = nullptr;   // device error word (kErr* bits)
     unsigned *err_host = nullptr;  // pinned mirror
+    unsigned *fast_sync = nullptr; // grid-arrival words of the fast fused kernel (self-resetting)
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
     uint64_t dispatches = 0, fused_calls = 0;
@@ -192,7 +193,8 @@ int strata_create(int device, strata_ctx **out) {
     if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&ctx->err_dev, sizeof(unsigned)) != cudaSuccess ||
         cudaHostAlloc(&ctx->err_host, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess ||
-        cudaMemset(ctx->err_dev, 0, sizeof(unsigned)) != cudaSuccess) {
+        cudaMemset(ctx->err_dev, 0, sizeof(unsigned)) != cudaSuccess || cudaMalloc(&ctx->fast_sync, 4 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(ctx->fast_sync, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
         strata_destroy(ctx);
         return STRATA_ERR_CUDA;
     }
@@ -214,6 +216,7 @@ int strata_destroy(strata_ctx *ctx) {
     ctx->buffers.clear();
     if (ctx->workspace) cudaFree(ctx->workspace);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
+    if (ctx->fast_sync) cudaFree(ctx->fast_sync);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -397,7 +400,8 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     if (l.experts < 1 || l.experts > 512 || l.top_k < 1 || l.top_k > std::min(l.experts, 32))
         return fail(ctx, STRATA_ERR_RANGE, "Router supports 1-512 experts and topK <= min(experts,32)");
     if (tokens < 1) return fail(ctx, STRATA_ERR_RANGE, "tokens must be an integer >= 1");
-    if (mode != STRATA_MOE_EXACT) return fail(ctx, STRATA_ERR_RANGE, "unknown mode %d", mode);
+    if (mode != STRATA_MOE_EXACT && mode != STRATA_MOE_FAST) return fail(ctx, STRATA_ERR_RANGE, "unknown mode %d", mode);
+    const bool fast = mode == STRATA_MOE_FAST && moe_fast_supported(tokens, l.width, l.ff, l.top_k, ctx->sms);
     const long long bw = blob_words_of(l.width, l.ff);
     struct Need {
         strata_buf h;
@@ -425,7 +429,8 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
         ptr[i] = b->ptr;
     }
     if (int r = use_device(ctx)) return r;
-    const size_t ws = moe_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k);
+    const size_t ws = fast ? moe_fast_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
+                           : moe_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k);
     if (ws > ctx->workspace_bytes) {
         CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "workspace resize");
         if (ctx->workspace) cudaFree(ctx->workspace);
@@ -440,9 +445,15 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     }
     MoeLayerDev L{l.width, l.ff, l.experts, l.top_k, (const float *)ptr[0], (const float *)ptr[1], (const unsigned *)ptr[2], bw,
                   (const unsigned *)ptr[3], (const float *)ptr[4]};
-    MoeScratch s = moe_scratch_carve(ctx->workspace, tokens, l.width, l.ff, l.experts, l.top_k);
-    cudaError_t e = moe_forward_exact(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], s, ctx->stream,
-                                      ctx->err_dev);
+    cudaError_t e;
+    if (fast) {
+        e = moe_forward_fast(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
+                             ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev);
+    } else {
+        MoeScratch s = moe_scratch_carve(ctx->workspace, tokens, l.width, l.ff, l.experts, l.top_k);
+        e = moe_forward_exact(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], s, ctx->stream,
+                              ctx->err_dev);
+    }
     if (e != cudaSuccess) return cuda_fail(ctx, e, "strata_moe_forward");
     ++ctx->fused_calls;
     return STRATA_OK;

@@ -35,8 +35,10 @@ __device__ __forceinline__ float half_bits(unsigned h) {
 // method: x*32/ln2 = k + r, 2^(k/32) from a 32-entry table, cubic in r, all in double
 // without fused multiply-add, rounded once to float. The table holds
 // bits(2^(i/32)) - (i << 47), computed from mathematics. Checked exhaustively on the host
-// against the C library's expf (oracle), and on the device against that oracle.
-static __constant__ unsigned long long c_exp2_tab[32] = {
+// against the C library's expf (oracle), and on the device against that oracle. The table
+// sits in global memory and is read through the L1 path: lanes index it divergently, which
+// the constant cache would serialise.
+static __device__ const unsigned long long c_exp2_tab[32] = {
     0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
     0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
     0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
@@ -53,28 +55,32 @@ __device__ __forceinline__ float ref_expf(float x) {
     const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0;
     const double c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0;
     const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
-    unsigned ux = __float_as_uint(x);
-    unsigned abstop = (ux >> 20) & 0x7ffu;
-    if (abstop >= 0x42bu) {
-        if (ux == 0xff800000u) return 0.0f;
-        if (abstop >= 0x7f8u) return __fadd_rn(x, x);
-        if (x > 0x1.62e42ep6f) return __uint_as_float(0x7f800000u);
-        if (x < -0x1.9fe368p6f) return 0.0f;
-    }
-    double xd = (double)x;
-    double z = __dmul_rn(inv_ln2_n, xd);
+    const unsigned ux = __float_as_uint(x);
+    const unsigned abstop = (ux >> 20) & 0x7ffu;
+    // Main path for every input (straight-line, so independent calls interleave); the rare
+    // |x| >= 88 / NaN / inf cases are selected afterwards, exactly as the branches of the
+    // published method resolve them.
+    const double xd = (double)x;
+    const double z = __dmul_rn(inv_ln2_n, xd);
     double kd = __dadd_rn(z, shift);
-    unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
+    const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
     kd = __dsub_rn(kd, shift);
-    double r = __dsub_rn(z, kd);
-    unsigned long long t = c_exp2_tab[ki & 31ull] + (ki << 47);
-    double s = __longlong_as_double((long long)t);
-    double p = __dadd_rn(__dmul_rn(c0, r), c1);
-    double r2 = __dmul_rn(r, r);
+    const double r = __dsub_rn(z, kd);
+    const unsigned long long t = __ldg(&c_exp2_tab[ki & 31ull]) + (ki << 47);
+    const double s = __longlong_as_double((long long)t);
+    const double p = __dadd_rn(__dmul_rn(c0, r), c1);
+    const double r2 = __dmul_rn(r, r);
     double y = __dadd_rn(__dmul_rn(c2, r), 1.0);
     y = __dadd_rn(__dmul_rn(p, r2), y);
     y = __dmul_rn(y, s);
-    return __double2float_rn(y);
+    const float main = __double2float_rn(y);
+    // selects, not branches: unrolled callers keep independent evaluations interleaved
+    float special = main;
+    special = x < -0x1.9fe368p6f ? 0.0f : special;
+    special = x > 0x1.62e42ep6f ? __uint_as_float(0x7f800000u) : special;
+    special = abstop >= 0x7f8u ? __fadd_rn(x, x) : special;
+    special = ux == 0xff800000u ? 0.0f : special;
+    return abstop < 0x42bu ? main : special;
 }
 
 // kernels/strata.cu:7-8

@@ -61,6 +61,14 @@ MoeScratch moe_scratch_carve(void *base, int tokens, int width, int ff, int expe
 cudaError_t moe_forward_exact(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights,
                               const MoeScratch &ws, cudaStream_t s, unsigned *err);
 
+// Fast fused layer for decode batches (csrc/moe_fast.cu): one cooperative launch of `grid`
+// CTAs (one per SM). `sync` is 4 zero-initialised words reserved for this kernel's grid
+// arrivals; the kernel leaves them zero again on exit.
+bool moe_fast_supported(int tokens, int width, int ff, int topK, int grid);
+size_t moe_fast_scratch_bytes(int tokens, int width, int ff, int experts, int topK);
+cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
+                             unsigned *sync, int grid, cudaStream_t s, unsigned *err);
+
 // Device synthetic generator (csrc/synth.cu), same bytes as stratacuda_b200/synth.py.
 cudaError_t synth_expert_blobs(unsigned *out, unsigned long long seed, int layer, int first_expert, int count, int width, int ff,
                                int shared, cudaStream_t s);
