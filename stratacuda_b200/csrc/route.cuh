@@ -90,4 +90,130 @@ __device__ __forceinline__ void route_warp(const float *logits, int experts, int
     __syncwarp();
 }
 
+
+// ---------------------------------------------------------------------------------------
+// The same routing for one token by a group of W consecutive warps (W in {1, 2, 4, 8}):
+// thread i of the group owns experts i + 32W m. Steps, each exact:
+//   max      order-free (fmaxf), so any partition gives the reference's value;
+//   exp      one ref_expf per expert, written back over the logits;
+//   sum      the reference's 64-lane order (lane l adds experts l, l+64, ... from 0, then the
+//            tree), recomputed by every warp of the group from shared memory;
+//   top-k    keys (probability bits + 1, inverted id) are a total order equal to the
+//            reference's selection order. The 512 keys form 8 subgroups of 64 (two per
+//            lane of one warp); each subgroup is bitonic-sorted and its first K keys become
+//            candidates. The global top K lie among them (an element beaten by fewer than K
+//            elements overall is beaten by fewer than K of its subgroup), and a candidate's
+//            rank is the number of candidates above it.
+//   weights  sel_k / max(sum_k sel_k, 2^-14), the sum in selection order.
+// `lg` holds the token's logits (512 floats; entries past `experts` are ignored) and is
+// overwritten. `red` holds W floats, `cand` 8*topK keys; ids/sel/weights receive topK
+// entries. Group synchronisation uses named barrier `bar_id` (W > 1).
+template <int W>
+__device__ __forceinline__ void group_sync(int bar_id) {
+    if (W == 1) __syncwarp();
+    else asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(32 * W) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int m) {
+    const unsigned lo = __shfl_xor_sync(0xffffffffu, (unsigned)v, m);
+    const unsigned hi = __shfl_xor_sync(0xffffffffu, (unsigned)(v >> 32), m);
+    return ((unsigned long long)hi << 32) | lo;
+}
+
+// Sorts 64 keys, element 2*lane + j in k_j, into descending order (bitonic network).
+__device__ __forceinline__ void warp_sort64_desc(unsigned long long &k0, unsigned long long &k1, int lane) {
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+        const bool desc = ((2 * lane) & size) == 0;  // direction of this element's block
+#pragma unroll
+        for (int stride = size >> 1; stride > 1; stride >>= 1) {
+            const unsigned long long o0 = shfl_xor_u64(k0, stride >> 1), o1 = shfl_xor_u64(k1, stride >> 1);
+            const bool take_max = (((2 * lane) & stride) == 0) == desc;  // lower element of a descending pair
+            k0 = take_max ? (k0 > o0 ? k0 : o0) : (k0 < o0 ? k0 : o0);
+            k1 = take_max ? (k1 > o1 ? k1 : o1) : (k1 < o1 ? k1 : o1);
+        }
+        const unsigned long long hi = k0 > k1 ? k0 : k1, lo = k0 > k1 ? k1 : k0;
+        k0 = desc ? hi : lo;
+        k1 = desc ? lo : hi;
+    }
+}
+
+template <int W>
+__device__ __forceinline__ void route_group(float *lg, int experts, int topK, float *red, unsigned long long *cand, int *ids,
+                                            float *sel, float *weights, int bar_id) {
+    constexpr int T = 32 * W, NPT = 512 / T;
+    const int i = threadIdx.x % T, lane = threadIdx.x & 31, wg = i >> 5;
+    float v[NPT];
+    float mx = -3.402823e38f;
+#pragma unroll
+    for (int m = 0; m < NPT; ++m) {
+        const int e = i + T * m;
+        v[m] = lg[e];
+        mx = fmaxf(mx, e < experts ? v[m] : -3.402823e38f);
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+    if (W > 1) {
+        if (lane == 0) red[wg] = mx;
+        group_sync<W>(bar_id);
+        mx = red[0];
+#pragma unroll
+        for (int k = 1; k < W; ++k) mx = fmaxf(mx, red[k]);
+    }
+#pragma unroll
+    for (int m = 0; m < NPT; ++m) {
+        const int e = i + T * m;
+        const float ex = ref_expf(__fsub_rn(v[m], mx));
+        v[m] = e < experts ? ex : 0.0f;
+        lg[e] = v[m];
+    }
+    group_sync<W>(bar_id);
+    float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+        sa = __fadd_rn(sa, lg[lane + 64 * m]);
+        sb = __fadd_rn(sb, lg[lane + 32 + 64 * m]);
+    }
+    const float inv = __fdiv_rn(1.0f, __shfl_sync(0xffffffffu, tree64(sa, sb), 0));
+#pragma unroll
+    for (int a = 0; a < NPT / 2; ++a) {
+        const int e0 = i + T * (2 * a), e1 = e0 + T;
+        const float p0 = __fmul_rn(v[2 * a], inv), p1 = __fmul_rn(v[2 * a + 1], inv);
+        unsigned long long k0 = e0 < experts && p0 >= 0.0f ? ((unsigned long long)(__float_as_uint(p0) + 1u) << 32) | (0xffffffffu - (unsigned)e0) : 0ull;
+        unsigned long long k1 = e1 < experts && p1 >= 0.0f ? ((unsigned long long)(__float_as_uint(p1) + 1u) << 32) | (0xffffffffu - (unsigned)e1) : 0ull;
+        warp_sort64_desc(k0, k1, lane);
+        unsigned long long *c = cand + (wg * (NPT / 2) + a) * topK;
+        if (2 * lane < topK) c[2 * lane] = k0;
+        if (2 * lane + 1 < topK) c[2 * lane + 1] = k1;
+    }
+    group_sync<W>(bar_id);
+    const int N = 8 * topK;
+    for (int c = i; c < N; c += T) {
+        const unsigned long long kc = cand[c];
+        if (kc == 0ull) continue;
+        int r = 0;
+        for (int c2 = 0; c2 < N; ++c2) r += cand[c2] > kc;
+        if (r < topK) {
+            ids[r] = (int)(0xffffffffu - (unsigned)kc);
+            sel[r] = __uint_as_float((unsigned)(kc >> 32) - 1u);
+        }
+    }
+    if (i < topK) {  // rounds past the last valid key find nothing: the reference records -1
+        int nz = 0;
+        for (int c2 = 0; c2 < N; ++c2) nz += cand[c2] != 0ull;
+        if (i >= nz) {
+            ids[i] = -1;
+            sel[i] = -1.0f;
+        }
+    }
+    group_sync<W>(bar_id);
+    if (i < topK) {
+        float denom = 0.0f;  // sequential, in selection order
+        for (int k = 0; k < topK; ++k) denom = __fadd_rn(denom, sel[k]);
+        denom = fmaxf(denom, 0.00006103515625f);
+        weights[i] = __fdiv_rn(sel[i], denom);
+    }
+    group_sync<W>(bar_id);
+}
+
 }  // namespace strata

@@ -119,3 +119,74 @@ def test_fast_falls_back_to_exact_outside_its_shapes(b, golden):
     assert np.array_equal(ids, g["ids_ref"])
     assert np.array_equal(bits(y), bits(g["y_ref"]))
     layer.free()
+
+
+def _check_against_oracle(b, port, layer, router, x, bias=None, seed=5, layer_index=0):
+    """Fast path vs the oracle on explicit host router/x: ids and weights bit-identical, y
+    within TOL; only the experts the oracle selects need their blobs on the host."""
+    from oracle.oracle import moe_layer_port, route_port
+    from stratacuda_b200 import _lib as L
+    from stratacuda_b200 import synth
+    T = x.shape[0]
+    xb = b.alloc(x.reshape(-1).copy())
+    y, ids, w = forward(b, layer, xb, T, L.MOE_FAST)
+    b.free(xb)
+    _, ids_o, w_o = route_port(port, x, router, layer.top_k, bias=bias)
+    assert np.array_equal(ids, ids_o)
+    assert np.array_equal(bits(w), bits(w_o))
+    blobs = np.zeros((layer.experts, layer.blob_words), np.uint32)
+    for e in sorted(set(ids_o.reshape(-1).tolist())):
+        blobs[e] = synth.expert_blob(seed, layer_index, e, layer.width, layer.ff)
+    y_o, _, _ = moe_layer_port(port, x, router, synth.shared_gate(seed, layer_index, layer.width), blobs,
+                               synth.expert_blob(seed, layer_index, 0, layer.width, layer.ff, True), layer.top_k, bias=bias)
+    for t in range(T):
+        assert rel_l2(y[t], y_o[t]) <= TOL, (t, rel_l2(y[t], y_o[t]))
+    return ids
+
+
+@pytest.mark.parametrize("B", [1, 3, 8])
+def test_fast_routing_ties_across_subgroups(b, port, B):
+    """Router rows repeat with period 37, so every probability occurs 8-9 times across all
+    eight 64-expert subgroups of the top-k merge: selection falls to the lowest-id
+    tie-break, which must match the reference's scan order exactly. 300 experts (a ragged
+    last subgroup), topK 32 (the largest supported)."""
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import MoeLayer
+    E, K = 300, 32
+    layer = MoeLayer.synthesize(b, seed=5, layer=0, width=WIDTH, ff=FF, experts=E, top_k=K)
+    base = synth.router_weights(5, 0, 37, WIDTH)
+    router = base[np.arange(E) % 37]
+    b.write(layer.router, router.reshape(-1))
+    x = synth.activations(60 + B, B, WIDTH)
+    ids = _check_against_oracle(b, port, layer, router, x)
+    assert all(len(set(r.tolist())) == K for r in ids)
+    layer.free()
+
+
+def test_fast_routing_all_equal_logits(b, port):
+    """A zero router: every probability is 1/E, the top-k is experts 0..k-1 in id order."""
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import MoeLayer
+    E, K = 512, 10
+    layer = MoeLayer.synthesize(b, seed=5, layer=0, width=WIDTH, ff=FF, experts=E, top_k=K)
+    router = np.zeros((E, WIDTH), np.float32)
+    b.write(layer.router, router.reshape(-1))
+    x = synth.activations(71, 2, WIDTH)
+    ids = _check_against_oracle(b, port, layer, router, x)
+    assert np.array_equal(ids, np.tile(np.arange(K, dtype=np.int32), (2, 1)))
+    layer.free()
+
+
+@pytest.mark.parametrize("B", [1, 7])
+def test_fast_routing_with_bias_and_few_experts(b, port, B):
+    """A router bias (Zipf-skewed: a few experts win for every token, so slots hold several
+    tokens) and 64 experts (one subgroup only) with topK 16."""
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import MoeLayer
+    E, K = 64, 16
+    layer = MoeLayer.synthesize(b, seed=5, layer=0, width=WIDTH, ff=FF, experts=E, top_k=K, zipf=1.1)
+    router = synth.router_weights(5, 0, E, WIDTH)
+    bias = synth.zipf_bias(5, E, 1.1)
+    x = synth.activations(80 + B, B, WIDTH)
+    _check_against_oracle(b, port, layer, router, x, bias=bias)
+    layer.free()
