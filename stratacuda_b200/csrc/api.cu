@@ -384,9 +384,9 @@ int strata_info(strata_ctx *ctx, char *json, size_t cap) {
     char buf[1024];
     int n = snprintf(buf, sizeof buf,
                      "{\"backend\":\"cuda\",\"device\":\"%s\",\"ordinal\":%d,\"sms\":%d,\"buffers\":%zu,\"bytesResident\":%llu,"
-                     "\"workspaceBytes\":%zu,\"dispatches\":%llu,\"fusedCalls\":%llu}",
+                     "\"workspaceBytes\":%zu,\"dispatches\":%llu,\"fusedCalls\":%llu,\"fastPdl\":%d}",
                      ctx->device_name, ctx->device, ctx->sms, ctx->buffers.size(), (unsigned long long)ctx->bytes_resident,
-                     ctx->workspace_bytes, (unsigned long long)ctx->dispatches, (unsigned long long)ctx->fused_calls);
+                     ctx->workspace_bytes, (unsigned long long)ctx->dispatches, (unsigned long long)ctx->fused_calls, moe_fast_pdl_state());
     if (json && cap) snprintf(json, cap, "%s", buf);
     return n;
 }

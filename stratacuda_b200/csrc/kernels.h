@@ -66,6 +66,7 @@ cudaError_t moe_forward_exact(const MoeLayerDev &L, const float *x, int tokens, 
 // arrivals; the kernel leaves them zero again on exit.
 bool moe_fast_supported(int tokens, int width, int ff, int topK, int grid);
 size_t moe_fast_scratch_bytes(int tokens, int width, int ff, int experts, int topK);
+int moe_fast_pdl_state();  // 1: launched with programmatic dependent launch, 0: refused, -1: not launched yet
 cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
                              unsigned *sync, int grid, cudaStream_t s, unsigned *err);
 

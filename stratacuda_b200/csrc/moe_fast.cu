@@ -9,26 +9,32 @@
 //   * forms hidden = silu(gate) * up for its 64 values and tokens;
 //   * multiplies the down projection's column slice (all H rows, code bytes 16j .. 16j+15,
 //     one scale group) with them: warp w takes rows H/8 w .. H/8 (w+1);
-//   * adds weight * result into y with atomics.
-// So the hidden values never leave the CTA: no second grid barrier, no global staging.
-// Units are dealt round-robin: unit u runs on CTA u % G. The y adds happen in no fixed
-// order, so y is not bit-reproducible run to run; it stays within 1e-5 relative L2 of the
-// reference (tested).
+//   * stores weight * result, one partial row of y per (group j, token-expert pair), to a
+//     global buffer with plain 16-byte stores.
+// So the hidden values never leave the CTA. Units are dealt round-robin: unit u runs on
+// CTA u % G. After a second grid arrival every CTA sums a slice of y from the partial rows
+// in a fixed order (group j, then the shared expert and the routed pairs in selection
+// order): y is the same bits run to run, within 1e-5 relative L2 of the reference (tested).
+// (Adding the partials with atomics instead serialised in L2: every y element received
+// one add per unit, up to ~90.)
 //
 // Phase 0 (from entry): x is staged in shared memory; router logits, row r of the 512 (+1
 // shared-gate row) on CTA r % G, warp r / G, in the reference's exact order
 // (kernels/strata.cu:156-165) so that the routing below is bit-identical; the remaining
 // warps turn x into integer tensor-core operands; y is zeroed. CTAs that own a shared-expert
 // unit start its copies at entry and compute its gate/up part before waiting at the arrival.
+// y is not touched before the final sum, so it needs no zeroing.
 // Phase 1 (after the arrival: all logits written): every CTA routes all tokens redundantly
 // (route.cuh route_group: up to 8 warps per token) and builds the expert slots, then runs
 // its units.
 //
 // Memory pipeline, per warp: a ring of gate/up stages (one 16-row x 128-byte box of codes,
-// 128-byte swizzle, plus one 16 x 16-byte box of FP16 scales, by TMA tensor copies) and one
-// down stage (H/8 rows x 16 bytes of codes by TMA, plus the rows' scale words by one bulk
-// copy). The down stages share their memory with the phase-0 copy of x and the routing
-// scratch, so they are first issued once routing is done.
+// 128-byte swizzle, by TMA tensor copy; the first chunk of a unit also brings the 16 rows'
+// FP16 scales, 1 KB contiguous, by one bulk copy) and one down stage (H/8 rows x 16 bytes of
+// codes plus each row's 4-byte scale word, by cp.async from all lanes: the rows are too short
+// for the TMA engine, which spends one request per box row). The down stages share their
+// memory with the phase-0 copy of x and the routing scratch, so they are first issued once
+// routing is done.
 //
 // Tensor-core math (exact integer products): mma.sync m16n8k32 u8 x s8 -> s32.
 //   A = weight codes c in {0..3} as u8: four codes per register by one shift and one mask.
@@ -40,7 +46,7 @@
 //   then total += scale * float(that) in F32, and the row is multiplied by 2^-k.
 // The only rounding is v (2^-22 of the vector's largest |x|) and the F32 accumulation.
 //
-// All waits (the grid arrival, mbarriers) are bounded: past the limit the kernel records
+// All waits (the grid arrivals, mbarriers) are bounded: past the limit the kernel records
 // kErrWaitTimeout, waits (bounded) for its own copies in flight and leaves.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -73,10 +79,10 @@ __device__ __forceinline__ bool mbar_try(unsigned long long *bar, unsigned parit
     unsigned ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(2000u)
+        : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -92,6 +98,14 @@ __device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *map, int x,
         "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned &r0, unsigned &r1, unsigned &r2, unsigned &r3) {
     asm volatile("ldmatrix.sync.aligned.x4.m8n8.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -108,14 +122,28 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
     return v;
 }
 __device__ __forceinline__ void named_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
-
-// Scale exponent: 2^k * maxabs < 2^22.
-__device__ __forceinline__ int scale_exp(float maxabs) {
-    if (!(maxabs > 0.0f) || !isfinite(maxabs)) return 0;
-    int e;
-    frexpf(maxabs, &e);  // maxabs = m * 2^e, m in [0.5, 1)
-    return 22 - e;
+__device__ __forceinline__ bool grid_arrive_wait(unsigned *counter, unsigned target, unsigned long long limit) {
+    __threadfence();
+    atomicAdd(counter, 1u);
+    for (unsigned long long i = 0;; ++i) {
+        if (ld_acquire(counter) >= target) return true;
+        if (i > limit) return false;
+        __nanosleep(32);
+    }
 }
+
+// Scale exponent k for maxabs >= 0: 2^k * maxabs < 2^22 (maxabs = m 2^e, m in [0.5, 1): k =
+// 22 - e), 0 for zero or non-finite maxabs, clamped to [-126, 126] so that 2^k and 2^-k are
+// normal floats (a vector whose largest element is subnormal then keeps fewer bits).
+__device__ __forceinline__ int scale_exp(float maxabs) {
+    const unsigned b = __float_as_uint(maxabs);
+    const int be = (int)(b >> 23);  // biased exponent (sign bit clear)
+    int k = 22 - (be - 126);
+    k = be == 0 ? 126 : k;
+    k = be >= 255 || b == 0u ? 0 : k;
+    return max(-126, min(126, k));
+}
+__device__ __forceinline__ float pow2f(int k) { return __uint_as_float((unsigned)(k + 127) << 23); }  // k in [-126, 127]
 // Byte of signed digit d of v = d0 + 256 d1 + 65536 d2 (each digit in [-128, 127]):
 // d0 = v mod 256, d1 = floor((v + 128) / 256) mod 256, d2 = floor((v + 32896) / 65536).
 __device__ __forceinline__ unsigned digit_byte(int v, int d) {
@@ -148,13 +176,12 @@ struct Params {
     float *weights;
     float *logits;   // [tokens][experts]
     float *sg;       // [tokens]
-    unsigned *sync;  // [0] arrivals, [2] exits
+    float *part;     // [F/64][tokens*topK + tokens][H] partial rows of y
+    unsigned *sync;  // [0] first arrival, [1] second arrival, [2] exits
     unsigned *err;
     unsigned long long spin_limit;
     // TMA maps: [0] routed experts, [1] the shared expert
     CUtensorMap tm_gu[2];  // gate/up codes: {H/4 bytes, 2F rows, experts}, box {128, 16, 1}, 128B swizzle
-    CUtensorMap tm_gs[2];  // gate/up scales: {2*H/64 bytes, 2F rows, experts}, box {16, 16, 1}
-    CUtensorMap tm_dc[2];  // down codes: {F/4 bytes, H rows, experts}, box {16, RB, 1}
 };
 
 template <int H, int F>
@@ -164,46 +191,45 @@ struct Geo {
     static constexpr int CPT = NG / 8;                 // gate/up chunks per warp and unit
     static constexpr int SGU = NG == 32 ? 4 : 3;       // gate/up stages per warp
     static constexpr int RW = H / kWarps;              // down rows per warp
-    static constexpr int RB = RW <= 256 ? RW : RW / 2; // rows per down box (TMA box dims <= 256)
-    static constexpr int NBOX = RW / RB;
-    static constexpr int DN_CODES = RW * 16;
-    static constexpr int DN_SCALES = RW * NJ * 2;
-    static constexpr int DN_STAGE = (DN_CODES + DN_SCALES + 127) / 128 * 128;
-    static_assert(NG % 8 == 0 && RW % 32 == 0 && RW % RB == 0 && DN_SCALES % 16 == 0, "geometry");
+    static constexpr int DN_CODES = RW * 16;           // 16 code bytes per row
+    static constexpr int DN_STAGE = (DN_CODES + RW * 4 + 127) / 128 * 128;  // + one scale word per row
+    static constexpr int GS_BYTES = 16 * 2 * NG;       // FP16 scales of a warp's 16 gate/up rows
+    static_assert(NG % 8 == 0 && RW % 32 == 0 && NJ % 2 == 0, "geometry");
 };
 
 template <int H, int F>
 struct Smem {
     using G = Geo<H, F>;
     unsigned char gu_codes[kWarps][G::SGU][2048];  // 1024-aligned (128-byte swizzle)
-    unsigned char gu_scales[kWarps][G::SGU][256];
+    alignas(16) unsigned short gu_scales[kWarps][2][G::GS_BYTES / 2];  // by unit parity
     union Region {
         unsigned char down[kWarps][G::DN_STAGE];  // after routing
         float x[kMaxTokens * H];                  // phase 0
         struct Route {
             float lg[kMaxTokens][512];
-            unsigned long long cand[kMaxTokens][8 * 32];
+            alignas(16) unsigned long long cand[kMaxTokens][8 * 32];
             float red[kMaxTokens][kWarps];
             float sel[kMaxTokens][32];
-        } r;  // routing
+            int nzc[kMaxTokens];
+            int owner[512];  // lowest pair index per expert
+            int cnt[512];    // pairs per expert
+            short slot_of[512];
+            int wcount[kWarps];
+        } r;  // routing and slot building
     } u;
     uint2 xf[G::NG * 2 * kMaxTokens * 4 * 3];  // x digits [group][h][token][q][digit]
-    uint2 hf[2 * kMaxTokens * 4 * 3];          // hidden digits [h][token slot][q][digit]
     int xsum[kMaxTokens][G::NG];
     float xscale[kMaxTokens];
     unsigned xmax[kMaxTokens];
-    float hid[kMaxTokens][64];
-    int hsum[kMaxTokens];
-    float hmul[kMaxTokens];  // 2^-k of the hidden digits times the routing weight
+    float sgw[kMaxTokens];                    // shared-expert weights sigmoid(shared-gate logit)
+    float hid[2][kMaxTokens][64];             // hidden values of the current unit (double-buffered by unit parity)
+    float hmaxw[2][kWarps][kMaxTokens];       // per-warp max |hidden| of each token slot
     int ids[kMaxPairs];
     float wts[kMaxPairs];
     short slot_expert[kMaxSlots];
     short slot_pair[kMaxSlots][kMaxTokens];
-    short slot_of_pair[kMaxPairs];
     unsigned char slot_n[kMaxSlots];
-    unsigned char first[kMaxPairs];
     unsigned long long bar_gu[kWarps][G::SGU];
-    unsigned long long bar_dn[kWarps];
     int n_slots;
     int abort_flag;
 };
@@ -211,28 +237,22 @@ struct Smem {
 template <int H, int F>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant__ Params P) {
     using Gm = Geo<H, F>;
-    constexpr int NG = Gm::NG, NJ = Gm::NJ, CPT = Gm::CPT, SGU = Gm::SGU, RW = Gm::RW, RB = Gm::RB;
+    constexpr int NG = Gm::NG, NJ = Gm::NJ, CPT = Gm::CPT, SGU = Gm::SGU, RW = Gm::RW;
     extern __shared__ unsigned char smem_raw[];
     auto &S = *reinterpret_cast<Smem<H, F> *>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
     const MoeLayerDev &L = P.L;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
     const int G = gridDim.x, cta = blockIdx.x;
     const int B = P.tokens, K = L.topK, E = L.experts;
-    const long long d_scales_b = 3LL * F * H / 4 + 2LL * F * (H / 64) * 2;
+    const long long d_codes_b = 2LL * F * H / 4, gu_scales_b = 3LL * F * H / 4, d_scales_b = gu_scales_b + 2LL * F * (H / 64) * 2;
 
     if (tid == 0) {
-        for (int w = 0; w < kWarps; ++w) {
+        for (int w = 0; w < kWarps; ++w)
             for (int s = 0; s < SGU; ++s) mbar_init(&S.bar_gu[w][s], 1);
-            mbar_init(&S.bar_dn[w], 1);
-        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.abort_flag = 0;
         S.n_slots = 1;
-        for (int i = 0; i < 2; ++i) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.tm_gu[i])) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.tm_gs[i])) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.tm_dc[i])) : "memory");
-        }
+        for (int i = 0; i < 2; ++i) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.tm_gu[i])) : "memory");
     }
     if (tid < kMaxTokens) S.xmax[tid] = 0u;
     __syncthreads();
@@ -250,30 +270,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         m = slot == 0 ? 1 : 0;
         e = slot == 0 ? 0 : S.slot_expert[slot];
     };
+    auto blob_of = [&](int slot, int e) {
+        return reinterpret_cast<const unsigned char *>(slot == 0 ? L.shared_blob : L.blobs + (long long)e * L.blob_words);
+    };
     auto issue_gu = [&](int k) {
         const int ui = k / CPT, sub = k % CPT, st = k % SGU;
         int slot, j, m, e;
         unit_of(ui, slot, j, m, e);
         if (lane == 0) {
             unsigned long long *bar = &S.bar_gu[warp][st];
-            mbar_expect(bar, 2048 + 256);
+            mbar_expect(bar, 2048 + (sub == 0 ? Gm::GS_BYTES : 0));
             tma_3d(S.gu_codes[warp][st], &P.tm_gu[m], 128 * sub, 128 * j + 16 * warp, e, bar);
-            tma_3d(S.gu_scales[warp][st], &P.tm_gs[m], 16 * sub, 128 * j + 16 * warp, e, bar);
+            if (sub == 0)  // the unit's scales ride on its first chunk (chunks are consumed in order)
+                bulk_copy(S.gu_scales[warp][ui & 1], blob_of(slot, e) + gu_scales_b + (long long)(128 * j + 16 * warp) * 2 * NG,
+                          Gm::GS_BYTES, bar);
         }
     };
-    auto issue_dn = [&](int ui) {
+    auto issue_dn = [&](int ui) {  // all lanes: row r of this warp's slice by lane r % 32
         int slot, j, m, e;
         unit_of(ui, slot, j, m, e);
-        if (lane == 0) {
-            unsigned long long *bar = &S.bar_dn[warp];
-            unsigned char *dst = S.u.down[warp];
-            mbar_expect(bar, Gm::DN_CODES + Gm::DN_SCALES);
-#pragma unroll
-            for (int b = 0; b < Gm::NBOX; ++b) tma_3d(dst + b * RB * 16, &P.tm_dc[m], 16 * j, RW * warp + RB * b, e, bar);
-            const unsigned char *blob =
-                reinterpret_cast<const unsigned char *>(slot == 0 ? L.shared_blob : L.blobs + (long long)e * L.blob_words);
-            bulk_copy(dst + Gm::DN_CODES, blob + d_scales_b + (long long)RW * warp * NJ * 2, Gm::DN_SCALES, bar);
+        const unsigned char *blob = blob_of(slot, e);
+        unsigned char *dst = S.u.down[warp];
+#pragma unroll 2
+        for (int r = lane; r < RW; r += 32) {
+            const long long row = (long long)RW * warp + r;
+            cp_async16(dst + 16 * r, blob + d_codes_b + row * (F / 4) + 16 * j);
+            cp_async4(dst + Gm::DN_CODES + 4 * r, blob + d_scales_b + (row * NJ + (j & ~1)) * 2);  // scales of groups j&~1, j|1
         }
+        cp_async_commit();
     };
     auto pump = [&]() {  // stages being refilled were last accessed through the generic proxy: order before the copies
         if (stalled) return;
@@ -316,14 +340,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         }
     };
     if (router_warp && row0 <= E) load_row(row0);
+    // Everything above reads only the layer's weights. The launch may overlap the previous
+    // kernel on the stream (programmatic dependent launch): wait for it to complete before
+    // touching x, the scratch or the arrival counters, and let the next launch get ready.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if ((reinterpret_cast<unsigned long long>(P.x) & 15ull) == 0) {
         const float4 *x4 = reinterpret_cast<const float4 *>(P.x);
         float4 *d4 = reinterpret_cast<float4 *>(S.u.x);
-        for (int i = tid; i < B * H / 4; i += kThreads) d4[i] = __ldg(x4 + i);
+        const int n4 = B * H / 4;
+        for (int base = 0; base < n4; base += 8 * kThreads) {  // eight loads in flight per thread
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = base + u * kThreads + tid;
+                if (i < n4) v[u] = __ldg(x4 + i);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = base + u * kThreads + tid;
+                if (i < n4) d4[i] = v[u];
+            }
+        }
     } else {
         for (int i = tid; i < B * H; i += kThreads) S.u.x[i] = __ldg(P.x + i);
     }
-    for (long long i = (long long)cta * kThreads + tid; i < (long long)B * H; i += (long long)G * kThreads) P.y[i] = 0.0f;
     __syncthreads();
     if (router_warp) {
         for (int r = row0; r <= E; r += G * RWARPS) {
@@ -360,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         for (int b = bi; b < B * NG * 4; b += nb) {
             const int t = b / (NG * 4), grp = (b >> 2) % NG, qq = b & 3;
             const int k = scale_exp(__uint_as_float(S.xmax[t]));
-            const float mul = ldexpf(1.0f, k);  // exact power of two
-            if (grp == 0 && qq == 0) S.xscale[t] = ldexpf(1.0f, -k);
+            const float mul = pow2f(k);  // exact power of two
+            if (grp == 0 && qq == 0) S.xscale[t] = pow2f(-k);
             const float4 *src = reinterpret_cast<const float4 *>(S.u.x + t * H + 64 * grp + 16 * qq);
             int v[16];
             int part = 0;
@@ -393,8 +434,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
     auto tok_of = [&](int ts) -> int { return slot_cur == 0 ? ts : S.slot_pair[slot_cur][ts] / K; };
 
     // Gate/up of unit ui: CPT chunks, then silu(gate) * up into S.hid[token slot][64].
-    auto gate_up = [&](auto ncg_c, int ui) {
-        constexpr int NCG = decltype(ncg_c)::value;
+    // One copy of the unit code (instruction fetch, not arithmetic, limited the kernel when
+    // every column-group count had its own): sized for four column groups, the groups past
+    // ncg = ceil(n_cur / 2) are skipped by warp-uniform branches.
+    constexpr int NCG = 4;
+    auto gate_up = [&](int ui) {
+        const int ncg = (n_cur + 1) / 2;
         int tokB[NCG], tokC[NCG];
         const int d = g & 3;
 #pragma unroll
@@ -412,34 +457,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
             if (!stalled && !__all_sync(0xffffffffu, wait_bar(&S.bar_gu[warp][st], (k / SGU) & 1))) fail_wait();
             if (!stalled) {
                 const unsigned base = smem_u32(S.gu_codes[warp][st]);
-                const unsigned short *scl = reinterpret_cast<const unsigned short *>(S.gu_scales[warp][st]);
+                const unsigned short *scl = S.gu_scales[warp][ui & 1] + sub * 8;  // row r: scl[r * NG + group in chunk]
                 unsigned w[4][4];
 #pragma unroll
                 for (int gp = 0; gp < 4; ++gp) {
                     const int c = 2 * gp + (lane >> 4);
                     ldsm_x4(base + r * 128 + ((c ^ (r & 7)) << 4), w[gp][0], w[gp][1], w[gp][2], w[gp][3]);
                 }
+                // expert scales are finite FP16 (rejected on load otherwise, src/model.js:164): the
+                // hardware conversion is exact for them
+                float s_lo[8], s_hi[8];
 #pragma unroll
                 for (int gl = 0; gl < 8; ++gl) {
-                    const int grp = sub * 8 + gl;
-                    const unsigned wl = w[gl >> 1][(gl & 1) ? 2 : 0], wh = w[gl >> 1][(gl & 1) ? 3 : 1];
-                    // expert scales are finite FP16 (rejected on load otherwise, src/model.js:164):
-                    // the hardware conversion is exact for them
-                    const float s_lo = __half2float(__ushort_as_half(scl[g * 8 + gl]));
-                    const float s_hi = __half2float(__ushort_as_half(scl[(g + 8) * 8 + gl]));
+                    s_lo[gl] = __half2float(__ushort_as_half(scl[g * NG + gl]));
+                    s_hi[gl] = __half2float(__ushort_as_half(scl[(g + 8) * NG + gl]));
+                }
+                // issue order matters (the MMA and ldmatrix statements keep their order): all
+                // operands, then 16 independent MMAs, then the combines
 #pragma unroll
-                    for (int cg = 0; cg < NCG; ++cg) {
-                        int c4[4] = {0, 0, 0, 0};
+                for (int cg = 0; cg < NCG; ++cg) {
+                    if (cg >= ncg) break;
+                    uint2 bf[8][2];
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const uint2 b = tokB[cg] >= 0 ? S.xf[(((grp * 2 + h) * kMaxTokens + tokB[cg]) * 4 + q) * 3 + d] : make_uint2(0u, 0u);
-                            imma(c4, (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
-                                 (wh >> (4 * h + 2)) & 0x03030303u, b.x, b.y);
+                    for (int gl = 0; gl < 8; ++gl)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+                            bf[gl][h] = tokB[cg] >= 0 ? S.xf[((((sub * 8 + gl) * 2 + h) * kMaxTokens + tokB[cg]) * 4 + q) * 3 + d] : make_uint2(0u, 0u);
+                    int c4[8][4];
+#pragma unroll
+                    for (int gl = 0; gl < 8; ++gl) c4[gl][0] = c4[gl][1] = c4[gl][2] = c4[gl][3] = 0;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int gl = 0; gl < 8; ++gl) {
+                            const unsigned wl = w[gl >> 1][(gl & 1) ? 2 : 0], wh = w[gl >> 1][(gl & 1) ? 3 : 1];
+                            imma(c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                                 (wh >> (4 * h + 2)) & 0x03030303u, bf[gl][h].x, bf[gl][h].y);
                         }
-                        const int d2lo = __shfl_down_sync(0xffffffffu, c4[0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[2], 1);
-                        const int xs = S.xsum[tokC[cg] >= 0 ? tokC[cg] : 0][grp];
-                        acc[cg][0] = fmaf(s_lo, (float)(c4[0] + 256 * c4[1] + 65536 * d2lo - xs), acc[cg][0]);
-                        acc[cg][1] = fmaf(s_hi, (float)(c4[2] + 256 * c4[3] + 65536 * d2hi - xs), acc[cg][1]);
+                    const int* xsr = S.xsum[tokC[cg] >= 0 ? tokC[cg] : 0] + sub * 8;
+#pragma unroll
+                    for (int gl = 0; gl < 8; ++gl) {
+                        const int d2lo = __shfl_down_sync(0xffffffffu, c4[gl][0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[gl][2], 1);
+                        const int xs = xsr[gl];
+                        acc[cg][0] = fmaf(s_lo[gl], (float)(c4[gl][0] + 256 * c4[gl][1] + 65536 * d2lo - xs), acc[cg][0]);
+                        acc[cg][1] = fmaf(s_hi[gl], (float)(c4[gl][2] + 256 * c4[gl][3] + 65536 * d2hi - xs), acc[cg][1]);
                     }
                 }
             }
@@ -448,89 +509,121 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         }
         // lanes with even q hold token slot 2cg + q/2; row g (gate when g is even) pairs with
         // row g+1 (up) four lanes down. Hidden index of row g: 8 warp + g/2 (+4 for row g+8).
+        // Each warp also records its largest |hidden| per token slot (NaN ignored, as fmaxf).
+        const int buf = ui & 1;
 #pragma unroll
         for (int cg = 0; cg < NCG; ++cg) {
+            if (cg >= ncg) break;
             const float sc = tokC[cg] >= 0 ? S.xscale[tokC[cg]] : 0.0f;
             const float gv0 = acc[cg][0] * sc, gv1 = acc[cg][1] * sc;
             const float up0 = __shfl_down_sync(0xffffffffu, gv0, 4), up1 = __shfl_down_sync(0xffffffffu, gv1, 4);
-            if (!(q & 1) && !(g & 1) && tokC[cg] >= 0) {
-                float *hrow = S.hid[2 * cg + (q >> 1)];
-                hrow[8 * warp + (g >> 1)] = __fmul_rn(ref_silu(gv0), up0);
-                hrow[8 * warp + 4 + (g >> 1)] = __fmul_rn(ref_silu(gv1), up1);
+            const bool own = !(q & 1) && !(g & 1) && tokC[cg] >= 0;
+            float h0 = 0.0f, h1 = 0.0f;
+            if (own) {
+                h0 = __fmul_rn(ref_silu(gv0), up0);
+                h1 = __fmul_rn(ref_silu(gv1), up1);
+                float *hrow = S.hid[buf][2 * cg + (q >> 1)];
+                hrow[8 * warp + (g >> 1)] = h0;
+                hrow[8 * warp + 4 + (g >> 1)] = h1;
             }
-        }
-    };
-
-    // Hidden digits of token slot `warp` (< n_cur): one warp per slot.
-    auto quantize_hidden = [&]() {
-        const int ts = warp;
-        float mx = fmaxf(fabsf(S.hid[ts][lane]), fabsf(S.hid[ts][lane + 32]));
-        mx = fmaxf(mx, 0.0f);
-#pragma unroll
-        for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
-        const int k = scale_exp(mx);
-        const float mul = ldexpf(1.0f, k);
-        int part = 0;
-        if (lane < 4) {  // lane = block q of 16 elements: both MMA halves
-            int v[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = __float2int_rn(S.hid[ts][16 * lane + i] * mul);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) part += v[i];
-            block_frags(v, &S.hf[((0 * kMaxTokens + ts) * 4 + lane) * 3], &S.hf[((1 * kMaxTokens + ts) * 4 + lane) * 3]);
-        }
-        part += __shfl_xor_sync(0xffffffffu, part, 1);
-        part += __shfl_xor_sync(0xffffffffu, part, 2);
-        if (lane == 0) {
-            const float w = slot_cur == 0 ? ref_sigmoid(__ldcg(P.sg + ts)) : S.wts[S.slot_pair[slot_cur][ts]];
-            S.hsum[ts] = part;
-            S.hmul[ts] = ldexpf(1.0f, -k) * w;
+            float m = fmaxf(fmaxf(0.0f, fabsf(h0)), fabsf(h1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+            if (g == 0 && !(q & 1) && tokC[cg] >= 0) S.hmaxw[buf][warp][2 * cg + (q >> 1)] = m;
         }
     };
 
     // Down slice of unit ui: rows RW warp .. RW (warp+1), scale group j; adds into y.
-    auto down = [&](auto ncg_c, int ui, int j) {
-        constexpr int NCG = decltype(ncg_c)::value;
-        if (!stalled && !__all_sync(0xffffffffu, wait_bar(&S.bar_dn[warp], ui & 1))) fail_wait();
-        if (!stalled) {
-            const int d = g & 3;
-            uint2 hb[NCG][2];
-            int tokC[NCG], hsC[NCG];
-            float hmC[NCG];
+    auto down = [&](int ui, int j) {
+        const int ncg = (n_cur + 1) / 2;
+        // Hidden B fragments, built by each lane for its own column (token slot tsB, digit d):
+        // v = round(h * 2^k), k from the slot's largest |h| over the eight warps' maxima. The four
+        // q lanes of a column hold the group's 64 elements between them, so their sum(v) is a
+        // two-step shuffle; combine lanes (even q, token slot tsC) read it from the lane with
+        // g = 4 (q / 2), whose column is that slot.
+        const int buf = ui & 1, d = g & 3;
+        uint2 hb[NCG][2];
+        int tokC[NCG], hsC[NCG], prow[NCG];
+        float hmC[NCG];
+        const int PP = B * K + B;
 #pragma unroll
-            for (int cg = 0; cg < NCG; ++cg) {
-                const int tsB = 2 * cg + (g >> 2), tsC = 2 * cg + (q >> 1);
+        for (int cg = 0; cg < NCG; ++cg) {
+            if (cg >= ncg) break;
+            const int tsB = min(2 * cg + (g >> 2), n_cur - 1), tsC = 2 * cg + (q >> 1);
+            float mx = 0.0f;
 #pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    hb[cg][h] = d < 3 && tsB < n_cur ? S.hf[((h * kMaxTokens + tsB) * 4 + q) * 3 + d] : make_uint2(0u, 0u);
-                tokC[cg] = tsC < n_cur ? tok_of(tsC) : -1;
-                hsC[cg] = tsC < n_cur ? S.hsum[tsC] : 0;
-                hmC[cg] = tsC < n_cur ? S.hmul[tsC] : 0.0f;
+            for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, S.hmaxw[buf][w][tsB]);
+            const int k = scale_exp(mx);
+            const float mul = pow2f(k);
+            int v[16];
+            int part = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                v[i] = __float2int_rn(S.hid[buf][tsB][16 * q + i] * mul);
+                part += v[i];
             }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            const bool live = d < 3 && 2 * cg + (g >> 2) < n_cur;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int lo[4] = {v[2 * h], v[2 * h + 4], v[2 * h + 8], v[2 * h + 12]};
+                const int hi[4] = {v[2 * h + 1], v[2 * h + 5], v[2 * h + 9], v[2 * h + 13]};
+                hb[cg][h] = live ? make_uint2(pack_digit(lo, d), pack_digit(hi, d)) : make_uint2(0u, 0u);
+            }
+            const int src = 16 * (q >> 1) + q;
+            hsC[cg] = __shfl_sync(0xffffffffu, part, src);
+            const float inv = __shfl_sync(0xffffffffu, pow2f(-k), src);
+            tokC[cg] = tsC < n_cur ? tok_of(tsC) : -1;
+            prow[cg] = tsC >= n_cur ? 0 : slot_cur == 0 ? B * K + tsC : S.slot_pair[slot_cur][tsC];  // partial row: pair, or shared token
+            const float w = tsC >= n_cur ? 0.0f : slot_cur == 0 ? S.sgw[tsC] : S.wts[S.slot_pair[slot_cur][tsC]];
+            hmC[cg] = inv * w;
+        }
+        cp_async_wait_all();  // this lane's copies (the only cp.async group in flight)
+        __syncwarp();         // ... and every lane's
+        if (!stalled) {
             const unsigned base = smem_u32(S.u.down[warp]);
             const unsigned short *dsc = reinterpret_cast<const unsigned short *>(S.u.down[warp] + Gm::DN_CODES);
-#pragma unroll 2
-            for (int p = 0; p < RW / 32; ++p) {  // two 16-row tiles per ldmatrix.x4
-                unsigned w[4];
-                ldsm_x4(base + (32 * p + 8 * (lane >> 3) + (lane & 7)) * 16, w[0], w[1], w[2], w[3]);
+            constexpr int MB = 4;  // 16-row tiles per batch: two ldmatrix.x4, then all MMAs, then the epilogues
+#pragma unroll 1
+            for (int mb = 0; mb < RW / 16; mb += MB) {
+                unsigned wt[MB][2];
 #pragma unroll
-                for (int tt = 0; tt < 2; ++tt) {
-                    const unsigned wl = w[2 * tt], wh = w[2 * tt + 1];
-                    const int rl = 32 * p + 16 * tt + g;
-                    const float s_lo = __half2float(__ushort_as_half(dsc[rl * NJ + j]));
-                    const float s_hi = __half2float(__ushort_as_half(dsc[(rl + 8) * NJ + j]));
+                for (int pp = 0; pp < MB / 2; ++pp)
+                    ldsm_x4(base + (16 * (mb + 2 * pp) + 8 * (lane >> 3) + (lane & 7)) * 16, wt[2 * pp][0], wt[2 * pp][1], wt[2 * pp + 1][0],
+                            wt[2 * pp + 1][1]);
+                float s_lo[MB], s_hi[MB];
 #pragma unroll
-                    for (int cg = 0; cg < NCG; ++cg) {
-                        int c4[4] = {0, 0, 0, 0};
+                for (int m = 0; m < MB; ++m) {
+                    const int rl = 16 * (mb + m) + g;
+                    s_lo[m] = __half2float(__ushort_as_half(dsc[2 * rl + (j & 1)]));
+                    s_hi[m] = __half2float(__ushort_as_half(dsc[2 * (rl + 8) + (j & 1)]));
+                }
 #pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            imma(c4, (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                for (int cg = 0; cg < NCG; ++cg) {
+                    if (cg >= ncg) break;
+                    int c4[MB][4];
+#pragma unroll
+                    for (int m = 0; m < MB; ++m) c4[m][0] = c4[m][1] = c4[m][2] = c4[m][3] = 0;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int m = 0; m < MB; ++m) {
+                            const unsigned wl = wt[m][0], wh = wt[m][1];
+                            imma(c4[m], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                                  (wh >> (4 * h + 2)) & 0x03030303u, hb[cg][h].x, hb[cg][h].y);
-                        const int d2lo = __shfl_down_sync(0xffffffffu, c4[0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[2], 1);
-                        if (!(q & 1) && tokC[cg] >= 0) {
-                            float *yr = P.y + (long long)tokC[cg] * H + RW * warp + rl;
-                            atomicAdd(yr, (float)(c4[0] + 256 * c4[1] + 65536 * d2lo - hsC[cg]) * s_lo * hmC[cg]);
-                            atomicAdd(yr + 8, (float)(c4[2] + 256 * c4[3] + 65536 * d2hi - hsC[cg]) * s_hi * hmC[cg]);
+                        }
+                    float *pr = P.part + ((long long)j * PP + prow[cg]) * H + RW * warp + 16 * mb + g;
+                    const bool store = !(q & 1) && tokC[cg] >= 0;
+#pragma unroll
+                    for (int m = 0; m < MB; ++m) {
+                        const int d2lo = __shfl_down_sync(0xffffffffu, c4[m][0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[m][2], 1);
+                        const float flo = (float)(c4[m][0] + 256 * c4[m][1] + 65536 * d2lo - hsC[cg]) * s_lo[m] * hmC[cg];
+                        const float fhi = (float)(c4[m][2] + 256 * c4[m][3] + 65536 * d2hi - hsC[cg]) * s_hi[m] * hmC[cg];
+                        if (store) {
+                            __stcg(pr + 16 * m, flo);
+                            __stcg(pr + 16 * m + 8, fhi);
                         }
                     }
                 }
@@ -539,21 +632,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         ++dn_done;
         pump();
     };
-    auto dispatch = [&](int ncg, auto &&fn) {
-        switch (ncg) {
-            case 1: fn(std::integral_constant<int, 1>{}); break;
-            case 2: fn(std::integral_constant<int, 2>{}); break;
-            case 3: fn(std::integral_constant<int, 3>{}); break;
-            default: fn(std::integral_constant<int, 4>{}); break;
-        }
-    };
-
     // The shared-expert unit's gate/up part runs while the grid arrives.
     const bool early_unit = cta < NJ;
     if (early_unit) {
         slot_cur = 0;
         n_cur = B;
-        dispatch((B + 1) / 2, [&](auto c) { gate_up(c, 0); });
+        gate_up(0);
     }
 
     // ------------------------------------------------------------------ arrival: routing
@@ -578,6 +662,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         } else {
             for (int i = tid; i < B * E; i += kThreads) S.u.r.lg[i / E][i % E] = __ldcg(P.logits + i);
         }
+        for (int e = tid; e < E; e += kThreads) {
+            S.u.r.owner[e] = 0x7fffffff;
+            S.u.r.cnt[e] = 0;
+        }
+        if (tid < B) {
+            S.u.r.nzc[tid] = 0;
+            S.sgw[tid] = ref_sigmoid(__ldcg(P.sg + tid));
+        }
         __syncthreads();
         const int W = B == 1 ? 8 : B == 2 ? 4 : B <= 4 ? 2 : 1;
         const int t = warp / W;
@@ -589,10 +681,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
             int *ids = S.ids + t * K;
             float *wts = S.wts + t * K;
             switch (W) {
-                case 8: route_group<8>(lg, E, K, red, cand, ids, sel, wts, 1 + t); break;
-                case 4: route_group<4>(lg, E, K, red, cand, ids, sel, wts, 1 + t); break;
-                case 2: route_group<2>(lg, E, K, red, cand, ids, sel, wts, 1 + t); break;
-                default: route_group<1>(lg, E, K, red, cand, ids, sel, wts, 1 + t); break;
+                case 8: route_group<8>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
+                case 4: route_group<4>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
+                case 2: route_group<2>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
+                default: route_group<1>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
             }
         }
         __syncthreads();
@@ -603,39 +695,39 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
                 P.weights[p] = S.wts[p];
             }
         // expert slots in first-appearance order (token-major), as src/prefill.js:56-60; an id
-        // outside [0, E) (only when fewer than topK experts have a probability) gets no slot
-        for (int p = tid; p < P2; p += kThreads) {
-            const int e = S.ids[p];
-            bool f = e >= 0 && e < E;
-            for (int r = 0; r < p && f; ++r) f = S.ids[r] != e;
-            S.first[p] = f;
-        }
-        __syncthreads();
-        for (int p = tid; p < P2; p += kThreads) {
-            if (S.first[p]) {
-                int s = 1, n = 0;
-                for (int r = 0; r < p; ++r) s += S.first[r];
-                for (int r = p; r < P2; ++r) n += S.ids[r] == S.ids[p];
-                S.slot_of_pair[p] = (short)s;
-                S.slot_expert[s] = (short)S.ids[p];
-                S.slot_n[s] = (unsigned char)n;
-            }
-            if (p == 0) {
-                int n = 1;
-                for (int r = 0; r < P2; ++r) n += S.first[r];
-                S.n_slots = n;
+        // outside [0, E) (only when fewer than topK experts have a probability) gets no slot.
+        // Pair p = thread p (B * topK <= 256): the lowest pair of an expert opens its slot,
+        // slots are numbered by a ballot prefix over pairs; a slot's tokens are listed in
+        // arrival order, which only permutes MMA columns within the CTA.
+        int pe = -1, prank = 0;
+        bool pvalid = false;
+        if (tid < P2) {
+            pe = S.ids[tid];
+            pvalid = pe >= 0 && pe < E;
+            if (pvalid) {
+                atomicMin(&S.u.r.owner[pe], tid);
+                prank = atomicAdd(&S.u.r.cnt[pe], 1);
             }
         }
         __syncthreads();
-        for (int p = tid; p < P2; p += kThreads) {
-            const int e = S.ids[p];
-            if (e < 0 || e >= E) continue;
-            int f = 0;
-            while (S.ids[f] != e) ++f;
-            int rank = 0;
-            for (int r = f; r < p; ++r) rank += S.ids[r] == e;
-            S.slot_pair[S.slot_of_pair[f]][rank] = (short)p;
+        const bool pfirst = pvalid && S.u.r.owner[pe] == tid;
+        const unsigned bal = __ballot_sync(0xffffffffu, pfirst);
+        if (lane == 0) S.u.r.wcount[warp] = __popc(bal);
+        __syncthreads();
+        if (pfirst) {
+            int sidx = 1 + __popc(bal & ((1u << lane) - 1u));
+            for (int w = 0; w < warp; ++w) sidx += S.u.r.wcount[w];
+            S.slot_expert[sidx] = (short)pe;
+            S.slot_n[sidx] = (unsigned char)S.u.r.cnt[pe];
+            S.u.r.slot_of[pe] = (short)sidx;
         }
+        if (tid == 0) {
+            int n = 1;
+            for (int w = 0; w < kWarps; ++w) n += S.u.r.wcount[w];
+            S.n_slots = n;
+        }
+        __syncthreads();
+        if (pvalid) S.slot_pair[S.u.r.slot_of[pe]][prank] = (short)tid;
         __syncthreads();
         const int NU = S.n_slots * NJ;
         n_units = cta < NU ? (NU - 1 - cta) / G + 1 : 0;
@@ -650,25 +742,58 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         unit_of(ui, slot, j, m, e);
         slot_cur = slot;
         n_cur = slot == 0 ? B : S.slot_n[slot];
-        const int ncg = (n_cur + 1) / 2;
-        if (!(ui == 0 && early_unit)) dispatch(ncg, [&](auto c) { gate_up(c, ui); });
-        __syncthreads();
-        if (S.abort_flag) break;  // uniform: nothing writes the flag between these barriers
-        if (warp < n_cur) quantize_hidden();
-        __syncthreads();
-        dispatch(ncg, [&](auto c) { down(c, ui, j); });
+        if (!(ui == 0 && early_unit)) gate_up(ui);
+        if (__syncthreads_or(stalled ? 1 : 0)) break;  // a warp's copies timed out: all leave together
+        down(ui, j);
+    }
+
+    // ------------------------------------------------------------------ second arrival: y
+    for (int k = gu_done; k < gu_issued; ++k) wait_bar(&S.bar_gu[warp][k % SGU], (k / SGU) & 1);
+    cp_async_wait_all();
+    if (stalled) atomicOr(&S.abort_flag, 1);
+    __syncthreads();
+    if (tid == 0 && !grid_arrive_wait(&P.sync[1], (unsigned)G, P.spin_limit)) S.abort_flag = 1;
+    __syncthreads();
+    if (!S.abort_flag) {
+        // y[t][r]: the terms of one float4 column (group j, then the shared expert and the
+        // routed pairs in selection order: NJ (K + 1) of them) are split over a warp's lanes
+        // (lane l adds terms l, l + 32, ...; a pair without an expert adds zero), then summed
+        // by a fixed shuffle tree: the order never changes, so y has the same bits every run.
+        const int PP = B * K + B, H4 = H / 4, NT = NJ * (K + 1);
+        const float4 *part4 = reinterpret_cast<const float4 *>(P.part);
+        for (int item = cta * kWarps + warp; item < B * H4; item += G * kWarps) {
+            const int t = item / H4, c = item % H4;
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int m = lane; m < NT; m += 32) {
+                const int jj = m / (K + 1), kk = m % (K + 1);  // kk == 0: shared expert, else routed pair kk - 1
+                const int row = kk == 0 ? B * K + t : t * K + kk - 1;
+                const bool ok = kk == 0 || (unsigned)S.ids[t * K + kk - 1] < (unsigned)E;
+                const float4 u = ok ? __ldcg(part4 + ((long long)jj * PP + row) * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                acc.x += u.x;
+                acc.y += u.y;
+                acc.z += u.z;
+                acc.w += u.w;
+            }
+#pragma unroll
+            for (int sft = 16; sft > 0; sft >>= 1) {
+                acc.x += __shfl_xor_sync(0xffffffffu, acc.x, sft);
+                acc.y += __shfl_xor_sync(0xffffffffu, acc.y, sft);
+                acc.z += __shfl_xor_sync(0xffffffffu, acc.z, sft);
+                acc.w += __shfl_xor_sync(0xffffffffu, acc.w, sft);
+            }
+            if (lane == 0) reinterpret_cast<float4 *>(P.y)[item] = acc;
+        }
     }
 
     // ------------------------------------------------------------------ exit
-    for (int k = gu_done; k < gu_issued; ++k) wait_bar(&S.bar_gu[warp][k % SGU], (k / SGU) & 1);
-    for (int k = dn_done; k < dn_issued; ++k) wait_bar(&S.bar_dn[warp], k & 1);
     __syncthreads();
     if (tid == 0) {
         if (S.abort_flag) raise_error(P.err, kErrWaitTimeout);
         __threadfence();
         const unsigned prev = atomicAdd(&P.sync[2], 1u);
-        if (prev == (unsigned)G - 1) {  // last CTA out resets the arrival counter for the next launch
+        if (prev == (unsigned)G - 1) {  // last CTA out resets the arrival counters for the next launch
             P.sync[0] = 0;
+            P.sync[1] = 0;
             __threadfence();
             P.sync[2] = 0;
         }
@@ -677,12 +802,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
 
 }  // namespace fast
 
+static int g_fast_pdl = -1;  // programmatic dependent launch with the cooperative launch: -1 untried, 1 accepted, 0 refused
+int moe_fast_pdl_state() { return g_fast_pdl; }
+
 size_t moe_fast_scratch_bytes(int tokens, int width, int ff, int experts, int topK) {
-    (void)width;
-    (void)ff;
-    (void)topK;
     auto a = [](size_t n) { return (n + 255) & ~size_t(255); };
-    return a(sizeof(float) * tokens * experts) + a(sizeof(float) * tokens);
+    return a(sizeof(float) * tokens * experts) + a(sizeof(float) * tokens) +
+           a(sizeof(float) * (size_t)(ff / 64) * (size_t)(tokens * topK + tokens) * width);
 }
 
 bool moe_fast_supported(int tokens, int width, int ff, int topK, int grid) {
@@ -718,7 +844,7 @@ bool map3d(CUtensorMap *m, const void *base, unsigned long long d0, unsigned lon
 struct MapSet {
     const void *blobs, *shared;
     int width, ff, experts;
-    CUtensorMap gu[2], gs[2], dc[2];
+    CUtensorMap gu[2];
 };
 std::mutex g_map_mutex;
 MapSet g_maps[64];
@@ -728,8 +854,6 @@ bool layer_maps(const MoeLayerDev &L, fast::Params &p) {
     std::lock_guard<std::mutex> lock(g_map_mutex);
     auto use = [&](const MapSet &m) {
         std::memcpy(p.tm_gu, m.gu, sizeof m.gu);
-        std::memcpy(p.tm_gs, m.gs, sizeof m.gs);
-        std::memcpy(p.tm_dc, m.dc, sizeof m.dc);
     };
     for (const MapSet &m : g_maps)
         if (m.blobs == L.blobs && m.shared == L.shared_blob && m.width == L.width && m.ff == L.ff && m.experts == L.experts) {
@@ -743,17 +867,10 @@ bool layer_maps(const MoeLayerDev &L, fast::Params &p) {
     m.ff = L.ff;
     m.experts = L.experts;
     const long long H = L.width, F = L.ff, bb = L.blob_words * 4;
-    const long long d_codes = 2 * F * H / 4, gu_scales = 3 * F * H / 4;
-    const unsigned rw = (unsigned)(H / fast::kWarps), rb = rw <= 256 ? rw : rw / 2;
     for (int i = 0; i < 2; ++i) {
         const unsigned char *base = reinterpret_cast<const unsigned char *>(i == 0 ? L.blobs : L.shared_blob);
         const unsigned long long ne = i == 0 ? (unsigned long long)L.experts : 1ull;
-        // the down slices of one row (16 bytes per unit) are read by F/64 different units:
-        // 128-byte L2 fills let the first reader bring the whole row
-        if (!map3d(&m.gu[i], base, H / 4, 2 * F, ne, H / 4, bb, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
-            !map3d(&m.gs[i], base + gu_scales, 2 * (H / 64), 2 * F, ne, 2 * (H / 64), bb, 16, 16, CU_TENSOR_MAP_SWIZZLE_NONE,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
-            !map3d(&m.dc[i], base + d_codes, F / 4, H, ne, F / 4, bb, 16, rb, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
+        if (!map3d(&m.gu[i], base, H / 4, 2 * F, ne, H / 4, bb, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return false;
     }
     g_maps[g_map_next] = m;
@@ -762,19 +879,40 @@ bool layer_maps(const MoeLayerDev &L, fast::Params &p) {
     return true;
 }
 
+// Cooperative (the grid arrivals need every CTA resident) and, where the runtime accepts the
+// combination, programmatic stream serialisation: the launch is prepared while the previous
+// kernel on the stream finishes; the kernel reads only weights before griddepcontrol.wait.
 template <int H, int F>
 cudaError_t launch_fast(const fast::Params &p, int grid, cudaStream_t s) {
     const size_t smem = sizeof(fast::Smem<H, F>) + 1024;  // + slack for the 1024-byte stage alignment
-    STRATA_CUDA_TRY(cudaFuncSetAttribute(fast::k_moe_fast<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    static int device_ready = -1;  // device whose attribute is set (the library drives one device per context)
+    int dev = 0;
+    STRATA_CUDA_TRY(cudaGetDevice(&dev));
+    if (device_ready != dev) {
+        STRATA_CUDA_TRY(cudaFuncSetAttribute(fast::k_moe_fast<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        device_ready = dev;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(fast::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
+    if (g_fast_pdl != 0) {
+        cfg.numAttrs = 2;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, fast::k_moe_fast<H, F>, p);
+        if (e == cudaSuccess || g_fast_pdl == 1) {
+            g_fast_pdl = e == cudaSuccess ? 1 : g_fast_pdl;
+            return e;
+        }
+        cudaGetLastError();  // refused: launch without it from now on
+        g_fast_pdl = 0;
+    }
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, fast::k_moe_fast<H, F>, p);
 }
@@ -796,9 +934,11 @@ cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, f
     prm.logits = reinterpret_cast<float *>(p);
     p += a(sizeof(float) * tokens * L.experts);
     prm.sg = reinterpret_cast<float *>(p);
+    p += a(sizeof(float) * tokens);
+    prm.part = reinterpret_cast<float *>(p);
     prm.sync = sync;
     prm.err = err;
-    prm.spin_limit = 1ull << 20;  // the grid wait sleeps 32 ns per try, mbarrier tries suspend <= 2 us: bounded to ~2 s
+    prm.spin_limit = 1ull << 20;  // grid waits sleep 32 ns per try; an mbarrier try suspends for a short, system-defined time
     if (!layer_maps(L, prm)) return cudaErrorInvalidValue;
     if (L.width == 2048 && L.ff == 512) return launch_fast<2048, 512>(prm, grid, s);
     if (L.width == 2560 && L.ff == 640) return launch_fast<2560, 640>(prm, grid, s);

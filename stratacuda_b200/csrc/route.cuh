@@ -106,8 +106,9 @@ __device__ __forceinline__ void route_warp(const float *logits, int experts, int
 //            rank is the number of candidates above it.
 //   weights  sel_k / max(sum_k sel_k, 2^-14), the sum in selection order.
 // `lg` holds the token's logits (512 floats; entries past `experts` are ignored) and is
-// overwritten. `red` holds W floats, `cand` 8*topK keys; ids/sel/weights receive topK
-// entries. Group synchronisation uses named barrier `bar_id` (W > 1).
+// overwritten. `red` holds W floats, `cand` 8*topK keys (16-byte aligned), `nzc` one int
+// that the caller zeroes before the call; ids/sel/weights receive topK entries. Group
+// synchronisation uses named barrier `bar_id` (W > 1).
 template <int W>
 __device__ __forceinline__ void group_sync(int bar_id) {
     if (W == 1) __syncwarp();
@@ -120,12 +121,14 @@ __device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v,
     return ((unsigned long long)hi << 32) | lo;
 }
 
-// Sorts 64 keys, element 2*lane + j in k_j, into descending order (bitonic network).
-__device__ __forceinline__ void warp_sort64_desc(unsigned long long &k0, unsigned long long &k1, int lane) {
-#pragma unroll
+// Sorts 64 keys, element 2*lane + j in k.x (j = 0) / k.y (j = 1), into descending order
+// (bitonic network). Kept out of line and rolled: one small copy serves every caller.
+static __device__ __noinline__ ulonglong2 warp_sort64_desc(ulonglong2 k, int lane) {
+    unsigned long long k0 = k.x, k1 = k.y;
+#pragma unroll 1
     for (int size = 2; size <= 64; size <<= 1) {
         const bool desc = ((2 * lane) & size) == 0;  // direction of this element's block
-#pragma unroll
+#pragma unroll 1
         for (int stride = size >> 1; stride > 1; stride >>= 1) {
             const unsigned long long o0 = shfl_xor_u64(k0, stride >> 1), o1 = shfl_xor_u64(k1, stride >> 1);
             const bool take_max = (((2 * lane) & stride) == 0) == desc;  // lower element of a descending pair
@@ -136,11 +139,12 @@ __device__ __forceinline__ void warp_sort64_desc(unsigned long long &k0, unsigne
         k0 = desc ? hi : lo;
         k1 = desc ? lo : hi;
     }
+    return make_ulonglong2(k0, k1);
 }
 
 template <int W>
-__device__ __forceinline__ void route_group(float *lg, int experts, int topK, float *red, unsigned long long *cand, int *ids,
-                                            float *sel, float *weights, int bar_id) {
+__device__ __forceinline__ void route_group(float *lg, int experts, int topK, float *red, unsigned long long *cand, int *nzc,
+                                            int *ids, float *sel, float *weights, int bar_id) {
     constexpr int T = 32 * W, NPT = 512 / T;
     const int i = threadIdx.x % T, lane = threadIdx.x & 31, wg = i >> 5;
     float v[NPT];
@@ -175,36 +179,44 @@ __device__ __forceinline__ void route_group(float *lg, int experts, int topK, fl
         sb = __fadd_rn(sb, lg[lane + 32 + 64 * m]);
     }
     const float inv = __fdiv_rn(1.0f, __shfl_sync(0xffffffffu, tree64(sa, sb), 0));
-#pragma unroll
+#pragma unroll 1  // one sort network in the code: unrolled copies cost more in instruction fetch than they gain
     for (int a = 0; a < NPT / 2; ++a) {
         const int e0 = i + T * (2 * a), e1 = e0 + T;
-        const float p0 = __fmul_rn(v[2 * a], inv), p1 = __fmul_rn(v[2 * a + 1], inv);
-        unsigned long long k0 = e0 < experts && p0 >= 0.0f ? ((unsigned long long)(__float_as_uint(p0) + 1u) << 32) | (0xffffffffu - (unsigned)e0) : 0ull;
-        unsigned long long k1 = e1 < experts && p1 >= 0.0f ? ((unsigned long long)(__float_as_uint(p1) + 1u) << 32) | (0xffffffffu - (unsigned)e1) : 0ull;
-        warp_sort64_desc(k0, k1, lane);
+        const float p0 = __fmul_rn(lg[e0], inv), p1 = __fmul_rn(lg[e1], inv);  // lg holds the masked exponentials
+        const ulonglong2 k = warp_sort64_desc(
+            make_ulonglong2(e0 < experts && p0 >= 0.0f ? ((unsigned long long)(__float_as_uint(p0) + 1u) << 32) | (0xffffffffu - (unsigned)e0) : 0ull,
+                            e1 < experts && p1 >= 0.0f ? ((unsigned long long)(__float_as_uint(p1) + 1u) << 32) | (0xffffffffu - (unsigned)e1) : 0ull),
+            lane);
+        const unsigned long long k0 = k.x, k1 = k.y;
         unsigned long long *c = cand + (wg * (NPT / 2) + a) * topK;
         if (2 * lane < topK) c[2 * lane] = k0;
         if (2 * lane + 1 < topK) c[2 * lane + 1] = k1;
+        const int nz = __popc(__ballot_sync(0xffffffffu, 2 * lane < topK && k0 != 0ull)) +
+                       __popc(__ballot_sync(0xffffffffu, 2 * lane + 1 < topK && k1 != 0ull));
+        if (lane == 0 && nz) atomicAdd(nzc, nz);
     }
     group_sync<W>(bar_id);
-    const int N = 8 * topK;
+    const int N = 8 * topK;  // even
+    const ulonglong2 *c2 = reinterpret_cast<const ulonglong2 *>(cand);
     for (int c = i; c < N; c += T) {
         const unsigned long long kc = cand[c];
         if (kc == 0ull) continue;
-        int r = 0;
-        for (int c2 = 0; c2 < N; ++c2) r += cand[c2] > kc;
+        int r0 = 0, r1 = 0;
+#pragma unroll 8
+        for (int x = 0; x < N / 2; ++x) {
+            const ulonglong2 v = c2[x];
+            r0 += v.x > kc;
+            r1 += v.y > kc;
+        }
+        const int r = r0 + r1;
         if (r < topK) {
             ids[r] = (int)(0xffffffffu - (unsigned)kc);
             sel[r] = __uint_as_float((unsigned)(kc >> 32) - 1u);
         }
     }
-    if (i < topK) {  // rounds past the last valid key find nothing: the reference records -1
-        int nz = 0;
-        for (int c2 = 0; c2 < N; ++c2) nz += cand[c2] != 0ull;
-        if (i >= nz) {
-            ids[i] = -1;
-            sel[i] = -1.0f;
-        }
+    if (i < topK && i >= *nzc) {  // rounds past the last valid key find nothing: the reference records -1
+        ids[i] = -1;
+        sel[i] = -1.0f;
     }
     group_sync<W>(bar_id);
     if (i < topK) {
