@@ -401,7 +401,9 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
         return fail(ctx, STRATA_ERR_RANGE, "Router supports 1-512 experts and topK <= min(experts,32)");
     if (tokens < 1) return fail(ctx, STRATA_ERR_RANGE, "tokens must be an integer >= 1");
     if (mode != STRATA_MOE_EXACT && mode != STRATA_MOE_FAST) return fail(ctx, STRATA_ERR_RANGE, "unknown mode %d", mode);
+    // FAST: the fused decode kernel up to its token limit, the tensor-core prefill path above it
     const bool fast = mode == STRATA_MOE_FAST && moe_fast_supported(tokens, l.width, l.ff, l.top_k, ctx->sms);
+    const bool prefill = mode == STRATA_MOE_FAST && !fast && moe_prefill_supported(l.width, l.ff, l.experts, l.top_k);
     const long long bw = blob_words_of(l.width, l.ff);
     struct Need {
         strata_buf h;
@@ -429,8 +431,9 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
         ptr[i] = b->ptr;
     }
     if (int r = use_device(ctx)) return r;
-    const size_t ws = fast ? moe_fast_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
-                           : moe_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k);
+    const size_t ws = fast      ? moe_fast_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
+                      : prefill ? moe_prefill_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
+                                : moe_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k);
     if (ws > ctx->workspace_bytes) {
         CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "workspace resize");
         if (ctx->workspace) cudaFree(ctx->workspace);
@@ -449,6 +452,9 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     if (fast) {
         e = moe_forward_fast(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
                              ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev);
+    } else if (prefill) {
+        e = moe_forward_prefill(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
+                                ctx->sms, ctx->stream, ctx->err_dev);
     } else {
         MoeScratch s = moe_scratch_carve(ctx->workspace, tokens, l.width, l.ff, l.experts, l.top_k);
         e = moe_forward_exact(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], s, ctx->stream,

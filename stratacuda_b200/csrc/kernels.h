@@ -70,6 +70,14 @@ int moe_fast_pdl_state();  // 1: launched with programmatic dependent launch, 0:
 cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
                              unsigned *sync, int grid, cudaStream_t s, unsigned *err);
 
+// Prompt / large-batch layer (csrc/prefill.cu): exact routing, expert products on tcgen05
+// tensor cores from Q2 weights dequantised to FP16 (y within 2e-3 relative L2). `grid` is
+// the GEMMs' persistent grid (one CTA per SM).
+bool moe_prefill_supported(int width, int ff, int experts, int topK);
+size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int topK);
+cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
+                                int grid, cudaStream_t s, unsigned *err);
+
 // Device synthetic generator (csrc/synth.cu), same bytes as stratacuda_b200/synth.py.
 cudaError_t synth_expert_blobs(unsigned *out, unsigned long long seed, int layer, int first_expert, int count, int width, int ff,
                                int shared, cudaStream_t s);

@@ -1,0 +1,439 @@
+// Mixture-of-experts layer for prompt batches (and decode batches above the fused decode
+// kernel's eight tokens): exact routing, then the expert products on tcgen05 tensor cores.
+//
+//   k_pf_logits  router logits (+ the shared-gate row), bit-identical to the reference
+//                (kernels/strata.cu:156-165): thread = one of the reference's 64 lanes for a
+//                register block of 8 tokens x 8 rows, lane-strided F32 sums without
+//                contraction, then the reference's tree across the two warps of the lane group
+//   k_pf_route   softmax / top-k / weights, one warp per token (route.cuh route_warp)
+//   k_pf_count   per token-chunk expert histograms
+//   k_pf_scan    per-expert offsets, the chunk list of the GEMMs (decreasing size)
+//   k_pf_place   stable (token-major) position of every (token, k) pair in its expert's
+//                segment, as src/prefill.js:55-61 groups them
+//   k_pf_xprep   B rows for the gate/up GEMM: each token's activations as FP16 times 2^k
+//                (largest |x| below 2^15), written at its pairs' positions and at row
+//                T*topK + t for the shared expert; per row the token, weight and 2^-k
+//   k_pf_gemm    gate/up (hidden = silu(gate) * up, FP16) then down (y += weight * D)
+// y is zeroed first and receives the shared expert and every routed pair by 16-byte atomic
+// adds, so y is not bit-reproducible run to run; it stays within 2e-3 relative L2 of the
+// reference (the FP16 tensor-core path's tolerance; tested). Routing is bit-exact.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "pf_gemm.cuh"
+#include "route.cuh"
+
+namespace strata {
+namespace pf {
+
+// ------------------------------------------------------------------ router logits
+constexpr int kLgT = 16, kLgR = 16, kLgKC = 256;  // CTA tile: tokens, rows; K chunk
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+        "@p cp.async.cg.shared.global [%0], [%1], 16;\n\t"
+        "@!p st.shared.v4.u32 [%0], {0, 0, 0, 0};\n\t}" ::"r"(su32(dst)),
+        "l"(src), "r"((unsigned)valid)
+        : "memory");
+}
+
+constexpr int kLgSmem = 2 * (kLgT + kLgR) * kLgKC * 4;  // double-buffered x and router tiles (64 KB)
+
+__global__ void __launch_bounds__(256) k_pf_logits(MoeLayerDev L, const float *__restrict__ x, int T, float *logits, float *sg) {
+    extern __shared__ __align__(16) float lg_smem[];
+    float(*xs)[kLgT][kLgKC] = reinterpret_cast<float(*)[kLgT][kLgKC]>(lg_smem);
+    float(*ws)[kLgR][kLgKC] = reinterpret_cast<float(*)[kLgR][kLgKC]>(lg_smem + 2 * kLgT * kLgKC);
+    const int H = L.width, E = L.experts;
+    const int t0 = blockIdx.x * kLgT, r0 = blockIdx.y * kLgR;
+    const int tid = threadIdx.x, lg = tid >> 6, l = tid & 63;
+    const int tb = (lg & 1) * 8, rb = (lg >> 1) * 8;  // this lane group's 8 tokens and 8 rows
+    auto load = [&](int buf, int c) {
+        for (int i = tid; i < kLgT * kLgKC / 4; i += 256) {  // 16 rows x 64 float4 each
+            const int row = i >> 6, c4 = i & 63;
+            const int t = t0 + row;
+            cp_async16(&xs[buf][row][4 * c4], x + (long long)min(t, T - 1) * H + c * kLgKC + 4 * c4, t < T);
+            const int r = r0 + row;
+            const float *W = r < E ? L.router + (long long)r * H : L.shared_gate;
+            cp_async16(&ws[buf][row][4 * c4], W + c * kLgKC + 4 * c4, r <= E);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    const int NC = H / kLgKC;
+    load(0, 0);
+    for (int c = 0; c < NC; ++c) {
+        if (c + 1 < NC) {
+            load((c + 1) & 1, c + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const int b = c & 1;
+#pragma unroll
+        for (int m = 0; m < kLgKC / 64; ++m) {  // element l + 64 m of the chunk: this lane's next term
+            float xv[8], wv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xv[i] = xs[b][tb + i][l + 64 * m];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) wv[j] = ws[b][rb + j][l + 64 * m];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], xv[i]));
+        }
+        __syncthreads();
+    }
+    // tree over the 64 lanes: lane l (< 32, first warp) adds lane l + 32 (second warp), then
+    // shuffles s = 16 .. 1; the staging reuses the x tiles
+    float *red = &xs[0][0][0] + lg * 64 * 32;  // [64 outputs][32 lanes]
+    if (l >= 32) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) red[(i * 8 + j) * 32 + (l - 32)] = acc[i][j];
+    }
+    __syncthreads();
+    if (l < 32) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float a = __fadd_rn(acc[i][j], red[(i * 8 + j) * 32 + l]);
+#pragma unroll
+                for (int s = 16; s > 0; s >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, s));
+                const int t = t0 + tb + i, r = r0 + rb + j;
+                if (l == 0 && t < T) {
+                    if (r < E) logits[(long long)t * E + r] = L.bias ? __fadd_rn(a, L.bias[r]) : a;
+                    else if (r == E) sg[t] = a;
+                }
+            }
+    }
+}
+
+// ------------------------------------------------------------------ routing
+__global__ void __launch_bounds__(128) k_pf_route(const float *logits, int T, int E, int K, int *ids, float *weights) {
+    __shared__ float lg[4][512];
+    __shared__ float sel[4][32];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 4 + w;
+    if (t >= T) return;
+    for (int e = lane; e < E; e += 32) lg[w][e] = logits[(long long)t * E + e];
+    __syncwarp();
+    route_warp(lg[w], E, K, ids + (long long)t * K, weights + (long long)t * K, sel[w]);
+}
+
+// ------------------------------------------------------------------ permutation
+constexpr int kTokChunk = 256;  // tokens per counting chunk
+
+__global__ void __launch_bounds__(256) k_pf_count(const int *ids, int T, int E, int K, int *chunk_counts) {
+    __shared__ int h[512];
+    for (int e = threadIdx.x; e < E; e += 256) h[e] = 0;
+    __syncthreads();
+    const int c = blockIdx.x;
+    const long long p0 = (long long)c * kTokChunk * K, p1 = min((long long)T * K, p0 + (long long)kTokChunk * K);
+    for (long long p = p0 + threadIdx.x; p < p1; p += 256) {
+        const int e = ids[p];
+        if (e >= 0 && e < E) atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += 256) chunk_counts[(long long)c * E + e] = h[e];
+}
+
+// One block of 512 threads: thread e walks the chunks (chunk_base = running count), then a
+// block scan gives the expert offsets; thread 0 writes the chunk list: the shared expert's
+// rows [T K, T K + T), then every expert's full 256-row chunks, then the remainders by
+// decreasing size (counting sort over 1..255).
+__global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, int T, int E, int K, int *offsets, Chunk *chunks,
+                                                 int *n_chunks) {
+    __shared__ int cnt[512], off[513];
+    __shared__ int rem_hist[256];
+    const int e = threadIdx.x;
+    int run = 0;
+    if (e < E)
+        for (int c = 0; c < n_tc; ++c) {
+            const int v = chunk_counts[(long long)c * E + e];
+            chunk_counts[(long long)c * E + e] = run;  // becomes the chunk's base within the expert
+            run += v;
+        }
+    cnt[e] = e < E ? run : 0;
+    if (e < 256) rem_hist[e] = 0;
+    __syncthreads();
+    if (e == 0) {
+        int s = 0;
+        for (int i = 0; i < E; ++i) {
+            off[i] = s;
+            s += cnt[i];
+        }
+        off[E] = s;
+    }
+    __syncthreads();
+    if (e <= E) offsets[e] = off[e];
+    if (e < E && (cnt[e] & 255)) atomicAdd(&rem_hist[cnt[e] & 255], 1);
+    __syncthreads();
+    if (e == 0) {
+        int n = 0;
+        for (int r = 0; r < T; r += kMaxN) chunks[n++] = Chunk{-1, T * K + r, min(kMaxN, T - r), 0};
+        for (int i = 0; i < E; ++i)
+            for (int r = 0; r + kMaxN <= cnt[i]; r += kMaxN) chunks[n++] = Chunk{i, off[i] + r, kMaxN, 0};
+        // remainders, largest first: start index of each size bucket
+        int start[256];
+        int s = n;
+        for (int sz = 255; sz >= 1; --sz) {
+            start[sz] = s;
+            s += rem_hist[sz];
+        }
+        for (int i = 0; i < E; ++i) {
+            const int r = cnt[i] & 255;
+            if (r) chunks[start[r]++] = Chunk{i, off[i] + (cnt[i] & ~255), r, 0};
+        }
+        *n_chunks = s;
+    }
+}
+
+// Stable positions: block c handles token chunk c in rounds of 256 pairs in (token, k) order;
+// a pair's rank = pairs of its expert in earlier chunks (chunk base) + earlier rounds (running
+// count) + earlier warps of the round (per-warp histograms) + earlier lanes (__match_any_sync).
+__global__ void __launch_bounds__(256) k_pf_place(const int *ids, int T, int E, int K, const int *chunk_base, const int *offsets,
+                                                  int *pos) {
+    __shared__ int run[512];
+    __shared__ unsigned short wh[8][512];
+    const int c = blockIdx.x, tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    for (int e = tid; e < E; e += 256) run[e] = 0;
+    const long long p0 = (long long)c * kTokChunk * K, p1 = min((long long)T * K, p0 + (long long)kTokChunk * K);
+    for (long long base = p0; base < p1; base += 256) {
+        for (int i = tid; i < 8 * 512; i += 256) (&wh[0][0])[i] = 0;
+        __syncthreads();
+        const long long p = base + tid;
+        const int e = p < p1 ? ids[p] : -1;
+        const bool valid = e >= 0 && e < E;
+        const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1);
+        const int rank_lane = __popc(same & ((1u << lane) - 1u));
+        if (valid && rank_lane == 0) wh[w][e] = (unsigned short)__popc(same);
+        __syncthreads();
+        if (valid) {
+            int before = 0;
+            for (int v = 0; v < w; ++v) before += wh[v][e];
+            pos[p] = offsets[e] + chunk_base[(long long)c * E + e] + run[e] + before + rank_lane;
+        } else if (p < p1) {
+            pos[p] = -1;
+        }
+        __syncthreads();
+        for (int e2 = tid; e2 < E; e2 += 256) {
+            int s = 0;
+#pragma unroll
+            for (int v = 0; v < 8; ++v) s += wh[v][e2];
+            run[e2] += s;
+        }
+        __syncthreads();
+    }
+}
+
+// One block per token: FP16 copies of x times 2^k at the token's pair rows and its shared row.
+__global__ void __launch_bounds__(256) k_pf_xprep(const float *__restrict__ x, int T, int H, int K, const int *pos, const float *weights,
+                                                  const float *sg, __half *B, float *row_scale, int *row_token, float *row_weight) {
+    const int t = blockIdx.x, tid = threadIdx.x;
+    __shared__ float red[8];
+    const int per = H / 256;  // 8 (H 2048) or 10 (H 2560)
+    float v[10];
+    float mx = 0.0f;
+    for (int i = 0; i < per; ++i) {
+        v[i] = x[(long long)t * H + tid * per + i];
+        mx = fmaxf(mx, fabsf(v[i]));
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red[i]);
+    // 2^k * max < 2^15 (FP16 keeps its 11 bits for the largest values)
+    const unsigned bits = __float_as_uint(mx);
+    int k = 15 - ((int)(bits >> 23) - 126);
+    k = (bits >> 23) == 0 ? 0 : k;
+    k = (bits >> 23) >= 255 ? 0 : k;
+    k = max(-126, min(126, k));
+    const float mul = __uint_as_float((unsigned)(k + 127) << 23), inv = __uint_as_float((unsigned)(127 - k) << 23);
+    __half h[10];
+    for (int i = 0; i < per; ++i) h[i] = __float2half_rn(v[i] * mul);
+    for (int kk = 0; kk <= K; ++kk) {
+        const long long row = kk < K ? pos[(long long)t * K + kk] : (long long)T * K + t;
+        if (row < 0) continue;
+        __half *dst = B + row * H + tid * per;
+        for (int i = 0; i < per; ++i) dst[i] = h[i];
+        if (tid == 0) {
+            row_scale[row] = inv;
+            row_token[row] = t;
+            row_weight[row] = kk < K ? weights[(long long)t * K + kk] : ref_sigmoid(sg[t]);
+        }
+    }
+}
+
+}  // namespace pf
+
+// ------------------------------------------------------------------ host
+namespace {
+
+struct PfScratch {
+    float *logits, *sg;
+    int *chunk_counts, *offsets, *pos, *row_token, *n_chunks;
+    float *row_scale, *row_weight;
+    pf::Chunk *chunks;
+    __half *B, *hidden;
+};
+size_t al(size_t n) { return (n + 255) & ~size_t(255); }
+PfScratch carve(void *base, int T, int H, int F, int E, int K) {
+    char *p = static_cast<char *>(base);
+    PfScratch s;
+    const long long rows = (long long)T * K + T;
+    const int n_tc = (T + pf::kTokChunk - 1) / pf::kTokChunk;
+    const int max_chunks = E + (T * K) / pf::kMaxN + (T + pf::kMaxN - 1) / pf::kMaxN + 1;
+    auto take = [&](size_t bytes) {
+        char *r = p;
+        p += al(bytes);
+        return r;
+    };
+    s.logits = (float *)take(sizeof(float) * T * E);
+    s.sg = (float *)take(sizeof(float) * T);
+    s.chunk_counts = (int *)take(sizeof(int) * (size_t)n_tc * E);
+    s.offsets = (int *)take(sizeof(int) * (E + 1));
+    s.pos = (int *)take(sizeof(int) * (size_t)T * K);
+    s.row_token = (int *)take(sizeof(int) * rows);
+    s.n_chunks = (int *)take(sizeof(int));
+    s.row_scale = (float *)take(sizeof(float) * rows);
+    s.row_weight = (float *)take(sizeof(float) * rows);
+    s.chunks = (pf::Chunk *)take(sizeof(pf::Chunk) * max_chunks);
+    s.B = (__half *)take(sizeof(__half) * rows * H);
+    s.hidden = (__half *)take(sizeof(__half) * rows * F);
+    return s;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+bool encode(CUtensorMap *m, CUtensorMapDataType dt, int rank, const void *base, const unsigned long long *dims,
+            const unsigned long long *strides, const unsigned *box, CUtensorMapSwizzle sw) {
+    auto fn = encoder();
+    if (!fn) return false;
+    cuuint64_t d[3] = {0, 0, 0}, st[2] = {0, 0};
+    cuuint32_t b[3] = {1, 1, 1}, es[3] = {1, 1, 1};
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        if (i + 1 < rank) st[i] = strides[i];
+    }
+    return fn(m, dt, rank, const_cast<void *>(base), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MODE>
+cudaError_t launch_gemm(const pf::GemmParams &p, int grid, cudaStream_t s) {
+    const size_t smem = sizeof(pf::GemmSmem) + 1024;
+    static int ready_device = -1;
+    int dev = 0;
+    STRATA_CUDA_TRY(cudaGetDevice(&dev));
+    if (ready_device != dev) {
+        STRATA_CUDA_TRY(cudaFuncSetAttribute(pf::k_pf_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        ready_device = dev;
+    }
+    pf::k_pf_gemm<MODE><<<grid, pf::kGemmThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int topK) {
+    const long long rows = (long long)tokens * topK + tokens;
+    const int n_tc = (tokens + pf::kTokChunk - 1) / pf::kTokChunk;
+    const int max_chunks = experts + (tokens * topK) / pf::kMaxN + (tokens + pf::kMaxN - 1) / pf::kMaxN + 1;
+    return al(sizeof(float) * tokens * experts) + al(sizeof(float) * tokens) + al(sizeof(int) * (size_t)n_tc * experts) +
+           al(sizeof(int) * (experts + 1)) + al(sizeof(int) * (size_t)tokens * topK) + al(sizeof(int) * rows) + al(sizeof(int)) +
+           al(sizeof(float) * rows) * 2 + al(sizeof(pf::Chunk) * max_chunks) + al(sizeof(__half) * rows * width) +
+           al(sizeof(__half) * rows * ff);
+}
+
+bool moe_prefill_supported(int width, int ff, int experts, int topK) {
+    return ((width == 2048 && ff == 512) || (width == 2560 && ff == 640)) && experts <= 512 && topK <= 32;
+}
+
+cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, float *y, int *ids, float *weights, void *scratch, int grid,
+                                cudaStream_t s, unsigned *err) {
+    const int H = L.width, F = L.ff, E = L.experts, K = L.topK;
+    const long long rows = (long long)T * K + T, bb = L.blob_words * 4;
+    PfScratch S = carve(scratch, T, H, F, E, K);
+    const int n_tc = (T + pf::kTokChunk - 1) / pf::kTokChunk;
+    static int logits_ready_device = -1;
+    int dev = 0;
+    STRATA_CUDA_TRY(cudaGetDevice(&dev));
+    if (logits_ready_device != dev) {
+        STRATA_CUDA_TRY(cudaFuncSetAttribute(pf::k_pf_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem));
+        logits_ready_device = dev;
+    }
+    pf::k_pf_logits<<<dim3((T + pf::kLgT - 1) / pf::kLgT, (E + 1 + pf::kLgR - 1) / pf::kLgR), 256, pf::kLgSmem, s>>>(L, x, T, S.logits,
+                                                                                                                   S.sg);
+    pf::k_pf_route<<<(T + 3) / 4, 128, 0, s>>>(S.logits, T, E, K, ids, weights);
+    pf::k_pf_count<<<n_tc, 256, 0, s>>>(ids, T, E, K, S.chunk_counts);
+    pf::k_pf_scan<<<1, 512, 0, s>>>(S.chunk_counts, n_tc, T, E, K, S.offsets, S.chunks, S.n_chunks);
+    pf::k_pf_place<<<n_tc, 256, 0, s>>>(ids, T, E, K, S.chunk_counts, S.offsets, S.pos);
+    pf::k_pf_xprep<<<T, 256, 0, s>>>(x, T, H, K, S.pos, weights, S.sg, S.B, S.row_scale, S.row_token, S.row_weight);
+    STRATA_CUDA_TRY(cudaGetLastError());
+    STRATA_CUDA_TRY(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * H, s));
+
+    const long long d_codes = 2LL * F * H / 4, gu_scales = 3LL * F * H / 4, d_scales = gu_scales + 2LL * F * (H / 64) * 2;
+    const unsigned char *blobs = reinterpret_cast<const unsigned char *>(L.blobs), *shared = reinterpret_cast<const unsigned char *>(L.shared_blob);
+    for (int mode = 0; mode < 2; ++mode) {
+        pf::GemmParams p;
+        std::memset(&p, 0, sizeof p);
+        p.chunks = S.chunks;
+        p.n_chunks = S.n_chunks;
+        p.blobs = blobs;
+        p.shared = shared;
+        p.blob_bytes = bb;
+        p.K = mode == 0 ? H : F;
+        p.rows_total = mode == 0 ? 2 * F : H;
+        p.NM = p.rows_total / 128;
+        p.codes_off = mode == 0 ? 0 : d_codes;
+        p.scales_off = mode == 0 ? gu_scales : d_scales;
+        p.row_scale = S.row_scale;
+        p.row_token = S.row_token;
+        p.row_weight = S.row_weight;
+        p.hidden = S.hidden;
+        p.y = y;
+        p.err = err;
+        p.spin_limit = 1ull << 22;
+        const unsigned long long cdims[3] = {(unsigned long long)p.K / 4, (unsigned long long)p.rows_total, (unsigned long long)E};
+        const unsigned long long cstr[2] = {(unsigned long long)p.K / 4, (unsigned long long)bb};
+        const unsigned cbox[3] = {64, 128, 1};
+        const unsigned long long sdims[3] = {(unsigned long long)p.K / 4, (unsigned long long)p.rows_total, 1ull};
+        if (!encode(&p.tm_codes[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blobs + p.codes_off, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_64B) ||
+            !encode(&p.tm_codes[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, shared + p.codes_off, sdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_64B))
+            return cudaErrorInvalidValue;
+        const void *bmat = mode == 0 ? (const void *)S.B : (const void *)S.hidden;
+        const unsigned long long bdims[2] = {(unsigned long long)p.K, (unsigned long long)rows};
+        const unsigned long long bstr[1] = {(unsigned long long)p.K * 2};
+        const unsigned bbox[2] = {64, 16};
+        if (!encode(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bmat, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaErrorInvalidValue;
+        STRATA_CUDA_TRY(mode == 0 ? launch_gemm<pf::kGateUp>(p, grid, s) : launch_gemm<pf::kDown>(p, grid, s));
+    }
+    return cudaSuccess;
+}
+
+}  // namespace strata
