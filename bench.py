@@ -4,7 +4,10 @@ Workload (the metric's decode b=1 case): one MoE layer, H 204
 routed experts, top-10 renormalised routing, one shared expert, expert intermediate 512,
 Q2 packed blobs (uniform 2-bit codes, FP16 scales |N(0,0.02)|), F32 router N(0,0.02),
 F32 activations N(0,1); seeded synthetic data. A step is one pass of the fused layer over
-one batch. Steps cycle over `--layers` distinct layer replicas (default 24: every layer's
+one batch. `--batch 8` and `--batch 64` are config 2's other decode sizes; `--batch 4096`
+is config 3 (prefill, router logits biased by a Zipf(1.1) per-expert offset). Batches above
+8 run the tensor-core prefill path; its roofline is the grouped GEMMs' FLOP rate against the
+measured sustained dense BF16 peak, timed by the library's phase profile in a second pass. Steps cycle over `--layers` distinct layer replicas (default 24: every layer's
 routed weights are evicted from the 126 MB L2 before the layer comes round again) with a
 fresh activation batch per step, so no step reads weights left in L2 by the previous one.
 
@@ -181,10 +184,20 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(batch: int, layers: int):
-    return {"workload": f"MoE layer decode b={batch} (H2048, E512 top-10, F512, Q2 experts + shared expert)", "batch": batch,
-            "hidden": WIDTH, "experts": EXPERTS, "top_k": TOPK, "ff": FF, "layers_cycled": layers,
+def workload_config(batch: int, layers: int, zipf=None):
+    kind = "prefill" if batch > 64 else "decode"
+    skew = f", Zipf({zipf}) router bias" if zipf else ""
+    return {"workload": f"MoE layer {kind} b={batch} (H2048, E512 top-10, F512, Q2 experts + shared expert{skew})", "batch": batch,
+            "hidden": WIDTH, "experts": EXPERTS, "top_k": TOPK, "ff": FF, "layers_cycled": layers, "zipf": zipf,
             "l2": "inputs larger than L2: distinct layer replicas cycled, fresh activations per step", "parallelism": "replicas"}
+
+
+def peak_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops_sustained"]), "measured (sustained dense bf16)"
+    return 1400.0, "fallback (sustained)"
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -198,8 +211,10 @@ def run_gpu_arm(args, world, rank, local):
     torch.cuda.set_device(local)
     b = CudaBackend(local)
     B, K, W, NL = args.batch, args.steps, args.warmup, args.layers
-    layers = [MoeLayer.synthesize(b, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK) for l in range(NL)]
-    n_x = K + W
+    zipf = args.zipf if args.zipf is not None else (1.1 if B > 64 else None)
+    layers = [MoeLayer.synthesize(b, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf) for l in range(NL)]
+    # distinct activation batches: every step for small batches, a ring of 8 for large ones
+    n_x = K + W if B <= 64 else min(K + W, 8)
     x_all = synth_activations(b, 2 + rank, n_x * B, WIDTH)
     y_all = b.alloc(n_x * B * WIDTH, zero=False)
     ids_all = b.alloc(n_x * B * TOPK, "i32")
@@ -215,13 +230,15 @@ def run_gpu_arm(args, world, rank, local):
     idss = [b.alloc(B * TOPK, "i32") for _ in range(n_x)]
     wss = [b.alloc(B * TOPK, zero=False) for _ in range(n_x)]
     b.idle()
+    slot = lambda s: s % n_x
 
     stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", local))
     from stratacuda_b200 import _lib as LL
     mode = LL.MOE_FAST if args.mode == "fast" else LL.MOE_EXACT
-    launches = 1 if (mode == LL.MOE_FAST and B <= 8) else 6
+    prefill = mode == LL.MOE_FAST and B > 8
+    launches = 1 if (mode == LL.MOE_FAST and B <= 8) else (8 if prefill else 6)
     for s in range(W):
-        layers[s % NL].forward(xs[s], B, ys[s], idss[s], wss[s], mode=mode)
+        layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
     b.idle()
     dist_barrier(world)
     torch.cuda.synchronize()
@@ -229,33 +246,40 @@ def run_gpu_arm(args, world, rank, local):
     with ClockSampler(local) as clocks:
         start.record(stream)
         for s in range(W, W + K):
-            layers[s % NL].forward(xs[s], B, ys[s], idss[s], wss[s], mode=mode)
+            layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
         end.record(stream)
         b.idle()
     torch.cuda.synchronize()
     dist_barrier(world)
     ms = start.elapsed_time(end)
     ms_max = dist_max(ms, world)
-    # algorithmic bytes per step from the routing that actually happened
+    # algorithmic bytes per step from the routing that actually happened (the last n_x steps)
     bytes_steps = []
-    for s in range(W, W + K):
-        ids = b.read(idss[s])
+    for s in range(max(W, W + K - n_x), W + K):
+        ids = b.read(idss[slot(s)])
         U = len(set(ids.tolist()))
         bytes_steps.append((U + 1) * BLOB_BYTES + ROUTER_BYTES + GATE_BYTES + 2 * B * WIDTH * 4)
     alg_bytes = float(np.mean(bytes_steps))
     step_s = ms / 1000.0 / K
     hbm_peak, peak_kind = peaks()
     achieved = alg_bytes / step_s / 1e9
+    if prefill:
+        roofline = prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K)
+    else:
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+                    "peak_kind": peak_kind,
+                    "kernel": ("k_moe_fast (one persistent launch per step)" if launches == 1 else "fused exact MoE layer (6 launches per step)"),
+                    "algorithmic_bytes_per_step": alg_bytes}
 
     # end to end through the C-ABI with host buffers (pinned), host-timed
-    e2e_steps = min(K, max(20, K // 2))
+    e2e_steps = min(K, max(20, K // 2)) if B <= 64 else min(K, 8)
     hx = torch.empty(e2e_steps, B * WIDTH, dtype=torch.float32, pin_memory=True)
     hx.copy_(torch.from_numpy(b.read(x_all, count=e2e_steps * B * WIDTH).reshape(e2e_steps, B * WIDTH)))
     hy = torch.empty(B * WIDTH, dtype=torch.float32, pin_memory=True)
     hx_np, hy_np = hx.numpy(), hy.numpy()
     lib, ctx = b.lib, b.ctx
     xbuf, ybuf = xs[0], ys[0]
-    for s in range(3):
+    for s in range(min(3, e2e_steps)):
         b.write(xbuf, hx_np[s])
         layers[s % NL].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
         b._check(lib.strata_read(ctx, ybuf.handle, hy_np.ctypes.data, B * WIDTH, 0))
@@ -275,21 +299,16 @@ def run_gpu_arm(args, world, rank, local):
                "sample": f"{info['tokens']} decode tokens (B=1) of layer 0 through the reference's WASM-path order, "
                          f"{info['seconds']} s on {info['cores']} host threads"}
 
-    traffic = None
     tp = ROOT / "profiles" / "traffic.json"
-    if tp.exists():
-        traffic = json.loads(tp.read_text()).get(f"decode_b{B}")
+    if tp.exists() and roofline["bound"] == "hbm":
+        roofline["traffic"] = json.loads(tp.read_text()).get(f"decode_b{B}")
 
     total_tokens = B * K * world
     line = {"metric": METRIC, "value": total_tokens / (ms_max / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded SplitMix64; BASELINE config 2 distributions)",
-            "config": workload_config(B, NL),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                         "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": ("k_moe_fast (one persistent launch per step)" if launches == 1
-                                    else "fused exact MoE layer (6 launches per step)"),
-                         "algorithmic_bytes_per_step": alg_bytes},
+            "config": workload_config(B, NL, zipf),
+            "roofline": roofline,
             "e2e": {"value": B * e2e_steps * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * WIDTH * 4,
                     "d2h_bytes_per_step": B * WIDTH * 4},
             "gpu_launches": launches * K,
@@ -303,6 +322,25 @@ def run_gpu_arm(args, world, rank, local):
     b.dispose()
 
 
+def prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K):
+    """Second pass with the library's phase profile: the grouped GEMMs' device time against
+    their algorithmic FLOPs, 2 * 3 * H * F * (pairs + tokens) per step (gate/up: 2F x H per
+    row, down: H x F per row; every pair and every token's shared-expert row)."""
+    steps = max(3, min(K, 20))
+    b.profile(True)
+    for s in range(steps):
+        layers[s % NL].forward(xs[s % n_x], B, ys[s % n_x], idss[s % n_x], wss[s % n_x], mode=mode)
+    ph, calls = b.profile_read()
+    b.profile(False)
+    flops = 2.0 * 3 * WIDTH * FF * (B * TOPK + B)
+    gemm_s = (ph["gemm_gate_up"] + ph["gemm_down"]) / 1000.0 / max(1, calls)
+    achieved = flops / gemm_s / 1e12
+    peak, kind = peak_tflops()
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+            "peak_kind": kind, "kernel": "k_pf_gemm gate/up + down (tcgen05, persistent)", "algorithmic_flops_per_step": flops,
+            "phase_ms_per_step": {k: v / max(1, calls) for k, v in ph.items()}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -314,6 +352,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--mode", default="fast", choices=["fast", "exact"])
+    ap.add_argument("--zipf", type=float, default=None, help="router bias skew (default: 1.1 for batches above 64)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

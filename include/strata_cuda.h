@@ -158,6 +158,17 @@ typedef struct {
 int strata_moe_forward_noalloc(const strata_moe_layer_dev *layer, const float *x, int32_t tokens, float *y, int32_t *ids,
                                float *weights, void *stream, char *msg, size_t msg_cap);
 
+/* ---- device-time profile of the fused layer (diagnostics; no reference counterpart) ----
+ * While enabled, strata_moe_forward records CUDA events around its phases on the context's
+ * stream. strata_profile_read synchronises, adds the phase times (milliseconds) of every call
+ * since the last read into ms[0..n) and resets them; *calls receives the number of calls.
+ * Phases: 0 routing (prefill path: router logits, top-k, permutation, activation rows),
+ * 1 gate/up tensor-core GEMM, 2 down tensor-core GEMM (both prefill path), 3 fused decode
+ * kernel (decode path). */
+#define STRATA_PHASES 4
+int strata_profile(strata_ctx *ctx, int32_t enable);
+int strata_profile_read(strata_ctx *ctx, double *ms, int32_t n, uint64_t *calls);
+
 /* ---- seeded synthetic workload (device generator; same bytes as stratacuda_b200/synth.py) ---- */
 /* `count` expert blobs of one layer starting at `first_expert` into buf at element offset. */
 int strata_synth_blobs(strata_ctx *ctx, strata_buf buf, uint64_t offset, uint64_t seed, int32_t layer, int32_t first_expert,

@@ -153,6 +153,19 @@ class CudaBackend:
         self.lib.strata_info(self.ctx, buf, len(buf))
         return json.loads(buf.value.decode())
 
+    PHASES = ("routing", "gemm_gate_up", "gemm_down", "decode_kernel")
+
+    def profile(self, enable: bool) -> None:
+        """Record device time of the fused layer's phases (strata_profile)."""
+        self._check(self.lib.strata_profile(self.ctx, int(bool(enable))))
+
+    def profile_read(self) -> tuple[dict, int]:
+        """Phase times in ms summed over the calls since the last read, and the call count."""
+        ms = (C.c_double * len(self.PHASES))()
+        calls = C.c_uint64(0)
+        self._check(self.lib.strata_profile_read(self.ctx, ms, len(self.PHASES), C.byref(calls)))
+        return dict(zip(self.PHASES, list(ms))), int(calls.value)
+
     @property
     def stream_handle(self) -> int:
         s = C.c_void_p()

@@ -3,6 +3,7 @@
 // fused mixture-of-experts layer and the synthetic-workload generator.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -34,6 +35,15 @@ struct strata_ctx {
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
     uint64_t dispatches = 0, fused_calls = 0;
+    // strata_profile: event pairs (phase, start, end) awaiting strata_profile_read
+    bool profile = false;
+    struct Mark {
+        int phase;
+        cudaEvent_t a, b;
+    };
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> spare_events;
+    uint64_t profiled_calls = 0;
     std::string last_error;
     char device_name[256] = {0};
     int sms = 0;
@@ -215,6 +225,13 @@ int strata_destroy(strata_ctx *ctx) {
     for (auto &kv : ctx->buffers) cudaFree(kv.second.ptr);
     ctx->buffers.clear();
     if (ctx->workspace) cudaFree(ctx->workspace);
+    for (const auto &m : ctx->marks) {
+        ctx->spare_events.push_back(m.a);
+        ctx->spare_events.push_back(m.b);
+    }
+    std::sort(ctx->spare_events.begin(), ctx->spare_events.end());
+    ctx->spare_events.erase(std::unique(ctx->spare_events.begin(), ctx->spare_events.end()), ctx->spare_events.end());
+    for (cudaEvent_t e : ctx->spare_events) cudaEventDestroy(e);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->fast_sync) cudaFree(ctx->fast_sync);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
@@ -391,6 +408,34 @@ int strata_info(strata_ctx *ctx, char *json, size_t cap) {
     return n;
 }
 
+int strata_profile(strata_ctx *ctx, int32_t enable) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    ctx->profile = enable != 0;
+    return STRATA_OK;
+}
+
+int strata_profile_read(strata_ctx *ctx, double *ms, int32_t n, uint64_t *calls) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (int r = use_device(ctx)) return r;
+    CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    for (int i = 0; i < n && ms; ++i) ms[i] = 0.0;
+    std::vector<cudaEvent_t> seen;
+    for (const auto &m : ctx->marks) {
+        float t = 0.0f;
+        CUDA_OR_FAIL(ctx, cudaEventElapsedTime(&t, m.a, m.b), "cudaEventElapsedTime");
+        if (ms && m.phase < n) ms[m.phase] += t;
+        seen.push_back(m.a);
+        seen.push_back(m.b);
+    }
+    std::sort(seen.begin(), seen.end());
+    seen.erase(std::unique(seen.begin(), seen.end()), seen.end());
+    for (cudaEvent_t e : seen) ctx->spare_events.push_back(e);
+    ctx->marks.clear();
+    if (calls) *calls = ctx->profiled_calls;
+    ctx->profiled_calls = 0;
+    return STRATA_OK;
+}
+
 int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                        strata_buf weights, int32_t mode) {
     if (!ctx) return STRATA_ERR_RANGE;
@@ -448,13 +493,38 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     }
     MoeLayerDev L{l.width, l.ff, l.experts, l.top_k, (const float *)ptr[0], (const float *)ptr[1], (const unsigned *)ptr[2], bw,
                   (const unsigned *)ptr[3], (const float *)ptr[4]};
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    if (ctx->profile && (fast || prefill)) {
+        for (cudaEvent_t &x : ev) {
+            if (!ctx->spare_events.empty()) {
+                x = ctx->spare_events.back();
+                ctx->spare_events.pop_back();
+            } else {
+                CUDA_OR_FAIL(ctx, cudaEventCreate(&x), "cudaEventCreate");
+            }
+        }
+        ++ctx->profiled_calls;
+    }
     cudaError_t e;
     if (fast) {
+        if (ev[0]) CUDA_OR_FAIL(ctx, cudaEventRecord(ev[0], ctx->stream), "cudaEventRecord");
         e = moe_forward_fast(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
                              ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev);
+        if (ev[0]) {
+            CUDA_OR_FAIL(ctx, cudaEventRecord(ev[1], ctx->stream), "cudaEventRecord");
+            ctx->marks.push_back({3, ev[0], ev[1]});
+            ctx->spare_events.push_back(ev[2]);
+            ctx->spare_events.push_back(ev[3]);
+        }
     } else if (prefill) {
         e = moe_forward_prefill(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
-                                ctx->sms, ctx->stream, ctx->err_dev);
+                                ctx->sms, ctx->stream, ctx->err_dev, ev[0] ? ev : nullptr);
+        if (ev[0]) {
+            // the three phases share their boundary events: copies of the handles in each pair
+            ctx->marks.push_back({0, ev[0], ev[1]});
+            ctx->marks.push_back({1, ev[1], ev[2]});
+            ctx->marks.push_back({2, ev[2], ev[3]});
+        }
     } else {
         MoeScratch s = moe_scratch_carve(ctx->workspace, tokens, l.width, l.ff, l.experts, l.top_k);
         e = moe_forward_exact(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], s, ctx->stream,

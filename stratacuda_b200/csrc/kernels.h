@@ -75,8 +75,10 @@ cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, f
 // the GEMMs' persistent grid (one CTA per SM).
 bool moe_prefill_supported(int width, int ff, int experts, int topK);
 size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int topK);
+// `marks` (nullable): four events recorded before routing, after routing, after the gate/up
+// GEMM and after the down GEMM.
 cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
-                                int grid, cudaStream_t s, unsigned *err);
+                                int grid, cudaStream_t s, unsigned *err, cudaEvent_t *marks = nullptr);
 
 // Device synthetic generator (csrc/synth.cu), same bytes as stratacuda_b200/synth.py.
 cudaError_t synth_expert_blobs(unsigned *out, unsigned long long seed, int layer, int first_expert, int count, int width, int ff,

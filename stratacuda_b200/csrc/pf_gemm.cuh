@@ -1,11 +1,14 @@
 // Grouped Q2 x FP16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), the engine of
 // the prefill path.
 //
-// One tile = (expert slot, 128 weight rows, up to 256 rows of the B matrix). D[128][N] =
+// One tile = (expert slot, 128 weight rows, up to 192 rows of the B matrix). D[128][N] =
 // A[128][K] . B[N][K]^T accumulates in TMEM (FP32, 128 lanes x N columns). A is the slot's
-// Q2 weights, dequantised in shared memory to FP16: w = (code - 1) * scale, exact in FP16 (the
-// scale is an FP16 and code - 1 is in {-1, 0, 1, 2}). B rows are FP16 activations (gate/up:
-// the tokens of the slot, scaled per token by a power of two; down: the hidden values).
+// Q2 weights, dequantised to FP16 straight into TMEM (tcgen05.st), where the MMA reads it:
+// w = (code - 1) * scale, exact in FP16 (the scale is an FP16 and code - 1 is in {-1, 0, 1,
+// 2}). Keeping A out of shared memory leaves shared-memory bandwidth to B alone (writing and
+// re-reading a dequantised A tile there cost as much as B itself). B rows are FP16
+// activations (gate/up: the tokens of the slot, scaled per token by a power of two; down:
+// the hidden values), by TMA into a 128-byte-swizzled K-major ring.
 //
 // Persistent kernel, one CTA per SM, tiles dealt round-robin (tile i on CTA i % G). Tile i is
 // chunk i / NM of the chunk list (slot, first B row, rows) and weight block i % NM; the chunk
@@ -13,10 +16,12 @@
 //   warp 0      TMA producer: per tile the rows' FP16 scales (one bulk copy); per 256-column
 //               super-block the packed codes (one 128-row x 64-byte box, 64-byte swizzle);
 //               per 64-column K-block the B rows (16-row boxes, 128-byte swizzle)
-//   warp 1      allocates TMEM (512 columns: two 256-column accumulators) and issues the MMAs
-//               from one thread: per K-block four tcgen05.mma (K = 16), then tcgen05.commit
-//   warps 2-9   dequantise: two threads per row convert its 64 codes of a K-block into the
-//               128-byte-swizzled K-major FP16 layout the MMA reads
+//   warp 1      allocates TMEM (512 columns: two 192-column accumulators and four 32-column
+//               A stages) and issues the MMAs from one thread: per K-block four tcgen05.mma
+//               (K = 16, A from TMEM, B from shared memory), then tcgen05.commit
+//   warps 2-9   dequantise: warp w writes TMEM lanes 32 (w % 4) .. (a warp reaches only its
+//               lane quarter): thread = one A row and half of its 64 codes of a K-block, 16
+//               32-bit columns of two FP16 each
 //   warps 10-13 epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32 (w % 4) ..),
 //               gate/up: hidden = silu(gate) * up -> FP16 rows; down: weighted rows added to y
 // The accumulators are double-buffered, so a tile's epilogue overlaps the next tile's MMAs.
@@ -35,9 +40,12 @@ constexpr int kGemmWarps = 14;
 constexpr int kGemmThreads = kGemmWarps * 32;
 constexpr int kDeqThreads = 256;  // warps 2-9
 constexpr int kEpiWarp0 = 10;     // warps 10-13
-constexpr int kStages = 3;        // B + dequantised-A stages
-constexpr int kApkStages = 2;     // packed-code super-blocks
-constexpr int kMaxN = 256;        // B rows per tile
+constexpr int kStages = 5;        // B stages
+constexpr int kAStages = 4;       // dequantised-A stages (TMEM)
+constexpr int kApkStages = 4;     // packed-code super-blocks
+constexpr int kMaxN = 192;        // B rows per tile
+constexpr int kAccCols = 192;     // TMEM columns per accumulator
+constexpr int kACol0 = 2 * kAccCols;  // first TMEM column of the A stages (32 columns each)
 constexpr int kKBlock = 64;       // K elements per stage (one scale group, one 128-byte swizzle row)
 constexpr int kSuper = 4;         // K-blocks per packed super-block (256 codes = 64 bytes per row)
 
@@ -168,6 +176,23 @@ __device__ __forceinline__ void tmem_ld32(unsigned taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(unsigned taddr, const unsigned (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]),
+        "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void mma_f16_ts(unsigned tmem_d, unsigned tmem_a, unsigned long long b, unsigned idesc, int accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // 16 codes (one 32-bit word, code i at bits 2i) times one FP16 scale -> 16 FP16 in order,
 // as 8 half2 words. The FP16 bits 0x6400 | c are 1024 + c; minus 1025 gives c - 1 exactly,
 // and (c - 1) * s is exact (c - 1 in {-1, 0, 1, 2}).
@@ -189,11 +214,13 @@ __device__ __forceinline__ void dequant16(unsigned w, __half2 s2, unsigned (&out
 
 struct __align__(1024) GemmSmem {
     unsigned char b[kStages][kMaxN * 128];      // B rows, 128-byte swizzle (1024-aligned)
-    unsigned char a16[kStages][128 * 128];      // dequantised A, 128-byte swizzle
     unsigned char apk[kApkStages][128 * 64];    // packed codes of a super-block, 64-byte swizzle
     unsigned char staging[kMaxN * 128];         // epilogue staging: gate/up hidden FP16 [N][64] / down F32 [32][128]
     unsigned short scl[2][128 * 40];            // FP16 scales of the tile's 128 rows (<= 40 groups per row)
-    unsigned long long full[kStages], empty[kStages], a16_full[kStages];
+    float row_f[kMaxN];                         // epilogue: per B row scale (gate/up) or weight (down)
+    int row_t[kMaxN];                           // epilogue: per B row token (down)
+    unsigned long long full[kStages], empty[kStages];
+    unsigned long long a_full[kAStages], a_empty[kAStages];
     unsigned long long apk_full[kApkStages], apk_empty[kApkStages];
     unsigned long long scl_full[2], scl_empty[2];
     unsigned long long tmem_full[2], tmem_empty[2];
@@ -219,7 +246,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
         for (int s = 0; s < kStages; ++s) {
             bar_init(&S.full[s], 1);
             bar_init(&S.empty[s], 1);
-            bar_init(&S.a16_full[s], kDeqThreads);
+        }
+        for (int s = 0; s < kAStages; ++s) {
+            bar_init(&S.a_full[s], kDeqThreads);
+            bar_init(&S.a_empty[s], 1);
         }
         for (int s = 0; s < kApkStages; ++s) {
             bar_init(&S.apk_full[s], 1);
@@ -235,7 +265,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.abort_flag = 0;
     }
-    if (warp == 1) {  // TMEM: 512 columns, two 256-column accumulators
+    if (warp == 1) {  // TMEM: 512 columns: two accumulators and the A stages
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(su32(&S.tmem_base)) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -306,17 +336,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
                 tc_fence_after();
                 const int N = (t.n + 15) & ~15;
                 const unsigned idesc = idesc_f16(128, N);
-                const unsigned d = tmem + buf * 256;
+                const unsigned d = tmem + buf * kAccCols;
                 for (int kb = 0; kb < NKB && ok; ++kb, ++kb_count) {
-                    const int s = kb_count % kStages;
-                    const unsigned ph = (kb_count / kStages) & 1;
-                    if (!(ok = wait(&S.full[s], ph) && wait(&S.a16_full[s], ph))) break;
+                    const int s = kb_count % kStages, sa = kb_count % kAStages;
+                    if (!(ok = wait(&S.full[s], (kb_count / kStages) & 1) && wait(&S.a_full[sa], (kb_count / kAStages) & 1))) break;
                     tc_fence_after();
-                    const unsigned long long ad = sw128_desc(su32(S.a16[s])), bd = sw128_desc(su32(S.b[s]));
+                    const unsigned a = tmem + kACol0 + 32 * sa;
+                    const unsigned long long bd = sw128_desc(su32(S.b[s]));
 #pragma unroll
-                    for (int k = 0; k < kKBlock / 16; ++k)  // K = 16 per MMA: +32 bytes inside the swizzled row
-                        mma_f16(d, ad + 2 * k, bd + 2 * k, idesc, kb > 0 || k > 0);
+                    for (int k = 0; k < kKBlock / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, +32 bytes inside the swizzled B row
+                        mma_f16_ts(d, a + 8 * k, bd + 2 * k, idesc, kb > 0 || k > 0);
                     mma_commit(&S.empty[s]);
+                    mma_commit(&S.a_empty[sa]);
                 }
                 if (ok) mma_commit(&S.tmem_full[buf]);
             }
@@ -326,39 +357,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
         }
     } else if (warp < kEpiWarp0) {
         // ---------------------------------------------------------------- dequantise
-        const int r = (tid - 64) >> 1, hf = (tid - 64) & 1;  // A row 0..127, half of its 64 codes
+        const int quarter = warp & 3, hf = (warp - 2) >> 2;  // TMEM lane quarter; codes 32 hf .. 32 hf + 31
+        const int r = 32 * quarter + lane;                   // A row 0..127 = TMEM lane
+        const unsigned tlane = (unsigned)(32 * quarter) << 16;
         int kb_count = 0, sb_count = 0, lt = 0;
         bool ok = true;
         for (int ti = cta; ti < n_tiles && ok; ti += G, ++lt) {
             const int ts = lt & 1;
-            if (!(ok = wait(&S.scl_full[ts], (lt >> 1) & 1))) break;
+            // waits are voted warp-wide: the TMEM stores below need the whole warp converged
+            if (!(ok = __all_sync(0xffffffffu, wait(&S.scl_full[ts], (lt >> 1) & 1)))) break;
             for (int sb = 0; sb < NSB && ok; ++sb, ++sb_count) {
-                const int sa = sb_count % kApkStages;
-                if (!(ok = wait(&S.apk_full[sa], (sb_count / kApkStages) & 1))) break;
+                const int sp = sb_count % kApkStages;
+                if (!(ok = __all_sync(0xffffffffu, wait(&S.apk_full[sp], (sb_count / kApkStages) & 1)))) break;
                 const int kb_end = min(NKB, (sb + 1) * kSuper);
                 for (int kb = sb * kSuper; kb < kb_end; ++kb, ++kb_count) {
-                    const int s = kb_count % kStages;
-                    if (!(ok = wait(&S.empty[s], ((kb_count / kStages) & 1) ^ 1))) break;
+                    const int sa = kb_count % kAStages;
+                    if (!(ok = __all_sync(0xffffffffu, wait(&S.a_empty[sa], ((kb_count / kAStages) & 1) ^ 1)))) break;
+                    tc_fence_after();
                     // row r's 16 code bytes of this K-block: chunk c of its 64-byte row, stored at
                     // c ^ ((r >> 1) & 3) by the 64-byte swizzle; this thread takes words 2 hf, 2 hf + 1
                     const int c = kb - sb * kSuper;
-                    const uint2 w = *reinterpret_cast<const uint2 *>(S.apk[sa] + r * 64 + ((c ^ ((r >> 1) & 3)) << 4) + 8 * hf);
+                    const uint2 w = *reinterpret_cast<const uint2 *>(S.apk[sp] + r * 64 + ((c ^ ((r >> 1) & 3)) << 4) + 8 * hf);
                     const __half sc = __ushort_as_half(S.scl[ts][r * NGRP + kb]);
                     const __half2 s2 = __halves2half2(sc, sc);
-                    unsigned o[2][8];
-                    dequant16(w.x, s2, o[0]);
-                    dequant16(w.y, s2, o[1]);
-                    unsigned char *row = S.a16[s] + r * 128;
+                    unsigned lo[8], hi[8], o[16];
+                    dequant16(w.x, s2, lo);
+                    dequant16(w.y, s2, hi);
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) {  // word 2 hf + q: 16 FP16 = chunks 2 (2 hf + q) and 2 (2 hf + q) + 1
-                        const int cq = 2 * (2 * hf + q);
-                        *reinterpret_cast<uint4 *>(row + ((cq ^ (r & 7)) << 4)) = make_uint4(o[q][0], o[q][1], o[q][2], o[q][3]);
-                        *reinterpret_cast<uint4 *>(row + (((cq + 1) ^ (r & 7)) << 4)) = make_uint4(o[q][4], o[q][5], o[q][6], o[q][7]);
+                    for (int i = 0; i < 8; ++i) {
+                        o[i] = lo[i];
+                        o[8 + i] = hi[i];
                     }
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
-                    bar_arrive(&S.a16_full[s]);
+                    // column j holds K elements 2j, 2j + 1: this half's 32 elements are 16 columns
+                    __syncwarp();
+                    tmem_st16(tmem + tlane + kACol0 + 32 * sa + 16 * hf, o);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    bar_arrive(&S.a_full[sa]);
                 }
-                bar_arrive(&S.apk_empty[sa]);
+                bar_arrive(&S.apk_empty[sp]);
             }
             bar_arrive(&S.scl_empty[ts]);
         }
@@ -375,21 +412,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
             const int buf = lt & 1;
             if (!(ok = ep_all(wait(&S.tmem_full[buf], (lt >> 1) & 1)))) break;
             tc_fence_after();
-            const unsigned tbase = tmem + ((unsigned)(32 * quarter) << 16) + buf * 256;
+            const unsigned tbase = tmem + ((unsigned)(32 * quarter) << 16) + buf * kAccCols;
             const int N = (t.n + 15) & ~15;
+            // the tile's B-row metadata, once
+            for (int i = et; i < t.n; i += 128) {
+                S.row_f[i] = MODE == kGateUp ? __ldg(P.row_scale + t.row0 + i) : __ldg(P.row_weight + t.row0 + i);
+                if (MODE == kDown) S.row_t[i] = __ldg(P.row_token + t.row0 + i);
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
             for (int c0 = 0; c0 < N; c0 += 32) {
                 float v[32];
+                __syncwarp();
                 tmem_ld32(tbase + c0, v);
                 if (MODE == kGateUp) {
                     // row 2i = gate_i, 2i + 1 = up_i (adjacent lanes); hidden index 64 mtile + row / 2
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int n = c0 + j;
-                        const float sc = n < t.n ? __ldg(P.row_scale + t.row0 + n) : 0.0f;
+                        const float sc = n < t.n ? S.row_f[n] : 0.0f;
                         const float a = v[j] * sc;
                         const float up = __shfl_xor_sync(0xffffffffu, a, 1);
                         if (!(lane & 1) && n < t.n) {
-                            const float h = __fmul_rn(ref_silu(a), up);
+                            const float h = a / (1.0f + __expf(-a)) * up;  // silu(gate) * up (prefill tolerance 2e-3)
                             reinterpret_cast<__half *>(S.staging)[n * 64 + (row >> 1)] = __float2half_rn(h);
                         }
                     }
@@ -403,8 +447,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
                         const int j = i >> 5, q = i & 31, n = c0 + j;
                         if (n < t.n) {
                             const float4 s4 = reinterpret_cast<const float4 *>(st)[j * 32 + q];
-                            const float w = __ldg(P.row_weight + t.row0 + n);
-                            float *dst = P.y + (long long)__ldg(P.row_token + t.row0 + n) * P.rows_total + 128 * t.mtile + 4 * q;
+                            const float w = S.row_f[n];
+                            float *dst = P.y + (long long)S.row_t[n] * P.rows_total + 128 * t.mtile + 4 * q;
                             asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(s4.x * w), "f"(s4.y * w),
                                          "f"(s4.z * w), "f"(s4.w * w)
                                          : "memory");
@@ -424,14 +468,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
                     const uint4 val = reinterpret_cast<const uint4 *>(S.staging)[n * 8 + q];
                     *reinterpret_cast<uint4 *>(P.hidden + (long long)(t.row0 + n) * HID + 64 * t.mtile + 8 * q) = val;
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
             }
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // staging and row metadata free for the next tile
         }
     }
 
     __syncthreads();
     if (tid == 0 && S.abort_flag) raise_error(P.err, kErrWaitTimeout);
     if (warp == 1) {
+        __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }

@@ -152,12 +152,12 @@ __global__ void __launch_bounds__(256) k_pf_count(const int *ids, int T, int E, 
 
 // One block of 512 threads: thread e walks the chunks (chunk_base = running count), then a
 // block scan gives the expert offsets; thread 0 writes the chunk list: the shared expert's
-// rows [T K, T K + T), then every expert's full 256-row chunks, then the remainders by
-// decreasing size (counting sort over 1..255).
+// rows [T K, T K + T), then every expert's full kMaxN-row chunks, then the remainders by
+// decreasing size (counting sort over 1 .. kMaxN - 1).
 __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, int T, int E, int K, int *offsets, Chunk *chunks,
                                                  int *n_chunks) {
     __shared__ int cnt[512], off[513];
-    __shared__ int rem_hist[256];
+    __shared__ int rem_hist[kMaxN];
     const int e = threadIdx.x;
     int run = 0;
     if (e < E)
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, in
             run += v;
         }
     cnt[e] = e < E ? run : 0;
-    if (e < 256) rem_hist[e] = 0;
+    if (e < kMaxN) rem_hist[e] = 0;
     __syncthreads();
     if (e == 0) {
         int s = 0;
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, in
     }
     __syncthreads();
     if (e <= E) offsets[e] = off[e];
-    if (e < E && (cnt[e] & 255)) atomicAdd(&rem_hist[cnt[e] & 255], 1);
+    if (e < E && cnt[e] % kMaxN) atomicAdd(&rem_hist[cnt[e] % kMaxN], 1);
     __syncthreads();
     if (e == 0) {
         int n = 0;
@@ -187,15 +187,15 @@ __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, in
         for (int i = 0; i < E; ++i)
             for (int r = 0; r + kMaxN <= cnt[i]; r += kMaxN) chunks[n++] = Chunk{i, off[i] + r, kMaxN, 0};
         // remainders, largest first: start index of each size bucket
-        int start[256];
+        int start[kMaxN];
         int s = n;
-        for (int sz = 255; sz >= 1; --sz) {
+        for (int sz = kMaxN - 1; sz >= 1; --sz) {
             start[sz] = s;
             s += rem_hist[sz];
         }
         for (int i = 0; i < E; ++i) {
-            const int r = cnt[i] & 255;
-            if (r) chunks[start[r]++] = Chunk{i, off[i] + (cnt[i] & ~255), r, 0};
+            const int r = cnt[i] % kMaxN;
+            if (r) chunks[start[r]++] = Chunk{i, off[i] + cnt[i] - r, r, 0};
         }
         *n_chunks = s;
     }
@@ -375,7 +375,9 @@ bool moe_prefill_supported(int width, int ff, int experts, int topK) {
 }
 
 cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, float *y, int *ids, float *weights, void *scratch, int grid,
-                                cudaStream_t s, unsigned *err) {
+                                cudaStream_t s, unsigned *err, cudaEvent_t *marks) {
+    auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
+    STRATA_CUDA_TRY(mark(0));
     const int H = L.width, F = L.ff, E = L.experts, K = L.topK;
     const long long rows = (long long)T * K + T, bb = L.blob_words * 4;
     PfScratch S = carve(scratch, T, H, F, E, K);
@@ -396,6 +398,7 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
     pf::k_pf_xprep<<<T, 256, 0, s>>>(x, T, H, K, S.pos, weights, S.sg, S.B, S.row_scale, S.row_token, S.row_weight);
     STRATA_CUDA_TRY(cudaGetLastError());
     STRATA_CUDA_TRY(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * H, s));
+    STRATA_CUDA_TRY(mark(1));
 
     const long long d_codes = 2LL * F * H / 4, gu_scales = 3LL * F * H / 4, d_scales = gu_scales + 2LL * F * (H / 64) * 2;
     const unsigned char *blobs = reinterpret_cast<const unsigned char *>(L.blobs), *shared = reinterpret_cast<const unsigned char *>(L.shared_blob);
@@ -432,6 +435,7 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
         const unsigned bbox[2] = {64, 16};
         if (!encode(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bmat, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaErrorInvalidValue;
         STRATA_CUDA_TRY(mode == 0 ? launch_gemm<pf::kGateUp>(p, grid, s) : launch_gemm<pf::kDown>(p, grid, s));
+        STRATA_CUDA_TRY(mark(2 + mode));
     }
     return cudaSuccess;
 }
