@@ -33,6 +33,7 @@ namespace pf {
 
 // ------------------------------------------------------------------ router logits
 constexpr int kLgT = 16, kLgR = 16, kLgKC = 256;  // CTA tile: tokens, rows; K chunk
+constexpr int kLgSmem = 2 * (kLgT + kLgR) * kLgKC * 4;  // double-buffered x and router tiles (64 KB)
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
     asm volatile(
@@ -43,8 +44,9 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool vali
         : "memory");
 }
 
-constexpr int kLgSmem = 2 * (kLgT + kLgR) * kLgKC * 4;  // double-buffered x and router tiles (64 KB)
-
+// Products and sums are scalar __fmul_rn / __fadd_rn (the paired F32 instructions of sm_100
+// did not reproduce the scalar rounded chains bit for bit when measured here). Within a K
+// chunk the next step's 16 operands are read while the current 128 operations issue.
 __global__ void __launch_bounds__(256) k_pf_logits(MoeLayerDev L, const float *__restrict__ x, int T, float *logits, float *sg) {
     extern __shared__ __align__(16) float lg_smem[];
     float(*xs)[kLgT][kLgKC] = reinterpret_cast<float(*)[kLgT][kLgKC]>(lg_smem);
@@ -80,17 +82,24 @@ __global__ void __launch_bounds__(256) k_pf_logits(MoeLayerDev L, const float *_
         }
         __syncthreads();
         const int b = c & 1;
+        float xv[2][8], wv[2][8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[0][i] = xs[b][tb + i][l];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[0][j] = ws[b][rb + j][l];
 #pragma unroll
         for (int m = 0; m < kLgKC / 64; ++m) {  // element l + 64 m of the chunk: this lane's next term
-            float xv[8], wv[8];
+            const int cur = m & 1;
+            if (m + 1 < kLgKC / 64) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) xv[i] = xs[b][tb + i][l + 64 * m];
+                for (int i = 0; i < 8; ++i) xv[cur ^ 1][i] = xs[b][tb + i][l + 64 * (m + 1)];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) wv[j] = ws[b][rb + j][l + 64 * m];
+                for (int j = 0; j < 8; ++j) wv[cur ^ 1][j] = ws[b][rb + j][l + 64 * (m + 1)];
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], xv[i]));
+                for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[cur][j], xv[cur][i]));
         }
         __syncthreads();
     }
@@ -150,15 +159,15 @@ __global__ void __launch_bounds__(256) k_pf_count(const int *ids, int T, int E, 
     for (int e = threadIdx.x; e < E; e += 256) chunk_counts[(long long)c * E + e] = h[e];
 }
 
-// One block of 512 threads: thread e walks the chunks (chunk_base = running count), then a
-// block scan gives the expert offsets; thread 0 writes the chunk list: the shared expert's
-// rows [T K, T K + T), then every expert's full kMaxN-row chunks, then the remainders by
-// decreasing size (counting sort over 1 .. kMaxN - 1).
+// One block of 512 threads, thread e = expert e: it walks the token chunks (chunk_base =
+// running count), block scans give the expert offsets and the positions of every expert's
+// full kMaxN-row chunks; the chunk list is the shared expert's rows [T K, T K + T), then the
+// full chunks, then the remainders by decreasing size (a counting sort over 1 .. kMaxN - 1).
 __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, int T, int E, int K, int *offsets, Chunk *chunks,
                                                  int *n_chunks) {
-    __shared__ int cnt[512], off[513];
-    __shared__ int rem_hist[kMaxN];
-    const int e = threadIdx.x;
+    __shared__ int wsum[16], wfull[16], total_full;
+    __shared__ int rem_hist[kMaxN], rem_start[kMaxN];
+    const int e = threadIdx.x, lane = e & 31, w = e >> 5;
     int run = 0;
     if (e < E)
         for (int c = 0; c < n_tc; ++c) {
@@ -166,38 +175,53 @@ __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, in
             chunk_counts[(long long)c * E + e] = run;  // becomes the chunk's base within the expert
             run += v;
         }
-    cnt[e] = e < E ? run : 0;
+    const int cnt = e < E ? run : 0, full = cnt / kMaxN, rem = cnt % kMaxN;
+    int a = cnt, f = full;  // inclusive warp scans
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ya = __shfl_up_sync(0xffffffffu, a, o), yf = __shfl_up_sync(0xffffffffu, f, o);
+        if (lane >= o) {
+            a += ya;
+            f += yf;
+        }
+    }
+    if (lane == 31) {
+        wsum[w] = a;
+        wfull[w] = f;
+    }
     if (e < kMaxN) rem_hist[e] = 0;
     __syncthreads();
     if (e == 0) {
-        int s = 0;
-        for (int i = 0; i < E; ++i) {
-            off[i] = s;
-            s += cnt[i];
+        int s1 = 0, s2 = 0;
+        for (int i = 0; i < 16; ++i) {
+            const int t1 = wsum[i], t2 = wfull[i];
+            wsum[i] = s1;
+            wfull[i] = s2;
+            s1 += t1;
+            s2 += t2;
         }
-        off[E] = s;
+        total_full = s2;
     }
     __syncthreads();
-    if (e <= E) offsets[e] = off[e];
-    if (e < E && cnt[e] % kMaxN) atomicAdd(&rem_hist[cnt[e] % kMaxN], 1);
+    const int off = wsum[w] + a - cnt, fpos = wfull[w] + f - full;
+    if (e < E) offsets[e] = off;
+    if (e == E - 1) offsets[E] = off + cnt;
+    if (e < E && rem) atomicAdd(&rem_hist[rem], 1);
     __syncthreads();
+    const int n_shared = (T + kMaxN - 1) / kMaxN;
     if (e == 0) {
-        int n = 0;
-        for (int r = 0; r < T; r += kMaxN) chunks[n++] = Chunk{-1, T * K + r, min(kMaxN, T - r), 0};
-        for (int i = 0; i < E; ++i)
-            for (int r = 0; r + kMaxN <= cnt[i]; r += kMaxN) chunks[n++] = Chunk{i, off[i] + r, kMaxN, 0};
-        // remainders, largest first: start index of each size bucket
-        int start[kMaxN];
-        int s = n;
+        int s = n_shared + total_full;
         for (int sz = kMaxN - 1; sz >= 1; --sz) {
-            start[sz] = s;
+            rem_start[sz] = s;
             s += rem_hist[sz];
         }
-        for (int i = 0; i < E; ++i) {
-            const int r = cnt[i] % kMaxN;
-            if (r) chunks[start[r]++] = Chunk{i, off[i] + cnt[i] - r, r, 0};
-        }
         *n_chunks = s;
+    }
+    __syncthreads();
+    for (int i = e; i < n_shared; i += 512) chunks[i] = Chunk{-1, T * K + i * kMaxN, min(kMaxN, T - i * kMaxN), 0};
+    if (e < E) {
+        for (int i = 0; i < full; ++i) chunks[n_shared + fpos + i] = Chunk{e, off + i * kMaxN, kMaxN, 0};
+        if (rem) chunks[atomicAdd(&rem_start[rem], 1)] = Chunk{e, off + cnt - rem, rem, 0};
     }
 }
 
@@ -239,17 +263,24 @@ __global__ void __launch_bounds__(256) k_pf_place(const int *ids, int T, int E, 
     }
 }
 
-// One block per token: FP16 copies of x times 2^k at the token's pair rows and its shared row.
+// One block per token: FP16 copies of x times 2^k at the token's pair rows and its shared row
+// (16-byte chunks of 8 elements; H <= 4096).
 __global__ void __launch_bounds__(256) k_pf_xprep(const float *__restrict__ x, int T, int H, int K, const int *pos, const float *weights,
                                                   const float *sg, __half *B, float *row_scale, int *row_token, float *row_weight) {
-    const int t = blockIdx.x, tid = threadIdx.x;
+    const int t = blockIdx.x, tid = threadIdx.x, nch = H / 8;
     __shared__ float red[8];
-    const int per = H / 256;  // 8 (H 2048) or 10 (H 2560)
-    float v[10];
+    float4 v[2][2];
     float mx = 0.0f;
-    for (int i = 0; i < per; ++i) {
-        v[i] = x[(long long)t * H + tid * per + i];
-        mx = fmaxf(mx, fabsf(v[i]));
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int ch = tid + 256 * u;
+        if (ch < nch) {
+            const float4 *src = reinterpret_cast<const float4 *>(x + (long long)t * H) + 2 * ch;
+            v[u][0] = __ldg(src);
+            v[u][1] = __ldg(src + 1);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[u][0].x), fabsf(v[u][0].y)), fmaxf(fabsf(v[u][0].z), fabsf(v[u][0].w))));
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[u][1].x), fabsf(v[u][1].y)), fmaxf(fabsf(v[u][1].z), fabsf(v[u][1].w))));
+        }
     }
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
@@ -264,13 +295,21 @@ __global__ void __launch_bounds__(256) k_pf_xprep(const float *__restrict__ x, i
     k = (bits >> 23) >= 255 ? 0 : k;
     k = max(-126, min(126, k));
     const float mul = __uint_as_float((unsigned)(k + 127) << 23), inv = __uint_as_float((unsigned)(127 - k) << 23);
-    __half h[10];
-    for (int i = 0; i < per; ++i) h[i] = __float2half_rn(v[i] * mul);
+    uint4 h[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const __half2 a = __floats2half2_rn(v[u][0].x * mul, v[u][0].y * mul), b = __floats2half2_rn(v[u][0].z * mul, v[u][0].w * mul);
+        const __half2 c = __floats2half2_rn(v[u][1].x * mul, v[u][1].y * mul), d = __floats2half2_rn(v[u][1].z * mul, v[u][1].w * mul);
+        h[u] = make_uint4(*reinterpret_cast<const unsigned *>(&a), *reinterpret_cast<const unsigned *>(&b),
+                          *reinterpret_cast<const unsigned *>(&c), *reinterpret_cast<const unsigned *>(&d));
+    }
     for (int kk = 0; kk <= K; ++kk) {
         const long long row = kk < K ? pos[(long long)t * K + kk] : (long long)T * K + t;
         if (row < 0) continue;
-        __half *dst = B + row * H + tid * per;
-        for (int i = 0; i < per; ++i) dst[i] = h[i];
+        uint4 *dst = reinterpret_cast<uint4 *>(B + row * H);
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+            if (tid + 256 * u < nch) dst[tid + 256 * u] = h[u];
         if (tid == 0) {
             row_scale[row] = inv;
             row_token[row] = t;
