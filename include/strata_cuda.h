@@ -158,6 +158,22 @@ typedef struct {
 int strata_moe_forward_noalloc(const strata_moe_layer_dev *layer, const float *x, int32_t tokens, float *y, int32_t *ids,
                                float *weights, void *stream, char *msg, size_t msg_cap);
 
+/* ---- expert-parallel layer over NCCL (one process per GPU) ----
+ * The fused entry point strata_moe_ep (the expert-parallel path of BASELINE's north star; the
+ * reference has no multi-GPU path). The 512 (layer.experts) routed experts are sharded evenly:
+ * rank r owns experts [r E/n, (r + 1) E/n), and its layer.experts_blob holds exactly those E/n
+ * blobs; router, shared gate and shared expert are replicated. A rank passes its own tokens and
+ * receives their y, ids and weights (routing over all E experts, bit-exact; y within 2e-3
+ * relative L2, the tensor-core path's tolerance).
+ * Setup: rank 0 calls strata_ep_unique_id, the 128 bytes are shared by the caller (e.g. a
+ * torch.distributed broadcast), every rank calls strata_ep_init. NCCL (libnccl.so.2) is bound
+ * at run time. Each forward reads the per-peer row counts back to the host once. */
+#define STRATA_EP_ID_BYTES 128
+int strata_ep_unique_id(strata_ctx *ctx, uint8_t *id, size_t cap);
+int strata_ep_init(strata_ctx *ctx, int32_t rank, int32_t n_ranks, const uint8_t *id);
+int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
+                          strata_buf weights);
+
 /* ---- device-time profile of the fused layer (diagnostics; no reference counterpart) ----
  * While enabled, strata_moe_forward records CUDA events around its phases on the context's
  * stream. strata_profile_read synchronises, adds the phase times (milliseconds) of every call

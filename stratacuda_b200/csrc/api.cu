@@ -44,6 +44,7 @@ struct strata_ctx {
     std::vector<Mark> marks;
     std::vector<cudaEvent_t> spare_events;
     uint64_t profiled_calls = 0;
+    EpComm *ep = nullptr;  // strata_ep_init
     std::string last_error;
     char device_name[256] = {0};
     int sms = 0;
@@ -232,6 +233,7 @@ int strata_destroy(strata_ctx *ctx) {
     std::sort(ctx->spare_events.begin(), ctx->spare_events.end());
     ctx->spare_events.erase(std::unique(ctx->spare_events.begin(), ctx->spare_events.end()), ctx->spare_events.end());
     for (cudaEvent_t e : ctx->spare_events) cudaEventDestroy(e);
+    if (ctx->ep) ep_destroy(ctx->ep);
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->fast_sync) cudaFree(ctx->fast_sync);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
@@ -433,6 +435,76 @@ int strata_profile_read(strata_ctx *ctx, double *ms, int32_t n, uint64_t *calls)
     ctx->marks.clear();
     if (calls) *calls = ctx->profiled_calls;
     ctx->profiled_calls = 0;
+    return STRATA_OK;
+}
+
+int strata_ep_unique_id(strata_ctx *ctx, uint8_t *id, size_t cap) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!id || cap < STRATA_EP_ID_BYTES) return fail(ctx, STRATA_ERR_RANGE, "unique id buffer needs %d bytes", STRATA_EP_ID_BYTES);
+    std::string err;
+    if (ep_unique_id(reinterpret_cast<char *>(id), &err)) return fail(ctx, STRATA_ERR_CUDA, "%s", err.c_str());
+    return STRATA_OK;
+}
+
+int strata_ep_init(strata_ctx *ctx, int32_t rank, int32_t n_ranks, const uint8_t *id) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!id || n_ranks < 1 || rank < 0 || rank >= n_ranks) return fail(ctx, STRATA_ERR_RANGE, "invalid rank %d of %d", rank, n_ranks);
+    if (int r = use_device(ctx)) return r;
+    if (ctx->ep) {
+        ep_destroy(ctx->ep);
+        ctx->ep = nullptr;
+    }
+    std::string err;
+    ctx->ep = ep_create(rank, n_ranks, reinterpret_cast<const char *>(id), &err);
+    if (!ctx->ep) return fail(ctx, STRATA_ERR_CUDA, "%s", err.c_str());
+    return STRATA_OK;
+}
+
+int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
+                          strata_buf weights) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!ctx->ep) return fail(ctx, STRATA_ERR_RANGE, "strata_ep_init has not been called");
+    if (!layer) return fail(ctx, STRATA_ERR_RANGE, "null layer");
+    const strata_moe_layer &l = *layer;
+    const int n = ep_ranks(ctx->ep);
+    if (!moe_prefill_supported(l.width, l.ff, l.experts, l.top_k))
+        return fail(ctx, STRATA_ERR_RANGE, "expert-parallel layer supports H 2048/F 512 and H 2560/F 640, <= 512 experts, topK <= 32");
+    if (l.top_k < 1 || l.top_k > l.experts || l.experts % n) return fail(ctx, STRATA_ERR_RANGE, "experts must be a multiple of the %d ranks", n);
+    if (tokens < 1) return fail(ctx, STRATA_ERR_RANGE, "tokens must be an integer >= 1");
+    const long long bw = blob_words_of(l.width, l.ff);
+    struct Need {
+        strata_buf h;
+        long long n;
+        const char *what;
+        bool optional;
+    } need[] = {{l.router, (long long)l.experts * l.width, "router", false},
+                {l.router_bias, l.experts, "router_bias", true},
+                {l.experts_blob, bw * (l.experts / n), "experts_blob (this rank's experts)", false},
+                {l.shared_blob, bw, "shared_blob", false},
+                {l.shared_gate, l.width, "shared_gate", false},
+                {x, (long long)tokens * l.width, "x", false},
+                {y, (long long)tokens * l.width, "y", false},
+                {ids, (long long)tokens * l.top_k, "ids", false},
+                {weights, (long long)tokens * l.top_k, "weights", false}};
+    void *ptr[9];
+    for (int i = 0; i < 9; ++i) {
+        ptr[i] = nullptr;
+        if (need[i].optional && need[i].h == 0) continue;
+        Buffer *b = find(ctx, need[i].h);
+        if (!b) return fail(ctx, STRATA_ERR_HANDLE, "ep layer: %s is not a live buffer", need[i].what);
+        if ((long long)b->length < need[i].n)
+            return fail(ctx, STRATA_ERR_LAYOUT, "ep layer: %s holds %llu elements, needs %lld", need[i].what, (unsigned long long)b->length,
+                        need[i].n);
+        ptr[i] = b->ptr;
+    }
+    if (int r = use_device(ctx)) return r;
+    MoeLayerDev L{l.width, l.ff, l.experts, l.top_k, (const float *)ptr[0], (const float *)ptr[1], (const unsigned *)ptr[2], bw,
+                  (const unsigned *)ptr[3], (const float *)ptr[4]};
+    std::string msg;
+    if (moe_forward_ep(L, ctx->ep, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->sms, ctx->stream,
+                       ctx->err_dev, &msg))
+        return fail(ctx, STRATA_ERR_CUDA, "strata_moe_ep_forward: %s", msg.c_str());
+    ++ctx->fused_calls;
     return STRATA_OK;
 }
 

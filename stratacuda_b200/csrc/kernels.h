@@ -1,5 +1,6 @@
 // Internal interface between the C-ABI layer (api.cu) and the kernel files.
 #pragma once
+#include <string>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -79,6 +80,17 @@ size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int
 // GEMM and after the down GEMM.
 cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
                                 int grid, cudaStream_t s, unsigned *err, cudaEvent_t *marks = nullptr);
+
+// Expert parallel over NCCL (csrc/prefill.cu): communicator from a unique id shared by the
+// ranks; forward of one layer whose L.blobs holds this rank's L.experts / n experts. Returns 0
+// or a nonzero code with `msg`.
+struct EpComm;
+int ep_unique_id(char *out128, std::string *err);
+EpComm *ep_create(int rank, int n_ranks, const char *id128, std::string *err);
+void ep_destroy(EpComm *c);
+int ep_ranks(const EpComm *c);
+int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int tokens, float *y, int *ids, float *weights, int grid, cudaStream_t s,
+                   unsigned *err, std::string *msg);
 
 // Device synthetic generator (csrc/synth.cu), same bytes as stratacuda_b200/synth.py.
 cudaError_t synth_expert_blobs(unsigned *out, unsigned long long seed, int layer, int first_expert, int count, int width, int ff,

@@ -19,9 +19,13 @@
 // reference (the FP16 tensor-core path's tolerance; tested). Routing is bit-exact.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cstring>
 #include <mutex>
+#include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -159,11 +163,12 @@ __global__ void __launch_bounds__(256) k_pf_count(const int *ids, int T, int E, 
     for (int e = threadIdx.x; e < E; e += 256) chunk_counts[(long long)c * E + e] = h[e];
 }
 
-// One block of 512 threads, thread e = expert e: it walks the token chunks (chunk_base =
-// running count), block scans give the expert offsets and the positions of every expert's
-// full kMaxN-row chunks; the chunk list is the shared expert's rows [T K, T K + T), then the
-// full chunks, then the remainders by decreasing size (a counting sort over 1 .. kMaxN - 1).
-__global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, int T, int E, int K, int *offsets, Chunk *chunks,
+// One block of 512 threads, thread e = bucket (expert) e: it walks the token chunks
+// (chunk_base = running count), block scans give the bucket offsets and the positions of every
+// bucket's full kMaxN-row chunks; the chunk list is the shared expert's Ts rows starting at
+// row shared0, then the full chunks, then the remainders by decreasing size (a counting sort
+// over 1 .. kMaxN - 1).
+__global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, int Ts, int shared0, int E, int *offsets, Chunk *chunks,
                                                  int *n_chunks) {
     __shared__ int wsum[16], wfull[16], total_full;
     __shared__ int rem_hist[kMaxN], rem_start[kMaxN];
@@ -208,7 +213,7 @@ __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, in
     if (e == E - 1) offsets[E] = off + cnt;
     if (e < E && rem) atomicAdd(&rem_hist[rem], 1);
     __syncthreads();
-    const int n_shared = (T + kMaxN - 1) / kMaxN;
+    const int n_shared = (Ts + kMaxN - 1) / kMaxN;
     if (e == 0) {
         int s = n_shared + total_full;
         for (int sz = kMaxN - 1; sz >= 1; --sz) {
@@ -218,7 +223,7 @@ __global__ void __launch_bounds__(512) k_pf_scan(int *chunk_counts, int n_tc, in
         *n_chunks = s;
     }
     __syncthreads();
-    for (int i = e; i < n_shared; i += 512) chunks[i] = Chunk{-1, T * K + i * kMaxN, min(kMaxN, T - i * kMaxN), 0};
+    for (int i = e; i < n_shared; i += 512) chunks[i] = Chunk{-1, shared0 + i * kMaxN, min(kMaxN, Ts - i * kMaxN), 0};
     if (e < E) {
         for (int i = 0; i < full; ++i) chunks[n_shared + fpos + i] = Chunk{e, off + i * kMaxN, kMaxN, 0};
         if (rem) chunks[atomicAdd(&rem_start[rem], 1)] = Chunk{e, off + cnt - rem, rem, 0};
@@ -263,10 +268,12 @@ __global__ void __launch_bounds__(256) k_pf_place(const int *ids, int T, int E, 
     }
 }
 
-// One block per token: FP16 copies of x times 2^k at the token's pair rows and its shared row
-// (16-byte chunks of 8 elements; H <= 4096).
+// One block per token: FP16 copies of x times 2^k at the token's pair rows and at its shared
+// row shared0 + t (16-byte chunks of 8 elements; H <= 4096). Row metadata: scale 2^-k, the
+// token (shared rows: token + token_base) and the weight (shared rows: sigmoid(sg)).
 __global__ void __launch_bounds__(256) k_pf_xprep(const float *__restrict__ x, int T, int H, int K, const int *pos, const float *weights,
-                                                  const float *sg, __half *B, float *row_scale, int *row_token, float *row_weight) {
+                                                  const float *sg, int shared0, int token_base, __half *B, float *row_scale, int *row_token,
+                                                  float *row_weight) {
     const int t = blockIdx.x, tid = threadIdx.x, nch = H / 8;
     __shared__ float red[8];
     float4 v[2][2];
@@ -304,7 +311,7 @@ __global__ void __launch_bounds__(256) k_pf_xprep(const float *__restrict__ x, i
                           *reinterpret_cast<const unsigned *>(&c), *reinterpret_cast<const unsigned *>(&d));
     }
     for (int kk = 0; kk <= K; ++kk) {
-        const long long row = kk < K ? pos[(long long)t * K + kk] : (long long)T * K + t;
+        const long long row = kk < K ? pos[(long long)t * K + kk] : (long long)shared0 + t;
         if (row < 0) continue;
         uint4 *dst = reinterpret_cast<uint4 *>(B + row * H);
 #pragma unroll
@@ -312,9 +319,109 @@ __global__ void __launch_bounds__(256) k_pf_xprep(const float *__restrict__ x, i
             if (tid + 256 * u < nch) dst[tid + 256 * u] = h[u];
         if (tid == 0) {
             row_scale[row] = inv;
-            row_token[row] = t;
+            row_token[row] = kk < K ? t : token_base + t;
             row_weight[row] = kk < K ? weights[(long long)t * K + kk] : ref_sigmoid(sg[t]);
         }
+    }
+}
+
+// ------------------------------------------------------------------ expert parallel
+// Destination rank of each (token, k) pair: experts are sharded evenly, rank r owns
+// [r El, (r + 1) El); ids outside [0, E) get -1 (no slot).
+__global__ void k_ep_dest(const int *ids, long long n, int E, int El, int *dest) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dest[i] = ids[i] >= 0 && ids[i] < E ? ids[i] / El : -1;
+}
+
+// One block per token: the token's FP16 row (times 2^k) at each of its pairs' send positions,
+// with the pair's metadata {local expert, token, weight bits, 2^-k bits}.
+__global__ void __launch_bounds__(256) k_ep_pack(const float *__restrict__ x, int H, int K, const int *ids, const float *weights, int El,
+                                                 const int *pos, __half *send_rows, int4 *send_meta) {
+    const int t = blockIdx.x, tid = threadIdx.x, nch = H / 8;
+    __shared__ float red[8];
+    float4 v[2][2];
+    float mx = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int ch = tid + 256 * u;
+        if (ch < nch) {
+            const float4 *src = reinterpret_cast<const float4 *>(x + (long long)t * H) + 2 * ch;
+            v[u][0] = __ldg(src);
+            v[u][1] = __ldg(src + 1);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[u][0].x), fabsf(v[u][0].y)), fmaxf(fabsf(v[u][0].z), fabsf(v[u][0].w))));
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[u][1].x), fabsf(v[u][1].y)), fmaxf(fabsf(v[u][1].z), fabsf(v[u][1].w))));
+        }
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red[i]);
+    const unsigned bits = __float_as_uint(mx);
+    int k = 15 - ((int)(bits >> 23) - 126);
+    k = (bits >> 23) == 0 ? 0 : k;
+    k = (bits >> 23) >= 255 ? 0 : k;
+    k = max(-126, min(126, k));
+    const float mul = __uint_as_float((unsigned)(k + 127) << 23), inv = __uint_as_float((unsigned)(127 - k) << 23);
+    uint4 h[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const __half2 a = __floats2half2_rn(v[u][0].x * mul, v[u][0].y * mul), b = __floats2half2_rn(v[u][0].z * mul, v[u][0].w * mul);
+        const __half2 c = __floats2half2_rn(v[u][1].x * mul, v[u][1].y * mul), d = __floats2half2_rn(v[u][1].z * mul, v[u][1].w * mul);
+        h[u] = make_uint4(*reinterpret_cast<const unsigned *>(&a), *reinterpret_cast<const unsigned *>(&b),
+                          *reinterpret_cast<const unsigned *>(&c), *reinterpret_cast<const unsigned *>(&d));
+    }
+    for (int kk = 0; kk < K; ++kk) {
+        const int p = pos[(long long)t * K + kk];
+        if (p < 0) continue;
+        uint4 *dst = reinterpret_cast<uint4 *>(send_rows + (long long)p * H);
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+            if (tid + 256 * u < nch) dst[tid + 256 * u] = h[u];
+        if (tid == 0)
+            send_meta[p] = make_int4(ids[(long long)t * K + kk] % El, t, __float_as_int(weights[(long long)t * K + kk]), __float_as_int(inv));
+    }
+}
+
+__global__ void k_ep_local_expert(const int4 *meta, int R, int *lid) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < R) lid[i] = meta[i].x;
+}
+
+// One warp per received row: its FP16 row at its position among the local experts' B rows;
+// the GEMMs' output row for it is its receive index i (sent back in that order).
+__global__ void k_ep_gather(const __half *recv_rows, const int4 *meta, int R, int H, const int *rpos, __half *B, float *row_scale,
+                            int *row_token, float *row_weight) {
+    const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (i >= R) return;
+    const int p = rpos[i];
+    const uint4 *src = reinterpret_cast<const uint4 *>(recv_rows + (long long)i * H);
+    uint4 *dst = reinterpret_cast<uint4 *>(B + (long long)p * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+    if (lane == 0) {
+        const int4 m = meta[i];
+        row_scale[p] = __int_as_float(m.w);
+        row_weight[p] = __int_as_float(m.z);
+        row_token[p] = i;
+    }
+}
+
+// y[t] = shared row + the token's returned pair rows in k order (pairs without an expert skip).
+__global__ void k_ep_combine(const float *ret, const int *pos, int K, int H, const float *shared, float *y) {
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+        float4 a = reinterpret_cast<const float4 *>(shared + (long long)t * H)[c];
+        for (int kk = 0; kk < K; ++kk) {
+            const int p = pos[(long long)t * K + kk];
+            if (p < 0) continue;
+            const float4 b = reinterpret_cast<const float4 *>(ret + (long long)p * H)[c];
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        reinterpret_cast<float4 *>(y + (long long)t * H)[c] = a;
     }
 }
 
@@ -397,6 +504,55 @@ cudaError_t launch_gemm(const pf::GemmParams &p, int grid, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// The gate/up and down GEMMs over a chunk list: B rows (FP16, b_rows of them) with their
+// scale, token and weight; hidden [b_rows][F]; y[token][H] += weight * down. `experts`
+// blobs start at L.blobs. marks (nullable): events after each GEMM.
+cudaError_t launch_moe_gemms(const MoeLayerDev &L, int experts, const pf::Chunk *chunks, const int *n_chunks, long long b_rows, const __half *B,
+                             __half *hidden, const float *row_scale, const int *row_token, const float *row_weight, float *y, int grid,
+                             cudaStream_t s, unsigned *err, cudaEvent_t *marks) {
+    const int H = L.width, F = L.ff;
+    const long long bb = L.blob_words * 4;
+    const long long d_codes = 2LL * F * H / 4, gu_scales = 3LL * F * H / 4, d_scales = gu_scales + 2LL * F * (H / 64) * 2;
+    const unsigned char *blobs = reinterpret_cast<const unsigned char *>(L.blobs), *shared = reinterpret_cast<const unsigned char *>(L.shared_blob);
+    for (int mode = 0; mode < 2; ++mode) {
+        pf::GemmParams p;
+        std::memset(&p, 0, sizeof p);
+        p.chunks = chunks;
+        p.n_chunks = n_chunks;
+        p.blobs = blobs;
+        p.shared = shared;
+        p.blob_bytes = bb;
+        p.K = mode == 0 ? H : F;
+        p.rows_total = mode == 0 ? 2 * F : H;
+        p.NM = p.rows_total / 128;
+        p.codes_off = mode == 0 ? 0 : d_codes;
+        p.scales_off = mode == 0 ? gu_scales : d_scales;
+        p.row_scale = row_scale;
+        p.row_token = row_token;
+        p.row_weight = row_weight;
+        p.hidden = hidden;
+        p.y = y;
+        p.err = err;
+        p.spin_limit = 1ull << 22;
+        const unsigned long long cdims[3] = {(unsigned long long)p.K / 4, (unsigned long long)p.rows_total, (unsigned long long)max(1, experts)};
+        const unsigned long long cstr[2] = {(unsigned long long)p.K / 4, (unsigned long long)bb};
+        const unsigned cbox[3] = {64, 128, 1};
+        const unsigned long long sdims[3] = {(unsigned long long)p.K / 4, (unsigned long long)p.rows_total, 1ull};
+        if (!encode(&p.tm_codes[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (blobs ? blobs : shared) + p.codes_off, cdims, cstr, cbox,
+                    CU_TENSOR_MAP_SWIZZLE_64B) ||
+            !encode(&p.tm_codes[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, shared + p.codes_off, sdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_64B))
+            return cudaErrorInvalidValue;
+        const void *bmat = mode == 0 ? (const void *)B : (const void *)hidden;
+        const unsigned long long bdims[2] = {(unsigned long long)p.K, (unsigned long long)max(1LL, b_rows)};
+        const unsigned long long bstr[1] = {(unsigned long long)p.K * 2};
+        const unsigned bbox[2] = {64, 16};
+        if (!encode(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bmat, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaErrorInvalidValue;
+        STRATA_CUDA_TRY(mode == 0 ? launch_gemm<pf::kGateUp>(p, grid, s) : launch_gemm<pf::kDown>(p, grid, s));
+        if (marks) STRATA_CUDA_TRY(cudaEventRecord(marks[mode], s));
+    }
+    return cudaSuccess;
+}
+
 }  // namespace
 
 size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int topK) {
@@ -418,7 +574,7 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
     auto mark = [&](int i) { return marks ? cudaEventRecord(marks[i], s) : cudaSuccess; };
     STRATA_CUDA_TRY(mark(0));
     const int H = L.width, F = L.ff, E = L.experts, K = L.topK;
-    const long long rows = (long long)T * K + T, bb = L.blob_words * 4;
+    const long long rows = (long long)T * K + T;
     PfScratch S = carve(scratch, T, H, F, E, K);
     const int n_tc = (T + pf::kTokChunk - 1) / pf::kTokChunk;
     static int logits_ready_device = -1;
@@ -432,51 +588,268 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
                                                                                                                    S.sg);
     pf::k_pf_route<<<(T + 3) / 4, 128, 0, s>>>(S.logits, T, E, K, ids, weights);
     pf::k_pf_count<<<n_tc, 256, 0, s>>>(ids, T, E, K, S.chunk_counts);
-    pf::k_pf_scan<<<1, 512, 0, s>>>(S.chunk_counts, n_tc, T, E, K, S.offsets, S.chunks, S.n_chunks);
+    pf::k_pf_scan<<<1, 512, 0, s>>>(S.chunk_counts, n_tc, T, T * K, E, S.offsets, S.chunks, S.n_chunks);
     pf::k_pf_place<<<n_tc, 256, 0, s>>>(ids, T, E, K, S.chunk_counts, S.offsets, S.pos);
-    pf::k_pf_xprep<<<T, 256, 0, s>>>(x, T, H, K, S.pos, weights, S.sg, S.B, S.row_scale, S.row_token, S.row_weight);
+    pf::k_pf_xprep<<<T, 256, 0, s>>>(x, T, H, K, S.pos, weights, S.sg, T * K, 0, S.B, S.row_scale, S.row_token, S.row_weight);
     STRATA_CUDA_TRY(cudaGetLastError());
     STRATA_CUDA_TRY(cudaMemsetAsync(y, 0, sizeof(float) * (size_t)T * H, s));
     STRATA_CUDA_TRY(mark(1));
 
-    const long long d_codes = 2LL * F * H / 4, gu_scales = 3LL * F * H / 4, d_scales = gu_scales + 2LL * F * (H / 64) * 2;
-    const unsigned char *blobs = reinterpret_cast<const unsigned char *>(L.blobs), *shared = reinterpret_cast<const unsigned char *>(L.shared_blob);
-    for (int mode = 0; mode < 2; ++mode) {
-        pf::GemmParams p;
-        std::memset(&p, 0, sizeof p);
-        p.chunks = S.chunks;
-        p.n_chunks = S.n_chunks;
-        p.blobs = blobs;
-        p.shared = shared;
-        p.blob_bytes = bb;
-        p.K = mode == 0 ? H : F;
-        p.rows_total = mode == 0 ? 2 * F : H;
-        p.NM = p.rows_total / 128;
-        p.codes_off = mode == 0 ? 0 : d_codes;
-        p.scales_off = mode == 0 ? gu_scales : d_scales;
-        p.row_scale = S.row_scale;
-        p.row_token = S.row_token;
-        p.row_weight = S.row_weight;
-        p.hidden = S.hidden;
-        p.y = y;
-        p.err = err;
-        p.spin_limit = 1ull << 22;
-        const unsigned long long cdims[3] = {(unsigned long long)p.K / 4, (unsigned long long)p.rows_total, (unsigned long long)E};
-        const unsigned long long cstr[2] = {(unsigned long long)p.K / 4, (unsigned long long)bb};
-        const unsigned cbox[3] = {64, 128, 1};
-        const unsigned long long sdims[3] = {(unsigned long long)p.K / 4, (unsigned long long)p.rows_total, 1ull};
-        if (!encode(&p.tm_codes[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blobs + p.codes_off, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_64B) ||
-            !encode(&p.tm_codes[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, shared + p.codes_off, sdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_64B))
-            return cudaErrorInvalidValue;
-        const void *bmat = mode == 0 ? (const void *)S.B : (const void *)S.hidden;
-        const unsigned long long bdims[2] = {(unsigned long long)p.K, (unsigned long long)rows};
-        const unsigned long long bstr[1] = {(unsigned long long)p.K * 2};
-        const unsigned bbox[2] = {64, 16};
-        if (!encode(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bmat, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaErrorInvalidValue;
-        STRATA_CUDA_TRY(mode == 0 ? launch_gemm<pf::kGateUp>(p, grid, s) : launch_gemm<pf::kDown>(p, grid, s));
-        STRATA_CUDA_TRY(mark(2 + mode));
-    }
+    STRATA_CUDA_TRY(launch_moe_gemms(L, L.experts, S.chunks, S.n_chunks, rows, S.B, S.hidden, S.row_scale, S.row_token, S.row_weight, y,
+                                     grid, s, err, marks ? marks + 2 : nullptr));
     return cudaSuccess;
+}
+
+
+// ------------------------------------------------------------------ expert parallel (host)
+// NCCL is bound at run time (the process's loaded libnccl.so.2 first, e.g. the one torch
+// brought, else the system's): the library itself needs no NCCL link dependency.
+namespace {
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+const NcclApi &nccl() {
+    static NcclApi a;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        a.GetUniqueId = reinterpret_cast<decltype(a.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+        a.CommInitRank = reinterpret_cast<decltype(a.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+        a.CommDestroy = reinterpret_cast<decltype(a.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        a.GroupStart = reinterpret_cast<decltype(a.GroupStart)>(dlsym(h, "ncclGroupStart"));
+        a.GroupEnd = reinterpret_cast<decltype(a.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
+        a.Send = reinterpret_cast<decltype(a.Send)>(dlsym(h, "ncclSend"));
+        a.Recv = reinterpret_cast<decltype(a.Recv)>(dlsym(h, "ncclRecv"));
+        a.GetErrorString = reinterpret_cast<decltype(a.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+        a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.GroupStart && a.GroupEnd && a.Send && a.Recv && a.GetErrorString;
+    });
+    return a;
+}
+}  // namespace
+
+struct EpComm {
+    ncclComm_t comm = nullptr;
+    int rank = 0, n = 1;
+    struct Buf {
+        void *p = nullptr;
+        size_t cap = 0;
+    };
+    Buf bufs[24];
+    int *h_off = nullptr;  // pinned: [0, n] send offsets, [n + 1, 2n] receive counts
+    ~EpComm() {
+        for (Buf &b : bufs)
+            if (b.p) cudaFree(b.p);
+        if (h_off) cudaFreeHost(h_off);
+        if (comm) nccl().CommDestroy(comm);
+    }
+    // grow-only device buffer i of at least `bytes`
+    void *get(int i, size_t bytes, cudaError_t &e) {
+        if (bufs[i].cap < bytes) {
+            if (bufs[i].p) cudaFree(bufs[i].p);
+            bufs[i].p = nullptr;
+            bufs[i].cap = 0;
+            const size_t want = (bytes + bytes / 4 + 255) & ~size_t(255);
+            e = cudaMalloc(&bufs[i].p, want);
+            if (e != cudaSuccess) return nullptr;
+            bufs[i].cap = want;
+        }
+        return bufs[i].p;
+    }
+};
+
+int ep_unique_id(char *out, std::string *err) {
+    if (!nccl().ok) {
+        *err = "libnccl.so.2 could not be loaded";
+        return 1;
+    }
+    ncclUniqueId id;
+    const ncclResult_t r = nccl().GetUniqueId(&id);
+    if (r != ncclSuccess) {
+        *err = std::string("ncclGetUniqueId: ") + nccl().GetErrorString(r);
+        return 1;
+    }
+    std::memcpy(out, id.internal, NCCL_UNIQUE_ID_BYTES);
+    return 0;
+}
+
+EpComm *ep_create(int rank, int n, const char *id_bytes, std::string *err) {
+    if (!nccl().ok) {
+        *err = "libnccl.so.2 could not be loaded";
+        return nullptr;
+    }
+    ncclUniqueId id;
+    std::memcpy(id.internal, id_bytes, NCCL_UNIQUE_ID_BYTES);
+    auto *c = new EpComm;
+    c->rank = rank;
+    c->n = n;
+    const ncclResult_t r = nccl().CommInitRank(&c->comm, n, id, rank);
+    if (r != ncclSuccess || cudaMallocHost(&c->h_off, sizeof(int) * (2 * n + 2)) != cudaSuccess) {
+        *err = std::string("ncclCommInitRank: ") + nccl().GetErrorString(r);
+        delete c;
+        return nullptr;
+    }
+    return c;
+}
+
+void ep_destroy(EpComm *c) { delete c; }
+int ep_ranks(const EpComm *c) { return c->n; }
+
+// One layer over the ranks of `c`: this rank's T tokens in, its y out; L.blobs holds this
+// rank's experts [rank El, (rank + 1) El), El = L.experts / n (L.experts is the layer's total).
+// Stages: exact routing; pairs bucketed by destination rank (stable) and packed as FP16 rows
+// with {local expert, token, weight, 2^-k}; counts, then rows, exchanged by grouped
+// ncclSend/ncclRecv; the received rows regrouped by local expert and run through the tensor-
+// core GEMMs together with this rank's shared-expert rows; outputs sent back; y[t] = shared
+// row + the token's returned rows in k order. The receive sizes are read back on the host
+// (as the reference reads its routing back, src/engine.js:137).
+int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float *y, int *ids, float *weights, int grid, cudaStream_t s,
+                   unsigned *err, std::string *msg) {
+    const int H = L.width, F = L.ff, E = L.experts, K = L.topK, n = c->n, El = E / n;
+    cudaError_t e = cudaSuccess;
+    auto fail_cuda = [&](cudaError_t ce, const char *what) {
+        *msg = std::string(what) + ": " + cudaGetErrorString(ce);
+        return 2;
+    };
+    auto fail_nccl = [&](ncclResult_t r, const char *what) {
+        *msg = std::string(what) + ": " + nccl().GetErrorString(r);
+        return 3;
+    };
+#define EP_CUDA(x, what)                              \
+    do {                                              \
+        cudaError_t _c = (x);                         \
+        if (_c != cudaSuccess) return fail_cuda(_c, what); \
+    } while (0)
+#define EP_NCCL(x, what)                              \
+    do {                                              \
+        ncclResult_t _r = (x);                        \
+        if (_r != ncclSuccess) return fail_nccl(_r, what); \
+    } while (0)
+#define EP_GET(ptr, type, i, count)                                                   \
+    type *ptr = static_cast<type *>(c->get(i, sizeof(type) * (size_t)(count) + 16, e)); \
+    if (!ptr) return fail_cuda(e, "cudaMalloc");
+    const long long P = (long long)T * K;
+    const int n_tc = (T + pf::kTokChunk - 1) / pf::kTokChunk;
+    // 1. routing
+    EP_GET(logits, float, 0, (long long)T * E);
+    EP_GET(sg, float, 1, T);
+    static int logits_ready_device = -1;
+    int dev = 0;
+    EP_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    if (logits_ready_device != dev) {
+        EP_CUDA(cudaFuncSetAttribute(pf::k_pf_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem), "cudaFuncSetAttribute");
+        logits_ready_device = dev;
+    }
+    pf::k_pf_logits<<<dim3((T + pf::kLgT - 1) / pf::kLgT, (E + 1 + pf::kLgR - 1) / pf::kLgR), 256, pf::kLgSmem, s>>>(L, x, T, logits, sg);
+    pf::k_pf_route<<<(T + 3) / 4, 128, 0, s>>>(logits, T, E, K, ids, weights);
+    // 2. destination buckets, stable positions, packed rows
+    EP_GET(dest, int, 2, P);
+    EP_GET(cc, int, 3, (long long)n_tc * max(n, 1));
+    EP_GET(off, int, 4, n + 1);
+    EP_GET(pos, int, 5, P);
+    EP_GET(dchunks, pf::Chunk, 6, P / pf::kMaxN + n + 2);
+    EP_GET(dn, int, 7, 1);
+    pf::k_ep_dest<<<(unsigned)((P + 255) / 256), 256, 0, s>>>(ids, P, E, El, dest);
+    pf::k_pf_count<<<n_tc, 256, 0, s>>>(dest, T, n, K, cc);
+    pf::k_pf_scan<<<1, 512, 0, s>>>(cc, n_tc, 0, 0, n, off, dchunks, dn);
+    pf::k_pf_place<<<n_tc, 256, 0, s>>>(dest, T, n, K, cc, off, pos);
+    EP_GET(send_rows, __half, 8, P * H);
+    EP_GET(send_meta, int4, 9, P);
+    pf::k_ep_pack<<<T, 256, 0, s>>>(x, H, K, ids, weights, El, pos, send_rows, send_meta);
+    EP_CUDA(cudaGetLastError(), "routing and packing kernels");
+    // 3. counts exchange
+    EP_GET(d_cnt, int, 10, 2 * n);
+    EP_CUDA(cudaMemcpyAsync(c->h_off, off, sizeof(int) * (n + 1), cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
+    EP_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    std::vector<int> soff(n + 1), sc(n), rc(n), roff(n + 1);
+    for (int i = 0; i <= n; ++i) soff[i] = c->h_off[i];
+    for (int i = 0; i < n; ++i) sc[i] = soff[i + 1] - soff[i];
+    EP_CUDA(cudaMemcpyAsync(d_cnt, sc.data(), sizeof(int) * n, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+    EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
+    for (int p = 0; p < n; ++p) {
+        EP_NCCL(nccl().Send(d_cnt + p, 1, ncclInt32, p, c->comm, s), "ncclSend");
+        EP_NCCL(nccl().Recv(d_cnt + n + p, 1, ncclInt32, p, c->comm, s), "ncclRecv");
+    }
+    EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
+    EP_CUDA(cudaMemcpyAsync(c->h_off + n + 1, d_cnt + n, sizeof(int) * n, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
+    EP_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    roff[0] = 0;
+    for (int i = 0; i < n; ++i) {
+        rc[i] = c->h_off[n + 1 + i];
+        roff[i + 1] = roff[i] + rc[i];
+    }
+    const int R = roff[n];
+    // 4. rows exchange
+    EP_GET(recv_rows, __half, 11, (long long)max(R, 1) * H);
+    EP_GET(recv_meta, int4, 12, max(R, 1));
+    EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
+    for (int p = 0; p < n; ++p) {
+        if (sc[p]) {
+            EP_NCCL(nccl().Send(send_rows + (long long)soff[p] * H, (size_t)sc[p] * H, ncclFloat16, p, c->comm, s), "ncclSend");
+            EP_NCCL(nccl().Send(send_meta + soff[p], (size_t)sc[p] * 4, ncclInt32, p, c->comm, s), "ncclSend");
+        }
+        if (rc[p]) {
+            EP_NCCL(nccl().Recv(recv_rows + (long long)roff[p] * H, (size_t)rc[p] * H, ncclFloat16, p, c->comm, s), "ncclRecv");
+            EP_NCCL(nccl().Recv(recv_meta + roff[p], (size_t)rc[p] * 4, ncclInt32, p, c->comm, s), "ncclRecv");
+        }
+    }
+    EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
+    // 5. local experts + shared expert on the tensor cores
+    const long long brows = (long long)R + T;
+    const int n_tc2 = max(1, (R + pf::kTokChunk - 1) / pf::kTokChunk);
+    const int max_chunks = El + (int)(brows / pf::kMaxN) + 4;
+    EP_GET(lid, int, 13, max(R, 1));
+    EP_GET(cc2, int, 14, (long long)n_tc2 * El);
+    EP_GET(off2, int, 15, El + 1);
+    EP_GET(rpos, int, 16, max(R, 1));
+    EP_GET(chunks, pf::Chunk, 17, max_chunks);
+    EP_GET(nchunks, int, 18, 1);
+    EP_GET(B, __half, 19, brows * H);
+    EP_GET(hidden, __half, 20, brows * F);
+    EP_GET(rmeta, float, 21, 3 * brows);  // row scale, token (as int), weight
+    EP_GET(Y, float, 22, brows * H);
+    EP_GET(ret, float, 23, max(P, 1LL) * H);
+    float *row_scale = rmeta, *row_weight = rmeta + 2 * brows;
+    int *row_token = reinterpret_cast<int *>(rmeta + brows);
+    if (R > 0) {
+        pf::k_ep_local_expert<<<(R + 255) / 256, 256, 0, s>>>(recv_meta, R, lid);
+        pf::k_pf_count<<<n_tc2, 256, 0, s>>>(lid, R, El, 1, cc2);
+    }
+    pf::k_pf_scan<<<1, 512, 0, s>>>(cc2, R > 0 ? n_tc2 : 0, T, R, El, off2, chunks, nchunks);
+    if (R > 0) {
+        pf::k_pf_place<<<n_tc2, 256, 0, s>>>(lid, R, El, 1, cc2, off2, rpos);
+        pf::k_ep_gather<<<(R + 7) / 8, 256, 0, s>>>(recv_rows, recv_meta, R, H, rpos, B, row_scale, row_token, row_weight);
+    }
+    pf::k_pf_xprep<<<T, 256, 0, s>>>(x, T, H, 0, nullptr, weights, sg, R, R, B, row_scale, row_token, row_weight);
+    EP_CUDA(cudaMemsetAsync(Y, 0, sizeof(float) * brows * H, s), "cudaMemsetAsync");
+    EP_CUDA(cudaGetLastError(), "expert grouping kernels");
+    MoeLayerDev Ll = L;
+    Ll.experts = El;
+    EP_CUDA(launch_moe_gemms(Ll, El, chunks, nchunks, brows, B, hidden, row_scale, row_token, row_weight, Y, grid, s, err, nullptr),
+            "expert GEMMs");
+    // 6. outputs back to their tokens' ranks
+    EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
+    for (int p = 0; p < n; ++p) {
+        if (rc[p]) EP_NCCL(nccl().Send(Y + (long long)roff[p] * H, (size_t)rc[p] * H, ncclFloat32, p, c->comm, s), "ncclSend");
+        if (sc[p]) EP_NCCL(nccl().Recv(ret + (long long)soff[p] * H, (size_t)sc[p] * H, ncclFloat32, p, c->comm, s), "ncclRecv");
+    }
+    EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
+    // 7. combine
+    pf::k_ep_combine<<<T, 128, 0, s>>>(ret, pos, K, H, Y + (long long)R * H, y);
+    EP_CUDA(cudaGetLastError(), "combine");
+#undef EP_CUDA
+#undef EP_NCCL
+#undef EP_GET
+    return 0;
 }
 
 }  // namespace strata

@@ -1,0 +1,110 @@
+"""Expert-parallel MoE layer over NCCL (strata_moe_ep_forward): one process per GPU.
+
+The layer's routed experts are sharded evenly: rank r holds experts [r E/n, (r + 1) E/n) and
+runs them for every rank's tokens that route there; router, shared gate and shared expert are
+replicated. Each rank passes its own tokens and gets back their y, ids and weights. The
+reference has no multi-GPU path; the layer's arithmetic is the tensor-core path's (routing
+bit-exact, y within 2e-3 relative L2).
+
+The NCCL communicator lives in the library (bound at run time to the process's libnccl.so.2);
+the ranks share its 128-byte unique id through torch.distributed (any backend).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib as L
+from . import synth
+from .backend import Buffer, CudaBackend
+from .moe import blob_layout
+
+
+def ep_init(backend: CudaBackend, rank: int, n_ranks: int) -> None:
+    """strata_ep_init on every rank; the unique id travels by torch.distributed.broadcast_object_list."""
+    import torch.distributed as dist
+    ident = [None]
+    if rank == 0:
+        buf = C.create_string_buffer(128)
+        backend._check(backend.lib.strata_ep_unique_id(backend.ctx, buf, 128))
+        ident[0] = bytes(buf.raw)
+    if n_ranks > 1:
+        dist.broadcast_object_list(ident, src=0)
+    backend._check(backend.lib.strata_ep_init(backend.ctx, int(rank), int(n_ranks), C.c_char_p(ident[0])))
+
+
+@dataclass
+class EpMoeLayer:
+    backend: CudaBackend
+    rank: int
+    n_ranks: int
+    width: int
+    ff: int
+    experts: int  # total over the ranks
+    top_k: int
+    router: Buffer
+    experts_blob: Buffer  # this rank's experts / n_ranks blobs
+    shared_blob: Buffer
+    shared_gate: Buffer
+    router_bias: Buffer | None = None
+
+    @property
+    def local_experts(self) -> int:
+        return self.experts // self.n_ranks
+
+    @property
+    def first_expert(self) -> int:
+        return self.rank * self.local_experts
+
+    def forward(self, x: Buffer, tokens: int, y: Buffer, ids: Buffer, weights: Buffer) -> None:
+        b = self.backend
+        st = L.StrataMoeLayer(self.width, self.ff, self.experts, self.top_k, self.router.handle,
+                              self.router_bias.handle if self.router_bias is not None else 0, self.experts_blob.handle,
+                              self.shared_blob.handle, self.shared_gate.handle)
+        b._check(b.lib.strata_moe_ep_forward(b.ctx, C.byref(st), x.handle, int(tokens), y.handle, ids.handle, weights.handle))
+
+    def free(self) -> None:
+        for buf in (self.router, self.experts_blob, self.shared_blob, self.shared_gate, self.router_bias):
+            if buf is not None:
+                self.backend.free(buf)
+
+    @classmethod
+    def synthesize(cls, backend: CudaBackend, rank: int, n_ranks: int, seed: int, layer: int, width: int = 2048, ff: int = 512,
+                   experts: int = 512, top_k: int = 10, zipf: float | None = None) -> "EpMoeLayer":
+        """The seeded synthetic layer of stratacuda_b200.moe.MoeLayer.synthesize, this rank's expert slice only."""
+        if experts % n_ranks:
+            raise ValueError("experts must be a multiple of the ranks")
+        words = blob_layout(width, ff)["blob_bytes"] // 4
+        lib, ctx = backend.lib, backend.ctx
+        el = experts // n_ranks
+        router = backend.alloc(experts * width, zero=False)
+        backend._check(lib.strata_synth_normals(ctx, router.handle, 0, seed, synth.TAG_ROUTER, layer, 0, experts * width, 0.02))
+        gate = backend.alloc(width, zero=False)
+        backend._check(lib.strata_synth_normals(ctx, gate.handle, 0, seed, synth.TAG_SHARED_GATE, layer, 0, width, 0.02))
+        blobs = backend.alloc(el * words, "u32", zero=False)
+        backend._check(lib.strata_synth_blobs(ctx, blobs.handle, 0, seed, layer, rank * el, el, width, ff, 0))
+        shared = backend.alloc(words, "u32", zero=False)
+        backend._check(lib.strata_synth_blobs(ctx, shared.handle, 0, seed, layer, 0, 1, width, ff, 1))
+        bias = None if zipf is None else backend.alloc(synth.zipf_bias(seed, experts, zipf))
+        return cls(backend, rank, n_ranks, width, ff, experts, top_k, router, blobs, shared, gate, bias)
+
+
+def plan_dispatch(ids: np.ndarray, experts: int, n_ranks: int):
+    """Host restatement of the dispatch plan the library computes on the device (used by the
+    CPU tests): pairs (t, k) bucketed by destination rank e // (E/n), token-major inside each
+    bucket. Returns (position of every pair in the send order or -1, per-rank counts)."""
+    el = experts // n_ranks
+    T, K = ids.shape
+    flat = ids.reshape(-1)
+    dest = np.where((flat >= 0) & (flat < experts), flat // el, -1)
+    counts = np.array([(dest == r).sum() for r in range(n_ranks)], np.int64)
+    offsets = np.concatenate([[0], np.cumsum(counts)])
+    pos = np.full(flat.shape, -1, np.int64)
+    seen = np.zeros(n_ranks, np.int64)
+    for p, d in enumerate(dest):
+        if d >= 0:
+            pos[p] = offsets[d] + seen[d]
+            seen[d] += 1
+    return pos.reshape(T, K), counts

@@ -1,0 +1,80 @@
+"""Expert-parallel layer (strata_moe_ep_forward, NCCL inside the library) against the exact
+single-GPU layer: routing ids and weights bit-identical, y within 2e-3 relative L2 per token.
+One rank runs on any GPU box; two ranks run as spawned processes when two GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_rank(rank, world, T, seed, zipf):
+    """EP forward of this rank's tokens and the exact full layer on the same GPU."""
+    from stratacuda_b200 import _lib as L
+    from stratacuda_b200.backend import CudaBackend
+    from stratacuda_b200.ep import EpMoeLayer, ep_init
+    from stratacuda_b200.moe import MoeLayer, synth_activations
+    b = CudaBackend(rank)
+    try:
+        ep_init(b, rank, world)
+        layer = EpMoeLayer.synthesize(b, rank, world, seed=seed, layer=0, zipf=zipf)
+        x = synth_activations(b, 90 + rank, T, layer.width)
+        y, ids, w = b.alloc(T * 2048), b.alloc(T * 10, "i32"), b.alloc(T * 10)
+        layer.forward(x, T, y, ids, w)
+        yv, idv, wv = b.read(y).reshape(T, 2048), b.read(ids).reshape(T, 10), b.read(w).reshape(T, 10)
+        full = MoeLayer.synthesize(b, seed=seed, layer=0, zipf=zipf)
+        full.forward(x, T, y, ids, w, mode=L.MOE_EXACT)
+        ye, ide, we = b.read(y).reshape(T, 2048), b.read(ids).reshape(T, 10), b.read(w).reshape(T, 10)
+        errs = [rel_l2(yv[t], ye[t]) for t in range(T)]
+        return bool(np.array_equal(idv, ide)), bool(np.array_equal(bits(wv), bits(we))), float(max(errs))
+    finally:
+        b.dispose()
+
+
+@pytest.mark.parametrize("T", [1, 300])
+def test_ep_single_rank(T):
+    ids_ok, w_ok, err = run_rank(0, 1, T, seed=4, zipf=None)
+    assert ids_ok and w_ok
+    assert err <= TOL, err
+
+
+def worker(rank, world, port, T, out):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        out[rank] = run_rank(rank, world, T, seed=6, zipf=1.1)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(600)
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("T", [5, 700])
+def test_ep_two_ranks(T):
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.spawn(worker, args=(2, free_port(), T, out), nprocs=2, join=True)
+    for r in range(2):
+        ids_ok, w_ok, err = out[r]
+        assert ids_ok and w_ok, r
+        assert err <= TOL, (r, err)
