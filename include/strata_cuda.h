@@ -179,9 +179,11 @@ int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata
  * stream. strata_profile_read synchronises, adds the phase times (milliseconds) of every call
  * since the last read into ms[0..n) and resets them; *calls receives the number of calls.
  * Phases: 0 routing (prefill path: router logits, top-k, permutation, activation rows),
- * 1 gate/up tensor-core GEMM, 2 down tensor-core GEMM (both prefill path), 3 fused decode
- * kernel (decode path). */
-#define STRATA_PHASES 4
+ * 1 gate/up tensor-core GEMM, 2 down tensor-core GEMM (prefill and expert-parallel paths),
+ * 3 fused decode kernel (decode path), 4 expert-parallel dispatch (counts and rows exchange,
+ * regrouping by local expert), 5 expert-parallel return (outputs back to their ranks, combine).
+ * strata_moe_ep_forward records phases 0, 4, 1, 2, 5. */
+#define STRATA_PHASES 6
 int strata_profile(strata_ctx *ctx, int32_t enable);
 int strata_profile_read(strata_ctx *ctx, double *ms, int32_t n, uint64_t *calls);
 

@@ -153,7 +153,7 @@ class CudaBackend:
         self.lib.strata_info(self.ctx, buf, len(buf))
         return json.loads(buf.value.decode())
 
-    PHASES = ("routing", "gemm_gate_up", "gemm_down", "decode_kernel")
+    PHASES = ("routing", "gemm_gate_up", "gemm_down", "decode_kernel", "ep_dispatch", "ep_return")
 
     def profile(self, enable: bool) -> None:
         """Record device time of the fused layer's phases (strata_profile)."""

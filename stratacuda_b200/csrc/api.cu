@@ -500,10 +500,35 @@ int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata
     if (int r = use_device(ctx)) return r;
     MoeLayerDev L{l.width, l.ff, l.experts, l.top_k, (const float *)ptr[0], (const float *)ptr[1], (const unsigned *)ptr[2], bw,
                   (const unsigned *)ptr[3], (const float *)ptr[4]};
+    // profile: boundaries start | packed | GEMMs start | gate/up done | down done | combined
+    cudaEvent_t ev[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    if (ctx->profile) {
+        for (cudaEvent_t &e : ev) {
+            if (!ctx->spare_events.empty()) {
+                e = ctx->spare_events.back();
+                ctx->spare_events.pop_back();
+            } else {
+                CUDA_OR_FAIL(ctx, cudaEventCreate(&e), "cudaEventCreate");
+            }
+        }
+        ++ctx->profiled_calls;
+    }
     std::string msg;
-    if (moe_forward_ep(L, ctx->ep, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->sms, ctx->stream,
-                       ctx->err_dev, &msg))
-        return fail(ctx, STRATA_ERR_CUDA, "strata_moe_ep_forward: %s", msg.c_str());
+    const int rc = moe_forward_ep(L, ctx->ep, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->sms,
+                                  ctx->stream, ctx->err_dev, &msg, ev[0] ? ev : nullptr);
+    if (ev[0]) {
+        if (rc) {
+            for (cudaEvent_t e : ev) ctx->spare_events.push_back(e);
+            --ctx->profiled_calls;
+        } else {
+            ctx->marks.push_back({0, ev[0], ev[1]});
+            ctx->marks.push_back({4, ev[1], ev[2]});
+            ctx->marks.push_back({1, ev[2], ev[3]});
+            ctx->marks.push_back({2, ev[3], ev[4]});
+            ctx->marks.push_back({5, ev[4], ev[5]});
+        }
+    }
+    if (rc) return fail(ctx, STRATA_ERR_CUDA, "strata_moe_ep_forward: %s", msg.c_str());
     ++ctx->fused_calls;
     return STRATA_OK;
 }

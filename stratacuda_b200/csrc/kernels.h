@@ -90,7 +90,8 @@ EpComm *ep_create(int rank, int n_ranks, const char *id128, std::string *err);
 void ep_destroy(EpComm *c);
 int ep_ranks(const EpComm *c);
 int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int tokens, float *y, int *ids, float *weights, int grid, cudaStream_t s,
-                   unsigned *err, std::string *msg);
+                   unsigned *err, std::string *msg,
+                   cudaEvent_t *marks = nullptr);
 
 // Device synthetic generator (csrc/synth.cu), same bytes as stratacuda_b200/synth.py.
 cudaError_t synth_expert_blobs(unsigned *out, unsigned long long seed, int layer, int first_expert, int count, int width, int ff,

@@ -13,9 +13,12 @@
 // Persistent kernel, one CTA per SM, tiles dealt round-robin (tile i on CTA i % G). Tile i is
 // chunk i / NM of the chunk list (slot, first B row, rows) and weight block i % NM; the chunk
 // list is ordered by decreasing rows, so the deal approximates longest-first. Warp roles:
-//   warp 0      TMA producer: per tile the rows' FP16 scales (one bulk copy); per 256-column
-//               super-block the packed codes (one 128-row x 64-byte box, 64-byte swizzle);
-//               per 64-column K-block the B rows (16-row boxes, 128-byte swizzle)
+//   warp 0      TMA producer of B: per 64-column K-block the B rows (64-row boxes, then
+//               16-row boxes for the rest; 128-byte swizzle)
+//   warp 14     TMA producer of A: per tile the rows' FP16 scales (one bulk copy); per
+//               256-column super-block the packed codes (one 128-row x 64-byte box, 64-byte
+//               swizzle). Its own thread, so the codes run ahead of the dequantisers while the
+//               B producer waits for free stages
 //   warp 1      allocates TMEM (512 columns: two 192-column accumulators and four 32-column
 //               A stages) and issues the MMAs from one thread: per K-block four tcgen05.mma
 //               (K = 16, A from TMEM, B from shared memory), then tcgen05.commit
@@ -36,7 +39,8 @@
 namespace strata {
 namespace pf {
 
-constexpr int kGemmWarps = 14;
+constexpr int kGemmWarps = 15;
+constexpr int kCodeWarp = 14;   // producer of scales and packed codes
 constexpr int kGemmThreads = kGemmWarps * 32;
 constexpr int kDeqThreads = 256;  // warps 2-9
 constexpr int kEpiWarp0 = 10;     // warps 10-13
@@ -82,6 +86,7 @@ struct GemmParams {
     unsigned long long spin_limit;
     CUtensorMap tm_codes[2];   // [0] routed blobs {K/4 bytes, rows_total, experts}, [1] shared; box {64, 128}, 64B swizzle
     CUtensorMap tm_b;          // B {K, rows} FP16, box {64, 16}, 128B swizzle
+    CUtensorMap tm_b64;        // the same matrix, box {64, 64}
 };
 
 __device__ __forceinline__ unsigned su32(const void *p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
@@ -157,6 +162,17 @@ __device__ __forceinline__ void mma_f16(unsigned tmem_d, unsigned long long a, u
 }
 __device__ __forceinline__ void mma_commit(unsigned long long *b) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b)) : "memory");
+}
+// One lane of the converged warp (elect.sync): the warp computes the MMA operands as
+// warp-uniform values and the elected lane issues.
+__device__ __forceinline__ bool elect_one() {
+    unsigned r;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r));
+    return r != 0;
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -293,9 +309,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
     };
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- producer
+        // ---------------------------------------------------------------- producer of B
         if (lane == 0) {
-            int kb_count = 0, sb_count = 0, lt = 0;
+            int kb_count = 0;
+            bool ok = true;
+            for (int ti = cta; ti < n_tiles && ok; ti += G) {
+                const Tile t = tile_at(ti);
+                const int nb = (t.n + 15) >> 4;  // 16-row B boxes: nb / 4 boxes of 64 rows, then nb % 4 of 16
+                for (int kb = 0; kb < NKB && ok; ++kb, ++kb_count) {
+                    const int s = kb_count % kStages;
+                    if (!(ok = wait(&S.empty[s], ((kb_count / kStages) & 1) ^ 1))) break;
+                    bar_expect(&S.full[s], nb * 16 * 128);
+                    int i = 0;
+                    for (; i + 4 <= nb; i += 4) tma2(S.b[s] + i * 16 * 128, &P.tm_b64, kKBlock * kb, t.row0 + 16 * i, &S.full[s]);
+                    for (; i < nb; ++i) tma2(S.b[s] + i * 16 * 128, &P.tm_b, kKBlock * kb, t.row0 + 16 * i, &S.full[s]);
+                }
+            }
+            // every issued copy must land before the CTA leaves
+            for (int k = max(0, kb_count - kStages); k < kb_count; ++k) drain(&S.full[k % kStages], (k / kStages) & 1);
+        }
+    } else if (warp == kCodeWarp) {
+        // ---------------------------------------------------------------- producer of A (scales, codes)
+        if (lane == 0) {
+            int sb_count = 0, lt = 0;
             bool ok = true;
             for (int ti = cta; ti < n_tiles && ok; ti += G, ++lt) {
                 const Tile t = tile_at(ti);
@@ -304,57 +340,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
                 const unsigned sbytes = 128u * NGRP * 2;
                 bar_expect(&S.scl_full[ts], sbytes);
                 bulk(S.scl[ts], tile_blob(t) + P.scales_off + (long long)t.mtile * 128 * NGRP * 2, sbytes, &S.scl_full[ts]);
-                const int nb = (t.n + 15) >> 4;  // 16-row B boxes
                 for (int sb = 0; sb < NSB && ok; ++sb, ++sb_count) {
                     const int sa = sb_count % kApkStages;
                     if (!(ok = wait(&S.apk_empty[sa], ((sb_count / kApkStages) & 1) ^ 1))) break;
                     bar_expect(&S.apk_full[sa], 128 * 64);
                     tma3(S.apk[sa], &P.tm_codes[t.slot < 0 ? 1 : 0], 64 * sb, 128 * t.mtile, t.slot < 0 ? 0 : t.slot, &S.apk_full[sa]);
-                    const int kb_end = min(NKB, (sb + 1) * kSuper);
-                    for (int kb = sb * kSuper; kb < kb_end; ++kb, ++kb_count) {
-                        const int s = kb_count % kStages;
-                        if (!(ok = wait(&S.empty[s], ((kb_count / kStages) & 1) ^ 1))) break;
-                        bar_expect(&S.full[s], nb * 16 * 128);
-                        for (int i = 0; i < nb; ++i) tma2(S.b[s] + i * 16 * 128, &P.tm_b, kKBlock * kb, t.row0 + 16 * i, &S.full[s]);
-                    }
                 }
             }
-            // every issued copy must land before the CTA leaves
-            for (int k = max(0, kb_count - kStages); k < kb_count; ++k) drain(&S.full[k % kStages], (k / kStages) & 1);
             for (int k = max(0, sb_count - kApkStages); k < sb_count; ++k) drain(&S.apk_full[k % kApkStages], (k / kApkStages) & 1);
             for (int k = max(0, lt - 2); k < lt; ++k) drain(&S.scl_full[k & 1], (k >> 1) & 1);  // lt = scale copies issued
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            int kb_count = 0, lt = 0;
-            bool ok = true;
-            for (int ti = cta; ti < n_tiles && ok; ti += G, ++lt) {
-                const Tile t = tile_at(ti);
-                const int buf = lt & 1;
-                if (!(ok = wait(&S.tmem_empty[buf], ((lt >> 1) & 1) ^ 1))) break;
+        // the warp runs converged (waits voted warp-wide) so the operands stay warp-uniform;
+        // one elected lane issues the MMAs and commits
+        int kb_count = 0, lt = 0;
+        bool ok = true;
+        for (int ti = cta; ti < n_tiles && ok; ti += G, ++lt) {
+            const Tile t = tile_at(ti);
+            const int buf = lt & 1;
+            if (!(ok = __all_sync(0xffffffffu, wait(&S.tmem_empty[buf], ((lt >> 1) & 1) ^ 1)))) break;
+            tc_fence_after();
+            const int N = (t.n + 15) & ~15;
+            const unsigned idesc = idesc_f16(128, N);
+            const unsigned d = tmem + buf * kAccCols;
+            for (int kb = 0; kb < NKB && ok; ++kb, ++kb_count) {
+                const int s = kb_count % kStages, sa = kb_count % kAStages;
+                if (!(ok = __all_sync(0xffffffffu, wait(&S.full[s], (kb_count / kStages) & 1) && wait(&S.a_full[sa], (kb_count / kAStages) & 1))))
+                    break;
                 tc_fence_after();
-                const int N = (t.n + 15) & ~15;
-                const unsigned idesc = idesc_f16(128, N);
-                const unsigned d = tmem + buf * kAccCols;
-                for (int kb = 0; kb < NKB && ok; ++kb, ++kb_count) {
-                    const int s = kb_count % kStages, sa = kb_count % kAStages;
-                    if (!(ok = wait(&S.full[s], (kb_count / kStages) & 1) && wait(&S.a_full[sa], (kb_count / kAStages) & 1))) break;
-                    tc_fence_after();
-                    const unsigned a = tmem + kACol0 + 32 * sa;
-                    const unsigned long long bd = sw128_desc(su32(S.b[s]));
+                const unsigned a = tmem + kACol0 + 32 * sa;
+                const unsigned long long bd = sw128_desc(su32(S.b[s]));
+                if (elect_one()) {
 #pragma unroll
                     for (int k = 0; k < kKBlock / 16; ++k)  // K = 16 per MMA: 8 TMEM columns of A, +32 bytes inside the swizzled B row
                         mma_f16_ts(d, a + 8 * k, bd + 2 * k, idesc, kb > 0 || k > 0);
                     mma_commit(&S.empty[s]);
                     mma_commit(&S.a_empty[sa]);
                 }
-                if (ok) mma_commit(&S.tmem_full[buf]);
+                __syncwarp();
             }
-            // every MMA issued must complete before TMEM is released
-            mma_commit(&S.mma_done);
-            drain(&S.mma_done, 0);
+            if (ok && elect_one()) mma_commit(&S.tmem_full[buf]);
+            __syncwarp();
         }
+        // every MMA issued must complete before TMEM is released
+        if (elect_one()) mma_commit(&S.mma_done);
+        __syncwarp();
+        drain(&S.mma_done, 0);
     } else if (warp < kEpiWarp0) {
         // ---------------------------------------------------------------- dequantise
         const int quarter = warp & 3, hf = (warp - 2) >> 2;  // TMEM lane quarter; codes 32 hf .. 32 hf + 31
@@ -433,7 +465,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
                         const float a = v[j] * sc;
                         const float up = __shfl_xor_sync(0xffffffffu, a, 1);
                         if (!(lane & 1) && n < t.n) {
-                            const float h = a / (1.0f + __expf(-a)) * up;  // silu(gate) * up (prefill tolerance 2e-3)
+                            const float h = __fdividef(a, 1.0f + __expf(-a)) * up;  // silu(gate) * up (prefill tolerance 2e-3)
                             reinterpret_cast<__half *>(S.staging)[n * 64 + (row >> 1)] = __float2half_rn(h);
                         }
                     }

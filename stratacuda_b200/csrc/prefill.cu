@@ -384,6 +384,12 @@ __global__ void __launch_bounds__(256) k_ep_pack(const float *__restrict__ x, in
     }
 }
 
+// Send counts per destination rank from the bucket offsets (the counts the ranks exchange).
+__global__ void k_ep_send_counts(const int *off, int n, int *cnt) {
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p < n) cnt[p] = off[p + 1] - off[p];
+}
+
 __global__ void k_ep_local_expert(const int4 *meta, int R, int *lid) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < R) lid[i] = meta[i].x;
@@ -545,8 +551,10 @@ cudaError_t launch_moe_gemms(const MoeLayerDev &L, int experts, const pf::Chunk 
         const void *bmat = mode == 0 ? (const void *)B : (const void *)hidden;
         const unsigned long long bdims[2] = {(unsigned long long)p.K, (unsigned long long)max(1LL, b_rows)};
         const unsigned long long bstr[1] = {(unsigned long long)p.K * 2};
-        const unsigned bbox[2] = {64, 16};
-        if (!encode(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bmat, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaErrorInvalidValue;
+        const unsigned bbox[2] = {64, 16}, bbox64[2] = {64, 64};
+        if (!encode(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bmat, bdims, bstr, bbox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode(&p.tm_b64, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, bmat, bdims, bstr, bbox64, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
         STRATA_CUDA_TRY(mode == 0 ? launch_gemm<pf::kGateUp>(p, grid, s) : launch_gemm<pf::kDown>(p, grid, s));
         if (marks) STRATA_CUDA_TRY(cudaEventRecord(marks[mode], s));
     }
@@ -711,9 +719,10 @@ int ep_ranks(const EpComm *c) { return c->n; }
 // ncclSend/ncclRecv; the received rows regrouped by local expert and run through the tensor-
 // core GEMMs together with this rank's shared-expert rows; outputs sent back; y[t] = shared
 // row + the token's returned rows in k order. The receive sizes are read back on the host
-// (as the reference reads its routing back, src/engine.js:137).
+// (as the reference reads its routing back, src/engine.js:137). marks (nullable): six events at
+// start, after packing, before the GEMMs, after gate/up, after down, after the combine.
 int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float *y, int *ids, float *weights, int grid, cudaStream_t s,
-                   unsigned *err, std::string *msg) {
+                   unsigned *err, std::string *msg, cudaEvent_t *marks) {
     const int H = L.width, F = L.ff, E = L.experts, K = L.topK, n = c->n, El = E / n;
     cudaError_t e = cudaSuccess;
     auto fail_cuda = [&](cudaError_t ce, const char *what) {
@@ -739,7 +748,12 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     if (!ptr) return fail_cuda(e, "cudaMalloc");
     const long long P = (long long)T * K;
     const int n_tc = (T + pf::kTokChunk - 1) / pf::kTokChunk;
+#define EP_MARK(i)                                                                   \
+    do {                                                                             \
+        if (marks) EP_CUDA(cudaEventRecord(marks[i], s), "cudaEventRecord");        \
+    } while (0)
     // 1. routing
+    EP_MARK(0);
     EP_GET(logits, float, 0, (long long)T * E);
     EP_GET(sg, float, 1, T);
     static int logits_ready_device = -1;
@@ -765,23 +779,23 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     EP_GET(send_rows, __half, 8, P * H);
     EP_GET(send_meta, int4, 9, P);
     pf::k_ep_pack<<<T, 256, 0, s>>>(x, H, K, ids, weights, El, pos, send_rows, send_meta);
-    EP_CUDA(cudaGetLastError(), "routing and packing kernels");
-    // 3. counts exchange
+    EP_MARK(1);
+    // 3. counts exchange; one host read of the send offsets and the receive counts
     EP_GET(d_cnt, int, 10, 2 * n);
-    EP_CUDA(cudaMemcpyAsync(c->h_off, off, sizeof(int) * (n + 1), cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
-    EP_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
-    std::vector<int> soff(n + 1), sc(n), rc(n), roff(n + 1);
-    for (int i = 0; i <= n; ++i) soff[i] = c->h_off[i];
-    for (int i = 0; i < n; ++i) sc[i] = soff[i + 1] - soff[i];
-    EP_CUDA(cudaMemcpyAsync(d_cnt, sc.data(), sizeof(int) * n, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync");
+    pf::k_ep_send_counts<<<(n + 127) / 128, 128, 0, s>>>(off, n, d_cnt);
+    EP_CUDA(cudaGetLastError(), "routing and packing kernels");
     EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
     for (int p = 0; p < n; ++p) {
         EP_NCCL(nccl().Send(d_cnt + p, 1, ncclInt32, p, c->comm, s), "ncclSend");
         EP_NCCL(nccl().Recv(d_cnt + n + p, 1, ncclInt32, p, c->comm, s), "ncclRecv");
     }
     EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
+    EP_CUDA(cudaMemcpyAsync(c->h_off, off, sizeof(int) * (n + 1), cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
     EP_CUDA(cudaMemcpyAsync(c->h_off + n + 1, d_cnt + n, sizeof(int) * n, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
     EP_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    std::vector<int> soff(n + 1), sc(n), rc(n), roff(n + 1);
+    for (int i = 0; i <= n; ++i) soff[i] = c->h_off[i];
+    for (int i = 0; i < n; ++i) sc[i] = soff[i + 1] - soff[i];
     roff[0] = 0;
     for (int i = 0; i < n; ++i) {
         rc[i] = c->h_off[n + 1 + i];
@@ -834,7 +848,9 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     EP_CUDA(cudaGetLastError(), "expert grouping kernels");
     MoeLayerDev Ll = L;
     Ll.experts = El;
-    EP_CUDA(launch_moe_gemms(Ll, El, chunks, nchunks, brows, B, hidden, row_scale, row_token, row_weight, Y, grid, s, err, nullptr),
+    EP_MARK(2);
+    EP_CUDA(launch_moe_gemms(Ll, El, chunks, nchunks, brows, B, hidden, row_scale, row_token, row_weight, Y, grid, s, err,
+                             marks ? marks + 3 : nullptr),
             "expert GEMMs");
     // 6. outputs back to their tokens' ranks
     EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
@@ -846,6 +862,8 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     // 7. combine
     pf::k_ep_combine<<<T, 128, 0, s>>>(ret, pos, K, H, Y + (long long)R * H, y);
     EP_CUDA(cudaGetLastError(), "combine");
+    EP_MARK(5);
+#undef EP_MARK
 #undef EP_CUDA
 #undef EP_NCCL
 #undef EP_GET
