@@ -87,6 +87,26 @@ __device__ __forceinline__ float ref_expf(float x) {
 __device__ __forceinline__ float ref_sigmoid(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, ref_expf(-x))); }
 __device__ __forceinline__ float ref_silu(float x) { return __fmul_rn(x, ref_sigmoid(x)); }
 
+// Paired F32 arithmetic (sm_100): each element of the pair is rounded to nearest exactly as
+// the scalar __fmul_rn / __fadd_rn would round it (measured bit for bit). The compiler turns a
+// paired product whose only use is a paired add into one fused multiply-add, which rounds
+// once; a caller that needs both roundings gives every product a second use (xor3 below).
+__device__ __forceinline__ unsigned long long mul2_rn(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long add2_rn(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned xor3(unsigned a, unsigned b, unsigned c) {
+    unsigned d;
+    asm("lop3.b32 %0, %1, %2, %3, 0x96;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // One warp emulates a reference workgroup of 64 lanes: thread t owns lanes t and t+32.
 // The reference's tree (partial[l] += partial[l+s], s = 32..1) is the in-thread s=32 add
 // followed by shuffle-down adds; the result is exact and valid in lane 0.

@@ -36,103 +36,196 @@ namespace strata {
 namespace pf {
 
 // ------------------------------------------------------------------ router logits
-constexpr int kLgT = 16, kLgR = 16, kLgKC = 256;  // CTA tile: tokens, rows; K chunk
-constexpr int kLgSmem = 2 * (kLgT + kLgR) * kLgKC * 4;  // double-buffered x and router tiles (64 KB)
+// Router logits (+ the shared-gate row as row E), bit-identical to the reference's order: lane
+// l of 64 sums x[k] w[k] over k = l mod 64 in increasing k, one rounding per multiply and per
+// add (scalar __fmul_rn / __fadd_rn; the paired F32 instructions are slower here than the
+// scalar pipe and fuse into a single-rounding multiply-add unless kept apart), then the tree
+// partial[l] += partial[l + s], s = 32 .. 1.
+//
+// Persistent, one CTA per SM: work item = 16 tokens x 3 row tiles of kLgR rows. Warp
+// kLgWarps is the producer: per item it loads the 16 tokens' x by 256-column chunks (one TMA
+// box each, rows past T read as zero) into a resident buffer, and streams the router rows of
+// each (row tile, chunk) step through a ring of stages (one TMA box each; the last row tile,
+// which holds the shared-gate row, comes from a per-call tail copy of those rows). Each x
+// chunk is released once the item's last row tile has used it, so the next item's x loads
+// while the current one finishes. Compute warps: thread i holds the reference's lanes 2i and
+// 2i + 1 (one 8-byte shared load gives both lanes' operands) for an 8-token x 4-row tile. The
+// tree is a transposing butterfly: at xor distance 16, 8, 4, 2, 1 (lane distance 32 .. 2)
+// each thread keeps half of its outputs and adds its partner's pair for them (both lanes at
+// once: add.rn.f32x2 rounds each element like __fadd_rn); the last add joins lanes 0 and 1.
+// Every add has the reference's operands; thread t ends with output t = 4 token + row.
+constexpr int kLgT = 16;                                // tokens per work item
+constexpr int kLgKC = 256;                              // K chunk (one 1 KB row segment per box row)
+constexpr int kLgGroup = 3;                             // row tiles per work item
+constexpr int kLgWarps = 12;                            // compute warps; warp kLgWarps produces
+constexpr int kLgWT = 8, kLgWR = 4;                     // warp tile: tokens, rows
+constexpr int kLgR = (kLgWarps / (kLgT / kLgWT)) * kLgWR;  // rows per row tile (24)
+constexpr int kLgMaxStages = 4, kLgMaxNC = 10;          // router stages; x chunks (H <= 2560)
+constexpr int kLgThreads = 32 * (kLgWarps + 1);
+constexpr size_t kLgSmemLimit = 227 * 1024;
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
-        "@p cp.async.cg.shared.global [%0], [%1], 16;\n\t"
-        "@!p st.shared.v4.u32 [%0], {0, 0, 0, 0};\n\t}" ::"r"(su32(dst)),
-        "l"(src), "r"((unsigned)valid)
-        : "memory");
+struct LgMaps {
+    CUtensorMap router;  // {H, E} F32, box {256, kLgR}
+    CUtensorMap tail;    // {H, kLgR} F32 (rows E / kLgR * kLgR .. : router rows, the gate, zeros), box {256, kLgR}
+    CUtensorMap x;       // {H, T} F32, box {256, 16}
+};
+struct __align__(8) LgBars {
+    unsigned long long full[kLgMaxStages], empty[kLgMaxStages], xfull[kLgMaxNC], xempty[kLgMaxNC];
+    int abort_flag;
+};
+inline int logits_stages(int H) {
+    const size_t fixed = 1024 + sizeof(LgBars) + (size_t)kLgT * H * 4;
+    const size_t stage = (size_t)kLgR * kLgKC * 4;
+    return (int)std::min<size_t>(kLgMaxStages, (kLgSmemLimit - fixed) / stage);
+}
+inline size_t logits_smem(int H) { return 1024 + sizeof(LgBars) + (size_t)kLgT * H * 4 + (size_t)logits_stages(H) * kLgR * kLgKC * 4; }
+
+// The last row tile's rows: router rows [r0, E), the shared gate at E, zeros up to kLgR.
+__global__ void k_lg_tail(const float *router, const float *gate, int E, int H, int r0, float *tail) {
+    const int i = blockIdx.x, r = r0 + i;
+    const float *src = r < E ? router + (long long)r * H : gate;
+    for (int k = threadIdx.x; k < H; k += blockDim.x) tail[(long long)i * H + k] = r <= E ? src[k] : 0.0f;
 }
 
-// Products and sums are scalar __fmul_rn / __fadd_rn (the paired F32 instructions of sm_100
-// did not reproduce the scalar rounded chains bit for bit when measured here). Within a K
-// chunk the next step's 16 operands are read while the current 128 operations issue.
-__global__ void __launch_bounds__(256) k_pf_logits(MoeLayerDev L, const float *__restrict__ x, int T, float *logits, float *sg) {
-    extern __shared__ __align__(16) float lg_smem[];
-    float(*xs)[kLgT][kLgKC] = reinterpret_cast<float(*)[kLgT][kLgKC]>(lg_smem);
-    float(*ws)[kLgR][kLgKC] = reinterpret_cast<float(*)[kLgR][kLgKC]>(lg_smem + 2 * kLgT * kLgKC);
-    const int H = L.width, E = L.experts;
-    const int t0 = blockIdx.x * kLgT, r0 = blockIdx.y * kLgR;
-    const int tid = threadIdx.x, lg = tid >> 6, l = tid & 63;
-    const int tb = (lg & 1) * 8, rb = (lg >> 1) * 8;  // this lane group's 8 tokens and 8 rows
-    auto load = [&](int buf, int c) {
-        for (int i = tid; i < kLgT * kLgKC / 4; i += 256) {  // 16 rows x 64 float4 each
-            const int row = i >> 6, c4 = i & 63;
-            const int t = t0 + row;
-            cp_async16(&xs[buf][row][4 * c4], x + (long long)min(t, T - 1) * H + c * kLgKC + 4 * c4, t < T);
-            const int r = r0 + row;
-            const float *W = r < E ? L.router + (long long)r * H : L.shared_gate;
-            cp_async16(&ws[buf][row][4 * c4], W + c * kLgKC + 4 * c4, r <= E);
+__global__ void __launch_bounds__(kLgThreads, 1)
+    k_pf_logits(const __grid_constant__ LgMaps M, MoeLayerDev L, int T, int ST, float *logits, float *sg, unsigned *err,
+                unsigned long long spin_limit) {
+    extern __shared__ unsigned char lg_raw[];
+    unsigned char *base = lg_raw + ((1024 - (su32(lg_raw) & 1023)) & 1023);
+    const int H = L.width, E = L.experts, NC = H / kLgKC;
+    float *xs = reinterpret_cast<float *>(base);       // [NC][16][256]
+    float *ws = xs + (size_t)NC * kLgT * kLgKC;         // [ST][kLgR][256]
+    LgBars &B = *reinterpret_cast<LgBars *>(ws + (size_t)ST * kLgR * kLgKC);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_full = E / kLgR, n_rt = n_full + 1, n_grp = (n_rt + kLgGroup - 1) / kLgGroup;
+    const int n_items = ((T + kLgT - 1) / kLgT) * n_grp;
+    if (tid == 0) {
+        for (int i = 0; i < ST; ++i) {
+            bar_init(&B.full[i], 1);
+            bar_init(&B.empty[i], kLgWarps);
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    float acc[8][8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-    const int NC = H / kLgKC;
-    load(0, 0);
-    for (int c = 0; c < NC; ++c) {
-        if (c + 1 < NC) {
-            load((c + 1) & 1, c + 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        for (int i = 0; i < NC; ++i) {
+            bar_init(&B.xfull[i], 1);
+            bar_init(&B.xempty[i], kLgWarps);
         }
-        __syncthreads();
-        const int b = c & 1;
-        float xv[2][8], wv[2][8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) xv[0][i] = xs[b][tb + i][l];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) wv[0][j] = ws[b][rb + j][l];
-#pragma unroll
-        for (int m = 0; m < kLgKC / 64; ++m) {  // element l + 64 m of the chunk: this lane's next term
-            const int cur = m & 1;
-            if (m + 1 < kLgKC / 64) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xv[cur ^ 1][i] = xs[b][tb + i][l + 64 * (m + 1)];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) wv[cur ^ 1][j] = ws[b][rb + j][l + 64 * (m + 1)];
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[cur][j], xv[cur][i]));
-        }
-        __syncthreads();
-    }
-    // tree over the 64 lanes: lane l (< 32, first warp) adds lane l + 32 (second warp), then
-    // shuffles s = 16 .. 1; the staging reuses the x tiles
-    float *red = &xs[0][0][0] + lg * 64 * 32;  // [64 outputs][32 lanes]
-    if (l >= 32) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) red[(i * 8 + j) * 32 + (l - 32)] = acc[i][j];
+        B.abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (l < 32) {
+    auto wait = [&](unsigned long long *b, unsigned parity) -> bool {
+        for (unsigned long long i = 0;; ++i) {
+            if (bar_try(b, parity)) return true;
+            if (i > spin_limit || *(volatile int *)&B.abort_flag) {
+                atomicOr(&B.abort_flag, 1);
+                return false;
+            }
+        }
+    };
+    if (warp == kLgWarps) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            int g = 0, it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+                const int t0 = (item / n_grp) * kLgT, rt0 = (item % n_grp) * kLgGroup;
+                const int nrt = min(kLgGroup, n_rt - rt0);
+                for (int rr = 0; rr < nrt && ok; ++rr)
+                    for (int c = 0; c < NC && ok; ++c, ++g) {
+                        if (rr == 0) {  // the item's x chunk c, once the previous item released it
+                            if (!(ok = wait(&B.xempty[c], (it & 1) ^ 1))) break;
+                            bar_expect(&B.xfull[c], kLgT * kLgKC * 4);
+                            tma2(xs + (size_t)c * kLgT * kLgKC, &M.x, c * kLgKC, t0, &B.xfull[c]);
+                        }
+                        const int st = g % ST, rt = rt0 + rr;
+                        if (!(ok = wait(&B.empty[st], ((g / ST) & 1) ^ 1))) break;
+                        bar_expect(&B.full[st], kLgR * kLgKC * 4);
+                        if (rt < n_full) tma2(ws + (size_t)st * kLgR * kLgKC, &M.router, c * kLgKC, rt * kLgR, &B.full[st]);
+                        else tma2(ws + (size_t)st * kLgR * kLgKC, &M.tail, c * kLgKC, 0, &B.full[st]);
+                    }
+            }
+            // every issued copy lands before the CTA leaves (bounded)
+            for (int k = max(0, g - ST); k < g; ++k)
+                for (unsigned long long i = 0; i <= spin_limit && !bar_try(&B.full[k % ST], (k / ST) & 1); ++i) {
+                }
+        }
+    } else {
+        // ---------------------------------------------------------------- compute
+        const int tb = (warp % (kLgT / kLgWT)) * kLgWT, rb = (warp / (kLgT / kLgWT)) * kLgWR;
+        typedef unsigned long long u64;
+        int g = 0, it = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+            const int t0 = (item / n_grp) * kLgT, rt0 = (item % n_grp) * kLgGroup;
+            const int nrt = min(kLgGroup, n_rt - rt0);
+            for (int rr = 0; rr < nrt && ok; ++rr) {
+                float acc[kLgWT][kLgWR][2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+                for (int i = 0; i < kLgWT; ++i)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                float a = __fadd_rn(acc[i][j], red[(i * 8 + j) * 32 + l]);
+                    for (int j = 0; j < kLgWR; ++j) acc[i][j][0] = acc[i][j][1] = 0.0f;
+                for (int c = 0; c < NC; ++c, ++g) {
+                    const int st = g % ST;
+                    if (!(ok = __all_sync(0xffffffffu, (rr > 0 || wait(&B.xfull[c], it & 1)) && wait(&B.full[st], (g / ST) & 1)))) break;
+                    const float *xb = xs + (size_t)c * kLgT * kLgKC + 2 * lane;
+                    const float *wb = ws + (size_t)st * kLgR * kLgKC + 2 * lane;
+                    float2 xv[2][kLgWT], wv[2][kLgWR];
 #pragma unroll
-                for (int s = 16; s > 0; s >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, s));
-                const int t = t0 + tb + i, r = r0 + rb + j;
-                if (l == 0 && t < T) {
+                    for (int i = 0; i < kLgWT; ++i) xv[0][i] = *reinterpret_cast<const float2 *>(xb + (tb + i) * kLgKC);
+#pragma unroll
+                    for (int j = 0; j < kLgWR; ++j) wv[0][j] = *reinterpret_cast<const float2 *>(wb + (rb + j) * kLgKC);
+#pragma unroll
+                    for (int m = 0; m < kLgKC / 64; ++m) {  // elements 2 lane + 64 m and + 1: the two lanes' next terms
+                        const int cur = m & 1;
+                        if (m + 1 < kLgKC / 64) {
+#pragma unroll
+                            for (int i = 0; i < kLgWT; ++i) xv[cur ^ 1][i] = *reinterpret_cast<const float2 *>(xb + (tb + i) * kLgKC + 64 * (m + 1));
+#pragma unroll
+                            for (int j = 0; j < kLgWR; ++j) wv[cur ^ 1][j] = *reinterpret_cast<const float2 *>(wb + (rb + j) * kLgKC + 64 * (m + 1));
+                        }
+#pragma unroll
+                        for (int i = 0; i < kLgWT; ++i)
+#pragma unroll
+                            for (int j = 0; j < kLgWR; ++j) {
+                                acc[i][j][0] = __fadd_rn(acc[i][j][0], __fmul_rn(wv[cur][j].x, xv[cur][i].x));
+                                acc[i][j][1] = __fadd_rn(acc[i][j][1], __fmul_rn(wv[cur][j].y, xv[cur][i].y));
+                            }
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        bar_arrive(&B.empty[st]);
+                        if (rr == nrt - 1) bar_arrive(&B.xempty[c]);
+                    }
+                }
+                if (!ok) break;
+                // row tile done: the tree and this thread's output
+                u64 v[kLgWT * kLgWR];
+#pragma unroll
+                for (int i = 0; i < kLgWT; ++i)
+#pragma unroll
+                    for (int j = 0; j < kLgWR; ++j) v[i * kLgWR + j] = ((u64)__float_as_uint(acc[i][j][1]) << 32) | __float_as_uint(acc[i][j][0]);
+#pragma unroll
+                for (int half = 16; half > 0; half >>= 1) {
+                    const bool upper = (lane & half) != 0;
+#pragma unroll
+                    for (int o = 0; o < half; ++o) {
+                        const u64 mine = upper ? v[o + half] : v[o];
+                        const u64 theirs = shfl_xor_u64(upper ? v[o] : v[o + half], half);
+                        v[o] = add2_rn(mine, theirs);
+                    }
+                }
+                const float a = __fadd_rn(__uint_as_float((unsigned)v[0]), __uint_as_float((unsigned)(v[0] >> 32)));
+                const int t = t0 + tb + lane / kLgWR, r = (rt0 + rr) * kLgR + rb + lane % kLgWR;
+                if (t < T) {
                     if (r < E) logits[(long long)t * E + r] = L.bias ? __fadd_rn(a, L.bias[r]) : a;
                     else if (r == E) sg[t] = a;
                 }
             }
+        }
     }
+    __syncthreads();
+    if (tid == 0 && B.abort_flag) raise_error(err, kErrWaitTimeout);
 }
+static_assert(kLgWT * kLgWR == 32, "the butterfly leaves one output per thread");
 
 // ------------------------------------------------------------------ routing
 __global__ void __launch_bounds__(128) k_pf_route(const float *logits, int T, int E, int K, int *ids, float *weights) {
@@ -442,6 +535,7 @@ struct PfScratch {
     float *row_scale, *row_weight;
     pf::Chunk *chunks;
     __half *B, *hidden;
+    float *tail;  // router logits: the last row tile's rows
 };
 size_t al(size_t n) { return (n + 255) & ~size_t(255); }
 PfScratch carve(void *base, int T, int H, int F, int E, int K) {
@@ -467,6 +561,7 @@ PfScratch carve(void *base, int T, int H, int F, int E, int K) {
     s.chunks = (pf::Chunk *)take(sizeof(pf::Chunk) * max_chunks);
     s.B = (__half *)take(sizeof(__half) * rows * H);
     s.hidden = (__half *)take(sizeof(__half) * rows * F);
+    s.tail = (float *)take(sizeof(float) * pf::kLgR * H);
     return s;
 }
 
@@ -494,6 +589,35 @@ bool encode(CUtensorMap *m, CUtensorMapDataType dt, int rank, const void *base, 
     }
     return fn(m, dt, rank, const_cast<void *>(base), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Router logits: the tail rows, the tensor maps, one persistent launch (one CTA per SM at most).
+cudaError_t launch_logits(const MoeLayerDev &L, const float *x, int T, float *logits, float *sg, float *tail, int sms, cudaStream_t s,
+                          unsigned *err) {
+    const int H = L.width, E = L.experts;
+    const int n_full = E / pf::kLgR;
+    pf::k_lg_tail<<<pf::kLgR, 256, 0, s>>>(L.router, L.shared_gate, E, H, n_full * pf::kLgR, tail);
+    pf::LgMaps M;
+    const unsigned long long rdims[2] = {(unsigned long long)H, (unsigned long long)std::max(1, E)},
+                             tdims[2] = {(unsigned long long)H, (unsigned long long)pf::kLgR}, xdims[2] = {(unsigned long long)H, (unsigned long long)T};
+    const unsigned long long rstr[1] = {(unsigned long long)H * 4};
+    const unsigned rbox[2] = {pf::kLgKC, pf::kLgR}, xbox[2] = {pf::kLgKC, pf::kLgT};
+    if (!encode(&M.router, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, L.router, rdims, rstr, rbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&M.tail, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, tail, tdims, rstr, rbox, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode(&M.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, x, xdims, rstr, xbox, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
+    static int ready_device = -1;
+    int dev = 0;
+    STRATA_CUDA_TRY(cudaGetDevice(&dev));
+    if (ready_device != dev) {
+        STRATA_CUDA_TRY(cudaFuncSetAttribute(pf::k_pf_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kLgSmemLimit));
+        ready_device = dev;
+    }
+    const int n_rt = n_full + 1, n_grp = (n_rt + pf::kLgGroup - 1) / pf::kLgGroup;
+    const long long n_items = (long long)((T + pf::kLgT - 1) / pf::kLgT) * n_grp;
+    const int grid = (int)std::min<long long>(n_items, std::max(1, sms));
+    pf::k_pf_logits<<<grid, pf::kLgThreads, pf::logits_smem(H), s>>>(M, L, T, pf::logits_stages(H), logits, sg, err, 1ull << 24);
+    return cudaGetLastError();
 }
 
 template <int MODE>
@@ -570,7 +694,7 @@ size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int
     return al(sizeof(float) * tokens * experts) + al(sizeof(float) * tokens) + al(sizeof(int) * (size_t)n_tc * experts) +
            al(sizeof(int) * (experts + 1)) + al(sizeof(int) * (size_t)tokens * topK) + al(sizeof(int) * rows) + al(sizeof(int)) +
            al(sizeof(float) * rows) * 2 + al(sizeof(pf::Chunk) * max_chunks) + al(sizeof(__half) * rows * width) +
-           al(sizeof(__half) * rows * ff);
+           al(sizeof(__half) * rows * ff) + al(sizeof(float) * pf::kLgR * width);
 }
 
 bool moe_prefill_supported(int width, int ff, int experts, int topK) {
@@ -585,15 +709,7 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
     const long long rows = (long long)T * K + T;
     PfScratch S = carve(scratch, T, H, F, E, K);
     const int n_tc = (T + pf::kTokChunk - 1) / pf::kTokChunk;
-    static int logits_ready_device = -1;
-    int dev = 0;
-    STRATA_CUDA_TRY(cudaGetDevice(&dev));
-    if (logits_ready_device != dev) {
-        STRATA_CUDA_TRY(cudaFuncSetAttribute(pf::k_pf_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem));
-        logits_ready_device = dev;
-    }
-    pf::k_pf_logits<<<dim3((T + pf::kLgT - 1) / pf::kLgT, (E + 1 + pf::kLgR - 1) / pf::kLgR), 256, pf::kLgSmem, s>>>(L, x, T, S.logits,
-                                                                                                                   S.sg);
+    STRATA_CUDA_TRY(launch_logits(L, x, T, S.logits, S.sg, S.tail, grid, s, err));
     pf::k_pf_route<<<(T + 3) / 4, 128, 0, s>>>(S.logits, T, E, K, ids, weights);
     pf::k_pf_count<<<n_tc, 256, 0, s>>>(ids, T, E, K, S.chunk_counts);
     pf::k_pf_scan<<<1, 512, 0, s>>>(S.chunk_counts, n_tc, T, T * K, E, S.offsets, S.chunks, S.n_chunks);
@@ -652,7 +768,7 @@ struct EpComm {
         void *p = nullptr;
         size_t cap = 0;
     };
-    Buf bufs[24];
+    Buf bufs[25];
     int *h_off = nullptr;  // pinned: [0, n] send offsets, [n + 1, 2n] receive counts
     ~EpComm() {
         for (Buf &b : bufs)
@@ -756,14 +872,8 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     EP_MARK(0);
     EP_GET(logits, float, 0, (long long)T * E);
     EP_GET(sg, float, 1, T);
-    static int logits_ready_device = -1;
-    int dev = 0;
-    EP_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
-    if (logits_ready_device != dev) {
-        EP_CUDA(cudaFuncSetAttribute(pf::k_pf_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem), "cudaFuncSetAttribute");
-        logits_ready_device = dev;
-    }
-    pf::k_pf_logits<<<dim3((T + pf::kLgT - 1) / pf::kLgT, (E + 1 + pf::kLgR - 1) / pf::kLgR), 256, pf::kLgSmem, s>>>(L, x, T, logits, sg);
+    EP_GET(tail, float, 24, (long long)pf::kLgR * H);
+    EP_CUDA(launch_logits(L, x, T, logits, sg, tail, grid, s, err), "router logits");
     pf::k_pf_route<<<(T + 3) / 4, 128, 0, s>>>(logits, T, E, K, ids, weights);
     // 2. destination buckets, stable positions, packed rows
     EP_GET(dest, int, 2, P);
