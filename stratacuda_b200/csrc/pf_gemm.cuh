@@ -15,7 +15,7 @@
 // list is ordered by decreasing rows, so the deal approximates longest-first. Warp roles:
 //   warp 0      TMA producer of B: per 64-column K-block the B rows (64-row boxes, then
 //               16-row boxes for the rest; 128-byte swizzle)
-//   warp 14     TMA producer of A: per tile the rows' FP16 scales (one bulk copy); per
+//   warp 18     TMA producer of A: per tile the rows' FP16 scales (one bulk copy); per
 //               256-column super-block the packed codes (one 128-row x 64-byte box, 64-byte
 //               swizzle). Its own thread, so the codes run ahead of the dequantisers while the
 //               B producer waits for free stages
@@ -25,8 +25,9 @@
 //   warps 2-9   dequantise: warp w writes TMEM lanes 32 (w % 4) .. (a warp reaches only its
 //               lane quarter): thread = one A row and half of its 64 codes of a K-block, 16
 //               32-bit columns of two FP16 each
-//   warps 10-13 epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32 (w % 4) ..),
-//               gate/up: hidden = silu(gate) * up -> FP16 rows; down: weighted rows added to y
+//   warps 10-17 epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32 (w % 4) ..;
+//               warps 10-13 take the even 32-column chunks, 14-17 the odd ones), gate/up:
+//               hidden = silu(gate) * up -> FP16 rows; down: weighted rows added to y
 // The accumulators are double-buffered, so a tile's epilogue overlaps the next tile's MMAs.
 // Every wait is bounded: past the limit the CTA records kErrWaitTimeout and all roles leave
 // (the producer and the MMA thread first wait, bounded, for their own operations in flight).
@@ -39,11 +40,12 @@
 namespace strata {
 namespace pf {
 
-constexpr int kGemmWarps = 15;
-constexpr int kCodeWarp = 14;   // producer of scales and packed codes
+constexpr int kGemmWarps = 19;
+constexpr int kCodeWarp = 18;   // producer of scales and packed codes
 constexpr int kGemmThreads = kGemmWarps * 32;
 constexpr int kDeqThreads = 256;  // warps 2-9
-constexpr int kEpiWarp0 = 10;     // warps 10-13
+constexpr int kEpiWarp0 = 10;     // warps 10-17
+constexpr int kEpiThreads = 256;
 constexpr int kStages = 5;        // B stages
 constexpr int kAStages = 4;       // dequantised-A stages (TMEM)
 constexpr int kApkStages = 4;     // packed-code super-blocks
@@ -129,13 +131,13 @@ __device__ __forceinline__ void bulk(void *dst, const void *src, unsigned bytes,
                  "r"(bytes), "r"(su32(b))
                  : "memory");
 }
-// AND of `ok` over the 128 epilogue threads (named barrier 1): their exits stay uniform.
+// AND of `ok` over the 256 epilogue threads (named barrier 1): their exits stay uniform.
 __device__ __forceinline__ bool ep_all(bool ok) {
     unsigned r;
     asm volatile(
         "{\n\t.reg .pred pi, po;\n\t"
         "setp.ne.u32 pi, %1, 0;\n\t"
-        "bar.red.and.pred po, 1, 128, pi;\n\t"
+        "bar.red.and.pred po, 1, 256, pi;\n\t"
         "selp.u32 %0, 1, 0, po;\n\t}"
         : "=r"(r)
         : "r"((unsigned)ok)
@@ -231,7 +233,7 @@ __device__ __forceinline__ void dequant16(unsigned w, __half2 s2, unsigned (&out
 struct __align__(1024) GemmSmem {
     unsigned char b[kStages][kMaxN * 128];      // B rows, 128-byte swizzle (1024-aligned)
     unsigned char apk[kApkStages][128 * 64];    // packed codes of a super-block, 64-byte swizzle
-    unsigned char staging[kMaxN * 128];         // epilogue staging: gate/up hidden FP16 [N][64] / down F32 [32][128]
+    unsigned char staging[2 * 32 * 128 * 4];    // epilogue staging: gate/up hidden FP16 [N][64] / down F32 [2 halves][32][128]
     unsigned short scl[2][128 * 40];            // FP16 scales of the tile's 128 rows (<= 40 groups per row)
     float row_f[kMaxN];                         // epilogue: per B row scale (gate/up) or weight (down)
     int row_t[kMaxN];                           // epilogue: per B row token (down)
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
             bar_init(&S.scl_full[s], 1);
             bar_init(&S.scl_empty[s], kDeqThreads);
             bar_init(&S.tmem_full[s], 1);
-            bar_init(&S.tmem_empty[s], 128);
+            bar_init(&S.tmem_empty[s], kEpiThreads);
         }
         bar_init(&S.mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -433,8 +435,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
         }
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int et = tid - 32 * kEpiWarp0;     // 0..127
+        const int et = tid - 32 * kEpiWarp0;     // 0..255
         const int quarter = warp & 3;            // TMEM lanes 32 quarter .. (a warp reaches only its quarter)
+        const int half = (warp - kEpiWarp0) >> 2;  // 32-column chunks half, half + 2, ...
+        const int ht = et & 127;                 // thread within the half
         const int row = 32 * quarter + lane;     // accumulator row = weight row within the tile
         const int HID = P.rows_total / 2;
         int lt = 0;
@@ -447,12 +451,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
             const unsigned tbase = tmem + ((unsigned)(32 * quarter) << 16) + buf * kAccCols;
             const int N = (t.n + 15) & ~15;
             // the tile's B-row metadata, once
-            for (int i = et; i < t.n; i += 128) {
+            for (int i = et; i < t.n; i += kEpiThreads) {
                 S.row_f[i] = MODE == kGateUp ? __ldg(P.row_scale + t.row0 + i) : __ldg(P.row_weight + t.row0 + i);
                 if (MODE == kDown) S.row_t[i] = __ldg(P.row_token + t.row0 + i);
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            for (int c0 = 0; c0 < N; c0 += 32) {
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            for (int c0 = 32 * half; c0 < N; c0 += 64) {
                 float v[32];
                 __syncwarp();
                 tmem_ld32(tbase + c0, v);
@@ -470,12 +474,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
                         }
                     }
                 } else {
-                    // stage [32 columns][128 rows] F32, then coalesced 16-byte reductions into y
-                    float *st = reinterpret_cast<float *>(S.staging);
+                    // stage [32 columns][128 rows] F32 (this half's area), then coalesced 16-byte reductions into y
+                    float *st = reinterpret_cast<float *>(S.staging) + half * 32 * 128;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) st[j * 128 + row] = v[j];
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
-                    for (int i = et; i < 32 * 32; i += 128) {  // 32 columns x 32 float4
+                    asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory");
+                    for (int i = ht; i < 32 * 32; i += 128) {  // 32 columns x 32 float4
                         const int j = i >> 5, q = i & 31, n = c0 + j;
                         if (n < t.n) {
                             const float4 s4 = reinterpret_cast<const float4 *>(st)[j * 32 + q];
@@ -486,22 +490,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_pf_gemm(const __grid_consta
                                          : "memory");
                         }
                     }
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory");
                 }
             }
             // accumulator drained: the MMA warp may reuse it
             tc_fence_before();
             bar_arrive(&S.tmem_empty[buf]);
             if (MODE == kGateUp) {
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                asm volatile("bar.sync 1, 256;" ::: "memory");
                 // hidden rows: t.n x 64 FP16 (128 bytes each) at column 64 mtile
-                for (int i = et; i < t.n * 8; i += 128) {
+                for (int i = et; i < t.n * 8; i += kEpiThreads) {
                     const int n = i >> 3, q = i & 7;
                     const uint4 val = reinterpret_cast<const uint4 *>(S.staging)[n * 8 + q];
                     *reinterpret_cast<uint4 *>(P.hidden + (long long)(t.row0 + n) * HID + 64 * t.mtile + 8 * q) = val;
                 }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");  // staging and row metadata free for the next tile
+            asm volatile("bar.sync 1, 256;" ::: "memory");  // staging and row metadata free for the next tile
         }
     }
 
