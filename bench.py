@@ -22,8 +22,10 @@ fresh activation batch per step, so no step reads weights left in L2 by the prev
           (oracle/_ref, WASM-path host order, 8 threads) on a bounded sample of the same
           workload; falls back to the C restatement when the native build is absent.
 
-Multi-GPU: every rank runs its own replica of the layer stack (the reference has no
-multi-GPU path; see DESIGN.md for the expert-parallel plan); scaling is weak.
+Multi-GPU: by default every rank runs its own replica of the layer stack (the reference has
+no multi-GPU path); scaling is weak. `--ep` runs BASELINE config 4 instead: 16384 tokens
+split over the ranks, the 512 experts sharded, Zipf(1.1) routing, NCCL dispatch and return
+inside the library; scaling is strong.
 """
 from __future__ import annotations
 
@@ -322,6 +324,96 @@ def run_gpu_arm(args, world, rank, local):
     b.dispose()
 
 
+def run_ep_arm(args, world, rank, local):
+    """one expert-parallel layer over the ranks (strata_moe_ep_forward).
+    16384 tokens split evenly over the ranks, the 512 experts sharded (E/N per rank), Zipf(1.1)
+    router bias, NCCL dispatch and return inside the library; strong scaling; device time of
+    the K steps (CUDA events on the library's stream), max over ranks."""
+    import torch
+
+    from stratacuda_b200.backend import CudaBackend
+    from stratacuda_b200.ep import EpMoeLayer, ep_init
+    from stratacuda_b200.moe import synth_activations
+
+    torch.cuda.set_device(local)
+    b = CudaBackend(local)
+    total, K, W, NL = args.ep_tokens, args.steps, args.warmup, args.layers
+    if total % world or EXPERTS % world:
+        raise SystemExit("--ep-tokens and the 512 experts must divide over the ranks")
+    T = total // world
+    zipf = args.zipf if args.zipf is not None else 1.1
+    ep_init(b, rank, world)
+    layers = [EpMoeLayer.synthesize(b, rank, world, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf)
+              for l in range(NL)]
+    n_x = 4
+    xs = [synth_activations(b, 2 + s, T, WIDTH, start_token=rank * T) for s in range(n_x)]
+    ys = [b.alloc(T * WIDTH, zero=False) for _ in range(n_x)]
+    idss = [b.alloc(T * TOPK, "i32") for _ in range(n_x)]
+    wss = [b.alloc(T * TOPK, zero=False) for _ in range(n_x)]
+    b.idle()
+    stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", local))
+    step = lambda s: layers[s % NL].forward(xs[s % n_x], T, ys[s % n_x], idss[s % n_x], wss[s % n_x])
+    for s in range(W):
+        step(s)
+    b.idle()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for s in range(W, W + K):
+            step(s)
+        end.record(stream)
+        b.idle()
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    ms_max = dist_max(start.elapsed_time(end), world)
+    # phase split (second pass, library profile)
+    b.profile(True)
+    for s in range(3):
+        step(s)
+    ph, calls = b.profile_read()
+    b.profile(False)
+    phases = {k: v / max(1, calls) for k, v in ph.items() if k != "decode_kernel"}
+    # end to end through the C-ABI: this rank's tokens from pinned host memory, y back
+    hx = torch.empty(T * WIDTH, dtype=torch.float32, pin_memory=True)
+    hx.copy_(torch.from_numpy(b.read(xs[0])))
+    hy = torch.empty(T * WIDTH, dtype=torch.float32, pin_memory=True)
+    hx_np, hy_np = hx.numpy(), hy.numpy()
+    e2e_steps = min(K, 5)
+    dist_barrier(world)
+    t0 = time.perf_counter()
+    for s in range(e2e_steps):
+        b.write(xs[0], hx_np)
+        layers[s % NL].forward(xs[0], T, ys[0], idss[0], wss[0])
+        b._check(b.lib.strata_read(b.ctx, ys[0].handle, hy_np.ctypes.data, T * WIDTH, 0))
+    e2e_s = dist_max(time.perf_counter() - t0, world)
+    flops = 2.0 * 3 * WIDTH * FF * (total * TOPK + total)  # whole job per step: routed pairs + shared rows
+    step_s = ms_max / 1000.0 / K
+    peak, kind = peak_tflops()
+    achieved = flops / step_s / world / 1e12
+    line = {"metric": METRIC, "value": total * K / (ms_max / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded SplitMix64; BASELINE config 4 distributions)",
+            "config": {"workload": f"expert-parallel MoE layer, {total} tokens over {world} GPU(s), E512 sharded {EXPERTS // world} per GPU, "
+                                   f"top-10, H2048, F512, Q2 experts + shared expert, Zipf({zipf}) router bias",
+                       "tokens": total, "tokens_per_rank": T, "experts_per_rank": EXPERTS // world, "hidden": WIDTH, "ff": FF, "top_k": TOPK,
+                       "layers_cycled": NL, "zipf": zipf, "l2": "inputs larger than L2: distinct layer replicas cycled",
+                       "parallelism": f"ep{world}"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "peak_kind": kind, "kernel": "whole expert-parallel step per GPU (routing, NCCL exchange, tcgen05 GEMMs)",
+                         "algorithmic_flops_per_step": flops, "phase_ms_per_step_rank0": phases},
+            "e2e": {"value": total * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": total * WIDTH * 4,
+                    "d2h_bytes_per_step": total * WIDTH * 4},
+            "gpu_launches": 18 * K,
+            "clocks": clocks.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for L in layers:
+        L.free()
+    b.dispose()
+
+
 def prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K):
     """Second pass with the library's phase profile: the grouped GEMMs' device time against
     their algorithmic FLOPs, 2 * 3 * H * F * (pairs + tokens) per step (gate/up: 2F x H per
@@ -352,7 +444,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--mode", default="fast", choices=["fast", "exact"])
-    ap.add_argument("--zipf", type=float, default=None, help="router bias skew (default: 1.1 for batches above 64)")
+    ap.add_argument("--zipf", type=float, default=None, help="router bias skew (default: 1.1 for batches above 64 and --ep)")
+    ap.add_argument("--ep", action="store_true", help="expert-parallel layer over the ranks (BASELINE config 4)")
+    ap.add_argument("--ep-tokens", type=int, default=16384, help="tokens of the expert-parallel job (split over the ranks)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -363,7 +457,10 @@ def main():
         return
     world, rank, local = dist_setup(args.gpus)
     try:
-        run_gpu_arm(args, world, rank, local)
+        if args.ep:
+            run_ep_arm(args, world, rank, local)
+        else:
+            run_gpu_arm(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist
