@@ -238,7 +238,7 @@ def run_gpu_arm(args, world, rank, local):
     from stratacuda_b200 import _lib as LL
     mode = LL.MOE_FAST if args.mode == "fast" else LL.MOE_EXACT
     prefill = mode == LL.MOE_FAST and B > 8
-    launches = 1 if (mode == LL.MOE_FAST and B <= 8) else (8 if prefill else 6)
+    launches = 1 if (mode == LL.MOE_FAST and B <= 8) else (9 if prefill else 6)
     for s in range(W):
         layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
     b.idle()
