@@ -186,12 +186,14 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(batch: int, layers: int, zipf=None):
+def workload_config(batch: int, layers: int, zipf=None, graph=None):
     kind = "prefill" if batch > 64 else "decode"
     skew = f", Zipf({zipf}) router bias" if zipf else ""
     return {"workload": f"MoE layer {kind} b={batch} (H2048, E512 top-10, F512, Q2 experts + shared expert{skew})", "batch": batch,
             "hidden": WIDTH, "experts": EXPERTS, "top_k": TOPK, "ff": FF, "layers_cycled": layers, "zipf": zipf,
-            "l2": "inputs larger than L2: distinct layer replicas cycled, fresh activations per step", "parallelism": "replicas"}
+            "l2": "inputs larger than L2: distinct layer replicas cycled, fresh activations per step", "parallelism": "replicas",
+            **({} if graph is None else {"timing": "CUDA events around one CUDA-graph replay of the K steps" if graph
+                                         else "CUDA events around K direct launches"})}
 
 
 def peak_tflops():
@@ -242,15 +244,28 @@ def run_gpu_arm(args, world, rank, local):
     for s in range(W):
         layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
     b.idle()
+    # the K timed steps are captured once as a CUDA graph and replayed (the launches are the
+    # same kernels with the same arguments; replay removes the per-call host launch path)
+    graph = None
+    if not args.no_graph:
+        b.capture_begin()
+        for s in range(W, W + K):
+            layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
+        graph = b.capture_end()
     dist_barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         start.record(stream)
-        for s in range(W, W + K):
-            layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
+        if graph is not None:
+            b.graph_launch(graph)
+        else:
+            for s in range(W, W + K):
+                layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
         end.record(stream)
         b.idle()
+    if graph is not None:
+        b.graph_free(graph)
     torch.cuda.synchronize()
     dist_barrier(world)
     ms = start.elapsed_time(end)
@@ -309,7 +324,7 @@ def run_gpu_arm(args, world, rank, local):
     line = {"metric": METRIC, "value": total_tokens / (ms_max / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded SplitMix64; BASELINE config 2 distributions)",
-            "config": workload_config(B, NL, zipf),
+            "config": workload_config(B, NL, zipf, graph=not args.no_graph),
             "roofline": roofline,
             "e2e": {"value": B * e2e_steps * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * WIDTH * 4,
                     "d2h_bytes_per_step": B * WIDTH * 4},
@@ -446,6 +461,7 @@ def main():
     ap.add_argument("--mode", default="fast", choices=["fast", "exact"])
     ap.add_argument("--zipf", type=float, default=None, help="router bias skew (default: 1.1 for batches above 64 and --ep)")
     ap.add_argument("--ep", action="store_true", help="expert-parallel layer over the ranks (BASELINE config 4)")
+    ap.add_argument("--no-graph", action="store_true", help="time direct launches instead of a CUDA graph replay of the K steps")
     ap.add_argument("--ep-tokens", type=int, default=16384, help="tokens of the expert-parallel job (split over the ranks)")
     args = ap.parse_args()
     if args.warmup < 3:

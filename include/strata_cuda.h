@@ -174,6 +174,20 @@ int strata_ep_init(strata_ctx *ctx, int32_t rank, int32_t n_ranks, const uint8_t
 int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                           strata_buf weights);
 
+/* ---- CUDA graphs of the context's stream (no reference counterpart: the B200 runtime replays
+ * captured work instead of relaunching it from the host) ----
+ * strata_capture_begin starts capturing the context's stream (thread-local mode): the calls
+ * that follow on this thread are recorded, not run. Calls that synchronise (read, idle, free)
+ * or that would grow the layer workspace fail while capturing, so run a layer once before
+ * capturing it. strata_capture_end instantiates the recorded work and returns a graph handle;
+ * strata_graph_launch replays it on the stream (stream-ordered, asynchronous);
+ * strata_graph_free synchronises and releases it. The graph keeps the buffers it was captured
+ * with: free a graph before freeing its buffers. */
+int strata_capture_begin(strata_ctx *ctx);
+int strata_capture_end(strata_ctx *ctx, uint64_t *graph);
+int strata_graph_launch(strata_ctx *ctx, uint64_t graph);
+int strata_graph_free(strata_ctx *ctx, uint64_t graph);
+
 /* ---- device-time profile of the fused layer (diagnostics; no reference counterpart) ----
  * While enabled, strata_moe_forward records CUDA events around its phases on the context's
  * stream. strata_profile_read synchronises, adds the phase times (milliseconds) of every call

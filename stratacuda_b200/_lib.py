@@ -53,6 +53,10 @@ SIGNATURES = {
     "strata_flush": ([_vp], _i),
     "strata_info": ([_vp, C.c_char_p, _sz], _i),
     "strata_profile": ([_vp, C.c_int32], _i),
+    "strata_capture_begin": ([_vp], _i),
+    "strata_capture_end": ([_vp, C.POINTER(C.c_uint64)], _i),
+    "strata_graph_launch": ([_vp, _u64], _i),
+    "strata_graph_free": ([_vp, _u64], _i),
     "strata_ep_unique_id": ([_vp, C.c_char_p, _sz], _i),
     "strata_ep_init": ([_vp, C.c_int32, C.c_int32, C.c_char_p], _i),
     "strata_moe_ep_forward": ([_vp, C.POINTER(StrataMoeLayer), _u64, C.c_int32, _u64, _u64, _u64], _i),

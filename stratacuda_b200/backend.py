@@ -166,6 +166,23 @@ class CudaBackend:
         self._check(self.lib.strata_profile_read(self.ctx, ms, len(self.PHASES), C.byref(calls)))
         return dict(zip(self.PHASES, list(ms))), int(calls.value)
 
+    def capture_begin(self) -> None:
+        """Record the calls that follow on this thread into a CUDA graph (strata_capture_begin)."""
+        self._check(self.lib.strata_capture_begin(self.ctx))
+
+    def capture_end(self) -> int:
+        """Instantiate the recorded calls; returns the graph handle (strata_capture_end)."""
+        h = C.c_uint64(0)
+        self._check(self.lib.strata_capture_end(self.ctx, C.byref(h)))
+        return int(h.value)
+
+    def graph_launch(self, graph: int) -> None:
+        """Replay a captured graph on the context's stream (strata_graph_launch)."""
+        self._check(self.lib.strata_graph_launch(self.ctx, int(graph)))
+
+    def graph_free(self, graph: int) -> None:
+        self._check(self.lib.strata_graph_free(self.ctx, int(graph)))
+
     @property
     def stream_handle(self) -> int:
         s = C.c_void_p()

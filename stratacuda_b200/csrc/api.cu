@@ -45,6 +45,14 @@ struct strata_ctx {
     std::vector<cudaEvent_t> spare_events;
     uint64_t profiled_calls = 0;
     EpComm *ep = nullptr;  // strata_ep_init
+    // strata_capture_*: the stream is being captured; instantiated graphs by handle
+    bool capturing = false;
+    struct Graph {
+        cudaGraph_t g;
+        cudaGraphExec_t exec;
+    };
+    std::unordered_map<uint64_t, Graph> graphs;
+    uint64_t next_graph = 1;
     std::string last_error;
     char device_name[256] = {0};
     int sms = 0;
@@ -96,6 +104,7 @@ int check_device_errors(strata_ctx *ctx) {
 }
 
 int sync(strata_ctx *ctx) {
+    if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "synchronising calls are not allowed while the stream is captured");
     CUDA_OR_FAIL(ctx, cudaMemcpyAsync(ctx->err_host, ctx->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx->stream),
                  "error word readback");
     CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
@@ -234,6 +243,11 @@ int strata_destroy(strata_ctx *ctx) {
     ctx->spare_events.erase(std::unique(ctx->spare_events.begin(), ctx->spare_events.end()), ctx->spare_events.end());
     for (cudaEvent_t e : ctx->spare_events) cudaEventDestroy(e);
     if (ctx->ep) ep_destroy(ctx->ep);
+    for (auto &kv : ctx->graphs) {
+        cudaGraphExecDestroy(kv.second.exec);
+        cudaGraphDestroy(kv.second.g);
+    }
+    ctx->graphs.clear();
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->fast_sync) cudaFree(ctx->fast_sync);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
@@ -278,6 +292,7 @@ int strata_free(strata_ctx *ctx, strata_buf buf) {
     if (!ctx) return STRATA_ERR_RANGE;
     Buffer *b = find(ctx, buf);
     if (!b) return STRATA_OK;  // src/backend.js:115 ignores unknown buffers
+    if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "buffers cannot be freed while the stream is captured");
     if (int r = use_device(ctx)) return r;
     cudaStreamSynchronize(ctx->stream);  // work that still reads the buffer completes first
     cudaFree(b->ptr);
@@ -293,6 +308,7 @@ int strata_write(strata_ctx *ctx, strata_buf buf, const void *data, uint64_t cou
     if (offset + count > b->length || offset + count < offset) return fail(ctx, STRATA_ERR_LAYOUT, "Invalid write: exceeds buffer");
     if (!count) return STRATA_OK;
     if (!data) return fail(ctx, STRATA_ERR_RANGE, "Invalid write: null data");
+    if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "host writes are not allowed while the stream is captured");
     if (int r = use_device(ctx)) return r;
     // Pageable memory is staged before this returns; page-locked memory is read later by the
     // stream and must stay unchanged until the next synchronising call.
@@ -306,6 +322,7 @@ int strata_read(strata_ctx *ctx, strata_buf buf, void *out, uint64_t count, uint
     Buffer *b = find(ctx, buf);
     if (!b) return fail(ctx, STRATA_ERR_HANDLE, "Invalid read: unknown buffer");
     if (offset + count > b->length || offset + count < offset) return fail(ctx, STRATA_ERR_LAYOUT, "Invalid read: exceeds buffer");
+    if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "reads are not allowed while the stream is captured");
     if (int r = use_device(ctx)) return r;
     if (count) {
         if (!out) return fail(ctx, STRATA_ERR_RANGE, "Invalid read: null destination");
@@ -408,6 +425,57 @@ int strata_info(strata_ctx *ctx, char *json, size_t cap) {
                      ctx->workspace_bytes, (unsigned long long)ctx->dispatches, (unsigned long long)ctx->fused_calls, moe_fast_pdl_state());
     if (json && cap) snprintf(json, cap, "%s", buf);
     return n;
+}
+
+int strata_capture_begin(strata_ctx *ctx) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "the stream is already being captured");
+    if (int r = use_device(ctx)) return r;
+    CUDA_OR_FAIL(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    ctx->capturing = true;
+    return STRATA_OK;
+}
+
+int strata_capture_end(strata_ctx *ctx, uint64_t *graph) {
+    if (!ctx || !graph) return STRATA_ERR_RANGE;
+    if (!ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "the stream is not being captured");
+    if (int r = use_device(ctx)) return r;
+    ctx->capturing = false;
+    cudaGraph_t g = nullptr;
+    CUDA_OR_FAIL(ctx, cudaStreamEndCapture(ctx->stream, &g), "cudaStreamEndCapture");
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+    if (e == cudaSuccess) e = cudaGraphUpload(exec, ctx->stream);  // the first replay needs no upload
+    if (e != cudaSuccess) {
+        if (exec) cudaGraphExecDestroy(exec);
+        cudaGraphDestroy(g);
+        return cuda_fail(ctx, e, "cudaGraphInstantiate");
+    }
+    const uint64_t h = ctx->next_graph++;
+    ctx->graphs[h] = {g, exec};
+    *graph = h;
+    return STRATA_OK;
+}
+
+int strata_graph_launch(strata_ctx *ctx, uint64_t graph) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    auto it = ctx->graphs.find(graph);
+    if (it == ctx->graphs.end()) return fail(ctx, STRATA_ERR_HANDLE, "graph %llu is not live", (unsigned long long)graph);
+    if (int r = use_device(ctx)) return r;
+    CUDA_OR_FAIL(ctx, cudaGraphLaunch(it->second.exec, ctx->stream), "cudaGraphLaunch");
+    return STRATA_OK;
+}
+
+int strata_graph_free(strata_ctx *ctx, uint64_t graph) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    auto it = ctx->graphs.find(graph);
+    if (it == ctx->graphs.end()) return fail(ctx, STRATA_ERR_HANDLE, "graph %llu is not live", (unsigned long long)graph);
+    if (int r = use_device(ctx)) return r;
+    CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    cudaGraphExecDestroy(it->second.exec);
+    cudaGraphDestroy(it->second.g);
+    ctx->graphs.erase(it);
+    return STRATA_OK;
 }
 
 int strata_profile(strata_ctx *ctx, int32_t enable) {
@@ -577,6 +645,8 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
                       : prefill ? moe_prefill_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
                                 : moe_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k);
     if (ws > ctx->workspace_bytes) {
+        if (ctx->capturing)
+            return fail(ctx, STRATA_ERR_RANGE, "the layer's workspace must be sized before capture: run the call once first");
         CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "workspace resize");
         if (ctx->workspace) cudaFree(ctx->workspace);
         ctx->workspace = nullptr;

@@ -20,10 +20,11 @@
 //
 // Phase 0 (from entry): x is staged in shared memory; router logits, row r of the 512 (+1
 // shared-gate row) on CTA r % G, warp r / G, in the reference's exact order
-// (kernels/strata.cu:156-165) so that the routing below is bit-identical; the remaining
-// warps turn x into integer tensor-core operands; y is zeroed. CTAs that own a shared-expert
-// unit start its copies at entry and compute its gate/up part before waiting at the arrival.
-// y is not touched before the final sum, so it needs no zeroing.
+// (kernels/strata.cu:156-165) so that the routing below is bit-identical. A CTA arrives as
+// soon as its rows are written; the remaining warps turn x into integer tensor-core operands
+// while the grid gathers. CTAs that own a shared-expert unit start its copies at entry and
+// compute its gate/up part before waiting at the arrival. y is not touched before the final
+// sum, so it needs no zeroing.
 // Phase 1 (after the arrival: all logits written): every CTA routes all tokens redundantly
 // (route.cuh route_group: up to 8 warps per token) and builds the expert slots, then runs
 // its units.
@@ -67,6 +68,7 @@ constexpr int kMaxTokens = 8;
 constexpr int kMaxPairs = kMaxTokens * 32;
 constexpr int kMaxSlots = kMaxPairs + 1;
 constexpr int kXBuildBarrier = 9;  // named barrier of the x-operand warps (route groups use 1..8)
+constexpr int kRowsBarrier = 10;   // named barrier of the router-row warps (before the first arrival)
 
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ void mbar_init(unsigned long long *bar, unsigned count) {
@@ -384,6 +386,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
                 }
             }
         }
+        // the CTA's rows are written: arrive now (routing needs only the logits); the x
+        // operands below are built while the grid gathers
+        named_sync(kRowsBarrier, 32 * RWARPS);
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(&P.sync[0], 1u);
+        }
     }
     const int xw0 = RWARPS < kWarps ? RWARPS : 0;  // first x-operand warp (all warps, after their rows, if none is free)
     if (warp >= xw0) {
@@ -422,11 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
             block_frags(v, &S.xf[(((grp * 2 + 0) * kMaxTokens + t) * 4 + qq) * 3], &S.xf[(((grp * 2 + 1) * kMaxTokens + t) * 4 + qq) * 3]);
         }
     }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        atomicAdd(&P.sync[0], 1u);
-    }
+    __syncthreads();  // the x operands are complete
 
     // ------------------------------------------------------------------ unit arithmetic
     // Column tokens of the current unit: token slot ts -> token index.
