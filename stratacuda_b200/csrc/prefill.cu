@@ -419,18 +419,32 @@ __global__ void __launch_bounds__(256) k_pf_xprep(const float *__restrict__ x, i
 }
 
 // ------------------------------------------------------------------ expert parallel
-// Destination rank of each (token, k) pair: experts are sharded evenly, rank r owns
-// [r El, (r + 1) El); ids outside [0, E) get -1 (no slot).
-__global__ void k_ep_dest(const int *ids, long long n, int E, int El, int *dest) {
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) dest[i] = ids[i] >= 0 && ids[i] < E ? ids[i] / El : -1;
+// Rows are deduplicated per (token, destination rank): a token whose experts sit on a rank is
+// sent there once, with the list of its pairs on that rank; the rank runs every pair and sums
+// the weighted results per received row (pre-combine), so one row per (token, rank) comes back.
+// Row metadata, kEpMetaFixed + 2 K ints: source token, pair count, 2^-k bits, 0, then per pair
+// (local expert, weight bits); unused pair slots hold local expert -1.
+constexpr int kEpMetaFixed = 4;
+__host__ __device__ inline int ep_meta_ints(int K) { return kEpMetaFixed + 2 * K; }
+
+// dst[t n + p] = p when token t has an expert on rank p (experts sharded evenly: rank p owns
+// [p El, (p + 1) El)), else -1. n <= 32.
+__global__ void k_ep_dest_rows(const int *ids, int T, int K, int E, int El, int n, int *dst) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    unsigned mask = 0u;
+    for (int kk = 0; kk < K; ++kk) {
+        const int e = ids[(long long)t * K + kk];
+        if (e >= 0 && e < E) mask |= 1u << (e / El);
+    }
+    for (int p = 0; p < n; ++p) dst[(long long)t * n + p] = (mask >> p) & 1u ? p : -1;
 }
 
-// One block per token: the token's FP16 row (times 2^k) at each of its pairs' send positions,
-// with the pair's metadata {local expert, token, weight bits, 2^-k bits}.
+// One block per token: the token's FP16 row (times 2^k, largest |x| < 2^15) at each of its
+// send rows, and each row's metadata (the token's pairs on that rank, in k order).
 __global__ void __launch_bounds__(256) k_ep_pack(const float *__restrict__ x, int H, int K, const int *ids, const float *weights, int El,
-                                                 const int *pos, __half *send_rows, int4 *send_meta) {
-    const int t = blockIdx.x, tid = threadIdx.x, nch = H / 8;
+                                                 int n, const int *pos, __half *send_rows, int *send_meta) {
+    const int t = blockIdx.x, tid = threadIdx.x, nch = H / 8, MS = ep_meta_ints(K);
     __shared__ float red[8];
     float4 v[2][2];
     float mx = 0.0f;
@@ -465,15 +479,33 @@ __global__ void __launch_bounds__(256) k_ep_pack(const float *__restrict__ x, in
         h[u] = make_uint4(*reinterpret_cast<const unsigned *>(&a), *reinterpret_cast<const unsigned *>(&b),
                           *reinterpret_cast<const unsigned *>(&c), *reinterpret_cast<const unsigned *>(&d));
     }
-    for (int kk = 0; kk < K; ++kk) {
-        const int p = pos[(long long)t * K + kk];
-        if (p < 0) continue;
-        uint4 *dst = reinterpret_cast<uint4 *>(send_rows + (long long)p * H);
+    for (int p = 0; p < n; ++p) {
+        const int row = pos[(long long)t * n + p];
+        if (row < 0) continue;
+        uint4 *dst = reinterpret_cast<uint4 *>(send_rows + (long long)row * H);
 #pragma unroll
         for (int u = 0; u < 2; ++u)
             if (tid + 256 * u < nch) dst[tid + 256 * u] = h[u];
-        if (tid == 0)
-            send_meta[p] = make_int4(ids[(long long)t * K + kk] % El, t, __float_as_int(weights[(long long)t * K + kk]), __float_as_int(inv));
+        if (tid == 0) {
+            int *m = send_meta + (long long)row * MS;
+            int np = 0;
+            for (int kk = 0; kk < K; ++kk) {
+                const int e = ids[(long long)t * K + kk];
+                if (e >= 0 && e / El == p) {
+                    m[kEpMetaFixed + 2 * np] = e % El;
+                    m[kEpMetaFixed + 2 * np + 1] = __float_as_int(weights[(long long)t * K + kk]);
+                    ++np;
+                }
+            }
+            for (int j = np; j < K; ++j) {
+                m[kEpMetaFixed + 2 * j] = -1;
+                m[kEpMetaFixed + 2 * j + 1] = 0;
+            }
+            m[0] = t;
+            m[1] = np;
+            m[2] = __float_as_int(inv);
+            m[3] = 0;
+        }
     }
 }
 
@@ -483,38 +515,44 @@ __global__ void k_ep_send_counts(const int *off, int n, int *cnt) {
     if (p < n) cnt[p] = off[p + 1] - off[p];
 }
 
-__global__ void k_ep_local_expert(const int4 *meta, int R, int *lid) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < R) lid[i] = meta[i].x;
+// Local expert of every pair slot of the received rows: lid[i K + j] (-1 for an unused slot).
+__global__ void k_ep_pair_experts(const int *meta, int R, int K, int *lid) {
+    const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= (long long)R * K) return;
+    const long long i = q / K;
+    lid[q] = meta[i * ep_meta_ints(K) + kEpMetaFixed + 2 * (q - i * K)];
 }
 
-// One warp per received row: its FP16 row at its position among the local experts' B rows;
-// the GEMMs' output row for it is its receive index i (sent back in that order).
-__global__ void k_ep_gather(const __half *recv_rows, const int4 *meta, int R, int H, const int *rpos, __half *B, float *row_scale,
+// One warp per received row: its FP16 row at each of its pairs' positions among the local
+// experts' B rows; every pair's GEMM output is added into row i of the result (pre-combine).
+__global__ void k_ep_gather(const __half *recv_rows, const int *meta, int R, int K, int H, const int *rpos, __half *B, float *row_scale,
                             int *row_token, float *row_weight) {
     const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (i >= R) return;
-    const int p = rpos[i];
+    const int *m = meta + (long long)i * ep_meta_ints(K);
     const uint4 *src = reinterpret_cast<const uint4 *>(recv_rows + (long long)i * H);
-    uint4 *dst = reinterpret_cast<uint4 *>(B + (long long)p * H);
-    for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
-    if (lane == 0) {
-        const int4 m = meta[i];
-        row_scale[p] = __int_as_float(m.w);
-        row_weight[p] = __int_as_float(m.z);
-        row_token[p] = i;
+    for (int j = 0; j < K; ++j) {
+        const int p = rpos[(long long)i * K + j];
+        if (p < 0) continue;
+        uint4 *dst = reinterpret_cast<uint4 *>(B + (long long)p * H);
+        for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+        if (lane == 0) {
+            row_scale[p] = __int_as_float(m[2]);
+            row_weight[p] = __int_as_float(m[kEpMetaFixed + 2 * j + 1]);
+            row_token[p] = i;
+        }
     }
 }
 
-// y[t] = shared row + the token's returned pair rows in k order (pairs without an expert skip).
-__global__ void k_ep_combine(const float *ret, const int *pos, int K, int H, const float *shared, float *y) {
+// y[t] = shared row + the token's returned rows in rank order.
+__global__ void k_ep_combine(const float *ret, const int *pos, int n, int H, const float *shared, float *y) {
     const int t = blockIdx.x;
     for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
         float4 a = reinterpret_cast<const float4 *>(shared + (long long)t * H)[c];
-        for (int kk = 0; kk < K; ++kk) {
-            const int p = pos[(long long)t * K + kk];
-            if (p < 0) continue;
-            const float4 b = reinterpret_cast<const float4 *>(ret + (long long)p * H)[c];
+        for (int p = 0; p < n; ++p) {
+            const int row = pos[(long long)t * n + p];
+            if (row < 0) continue;
+            const float4 b = reinterpret_cast<const float4 *>(ret + (long long)row * H)[c];
             a.x += b.x;
             a.y += b.y;
             a.z += b.z;
@@ -830,13 +868,15 @@ int ep_ranks(const EpComm *c) { return c->n; }
 
 // One layer over the ranks of `c`: this rank's T tokens in, its y out; L.blobs holds this
 // rank's experts [rank El, (rank + 1) El), El = L.experts / n (L.experts is the layer's total).
-// Stages: exact routing; pairs bucketed by destination rank (stable) and packed as FP16 rows
-// with {local expert, token, weight, 2^-k}; counts, then rows, exchanged by grouped
-// ncclSend/ncclRecv; the received rows regrouped by local expert and run through the tensor-
-// core GEMMs together with this rank's shared-expert rows; outputs sent back; y[t] = shared
-// row + the token's returned rows in k order. The receive sizes are read back on the host
-// (as the reference reads its routing back, src/engine.js:137). marks (nullable): six events at
-// start, after packing, before the GEMMs, after gate/up, after down, after the combine.
+// Stages: exact routing; one row per (token, destination rank) bucketed by rank (stable,
+// token-major), packed as an FP16 row with its pair list {local expert, weight} and 2^-k;
+// counts, then rows, exchanged by grouped ncclSend/ncclRecv; the received rows' pairs grouped
+// by local expert and run through the tensor-core GEMMs together with this rank's shared-
+// expert rows, the down GEMM adding each pair's weighted result into its received row (pre-
+// combine); one row per received row sent back; y[t] = shared row + the token's returned rows
+// in rank order. The receive sizes are read back on the host (as the reference reads its
+// routing back, src/engine.js:137). marks (nullable): six events at start, after packing,
+// before the GEMMs, after gate/up, after down, after the combine.
 int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float *y, int *ids, float *weights, int grid, cudaStream_t s,
                    unsigned *err, std::string *msg, cudaEvent_t *marks) {
     const int H = L.width, F = L.ff, E = L.experts, K = L.topK, n = c->n, El = E / n;
@@ -862,7 +902,6 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
 #define EP_GET(ptr, type, i, count)                                                   \
     type *ptr = static_cast<type *>(c->get(i, sizeof(type) * (size_t)(count) + 16, e)); \
     if (!ptr) return fail_cuda(e, "cudaMalloc");
-    const long long P = (long long)T * K;
     const int n_tc = (T + pf::kTokChunk - 1) / pf::kTokChunk;
 #define EP_MARK(i)                                                                   \
     do {                                                                             \
@@ -875,20 +914,27 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     EP_GET(tail, float, 24, (long long)pf::kLgR * H);
     EP_CUDA(launch_logits(L, x, T, logits, sg, tail, grid, s, err), "router logits");
     pf::k_pf_route<<<(T + 3) / 4, 128, 0, s>>>(logits, T, E, K, ids, weights);
-    // 2. destination buckets, stable positions, packed rows
-    EP_GET(dest, int, 2, P);
-    EP_GET(cc, int, 3, (long long)n_tc * max(n, 1));
+    // 2. one row per (token, destination rank): buckets by rank (stable, token-major), packed
+    //    FP16 rows and their pair lists
+    if (n > 32) {
+        *msg = "expert parallelism supports at most 32 ranks";
+        return 2;
+    }
+    const long long TN = (long long)T * n;
+    const int MS = pf::ep_meta_ints(K);
+    EP_GET(dest, int, 2, TN);
+    EP_GET(cc, int, 3, (long long)n_tc * n);
     EP_GET(off, int, 4, n + 1);
-    EP_GET(pos, int, 5, P);
-    EP_GET(dchunks, pf::Chunk, 6, P / pf::kMaxN + n + 2);
+    EP_GET(pos, int, 5, TN);
+    EP_GET(dchunks, pf::Chunk, 6, TN / pf::kMaxN + n + 2);
     EP_GET(dn, int, 7, 1);
-    pf::k_ep_dest<<<(unsigned)((P + 255) / 256), 256, 0, s>>>(ids, P, E, El, dest);
-    pf::k_pf_count<<<n_tc, 256, 0, s>>>(dest, T, n, K, cc);
+    pf::k_ep_dest_rows<<<(T + 255) / 256, 256, 0, s>>>(ids, T, K, E, El, n, dest);
+    pf::k_pf_count<<<n_tc, 256, 0, s>>>(dest, T, n, n, cc);
     pf::k_pf_scan<<<1, 512, 0, s>>>(cc, n_tc, 0, 0, n, off, dchunks, dn);
-    pf::k_pf_place<<<n_tc, 256, 0, s>>>(dest, T, n, K, cc, off, pos);
-    EP_GET(send_rows, __half, 8, P * H);
-    EP_GET(send_meta, int4, 9, P);
-    pf::k_ep_pack<<<T, 256, 0, s>>>(x, H, K, ids, weights, El, pos, send_rows, send_meta);
+    pf::k_pf_place<<<n_tc, 256, 0, s>>>(dest, T, n, n, cc, off, pos);
+    EP_GET(send_rows, __half, 8, TN * H);
+    EP_GET(send_meta, int, 9, TN * MS);
+    pf::k_ep_pack<<<T, 256, 0, s>>>(x, H, K, ids, weights, El, n, pos, send_rows, send_meta);
     EP_MARK(1);
     // 3. counts exchange; one host read of the send offsets and the receive counts
     EP_GET(d_cnt, int, 10, 2 * n);
@@ -914,47 +960,49 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     const int R = roff[n];
     // 4. rows exchange
     EP_GET(recv_rows, __half, 11, (long long)max(R, 1) * H);
-    EP_GET(recv_meta, int4, 12, max(R, 1));
+    EP_GET(recv_meta, int, 12, (long long)max(R, 1) * MS);
     EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
     for (int p = 0; p < n; ++p) {
         if (sc[p]) {
             EP_NCCL(nccl().Send(send_rows + (long long)soff[p] * H, (size_t)sc[p] * H, ncclFloat16, p, c->comm, s), "ncclSend");
-            EP_NCCL(nccl().Send(send_meta + soff[p], (size_t)sc[p] * 4, ncclInt32, p, c->comm, s), "ncclSend");
+            EP_NCCL(nccl().Send(send_meta + (long long)soff[p] * MS, (size_t)sc[p] * MS, ncclInt32, p, c->comm, s), "ncclSend");
         }
         if (rc[p]) {
             EP_NCCL(nccl().Recv(recv_rows + (long long)roff[p] * H, (size_t)rc[p] * H, ncclFloat16, p, c->comm, s), "ncclRecv");
-            EP_NCCL(nccl().Recv(recv_meta + roff[p], (size_t)rc[p] * 4, ncclInt32, p, c->comm, s), "ncclRecv");
+            EP_NCCL(nccl().Recv(recv_meta + (long long)roff[p] * MS, (size_t)rc[p] * MS, ncclInt32, p, c->comm, s), "ncclRecv");
         }
     }
     EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
-    // 5. local experts + shared expert on the tensor cores
-    const long long brows = (long long)R + T;
+    // 5. the received rows' pairs grouped by local expert (pair slot i K + j of row i), this
+    //    rank's shared-expert rows after them; the GEMMs add every pair of received row i into
+    //    Y[i] (pre-combine) and token t's shared expert into Y[R + t]
+    const long long QK = (long long)R * K, brows = QK + T;
     const int n_tc2 = max(1, (R + pf::kTokChunk - 1) / pf::kTokChunk);
     const int max_chunks = El + (int)(brows / pf::kMaxN) + 4;
-    EP_GET(lid, int, 13, max(R, 1));
+    EP_GET(lid, int, 13, max(QK, 1LL));
     EP_GET(cc2, int, 14, (long long)n_tc2 * El);
     EP_GET(off2, int, 15, El + 1);
-    EP_GET(rpos, int, 16, max(R, 1));
+    EP_GET(rpos, int, 16, max(QK, 1LL));
     EP_GET(chunks, pf::Chunk, 17, max_chunks);
     EP_GET(nchunks, int, 18, 1);
     EP_GET(B, __half, 19, brows * H);
     EP_GET(hidden, __half, 20, brows * F);
-    EP_GET(rmeta, float, 21, 3 * brows);  // row scale, token (as int), weight
-    EP_GET(Y, float, 22, brows * H);
-    EP_GET(ret, float, 23, max(P, 1LL) * H);
+    EP_GET(rmeta, float, 21, 3 * brows);  // row scale, Y row (as int), weight
+    EP_GET(Y, float, 22, ((long long)R + T) * H);
+    EP_GET(ret, float, 23, max(TN, 1LL) * H);
     float *row_scale = rmeta, *row_weight = rmeta + 2 * brows;
     int *row_token = reinterpret_cast<int *>(rmeta + brows);
     if (R > 0) {
-        pf::k_ep_local_expert<<<(R + 255) / 256, 256, 0, s>>>(recv_meta, R, lid);
-        pf::k_pf_count<<<n_tc2, 256, 0, s>>>(lid, R, El, 1, cc2);
+        pf::k_ep_pair_experts<<<(unsigned)((QK + 255) / 256), 256, 0, s>>>(recv_meta, R, K, lid);
+        pf::k_pf_count<<<n_tc2, 256, 0, s>>>(lid, R, El, K, cc2);
     }
-    pf::k_pf_scan<<<1, 512, 0, s>>>(cc2, R > 0 ? n_tc2 : 0, T, R, El, off2, chunks, nchunks);
+    pf::k_pf_scan<<<1, 512, 0, s>>>(cc2, R > 0 ? n_tc2 : 0, T, (int)QK, El, off2, chunks, nchunks);
     if (R > 0) {
-        pf::k_pf_place<<<n_tc2, 256, 0, s>>>(lid, R, El, 1, cc2, off2, rpos);
-        pf::k_ep_gather<<<(R + 7) / 8, 256, 0, s>>>(recv_rows, recv_meta, R, H, rpos, B, row_scale, row_token, row_weight);
+        pf::k_pf_place<<<n_tc2, 256, 0, s>>>(lid, R, El, K, cc2, off2, rpos);
+        pf::k_ep_gather<<<(R + 7) / 8, 256, 0, s>>>(recv_rows, recv_meta, R, K, H, rpos, B, row_scale, row_token, row_weight);
     }
-    pf::k_pf_xprep<<<T, 256, 0, s>>>(x, T, H, 0, nullptr, weights, sg, R, R, B, row_scale, row_token, row_weight);
-    EP_CUDA(cudaMemsetAsync(Y, 0, sizeof(float) * brows * H, s), "cudaMemsetAsync");
+    pf::k_pf_xprep<<<T, 256, 0, s>>>(x, T, H, 0, nullptr, weights, sg, (int)QK, R, B, row_scale, row_token, row_weight);
+    EP_CUDA(cudaMemsetAsync(Y, 0, sizeof(float) * ((long long)R + T) * H, s), "cudaMemsetAsync");
     EP_CUDA(cudaGetLastError(), "expert grouping kernels");
     MoeLayerDev Ll = L;
     Ll.experts = El;
@@ -962,15 +1010,15 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     EP_CUDA(launch_moe_gemms(Ll, El, chunks, nchunks, brows, B, hidden, row_scale, row_token, row_weight, Y, grid, s, err,
                              marks ? marks + 3 : nullptr),
             "expert GEMMs");
-    // 6. outputs back to their tokens' ranks
+    // 6. one pre-combined row per received row back to its token's rank
     EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
     for (int p = 0; p < n; ++p) {
         if (rc[p]) EP_NCCL(nccl().Send(Y + (long long)roff[p] * H, (size_t)rc[p] * H, ncclFloat32, p, c->comm, s), "ncclSend");
         if (sc[p]) EP_NCCL(nccl().Recv(ret + (long long)soff[p] * H, (size_t)sc[p] * H, ncclFloat32, p, c->comm, s), "ncclRecv");
     }
     EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
-    // 7. combine
-    pf::k_ep_combine<<<T, 128, 0, s>>>(ret, pos, K, H, Y + (long long)R * H, y);
+    // 7. combine: shared row + the returned rows in rank order
+    pf::k_ep_combine<<<T, 128, 0, s>>>(ret, pos, n, H, Y + (long long)R * H, y);
     EP_CUDA(cudaGetLastError(), "combine");
     EP_MARK(5);
 #undef EP_MARK

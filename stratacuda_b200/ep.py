@@ -93,18 +93,28 @@ class EpMoeLayer:
 
 def plan_dispatch(ids: np.ndarray, experts: int, n_ranks: int):
     """Host restatement of the dispatch plan the library computes on the device (used by the
-    CPU tests): pairs (t, k) bucketed by destination rank e // (E/n), token-major inside each
-    bucket. Returns (position of every pair in the send order or -1, per-rank counts)."""
+    CPU tests). One row per (token, destination rank) that owns at least one of the token's
+    experts (rank r owns [r E/n, (r + 1) E/n)), bucketed by rank, token-major inside a bucket.
+    Returns (row of every (token, rank) in the send order or -1 [T, n], rows per rank [n],
+    pairs: for every send row the token's (k, expert) pairs on that rank in k order)."""
     el = experts // n_ranks
     T, K = ids.shape
-    flat = ids.reshape(-1)
-    dest = np.where((flat >= 0) & (flat < experts), flat // el, -1)
-    counts = np.array([(dest == r).sum() for r in range(n_ranks)], np.int64)
+    owner = np.where((ids >= 0) & (ids < experts), ids // el, -1)
+    has = np.zeros((T, n_ranks), bool)
+    for t in range(T):
+        for k in range(K):
+            if owner[t, k] >= 0:
+                has[t, owner[t, k]] = True
+    counts = has.sum(axis=0).astype(np.int64)
     offsets = np.concatenate([[0], np.cumsum(counts)])
-    pos = np.full(flat.shape, -1, np.int64)
+    pos = np.full((T, n_ranks), -1, np.int64)
+    pairs = [None] * int(counts.sum())
     seen = np.zeros(n_ranks, np.int64)
-    for p, d in enumerate(dest):
-        if d >= 0:
-            pos[p] = offsets[d] + seen[d]
-            seen[d] += 1
-    return pos.reshape(T, K), counts
+    for t in range(T):
+        for p in range(n_ranks):
+            if has[t, p]:
+                row = offsets[p] + seen[p]
+                seen[p] += 1
+                pos[t, p] = row
+                pairs[row] = [(k, int(ids[t, k])) for k in range(K) if owner[t, k] == p]
+    return pos, counts, pairs

@@ -1,9 +1,10 @@
 """Expert-parallel dispatch/combine protocol on CPU ranks (gloo, world size 2): the host
-restatement of the plan the library runs on the device (stratacuda_b200.ep.plan_dispatch:
-pairs bucketed by destination rank, token-major inside a bucket), exchanged with variable
-all-to-alls, a stand-in expert applied on the owning rank, results returned and combined.
-Every pair must reach the rank that owns its expert and every token must get back exactly
-its K contributions. No GPU."""
+restatement of the plan the library runs on the device (stratacuda_b200.ep.plan_dispatch: one
+row per (token, destination rank), bucketed by rank, token-major inside a bucket, with the
+token's pairs on that rank), exchanged with variable all-to-alls; the owning rank applies a
+stand-in expert to every pair and sums the weighted results per received row (pre-combine);
+one row per (token, rank) comes back and the source adds them in rank order. Every token must
+get exactly the weighted sum of its K experts. No GPU."""
 import os
 import socket
 
@@ -37,61 +38,72 @@ def worker(rank, world, port, T, seed, out):
         ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int64)
         if T > 3:
             ids[3, 5] = -1  # a pair without an expert travels nowhere
+            ids[2] = np.arange(K)  # every expert on rank 0: one row, to rank 0 only
+        w = rng.random((T, K))
         x = rng.standard_normal((T, H))
-        pos, counts = plan_dispatch(ids, E, world)
+        pos, counts, pairs = plan_dispatch(ids, E, world)
         el = E // world
-        # send order: rows of x per pair, the pair's expert, the owning rank check
         S = int(counts.sum())
+        # a send row: the token's x, then K (expert, weight) slots (expert -1 unused)
         send_x = np.zeros((S, H))
-        send_e = np.zeros(S, np.int64)
+        send_meta = np.full((S, 2 * K), -1.0)
         for t in range(T):
-            for k in range(K):
-                p = pos[t, k]
-                if p >= 0:
-                    send_x[p] = x[t]
-                    send_e[p] = ids[t, k]
+            for p in range(world):
+                row = pos[t, p]
+                if row >= 0:
+                    send_x[row] = x[t]
+                    for j, (k, e) in enumerate(pairs[row]):
+                        send_meta[row, 2 * j], send_meta[row, 2 * j + 1] = e, w[t, k]
         rcounts = torch.empty(world, dtype=torch.int64)
         dist.all_to_all_single(rcounts, torch.tensor(counts))
         rc = rcounts.tolist()
         R = sum(rc)
         recv_x = torch.empty((R, H), dtype=torch.float64)
-        recv_e = torch.empty(R, dtype=torch.int64)
+        recv_meta = torch.empty((R, 2 * K), dtype=torch.float64)
         dist.all_to_all_single(recv_x, torch.from_numpy(send_x), rc, counts.tolist())
-        dist.all_to_all_single(recv_e, torch.from_numpy(send_e), rc, counts.tolist())
-        assert all(rank * el <= int(e) < (rank + 1) * el for e in recv_e.tolist()), "pair on the wrong rank"
-        outs = torch.stack([torch.from_numpy(expert_fn(int(e), r.numpy())) for e, r in zip(recv_e, recv_x)]) if R else \
-            torch.empty((0, H), dtype=torch.float64)
+        dist.all_to_all_single(recv_meta, torch.from_numpy(send_meta), rc, counts.tolist())
+        outs = torch.zeros((R, H), dtype=torch.float64)
+        for i in range(R):  # pre-combine: the weighted sum of the row's pairs
+            for j in range(K):
+                e = int(recv_meta[i, 2 * j])
+                if e < 0:
+                    continue
+                assert rank * el <= e < (rank + 1) * el, "pair on the wrong rank"
+                outs[i] += float(recv_meta[i, 2 * j + 1]) * torch.from_numpy(expert_fn(e, recv_x[i].numpy()))
         back = torch.empty((S, H), dtype=torch.float64)
         dist.all_to_all_single(back, outs, counts.tolist(), rc)
         y = np.zeros((T, H))
         for t in range(T):
-            for k in range(K):
-                if pos[t, k] >= 0:
-                    y[t] += back[pos[t, k]].numpy()
+            for p in range(world):
+                if pos[t, p] >= 0:
+                    y[t] += back[pos[t, p]].numpy()
         ref = np.zeros((T, H))
         for t in range(T):
             for k in range(K):
                 if ids[t, k] >= 0:
-                    ref[t] += expert_fn(int(ids[t, k]), x[t])
-        out[rank] = float(np.abs(y - ref).max())
+                    ref[t] += w[t, k] * expert_fn(int(ids[t, k]), x[t])
+        out[rank] = (float(np.abs(y - ref).max()), S, T)
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("T", [1, 37])
 def test_ep_plan_two_ranks(T):
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(worker, args=(2, free_port(), T, 5, out), nprocs=2, join=True)
     assert set(out.keys()) == {0, 1}
-    assert max(out.values()) < 1e-9
+    for err, rows, tokens in out.values():
+        assert err < 1e-9
+        assert rows <= 2 * tokens  # at most one row per (token, rank)
 
 
 def test_plan_dispatch_is_stable_and_complete():
     from stratacuda_b200.ep import plan_dispatch
-    ids = np.array([[5, 300, 1], [300, 2, 511], [-1, 256, 4]])
-    pos, counts = plan_dispatch(ids, 512, 2)
-    # rank 0 (experts 0..255) in token-major order: (0,0) e5, (0,2) e1, (1,1) e2, (2,2) e4;
-    # rank 1 (256..511): (0,1) e300, (1,0) e300, (1,2) e511, (2,1) e256; (2,0) has no expert
-    assert counts.tolist() == [4, 4]
-    assert pos.tolist() == [[0, 4, 1], [5, 2, 6], [-1, 7, 3]]
+    ids = np.array([[5, 300, 1], [300, 2, 511], [-1, 256, 4], [7, 8, 9]])
+    pos, counts, pairs = plan_dispatch(ids, 512, 2)
+    # rank 0 (experts 0..255), token-major: t0, t1, t2, t3; rank 1 (256..511): t0, t1, t2
+    assert counts.tolist() == [4, 3]
+    assert pos.tolist() == [[0, 4], [1, 5], [2, 6], [3, -1]]
+    assert pairs[0] == [(0, 5), (2, 1)] and pairs[4] == [(1, 300)]
+    assert pairs[5] == [(0, 300), (2, 511)] and pairs[6] == [(1, 256)] and pairs[3] == [(0, 7), (1, 8), (2, 9)]
