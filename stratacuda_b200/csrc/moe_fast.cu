@@ -52,6 +52,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -769,15 +770,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         for (int item = cta * kWarps + warp; item < B * H4; item += G * kWarps) {
             const int t = item / H4, c = item % H4;
             float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int m = lane; m < NT; m += 32) {
-                const int jj = m / (K + 1), kk = m % (K + 1);  // kk == 0: shared expert, else routed pair kk - 1
-                const int row = kk == 0 ? B * K + t : t * K + kk - 1;
-                const bool ok = kk == 0 || (unsigned)S.ids[t * K + kk - 1] < (unsigned)E;
-                const float4 u = ok ? __ldcg(part4 + ((long long)jj * PP + row) * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                acc.x += u.x;
-                acc.y += u.y;
-                acc.z += u.z;
-                acc.w += u.w;
+            for (int m0 = 0; m0 < NT; m0 += 96) {  // three terms per lane: their loads are all in flight before the adds
+                float4 u[3];
+#pragma unroll
+                for (int v = 0; v < 3; ++v) {
+                    const int m = m0 + lane + 32 * v;
+                    const int jj = m / (K + 1), kk = m % (K + 1);  // kk == 0: shared expert, else routed pair kk - 1
+                    const int row = kk == 0 ? B * K + t : t * K + kk - 1;
+                    const bool ok = m < NT && (kk == 0 || (unsigned)S.ids[t * K + kk - 1] < (unsigned)E);
+                    u[v] = ok ? __ldcg(part4 + ((long long)jj * PP + row) * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+#pragma unroll
+                for (int v = 0; v < 3; ++v) {
+                    acc.x += u[v].x;
+                    acc.y += u[v].y;
+                    acc.z += u[v].z;
+                    acc.w += u[v].w;
+                }
             }
 #pragma unroll
             for (int sft = 16; sft > 0; sft >>= 1) {
@@ -908,6 +917,10 @@ cudaError_t launch_fast(const fast::Params &p, int grid, cudaStream_t s) {
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
+    if (g_fast_pdl < 0) {  // STRATA_FAST_PDL=0 launches without programmatic dependent launch
+        const char *env = std::getenv("STRATA_FAST_PDL");
+        if (env && env[0] == '0') g_fast_pdl = 0;
+    }
     if (g_fast_pdl != 0) {
         cfg.numAttrs = 2;
         const cudaError_t e = cudaLaunchKernelEx(&cfg, fast::k_moe_fast<H, F>, p);
