@@ -705,6 +705,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         // Pair p = thread p (B * topK <= 256): the lowest pair of an expert opens its slot,
         // slots are numbered by a ballot prefix over pairs; a slot's tokens are listed in
         // arrival order, which only permutes MMA columns within the CTA.
+        if (B == 1) {
+            // one token: its pairs are its selections in k order and their experts are distinct,
+            // so slot s (>= 1) is the s-th valid selection; one thread fills the table
+            if (tid == 0) {
+                int n = 1;
+                for (int k = 0; k < K; ++k) {
+                    const int e = S.ids[k];
+                    if (e < 0 || e >= E) continue;
+                    S.slot_expert[n] = (short)e;
+                    S.slot_n[n] = 1;
+                    S.slot_pair[n][0] = (short)k;
+                    ++n;
+                }
+                S.n_slots = n;
+            }
+            __syncthreads();
+        } else {
         int pe = -1, prank = 0;
         bool pvalid = false;
         if (tid < P2) {
@@ -735,6 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         __syncthreads();
         if (pvalid) S.slot_pair[S.u.r.slot_of[pe]][prank] = (short)tid;
         __syncthreads();
+        }
         const int NU = S.n_slots * NJ;
         n_units = cta < NU ? (NU - 1 - cta) / G + 1 : 0;
         gu_known = n_units * CPT;
