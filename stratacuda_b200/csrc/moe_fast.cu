@@ -1,5 +1,5 @@
 // Fast fused mixture-of-experts layer for decode batches (tokens <= 8): ONE persistent
-// cooperative launch, one CTA per SM, 8 warps, one grid-wide arrival.
+// cooperative launch, one CTA per SM, 8 warps, two grid-wide arrivals (three from 3 tokens).
 //
 // Work units. An expert's layer splits by hidden columns into F/64 units: unit (slot, j)
 // owns hidden values [64j, 64j+64) of one expert slot (slot 0 = the shared expert, slots
@@ -25,9 +25,11 @@
 // while the grid gathers. CTAs that own a shared-expert unit start its copies at entry and
 // compute its gate/up part before waiting at the arrival. y is not touched before the final
 // sum, so it needs no zeroing.
-// Phase 1 (after the arrival: all logits written): every CTA routes all tokens redundantly
-// (route.cuh route_group: up to 8 warps per token) and builds the expert slots, then runs
-// its units.
+// Phase 1 (after the arrival: all logits written): with one or two tokens every CTA routes
+// them redundantly (route.cuh route_group: 8 or 4 warps per token), so only the logits cross
+// the grid; with more, CTA G-1-t routes token t with all 8 warps and a third arrival hands
+// the ids and weights to every CTA (one warp per token on every CTA took 16 us at 8 tokens).
+// Each CTA then builds the expert slots and runs its units.
 //
 // Memory pipeline, per warp: a ring of gate/up stages (one 16-row x 128-byte box of codes,
 // 128-byte swizzle, by TMA tensor copy; the first chunk of a unit also brings the 16 rows'
@@ -68,8 +70,9 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kMaxTokens = 8;
 constexpr int kMaxPairs = kMaxTokens * 32;
 constexpr int kMaxSlots = kMaxPairs + 1;
-constexpr int kXBuildBarrier = 9;  // named barrier of the x-operand warps (route groups use 1..8)
-constexpr int kRowsBarrier = 10;   // named barrier of the router-row warps (before the first arrival)
+constexpr int kXBuildBarrier = 9;     // named barrier of the x-operand warps (route groups use 1..8)
+constexpr int kRowsBarrier = 10;      // named barrier of the router-row warps
+constexpr int kSplitRouteTokens = 3;  // from this many tokens on, routing is split over CTAs
 
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ void mbar_init(unsigned long long *bar, unsigned count) {
@@ -180,7 +183,7 @@ struct Params {
     float *logits;   // [tokens][experts]
     float *sg;       // [tokens]
     float *part;     // [F/64][tokens*topK + tokens][H] partial rows of y
-    unsigned *sync;  // [0] first arrival, [1] second arrival, [2] exits
+    unsigned *sync;  // [0] first arrival, [1] second arrival, [2] exits, [3] routed tokens (split routing)
     unsigned *err;
     unsigned long long spin_limit;
     // TMA maps: [0] routed experts, [1] the shared expert
@@ -237,7 +240,73 @@ struct Smem {
     int abort_flag;
 };
 
+// Bounded wait of thread 0 for *counter >= target, then a CTA barrier; sets abort on timeout.
+__device__ __forceinline__ void cta_spin_until(const unsigned *counter, unsigned target, unsigned long long limit, int *abort_flag) {
+    if (threadIdx.x == 0) {
+        for (unsigned long long i = 0;; ++i) {
+            if (ld_acquire(counter) >= target) break;
+            if (i > limit) {
+                *abort_flag = 1;
+                break;
+            }
+            __nanosleep(32);
+        }
+    }
+    __syncthreads();
+}
+
+// Split routing (three or more tokens), out of line so that the one-token path keeps its
+// code compact (instruction fetch is on that path's critical path). Token t on this CTA:
+// wait for every logit, route with all eight warps, publish ids and weights, arrive.
 template <int H, int F>
+__device__ __noinline__ void split_route_token(const Params &P, Smem<H, F> &S, int t) {
+    const int tid = threadIdx.x, E = P.L.experts, K = P.L.topK;
+    cta_spin_until(&P.sync[0], gridDim.x, P.spin_limit, &S.abort_flag);
+    if (S.abort_flag) return;
+    float *lg = S.u.r.lg[0];
+    const float *src = P.logits + (long long)t * E;
+    if ((E & 3) == 0) {
+        for (int i = tid; i < E / 4; i += kThreads) reinterpret_cast<float4 *>(lg)[i] = __ldcg(reinterpret_cast<const float4 *>(src) + i);
+    } else {
+        for (int i = tid; i < E; i += kThreads) lg[i] = __ldcg(src + i);
+    }
+    if (tid == 0) S.u.r.nzc[0] = 0;
+    __syncthreads();
+    route_group<8>(lg, E, K, S.u.r.red[0], S.u.r.cand[0], &S.u.r.nzc[0], S.ids + t * K, S.u.r.sel[0], S.wts + t * K, 1);
+    __syncthreads();
+    for (int k = tid; k < K; k += kThreads) {
+        P.ids[t * K + k] = S.ids[t * K + k];
+        P.weights[t * K + k] = S.wts[t * K + k];
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(&P.sync[3], 1u);
+    }
+}
+// Every CTA, split routing: wait for all B tokens' routing, then take the ids and weights.
+template <int H, int F>
+__device__ __noinline__ void split_route_receive(const Params &P, Smem<H, F> &S) {
+    const int tid = threadIdx.x, B = P.tokens, K = P.L.topK;
+    cta_spin_until(&P.sync[3], (unsigned)B, P.spin_limit, &S.abort_flag);  // every token routed (and so every logit written)
+    if (S.abort_flag) return;
+    for (int p = tid; p < B * K; p += kThreads) {
+        S.ids[p] = __ldcg(P.ids + p);
+        S.wts[p] = __ldcg(P.weights + p);
+    }
+    for (int e = tid; e < P.L.experts; e += kThreads) {
+        S.u.r.owner[e] = 0x7fffffff;
+        S.u.r.cnt[e] = 0;
+    }
+    if (tid < B) S.sgw[tid] = ref_sigmoid(__ldcg(P.sg + tid));
+    __syncthreads();
+}
+
+// SPLIT: the instance for three or more tokens (split routing, router rows two tokens at a
+// time, 16-byte x loads); the other one keeps the one-token code compact: the presence of
+// the split code alone, even out of line, cost the one-token launch 0.8 us (instruction
+// fetch is on its critical path).
+template <int H, int F, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant__ Params P) {
     using Gm = Geo<H, F>;
     constexpr int NG = Gm::NG, NJ = Gm::NJ, CPT = Gm::CPT, SGU = Gm::SGU, RW = Gm::RW;
@@ -370,9 +439,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
     }
     __syncthreads();
     if (router_warp) {
+        auto store_logit = [&](int r, int t, float v) {
+            if (r < E) P.logits[(long long)t * E + r] = L.bias ? __fadd_rn(v, L.bias[r]) : v;
+            else P.sg[t] = v;
+        };
         for (int r = row0; r <= E; r += G * RWARPS) {
             if (r != row0) load_row(r);
-            for (int t = 0; t < B; ++t) {
+            int t = 0;
+            for (; SPLIT && t + 1 < B; t += 2) {  // several tokens: two at a time, four independent chains
+                const float *xa = S.u.x + t * H, *xb = xa + H;
+                float la = 0.0f, ha = 0.0f, lb = 0.0f, hb = 0.0f;
+#pragma unroll
+                for (int j = 0; j < NG; ++j) {
+                    la = __fadd_rn(la, __fmul_rn(wv[2 * j], xa[64 * j + lane]));
+                    ha = __fadd_rn(ha, __fmul_rn(wv[2 * j + 1], xa[64 * j + 32 + lane]));
+                    lb = __fadd_rn(lb, __fmul_rn(wv[2 * j], xb[64 * j + lane]));
+                    hb = __fadd_rn(hb, __fmul_rn(wv[2 * j + 1], xb[64 * j + 32 + lane]));
+                }
+                const float va = tree64(la, ha), vb = tree64(lb, hb);
+                if (lane == 0) {
+                    store_logit(r, t, va);
+                    store_logit(r, t + 1, vb);
+                }
+            }
+            for (; t < B; ++t) {
                 const float *xv = S.u.x + t * H;
                 float lo = 0.0f, hi = 0.0f;
 #pragma unroll
@@ -381,10 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
                     hi = __fadd_rn(hi, __fmul_rn(wv[2 * j + 1], xv[64 * j + 32 + lane]));
                 }
                 const float v = tree64(lo, hi);
-                if (lane == 0) {
-                    if (r < E) P.logits[(long long)t * E + r] = L.bias ? __fadd_rn(v, L.bias[r]) : v;
-                    else P.sg[t] = v;
-                }
+                if (lane == 0) store_logit(r, t, v);
             }
         }
         // the CTA's rows are written: arrive now (routing needs only the logits); the x
@@ -398,9 +485,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
     const int xw0 = RWARPS < kWarps ? RWARPS : 0;  // first x-operand warp (all warps, after their rows, if none is free)
     if (warp >= xw0) {
         const int bi = tid - 32 * xw0, nb = kThreads - 32 * xw0;
-        for (int t = 0; t < B; ++t) {  // per-token max |x| (NaN ignored, as fmaxf)
+        for (int t = 0; t < B; ++t) {  // per-token max |x| (NaN ignored, as fmaxf; max is order-free)
             float mx = 0.0f;
-            for (int e = bi; e < H; e += nb) mx = fmaxf(mx, fabsf(S.u.x[t * H + e]));
+            if constexpr (SPLIT) {  // several tokens: 16-byte loads, two chains
+                const float4 *x4 = reinterpret_cast<const float4 *>(S.u.x + t * H);
+                float m1 = 0.0f;
+                for (int e = bi; e < H / 4; e += nb) {
+                    const float4 v = x4[e];
+                    mx = fmaxf(mx, fmaxf(fabsf(v.x), fabsf(v.y)));
+                    m1 = fmaxf(m1, fmaxf(fabsf(v.z), fabsf(v.w)));
+                }
+                mx = fmaxf(mx, m1);
+            } else {
+                for (int e = bi; e < H; e += nb) mx = fmaxf(mx, fabsf(S.u.x[t * H + e]));
+            }
 #pragma unroll
             for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
             if (lane == 0) atomicMax(&S.xmax[t], __float_as_uint(mx));
@@ -408,6 +506,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         named_sync(kXBuildBarrier, nb);
         // blocks of 16 elements (token, group, q); B * NG * 4 is a multiple of 32, so whole
         // warps run each iteration and the group-sum shuffles see all four blocks of a group
+        // (measured: letting the router warps join through a shared counter cost 0.25 us at
+        // one token and saved 0.2 us at eight)
         for (int b = bi; b < B * NG * 4; b += nb) {
             const int t = b / (NG * 4), grp = (b >> 2) % NG, qq = b & 3;
             const int k = scale_exp(__uint_as_float(S.xmax[t]));
@@ -647,59 +747,60 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
     }
 
     // ------------------------------------------------------------------ arrival: routing
-    if (tid == 0) {
-        for (unsigned long long i = 0;; ++i) {
-            if (ld_acquire(&P.sync[0]) >= (unsigned)G) break;
-            if (i > P.spin_limit) {
-                S.abort_flag = 1;
-                break;
+    // Three or more tokens: routing is split over the last B CTAs (CTA G-1-t routes token t
+    // with all eight warps and publishes its ids and weights; a third arrival hands them to
+    // every CTA). Fewer tokens: every CTA routes every token itself, which spares the
+    // arrival (route_group with 8 or 4 warps per token is as fast as one token on a CTA).
+    int n_units = 0;
+    if constexpr (SPLIT) {
+        if (G - 1 - cta < B) split_route_token<H, F>(P, S, G - 1 - cta);
+        split_route_receive<H, F>(P, S);
+    } else {
+        cta_spin_until(&P.sync[0], (unsigned)G, P.spin_limit, &S.abort_flag);
+        if (!S.abort_flag) {
+            if ((E & 3) == 0) {
+                for (int i = tid; i < B * E / 4; i += kThreads) {
+                    const int t = i / (E / 4), e4 = i % (E / 4);
+                    reinterpret_cast<float4 *>(S.u.r.lg[t])[e4] = __ldcg(reinterpret_cast<const float4 *>(P.logits) + i);
+                }
+            } else {
+                for (int i = tid; i < B * E; i += kThreads) S.u.r.lg[i / E][i % E] = __ldcg(P.logits + i);
             }
-            __nanosleep(32);
+            for (int e = tid; e < E; e += kThreads) {
+                S.u.r.owner[e] = 0x7fffffff;
+                S.u.r.cnt[e] = 0;
+            }
+            if (tid < B) {
+                S.u.r.nzc[tid] = 0;
+                S.sgw[tid] = ref_sigmoid(__ldcg(P.sg + tid));
+            }
+            __syncthreads();
+            const int W = B == 1 ? 8 : B == 2 ? 4 : B <= 4 ? 2 : 1;
+            const int t = warp / W;
+            if (t < B) {
+                float *lg = S.u.r.lg[t];
+                float *red = S.u.r.red[t];
+                unsigned long long *cand = S.u.r.cand[t];
+                float *sel = S.u.r.sel[t];
+                int *ids = S.ids + t * K;
+                float *wts = S.wts + t * K;
+                switch (W) {
+                    case 8: route_group<8>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
+                    case 4: route_group<4>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
+                    case 2: route_group<2>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
+                    default: route_group<1>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
+                }
+            }
+            __syncthreads();
+            if (cta == 0)
+                for (int p = tid; p < B * K; p += kThreads) {
+                    P.ids[p] = S.ids[p];
+                    P.weights[p] = S.wts[p];
+                }
         }
     }
-    __syncthreads();
-    int n_units = 0;
     if (!S.abort_flag) {
-        if ((E & 3) == 0) {
-            for (int i = tid; i < B * E / 4; i += kThreads) {
-                const int t = i / (E / 4), e4 = i % (E / 4);
-                reinterpret_cast<float4 *>(S.u.r.lg[t])[e4] = __ldcg(reinterpret_cast<const float4 *>(P.logits) + i);
-            }
-        } else {
-            for (int i = tid; i < B * E; i += kThreads) S.u.r.lg[i / E][i % E] = __ldcg(P.logits + i);
-        }
-        for (int e = tid; e < E; e += kThreads) {
-            S.u.r.owner[e] = 0x7fffffff;
-            S.u.r.cnt[e] = 0;
-        }
-        if (tid < B) {
-            S.u.r.nzc[tid] = 0;
-            S.sgw[tid] = ref_sigmoid(__ldcg(P.sg + tid));
-        }
-        __syncthreads();
-        const int W = B == 1 ? 8 : B == 2 ? 4 : B <= 4 ? 2 : 1;
-        const int t = warp / W;
-        if (t < B) {
-            float *lg = S.u.r.lg[t];
-            float *red = S.u.r.red[t];
-            unsigned long long *cand = S.u.r.cand[t];
-            float *sel = S.u.r.sel[t];
-            int *ids = S.ids + t * K;
-            float *wts = S.wts + t * K;
-            switch (W) {
-                case 8: route_group<8>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
-                case 4: route_group<4>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
-                case 2: route_group<2>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
-                default: route_group<1>(lg, E, K, red, cand, &S.u.r.nzc[t], ids, sel, wts, 1 + t); break;
-            }
-        }
-        __syncthreads();
         const int P2 = B * K;
-        if (cta == 0)
-            for (int p = tid; p < P2; p += kThreads) {
-                P.ids[p] = S.ids[p];
-                P.weights[p] = S.wts[p];
-            }
         // expert slots in first-appearance order (token-major), as src/prefill.js:56-60; an id
         // outside [0, E) (only when fewer than topK experts have a probability) gets no slot.
         // Pair p = thread p (B * topK <= 256): the lowest pair of an expert opens its slot,
@@ -826,6 +927,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         if (prev == (unsigned)G - 1) {  // last CTA out resets the arrival counters for the next launch
             P.sync[0] = 0;
             P.sync[1] = 0;
+            if constexpr (SPLIT) P.sync[3] = 0;
             __threadfence();
             P.sync[2] = 0;
         }
@@ -914,14 +1016,14 @@ bool layer_maps(const MoeLayerDev &L, fast::Params &p) {
 // Cooperative (the grid arrivals need every CTA resident) and, where the runtime accepts the
 // combination, programmatic stream serialisation: the launch is prepared while the previous
 // kernel on the stream finishes; the kernel reads only weights before griddepcontrol.wait.
-template <int H, int F>
-cudaError_t launch_fast(const fast::Params &p, int grid, cudaStream_t s) {
+template <int H, int F, bool SPLIT>
+cudaError_t launch_fast_as(const fast::Params &p, int grid, cudaStream_t s) {
     const size_t smem = sizeof(fast::Smem<H, F>) + 1024;  // + slack for the 1024-byte stage alignment
     static int device_ready = -1;  // device whose attribute is set (the library drives one device per context)
     int dev = 0;
     STRATA_CUDA_TRY(cudaGetDevice(&dev));
     if (device_ready != dev) {
-        STRATA_CUDA_TRY(cudaFuncSetAttribute(fast::k_moe_fast<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        STRATA_CUDA_TRY(cudaFuncSetAttribute(fast::k_moe_fast<H, F, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         device_ready = dev;
     }
     cudaLaunchConfig_t cfg = {};
@@ -941,7 +1043,7 @@ cudaError_t launch_fast(const fast::Params &p, int grid, cudaStream_t s) {
     }
     if (g_fast_pdl != 0) {
         cfg.numAttrs = 2;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, fast::k_moe_fast<H, F>, p);
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, fast::k_moe_fast<H, F, SPLIT>, p);
         if (e == cudaSuccess || g_fast_pdl == 1) {
             g_fast_pdl = e == cudaSuccess ? 1 : g_fast_pdl;
             return e;
@@ -950,7 +1052,15 @@ cudaError_t launch_fast(const fast::Params &p, int grid, cudaStream_t s) {
         g_fast_pdl = 0;
     }
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, fast::k_moe_fast<H, F>, p);
+    return cudaLaunchKernelEx(&cfg, fast::k_moe_fast<H, F, SPLIT>, p);
+}
+
+// Split routing from kSplitRouteTokens tokens on, when the grid has a CTA per token beyond
+// the shared-expert units' CTAs.
+template <int H, int F>
+cudaError_t launch_fast(const fast::Params &p, int grid, cudaStream_t s) {
+    if (p.tokens >= fast::kSplitRouteTokens && grid >= F / 64 + p.tokens) return launch_fast_as<H, F, true>(p, grid, s);
+    return launch_fast_as<H, F, false>(p, grid, s);
 }
 
 }  // namespace
