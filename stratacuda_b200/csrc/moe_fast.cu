@@ -259,7 +259,7 @@ __device__ __forceinline__ void cta_spin_until(const unsigned *counter, unsigned
 // code compact (instruction fetch is on that path's critical path). Token t on this CTA:
 // wait for every logit, route with all eight warps, publish ids and weights, arrive.
 template <int H, int F>
-__device__ __noinline__ void split_route_token(const Params &P, Smem<H, F> &S, int t) {
+__device__ __forceinline__ void split_route_token(const Params &P, Smem<H, F> &S, int t) {
     const int tid = threadIdx.x, E = P.L.experts, K = P.L.topK;
     cta_spin_until(&P.sync[0], gridDim.x, P.spin_limit, &S.abort_flag);
     if (S.abort_flag) return;
@@ -286,7 +286,7 @@ __device__ __noinline__ void split_route_token(const Params &P, Smem<H, F> &S, i
 }
 // Every CTA, split routing: wait for all B tokens' routing, then take the ids and weights.
 template <int H, int F>
-__device__ __noinline__ void split_route_receive(const Params &P, Smem<H, F> &S) {
+__device__ __forceinline__ void split_route_receive(const Params &P, Smem<H, F> &S) {
     const int tid = threadIdx.x, B = P.tokens, K = P.L.topK;
     cta_spin_until(&P.sync[3], (unsigned)B, P.spin_limit, &S.abort_flag);  // every token routed (and so every logit written)
     if (S.abort_flag) return;
@@ -335,8 +335,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
     int gu_known = cta < NJ ? CPT : 0, dn_known = 0;
     int gu_issued = 0, gu_done = 0, dn_issued = 0, dn_done = 0;
     bool stalled = false;  // this warp saw a wait time out: issue nothing more
+    // Unit index of the CTA's unit ui. One or two tokens: round-robin, unit u on CTA u % G.
+    // Split instance: the CTAs of the shared-expert units (0 .. NJ-1, whose unit carries
+    // every token) sit out the first round of routed units, and every later round starts at
+    // CTA NJ, so a partial last round also misses them.
+    auto unit_index = [&](int ui) -> int {
+        if constexpr (SPLIT) {
+            if (ui == 0) return cta;
+            return cta < NJ ? (ui + 1) * G + cta - NJ : ui * G + cta - NJ;
+        } else {
+            return cta + ui * G;
+        }
+    };
     auto unit_of = [&](int ui, int &slot, int &j, int &m, int &e) {
-        const int u = cta + ui * G;
+        const int u = unit_index(ui);
         slot = u / NJ;
         j = u % NJ;
         m = slot == 0 ? 1 : 0;
@@ -855,7 +867,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         __syncthreads();
         }
         const int NU = S.n_slots * NJ;
-        n_units = cta < NU ? (NU - 1 - cta) / G + 1 : 0;
+        if constexpr (SPLIT) {
+            while (unit_index(n_units) < NU) ++n_units;
+        } else {
+            n_units = cta < NU ? (NU - 1 - cta) / G + 1 : 0;
+        }
         gu_known = n_units * CPT;
         dn_known = n_units;
         pump();
@@ -886,35 +902,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
         // by a fixed shuffle tree: the order never changes, so y has the same bits every run.
         const int PP = B * K + B, H4 = H / 4, NT = NJ * (K + 1);
         const float4 *part4 = reinterpret_cast<const float4 *>(P.part);
-        for (int item = cta * kWarps + warp; item < B * H4; item += G * kWarps) {
-            const int t = item / H4, c = item % H4;
-            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        // Several tokens: NB items of a warp at once (their loads all in flight; each item's
+        // additions in the same order as one at a time).
+        constexpr int NB = SPLIT ? 4 : 1;
+        const int stride = G * kWarps;
+        for (int item0 = cta * kWarps + warp; item0 < B * H4; item0 += NB * stride) {
+            float4 acc[NB];
+#pragma unroll
+            for (int n = 0; n < NB; ++n) acc[n] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             for (int m0 = 0; m0 < NT; m0 += 96) {  // three terms per lane: their loads are all in flight before the adds
-                float4 u[3];
+                float4 u[NB][3];
 #pragma unroll
-                for (int v = 0; v < 3; ++v) {
-                    const int m = m0 + lane + 32 * v;
-                    const int jj = m / (K + 1), kk = m % (K + 1);  // kk == 0: shared expert, else routed pair kk - 1
-                    const int row = kk == 0 ? B * K + t : t * K + kk - 1;
-                    const bool ok = m < NT && (kk == 0 || (unsigned)S.ids[t * K + kk - 1] < (unsigned)E);
-                    u[v] = ok ? __ldcg(part4 + ((long long)jj * PP + row) * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                for (int n = 0; n < NB; ++n) {
+                    const int item = item0 + n * stride, t = min(item / H4, B - 1), c = item % H4;  // t clamped: past the end, nothing is read
+#pragma unroll
+                    for (int v = 0; v < 3; ++v) {
+                        const int m = m0 + lane + 32 * v;
+                        const int jj = m / (K + 1), kk = m % (K + 1);  // kk == 0: shared expert, else routed pair kk - 1
+                        const int row = kk == 0 ? B * K + t : t * K + kk - 1;
+                        const bool ok = item < B * H4 && m < NT && (kk == 0 || (unsigned)S.ids[t * K + kk - 1] < (unsigned)E);
+                        u[n][v] = ok ? __ldcg(part4 + ((long long)jj * PP + row) * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    }
                 }
 #pragma unroll
-                for (int v = 0; v < 3; ++v) {
-                    acc.x += u[v].x;
-                    acc.y += u[v].y;
-                    acc.z += u[v].z;
-                    acc.w += u[v].w;
-                }
+                for (int n = 0; n < NB; ++n)
+#pragma unroll
+                    for (int v = 0; v < 3; ++v) {
+                        acc[n].x += u[n][v].x;
+                        acc[n].y += u[n][v].y;
+                        acc[n].z += u[n][v].z;
+                        acc[n].w += u[n][v].w;
+                    }
             }
 #pragma unroll
-            for (int sft = 16; sft > 0; sft >>= 1) {
-                acc.x += __shfl_xor_sync(0xffffffffu, acc.x, sft);
-                acc.y += __shfl_xor_sync(0xffffffffu, acc.y, sft);
-                acc.z += __shfl_xor_sync(0xffffffffu, acc.z, sft);
-                acc.w += __shfl_xor_sync(0xffffffffu, acc.w, sft);
+            for (int n = 0; n < NB; ++n) {
+#pragma unroll
+                for (int sft = 16; sft > 0; sft >>= 1) {
+                    acc[n].x += __shfl_xor_sync(0xffffffffu, acc[n].x, sft);
+                    acc[n].y += __shfl_xor_sync(0xffffffffu, acc[n].y, sft);
+                    acc[n].z += __shfl_xor_sync(0xffffffffu, acc[n].z, sft);
+                    acc[n].w += __shfl_xor_sync(0xffffffffu, acc[n].w, sft);
+                }
+                const int item = item0 + n * stride;
+                if (lane == 0 && item < B * H4) reinterpret_cast<float4 *>(P.y)[item] = acc[n];
             }
-            if (lane == 0) reinterpret_cast<float4 *>(P.y)[item] = acc;
         }
     }
 
