@@ -5,9 +5,11 @@ routed experts, top-10 renormalised routing, one shared expert, expert intermedi
 Q2 packed blobs (uniform 2-bit codes, FP16 scales |N(0,0.02)|), F32 router N(0,0.02),
 F32 activations N(0,1); seeded synthetic data. A step is one pass of the fused layer over
 one batch. `--batch 8` and `--batch 64` are config 2's other decode sizes; `--batch 4096`
-is config 3 (prefill, router logits biased by a Zipf(1.1) per-expert offset). Batches above
-8 run the tensor-core prefill path; its roofline is the grouped GEMMs' FLOP rate against the
-measured sustained dense BF16 peak, timed by the library's phase profile in a second pass. Steps cycle over `--layers` distinct layer replicas (default 24: every layer's
+is config 3 (prefill, router logits biased by a Zipf(1.1) per-expert offset). Batches of 9 to
+64 run the medium-batch layer (HBM roofline, like decode); batches above 64 run the
+tensor-core prefill path, whose roofline is the grouped GEMMs' FLOP rate against the
+measured sustained dense BF16 peak, timed by the library's phase profile in a second pass.
+Steps cycle over `--layers` distinct layer replicas (default 24: every layer's
 routed weights are evicted from the 126 MB L2 before the layer comes round again) with a
 fresh activation batch per step, so no step reads weights left in L2 by the previous one.
 
@@ -239,8 +241,11 @@ def run_gpu_arm(args, world, rank, local):
     stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", local))
     from stratacuda_b200 import _lib as LL
     mode = LL.MOE_FAST if args.mode == "fast" else LL.MOE_EXACT
-    prefill = mode == LL.MOE_FAST and B > 8
-    launches = 1 if (mode == LL.MOE_FAST and B <= 8) else (9 if prefill else 6)
+    medium = mode == LL.MOE_FAST and 8 < B <= 64
+    prefill = mode == LL.MOE_FAST and B > 64
+    # kernels per step: decode 1; medium 4 (router tail rows, exact logits, top-k, the layer);
+    # prefill 9; exact 6
+    launches = 1 if (mode == LL.MOE_FAST and B <= 8) else 4 if medium else 9 if prefill else 6
     for s in range(W):
         layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
     b.idle()
@@ -285,7 +290,9 @@ def run_gpu_arm(args, world, rank, local):
     else:
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
                     "peak_kind": peak_kind,
-                    "kernel": ("k_moe_fast (one persistent launch per step)" if launches == 1 else "fused exact MoE layer (6 launches per step)"),
+                    "kernel": ("k_moe_fast (one persistent launch per step)" if launches == 1
+                               else "k_moe_medium (after the exact router kernels: 4 launches per step)" if medium
+                               else "fused exact MoE layer (6 launches per step)"),
                     "algorithmic_bytes_per_step": alg_bytes}
 
     # end to end through the C-ABI with host buffers (pinned), host-timed

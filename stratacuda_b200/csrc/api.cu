@@ -611,9 +611,11 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
         return fail(ctx, STRATA_ERR_RANGE, "Router supports 1-512 experts and topK <= min(experts,32)");
     if (tokens < 1) return fail(ctx, STRATA_ERR_RANGE, "tokens must be an integer >= 1");
     if (mode != STRATA_MOE_EXACT && mode != STRATA_MOE_FAST) return fail(ctx, STRATA_ERR_RANGE, "unknown mode %d", mode);
-    // FAST: the fused decode kernel up to its token limit, the tensor-core prefill path above it
+    // FAST: the fused decode kernel up to 8 tokens, the medium-batch layer up to 64, the
+    // tensor-core prefill path above
     const bool fast = mode == STRATA_MOE_FAST && moe_fast_supported(tokens, l.width, l.ff, l.top_k, ctx->sms);
-    const bool prefill = mode == STRATA_MOE_FAST && !fast && moe_prefill_supported(l.width, l.ff, l.experts, l.top_k);
+    const bool medium = mode == STRATA_MOE_FAST && !fast && moe_medium_supported(tokens, l.width, l.ff, l.experts, l.top_k, ctx->sms);
+    const bool prefill = mode == STRATA_MOE_FAST && !fast && !medium && moe_prefill_supported(l.width, l.ff, l.experts, l.top_k);
     const long long bw = blob_words_of(l.width, l.ff);
     struct Need {
         strata_buf h;
@@ -642,6 +644,7 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     }
     if (int r = use_device(ctx)) return r;
     const size_t ws = fast      ? moe_fast_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
+                      : medium  ? moe_medium_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
                       : prefill ? moe_prefill_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k)
                                 : moe_scratch_bytes(tokens, l.width, l.ff, l.experts, l.top_k);
     if (ws > ctx->workspace_bytes) {
@@ -661,7 +664,7 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     MoeLayerDev L{l.width, l.ff, l.experts, l.top_k, (const float *)ptr[0], (const float *)ptr[1], (const unsigned *)ptr[2], bw,
                   (const unsigned *)ptr[3], (const float *)ptr[4]};
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
-    if (ctx->profile && (fast || prefill)) {
+    if (ctx->profile && (fast || medium || prefill)) {
         for (cudaEvent_t &x : ev) {
             if (!ctx->spare_events.empty()) {
                 x = ctx->spare_events.back();
@@ -673,10 +676,12 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
         ++ctx->profiled_calls;
     }
     cudaError_t e;
-    if (fast) {
+    if (fast || medium) {
         if (ev[0]) CUDA_OR_FAIL(ctx, cudaEventRecord(ev[0], ctx->stream), "cudaEventRecord");
-        e = moe_forward_fast(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
-                             ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev);
+        e = fast ? moe_forward_fast(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
+                                    ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev)
+                 : moe_forward_medium(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
+                                      ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev);
         if (ev[0]) {
             CUDA_OR_FAIL(ctx, cudaEventRecord(ev[1], ctx->stream), "cudaEventRecord");
             ctx->marks.push_back({3, ev[0], ev[1]});

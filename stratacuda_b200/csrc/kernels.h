@@ -1,6 +1,7 @@
 // Internal interface between the C-ABI layer (api.cu) and the kernel files.
 #pragma once
 #include <string>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -70,6 +71,28 @@ size_t moe_fast_scratch_bytes(int tokens, int width, int ff, int experts, int to
 int moe_fast_pdl_state();  // 1: launched with programmatic dependent launch, 0: refused, -1: not launched yet
 cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
                              unsigned *sync, int grid, cudaStream_t s, unsigned *err);
+
+// TMA maps of a layer's routed experts [0] and shared expert [1], cached by blob address
+// (csrc/moe_fast.cu): gate/up codes (boxes of 16 rows x 128 bytes, 128-byte swizzle), gate/up
+// scales (16 rows x 8 groups) and down codes (16 full rows; 128-byte swizzle for 128-byte rows).
+struct MoeMaps {
+    CUtensorMap gu[2], gs[2], dc[2];
+};
+bool moe_tensor_maps(const MoeLayerDev &L, MoeMaps *maps);
+
+// Medium-batch layer (csrc/moe_medium.cu), 9 .. 64 tokens: the exact router kernels, then one
+// cooperative launch of integer tensor-core units on the 2-bit codes (y within 1e-5 relative
+// L2). `sync` as for moe_forward_fast (the two kernels never overlap on a stream).
+bool moe_medium_supported(int tokens, int width, int ff, int experts, int topK, int grid);
+size_t moe_medium_scratch_bytes(int tokens, int width, int ff, int experts, int topK);
+cudaError_t moe_forward_medium(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
+                               unsigned *sync, int grid, cudaStream_t s, unsigned *err);
+
+// Exact router (csrc/prefill.cu): logits [T][E] + shared-gate logits [T] by the persistent
+// logits kernel (`tail`: moe_logits_tail_bytes of scratch), then ids/weights [T][topK].
+size_t moe_logits_tail_bytes(int width);
+cudaError_t moe_route_exact(const MoeLayerDev &L, const float *x, int T, float *logits, float *sg, float *tail, int *ids, float *weights,
+                            int grid, cudaStream_t s, unsigned *err);
 
 // Prompt / large-batch layer (csrc/prefill.cu): exact routing, expert products on tcgen05
 // tensor cores from Q2 weights dequantised to FP16 (y within 2e-3 relative L2). `grid` is

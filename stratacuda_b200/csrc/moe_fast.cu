@@ -60,118 +60,19 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "q2mma.cuh"
 #include "route.cuh"
 
 namespace strata {
 namespace fast {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kMaxTokens = 8;
+using namespace q2;
+
 constexpr int kMaxPairs = kMaxTokens * 32;
 constexpr int kMaxSlots = kMaxPairs + 1;
 constexpr int kXBuildBarrier = 9;     // named barrier of the x-operand warps (route groups use 1..8)
 constexpr int kRowsBarrier = 10;      // named barrier of the router-row warps
 constexpr int kSplitRouteTokens = 3;  // from this many tokens on, routing is split over CTAs
-
-__device__ __forceinline__ unsigned smem_u32(const void *p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ void mbar_init(unsigned long long *bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect(unsigned long long *bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(unsigned long long *bar, unsigned parity) {
-    unsigned ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes, unsigned long long *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *map, int x, int y, int z, unsigned long long *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned &r0, unsigned &r1, unsigned &r2, unsigned &r3) {
-    asm volatile("ldmatrix.sync.aligned.x4.m8n8.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-__device__ __forceinline__ void imma(int (&d)[4], unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0, unsigned b1) {
-    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void named_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
-__device__ __forceinline__ bool grid_arrive_wait(unsigned *counter, unsigned target, unsigned long long limit) {
-    __threadfence();
-    atomicAdd(counter, 1u);
-    for (unsigned long long i = 0;; ++i) {
-        if (ld_acquire(counter) >= target) return true;
-        if (i > limit) return false;
-        __nanosleep(32);
-    }
-}
-
-// Scale exponent k for maxabs >= 0: 2^k * maxabs < 2^22 (maxabs = m 2^e, m in [0.5, 1): k =
-// 22 - e), 0 for zero or non-finite maxabs, clamped to [-126, 126] so that 2^k and 2^-k are
-// normal floats (a vector whose largest element is subnormal then keeps fewer bits).
-__device__ __forceinline__ int scale_exp(float maxabs) {
-    const unsigned b = __float_as_uint(maxabs);
-    const int be = (int)(b >> 23);  // biased exponent (sign bit clear)
-    int k = 22 - (be - 126);
-    k = be == 0 ? 126 : k;
-    k = be >= 255 || b == 0u ? 0 : k;
-    return max(-126, min(126, k));
-}
-__device__ __forceinline__ float pow2f(int k) { return __uint_as_float((unsigned)(k + 127) << 23); }  // k in [-126, 127]
-// Byte of signed digit d of v = d0 + 256 d1 + 65536 d2 (each digit in [-128, 127]):
-// d0 = v mod 256, d1 = floor((v + 128) / 256) mod 256, d2 = floor((v + 32896) / 65536).
-__device__ __forceinline__ unsigned digit_byte(int v, int d) {
-    const int bias = d == 0 ? 0 : d == 1 ? 128 : 32896;
-    return (unsigned)((v + bias) >> (8 * d)) & 255u;
-}
-__device__ __forceinline__ unsigned pack_digit(const int *v, int d) {
-    return digit_byte(v[0], d) | digit_byte(v[1], d) << 8 | digit_byte(v[2], d) << 16 | digit_byte(v[3], d) << 24;
-}
-// B-fragment words of 16 consecutive elements e0..e15 of a 64-group (block q of 16): for MMA
-// half h, register b0 byte i is element 2h + 4i, b1 byte i is element 2h + 1 + 4i (the A
-// side: (w >> 4h) & 0x03030303 of the row's word q holds codes 16q + 2h + 4i).
-__device__ __forceinline__ void block_frags(const int (&v)[16], uint2 *dst_h0, uint2 *dst_h1) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int lo[4] = {v[2 * h], v[2 * h + 4], v[2 * h + 8], v[2 * h + 12]};
-        const int hi[4] = {v[2 * h + 1], v[2 * h + 5], v[2 * h + 9], v[2 * h + 13]};
-        uint2 *dst = h ? dst_h1 : dst_h0;
-#pragma unroll
-        for (int d = 0; d < 3; ++d) dst[d] = make_uint2(pack_digit(lo, d), pack_digit(hi, d));
-    }
-}
 
 struct Params {
     MoeLayerDev L;
@@ -190,18 +91,6 @@ struct Params {
     CUtensorMap tm_gu[2];  // gate/up codes: {H/4 bytes, 2F rows, experts}, box {128, 16, 1}, 128B swizzle
 };
 
-template <int H, int F>
-struct Geo {
-    static constexpr int NG = H / 64;                  // scale groups per gate/up row
-    static constexpr int NJ = F / 64;                  // units per expert
-    static constexpr int CPT = NG / 8;                 // gate/up chunks per warp and unit
-    static constexpr int SGU = NG == 32 ? 4 : 3;       // gate/up stages per warp
-    static constexpr int RW = H / kWarps;              // down rows per warp
-    static constexpr int DN_CODES = RW * 16;           // 16 code bytes per row
-    static constexpr int DN_STAGE = (DN_CODES + RW * 4 + 127) / 128 * 128;  // + one scale word per row
-    static constexpr int GS_BYTES = 16 * 2 * NG;       // FP16 scales of a warp's 16 gate/up rows
-    static_assert(NG % 8 == 0 && RW % 32 == 0 && NJ % 2 == 0, "geometry");
-};
 
 template <int H, int F>
 struct Smem {
@@ -1010,15 +899,18 @@ struct MapSet {
     const void *blobs, *shared;
     int width, ff, experts;
     CUtensorMap gu[2];
+    MoeMaps all;  // the maps of the medium-batch layer
 };
 std::mutex g_map_mutex;
 MapSet g_maps[64];
 int g_map_next = 0;
 
-bool layer_maps(const MoeLayerDev &L, fast::Params &p) {
+// gu2 receives the two gate/up maps, all (nullable) the medium-batch layer's maps.
+bool layer_maps(const MoeLayerDev &L, CUtensorMap *gu2, MoeMaps *all) {
     std::lock_guard<std::mutex> lock(g_map_mutex);
     auto use = [&](const MapSet &m) {
-        std::memcpy(p.tm_gu, m.gu, sizeof m.gu);
+        std::memcpy(gu2, m.gu, sizeof m.gu);
+        if (all) *all = m.all;
     };
     for (const MapSet &m : g_maps)
         if (m.blobs == L.blobs && m.shared == L.shared_blob && m.width == L.width && m.ff == L.ff && m.experts == L.experts) {
@@ -1037,12 +929,30 @@ bool layer_maps(const MoeLayerDev &L, fast::Params &p) {
         const unsigned long long ne = i == 0 ? (unsigned long long)L.experts : 1ull;
         if (!map3d(&m.gu[i], base, H / 4, 2 * F, ne, H / 4, bb, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return false;
+        m.all.gu[i] = m.gu[i];
+        // gate/up scales {2 NG bytes, 2F rows}, box {16 bytes = 8 groups, 16 rows}
+        if (!map3d(&m.all.gs[i], base + 3 * F * H / 4, H / 32, 2 * F, ne, H / 32, bb, 16, 16, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE))
+            return false;
+        // down codes {F/4 bytes, H rows}, box {F/4, 16 rows}: 128-byte swizzle for 128-byte rows
+        if (!map3d(&m.all.dc[i], base + 2 * F * H / 4, F / 4, H, ne, F / 4, bb, F / 4, 16,
+                   F / 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return false;
     }
     g_maps[g_map_next] = m;
     g_map_next = (g_map_next + 1) % 64;
     use(m);
     return true;
 }
+
+}  // namespace
+
+bool moe_tensor_maps(const MoeLayerDev &L, MoeMaps *maps) {
+    CUtensorMap gu[2];
+    return layer_maps(L, gu, maps);
+}
+
+namespace {
 
 // Cooperative (the grid arrivals need every CTA resident) and, where the runtime accepts the
 // combination, programmatic stream serialisation: the launch is prepared while the previous
@@ -1116,7 +1026,7 @@ cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, f
     prm.sync = sync;
     prm.err = err;
     prm.spin_limit = 1ull << 20;  // grid waits sleep 32 ns per try; an mbarrier try suspends for a short, system-defined time
-    if (!layer_maps(L, prm)) return cudaErrorInvalidValue;
+    if (!layer_maps(L, prm.tm_gu, nullptr)) return cudaErrorInvalidValue;
     if (L.width == 2048 && L.ff == 512) return launch_fast<2048, 512>(prm, grid, s);
     if (L.width == 2560 && L.ff == 640) return launch_fast<2560, 640>(prm, grid, s);
     return cudaErrorInvalidValue;

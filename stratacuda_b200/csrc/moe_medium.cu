@@ -1,0 +1,742 @@
+// Medium-batch fused mixture-of-experts layer (9 .. 64 tokens): integer tensor-core products on
+// the raw 2-bit codes (as the decode kernel, csrc/moe_fast.cu), one whole expert per work unit,
+// after the exact router kernels.
+//
+// At these batch sizes an expert sees one or two tokens on average (640 token-expert pairs
+// over ~370 distinct experts at 64 tokens), so the layer is a bandwidth-bound product of the
+// weights with a few columns: dequantising every weight to FP16 for the tcgen05 GEMMs of the
+// prefill path costs far more than the weight bytes themselves. Here the weights stay as
+// codes (u8 x s8 mma.sync, activations as three signed 8-bit digits, exact integer products).
+//
+// Launches: the exact router logits (k_pf_logits) and top-k (k_pf_route) of the prefill path,
+// then ONE persistent cooperative kernel, one CTA per SM, 8 warps:
+//   A. CTA c turns tokens c, c + G, ... into their digit records in global memory (the digits
+//      of the 64-element groups in the MMA operand layout, each group's digit sum and the
+//      scale 2^-k) and arrives. Every CTA builds the pair table: pairs (t * topK + k) ordered
+//      by expert, token-major within an expert (a stable counting sort; src/prefill.js:55-61
+//      orders them the same way), and numbers the token groups: the shared expert's groups of
+//      two tokens first (its weights are read again from L2 for each; groups of eight made its
+//      units the slowest of the layer), then each routed expert's pairs in groups of eight.
+//   B. Work unit = one token group with its whole expert, dealt round-robin (unit u on CTA
+//      u % G). The unit copies its tokens' digit records into shared memory (one bulk copy
+//      each, issued while the unit before finishes), then
+//        gate/up: warp w takes the 16-row tiles w, w + 8, ... of the 2F interleaved rows (a
+//        tile is 8 hidden values), full width, and forms silu(gate) * up;
+//        hidden -> digits: each token's F hidden values as three signed 8-bit digits (one
+//        rounding, 2^-22 of the token's largest |h|), the same operand layout as x;
+//        down: warp w takes H/8 rows, 16 full rows per copy;
+//      and stores weight * result as one partial row of y per pair (per token for the shared
+//      expert).
+//   C. After a second arrival every CTA sums a slice of y from the partial rows in a fixed
+//      order (the shared expert, then the routed pairs in selection order): the same bits
+//      every run.
+// Whole experts per unit keep every copy a TMA box of full rows (splitting an expert by hidden
+// columns left 16 bytes of each 128-byte down row per unit: 2,048 small requests per unit,
+// measured 307 us per 64-token layer). Per warp, one ring of SGU stages carries the unit's
+// chunks in order: gate/up chunks (16 rows x 128 bytes of codes, 128-byte swizzle, plus the 16
+// rows' 8 group scales by a second TMA box), then down chunks (16 full rows of codes, plus
+// their scales by one bulk copy). Every wait is bounded: past the limit the kernel records
+// kErrWaitTimeout and leaves.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "q2mma.cuh"
+
+namespace strata {
+namespace medium {
+
+using namespace q2;
+
+constexpr int kMaxBatch = 64;
+constexpr int kMaxTopK = 32;
+constexpr int kMaxPairs = kMaxBatch * kMaxTopK;
+constexpr int kMaxExperts = 512;
+constexpr int kSharedGroup = 2;  // tokens per shared-expert unit (its weights are read once per unit, from L2 after the first)
+
+// Digit record of one vector of N elements: digits uint2[N/64][2][4][3] (group, MMA half,
+// 16-element block q, digit), int sum[N/64], float scale (2^-k). In shared memory, slots are
+// STRIDE bytes apart, 96 modulo 128, so the two slots a warp reads together mostly fall on
+// distinct banks.
+template <int N>
+struct Rec {
+    static constexpr int NGR = N / 64;
+    static constexpr int DIGITS = NGR * 2 * 4 * 3;
+    static constexpr int SUM = DIGITS * 8;
+    static constexpr int SCALE = SUM + NGR * 4;
+    static constexpr int BYTES = (SCALE + 4 + 15) / 16 * 16;
+    static constexpr int STRIDE = BYTES + (96 - BYTES % 128 + 128) % 128;
+    static_assert(BYTES % 16 == 0 && STRIDE % 128 == 96, "record layout");
+};
+
+template <int H, int F>
+struct MGeo {
+    static constexpr int NG = H / 64;                          // gate/up scale groups per row
+    static constexpr int NJ = F / 64;                          // down scale groups per row
+    static constexpr int CPT = NG / 8;                         // gate/up chunks per 16-row tile
+    static constexpr int RTW = F / 64;                         // gate/up tiles per warp (2F / 16 / 8)
+    static constexpr int RW = H / kWarps;                      // down rows per warp
+    static constexpr int DTW = RW / 16;                        // down tiles per warp
+    static constexpr int GU_CHUNKS = RTW * CPT;                // per warp and unit
+    static constexpr int CHUNKS = GU_CHUNKS + DTW;             // per warp and unit
+    static constexpr int DROW = F / 4;                         // bytes of a down row
+    static constexpr int CODE_STAGE = F == 512 ? 2048 : 3072;  // 1024-aligned (128-byte swizzle)
+    static constexpr int SCL_STAGE = 384;                      // >= 16 rows x NJ x 2 bytes, a multiple of 128
+    static constexpr int SGU = F == 512 ? 6 : 3;               // stages per warp (shared-memory budget)
+    static_assert(NG % 8 == 0 && RW % 16 == 0 && 16 * DROW <= CODE_STAGE && 32 * NJ <= SCL_STAGE, "geometry");
+};
+
+struct Params {
+    MoeLayerDev L;
+    const float *x;
+    int tokens;
+    float *y;
+    const int *ids;        // [tokens][topK], from the router kernel
+    const float *weights;  // [tokens][topK]
+    const float *sg;       // [tokens] shared-gate logits
+    unsigned char *xrec;   // [tokens] digit records of x (Rec<H>::BYTES each)
+    float *part;           // [tokens*topK + tokens][H] partial rows of y
+    unsigned *sync;        // [0] digit records written, [1] partial rows written, [2] exits
+    unsigned *err;
+    unsigned long long spin_limit;
+    MoeMaps maps;  // [0] routed experts, [1] the shared expert
+};
+
+template <int H, int F>
+struct Smem {
+    using G = MGeo<H, F>;
+    unsigned char codes[kWarps][G::SGU][G::CODE_STAGE];  // 1024-aligned
+    alignas(128) unsigned short scl[kWarps][G::SGU][G::SCL_STAGE / 2];
+    alignas(128) unsigned char xrec[kMaxTokens][Rec<H>::STRIDE];  // the unit's tokens: x digits
+    alignas(128) unsigned char hrec[kMaxTokens][Rec<F>::STRIDE];  // the unit's tokens: hidden digits
+    float hid[kMaxTokens][F];
+    float hmaxw[kWarps][kMaxTokens];  // per-warp max |hidden| of each token slot
+    short pairs[kMaxPairs];           // pairs ordered by expert, token-major within one
+    int off[kMaxExperts + 1];         // expert e's pairs: pairs[off[e] .. off[e+1])
+    int gstart[kMaxExperts + 1];      // expert e's token groups: [gstart[e], gstart[e+1])
+    int run[kMaxExperts];             // pair counts, then placement cursors
+    int ids[kMaxPairs];               // the routed ids
+    int scan_w[2][kWarps];
+    float sgw[kMaxBatch];     // sigmoid(shared-gate logit) per token
+    int urow[2][kMaxTokens];  // unit token slot -> partial row (by unit parity)
+    float uw[2][kMaxTokens];  // unit token slot -> weight
+    unsigned xmax;
+    unsigned long long bar[kWarps][G::SGU];
+    unsigned long long bar_x;
+    int abort_flag;
+};
+
+// Block-wide exclusive scan of two sequences over [0, n) (n <= 512, 256 threads: thread i
+// holds entries 2i and 2i+1); out[n] receives each total.
+template <int H, int F>
+__device__ __forceinline__ void scan2(Smem<H, F> &S, const int (&a)[2], const int (&b)[2], int n, int *out_a, int *out_b, int base_b) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int sa = a[0] + a[1], sb = b[0] + b[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ua = __shfl_up_sync(0xffffffffu, sa, o), ub = __shfl_up_sync(0xffffffffu, sb, o);
+        if (lane >= o) {
+            sa += ua;
+            sb += ub;
+        }
+    }
+    if (lane == 31) {
+        S.scan_w[0][warp] = sa;
+        S.scan_w[1][warp] = sb;
+    }
+    __syncthreads();
+    int wa = 0, wb = 0, ta = 0, tb = 0;
+    for (int w = 0; w < kWarps; ++w) {
+        if (w < warp) {
+            wa += S.scan_w[0][w];
+            wb += S.scan_w[1][w];
+        }
+        ta += S.scan_w[0][w];
+        tb += S.scan_w[1][w];
+    }
+    const int ea = wa + sa - (a[0] + a[1]), eb = wb + sb - (b[0] + b[1]);  // exclusive prefix of entry 2 tid
+    if (2 * tid < n) {
+        out_a[2 * tid] = ea;
+        out_b[2 * tid] = base_b + eb;
+    }
+    if (2 * tid + 1 < n) {
+        out_a[2 * tid + 1] = ea + a[0];
+        out_b[2 * tid + 1] = base_b + eb + b[0];
+    }
+    if (tid == 0) {
+        out_a[n] = ta;
+        out_b[n] = base_b + tb;
+    }
+}
+
+// 16 rows x GPC groups of one chunk against the digit records of the unit's token slots (MMA
+// columns: token slot 2 cg + g / 4, digit g % 4, the fourth digit zero). `code` is the chunk's
+// codes in shared memory (SWZ: 128-byte rows with the 128-byte swizzle; else ROWB-byte rows),
+// `scl` its scales [16 rows][SCLN] (the chunk's groups from column 0), `g0` the chunk's first
+// group in the records (RSTRIDE bytes apart, group sums at byte `sum_off`). Adds
+// scale * sum((c - 1) v) per group into acc.
+template <int GPC, bool SWZ, int ROWB, int SCLN, int RSTRIDE>
+__device__ __forceinline__ void mma_chunk(unsigned code, const unsigned short *scl, const unsigned char *recs, int sum_off, int g0,
+                                          const int (&tsB)[4], const int (&tsC)[4], int ncg, float (&acc)[4][2]) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3, d = g & 3;
+    const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
+    unsigned w[GPC / 2][4];
+#pragma unroll
+    for (int gp = 0; gp < GPC / 2; ++gp) {
+        const int c = 2 * gp + (lane >> 4);
+        const unsigned addr = SWZ ? code + r * 128 + ((c ^ (r & 7)) << 4) : code + r * ROWB + (c << 4);
+        ldsm_x4(addr, w[gp][0], w[gp][1], w[gp][2], w[gp][3]);
+    }
+    // expert scales are finite FP16 (rejected on load otherwise, src/model.js:164): exact conversion
+    float s_lo[GPC], s_hi[GPC];
+#pragma unroll
+    for (int gl = 0; gl < GPC; ++gl) {
+        s_lo[gl] = __half2float(__ushort_as_half(scl[g * SCLN + gl]));
+        s_hi[gl] = __half2float(__ushort_as_half(scl[(g + 8) * SCLN + gl]));
+    }
+#pragma unroll
+    for (int cg = 0; cg < 4; ++cg) {
+        if (cg >= ncg) break;
+        const uint2 *dg = reinterpret_cast<const uint2 *>(recs + (tsB[cg] >= 0 ? tsB[cg] : 0) * RSTRIDE);
+        uint2 bf[GPC][2];
+#pragma unroll
+        for (int gl = 0; gl < GPC; ++gl)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) bf[gl][h] = tsB[cg] >= 0 ? dg[(((g0 + gl) * 2 + h) * 4 + q) * 3 + d] : make_uint2(0u, 0u);
+        int c4[GPC][4];
+#pragma unroll
+        for (int gl = 0; gl < GPC; ++gl) c4[gl][0] = c4[gl][1] = c4[gl][2] = c4[gl][3] = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int gl = 0; gl < GPC; ++gl) {
+                const unsigned wl = w[gl >> 1][(gl & 1) ? 2 : 0], wh = w[gl >> 1][(gl & 1) ? 3 : 1];
+                imma(c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                     (wh >> (4 * h + 2)) & 0x03030303u, bf[gl][h].x, bf[gl][h].y);
+            }
+        const int *xsr = reinterpret_cast<const int *>(recs + (tsC[cg] >= 0 ? tsC[cg] : 0) * RSTRIDE + sum_off) + g0;
+#pragma unroll
+        for (int gl = 0; gl < GPC; ++gl) {
+            const int d2lo = __shfl_down_sync(0xffffffffu, c4[gl][0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[gl][2], 1);
+            const int xs = xsr[gl];
+            acc[cg][0] = fmaf(s_lo[gl], (float)(c4[gl][0] + 256 * c4[gl][1] + 65536 * d2lo - xs), acc[cg][0]);
+            acc[cg][1] = fmaf(s_hi[gl], (float)(c4[gl][2] + 256 * c4[gl][3] + 65536 * d2hi - xs), acc[cg][1]);
+        }
+    }
+}
+
+template <int H, int F>
+__global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constant__ Params P) {
+    using Gm = MGeo<H, F>;
+    using RX = Rec<H>;
+    using RH = Rec<F>;
+    constexpr int NG = Gm::NG, NJ = Gm::NJ, CPT = Gm::CPT, SGU = Gm::SGU, RW = Gm::RW, RTW = Gm::RTW, DTW = Gm::DTW;
+    constexpr int GU_CHUNKS = Gm::GU_CHUNKS, CHUNKS = Gm::CHUNKS;
+    extern __shared__ unsigned char smem_raw[];
+    auto &S = *reinterpret_cast<Smem<H, F> *>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
+    const MoeLayerDev &L = P.L;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
+    const int G = gridDim.x, cta = blockIdx.x;
+    const int B = P.tokens, K = L.topK, E = L.experts, P2 = B * K, SG = (B + kSharedGroup - 1) / kSharedGroup;
+    const long long d_scales_b = 3LL * F * H / 4 + 2LL * F * (H / 64) * 2;
+
+    if (tid == 0) {
+        for (int w = 0; w < kWarps; ++w)
+            for (int s = 0; s < SGU; ++s) mbar_init(&S.bar[w][s], 1);
+        mbar_init(&S.bar_x, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        S.abort_flag = 0;
+        for (int i = 0; i < 2; ++i) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.gu[i])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.gs[i])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.dc[i])) : "memory");
+        }
+    }
+    for (int e = tid; e < E; e += kThreads) S.run[e] = 0;
+    __syncthreads();
+
+    // ------------------------------------------------------------------ A1: digit records of tokens cta, cta + G, ...
+    for (int t = cta; t < B; t += G) {
+        const float *xt = P.x + (long long)t * H;
+        unsigned char *rec = P.xrec + (long long)t * RX::BYTES;
+        if (tid == 0) S.xmax = 0u;
+        __syncthreads();
+        float mx = 0.0f;  // largest |x| (NaN ignored, as fmaxf; max is order-free)
+        for (int i = tid; i < H / 4; i += kThreads) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(xt) + i);
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+#pragma unroll
+        for (int s = 16; s > 0; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+        if (lane == 0) atomicMax(&S.xmax, __float_as_uint(mx));
+        __syncthreads();
+        const int k = scale_exp(__uint_as_float(S.xmax));
+        const float mul = pow2f(k);  // exact power of two
+        // blocks of 16 elements (group, q), one per thread; NG * 4 is a multiple of 32, so whole
+        // warps take part and the group-sum shuffles see all four blocks of a group
+        for (int b = tid; b < NG * 4; b += kThreads) {
+            const int grp = b >> 2, qq = b & 3;
+            const float4 *src = reinterpret_cast<const float4 *>(xt + 64 * grp + 16 * qq);
+            int v[16];
+            int part = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 f = __ldg(src + i);
+                v[4 * i] = __float2int_rn(f.x * mul);
+                v[4 * i + 1] = __float2int_rn(f.y * mul);
+                v[4 * i + 2] = __float2int_rn(f.z * mul);
+                v[4 * i + 3] = __float2int_rn(f.w * mul);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) part += v[i];
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            uint2 *dg = reinterpret_cast<uint2 *>(rec);
+            block_frags(v, dg + ((grp * 2 + 0) * 4 + qq) * 3, dg + ((grp * 2 + 1) * 4 + qq) * 3);
+            if (qq == 0) reinterpret_cast<int *>(rec + RX::SUM)[grp] = part;
+        }
+        if (tid == 0) *reinterpret_cast<float *>(rec + RX::SCALE) = pow2f(-k);
+        __syncthreads();
+    }
+    const int n_rec_ctas = min(G, B);  // CTAs that write records
+    if (cta < B && tid == 0) {         // the records are read by bulk copies (async proxy) on other SMs
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        atomicAdd(&P.sync[0], 1u);
+    }
+
+    // ------------------------------------------------------------------ A2: pair table, token groups
+    for (int p = tid; p < P2; p += kThreads) {
+        const int e = __ldg(P.ids + p);
+        S.ids[p] = e;
+        if (e >= 0 && e < E) atomicAdd(&S.run[e], 1);
+    }
+    for (int t = tid; t < B; t += kThreads) S.sgw[t] = ref_sigmoid(__ldg(P.sg + t));
+    __syncthreads();
+    {
+        int c[2], ng[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int e = 2 * tid + i;
+            c[i] = e < E ? S.run[e] : 0;
+            ng[i] = (c[i] + kMaxTokens - 1) / kMaxTokens;
+        }
+        scan2(S, c, ng, E, S.off, S.gstart, SG);
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kThreads) S.run[e] = S.off[e];  // placement cursors
+    __syncthreads();
+    if (warp == 0) {  // stable placement, 32 pairs at a time in pair order
+        for (int base = 0; base < P2; base += 32) {
+            const int p = base + lane;
+            const int e = p < P2 ? S.ids[p] : -1;
+            const bool valid = e >= 0 && e < E;
+            const unsigned same = __match_any_sync(0xffffffffu, valid ? e : -1 - lane);
+            const int rank = __popc(same & ((1u << lane) - 1u));
+            if (valid) S.pairs[S.run[e] + rank] = (short)p;
+            __syncwarp();
+            if (valid && rank == __popc(same) - 1) S.run[e] += __popc(same);  // the last lane of each expert advances its cursor
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    const int NU = S.gstart[E];
+    const int n_units = cta < NU ? (NU - 1 - cta) / G + 1 : 0;
+
+    // ------------------------------------------------------------------ copy pipeline (per warp)
+    int issued = 0, done = 0;
+    const int known = n_units * CHUNKS;
+    bool stalled = false;          // this warp saw a wait time out: issue nothing more
+    int memo_gi = -1, memo_e = 0;  // the last routed group looked up
+    // unit ui -> token group gi, map m (1: shared expert), expert e, group index tg within it
+    auto unit_of = [&](int ui, int &gi, int &m, int &e, int &tg) {
+        gi = cta + ui * G;
+        if (gi < SG) {
+            m = 1;
+            e = 0;
+            tg = gi;
+            return;
+        }
+        if (gi != memo_gi) {
+            int lo = 0, hi = E;  // the expert with gstart[e] <= gi < gstart[e + 1]
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (S.gstart[mid] <= gi) lo = mid;
+                else hi = mid;
+            }
+            memo_gi = gi;
+            memo_e = lo;
+        }
+        m = 0;
+        e = memo_e;
+        tg = gi - S.gstart[e];
+    };
+    auto blob_of = [&](int m, int e) {
+        return reinterpret_cast<const unsigned char *>(m ? L.shared_blob : L.blobs + (long long)e * L.blob_words);
+    };
+    // chunk c of this warp: unit c / CHUNKS; within it, the gate/up chunks (tile i, column chunk
+    // sub) first, then the down tiles
+    auto issue = [&](int c) {
+        const int ui = c / CHUNKS, idx = c % CHUNKS, st = c % SGU;
+        int gi, m, e, tg;
+        unit_of(ui, gi, m, e, tg);
+        if (lane == 0) {
+            unsigned long long *bar = &S.bar[warp][st];
+            if (idx < GU_CHUNKS) {
+                const int tile = warp + kWarps * (idx / CPT), sub = idx % CPT;
+                mbar_expect(bar, 2048 + 256);
+                tma_3d(S.codes[warp][st], &P.maps.gu[m], 128 * sub, 16 * tile, e, bar);
+                tma_3d(S.scl[warp][st], &P.maps.gs[m], 16 * sub, 16 * tile, e, bar);  // [16 rows][8 groups]
+            } else {
+                const int row0 = RW * warp + 16 * (idx - GU_CHUNKS);
+                mbar_expect(bar, 16 * Gm::DROW + 32 * NJ);
+                tma_3d(S.codes[warp][st], &P.maps.dc[m], 0, row0, e, bar);
+                bulk_copy(S.scl[warp][st], blob_of(m, e) + d_scales_b + (long long)row0 * NJ * 2, 32 * NJ, bar);  // [16 rows][NJ]
+            }
+        }
+    };
+    auto pump = [&]() {  // stages being refilled were last read through the generic proxy: order before the copies
+        if (stalled) return;
+        if (issued < known && issued < done + SGU) {
+            __syncwarp();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            while (issued < known && issued < done + SGU) issue(issued++);
+            __syncwarp();
+        }
+    };
+    auto wait_bar = [&](unsigned long long *bar, unsigned parity) -> bool {
+        for (unsigned long long i = 0;; ++i) {
+            if (mbar_try(bar, parity)) return true;
+            if (i > P.spin_limit) return false;
+        }
+    };
+    auto fail_wait = [&]() {  // warp-uniform: callers vote on the wait result
+        stalled = true;
+        atomicOr(&S.abort_flag, 1);
+    };
+    auto take = [&]() -> int {  // the next chunk's stage once it has landed, -1 after a timeout
+        const int c = done, st = c % SGU;
+        if (!stalled && !__all_sync(0xffffffffu, wait_bar(&S.bar[warp][st], (c / SGU) & 1))) fail_wait();
+        return stalled ? -1 : st;
+    };
+    auto release = [&]() {
+        ++done;
+        pump();
+    };
+    // Token slots of unit ui (warp 0): partial rows and weights (by unit parity), and lane n's
+    // bulk copy of slot n's x digit record. Called once every warp has finished reading the x
+    // digits of the unit before.
+    auto stage_unit = [&](int ui) {
+        int gi, m, e, tg;
+        unit_of(ui, gi, m, e, tg);
+        const int n = m ? min(kSharedGroup, B - kSharedGroup * tg) : min(kMaxTokens, S.off[e + 1] - S.off[e] - kMaxTokens * tg);
+        const int buf = ui & 1;
+        int tok = 0;
+        if (lane < n) {
+            if (m) {
+                tok = kSharedGroup * tg + lane;
+                S.urow[buf][lane] = P2 + tok;
+                S.uw[buf][lane] = S.sgw[tok];
+            } else {
+                const int pr = S.pairs[S.off[e] + kMaxTokens * tg + lane];
+                tok = pr / K;
+                S.urow[buf][lane] = pr;
+                S.uw[buf][lane] = __ldg(P.weights + pr);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_expect(&S.bar_x, (unsigned)(n * RX::BYTES));
+        }
+        __syncwarp();
+        if (lane < n) bulk_copy(S.xrec[lane], P.xrec + (long long)tok * RX::BYTES, RX::BYTES, &S.bar_x);
+    };
+
+    pump();  // weights need no digits: the first unit's copies start now
+
+    // ------------------------------------------------------------------ arrival: digit records
+    if (tid == 0) {
+        for (unsigned long long i = 0;; ++i) {
+            if (ld_acquire(&P.sync[0]) >= (unsigned)n_rec_ctas) break;
+            if (i > P.spin_limit) {
+                S.abort_flag = 1;
+                break;
+            }
+            __nanosleep(32);
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");  // the records are read by bulk copies
+    }
+    __syncthreads();
+    if (S.abort_flag) stalled = true;
+    int x_staged = -1;  // the last unit whose x digits were requested (the same on every thread)
+    if (n_units > 0 && !stalled) {
+        if (warp == 0) stage_unit(0);
+        x_staged = 0;
+    }
+
+    // ------------------------------------------------------------------ units
+    constexpr int NCG = 4;
+    for (int ui = 0; ui < n_units; ++ui) {
+        int gi, m, e, tg;
+        unit_of(ui, gi, m, e, tg);
+        const int n_cur = m ? min(kSharedGroup, B - kSharedGroup * tg) : min(kMaxTokens, S.off[e + 1] - S.off[e] - kMaxTokens * tg);
+        const int ncg = (n_cur + 1) / 2, buf = ui & 1;
+        int tsB[NCG], tsC[NCG];
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg) {
+            const int b = 2 * cg + (g >> 2), c = 2 * cg + (q >> 1);
+            tsB[cg] = (g & 3) < 3 && b < n_cur ? b : -1;
+            tsC[cg] = c < n_cur ? c : -1;
+        }
+        if (!stalled && !__all_sync(0xffffffffu, wait_bar(&S.bar_x, ui & 1))) fail_wait();  // the slots' x digits
+
+        // gate/up: tiles warp + 8 i; a tile holds 8 hidden values (rows 2h, 2h+1 interleaved)
+        float hmax[NCG];
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg) hmax[cg] = 0.0f;
+        for (int i = 0; i < RTW; ++i) {
+            const int tile = warp + kWarps * i;
+            float acc[NCG][2];
+#pragma unroll
+            for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
+            for (int sub = 0; sub < CPT; ++sub) {
+                const int st = take();
+                if (st >= 0)
+                    mma_chunk<8, true, 128, 8, RX::STRIDE>(smem_u32(S.codes[warp][st]), S.scl[warp][st], &S.xrec[0][0], RX::SUM, 8 * sub, tsB,
+                                                           tsC, ncg, acc);
+                release();
+            }
+            // lanes with even q hold token slot 2cg + q/2; row g (gate when g is even) pairs with
+            // row g+1 (up) four lanes down: hidden 8 tile + g/2 (+4 for row g+8)
+#pragma unroll
+            for (int cg = 0; cg < NCG; ++cg) {
+                if (cg >= ncg) break;
+                const float sc = tsC[cg] >= 0 ? *reinterpret_cast<const float *>(S.xrec[tsC[cg]] + RX::SCALE) : 0.0f;
+                const float gv0 = acc[cg][0] * sc, gv1 = acc[cg][1] * sc;
+                const float up0 = __shfl_down_sync(0xffffffffu, gv0, 4), up1 = __shfl_down_sync(0xffffffffu, gv1, 4);
+                if (!(q & 1) && !(g & 1) && tsC[cg] >= 0) {
+                    const float h0 = __fmul_rn(ref_silu(gv0), up0), h1 = __fmul_rn(ref_silu(gv1), up1);
+                    S.hid[tsC[cg]][8 * tile + (g >> 1)] = h0;
+                    S.hid[tsC[cg]][8 * tile + 4 + (g >> 1)] = h1;
+                    hmax[cg] = fmaxf(hmax[cg], fmaxf(fabsf(h0), fabsf(h1)));  // NaN ignored, as fmaxf
+                }
+            }
+        }
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg) {
+            if (cg >= ncg) break;
+            float mh = hmax[cg];
+            mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 4));
+            mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 8));
+            mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 16));
+            if (g == 0 && !(q & 1) && tsC[cg] >= 0) S.hmaxw[warp][tsC[cg]] = mh;
+        }
+        if (__syncthreads_or(stalled ? 1 : 0)) break;  // a warp's copies timed out: all leave together
+        if (ui + 1 < n_units) {                       // every warp is done with this unit's x digits
+            if (warp == 0) stage_unit(ui + 1);
+            x_staged = ui + 1;
+        }
+
+        // hidden -> digit records: blocks of 16 values (slot, group, q), 32 per warp iteration
+        for (int b0 = warp * 32; b0 < n_cur * NJ * 4; b0 += kThreads) {
+            const int b = b0 + lane;
+            const bool live = b < n_cur * NJ * 4;
+            const int ts = live ? b / (NJ * 4) : 0, grp = (b >> 2) % NJ, qq = b & 3;
+            float mx = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, S.hmaxw[w][ts]);
+            const int k = scale_exp(mx);
+            const float mul = pow2f(k);
+            int v[16];
+            int part = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                v[i] = live ? __float2int_rn(S.hid[ts][64 * grp + 16 * qq + i] * mul) : 0;
+                part += v[i];
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            if (live) {
+                unsigned char *rec = S.hrec[ts];
+                uint2 *dg = reinterpret_cast<uint2 *>(rec);
+                block_frags(v, dg + ((grp * 2 + 0) * 4 + qq) * 3, dg + ((grp * 2 + 1) * 4 + qq) * 3);
+                if (qq == 0) reinterpret_cast<int *>(rec + RH::SUM)[grp] = part;
+                if (grp == 0 && qq == 0) *reinterpret_cast<float *>(rec + RH::SCALE) = pow2f(-k);
+            }
+        }
+        __syncthreads();
+
+        // down: rows RW warp + 16 dt (+ g, + g + 8); lanes with even q hold token slot 2cg + q/2
+        float wsc[NCG];
+        int prow[NCG];
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg) {
+            wsc[cg] = tsC[cg] >= 0 ? *reinterpret_cast<const float *>(S.hrec[tsC[cg]] + RH::SCALE) * S.uw[buf][tsC[cg]] : 0.0f;
+            prow[cg] = tsC[cg] >= 0 ? S.urow[buf][tsC[cg]] : 0;
+        }
+        for (int dt = 0; dt < DTW; ++dt) {
+            float acc[NCG][2];
+#pragma unroll
+            for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
+            const int st = take();
+            if (st >= 0)
+                mma_chunk<NJ, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(smem_u32(S.codes[warp][st]), S.scl[warp][st], &S.hrec[0][0], RH::SUM,
+                                                                         0, tsB, tsC, ncg, acc);
+            release();
+            const int row = RW * warp + 16 * dt + g;
+#pragma unroll
+            for (int cg = 0; cg < NCG; ++cg) {
+                if (cg >= ncg) break;
+                if (!(q & 1) && tsC[cg] >= 0) {
+                    float *pr = P.part + (long long)prow[cg] * H + row;
+                    __stcg(pr, acc[cg][0] * wsc[cg]);
+                    __stcg(pr + 8, acc[cg][1] * wsc[cg]);
+                }
+            }
+        }
+    }
+
+    // ------------------------------------------------------------------ second arrival: y
+    for (int c = done; c < issued; ++c) wait_bar(&S.bar[warp][c % SGU], (c / SGU) & 1);
+    if (x_staged >= 0) wait_bar(&S.bar_x, x_staged & 1);  // no copy may be in flight at exit
+    if (stalled) atomicOr(&S.abort_flag, 1);
+    __syncthreads();
+    if (tid == 0 && !grid_arrive_wait(&P.sync[1], (unsigned)G, P.spin_limit)) S.abort_flag = 1;
+    __syncthreads();
+    if (!S.abort_flag) {
+        // y[t][r]: the K + 1 terms of one float4 column (the shared expert, then the routed pairs
+        // in selection order; a pair without an expert adds zero): lane l adds terms l and l + 32,
+        // then a fixed shuffle tree. Four items of a warp at once: their loads are all in flight.
+        const int H4 = H / 4, NT = K + 1;
+        const float4 *part4 = reinterpret_cast<const float4 *>(P.part);
+        constexpr int NB = 4;
+        const int stride = G * kWarps;
+        auto term = [&](int t, int mm, int c, bool in) -> float4 {
+            const int row = mm == 0 ? P2 + t : t * K + mm - 1;
+            const bool ok = in && mm < NT && (mm == 0 || (unsigned)S.ids[t * K + mm - 1] < (unsigned)E);
+            return ok ? __ldcg(part4 + (long long)row * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        };
+        for (int item0 = cta * kWarps + warp; item0 < B * H4; item0 += NB * stride) {
+            float4 u[NB][2];
+#pragma unroll
+            for (int n = 0; n < NB; ++n) {
+                const int item = item0 + n * stride, t = min(item / H4, B - 1), c = item % H4;  // t clamped: past the end, nothing is read
+                u[n][0] = term(t, lane, c, item < B * H4);
+                u[n][1] = term(t, lane + 32, c, item < B * H4);
+            }
+#pragma unroll
+            for (int n = 0; n < NB; ++n) {
+                float4 a = u[n][0];
+                a.x += u[n][1].x;
+                a.y += u[n][1].y;
+                a.z += u[n][1].z;
+                a.w += u[n][1].w;
+#pragma unroll
+                for (int sft = 16; sft > 0; sft >>= 1) {
+                    a.x += __shfl_xor_sync(0xffffffffu, a.x, sft);
+                    a.y += __shfl_xor_sync(0xffffffffu, a.y, sft);
+                    a.z += __shfl_xor_sync(0xffffffffu, a.z, sft);
+                    a.w += __shfl_xor_sync(0xffffffffu, a.w, sft);
+                }
+                const int item = item0 + n * stride;
+                if (lane == 0 && item < B * H4) reinterpret_cast<float4 *>(P.y)[item] = a;
+            }
+        }
+    }
+
+    // ------------------------------------------------------------------ exit
+    __syncthreads();
+    if (tid == 0) {
+        if (S.abort_flag) raise_error(P.err, kErrWaitTimeout);
+        __threadfence();
+        const unsigned prev = atomicAdd(&P.sync[2], 1u);
+        if (prev == (unsigned)G - 1) {  // last CTA out resets the arrival counters for the next launch
+            P.sync[0] = 0;
+            P.sync[1] = 0;
+            __threadfence();
+            P.sync[2] = 0;
+        }
+    }
+}
+
+}  // namespace medium
+
+size_t moe_medium_scratch_bytes(int tokens, int width, int ff, int experts, int topK) {
+    auto a = [](size_t n) { return (n + 255) & ~size_t(255); };
+    const size_t rec = width == 2048 ? medium::Rec<2048>::BYTES : medium::Rec<2560>::BYTES;
+    return a(sizeof(float) * tokens * experts) + a(sizeof(float) * tokens) + a(moe_logits_tail_bytes(width)) + a(rec * tokens) +
+           a(sizeof(float) * (size_t)(tokens * topK + tokens) * width);
+}
+
+bool moe_medium_supported(int tokens, int width, int ff, int experts, int topK, int grid) {
+    return tokens > q2::kMaxTokens && tokens <= medium::kMaxBatch && topK >= 1 && topK <= medium::kMaxTopK && experts >= 1 &&
+           experts <= medium::kMaxExperts && grid >= 1 && ((width == 2048 && ff == 512) || (width == 2560 && ff == 640));
+}
+
+namespace {
+
+template <int H, int F>
+cudaError_t launch_medium(const medium::Params &p, int grid, cudaStream_t s) {
+    const size_t smem = sizeof(medium::Smem<H, F>) + 1024;  // + slack for the 1024-byte stage alignment
+    static int device_ready = -1;
+    int dev = 0;
+    STRATA_CUDA_TRY(cudaGetDevice(&dev));
+    if (device_ready != dev) {
+        STRATA_CUDA_TRY(cudaFuncSetAttribute(medium::k_moe_medium<H, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        device_ready = dev;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(q2::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // the grid arrivals need every CTA resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, medium::k_moe_medium<H, F>, p);
+}
+
+}  // namespace
+
+cudaError_t moe_forward_medium(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
+                               unsigned *sync, int grid, cudaStream_t s, unsigned *err) {
+    char *p = static_cast<char *>(scratch);
+    auto a = [](size_t n) { return (n + 255) & ~size_t(255); };
+    float *logits = reinterpret_cast<float *>(p);
+    p += a(sizeof(float) * tokens * L.experts);
+    float *sg = reinterpret_cast<float *>(p);
+    p += a(sizeof(float) * tokens);
+    float *tail = reinterpret_cast<float *>(p);
+    p += a(moe_logits_tail_bytes(L.width));
+    unsigned char *xrec = reinterpret_cast<unsigned char *>(p);
+    p += a((L.width == 2048 ? medium::Rec<2048>::BYTES : medium::Rec<2560>::BYTES) * (size_t)tokens);
+    float *part = reinterpret_cast<float *>(p);
+    STRATA_CUDA_TRY(moe_route_exact(L, x, tokens, logits, sg, tail, ids, weights, grid, s, err));
+
+    medium::Params prm;
+    std::memset(&prm, 0, sizeof prm);
+    prm.L = L;
+    prm.x = x;
+    prm.tokens = tokens;
+    prm.y = y;
+    prm.ids = ids;
+    prm.weights = weights;
+    prm.sg = sg;
+    prm.xrec = xrec;
+    prm.part = part;
+    prm.sync = sync;
+    prm.err = err;
+    prm.spin_limit = 1ull << 20;  // grid waits sleep 32 ns per try; an mbarrier try suspends for a short, system-defined time
+    if (!moe_tensor_maps(L, &prm.maps)) return cudaErrorInvalidValue;
+    if (L.width == 2048 && L.ff == 512) return launch_medium<2048, 512>(prm, grid, s);
+    if (L.width == 2560 && L.ff == 640) return launch_medium<2560, 640>(prm, grid, s);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace strata

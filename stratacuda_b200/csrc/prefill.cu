@@ -735,6 +735,15 @@ size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int
            al(sizeof(__half) * rows * ff) + al(sizeof(float) * pf::kLgR * width);
 }
 
+size_t moe_logits_tail_bytes(int width) { return sizeof(float) * pf::kLgR * width; }
+
+cudaError_t moe_route_exact(const MoeLayerDev &L, const float *x, int T, float *logits, float *sg, float *tail, int *ids, float *weights,
+                            int grid, cudaStream_t s, unsigned *err) {
+    STRATA_CUDA_TRY(launch_logits(L, x, T, logits, sg, tail, grid, s, err));
+    pf::k_pf_route<<<(T + 3) / 4, 128, 0, s>>>(logits, T, L.experts, L.topK, ids, weights);
+    return cudaGetLastError();
+}
+
 bool moe_prefill_supported(int width, int ff, int experts, int topK) {
     return ((width == 2048 && ff == 512) || (width == 2560 && ff == 640)) && experts <= 512 && topK <= 32;
 }

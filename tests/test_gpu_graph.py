@@ -7,7 +7,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("T", [1, 8, 64])
+@pytest.mark.parametrize("T", [1, 8, 64, 100])
 def test_graph_replay_matches_direct_call(T):
     from stratacuda_b200 import _lib as L
     from stratacuda_b200.backend import CudaBackend, StrataError
@@ -30,7 +30,7 @@ def test_graph_replay_matches_direct_call(T):
         y_graph, ids_graph = b.read(y), b.read(ids)
         b.graph_free(g)
         assert np.array_equal(ids_graph, ids_direct)
-        if T <= 8:  # the fused decode kernel sums y in a fixed order
+        if T <= 64:  # the decode and medium-batch kernels sum y in a fixed order
             assert np.array_equal(y_graph.view(np.uint32), y_direct.view(np.uint32))
         else:  # the prefill path adds with atomics: same routing, y within the path's tolerance
             assert np.linalg.norm(y_graph - y_direct) <= 2e-3 * np.linalg.norm(y_direct)
