@@ -72,9 +72,10 @@ int moe_fast_pdl_state();  // 1: launched with programmatic dependent launch, 0:
 cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
                              unsigned *sync, int grid, cudaStream_t s, unsigned *err);
 
-// TMA maps of a layer's routed experts [0] and shared expert [1], cached by blob address
-// (csrc/moe_fast.cu): gate/up codes (boxes of 16 rows x 128 bytes, 128-byte swizzle), gate/up
-// scales (16 rows x 8 groups) and down codes (16 full rows; 128-byte swizzle for 128-byte rows).
+// TMA maps of the medium-batch layer for a layer's routed experts [0] and shared expert [1],
+// cached by blob address (csrc/moe_fast.cu), all boxes of 128 rows: gate/up codes (128 bytes,
+// 128-byte swizzle), gate/up scales (8 groups) and down codes (full rows; 128-byte swizzle for
+// 128-byte rows).
 struct MoeMaps {
     CUtensorMap gu[2], gs[2], dc[2];
 };

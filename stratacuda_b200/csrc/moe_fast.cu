@@ -929,13 +929,15 @@ bool layer_maps(const MoeLayerDev &L, CUtensorMap *gu2, MoeMaps *all) {
         const unsigned long long ne = i == 0 ? (unsigned long long)L.experts : 1ull;
         if (!map3d(&m.gu[i], base, H / 4, 2 * F, ne, H / 4, bb, 128, 16, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return false;
-        m.all.gu[i] = m.gu[i];
-        // gate/up scales {2 NG bytes, 2F rows}, box {16 bytes = 8 groups, 16 rows}
-        if (!map3d(&m.all.gs[i], base + 3 * F * H / 4, H / 32, 2 * F, ne, H / 32, bb, 16, 16, CU_TENSOR_MAP_SWIZZLE_NONE,
+        // the medium-batch layer copies 128 rows at a time (one box per CTA step)
+        if (!map3d(&m.all.gu[i], base, H / 4, 2 * F, ne, H / 4, bb, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return false;
+        // gate/up scales {2 NG bytes, 2F rows}, box {16 bytes = 8 groups, 128 rows}
+        if (!map3d(&m.all.gs[i], base + 3 * F * H / 4, H / 32, 2 * F, ne, H / 32, bb, 16, 128, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_NONE))
             return false;
-        // down codes {F/4 bytes, H rows}, box {F/4, 16 rows}: 128-byte swizzle for 128-byte rows
-        if (!map3d(&m.all.dc[i], base + 2 * F * H / 4, F / 4, H, ne, F / 4, bb, F / 4, 16,
+        // down codes {F/4 bytes, H rows}, box {F/4, 128 rows}: 128-byte swizzle for 128-byte rows
+        if (!map3d(&m.all.dc[i], base + 2 * F * H / 4, F / 4, H, ne, F / 4, bb, F / 4, 128,
                    F / 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return false;
     }

@@ -32,11 +32,12 @@
 //      every run.
 // Whole experts per unit keep every copy a TMA box of full rows (splitting an expert by hidden
 // columns left 16 bytes of each 128-byte down row per unit: 2,048 small requests per unit,
-// measured 307 us per 64-token layer). Per warp, one ring of SGU stages carries the unit's
-// chunks in order: gate/up chunks (16 rows x 128 bytes of codes, 128-byte swizzle, plus the 16
-// rows' 8 group scales by a second TMA box), then down chunks (16 full rows of codes, plus
-// their scales by one bulk copy). Every wait is bounded: past the limit the kernel records
-// kErrWaitTimeout and leaves.
+// measured 307 us per 64-token layer). The copies run through one CTA-wide ring of NST
+// stages: a step is 128 rows (the 8 warps' 16-row slices side by side), one TMA box of codes
+// (gate/up: 128 bytes of columns, 128-byte swizzle; down: full rows) plus one copy of their
+// scales; thread 0 produces, every warp consumes its slice and frees the stage (per-warp boxes
+// of 16 rows capped the copies near 2 TB/s). Every wait is bounded: past the limit the kernel
+// records kErrWaitTimeout and leaves.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -72,21 +73,21 @@ struct Rec {
     static_assert(BYTES % 16 == 0 && STRIDE % 128 == 96, "record layout");
 };
 
+// A step is 128 rows: the 8 warps' 16-row tiles side by side, one TMA box of codes and one
+// copy of their scales per step.
 template <int H, int F>
 struct MGeo {
-    static constexpr int NG = H / 64;                          // gate/up scale groups per row
-    static constexpr int NJ = F / 64;                          // down scale groups per row
-    static constexpr int CPT = NG / 8;                         // gate/up chunks per 16-row tile
-    static constexpr int RTW = F / 64;                         // gate/up tiles per warp (2F / 16 / 8)
-    static constexpr int RW = H / kWarps;                      // down rows per warp
-    static constexpr int DTW = RW / 16;                        // down tiles per warp
-    static constexpr int GU_CHUNKS = RTW * CPT;                // per warp and unit
-    static constexpr int CHUNKS = GU_CHUNKS + DTW;             // per warp and unit
-    static constexpr int DROW = F / 4;                         // bytes of a down row
-    static constexpr int CODE_STAGE = F == 512 ? 2048 : 3072;  // 1024-aligned (128-byte swizzle)
-    static constexpr int SCL_STAGE = 384;                      // >= 16 rows x NJ x 2 bytes, a multiple of 128
-    static constexpr int SGU = F == 512 ? 6 : 3;               // stages per warp (shared-memory budget)
-    static_assert(NG % 8 == 0 && RW % 16 == 0 && 16 * DROW <= CODE_STAGE && 32 * NJ <= SCL_STAGE, "geometry");
+    static constexpr int NG = H / 64;                // gate/up scale groups per row
+    static constexpr int NJ = F / 64;                // down scale groups per row
+    static constexpr int CPT = NG / 8;               // gate/up column chunks (128 bytes) per row
+    static constexpr int GU_STEPS = (2 * F / 128) * CPT;  // per unit: 128-row blocks x column chunks
+    static constexpr int DN_STEPS = H / 128;         // per unit: 128-row blocks of full down rows
+    static constexpr int STEPS = GU_STEPS + DN_STEPS;
+    static constexpr int DROW = F / 4;               // bytes of a down row
+    static constexpr int STAGE = 128 * DROW > 16384 ? 128 * DROW : 16384;  // codes of a step (1024-aligned)
+    static constexpr int SSTAGE = 128 * (NJ > 8 ? NJ : 8) * 2;            // scales of a step
+    static constexpr int NST = F == 512 ? 6 : 4;     // stages (shared-memory budget)
+    static_assert(NG % 8 == 0 && H % 128 == 0 && STAGE % 1024 == 0 && SSTAGE % 128 == 0, "geometry");
 };
 
 struct Params {
@@ -108,8 +109,8 @@ struct Params {
 template <int H, int F>
 struct Smem {
     using G = MGeo<H, F>;
-    unsigned char codes[kWarps][G::SGU][G::CODE_STAGE];  // 1024-aligned
-    alignas(128) unsigned short scl[kWarps][G::SGU][G::SCL_STAGE / 2];
+    unsigned char codes[G::NST][G::STAGE];  // 1024-aligned
+    alignas(128) unsigned short scl[G::NST][G::SSTAGE / 2];
     alignas(128) unsigned char xrec[kMaxTokens][Rec<H>::STRIDE];  // the unit's tokens: x digits
     alignas(128) unsigned char hrec[kMaxTokens][Rec<F>::STRIDE];  // the unit's tokens: hidden digits
     float hid[kMaxTokens][F];
@@ -124,7 +125,7 @@ struct Smem {
     int urow[2][kMaxTokens];  // unit token slot -> partial row (by unit parity)
     float uw[2][kMaxTokens];  // unit token slot -> weight
     unsigned xmax;
-    unsigned long long bar[kWarps][G::SGU];
+    unsigned long long full[G::NST], empty[G::NST];
     unsigned long long bar_x;
     int abort_flag;
 };
@@ -233,8 +234,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     using Gm = MGeo<H, F>;
     using RX = Rec<H>;
     using RH = Rec<F>;
-    constexpr int NG = Gm::NG, NJ = Gm::NJ, CPT = Gm::CPT, SGU = Gm::SGU, RW = Gm::RW, RTW = Gm::RTW, DTW = Gm::DTW;
-    constexpr int GU_CHUNKS = Gm::GU_CHUNKS, CHUNKS = Gm::CHUNKS;
+    constexpr int NG = Gm::NG, NJ = Gm::NJ, CPT = Gm::CPT, NST = Gm::NST, GU_STEPS = Gm::GU_STEPS, DN_STEPS = Gm::DN_STEPS;
+    constexpr int STEPS = Gm::STEPS;
     extern __shared__ unsigned char smem_raw[];
     auto &S = *reinterpret_cast<Smem<H, F> *>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
     const MoeLayerDev &L = P.L;
@@ -244,8 +245,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     const long long d_scales_b = 3LL * F * H / 4 + 2LL * F * (H / 64) * 2;
 
     if (tid == 0) {
-        for (int w = 0; w < kWarps; ++w)
-            for (int s = 0; s < SGU; ++s) mbar_init(&S.bar[w][s], 1);
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], kWarps);
+        }
         mbar_init(&S.bar_x, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.abort_flag = 0;
@@ -346,10 +349,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     const int NU = S.gstart[E];
     const int n_units = cta < NU ? (NU - 1 - cta) / G + 1 : 0;
 
-    // ------------------------------------------------------------------ copy pipeline (per warp)
-    int issued = 0, done = 0;
-    const int known = n_units * CHUNKS;
-    bool stalled = false;          // this warp saw a wait time out: issue nothing more
+    // ------------------------------------------------------------------ copy pipeline (CTA-wide ring)
+    // Step c of this CTA: unit c / STEPS; within it the gate/up steps (128-row block, column
+    // chunk) first, then the down steps. Thread 0 produces (one TMA box of codes + one copy of
+    // scales per step); every warp consumes every step (its 16-row slice) and arrives on the
+    // stage's empty barrier.
+    const int total = n_units * STEPS;
+    int produced = 0, done = 0;    // produced: thread 0's count; done: steps consumed (every warp)
+    bool stalled = false;          // this warp saw a wait time out
     int memo_gi = -1, memo_e = 0;  // the last routed group looked up
     // unit ui -> token group gi, map m (1: shared expert), expert e, group index tg within it
     auto unit_of = [&](int ui, int &gi, int &m, int &e, int &tg) {
@@ -377,36 +384,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     auto blob_of = [&](int m, int e) {
         return reinterpret_cast<const unsigned char *>(m ? L.shared_blob : L.blobs + (long long)e * L.blob_words);
     };
-    // chunk c of this warp: unit c / CHUNKS; within it, the gate/up chunks (tile i, column chunk
-    // sub) first, then the down tiles
-    auto issue = [&](int c) {
-        const int ui = c / CHUNKS, idx = c % CHUNKS, st = c % SGU;
-        int gi, m, e, tg;
-        unit_of(ui, gi, m, e, tg);
-        if (lane == 0) {
-            unsigned long long *bar = &S.bar[warp][st];
-            if (idx < GU_CHUNKS) {
-                const int tile = warp + kWarps * (idx / CPT), sub = idx % CPT;
-                mbar_expect(bar, 2048 + 256);
-                tma_3d(S.codes[warp][st], &P.maps.gu[m], 128 * sub, 16 * tile, e, bar);
-                tma_3d(S.scl[warp][st], &P.maps.gs[m], 16 * sub, 16 * tile, e, bar);  // [16 rows][8 groups]
-            } else {
-                const int row0 = RW * warp + 16 * (idx - GU_CHUNKS);
-                mbar_expect(bar, 16 * Gm::DROW + 32 * NJ);
-                tma_3d(S.codes[warp][st], &P.maps.dc[m], 0, row0, e, bar);
-                bulk_copy(S.scl[warp][st], blob_of(m, e) + d_scales_b + (long long)row0 * NJ * 2, 32 * NJ, bar);  // [16 rows][NJ]
-            }
-        }
-    };
-    auto pump = [&]() {  // stages being refilled were last read through the generic proxy: order before the copies
-        if (stalled) return;
-        if (issued < known && issued < done + SGU) {
-            __syncwarp();
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            while (issued < known && issued < done + SGU) issue(issued++);
-            __syncwarp();
-        }
-    };
     auto wait_bar = [&](unsigned long long *bar, unsigned parity) -> bool {
         for (unsigned long long i = 0;; ++i) {
             if (mbar_try(bar, parity)) return true;
@@ -417,14 +394,45 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         stalled = true;
         atomicOr(&S.abort_flag, 1);
     };
-    auto take = [&]() -> int {  // the next chunk's stage once it has landed, -1 after a timeout
-        const int c = done, st = c % SGU;
-        if (!stalled && !__all_sync(0xffffffffu, wait_bar(&S.bar[warp][st], (c / SGU) & 1))) fail_wait();
+    auto produce = [&]() {  // thread 0: the next step into its stage, once every warp has freed it
+        const int c = produced, st = c % NST;
+        if (c >= NST && !wait_bar(&S.empty[st], ((c / NST) - 1) & 1)) {
+            S.abort_flag = 1;
+            return false;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the stage was read through the generic proxy
+        const int ui = c / STEPS, idx = c % STEPS;
+        int gi, m, e, tg;
+        unit_of(ui, gi, m, e, tg);
+        if (idx < GU_STEPS) {
+            const int blk = idx / CPT, sub = idx % CPT;
+            mbar_expect(&S.full[st], 16384 + 128 * 16);
+            tma_3d(S.codes[st], &P.maps.gu[m], 128 * sub, 128 * blk, e, &S.full[st]);
+            tma_3d(S.scl[st], &P.maps.gs[m], 16 * sub, 128 * blk, e, &S.full[st]);  // [128 rows][8 groups]
+        } else {
+            const int row0 = 128 * (idx - GU_STEPS);
+            mbar_expect(&S.full[st], 128 * Gm::DROW + 128 * NJ * 2);
+            tma_3d(S.codes[st], &P.maps.dc[m], 0, row0, e, &S.full[st]);
+            bulk_copy(S.scl[st], blob_of(m, e) + d_scales_b + (long long)row0 * NJ * 2, 128 * NJ * 2, &S.full[st]);  // [128 rows][NJ]
+        }
+        ++produced;
+        return true;
+    };
+    auto take = [&]() -> int {  // the next step's stage once it has landed, -1 after a timeout
+        const int c = done, st = c % NST;
+        if (!stalled && !__all_sync(0xffffffffu, wait_bar(&S.full[st], (c / NST) & 1))) fail_wait();
         return stalled ? -1 : st;
     };
+    // this warp is done with step `done`; thread 0 then refills the stage freed two steps ago
+    // (waiting there for the slowest warp, not for the step just read)
     auto release = [&]() {
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&S.empty[done % NST])) : "memory");
         ++done;
-        pump();
+        if (tid == 0 && !stalled && done >= 2 && produced < total && produced < done + NST - 2 + 1) {
+            if (!produce()) stalled = true;
+        }
+        __syncwarp();
     };
     // Token slots of unit ui (warp 0): partial rows and weights (by unit parity), and lane n's
     // bulk copy of slot n's x digit record. Called once every warp has finished reading the x
@@ -456,7 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         if (lane < n) bulk_copy(S.xrec[lane], P.xrec + (long long)tok * RX::BYTES, RX::BYTES, &S.bar_x);
     };
 
-    pump();  // weights need no digits: the first unit's copies start now
+    if (tid == 0)  // weights need no digits: the first steps' copies start now
+        for (int i = 0; i < NST && i < total; ++i) produce();
 
     // ------------------------------------------------------------------ arrival: digit records
     if (tid == 0) {
@@ -498,16 +507,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         float hmax[NCG];
 #pragma unroll
         for (int cg = 0; cg < NCG; ++cg) hmax[cg] = 0.0f;
-        for (int i = 0; i < RTW; ++i) {
-            const int tile = warp + kWarps * i;
+        for (int i = 0; i < 2 * F / 128; ++i) {
+            const int tile = warp + kWarps * i;  // rows 16 tile .. 16 tile + 15: this warp's slice of block i
             float acc[NCG][2];
 #pragma unroll
             for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
             for (int sub = 0; sub < CPT; ++sub) {
                 const int st = take();
                 if (st >= 0)
-                    mma_chunk<8, true, 128, 8, RX::STRIDE>(smem_u32(S.codes[warp][st]), S.scl[warp][st], &S.xrec[0][0], RX::SUM, 8 * sub, tsB,
-                                                           tsC, ncg, acc);
+                    mma_chunk<8, true, 128, 8, RX::STRIDE>(smem_u32(S.codes[st]) + 2048 * warp, S.scl[st] + 16 * 8 * warp, &S.xrec[0][0],
+                                                           RX::SUM, 8 * sub, tsB, tsC, ncg, acc);
                 release();
             }
             // lanes with even q hold token slot 2cg + q/2; row g (gate when g is even) pairs with
@@ -570,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         }
         __syncthreads();
 
-        // down: rows RW warp + 16 dt (+ g, + g + 8); lanes with even q hold token slot 2cg + q/2
+        // down: rows 128 dt + 16 warp (+ g, + g + 8); lanes with even q hold token slot 2cg + q/2
         float wsc[NCG];
         int prow[NCG];
 #pragma unroll
@@ -578,16 +587,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
             wsc[cg] = tsC[cg] >= 0 ? *reinterpret_cast<const float *>(S.hrec[tsC[cg]] + RH::SCALE) * S.uw[buf][tsC[cg]] : 0.0f;
             prow[cg] = tsC[cg] >= 0 ? S.urow[buf][tsC[cg]] : 0;
         }
-        for (int dt = 0; dt < DTW; ++dt) {
+        for (int dt = 0; dt < DN_STEPS; ++dt) {
             float acc[NCG][2];
 #pragma unroll
             for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
             const int st = take();
             if (st >= 0)
-                mma_chunk<NJ, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(smem_u32(S.codes[warp][st]), S.scl[warp][st], &S.hrec[0][0], RH::SUM,
-                                                                         0, tsB, tsC, ncg, acc);
+                mma_chunk<NJ, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(smem_u32(S.codes[st]) + 16 * Gm::DROW * warp, S.scl[st] + 16 * NJ * warp,
+                                                                         &S.hrec[0][0], RH::SUM, 0, tsB, tsC, ncg, acc);
             release();
-            const int row = RW * warp + 16 * dt + g;
+            const int row = 128 * dt + 16 * warp + g;
 #pragma unroll
             for (int cg = 0; cg < NCG; ++cg) {
                 if (cg >= ncg) break;
@@ -601,7 +610,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     }
 
     // ------------------------------------------------------------------ second arrival: y
-    for (int c = done; c < issued; ++c) wait_bar(&S.bar[warp][c % SGU], (c / SGU) & 1);
+    if (tid == 0)  // no copy may be in flight at exit
+        for (int c = done; c < produced; ++c) wait_bar(&S.full[c % NST], (c / NST) & 1);
     if (x_staged >= 0) wait_bar(&S.bar_x, x_staged & 1);  // no copy may be in flight at exit
     if (stalled) atomicOr(&S.abort_flag, 1);
     __syncthreads();
