@@ -121,10 +121,13 @@ typedef struct {
  * routed ids (i32 [tokens * top_k]) and weights (f32 [tokens * top_k]). Routing is
  * bit-identical to strata_router_batch; y follows the reference's combine order.
  *   mode 0: exact — every dot product in the reference's reduction order (bit-identical y).
- *   mode 1: fast — one persistent tensor-core launch for decode batches (tokens <= 8 at
- *           H/F = 2048/512 or 2560/640; other shapes run the exact mode). Routing is still
- *           bit-identical; y is within 1e-5 relative L2 and, being accumulated with atomics,
- *           not bit-reproducible from run to run.
+ *   mode 1: fast — at H/F = 2048/512 or 2560/640 (other shapes run the exact mode):
+ *           tokens <= 8: one persistent integer tensor-core launch (decode);
+ *           9 .. 64: the exact router kernels, then one integer tensor-core launch;
+ *           above 64: the tcgen05 prefill path (FP16 operands).
+ *           Routing is still bit-identical. y is within 1e-5 relative L2 up to 64 tokens and
+ *           the same bits run to run (fixed summation order); within 2e-3 above 64 tokens,
+ *           where the GEMM epilogues add with atomics.
  * Stream-ordered; does not synchronise. */
 #define STRATA_MOE_EXACT 0
 #define STRATA_MOE_FAST 1
