@@ -620,10 +620,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     if (!S.abort_flag) {
         // y[t][r]: the K + 1 terms of one float4 column (the shared expert, then the routed pairs
         // in selection order; a pair without an expert adds zero): lane l adds terms l and l + 32,
-        // then a fixed shuffle tree. Four items of a warp at once: their loads are all in flight.
+        // then a fixed shuffle tree. Eight items of a warp at once: their loads are all in flight.
         const int H4 = H / 4, NT = K + 1;
         const float4 *part4 = reinterpret_cast<const float4 *>(P.part);
-        constexpr int NB = 4;
+        constexpr int NB = 8;
         const int stride = G * kWarps;
         auto term = [&](int t, int mm, int c, bool in) -> float4 {
             const int row = mm == 0 ? P2 + t : t * K + mm - 1;

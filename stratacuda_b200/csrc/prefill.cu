@@ -88,7 +88,7 @@ __global__ void k_lg_tail(const float *router, const float *gate, int E, int H, 
 }
 
 __global__ void __launch_bounds__(kLgThreads, 1)
-    k_pf_logits(const __grid_constant__ LgMaps M, MoeLayerDev L, int T, int ST, float *logits, float *sg, unsigned *err,
+    k_pf_logits(const __grid_constant__ LgMaps M, MoeLayerDev L, int T, int ST, int group, float *logits, float *sg, unsigned *err,
                 unsigned long long spin_limit) {
     extern __shared__ unsigned char lg_raw[];
     unsigned char *base = lg_raw + ((1024 - (su32(lg_raw) & 1023)) & 1023);
@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
     float *ws = xs + (size_t)NC * kLgT * kLgKC;         // [ST][kLgR][256]
     LgBars &B = *reinterpret_cast<LgBars *>(ws + (size_t)ST * kLgR * kLgKC);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_full = E / kLgR, n_rt = n_full + 1, n_grp = (n_rt + kLgGroup - 1) / kLgGroup;
+    const int n_full = E / kLgR, n_rt = n_full + 1, n_grp = (n_rt + group - 1) / group;
     const int n_items = ((T + kLgT - 1) / kLgT) * n_grp;
     if (tid == 0) {
         for (int i = 0; i < ST; ++i) {
@@ -127,8 +127,8 @@ __global__ void __launch_bounds__(kLgThreads, 1)
             int g = 0, it = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-                const int t0 = (item / n_grp) * kLgT, rt0 = (item % n_grp) * kLgGroup;
-                const int nrt = min(kLgGroup, n_rt - rt0);
+                const int t0 = (item / n_grp) * kLgT, rt0 = (item % n_grp) * group;
+                const int nrt = min(group, n_rt - rt0);
                 for (int rr = 0; rr < nrt && ok; ++rr)
                     for (int c = 0; c < NC && ok; ++c, ++g) {
                         if (rr == 0) {  // the item's x chunk c, once the previous item released it
@@ -155,8 +155,8 @@ __global__ void __launch_bounds__(kLgThreads, 1)
         int g = 0, it = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-            const int t0 = (item / n_grp) * kLgT, rt0 = (item % n_grp) * kLgGroup;
-            const int nrt = min(kLgGroup, n_rt - rt0);
+            const int t0 = (item / n_grp) * kLgT, rt0 = (item % n_grp) * group;
+            const int nrt = min(group, n_rt - rt0);
             for (int rr = 0; rr < nrt && ok; ++rr) {
                 float acc[kLgWT][kLgWR][2];
 #pragma unroll
@@ -651,10 +651,13 @@ cudaError_t launch_logits(const MoeLayerDev &L, const float *x, int T, float *lo
         STRATA_CUDA_TRY(cudaFuncSetAttribute(pf::k_pf_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kLgSmemLimit));
         ready_device = dev;
     }
-    const int n_rt = n_full + 1, n_grp = (n_rt + pf::kLgGroup - 1) / pf::kLgGroup;
-    const long long n_items = (long long)((T + pf::kLgT - 1) / pf::kLgT) * n_grp;
+    // row tiles per work item: kLgGroup share one copy of the item's x; with too few items to
+    // fill the SMs (small batches), one tile per item
+    const int n_rt = n_full + 1, n_tt = (T + pf::kLgT - 1) / pf::kLgT;
+    const int group = (long long)n_tt * ((n_rt + pf::kLgGroup - 1) / pf::kLgGroup) >= sms ? pf::kLgGroup : 1;
+    const long long n_items = (long long)n_tt * ((n_rt + group - 1) / group);
     const int grid = (int)std::min<long long>(n_items, std::max(1, sms));
-    pf::k_pf_logits<<<grid, pf::kLgThreads, pf::logits_smem(H), s>>>(M, L, T, pf::logits_stages(H), logits, sg, err, 1ull << 24);
+    pf::k_pf_logits<<<grid, pf::kLgThreads, pf::logits_smem(H), s>>>(M, L, T, pf::logits_stages(H), group, logits, sg, err, 1ull << 24);
     return cudaGetLastError();
 }
 
