@@ -16,7 +16,9 @@ fresh activation batch per step, so no step reads weights left in L2 by the prev
   value   device time (CUDA events on the library's stream) of K fused steps, inputs
           resident in HBM; whole-job tokens/s (sum over ranks / max time over ranks).
   e2e     the same steps through the C-ABI with host buffers: strata_write of the batch
-          from pinned memory, strata_moe_forward, strata_read of y, host-timed.
+          from pinned memory, the layer call (replayed from its captured CUDA graph with
+          strata_graph_launch; strata_moe_forward itself with --no-graph), strata_read of y,
+          host-timed.
   roofline  algorithmic bytes of each step (the U+1 distinct expert blobs actually routed,
           router rows, shared gate, activations in and out) over the measured step time,
           against the measured HBM copy bandwidth.
@@ -303,18 +305,34 @@ def run_gpu_arm(args, world, rank, local):
     hx_np, hy_np = hx.numpy(), hy.numpy()
     lib, ctx = b.lib, b.ctx
     xbuf, ybuf = xs[0], ys[0]
-    for s in range(min(3, e2e_steps)):
+    # Each layer's call is captured once (the decode-loop pattern of the graph API): a step is
+    # strata_write of the batch from pinned memory, strata_graph_launch of that layer's call,
+    # strata_read of y into pinned memory. --no-graph calls strata_moe_forward every step.
+    e2e_graphs = []
+    if not args.no_graph:
+        for l in range(min(NL, e2e_steps)):
+            b.capture_begin()
+            layers[l].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
+            e2e_graphs.append(b.capture_end())
+
+    def e2e_step(s):
         b.write(xbuf, hx_np[s])
-        layers[s % NL].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
+        if e2e_graphs:
+            b.graph_launch(e2e_graphs[s % len(e2e_graphs)])
+        else:
+            layers[s % NL].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
         b._check(lib.strata_read(ctx, ybuf.handle, hy_np.ctypes.data, B * WIDTH, 0))
+
+    for s in range(min(3, e2e_steps)):
+        e2e_step(s)
     dist_barrier(world)
     t0 = time.perf_counter()
     for s in range(e2e_steps):
-        b.write(xbuf, hx_np[s])
-        layers[s % NL].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
-        b._check(lib.strata_read(ctx, ybuf.handle, hy_np.ctypes.data, B * WIDTH, 0))
+        e2e_step(s)
     e2e_s = time.perf_counter() - t0
     e2e_s = dist_max(e2e_s, world)
+    for g in e2e_graphs:
+        b.graph_free(g)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -334,7 +352,10 @@ def run_gpu_arm(args, world, rank, local):
             "config": workload_config(B, NL, zipf, graph=not args.no_graph),
             "roofline": roofline,
             "e2e": {"value": B * e2e_steps * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * WIDTH * 4,
-                    "d2h_bytes_per_step": B * WIDTH * 4},
+                    "d2h_bytes_per_step": B * WIDTH * 4, "steps": e2e_steps,
+                    "calls": ("strata_write (pinned host) + strata_graph_launch of the layer's captured strata_moe_forward + strata_read "
+                              "(pinned host, synchronising), host-timed" if e2e_graphs or not args.no_graph else
+                              "strata_write (pinned host) + strata_moe_forward + strata_read (pinned host, synchronising), host-timed")},
             "gpu_launches": launches * K,
             "clocks": clocks.summary()}
     if cpu:
