@@ -101,6 +101,16 @@ __device__ __forceinline__ unsigned long long add2_rn(unsigned long long a, unsi
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+// The rounded products of a paired multiply as an FMA with the addend neg0 = (-0, -0): a rounded
+// product plus -0 is that product, bit for bit (a +0 product stays +0). neg0 must reach the kernel
+// at run time (an argument): a literal -0 lets the compiler see a plain multiply and fuse it
+// into the following add (measured: weights off by a few ulps), an unknown addend cannot be.
+__device__ __forceinline__ unsigned long long mul_rn2(unsigned long long a, unsigned long long b, unsigned long long neg0) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(neg0));
+    return d;
+}
+constexpr unsigned long long kNegZero2 = 0x8000000080000000ull;  // the host passes this as neg0
 __device__ __forceinline__ unsigned xor3(unsigned a, unsigned b, unsigned c) {
     unsigned d;
     asm("lop3.b32 %0, %1, %2, %3, 0x96;" : "=r"(d) : "r"(a), "r"(b), "r"(c));

@@ -89,7 +89,7 @@ __global__ void k_lg_tail(const float *router, const float *gate, int E, int H, 
 
 __global__ void __launch_bounds__(kLgThreads, 1)
     k_pf_logits(const __grid_constant__ LgMaps M, MoeLayerDev L, int T, int ST, int group, float *logits, float *sg, unsigned *err,
-                unsigned long long spin_limit) {
+                unsigned long long spin_limit, unsigned long long neg0) {
     extern __shared__ unsigned char lg_raw[];
     unsigned char *base = lg_raw + ((1024 - (su32(lg_raw) & 1023)) & 1023);
     const int H = L.width, E = L.experts, NC = H / kLgKC;
@@ -158,37 +158,38 @@ __global__ void __launch_bounds__(kLgThreads, 1)
             const int t0 = (item / n_grp) * kLgT, rt0 = (item % n_grp) * group;
             const int nrt = min(group, n_rt - rt0);
             for (int rr = 0; rr < nrt && ok; ++rr) {
-                float acc[kLgWT][kLgWR][2];
+                // per (token, row): the two reference lanes' partial sums as one f32 pair (low: lane
+                // 2 l, high: lane 2 l + 1)
+                u64 acc[kLgWT][kLgWR];
 #pragma unroll
                 for (int i = 0; i < kLgWT; ++i)
 #pragma unroll
-                    for (int j = 0; j < kLgWR; ++j) acc[i][j][0] = acc[i][j][1] = 0.0f;
+                    for (int j = 0; j < kLgWR; ++j) acc[i][j] = 0ull;
                 for (int c = 0; c < NC; ++c, ++g) {
                     const int st = g % ST;
                     if (!(ok = __all_sync(0xffffffffu, (rr > 0 || wait(&B.xfull[c], it & 1)) && wait(&B.full[st], (g / ST) & 1)))) break;
                     const float *xb = xs + (size_t)c * kLgT * kLgKC + 2 * lane;
                     const float *wb = ws + (size_t)st * kLgR * kLgKC + 2 * lane;
-                    float2 xv[2][kLgWT], wv[2][kLgWR];
+                    u64 xv[2][kLgWT], wv[2][kLgWR];
 #pragma unroll
-                    for (int i = 0; i < kLgWT; ++i) xv[0][i] = *reinterpret_cast<const float2 *>(xb + (tb + i) * kLgKC);
+                    for (int i = 0; i < kLgWT; ++i) xv[0][i] = *reinterpret_cast<const u64 *>(xb + (tb + i) * kLgKC);
 #pragma unroll
-                    for (int j = 0; j < kLgWR; ++j) wv[0][j] = *reinterpret_cast<const float2 *>(wb + (rb + j) * kLgKC);
+                    for (int j = 0; j < kLgWR; ++j) wv[0][j] = *reinterpret_cast<const u64 *>(wb + (rb + j) * kLgKC);
 #pragma unroll
                     for (int m = 0; m < kLgKC / 64; ++m) {  // elements 2 lane + 64 m and + 1: the two lanes' next terms
                         const int cur = m & 1;
                         if (m + 1 < kLgKC / 64) {
 #pragma unroll
-                            for (int i = 0; i < kLgWT; ++i) xv[cur ^ 1][i] = *reinterpret_cast<const float2 *>(xb + (tb + i) * kLgKC + 64 * (m + 1));
+                            for (int i = 0; i < kLgWT; ++i) xv[cur ^ 1][i] = *reinterpret_cast<const u64 *>(xb + (tb + i) * kLgKC + 64 * (m + 1));
 #pragma unroll
-                            for (int j = 0; j < kLgWR; ++j) wv[cur ^ 1][j] = *reinterpret_cast<const float2 *>(wb + (rb + j) * kLgKC + 64 * (m + 1));
+                            for (int j = 0; j < kLgWR; ++j) wv[cur ^ 1][j] = *reinterpret_cast<const u64 *>(wb + (rb + j) * kLgKC + 64 * (m + 1));
                         }
+                        // the reference's rounded product then rounded add, two lanes per instruction
+                        // (mul_rn2: an FMA with the run-time addend neg0 = (-0, -0), never fused with the add)
 #pragma unroll
                         for (int i = 0; i < kLgWT; ++i)
 #pragma unroll
-                            for (int j = 0; j < kLgWR; ++j) {
-                                acc[i][j][0] = __fadd_rn(acc[i][j][0], __fmul_rn(wv[cur][j].x, xv[cur][i].x));
-                                acc[i][j][1] = __fadd_rn(acc[i][j][1], __fmul_rn(wv[cur][j].y, xv[cur][i].y));
-                            }
+                            for (int j = 0; j < kLgWR; ++j) acc[i][j] = add2_rn(acc[i][j], mul_rn2(wv[cur][j], xv[cur][i], neg0));
                     }
                     __syncwarp();
                     if (lane == 0) {
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
 #pragma unroll
                 for (int i = 0; i < kLgWT; ++i)
 #pragma unroll
-                    for (int j = 0; j < kLgWR; ++j) v[i * kLgWR + j] = ((u64)__float_as_uint(acc[i][j][1]) << 32) | __float_as_uint(acc[i][j][0]);
+                    for (int j = 0; j < kLgWR; ++j) v[i * kLgWR + j] = acc[i][j];
 #pragma unroll
                 for (int half = 16; half > 0; half >>= 1) {
                     const bool upper = (lane & half) != 0;
@@ -657,7 +658,8 @@ cudaError_t launch_logits(const MoeLayerDev &L, const float *x, int T, float *lo
     const int group = (long long)n_tt * ((n_rt + pf::kLgGroup - 1) / pf::kLgGroup) >= sms ? pf::kLgGroup : 1;
     const long long n_items = (long long)n_tt * ((n_rt + group - 1) / group);
     const int grid = (int)std::min<long long>(n_items, std::max(1, sms));
-    pf::k_pf_logits<<<grid, pf::kLgThreads, pf::logits_smem(H), s>>>(M, L, T, pf::logits_stages(H), group, logits, sg, err, 1ull << 24);
+    pf::k_pf_logits<<<grid, pf::kLgThreads, pf::logits_smem(H), s>>>(M, L, T, pf::logits_stages(H), group, logits, sg, err, 1ull << 24,
+                                                                      kNegZero2);
     return cudaGetLastError();
 }
 
