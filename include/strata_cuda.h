@@ -37,7 +37,7 @@ extern "C" {
 #define STRATA_ERR_HANDLE 4  /* not a live buffer of this context: src/backend.js:138-143 */
 #define STRATA_ERR_ALLOC 5   /* device allocation failed: wasm/runtime.js:7 "WASM allocation failed" */
 #define STRATA_ERR_CUDA 6    /* CUDA runtime error (the message names it) */
-#define STRATA_ERR_DEVICE 7  /* a kernel recorded an out-of-range index, an invalid routing or a timed-out wait */
+#define STRATA_ERR_DEVICE 7  /* a kernel recorded an out-of-range index, an invalid routing, a timed-out wait or a non-finite PLE scale */
 
 #define STRATA_F32 0
 #define STRATA_I32 1
@@ -85,7 +85,7 @@ int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *t
 
 /* ---- dispatch (run, src/backend.js:101-113; validateDispatch :10-56) ----
  * Runs one reference entry of kernels/strata.cu by name with the reference's grid of 64-lane
- * workgroups. Supported names: strata_unpack_half, strata_expert_scales, strata_q2_gate_up,
+ * workgroups. Supported names: strata_unpack_half, strata_expert_scales, strata_ple_decode, strata_q2_gate_up,
  * strata_q2_down, strata_project, strata_bf16_project, strata_q2_project, strata_quant_project,
  * strata_elementwise, strata_router, strata_router_batch, strata_moe_combine,
  * strata_moe_combine_batch, strata_gather_rows, strata_scatter_rows. Results are bit-identical
@@ -176,6 +176,18 @@ int strata_ep_unique_id(strata_ctx *ctx, uint8_t *id, size_t cap);
 int strata_ep_init(strata_ctx *ctx, int32_t rank, int32_t n_ranks, const uint8_t *id);
 int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                           strata_buf weights);
+
+/* ---- per-layer embeddings (PLE) on the device ----
+ * Replaces the host-side row gather of src/model.js:230-242 (plePackedRows) followed by the
+ * strata_ple_decode dispatch of src/ops.js:79-83. The IQ4_NL table (rows of head_dim values,
+ * head_dim / 32 * 18 bytes each: per 32 values an FP16 scale and 16 code bytes) stays resident
+ * in `table` (u32 words); the host still computes the n-gram row ids (src/model.js ngramRows)
+ * and writes them to `ids` (i32). Values[h * head_dim + j] receive exactly what
+ * strata_ple_decode gives for the same rows packed one after another. head_dim must be a
+ * multiple of 32 ("Invalid packed PLE layout"). A row outside the table reads zeros and a
+ * non-finite scale ("Non-finite PLE scales", src/model.js:241) are reported by the next
+ * synchronising call. Stream-ordered. */
+int strata_ple_gather_decode(strata_ctx *ctx, strata_buf table, strata_buf ids, int32_t rows, int32_t head_dim, strata_buf values);
 
 /* ---- CUDA graphs of the context's stream (no reference counterpart: the B200 runtime replays
  * captured work instead of relaunching it from the host) ----

@@ -29,6 +29,7 @@ HERE = pathlib.Path(__file__).resolve().parent
 SIGNATURES: dict[str, list[tuple[str, str]]] = {
     "strata_unpack_half": [("Packed", "u*"), ("Values", "f*"), ("count", "i")],
     "strata_expert_scales": [("Blob", "u*"), ("Scales", "f*"), ("offset", "i"), ("count", "i")],
+    "strata_ple_decode": [("Packed", "u*"), ("Values", "f*"), ("count", "i")],
     "strata_q2_gate_up": [("X", "f*"), ("Blob", "u*"), ("Scales", "f*"), ("Mapping", "i*"), ("Hidden", "f*"),
                           ("width", "i"), ("ff", "i"), ("tokens", "i"), ("mapped", "i"), ("expanded", "i"),
                           ("codeOffset", "i"), ("scaleOffset", "i")],

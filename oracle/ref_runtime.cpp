@@ -220,6 +220,7 @@ static int ref_parallel(unsigned gx, unsigned gy, unsigned gz, const std::functi
 
 REF_ENTRY(strata_unpack_half, P(const unsigned int *Packed, float *Values, int count), P(Packed, Values, count))
 REF_ENTRY(strata_expert_scales, P(const unsigned int *Blob, float *Scales, int offset, int count), P(Blob, Scales, offset, count))
+REF_ENTRY(strata_ple_decode, P(const unsigned int *Packed, float *Values, int count), P(Packed, Values, count))
 REF_ENTRY(strata_q2_gate_up,
           P(const float *X, const unsigned int *Blob, const float *Scales, const int *Mapping, float *Hidden, int width, int ff,
             int tokens, int mapped, int expanded, int codeOffset, int scaleOffset),

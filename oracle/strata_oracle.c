@@ -76,6 +76,19 @@ int oracle_strata_unpack_half(unsigned gx, unsigned gy, unsigned gz, const unsig
     return 0;
 }
 
+/* kernels/strata.cu:81-87 — IQ4_NL rows of 32 values in 18 bytes: an FP16 scale, then 16 bytes
+   of codes (value i of the block: low nibble of byte i for i < 16, high nibble of byte i - 16). */
+int oracle_strata_ple_decode(unsigned gx, unsigned gy, unsigned gz, const unsigned int *Packed, float *Values, int count) {
+    (void)gy; (void)gz;
+    for (long i = 0; i < (long)gx * LANES && i < count; ++i) {
+        int block = (int)(i / 32), scale_byte = block * 18, code_byte = scale_byte + 2 + (int)(i % 16);
+        unsigned int half = (Packed[scale_byte / 4] >> ((scale_byte % 4) * 8)) & 65535u;
+        int code = (int)((Packed[code_byte / 4] >> ((code_byte % 4) * 8 + (i % 32 < 16 ? 0 : 4))) & 15u);
+        Values[i] = oracle_half_bits(half) * o_iq4(code);
+    }
+    return 0;
+}
+
 /* kernels/strata.cu:35-37 */
 int oracle_strata_expert_scales(unsigned gx, unsigned gy, unsigned gz, const unsigned int *Blob, float *Scales, int offset, int count) {
     (void)gy; (void)gz;

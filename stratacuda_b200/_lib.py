@@ -53,6 +53,7 @@ SIGNATURES = {
     "strata_flush": ([_vp], _i),
     "strata_info": ([_vp, C.c_char_p, _sz], _i),
     "strata_profile": ([_vp, C.c_int32], _i),
+    "strata_ple_gather_decode": ([_vp, _u64, _u64, C.c_int32, C.c_int32, _u64], _i),
     "strata_capture_begin": ([_vp], _i),
     "strata_capture_end": ([_vp, C.POINTER(C.c_uint64)], _i),
     "strata_graph_launch": ([_vp, _u64], _i),

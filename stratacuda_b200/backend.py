@@ -166,6 +166,12 @@ class CudaBackend:
         self._check(self.lib.strata_profile_read(self.ctx, ms, len(self.PHASES), C.byref(calls)))
         return dict(zip(self.PHASES, list(ms))), int(calls.value)
 
+    def ple_gather_decode(self, table, ids, rows: int, head_dim: int, values) -> None:
+        """Decode rows ids[0:rows] of a device-resident IQ4_NL per-layer-embedding table into
+        values[rows * head_dim] (strata_ple_gather_decode). Stream-ordered; a row outside the
+        table or a non-finite scale is reported by the next synchronising call."""
+        self._check(self.lib.strata_ple_gather_decode(self.ctx, table.handle, ids.handle, rows, head_dim, values.handle))
+
     def capture_begin(self) -> None:
         """Record the calls that follow on this thread into a CUDA graph (strata_capture_begin)."""
         self._check(self.lib.strata_capture_begin(self.ctx))

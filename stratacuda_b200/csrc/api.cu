@@ -100,6 +100,7 @@ int check_device_errors(strata_ctx *ctx) {
     if (e & kErrIndex) what += "an index outside its buffer was skipped; ";
     if (e & kErrRouting) what += "invalid expert routing result; ";
     if (e & kErrWaitTimeout) what += "a bounded device wait timed out; ";
+    if (e & kErrPleScale) what += "Non-finite PLE scales; ";
     return fail(ctx, STRATA_ERR_DEVICE, "device check failed: %s", what.c_str());
 }
 
@@ -180,6 +181,11 @@ int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params
         for (const char *p : {"codeOffset", "scaleOffset", "weightRow"})
             if (!int_in(I(p), 0)) return fail(ctx, STRATA_ERR_RANGE, "%s must be an integer >= 0", p);
         if (!int_in(I("rowStride"), 1, 2)) return fail(ctx, STRATA_ERR_RANGE, "expert row stride must be an integer in [1, 2]");
+    }
+    if (n == "strata_ple_decode") {  // src/backend.js:29
+        if (!int_in(I("count"))) return fail(ctx, STRATA_ERR_RANGE, "%s.count must be an integer in [1, 2147483647]", name);
+        if (I("count") % 32 || (I("count") / 32 * 18 + 3) / 4 > len("Packed") || I("count") > len("Values"))
+            return fail(ctx, STRATA_ERR_LAYOUT, "Invalid packed PLE layout");
     }
     if (n == "strata_q2_gate_up" || n == "strata_q2_down") {
         if (!int_in(I("width")) || !int_in(I("ff")))
@@ -425,6 +431,21 @@ int strata_info(strata_ctx *ctx, char *json, size_t cap) {
                      ctx->workspace_bytes, (unsigned long long)ctx->dispatches, (unsigned long long)ctx->fused_calls, moe_fast_pdl_state());
     if (json && cap) snprintf(json, cap, "%s", buf);
     return n;
+}
+
+int strata_ple_gather_decode(strata_ctx *ctx, strata_buf table, strata_buf ids, int32_t rows, int32_t head_dim, strata_buf values) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (rows < 1) return fail(ctx, STRATA_ERR_RANGE, "rows must be an integer >= 1");
+    if (head_dim < 32 || head_dim % 32) return fail(ctx, STRATA_ERR_LAYOUT, "Invalid packed PLE layout");
+    Buffer *t = find(ctx, table), *d = find(ctx, ids), *v = find(ctx, values);
+    if (!t || !d || !v) return fail(ctx, STRATA_ERR_HANDLE, "strata_ple_gather_decode: unknown buffer");
+    if ((long long)d->length < rows || (long long)v->length < (long long)rows * head_dim)
+        return fail(ctx, STRATA_ERR_LAYOUT, "Invalid packed PLE layout");
+    if (int r = use_device(ctx)) return r;
+    cudaError_t e = ple_gather_decode((const unsigned *)t->ptr, (long long)t->length, (const int *)d->ptr, (long long)d->length, rows, head_dim,
+                                      (float *)v->ptr, (long long)v->length, ctx->stream, ctx->err_dev);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "strata_ple_gather_decode");
+    return STRATA_OK;
 }
 
 int strata_capture_begin(strata_ctx *ctx) {

@@ -174,6 +174,34 @@ __device__ __forceinline__ float iq4(int c) {
     const float t[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f, 1.f, 13.f, 25.f, 38.f, 53.f, 69.f, 89.f, 113.f};
     return (c >= 0 && c < 15) ? t[c] : 113.0f;
 }
+// kernels/strata.cu:81-87 — IQ4_NL blocks of 32 values in 18 bytes: an FP16 scale, then 16 code
+// bytes (value i of a block: low nibble of byte i for i < 16, else high nibble of byte i - 16).
+// The scale starts at an even byte (18 per block), so it never straddles two words.
+__device__ __forceinline__ float ple_value(const UB &Packed, long long byte0, int i, unsigned *err) {
+    const long long scale_byte = byte0 + (long long)(i / 32) * 18, code_byte = scale_byte + 2 + i % 16;
+    const unsigned half = (Packed.get(scale_byte / 4, err) >> ((scale_byte % 4) * 8)) & 65535u;
+    const int code = (int)((Packed.get(code_byte / 4, err) >> ((code_byte % 4) * 8 + (i % 32 < 16 ? 0 : 4))) & 15u);
+    return __fmul_rn(half_bits(half), iq4(code));
+}
+__global__ void k_ple_decode(Grid g, UB Packed, FB Values, int count, unsigned *err) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < (long long)g.x * STRATA_LANES && i < count) Values.set(i, ple_value(Packed, 0, (int)i, err), err);
+}
+// Rows Ids[h] of a device-resident IQ4_NL table (rows of head_dim values, head_dim / 32 * 18
+// bytes each) decoded into Values[h * head_dim + j]: the values strata_ple_decode gives for the
+// same rows packed one after another (src/model.js:230-242 gathers them on the host). A row
+// outside the table reads zeros and sets kErrIndex; a non-finite scale sets kErrPleScale
+// (src/model.js:241 rejects those rows).
+__global__ void k_ple_gather_decode(UB Table, IB Ids, FB Values, int rows, int head_dim, unsigned *err) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * head_dim) return;
+    const int h = (int)(i / head_dim), j = (int)(i % head_dim);
+    const long long byte0 = (long long)Ids.get(h, err) * (head_dim / 32 * 18);
+    const long long scale_byte = byte0 + (long long)(j / 32) * 18;
+    if (j % 32 == 0 && ((Table.get(scale_byte / 4, err) >> ((scale_byte % 4) * 8)) & 0x7c00u) == 0x7c00u) raise_error(err, kErrPleScale);
+    Values.set(i, ple_value(Table, byte0, j, err), err);
+}
+
 __device__ __forceinline__ long long group_of(long long index, int size) {
     if (size == 16) return index >> 4;
     if (size == 32) return index >> 5;
@@ -300,6 +328,10 @@ cudaError_t L_unpack_half(const KArg *a, const unsigned g[3], cudaStream_t s, un
     k_unpack_half<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, err);
     return cudaGetLastError();
 }
+cudaError_t L_ple_decode(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_ple_decode<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, err);
+    return cudaGetLastError();
+}
 cudaError_t L_expert_scales(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     k_expert_scales<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, a[3].i, err);
     return cudaGetLastError();
@@ -361,11 +393,21 @@ cudaError_t L_scatter_rows(const KArg *a, const unsigned g[3], cudaStream_t s, u
 }
 }  // namespace
 
+cudaError_t ple_gather_decode(const unsigned *table, long long table_words, const int *ids, long long ids_len, int rows, int head_dim,
+                              float *values, long long values_len, cudaStream_t s, unsigned *err) {
+    const long long n = (long long)rows * head_dim;
+    k_ple_gather_decode<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(UB{const_cast<unsigned *>(table), table_words},
+                                                                      IB{const_cast<int *>(ids), ids_len}, FB{values, values_len}, rows,
+                                                                      head_dim, err);
+    return cudaGetLastError();
+}
+
 // Parameter lists in kernels/strata.cu order and spelling. Kinds: 'f' float buffer, 'u' u32
 // buffer, 'i' i32 buffer, 'I' i32 scalar, 'F' f32 scalar.
 const KernelSpec kKernels[] = {
     {"strata_unpack_half", "Packed:u Values:f count:I", L_unpack_half},
     {"strata_expert_scales", "Blob:u Scales:f offset:I count:I", L_expert_scales},
+    {"strata_ple_decode", "Packed:u Values:f count:I", L_ple_decode},
     {"strata_q2_gate_up",
      "X:f Blob:u Scales:f Mapping:i Hidden:f width:I ff:I tokens:I mapped:I expanded:I codeOffset:I scaleOffset:I", L_q2_gate_up},
     {"strata_q2_down",

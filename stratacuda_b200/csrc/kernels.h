@@ -12,6 +12,7 @@ enum : unsigned {
     kErrIndex = 1u,        // a data-dependent index (mapping, gather index, expert id) was out of range
     kErrWaitTimeout = 2u,  // a bounded spin-wait gave up
     kErrRouting = 4u,      // a routed expert id was invalid or repeated (src/engine.js:138)
+    kErrPleScale = 8u,     // a gathered PLE row has a non-finite FP16 scale (src/model.js:241)
 };
 
 // One resolved argument of a reference-compatible dispatch: a device buffer (ptr, length in
@@ -116,6 +117,11 @@ int ep_ranks(const EpComm *c);
 int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int tokens, float *y, int *ids, float *weights, int grid, cudaStream_t s,
                    unsigned *err, std::string *msg,
                    cudaEvent_t *marks = nullptr);
+
+// Per-layer embedding rows (csrc/compat.cu): rows ids[0 .. rows) of a device-resident IQ4_NL
+// table decoded into values[rows * head_dim]; lengths in elements, for the bounds checks.
+cudaError_t ple_gather_decode(const unsigned *table, long long table_words, const int *ids, long long ids_len, int rows, int head_dim,
+                              float *values, long long values_len, cudaStream_t s, unsigned *err);
 
 // Device synthetic generator (csrc/synth.cu), same bytes as stratacuda_b200/synth.py.
 cudaError_t synth_expert_blobs(unsigned *out, unsigned long long seed, int layer, int first_expert, int count, int width, int ff,
