@@ -56,6 +56,40 @@ SIGNATURES: dict[str, list[tuple[str, str]]] = {
                                  ("Y", "f*"), ("width", "i"), ("count", "i"), ("tokens", "i")],
     "strata_gather_rows": [("X", "f*"), ("Indices", "i*"), ("Y", "f*"), ("width", "i"), ("rows", "i")],
     "strata_scatter_rows": [("X", "f*"), ("Indices", "i*"), ("Y", "f*"), ("width", "i"), ("rows", "i")],
+    # the remaining entries (kernels/strata.cu:72-534)
+    "strata_embedding": [("Values", "f*"), ("Codes", "u*"), ("Scales", "f*"), ("Offsets", "f*"), ("Residual", "f*"), ("width", "i"), ("streams", "i"), ("outputOffset", "i"), ("format", "i"), ("bits", "i"), ("groupSize", "i"), ("bias", "i"), ("codebook", "i"), ("hasOffset", "i")],
+    "strata_embed": [("Row", "f*"), ("Residual", "f*"), ("width", "i"), ("streams", "i")],
+    "strata_embed_batch": [("Rows", "f*"), ("Residual", "f*"), ("width", "i"), ("streams", "i"), ("tokens", "i")],
+    "strata_rope_frequencies": [("High", "f*"), ("Low", "f*"), ("rotary", "i"), ("base", "f")],
+    "strata_rope_table": [("High", "f*"), ("Low", "f*"), ("Cos", "f*"), ("Sin", "f*"), ("rotary", "i"), ("context", "i")],
+    "strata_rope_position": [("X", "f*"), ("Cos", "f*"), ("Sin", "f*"), ("Y", "f*"), ("dim", "i"), ("heads", "i"), ("rotary", "i"), ("position", "i"), ("tokens", "i")],
+    "strata_rope": [("X", "f*"), ("Cos", "f*"), ("Sin", "f*"), ("Y", "f*"), ("dim", "i"), ("heads", "i"), ("rotary", "i")],
+    "strata_rope_batch": [("X", "f*"), ("Cos", "f*"), ("Sin", "f*"), ("Y", "f*"), ("dim", "i"), ("heads", "i"), ("rotary", "i"), ("tokens", "i")],
+    "strata_gemv": [("X", "f*"), ("W", "f*"), ("Y", "f*"), ("cols", "i"), ("rows", "i"), ("tokens", "i")],
+    "strata_quant_gemv": [("X", "f*"), ("Codes", "u*"), ("Scales", "f*"), ("Offsets", "f*"), ("Y", "f*"), ("cols", "i"), ("rows", "i"), ("bits", "i"), ("groupSize", "i"), ("bias", "i"), ("codebook", "i"), ("hasOffset", "i")],
+    "strata_norm": [("X", "f*"), ("W", "f*"), ("Y", "f*"), ("cols", "i"), ("rows", "i"), ("weightRows", "i"), ("mode", "i"), ("epsilon", "f"), ("scale", "f")],
+    "strata_ple_gate": [("Key", "f*"), ("Query", "f*"), ("Gate", "f*"), ("width", "i"), ("streams", "i")],
+    "strata_argmax": [("Logits", "f*"), ("Token", "i*"), ("count", "i")],
+    "strata_attention": [("Q", "f*"), ("Keys", "f*"), ("Values", "f*"), ("Cells", "i*"), ("Y", "f*"), ("dim", "i"), ("heads", "i"), ("kvHeads", "i"), ("count", "i"), ("scale", "f")],
+    "strata_attention_batch": [("Q", "f*"), ("Keys", "f*"), ("Values", "f*"), ("Y", "f*"), ("dim", "i"), ("heads", "i"), ("kvHeads", "i"), ("position", "i"), ("scale", "f")],
+    "strata_kv_append": [("K", "f*"), ("V", "f*"), ("Keys", "f*"), ("Values", "f*"), ("width", "i"), ("position", "i")],
+    "strata_kv_append_batch": [("K", "f*"), ("V", "f*"), ("Keys", "f*"), ("Values", "f*"), ("width", "i"), ("position", "i"), ("tokens", "i")],
+    "strata_attention_gate": [("Attention", "f*"), ("FullQ", "f*"), ("Y", "f*"), ("dim", "i"), ("heads", "i")],
+    "strata_attention_gate_batch": [("Attention", "f*"), ("FullQ", "f*"), ("Y", "f*"), ("dim", "i"), ("heads", "i"), ("tokens", "i")],
+    "strata_slice": [("X", "f*"), ("Y", "f*"), ("width", "i"), ("rows", "i"), ("stride", "i"), ("offset", "i")],
+    "strata_hc_mix": [("Norm", "f*"), ("Gate", "f*"), ("Mixed", "f*"), ("width", "i"), ("streams", "i")],
+    "strata_hc_mix_batch": [("Norm", "f*"), ("Gate", "f*"), ("Mixed", "f*"), ("width", "i"), ("streams", "i"), ("tokens", "i")],
+    "strata_hc_write": [("Residual", "f*"), ("Output", "f*"), ("Inject", "f*"), ("width", "i"), ("streams", "i")],
+    "strata_hc_write_batch": [("Residual", "f*"), ("Output", "f*"), ("Inject", "f*"), ("width", "i"), ("streams", "i"), ("tokens", "i")],
+    "strata_ple_broadcast": [("Value", "f*"), ("Gate", "f*"), ("Y", "f*"), ("width", "i"), ("streams", "i")],
+    "strata_ple_broadcast_batch": [("Value", "f*"), ("Gate", "f*"), ("Y", "f*"), ("width", "i"), ("streams", "i"), ("tokens", "i")],
+    "strata_ple_add": [("Residual", "f*"), ("Gated", "f*"), ("Conv", "f*"), ("n", "i")],
+    "strata_conv": [("History", "f*"), ("X", "f*"), ("W", "f*"), ("Y", "f*"), ("channels", "i"), ("taps", "i"), ("dilation", "i"), ("activation", "i")],
+    "strata_conv_batch": [("History", "f*"), ("X", "f*"), ("W", "f*"), ("Y", "f*"), ("channels", "i"), ("taps", "i"), ("dilation", "i"), ("activation", "i"), ("tokens", "i")],
+    "strata_gdn_gates": [("Alpha", "f*"), ("Beta", "f*"), ("A", "f*"), ("Dt", "f*"), ("Decay", "f*"), ("Strength", "f*"), ("heads", "i")],
+    "strata_gdn_gates_batch": [("Alpha", "f*"), ("Beta", "f*"), ("A", "f*"), ("Dt", "f*"), ("Decay", "f*"), ("Strength", "f*"), ("heads", "i"), ("tokens", "i")],
+    "strata_gdn_step": [("State", "f*"), ("Q", "f*"), ("K", "f*"), ("V", "f*"), ("Decay", "f*"), ("Beta", "f*"), ("Y", "f*"), ("dim", "i"), ("keyHeads", "i"), ("valueHeads", "i")],
+    "strata_gdn_batch": [("State", "f*"), ("Q", "f*"), ("K", "f*"), ("V", "f*"), ("Decay", "f*"), ("Beta", "f*"), ("Y", "f*"), ("dim", "i"), ("keyHeads", "i"), ("valueHeads", "i"), ("tokens", "i")],
 }
 _CTYPE = {"f*": C.c_void_p, "u*": C.c_void_p, "i*": C.c_void_p, "i": C.c_int, "f": C.c_float}
 _DTYPE = {"f*": np.float32, "u*": np.uint32, "i*": np.int32}

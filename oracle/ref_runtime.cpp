@@ -257,3 +257,71 @@ REF_ENTRY(strata_moe_combine_batch,
           P(Parts, Weights, Shared, SharedGate, Y, width, count, tokens))
 REF_ENTRY(strata_gather_rows, P(const float *X, const int *Indices, float *Y, int width, int rows), P(X, Indices, Y, width, rows))
 REF_ENTRY(strata_scatter_rows, P(const float *X, const int *Indices, float *Y, int width, int rows), P(X, Indices, Y, width, rows))
+
+// The remaining entries (kernels/strata.cu:72-534).
+REF_ENTRY(strata_embedding, P(float *Values, unsigned int *Codes, float *Scales, float *Offsets, float *Residual, int width, int streams, int outputOffset, int format, int bits, int groupSize, int bias, int codebook, int hasOffset),
+          P(Values, Codes, Scales, Offsets, Residual, width, streams, outputOffset, format, bits, groupSize, bias, codebook, hasOffset))
+REF_ENTRY(strata_embed, P(float *Row, float *Residual, int width, int streams),
+          P(Row, Residual, width, streams))
+REF_ENTRY(strata_embed_batch, P(float *Rows, float *Residual, int width, int streams, int tokens),
+          P(Rows, Residual, width, streams, tokens))
+REF_ENTRY(strata_rope_frequencies, P(float *High, float *Low, int rotary, float base),
+          P(High, Low, rotary, base))
+REF_ENTRY(strata_rope_table, P(float *High, float *Low, float *Cos, float *Sin, int rotary, int context),
+          P(High, Low, Cos, Sin, rotary, context))
+REF_ENTRY(strata_rope_position, P(float *X, float *Cos, float *Sin, float *Y, int dim, int heads, int rotary, int position, int tokens),
+          P(X, Cos, Sin, Y, dim, heads, rotary, position, tokens))
+REF_ENTRY(strata_rope, P(float *X, float *Cos, float *Sin, float *Y, int dim, int heads, int rotary),
+          P(X, Cos, Sin, Y, dim, heads, rotary))
+REF_ENTRY(strata_rope_batch, P(float *X, float *Cos, float *Sin, float *Y, int dim, int heads, int rotary, int tokens),
+          P(X, Cos, Sin, Y, dim, heads, rotary, tokens))
+REF_ENTRY(strata_gemv, P(float *X, float *W, float *Y, int cols, int rows, int tokens),
+          P(X, W, Y, cols, rows, tokens))
+REF_ENTRY(strata_quant_gemv, P(float *X, unsigned int *Codes, float *Scales, float *Offsets, float *Y, int cols, int rows, int bits, int groupSize, int bias, int codebook, int hasOffset),
+          P(X, Codes, Scales, Offsets, Y, cols, rows, bits, groupSize, bias, codebook, hasOffset))
+REF_ENTRY(strata_norm, P(float *X, float *W, float *Y, int cols, int rows, int weightRows, int mode, float epsilon, float scale),
+          P(X, W, Y, cols, rows, weightRows, mode, epsilon, scale))
+REF_ENTRY(strata_ple_gate, P(float *Key, float *Query, float *Gate, int width, int streams),
+          P(Key, Query, Gate, width, streams))
+REF_ENTRY(strata_argmax, P(float *Logits, int *Token, int count),
+          P(Logits, Token, count))
+REF_ENTRY(strata_attention, P(float *Q, float *Keys, float *Values, int *Cells, float *Y, int dim, int heads, int kvHeads, int count, float scale),
+          P(Q, Keys, Values, Cells, Y, dim, heads, kvHeads, count, scale))
+REF_ENTRY(strata_attention_batch, P(float *Q, float *Keys, float *Values, float *Y, int dim, int heads, int kvHeads, int position, float scale),
+          P(Q, Keys, Values, Y, dim, heads, kvHeads, position, scale))
+REF_ENTRY(strata_kv_append, P(float *K, float *V, float *Keys, float *Values, int width, int position),
+          P(K, V, Keys, Values, width, position))
+REF_ENTRY(strata_kv_append_batch, P(float *K, float *V, float *Keys, float *Values, int width, int position, int tokens),
+          P(K, V, Keys, Values, width, position, tokens))
+REF_ENTRY(strata_attention_gate, P(float *Attention, float *FullQ, float *Y, int dim, int heads),
+          P(Attention, FullQ, Y, dim, heads))
+REF_ENTRY(strata_attention_gate_batch, P(float *Attention, float *FullQ, float *Y, int dim, int heads, int tokens),
+          P(Attention, FullQ, Y, dim, heads, tokens))
+REF_ENTRY(strata_slice, P(float *X, float *Y, int width, int rows, int stride, int offset),
+          P(X, Y, width, rows, stride, offset))
+REF_ENTRY(strata_hc_mix, P(float *Norm, float *Gate, float *Mixed, int width, int streams),
+          P(Norm, Gate, Mixed, width, streams))
+REF_ENTRY(strata_hc_mix_batch, P(float *Norm, float *Gate, float *Mixed, int width, int streams, int tokens),
+          P(Norm, Gate, Mixed, width, streams, tokens))
+REF_ENTRY(strata_hc_write, P(float *Residual, float *Output, float *Inject, int width, int streams),
+          P(Residual, Output, Inject, width, streams))
+REF_ENTRY(strata_hc_write_batch, P(float *Residual, float *Output, float *Inject, int width, int streams, int tokens),
+          P(Residual, Output, Inject, width, streams, tokens))
+REF_ENTRY(strata_ple_broadcast, P(float *Value, float *Gate, float *Y, int width, int streams),
+          P(Value, Gate, Y, width, streams))
+REF_ENTRY(strata_ple_broadcast_batch, P(float *Value, float *Gate, float *Y, int width, int streams, int tokens),
+          P(Value, Gate, Y, width, streams, tokens))
+REF_ENTRY(strata_ple_add, P(float *Residual, float *Gated, float *Conv, int n),
+          P(Residual, Gated, Conv, n))
+REF_ENTRY(strata_conv, P(float *History, float *X, float *W, float *Y, int channels, int taps, int dilation, int activation),
+          P(History, X, W, Y, channels, taps, dilation, activation))
+REF_ENTRY(strata_conv_batch, P(float *History, float *X, float *W, float *Y, int channels, int taps, int dilation, int activation, int tokens),
+          P(History, X, W, Y, channels, taps, dilation, activation, tokens))
+REF_ENTRY(strata_gdn_gates, P(float *Alpha, float *Beta, float *A, float *Dt, float *Decay, float *Strength, int heads),
+          P(Alpha, Beta, A, Dt, Decay, Strength, heads))
+REF_ENTRY(strata_gdn_gates_batch, P(float *Alpha, float *Beta, float *A, float *Dt, float *Decay, float *Strength, int heads, int tokens),
+          P(Alpha, Beta, A, Dt, Decay, Strength, heads, tokens))
+REF_ENTRY(strata_gdn_step, P(float *State, float *Q, float *K, float *V, float *Decay, float *Beta, float *Y, int dim, int keyHeads, int valueHeads),
+          P(State, Q, K, V, Decay, Beta, Y, dim, keyHeads, valueHeads))
+REF_ENTRY(strata_gdn_batch, P(float *State, float *Q, float *K, float *V, float *Decay, float *Beta, float *Y, int dim, int keyHeads, int valueHeads, int tokens),
+          P(State, Q, K, V, Decay, Beta, Y, dim, keyHeads, valueHeads, tokens))

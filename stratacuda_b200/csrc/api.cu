@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <cmath>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -125,9 +126,12 @@ std::vector<Entry> &entries() {
     static std::vector<Entry> table;
     static std::once_flag once;
     std::call_once(once, [] {
-        for (int k = 0; k < kNumKernels; ++k) {
-            Entry e{&kKernels[k], {}};
-            const char *p = kKernels[k].params;
+        std::vector<const KernelSpec *> specs;
+        for (int k = 0; k < kNumKernels; ++k) specs.push_back(&kKernels[k]);
+        for (int k = 0; k < kNumEngineKernels; ++k) specs.push_back(&kEngineKernels[k]);
+        for (const KernelSpec *spec : specs) {
+            Entry e{spec, {}};
+            const char *p = spec->params;
             while (*p) {
                 while (*p == ' ') ++p;
                 const char *c = strchr(p, ':');
@@ -160,7 +164,7 @@ int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params
         if (I("experts") > 512 || I("topK") > std::min(I("experts"), 32LL))
             return fail(ctx, STRATA_ERR_RANGE, "Router supports 1-512 experts and topK <= min(experts,32)");
     }
-    if (n == "strata_quant_project") {
+    if (n == "strata_quant_project" || n == "strata_quant_gemv") {
         long long bits = I("bits");
         if (bits != 2 && bits != 4 && bits != 8) return fail(ctx, STRATA_ERR_RANGE, "Canonical code width must be 2, 4 or 8");
         if (!int_in(I("cols")) || !int_in(I("groupSize")))
@@ -197,6 +201,116 @@ int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params
         if (n == "strata_q2_down" && !int_in(I("outputOffset"), 0))
             return fail(ctx, STRATA_ERR_RANGE, "expert output offset must be an integer >= 0");
     }
+    if (n == "strata_embedding") {
+        if (!int_in(I("width")) || !int_in(I("streams")))
+            return fail(ctx, STRATA_ERR_RANGE, "%s.width and streams must be integers in [1, 2147483647]", name);
+        if (!int_in(I("outputOffset"), 0)) return fail(ctx, STRATA_ERR_RANGE, "embedding output offset must be an integer >= 0");
+        const long long format = I("format");
+        if (I("outputOffset") + I("width") * I("streams") > len("Residual") || format < 0 || format > 2)
+            return fail(ctx, STRATA_ERR_LAYOUT, "Embedding exceeds buffer layout");
+        if (format == 2) {
+            const long long bits = I("bits");
+            if (!int_in(I("groupSize"))) return fail(ctx, STRATA_ERR_RANGE, "%s.groupSize must be an integer in [1, 2147483647]", name);
+            if ((bits != 2 && bits != 4 && bits != 8) || I("width") % I("groupSize"))
+                return fail(ctx, STRATA_ERR_LAYOUT, "Invalid packed embedding layout");
+        }
+    }
+    if (n == "strata_rope_position") {
+        if (!int_in(I("position"), 0, 2047)) return fail(ctx, STRATA_ERR_RANGE, "RoPE position must be an integer in [0, 2047]");
+        for (const char *p : {"rotary", "dim", "heads", "tokens"})
+            if (!int_in(I(p))) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p);
+        if (I("rotary") % 2 || I("rotary") > I("dim") || I("position") + I("tokens") > 2048 ||
+            len("Cos") < (I("position") + I("tokens")) * I("rotary") / 2 || len("Sin") != len("Cos") ||
+            len("X") != I("dim") * I("heads") * I("tokens") || len("Y") != len("X"))
+            return fail(ctx, STRATA_ERR_LAYOUT, "Invalid RoPE layout");
+    }
+    if (n == "strata_rope_frequencies") {
+        const float base = a[idx("base")].f;
+        if (!int_in(I("rotary"))) return fail(ctx, STRATA_ERR_RANGE, "%s.rotary must be an integer in [1, 2147483647]", name);
+        if (!std::isfinite(base) || base <= 1.0f || I("rotary") % 2) return fail(ctx, STRATA_ERR_LAYOUT, "Invalid RoPE frequencies");
+    }
+    if (n == "strata_attention" || n == "strata_attention_batch") {
+        for (const char *p : {"heads", "kvHeads", "dim"})
+            if (!int_in(I(p))) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p);
+        if (I("heads") % I("kvHeads"))  // a RangeError for decode, an Error for prompts (src/backend.js:37,41)
+            return fail(ctx, n == "strata_attention" ? STRATA_ERR_RANGE : STRATA_ERR_LAYOUT, "Attention heads must be divisible by KV heads");
+        if (n == "strata_attention" && !int_in(I("count"), 1, 2048))
+            return fail(ctx, STRATA_ERR_RANGE, "attention selected cells must be an integer in [1, 2048]");
+        if (n == "strata_attention_batch") {
+            if (!int_in(I("position"), 0, 2047)) return fail(ctx, STRATA_ERR_RANGE, "attention position must be an integer in [0, 2047]");
+            const long long row = I("heads") * I("dim");
+            if (len("Q") % row || I("position") + len("Q") / row > 2048)
+                return fail(ctx, STRATA_ERR_LAYOUT, "Batched attention exceeds 2048 cells");
+        }
+    }
+    if (n == "strata_rope") {
+        if (!int_in(I("rotary")) || !int_in(I("dim")))
+            return fail(ctx, STRATA_ERR_RANGE, "%s.rotary and dim must be integers in [1, 2147483647]", name);
+        if (I("rotary") % 2 || I("rotary") > I("dim")) return fail(ctx, STRATA_ERR_RANGE, "Rotary width must be even and <= head dimension");
+    }
+    if (n == "strata_norm") {
+        if (!int_in(I("rows")) || !int_in(I("weightRows")))
+            return fail(ctx, STRATA_ERR_RANGE, "%s.rows and weightRows must be integers in [1, 2147483647]", name);
+        if (I("rows") % I("weightRows")) return fail(ctx, STRATA_ERR_RANGE, "Normalization weight rows must divide input rows");
+    }
+    // Beyond the reference: parameters that these entries divide by must be positive. The
+    // reference does not check them; its CPU build traps on an integer division by zero.
+    static const struct {
+        const char *entry, *params;
+    } kDivisors[] = {
+        {"strata_embed", "width"},           {"strata_embed_batch", "width streams"}, {"strata_hc_mix_batch", "width"},
+        {"strata_hc_write", "width"},        {"strata_hc_write_batch", "width streams"},
+        {"strata_ple_broadcast", "width"},   {"strata_ple_broadcast_batch", "width streams"},
+        {"strata_slice", "width"},           {"strata_rope_batch", "dim rotary"},  {"strata_rope_table", "rotary"},
+        {"strata_attention_gate", "dim"},    {"strata_attention_gate_batch", "dim"}, {"strata_gdn_gates_batch", "heads"},
+        {"strata_gdn_step", "dim keyHeads valueHeads"}, {"strata_gdn_batch", "dim keyHeads valueHeads"},
+    };
+    for (const auto &d : kDivisors) {
+        if (n != d.entry) continue;
+        std::string list(d.params), p;
+        for (size_t at = 0; at <= list.size(); ++at) {
+            if (at < list.size() && list[at] != ' ') {
+                p += list[at];
+                continue;
+            }
+            if (p.empty()) continue;
+            const long long v = I(p.c_str());
+            if (!int_in(v) || (p == "rotary" && v < 2))
+                return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [%d, 2147483647]", name, p.c_str(), p == "rotary" ? 2 : 1);
+            p.clear();
+        }
+    }
+    // Beyond the reference: every loop extent must fit the buffer it walks, so a malformed
+    // dispatch is rejected instead of spinning over skipped out-of-range reads.
+    auto fits = [&](long long need, const char *buf) { return need >= 0 && need <= len(buf); };
+    bool ok = true;
+    if (n == "strata_conv" || n == "strata_conv_batch") {
+        const long long c = I("channels"), taps = I("taps"), dil = I("dilation"), t = n == "strata_conv" ? 1 : I("tokens");
+        ok = int_in(c) && int_in(taps) && int_in(dil) && int_in(t) && fits(c * (taps - 1) * dil, "History") && fits(c * taps, "W") &&
+             fits(t * c, "X") && fits(t * c, "Y");
+    } else if (n == "strata_gdn_step" || n == "strata_gdn_batch") {
+        const long long d = I("dim"), vh = I("valueHeads"), kh = I("keyHeads"), t = n == "strata_gdn_step" ? 1 : I("tokens");
+        ok = int_in(d) && int_in(vh) && int_in(kh) && int_in(t) && fits(d * vh * d, "State") && fits(t * kh * d, "Q") &&
+             fits(t * kh * d, "K") && fits(t * vh * d, "V") && fits(t * vh * d, "Y");
+    } else if (n == "strata_norm") {
+        ok = int_in(I("cols")) && fits(I("rows") * I("cols"), "X") && fits(I("rows") * I("cols"), "Y");
+    } else if (n == "strata_gemv") {
+        ok = int_in(I("cols")) && int_in(I("rows")) && int_in(I("tokens")) && fits(I("rows") * I("cols"), "W") &&
+             fits(I("tokens") * I("cols"), "X");
+    } else if (n == "strata_quant_gemv") {
+        ok = fits(I("cols"), "X");
+    } else if (n == "strata_ple_gate") {
+        ok = int_in(I("width")) && int_in(I("streams")) && fits(I("streams") * I("width"), "Key") &&
+             fits(I("streams") * I("width"), "Query");
+    } else if (n == "strata_argmax") {
+        ok = int_in(I("count")) && fits(I("count"), "Logits");
+    } else if (n == "strata_attention") {
+        ok = fits(I("heads") * I("dim"), "Q") && fits(I("count"), "Cells");
+    } else if (n == "strata_hc_mix" || n == "strata_hc_mix_batch") {
+        ok = int_in(I("width")) && int_in(I("streams")) &&
+             fits((n == "strata_hc_mix" ? 1 : I("tokens")) * I("streams") * I("width"), "Norm");
+    }
+    if (!ok) return fail(ctx, STRATA_ERR_LAYOUT, "%s: a loop extent exceeds its buffer layout", name);
     return STRATA_OK;
 }
 

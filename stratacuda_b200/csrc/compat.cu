@@ -10,49 +10,10 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "route.cuh"
+#include "compat.cuh"
 
 namespace strata {
 namespace {
-
-template <typename T>
-struct Buf {
-    T *p;
-    long long n;
-    __device__ __forceinline__ T get(long long i, unsigned *err) const {
-        if (i < 0 || i >= n) { raise_error(err, kErrIndex); return T(0); }
-        return p[i];
-    }
-    __device__ __forceinline__ void set(long long i, T v, unsigned *err) const {
-        if (i < 0 || i >= n) { raise_error(err, kErrIndex); return; }
-        p[i] = v;
-    }
-};
-using FB = Buf<float>;
-using UB = Buf<unsigned>;
-using IB = Buf<int>;
-
-__device__ __forceinline__ float half_of(const UB &b, long long h, unsigned *err) {
-    return half_bits((b.get(h / 2, err) >> ((h % 2) * 16)) & 65535u);
-}
-__device__ __forceinline__ int code_of(const UB &b, long long codeOffset, long long index, unsigned *err) {
-    return (int)((b.get(codeOffset + index / 16, err) >> ((index % 16) * 2)) & 3u) - 1;
-}
-
-struct Grid {
-    unsigned x, y, z;
-};
-constexpr int kWarpsPerBlock = 4;
-
-// Workgroup (x, y, z) handled by this warp, or false when past the dispatch grid.
-__device__ __forceinline__ bool my_group(const Grid g, unsigned &gx, unsigned &gy, unsigned &gz) {
-    unsigned long long w = (unsigned long long)blockIdx.x * kWarpsPerBlock + threadIdx.x / 32;
-    unsigned long long total = (unsigned long long)g.x * g.y * g.z;
-    if (w >= total) return false;
-    gx = (unsigned)(w % g.x);
-    gy = (unsigned)((w / g.x) % g.y);
-    gz = (unsigned)(w / ((unsigned long long)g.x * g.y));
-    return true;
-}
 
 // ---------------------------------------------------------------- element kernels
 // (one reference lane per thread: i = blockIdx.x * 64 + threadIdx.x over the x extent)
@@ -170,10 +131,6 @@ __global__ void k_q2_project(Grid g, FB X, UB Blob, FB Y, int cols, int rows, in
     if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
 }
 
-__device__ __forceinline__ float iq4(int c) {
-    const float t[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f, 1.f, 13.f, 25.f, 38.f, 53.f, 69.f, 89.f, 113.f};
-    return (c >= 0 && c < 15) ? t[c] : 113.0f;
-}
 // kernels/strata.cu:81-87 — IQ4_NL blocks of 32 values in 18 bytes: an FP16 scale, then 16 code
 // bytes (value i of a block: low nibble of byte i for i < 16, else high nibble of byte i - 16).
 // The scale starts at an even byte (18 per block), so it never straddles two words.
@@ -311,18 +268,6 @@ __global__ void k_router_batch(Grid g, FB Logits, IB Ids, FB Weights, int expert
 
 // ---------------------------------------------------------------- launchers
 
-inline Grid grid_of(const unsigned g[3]) { return Grid{g[0], g[1], g[2]}; }
-inline unsigned group_blocks(const unsigned g[3]) {
-    unsigned long long total = (unsigned long long)g[0] * g[1] * g[2];
-    return (unsigned)((total + kWarpsPerBlock - 1) / kWarpsPerBlock);
-}
-inline unsigned lane_blocks(const unsigned g[3]) { return (unsigned)(((unsigned long long)g[0] * STRATA_LANES + 255) / 256); }
-
-#define F(i) FB{(float *)a[i].ptr, a[i].len}
-#define U(i) UB{(unsigned *)a[i].ptr, a[i].len}
-#define I(i) IB{(int *)a[i].ptr, a[i].len}
-#define GROUPS group_blocks(g), kWarpsPerBlock * 32, 0, s
-#define LANESL lane_blocks(g), 256, 0, s
 
 cudaError_t L_unpack_half(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     k_unpack_half<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, err);

@@ -1,0 +1,634 @@
+// The rest of the reference's kernels (kernels/strata.cu:72-534 apart from the mixture-of-experts
+// entries in compat.cu): embeddings, RoPE, norms, hyper-connection mixing, the gated delta-net
+// recurrence, causal convolution, attention, per-layer-embedding gating and greedy argmax. With
+// them strata_run() serves every entry that src/engine.js, src/ops.js and src/prefill.js
+// dispatch, so the reference host runs a whole model on this library.
+//
+// Numerics: every F32 product, sum and quotient is rounded separately in the reference's order
+// (__fmul_rn / __fadd_rn / __fdiv_rn / __fsqrt_rn, no contraction), reductions keep the
+// 64-lane stride and the shared-memory tree, and expf is the reference's own (ref_expf), so
+// results are bit-identical to the reference's CPU build. The three other transcendentals
+// (logf in the softplus, cosf / sinf of the RoPE table) are evaluated in double precision and
+// rounded once to float: the reference leaves them to its C library, whose float versions are
+// not correctly rounded in every case, so these agree with it to within an ulp.
+//
+// Layout: as in compat.cu, a reference workgroup is one warp (thread t owns lanes t and t+32)
+// and element entries run one reference lane per thread. Every access is bounds-checked
+// against its buffer; an out-of-range index sets the device error word instead of faulting.
+#include "compat.cuh"
+
+namespace strata {
+namespace {
+
+constexpr int kMaxCells = 2048;  // kernels/strata.cu:333, the shared score array
+
+// Index of this thread's reference lane for an element entry, or -1 past the dispatch grid or n.
+// Workgroups beyond the first along y and z repeat the same lanes in the reference; each lane
+// runs once here (for the in-place entries the repeats would race with one another).
+__device__ __forceinline__ long long lane_index(const Grid g, long long n) {
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    return (i < (long long)g.x * STRATA_LANES && i < n) ? i : -1;
+}
+
+__device__ __forceinline__ float max_tree64(float lo, float hi) {
+    float a = fmaxf(lo, hi);
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) a = fmaxf(a, __shfl_down_sync(0xffffffffu, a, s));
+    return a;
+}
+
+// log(x) and cos / sin rounded once from double precision.
+__device__ __forceinline__ float log_f(float x) { return __double2float_rn(log((double)x)); }
+__device__ __forceinline__ float cos_f(float x) { return __double2float_rn(cos((double)x)); }
+__device__ __forceinline__ float sin_f(float x) { return __double2float_rn(sin((double)x)); }
+
+// Rotated value of element d of one head row (NeoX half split): a = x[pair], b = x[pair + half].
+__device__ __forceinline__ float rotate(float a, float b, float c, float s, bool first) {
+    return first ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)) : __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+
+// ---------------------------------------------------------------- embeddings
+
+// kernels/strata.cu:72-80: one token row (F32, BF16 or canonical packed codes) copied to every
+// stream of the residual.
+__global__ void k_embedding(Grid g, FB Values, UB Codes, FB Scales, FB Offsets, FB Residual, int width, int streams, int outputOffset,
+                            int format, int bits, int groupSize, int bias, int codebook, int hasOffset, unsigned *err) {
+    long long i = lane_index(g, width);
+    if (i < 0) return;
+    float value = 0.0f;
+    if (format == 0) {
+        value = Values.get(i, err);
+    } else if (format == 1) {
+        value = __uint_as_float(((Codes.get(i / 2, err) >> ((i % 2) * 16)) & 65535u) << 16);
+    } else {
+        long long bit = i * bits;
+        int code = (int)((Codes.get(bit / 32, err) >> (bit % 32)) & ((1u << bits) - 1u));
+        long long group = i / groupSize;
+        value = __fmul_rn(codebook == 1 ? iq4(code) : (float)(code + bias), Scales.get(group, err));
+        if (hasOffset != 0) value = __fadd_rn(value, Offsets.get(group, err));
+    }
+    for (int stream = 0; stream < streams; ++stream) Residual.set((long long)outputOffset + (long long)stream * width + i, value, err);
+}
+
+// kernels/strata.cu:282-284 and :399-402
+__global__ void k_embed(Grid g, FB Row, FB Residual, int width, int streams, int tokens, unsigned *err) {
+    const long long hc = (long long)width * streams;
+    long long i = lane_index(g, hc * tokens);
+    if (i >= 0) Residual.set(i, Row.get((i / hc) * width + i % width, err), err);
+}
+
+// ---------------------------------------------------------------- RoPE
+
+// kernels/strata.cu:90-104: inverse frequencies base^(-2i/rotary) from a range-reduced log
+// series and an exp series, in double arithmetic with every operation rounded on its own (the
+// reference's CPU target has no fused multiply-add), split into a float and its remainder.
+__global__ void k_rope_frequencies(Grid g, FB High, FB Low, int rotary, float base, unsigned *err) {
+    long long i = lane_index(g, rotary / 2);
+    if (i < 0) return;
+    double value = (double)base;
+    int exponent = 0;
+    while (value >= 2.0) {  // at most 128 halvings for a finite float base
+        value = __dmul_rn(value, 0.5);
+        exponent += 1;
+    }
+    const double y = __ddiv_rn(__dsub_rn(value, 1.0), __dadd_rn(value, 1.0));
+    double term = y, logarithm = 0.0;
+    for (int n = 1; n <= 49; n += 2) {
+        logarithm = __dadd_rn(logarithm, __ddiv_rn(term, (double)n));
+        term = __dmul_rn(__dmul_rn(term, y), y);
+    }
+    const double ln2 = 0.693147180559945309417232121458176568;
+    logarithm = __dadd_rn(__dmul_rn(2.0, logarithm), __dmul_rn((double)exponent, ln2));
+    const double power = __ddiv_rn(__dmul_rn(-logarithm, (double)(2 * i)), (double)rotary);
+    int whole = (int)__double2float_rn(__ddiv_rn(power, ln2));
+    const double remainder = __dsub_rn(power, __dmul_rn((double)whole, ln2));
+    double result = 1.0;
+    term = 1.0;
+    for (int n = 1; n <= 20; ++n) {
+        term = __ddiv_rn(__dmul_rn(term, remainder), (double)n);
+        result = __dadd_rn(result, term);
+    }
+    for (; whole < 0; ++whole) result = __dmul_rn(result, 0.5);
+    const float high = __double2float_rn(result);
+    High.set(i, high, err);
+    Low.set(i, __double2float_rn(__dsub_rn(result, (double)high)), err);
+}
+
+// kernels/strata.cu:105-111: cos / sin of position * frequency, reduced by whole turns in double.
+__global__ void k_rope_table(Grid g, FB High, FB Low, FB Cos, FB Sin, int rotary, int context, unsigned *err) {
+    const int half = rotary / 2;
+    long long i = lane_index(g, (long long)context * half);
+    if (i < 0) return;
+    const long long pair = i % half;
+    const double angle = __dmul_rn((double)(i / half), __dadd_rn((double)High.get(pair, err), (double)Low.get(pair, err)));
+    const double turn = 6.283185307179586476925286766559005768;
+    const int wraps = (int)__double2float_rn(__dadd_rn(__ddiv_rn(angle, turn), 0.5));
+    const float reduced = __double2float_rn(__dsub_rn(angle, __dmul_rn((double)wraps, turn)));
+    Cos.set(i, cos_f(reduced), err);
+    Sin.set(i, sin_f(reduced), err);
+}
+
+// kernels/strata.cu:113-120 (rope_position: table row position + token), :319-327 (rope: one
+// row of Cos / Sin) and :445-452 (rope_batch: table row = token). `mode` 0 / 1 / 2 picks which.
+__global__ void k_rope(Grid g, FB X, FB Cos, FB Sin, FB Y, int dim, int heads, int rotary, int position, int tokens, int mode,
+                       unsigned *err) {
+    long long i = lane_index(g, (long long)dim * heads * tokens);
+    if (i < 0) return;
+    const long long d = i % dim;
+    if (d >= rotary) {
+        Y.set(i, X.get(i, err), err);
+        return;
+    }
+    const int half = rotary / 2;
+    const long long pair = d % half, row = i - d, token = i / ((long long)dim * heads);
+    const long long angle = mode == 1 ? pair : (mode == 0 ? (position + token) : token) * half + pair;
+    const float a = X.get(row + pair, err), b = X.get(row + pair + half, err);
+    Y.set(i, rotate(a, b, Cos.get(angle, err), Sin.get(angle, err), d < half), err);
+}
+
+// ---------------------------------------------------------------- reductions over a row
+
+// kernels/strata.cu:121-131: Y[token, row] = W[row] . X[token], 64-lane stride then the tree.
+__global__ void k_gemv(Grid g, FB X, FB W, FB Y, int cols, int rows, int tokens, unsigned *err) {
+    unsigned row, token, z;
+    if (!my_group(g, row, token, z) || (int)row >= rows || (int)token >= tokens) return;
+    const int t = threadIdx.x & 31;
+    float lo = 0.0f, hi = 0.0f;
+    for (int i = t; i < cols; i += STRATA_LANES) {
+        lo = __fadd_rn(lo, __fmul_rn(W.get((long long)row * cols + i, err), X.get((long long)token * cols + i, err)));
+        if (i + 32 < cols)
+            hi = __fadd_rn(hi, __fmul_rn(W.get((long long)row * cols + i + 32, err), X.get((long long)token * cols + i + 32, err)));
+    }
+    const float r = tree64(lo, hi);
+    if (t == 0) Y.set((long long)token * rows + row, r, err);
+}
+
+// kernels/strata.cu:134-153: one row of canonical packed codes (2, 4 or 8 bits, affine or IQ4_NL,
+// scale and optional offset per group) against one input vector.
+__global__ void k_quant_gemv(Grid g, FB X, UB Codes, FB Scales, FB Offsets, FB Y, int cols, int rows, int bits, int groupSize, int bias,
+                             int codebook, int hasOffset, unsigned *err) {
+    unsigned row, y, z;
+    if (!my_group(g, row, y, z) || (int)row >= rows) return;
+    const int t = threadIdx.x & 31;
+    const unsigned mask = (1u << bits) - 1u;
+    float acc[2] = {0.0f, 0.0f};
+    for (int i0 = t; i0 < cols; i0 += STRATA_LANES)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int i = i0 + 32 * h;
+            if (i >= cols) continue;
+            const long long index = (long long)row * cols + i, bit = index * bits;
+            const int code = (int)((Codes.get(bit / 32, err) >> (bit % 32)) & mask);
+            const long long group = index / groupSize;
+            float weight = __fmul_rn(codebook == 1 ? iq4(code) : (float)(code + bias), Scales.get(group, err));
+            if (hasOffset != 0) weight = __fadd_rn(weight, Offsets.get(group, err));
+            acc[h] = __fadd_rn(acc[h], __fmul_rn(weight, X.get(i, err)));
+        }
+    const float r = tree64(acc[0], acc[1]);
+    if (t == 0) Y.set(row, r, err);
+}
+
+// kernels/strata.cu:214-227: mode 0 weighted RMSNorm (gamma row `row % weightRows`), mode 1 L2 norm.
+__global__ void k_norm(Grid g, FB X, FB W, FB Y, int cols, int rows, int weightRows, int mode, float epsilon, float scale, unsigned *err) {
+    unsigned row, y, z;
+    if (!my_group(g, row, y, z) || (int)row >= rows) return;
+    const int t = threadIdx.x & 31;
+    const long long base = (long long)row * cols;
+    float lo = 0.0f, hi = 0.0f;
+    for (int i = t; i < cols; i += STRATA_LANES) {
+        const float a = X.get(base + i, err);
+        lo = __fadd_rn(lo, __fmul_rn(a, a));
+        if (i + 32 < cols) {
+            const float b = X.get(base + i + 32, err);
+            hi = __fadd_rn(hi, __fmul_rn(b, b));
+        }
+    }
+    const float ss = __shfl_sync(0xffffffffu, tree64(lo, hi), 0);
+    const float inv = __fdiv_rn(scale, __fsqrt_rn(__fadd_rn(mode == 0 ? __fdiv_rn(ss, (float)cols) : ss, epsilon)));
+    const long long wbase = (long long)(row % weightRows) * cols;
+    for (int i = t; i < cols; i += 32) {
+        const float w = mode == 0 ? W.get(wbase + i, err) : 1.0f;
+        Y.set(base + i, __fmul_rn(__fmul_rn(X.get(base + i, err), inv), w), err);
+    }
+}
+
+// kernels/strata.cu:367-377: per stream, gate = sigmoid(sign(v) sqrt(max(|v|, 1e-6))) with
+// v = key . query / sqrt(width).
+__global__ void k_ple_gate(Grid g, FB Key, FB Query, FB Gate, int width, int streams, unsigned *err) {
+    unsigned c, y, z;
+    if (!my_group(g, c, y, z) || (int)c >= streams) return;
+    const int t = threadIdx.x & 31;
+    const long long base = (long long)c * width;
+    float lo = 0.0f, hi = 0.0f;
+    for (int d = t; d < width; d += STRATA_LANES) {
+        lo = __fadd_rn(lo, __fmul_rn(Key.get(base + d, err), Query.get(base + d, err)));
+        if (d + 32 < width) hi = __fadd_rn(hi, __fmul_rn(Key.get(base + d + 32, err), Query.get(base + d + 32, err)));
+    }
+    const float dot = tree64(lo, hi);
+    if (t == 0) {
+        const float v = __fdiv_rn(dot, __fsqrt_rn((float)width));
+        const float sign = v > 0.0f ? 1.0f : (v < 0.0f ? -1.0f : 0.0f);
+        Gate.set(c, ref_sigmoid(__fmul_rn(sign, __fsqrt_rn(fmaxf(fabsf(v), 0.000001f)))), err);
+    }
+}
+
+// kernels/strata.cu:386-397: greedy token, the lowest index wins a tie. Every workgroup of the
+// dispatch would write the same answer; one warp computes it.
+__global__ void k_argmax(FB Logits, IB Token, int count, unsigned *err) {
+    const int t = threadIdx.x & 31;
+    float best[2];
+    int id[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        best[h] = -3.402823e38f;
+        id[h] = count;
+        for (int i = t + 32 * h; i < count; i += STRATA_LANES) {
+            const float v = Logits.get(i, err);
+            if (v > best[h] || (v == best[h] && i < id[h])) {
+                best[h] = v;
+                id[h] = i;
+            }
+        }
+    }
+    // The tree: lane l takes lane l + s when that holds a larger value, or an equal one with a
+    // lower index; s = 32 is in-thread, the rest are shuffles.
+    float b = best[0];
+    int k = id[0];
+    if (best[1] > b || (best[1] == b && id[1] < k)) {
+        b = best[1];
+        k = id[1];
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+        const float ob = __shfl_down_sync(0xffffffffu, b, s);
+        const int ok = __shfl_down_sync(0xffffffffu, k, s);
+        if (t < s && (ob > b || (ob == b && ok < k))) {
+            b = ob;
+            k = ok;
+        }
+    }
+    if (t == 0) Token.set(0, k, err);
+}
+
+// ---------------------------------------------------------------- attention
+
+// kernels/strata.cu:334-356 (decode: the Cells list, count cells) and :512-534 (prompt: query
+// token = z, its causal prefix of position + token + 1 cells). One warp per (head, 64-wide
+// output tile); the tile's scores stay in shared memory.
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_attention(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads,
+                                                                   int kvHeads, int count, int position, float scale, int batch,
+                                                                   unsigned *err) {
+    __shared__ float scores_all[kWarpsPerBlock][kMaxCells];
+    unsigned h, tile, token;
+    if (!my_group(g, h, tile, token) || (int)h >= heads) return;
+    float *scores = scores_all[(threadIdx.x / 32) % kWarpsPerBlock];
+    const int t = threadIdx.x & 31;
+    const long long cells = batch ? (long long)position + token + 1 : count;
+    if (cells > kMaxCells || cells < 1) {
+        raise_error(err, kErrIndex);
+        return;
+    }
+    const int n = (int)cells;
+    const int kh = (int)h / (heads / kvHeads);
+    const long long qbase = batch ? ((long long)token * heads + h) * dim : (long long)h * dim;
+    auto cell = [&](int c) -> long long { return batch ? c : Cells.get(c, err); };
+    float mx[2] = {-3.402823e38f, -3.402823e38f};
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+        for (int c = t + 32 * half; c < n; c += STRATA_LANES) {
+            const long long kbase = (cell(c) * kvHeads + kh) * dim;
+            float score = 0.0f;
+            for (int j = 0; j < dim; ++j) score = __fadd_rn(score, __fmul_rn(Q.get(qbase + j, err), Keys.get(kbase + j, err)));
+            score = __fmul_rn(score, scale);
+            scores[c] = score;
+            mx[half] = fmaxf(mx[half], score);
+        }
+    const float m = __shfl_sync(0xffffffffu, max_tree64(mx[0], mx[1]), 0);
+    float sum[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+        for (int c = t + 32 * half; c < n; c += STRATA_LANES) {
+            const float p = ref_expf(__fsub_rn(scores[c], m));
+            scores[c] = p;
+            sum[half] = __fadd_rn(sum[half], p);
+        }
+    const float total = __shfl_sync(0xffffffffu, tree64(sum[0], sum[1]), 0);
+    __syncwarp();
+    const long long ybase = batch ? ((long long)token * heads + h) * dim : (long long)h * dim;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int d = (int)tile * STRATA_LANES + t + 32 * half;
+        if (d >= dim) continue;
+        float value = 0.0f;
+        for (int c = 0; c < n; ++c) value = __fadd_rn(value, __fmul_rn(scores[c], Values.get((cell(c) * kvHeads + kh) * dim + d, err)));
+        Y.set(ybase + d, __fdiv_rn(value, total), err);
+    }
+}
+
+// kernels/strata.cu:328-330 and :453-456
+__global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, int position, int tokens, unsigned *err) {
+    long long i = lane_index(g, (long long)width * tokens);
+    if (i < 0) return;
+    const long long at = (long long)position * width + i;
+    Keys.set(at, K.get(i, err), err);
+    Values.set(at, V.get(i, err), err);
+}
+
+// kernels/strata.cu:357-359 and :457-459: attention output times sigmoid of the gate half of
+// each head's [query | gate] row.
+__global__ void k_attention_gate(Grid g, FB Attention, FB FullQ, FB Y, int dim, int heads, int tokens, unsigned *err) {
+    long long i = lane_index(g, (long long)dim * heads * tokens);
+    if (i >= 0) Y.set(i, __fmul_rn(Attention.get(i, err), ref_sigmoid(FullQ.get((i / dim) * dim * 2 + dim + i % dim, err))), err);
+}
+
+// kernels/strata.cu:314-316
+__global__ void k_slice(Grid g, FB X, FB Y, int width, int rows, int stride, int offset, unsigned *err) {
+    long long i = lane_index(g, (long long)width * rows);
+    if (i >= 0) Y.set(i, X.get((i / width) * stride + offset + i % width, err), err);
+}
+
+// ---------------------------------------------------------------- hyper-connections
+
+// kernels/strata.cu:273-277 and :403-408: mean over streams of norm * sigmoid(gate).
+__global__ void k_hc_mix(Grid g, FB Norm, FB Gate, FB Mixed, int width, int streams, int tokens, unsigned *err) {
+    long long i = lane_index(g, (long long)width * tokens);
+    if (i < 0) return;
+    const long long token = i / width, d = i % width;
+    float v = 0.0f;
+    for (int c = 0; c < streams; ++c) {
+        const long long p = (token * streams + c) * width + d;
+        v = __fadd_rn(v, __fmul_rn(Norm.get(p, err), ref_sigmoid(Gate.get(p, err))));
+    }
+    Mixed.set(i, __fdiv_rn(v, (float)streams), err);
+}
+
+// kernels/strata.cu:278-281 and :409-412: residual += output * 2 sigmoid(inject / streams).
+__global__ void k_hc_write(Grid g, FB Residual, FB Output, FB Inject, int width, int streams, int tokens, unsigned *err) {
+    const long long hc = (long long)width * streams;
+    long long i = lane_index(g, hc * tokens);
+    if (i < 0) return;
+    const float gain = __fmul_rn(2.0f, ref_sigmoid(__fdiv_rn(Inject.get(i / width, err), (float)streams)));
+    Residual.set(i, __fadd_rn(Residual.get(i, err), __fmul_rn(Output.get((i / hc) * width + i % width, err), gain)), err);
+}
+
+// ---------------------------------------------------------------- per-layer embeddings
+
+// kernels/strata.cu:378-380 and :460-463
+__global__ void k_ple_broadcast(Grid g, FB Value, FB Gate, FB Y, int width, int streams, int tokens, unsigned *err) {
+    const long long hc = (long long)width * streams;
+    long long i = lane_index(g, hc * tokens);
+    if (i >= 0) Y.set(i, __fmul_rn(Value.get((i / hc) * width + i % width, err), Gate.get(i / width, err)), err);
+}
+
+// kernels/strata.cu:381-383
+__global__ void k_ple_add(Grid g, FB Residual, FB Gated, FB Conv, int n, unsigned *err) {
+    long long i = lane_index(g, n);
+    if (i >= 0) Residual.set(i, __fadd_rn(Residual.get(i, err), __fadd_rn(Gated.get(i, err), Conv.get(i, err))), err);
+}
+
+// ---------------------------------------------------------------- recurrences
+
+// kernels/strata.cu:287-295 and :413-424: causal convolution over a channel-major history
+// (tap 0 oldest), optional SiLU, then the history shifts by one. One thread per channel walks
+// the tokens in order; neighbouring channels are neighbouring threads.
+__global__ void k_conv(Grid g, FB History, FB X, FB W, FB Y, int channels, int taps, int dilation, int activation, int tokens, int batch,
+                       unsigned *err) {
+    long long c = lane_index(g, channels);
+    if (c < 0) return;
+    const long long history = (long long)(taps - 1) * dilation, hbase = c * history;
+    for (int token = 0; token < tokens; ++token) {
+        const long long at = (long long)token * channels + c;
+        float sum = 0.0f;
+        for (int t = 0; t < taps - 1; ++t)
+            sum = __fadd_rn(sum, __fmul_rn(History.get(hbase + (long long)t * dilation, err), W.get(c * taps + t, err)));
+        const float x = X.get(at, err);
+        sum = __fadd_rn(sum, __fmul_rn(x, W.get(c * taps + taps - 1, err)));
+        Y.set(at, activation == 1 ? ref_silu(sum) : sum, err);
+        for (long long t = 0; t < history - 1; ++t) History.set(hbase + t, History.get(hbase + t + 1, err), err);
+        if (batch || history > 0) History.set(hbase + history - 1, x, err);
+    }
+}
+
+// kernels/strata.cu:296-301 and :425-431: decay = exp(A softplus(alpha + dt)), strength = sigmoid(beta).
+__global__ void k_gdn_gates(Grid g, FB Alpha, FB Beta, FB A, FB Dt, FB Decay, FB Strength, int heads, int tokens, unsigned *err) {
+    long long i = lane_index(g, (long long)heads * tokens);
+    if (i < 0) return;
+    const float x = __fadd_rn(Alpha.get(i, err), Dt.get(i % heads, err));
+    const float sp = x > 20.0f ? x : log_f(__fadd_rn(1.0f, ref_expf(x)));
+    Decay.set(i, ref_expf(__fmul_rn(A.get(i % heads, err), sp)), err);
+    Strength.set(i, ref_sigmoid(Beta.get(i, err)), err);
+}
+
+// kernels/strata.cu:304-313 and :432-444: the gated delta rule. State is [dim_k][valueHeads][dim_v];
+// thread jh owns column jh of every key row, so each of its dim loads is one coalesced row.
+// Value head h reads key head h % keyHeads.
+__global__ void k_gdn(Grid g, FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int dim, int keyHeads, int valueHeads, int tokens,
+                      unsigned *err) {
+    const long long stride = (long long)valueHeads * dim;
+    long long jh = lane_index(g, stride);
+    if (jh < 0) return;
+    const long long h = jh / dim, kh = h % keyHeads;
+    for (int token = 0; token < tokens; ++token) {
+        const long long kbase = ((long long)token * keyHeads + kh) * dim, gh = (long long)token * valueHeads + h;
+        const float decay = Decay.get(gh, err);
+        float prediction = 0.0f;
+        for (int i = 0; i < dim; ++i) {
+            const long long ix = i * stride + jh;
+            const float s = __fmul_rn(State.get(ix, err), decay);
+            State.set(ix, s, err);
+            prediction = __fadd_rn(prediction, __fmul_rn(s, K.get(kbase + i, err)));
+        }
+        const float delta = __fmul_rn(__fsub_rn(V.get(token * stride + jh, err), prediction), Beta.get(gh, err));
+        float result = 0.0f;
+        for (int i = 0; i < dim; ++i) {
+            const long long ix = i * stride + jh;
+            const float s = __fadd_rn(State.get(ix, err), __fmul_rn(K.get(kbase + i, err), delta));
+            State.set(ix, s, err);
+            result = __fadd_rn(result, __fmul_rn(s, Q.get(kbase + i, err)));
+        }
+        Y.set(token * stride + jh, result, err);
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+
+#define SCALAR_TOKENS 1
+cudaError_t L_embedding(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_embedding<<<LANESL>>>(grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, a[12].i,
+                            a[13].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_embed(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_embed<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_embed_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_embed<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, a[4].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_rope_frequencies(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_rope_frequencies<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].f, err);
+    return cudaGetLastError();
+}
+cudaError_t L_rope_table(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_rope_table<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_rope_position(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, 0, err);
+    return cudaGetLastError();
+}
+cudaError_t L_rope(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, SCALAR_TOKENS, 1, err);
+    return cudaGetLastError();
+}
+cudaError_t L_rope_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i, 2, err);
+    return cudaGetLastError();
+}
+cudaError_t L_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_gemv<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_quant_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_quant_gemv<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_norm(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_norm<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].f, a[8].f, err);
+    return cudaGetLastError();
+}
+cudaError_t L_ple_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_ple_gate<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_argmax(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_argmax<<<1, 32, 0, s>>>(F(0), I(1), a[2].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_attention(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_attention<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, 0, a[9].f, 0, err);
+    return cudaGetLastError();
+}
+cudaError_t L_attention_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_attention<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i, a[8].f, 1, err);
+    return cudaGetLastError();
+}
+cudaError_t L_kv_append(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_kv_append_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_attention_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_attention_gate<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_attention_gate_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_attention_gate<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_slice(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_slice<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_hc_mix(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_hc_mix<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_hc_mix_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_hc_mix<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_hc_write(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_hc_write<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_hc_write_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_hc_write<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_ple_broadcast(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_ple_broadcast<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_ple_broadcast_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_ple_broadcast<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_ple_add(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_ple_add<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_conv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_conv<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, SCALAR_TOKENS, 0, err);
+    return cudaGetLastError();
+}
+cudaError_t L_conv_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_conv<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, 1, err);
+    return cudaGetLastError();
+}
+cudaError_t L_gdn_gates(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_gdn_gates<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_gdn_gates_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_gdn_gates<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, a[7].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_gdn_step(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_gdn<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), F(6), a[7].i, a[8].i, a[9].i, SCALAR_TOKENS, err);
+    return cudaGetLastError();
+}
+cudaError_t L_gdn_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_gdn<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), F(6), a[7].i, a[8].i, a[9].i, a[10].i, err);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+// Parameter lists in kernels/strata.cu order and spelling (kinds as in compat.cu's table).
+const KernelSpec kEngineKernels[] = {
+    {"strata_embedding",
+     "Values:f Codes:u Scales:f Offsets:f Residual:f width:I streams:I outputOffset:I format:I bits:I groupSize:I bias:I codebook:I "
+     "hasOffset:I",
+     L_embedding},
+    {"strata_embed", "Row:f Residual:f width:I streams:I", L_embed},
+    {"strata_embed_batch", "Rows:f Residual:f width:I streams:I tokens:I", L_embed_batch},
+    {"strata_rope_frequencies", "High:f Low:f rotary:I base:F", L_rope_frequencies},
+    {"strata_rope_table", "High:f Low:f Cos:f Sin:f rotary:I context:I", L_rope_table},
+    {"strata_rope_position", "X:f Cos:f Sin:f Y:f dim:I heads:I rotary:I position:I tokens:I", L_rope_position},
+    {"strata_rope", "X:f Cos:f Sin:f Y:f dim:I heads:I rotary:I", L_rope},
+    {"strata_rope_batch", "X:f Cos:f Sin:f Y:f dim:I heads:I rotary:I tokens:I", L_rope_batch},
+    {"strata_gemv", "X:f W:f Y:f cols:I rows:I tokens:I", L_gemv},
+    {"strata_quant_gemv", "X:f Codes:u Scales:f Offsets:f Y:f cols:I rows:I bits:I groupSize:I bias:I codebook:I hasOffset:I",
+     L_quant_gemv},
+    {"strata_norm", "X:f W:f Y:f cols:I rows:I weightRows:I mode:I epsilon:F scale:F", L_norm},
+    {"strata_ple_gate", "Key:f Query:f Gate:f width:I streams:I", L_ple_gate},
+    {"strata_argmax", "Logits:f Token:i count:I", L_argmax},
+    {"strata_attention", "Q:f Keys:f Values:f Cells:i Y:f dim:I heads:I kvHeads:I count:I scale:F", L_attention},
+    {"strata_attention_batch", "Q:f Keys:f Values:f Y:f dim:I heads:I kvHeads:I position:I scale:F", L_attention_batch},
+    {"strata_kv_append", "K:f V:f Keys:f Values:f width:I position:I", L_kv_append},
+    {"strata_kv_append_batch", "K:f V:f Keys:f Values:f width:I position:I tokens:I", L_kv_append_batch},
+    {"strata_attention_gate", "Attention:f FullQ:f Y:f dim:I heads:I", L_attention_gate},
+    {"strata_attention_gate_batch", "Attention:f FullQ:f Y:f dim:I heads:I tokens:I", L_attention_gate_batch},
+    {"strata_slice", "X:f Y:f width:I rows:I stride:I offset:I", L_slice},
+    {"strata_hc_mix", "Norm:f Gate:f Mixed:f width:I streams:I", L_hc_mix},
+    {"strata_hc_mix_batch", "Norm:f Gate:f Mixed:f width:I streams:I tokens:I", L_hc_mix_batch},
+    {"strata_hc_write", "Residual:f Output:f Inject:f width:I streams:I", L_hc_write},
+    {"strata_hc_write_batch", "Residual:f Output:f Inject:f width:I streams:I tokens:I", L_hc_write_batch},
+    {"strata_ple_broadcast", "Value:f Gate:f Y:f width:I streams:I", L_ple_broadcast},
+    {"strata_ple_broadcast_batch", "Value:f Gate:f Y:f width:I streams:I tokens:I", L_ple_broadcast_batch},
+    {"strata_ple_add", "Residual:f Gated:f Conv:f n:I", L_ple_add},
+    {"strata_conv", "History:f X:f W:f Y:f channels:I taps:I dilation:I activation:I", L_conv},
+    {"strata_conv_batch", "History:f X:f W:f Y:f channels:I taps:I dilation:I activation:I tokens:I", L_conv_batch},
+    {"strata_gdn_gates", "Alpha:f Beta:f A:f Dt:f Decay:f Strength:f heads:I", L_gdn_gates},
+    {"strata_gdn_gates_batch", "Alpha:f Beta:f A:f Dt:f Decay:f Strength:f heads:I tokens:I", L_gdn_gates_batch},
+    {"strata_gdn_step", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I", L_gdn_step},
+    {"strata_gdn_batch", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I tokens:I", L_gdn_batch},
+};
+const int kNumEngineKernels = sizeof(kEngineKernels) / sizeof(kEngineKernels[0]);
+
+}  // namespace strata

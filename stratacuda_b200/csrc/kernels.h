@@ -29,8 +29,10 @@ struct KernelSpec {
     const char *params;  // "Name:kind ..." with kind f/u/i (buffers) or I/F (scalars)
     Launcher launch;
 };
-extern const KernelSpec kKernels[];
+extern const KernelSpec kKernels[];  // compat.cu: the mixture-of-experts entries
 extern const int kNumKernels;
+extern const KernelSpec kEngineKernels[];  // engine_ops.cu: every other entry of the reference
+extern const int kNumEngineKernels;
 
 // Device view of one mixture-of-experts layer (see strata_moe_layer in include/strata_cuda.h).
 struct MoeLayerDev {

@@ -1,0 +1,655 @@
+"""The reference's model host on this library: a whole decode step and layer-major prompt chunks
+of the hybrid model (gated-delta-net layers with a full-attention layer every `qsaInterval`,
+hyper-connection streams, a per-layer embedding on layer `pleLayer`, and a routed mixture of
+experts with a shared expert), every tensor operation a strata_run() dispatch of the
+reference's own entries.
+
+It follows, call for call:
+
+* ``Ops`` — src/ops.js:5-126 (projection, norm, elementwise, slice, RoPE, embedding, PLE).
+* ``StrataEngine`` — src/engine.js:7-222 (step, prefill, reset, checkpoint / restore).
+* ``PromptBatch`` — src/prefill.js:5-97 and ``prefill_chunks`` — src/prefill.js:99-111.
+
+so that a model run here gives the reference's numbers. Two changes of placement, neither of
+which changes a value:
+
+* Whole-model residency. Every weight is uploaded to HBM once and kept; a projection is one
+  dispatch over all of its rows (the reference streams tiles of at most 256 rows through a
+  bounded cache because its targets have small buffers; each output row is computed alone, so
+  tiling never changed a result).
+* On-device gathers. The token embedding row is copied out of the resident table on the device,
+  and the per-layer-embedding rows are gathered from the resident PLE table with
+  strata_gather_rows; only the n-gram row ids (src/model.js:22-34) come from the host.
+
+The engine takes any backend with the reference protocol (src/backend.js:58-206): ``alloc``,
+``write``, ``read``, ``copy``, ``zero``, ``free``, ``run``, ``idle``. On a B200 that is
+``stratacuda_b200.backend.CudaBackend``.
+"""
+from __future__ import annotations
+
+import math
+import uuid
+
+import numpy as np
+
+from .model import require_integer, validate_geometry
+
+
+def grid(n: int):
+    """src/ops.js:2 — ceil(n / 64) workgroups of 64 lanes."""
+    return [(int(n) + 63) // 64, 1, 1]
+
+
+def _f32(x: float) -> float:
+    return float(np.float32(x))
+
+
+class Ops:
+    """src/ops.js:5-126 with whole-model residency."""
+
+    def __init__(self, backend, store):
+        self.b = backend
+        self.store = store
+        self.g = store.config
+        self.temporary = []
+        self.resident = {}
+        self.rope = None
+
+    # ---- buffers (src/ops.js:13-16)
+    def alloc(self, data_or_length, type: str = "f32"):
+        buf = self.b.alloc(data_or_length, type, zero=False)
+        self.temporary.append(buf)
+        return buf
+
+    def release(self, *buffers) -> None:
+        for buf in buffers:
+            if any(buf is t for t in self.temporary):
+                self.temporary = [t for t in self.temporary if t is not buf]
+                self.b.free(buf)
+
+    def clear_temporary(self) -> None:
+        self.b.idle()
+        for buf in self.temporary:
+            self.b.free(buf)
+        self.temporary = []
+
+    def weight(self, name: str):
+        """The whole tensor, resident in device memory after its first use."""
+        buf = self.resident.get(name)
+        if buf is None:
+            t = self.store.describe(name)
+            if t.get("format", "f32") != "f32":
+                raise ValueError(f"{name}: the engine takes F32 tensors")
+            buf = self.b.alloc(np.ascontiguousarray(t["data"], np.float32), "f32", zero=False)
+            self.resident[name] = buf
+        return buf
+
+    vector = weight  # src/ops.js:117
+
+    # ---- tensor operations
+    def mat(self, name: str, x, tokens: int = 1):
+        """src/ops.js:98-116: Y[token, row] = W[row] . X[token] for every row of `name`."""
+        shape = self.store.describe(name)["shape"]
+        cols, rows = shape[0], int(np.prod(shape[1:])) if len(shape) > 1 else 1
+        if x.length != cols * tokens:
+            raise ValueError(f"{name}: expected {cols * tokens} inputs, got {x.length}")
+        y = self.alloc(rows * tokens)
+        self.b.run("strata_project", dict(X=x, W=self.weight(name), Y=y, cols=cols, rows=rows, tokens=tokens, outputStride=rows,
+                                          outputOffset=0), [rows, tokens, 1])
+        return y
+
+    def norm(self, x, w, cols: int, rows: int = 1, weight_rows: int = 1, mode: int = 0, scale: float = 1.0):
+        """src/ops.js:118-121: RMSNorm (mode 0, gamma row `row % weight_rows`) or L2 norm (mode 1)."""
+        y = self.alloc(cols * rows)
+        self.b.run("strata_norm", dict(X=x, W=w, Y=y, cols=cols, rows=rows, weightRows=weight_rows, mode=mode, epsilon=1e-6,
+                                       scale=_f32(scale)), [rows, 1, 1])
+        return y
+
+    def elem(self, a, b=None, mode: int = 0, scale: float = 1.0):
+        """src/ops.js:122-125."""
+        b = a if b is None else b
+        if a.length != b.length:
+            raise ValueError("Elementwise input shapes disagree")
+        y = self.alloc(a.length)
+        self.b.run("strata_elementwise", dict(A=a, B=b, Y=y, n=a.length, mode=mode, scale=_f32(scale)), grid(a.length))
+        return y
+
+    def slice(self, x, width: int, rows: int = 1, stride: int | None = None, offset: int = 0):
+        """src/ops.js:126-130."""
+        stride = width if stride is None else stride
+        require_integer(width, "slice width")
+        require_integer(rows, "slice rows")
+        if offset < 0 or (rows - 1) * stride + offset + width > x.length:
+            raise ValueError("Slice exceeds buffer")
+        y = self.alloc(width * rows)
+        self.b.run("strata_slice", dict(X=x, Y=y, width=width, rows=rows, stride=stride, offset=offset), grid(width * rows))
+        return y
+
+    def embedding(self, token: int, output, output_offset: int = 0) -> None:
+        """src/ops.js:76-81: the token's row of the resident table into every residual stream."""
+        g = self.g
+        row = self.alloc(g["width"])
+        self.b.copy(self.weight("token_embd.weight"), row, g["width"], token * g["width"], 0)
+        self.b.run("strata_embedding", dict(Values=row, Codes=row, Scales=row, Offsets=row, Residual=output, width=g["width"],
+                                            streams=g["streams"], outputOffset=output_offset, format=0, bits=0, groupSize=1, bias=0,
+                                            codebook=0, hasOffset=0), grid(g["width"]))
+        self.release(row)
+
+    def ple(self, token: int, previous):
+        """src/ops.js:82-86 / src/model.js:70: the token's pleHeads rows of the resident PLE table."""
+        g = self.g
+        ids = self.alloc(self.store.ple_indices(token, previous).astype(np.int32), "i32")
+        out = self.alloc(g["width"])
+        self.b.run("strata_gather_rows", dict(X=self.weight("per_layer_token_embd.weight"), Indices=ids, Y=out, width=g["pleHeadDim"],
+                                              rows=g["pleHeads"]), grid(g["width"]))
+        self.release(ids)
+        return out
+
+    def rotate(self, x, heads: int, position: int, tokens: int = 1):
+        """src/ops.js:87-97: the RoPE table is built once on the device, then rows rotate at `position`."""
+        g = self.g
+        if self.rope is None:
+            half = g["rotary"] // 2
+            cos, sin = self.b.alloc(g["context"] * half), self.b.alloc(g["context"] * half)
+            hi, lo = self.alloc(half), self.alloc(half)
+            self.b.run("strata_rope_frequencies", dict(High=hi, Low=lo, rotary=g["rotary"], base=float(g["ropeBase"])), grid(half))
+            self.b.run("strata_rope_table", dict(High=hi, Low=lo, Cos=cos, Sin=sin, rotary=g["rotary"], context=g["context"]),
+                       grid(g["context"] * half))
+            self.release(hi, lo)
+            self.rope = (cos, sin)
+        y = self.alloc(x.length)
+        self.b.run("strata_rope_position", dict(X=x, Cos=self.rope[0], Sin=self.rope[1], Y=y, dim=g["headDim"], heads=heads,
+                                                rotary=g["rotary"], position=position, tokens=tokens), grid(x.length))
+        return y
+
+    def dispose(self) -> None:
+        self.clear_temporary()
+        for buf in self.resident.values():
+            self.b.free(buf)
+        self.resident = {}
+        if self.rope:
+            for buf in self.rope:
+                self.b.free(buf)
+        self.rope = None
+
+
+class StrataEngine:
+    """src/engine.js:7-222 for one backend (no CPU expert lane: every expert runs on the device)."""
+
+    def __init__(self, store, backend):
+        self.store = store
+        self.g = validate_geometry(store.config)
+        self.b = backend
+        self.ops = Ops(backend, store)
+        self.position = 0
+        self.previous = []
+        self.states = []
+        self.persistent = []
+        self.failed = False
+        self.disposed = False
+        self.owner = str(uuid.uuid4())
+        self.stats = dict(tokens=0, routes=[])
+
+    @classmethod
+    def create(cls, store, backend) -> "StrataEngine":
+        engine = cls(store, backend)
+        try:
+            engine.initialize()
+        except Exception:
+            engine.dispose()
+            raise
+        return engine
+
+    def keep(self, n: int):
+        buf = self.b.alloc(n, "f32", zero=True)
+        self.persistent.append(buf)
+        return buf
+
+    def is_attention(self, layer: int) -> bool:
+        return layer % self.g["qsaInterval"] == self.g["qsaInterval"] - 1
+
+    def expected_shapes(self):
+        """src/engine.js:31-52."""
+        g = self.g
+        hc, c = g["width"] * g["streams"], (2 * g["keyHeads"] + g["valueHeads"]) * g["ssmDim"]
+        specs = []
+        add = lambda name, shape: specs.append((name, shape))
+
+        def gr(prefix, inject=True):
+            add(prefix + "norm.weight", [hc])
+            add(prefix + "down.weight", [hc, g["rank"]])
+            add(prefix + "up.weight", [g["rank"], hc])
+            if inject:
+                add(prefix + "inject.weight", [hc, g["streams"]])
+
+        add("token_embd.weight", [g["width"], g["vocab"]])
+        add("output.weight", [g["width"], g["vocab"]])
+        gr("output_hc_", False)
+        for layer in range(g["layers"]):
+            p = f"blk.{layer}."
+            gr(p + "hc_attn_")
+            gr(p + "hc_ffn_")
+            add(p + "ffn_gate_inp.weight", [g["width"], g["experts"]])
+            add(p + "ffn_gate_inp_shexp.weight", [g["width"]])
+            for role in ("gate", "up", "down"):
+                add(p + "ffn_" + role + "_shexp.weight", [g["ff"], g["width"]] if role == "down" else [g["width"], g["ff"]])
+            for e in range(g["experts"]):
+                for role in ("gate", "up", "down"):
+                    add(p + f"expert.{e}.{role}", [g["ff"], g["width"]] if role == "down" else [g["width"], g["ff"]])
+            if self.is_attention(layer):
+                add(p + "attn_q.weight", [g["width"], 2 * g["heads"] * g["headDim"]])
+                add(p + "attn_k.weight", [g["width"], g["kvHeads"] * g["headDim"]])
+                add(p + "attn_v.weight", [g["width"], g["kvHeads"] * g["headDim"]])
+                add(p + "attn_output.weight", [g["heads"] * g["headDim"], g["width"]])
+                add(p + "attn_q_norm.weight", [g["headDim"]])
+                add(p + "attn_k_norm.weight", [g["headDim"]])
+            else:
+                add(p + "attn_qkv.weight", [g["width"], c])
+                add(p + "attn_gate.weight", [g["width"], g["valueHeads"] * g["ssmDim"]])
+                add(p + "ssm_out.weight", [g["valueHeads"] * g["ssmDim"], g["width"]])
+                add(p + "ssm_conv1d.weight", [4, c])
+                add(p + "ssm_alpha.weight", [g["width"], g["valueHeads"]])
+                add(p + "ssm_beta.weight", [g["width"], g["valueHeads"]])
+                add(p + "ssm_a", [g["valueHeads"]])
+                add(p + "ssm_dt.bias", [g["valueHeads"]])
+                add(p + "ssm_norm.weight", [g["ssmDim"]])
+        p = f"blk.{g['pleLayer']}.ple_"
+        add(p + "key.weight", [g["width"], hc])
+        add(p + "value.weight", [g["width"], g["width"]])
+        for suffix in ("norm_key", "norm_query", "norm_conv"):
+            add(p + suffix + ".weight", [hc])
+        add(p + "conv1d.weight", [g["pleTaps"], hc])
+        return specs
+
+    def initialize(self) -> None:
+        """src/engine.js:53-72: shape gates before any allocation, then the recurrent state."""
+        def trim(shape):
+            shape = list(shape)
+            while len(shape) > 1 and shape[-1] == 1:
+                shape.pop()
+            return shape
+
+        for name, expected in self.expected_shapes():
+            found = trim(self.store.describe(name)["shape"])
+            if found != trim(expected):
+                raise ValueError(f"{name}: expected {expected}, found {found}")
+        g = self.g
+        c = (2 * g["keyHeads"] + g["valueHeads"]) * g["ssmDim"]
+        self.residual = self.keep(g["width"] * g["streams"])
+        self.ple_history = self.keep((g["pleTaps"] - 1) * g["pleDilation"] * g["width"] * g["streams"])
+        for layer in range(g["layers"]):
+            if self.is_attention(layer):
+                kv = g["context"] * g["kvHeads"] * g["headDim"]
+                self.states.append(dict(keys=self.keep(kv), values=self.keep(kv)))
+            else:
+                self.states.append(dict(state=self.keep(g["ssmDim"] * g["valueHeads"] * g["ssmDim"]), conv=self.keep(c * 3)))
+
+    # ---- one token (src/engine.js:73-156)
+    def hc(self, prefix: str, inject: bool = True):
+        g, o = self.g, self.ops
+        norm = o.norm(self.residual, o.vector(prefix + "norm.weight"), g["width"], g["streams"], g["streams"])
+        down = o.mat(prefix + "down.weight", norm)
+        lo = o.elem(down, down, 1, 1 / g["streams"])
+        gate = o.mat(prefix + "up.weight", lo)
+        mixed = o.alloc(g["width"])
+        self.b.run("strata_hc_mix", dict(Norm=norm, Gate=gate, Mixed=mixed, width=g["width"], streams=g["streams"]), grid(g["width"]))
+        return mixed, (o.mat(prefix + "inject.weight", norm) if inject else None)
+
+    def hc_write(self, output, inject) -> None:
+        g = self.g
+        self.b.run("strata_hc_write", dict(Residual=self.residual, Output=output, Inject=inject, width=g["width"], streams=g["streams"]),
+                   grid(g["width"] * g["streams"]))
+
+    def ple(self, token: int) -> None:
+        g, o, b = self.g, self.ops, self.b
+        p, hc = f"blk.{g['pleLayer']}.ple_", g["width"] * g["streams"]
+        emb = o.ple(token, self.previous)
+        key = o.norm(o.mat(p + "key.weight", emb), o.vector(p + "norm_key.weight"), g["width"], g["streams"], g["streams"])
+        query = o.norm(self.residual, o.vector(p + "norm_query.weight"), g["width"], g["streams"], g["streams"])
+        value = o.mat(p + "value.weight", emb)
+        gate, gated = o.alloc(g["streams"]), o.alloc(hc)
+        b.run("strata_ple_gate", dict(Key=key, Query=query, Gate=gate, width=g["width"], streams=g["streams"]), [g["streams"], 1, 1])
+        b.run("strata_ple_broadcast", dict(Value=value, Gate=gate, Y=gated, width=g["width"], streams=g["streams"]), grid(hc))
+        norm = o.norm(gated, o.vector(p + "norm_conv.weight"), g["width"], g["streams"], g["streams"])
+        conv = o.alloc(hc)
+        b.run("strata_conv", dict(History=self.ple_history, X=norm, W=o.vector(p + "conv1d.weight"), Y=conv, channels=hc, taps=g["pleTaps"],
+                                  dilation=g["pleDilation"], activation=1), grid(hc))
+        b.run("strata_ple_add", dict(Residual=self.residual, Gated=gated, Conv=conv, n=hc), grid(hc))
+
+    def gdn(self, layer: int, x):
+        g, o, b = self.g, self.ops, self.b
+        p, st = f"blk.{layer}.", self.states[layer]
+        qk, vn = g["ssmDim"] * g["keyHeads"], g["ssmDim"] * g["valueHeads"]
+        c = 2 * qk + vn
+        qkv = o.mat(p + "attn_qkv.weight", x)
+        convolved = o.alloc(c)
+        b.run("strata_conv", dict(History=st["conv"], X=qkv, W=o.vector(p + "ssm_conv1d.weight"), Y=convolved, channels=c, taps=4,
+                                  dilation=1, activation=1), grid(c))
+        qr, kr, v = o.slice(convolved, qk), o.slice(convolved, qk, 1, qk, qk), o.slice(convolved, vn, 1, vn, 2 * qk)
+        q = o.norm(qr, qr, g["ssmDim"], g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
+        k = o.norm(kr, kr, g["ssmDim"], g["keyHeads"], 1, 1)
+        alpha, beta = o.mat(p + "ssm_alpha.weight", x), o.mat(p + "ssm_beta.weight", x)
+        decay, strength = o.alloc(g["valueHeads"]), o.alloc(g["valueHeads"])
+        b.run("strata_gdn_gates", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
+                                       Strength=strength, heads=g["valueHeads"]), grid(g["valueHeads"]))
+        y = o.alloc(vn)
+        b.run("strata_gdn_step", dict(State=st["state"], Q=q, K=k, V=v, Decay=decay, Beta=strength, Y=y, dim=g["ssmDim"],
+                                      keyHeads=g["keyHeads"], valueHeads=g["valueHeads"]), grid(vn))
+        z = o.mat(p + "attn_gate.weight", x)
+        norm = o.norm(y, o.vector(p + "ssm_norm.weight"), g["ssmDim"], g["valueHeads"])
+        return o.mat(p + "ssm_out.weight", o.elem(norm, z, 4))
+
+    def qsa(self, layer: int, x):
+        g, o, b = self.g, self.ops, self.b
+        p, st, hd = f"blk.{layer}.", self.states[layer], g["headDim"]
+        full = o.mat(p + "attn_q.weight", x)
+        qr = o.slice(full, hd, g["heads"], hd * 2)
+        q = o.rotate(o.norm(qr, o.vector(p + "attn_q_norm.weight"), hd, g["heads"]), g["heads"], self.position)
+        kr = o.mat(p + "attn_k.weight", x)
+        k = o.rotate(o.norm(kr, o.vector(p + "attn_k_norm.weight"), hd, g["kvHeads"]), g["kvHeads"], self.position)
+        v = o.mat(p + "attn_v.weight", x)
+        b.run("strata_kv_append", dict(K=k, V=v, Keys=st["keys"], Values=st["values"], width=g["kvHeads"] * hd, position=self.position),
+              grid(g["kvHeads"] * hd))
+        cells = o.alloc(np.arange(self.position + 1, dtype=np.int32), "i32")
+        attn, gated = o.alloc(g["heads"] * hd), o.alloc(g["heads"] * hd)
+        b.run("strata_attention", dict(Q=q, Keys=st["keys"], Values=st["values"], Cells=cells, Y=attn, dim=hd, heads=g["heads"],
+                                       kvHeads=g["kvHeads"], count=self.position + 1, scale=_f32(1 / math.sqrt(hd))),
+              [g["heads"], (hd + 63) // 64, 1])
+        b.run("strata_attention_gate", dict(Attention=attn, FullQ=full, Y=gated, dim=hd, heads=g["heads"]), grid(g["heads"] * hd))
+        return o.mat(p + "attn_output.weight", gated)
+
+    def expert(self, prefix: str, x, shared: bool = False, tokens: int = 1):
+        """src/engine.js:124-132 for F32 experts: gate and up projections, SiLU(gate) * up, down."""
+        o = self.ops
+        name = (lambda r: prefix + "ffn_" + r + "_shexp.weight") if shared else (lambda r: prefix + r)
+        gate, up = o.mat(name("gate"), x, tokens), o.mat(name("up"), x, tokens)
+        return o.mat(name("down"), o.elem(gate, up, 3), tokens)
+
+    def check_route(self, ids, message: str) -> None:
+        if any(i < 0 or i >= self.g["experts"] for i in ids) or len(set(ids)) != self.g["topK"]:
+            raise RuntimeError(message)
+
+    def moe(self, layer: int, x):
+        g, o, b = self.g, self.ops, self.b
+        p = f"blk.{layer}."
+        logits = o.mat(p + "ffn_gate_inp.weight", x)
+        ids, weights = o.alloc(g["topK"], "i32"), o.alloc(g["topK"])
+        b.run("strata_router", dict(Logits=logits, Ids=ids, Weights=weights, experts=g["experts"], topK=g["topK"]), [1, 1, 1])
+        selected = [int(i) for i in b.read(ids, "i32")]
+        self.check_route(selected, "Invalid expert routing result")
+        self.stats["routes"].append(dict(layer=layer, ids=selected))
+        parts = o.alloc(g["width"] * g["topK"])
+        for index, e in enumerate(selected):
+            result = self.expert(p + f"expert.{e}.", x)
+            b.copy(result, parts, g["width"], 0, index * g["width"])
+        shared = self.expert(p, x, True)
+        shared_gate = o.mat(p + "ffn_gate_inp_shexp.weight", x)
+        y = o.alloc(g["width"])
+        b.run("strata_moe_combine", dict(Parts=parts, Weights=weights, Shared=shared, SharedGate=shared_gate, Y=y, width=g["width"],
+                                         count=g["topK"]), grid(g["width"]))
+        return y
+
+    def _layer(self, layer: int, batch=None) -> None:
+        """One layer: PLE (on its layer), token mixer through the attention hyper-connection, then
+        the mixture of experts through the feed-forward one (src/engine.js:176-182)."""
+        host = batch or self
+        if layer == self.g["pleLayer"]:
+            if batch is None:
+                self.ple(self._token)
+            else:
+                batch.ple()
+        mixed, inject = host.hc(f"blk.{layer}.hc_attn_")
+        y = host.qsa(layer, mixed) if self.is_attention(layer) else host.gdn(layer, mixed)
+        host.hc_write(y, inject)
+        mixed, inject = host.hc(f"blk.{layer}.hc_ffn_")
+        host.hc_write(host.moe(layer, mixed), inject)
+        self.ops.clear_temporary()
+
+    def _predict(self, logits: bool) -> dict:
+        """src/engine.js:186-193 / src/prefill.js:103-108: output hyper-connection, vocabulary
+        projection and greedy argmax."""
+        g, o, b = self.g, self.ops, self.b
+        head, _ = self.hc("output_hc_", False)
+        values = o.mat("output.weight", head)
+        nxt = o.alloc(1, "i32")
+        b.run("strata_argmax", dict(Logits=values, Token=nxt, count=g["vocab"]), [1, 1, 1])
+        result = dict(token=int(b.read(nxt, "i32")[0]))
+        require_integer(result["token"], "generated token", 0, g["vocab"] - 1)
+        if logits:
+            result["logits"] = np.array(b.read(values), np.float32)
+            if not np.all(np.isfinite(result["logits"])):
+                raise RuntimeError("Non-finite logits")
+        return result
+
+    def _check_ready(self) -> None:
+        if self.disposed:
+            raise RuntimeError("Session is disposed")
+        if self.failed:
+            raise RuntimeError("Session failed; reset it before continuing")
+
+    def step(self, token: int, logits: bool = False, predict: bool = True) -> dict:
+        """src/engine.js:172-196: one decode step; returns {position, token[, logits]}."""
+        self._check_ready()
+        if logits and not predict:
+            raise ValueError("Logits require prediction")
+        require_integer(token, "token", 0, self.g["vocab"] - 1)
+        if self.position >= self.g["context"]:
+            raise ValueError("Context capacity reached; reset or create a larger session")
+        self.stats["routes"] = []
+        try:
+            self.ops.embedding(token, self.residual)
+            self._token = token
+            for layer in range(self.g["layers"]):
+                self._layer(layer)
+            result = dict(position=self.position)
+            if predict:
+                result.update(self._predict(logits))
+            self.ops.clear_temporary()
+        except Exception:
+            self.failed = True
+            raise
+        self.previous = (self.previous + [token])[-2:]
+        self.position += 1
+        self.stats["tokens"] += 1
+        return result
+
+    def prefill(self, tokens, chunk_size: int = 16, logits: bool = False, predict: bool = True) -> dict:
+        """src/engine.js:161-168 and src/prefill.js:99-111: layer-major prompt chunks."""
+        self._check_ready()
+        tokens = [int(t) for t in tokens]
+        if not tokens:
+            raise ValueError("Prompt is empty")
+        for t in tokens:
+            require_integer(t, "token", 0, self.g["vocab"] - 1)
+        if self.position + len(tokens) > self.g["context"]:
+            raise ValueError("Context capacity reached")
+        require_integer(chunk_size, "prompt chunk size", 1, 64)
+        if logits and not predict:
+            raise ValueError("Logits require prediction")
+        self.stats["routes"] = []
+        try:
+            for offset in range(0, len(tokens), chunk_size):
+                PromptBatch(self, tokens[offset:offset + chunk_size]).run()
+            result = dict(position=self.position - 1)
+            if predict:
+                result.update(self._predict(logits))
+            self.ops.clear_temporary()
+        except Exception:
+            self.failed = True
+            raise
+        return result
+
+    # ---- session state (src/engine.js:197-222)
+    def reset(self) -> None:
+        self.ops.clear_temporary()
+        for buf in self.persistent:
+            self.b.zero(buf)
+        self.position, self.previous, self.failed = 0, [], False
+
+    def checkpoint(self) -> dict:
+        self._check_ready()
+        return dict(owner=self.owner, geometry=dict(self.g), position=self.position, previous=list(self.previous),
+                    buffers=[np.array(self.b.read(buf), np.float32) for buf in self.persistent])
+
+    def restore(self, state: dict) -> None:
+        bufs = state.get("buffers", [])
+        ok = (state.get("owner") == self.owner and state.get("geometry") == self.g and len(bufs) == len(self.persistent)
+              and all(isinstance(a, np.ndarray) and a.dtype == np.float32 and a.size == p.length and np.all(np.isfinite(a))
+                      for a, p in zip(bufs, self.persistent))
+              and isinstance(state.get("position"), int) and 0 <= state["position"] <= self.g["context"]
+              and len(state.get("previous", [])) == min(state["position"], 2)
+              and all(isinstance(t, int) and 0 <= t < self.g["vocab"] for t in state["previous"]))
+        if not ok:
+            raise ValueError("Checkpoint does not match this model/session geometry")
+        self.ops.clear_temporary()
+        for a, buf in zip(bufs, self.persistent):
+            self.b.write(buf, a)
+        self.position, self.previous, self.failed = state["position"], list(state["previous"]), False
+
+    def dispose(self) -> None:
+        if self.disposed:
+            return
+        self.ops.dispose()
+        for buf in self.persistent:
+            self.b.free(buf)
+        self.persistent = []
+        self.disposed = True
+
+
+class PromptBatch:
+    """src/prefill.js:5-97: one chunk of prompt tokens through every layer, layer by layer; each
+    projection and each routed expert runs once over all of the chunk's tokens."""
+
+    def __init__(self, engine: StrataEngine, tokens):
+        self.e, self.g, self.o, self.b = engine, engine.g, engine.ops, engine.b
+        self.tokens, self.n, self.position = list(tokens), len(tokens), engine.position
+
+    def mat(self, name, x):
+        return self.o.mat(name, x, self.n)
+
+    def hc(self, prefix: str, inject: bool = True):
+        g, o, n = self.g, self.o, self.n
+        norm = o.norm(self.residual, o.vector(prefix + "norm.weight"), g["width"], n * g["streams"], g["streams"])
+        down = self.mat(prefix + "down.weight", norm)
+        gate = self.mat(prefix + "up.weight", o.elem(down, down, 1, 1 / g["streams"]))
+        mixed = o.alloc(n * g["width"])
+        self.b.run("strata_hc_mix_batch", dict(Norm=norm, Gate=gate, Mixed=mixed, width=g["width"], streams=g["streams"], tokens=n),
+                   grid(n * g["width"]))
+        return mixed, (self.mat(prefix + "inject.weight", norm) if inject else None)
+
+    def hc_write(self, output, inject) -> None:
+        g, n = self.g, self.n
+        self.b.run("strata_hc_write_batch", dict(Residual=self.residual, Output=output, Inject=inject, width=g["width"],
+                                                 streams=g["streams"], tokens=n), grid(n * g["width"] * g["streams"]))
+
+    def ple(self) -> None:
+        g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
+        p, hc = f"blk.{g['pleLayer']}.ple_", g["width"] * g["streams"]
+        emb, previous = o.alloc(n * g["width"]), list(e.previous)
+        for i, t in enumerate(self.tokens):
+            row = o.ple(t, previous)
+            b.copy(row, emb, g["width"], 0, i * g["width"])
+            o.release(row)
+            previous = (previous + [t])[-2:]
+        key = o.norm(self.mat(p + "key.weight", emb), o.vector(p + "norm_key.weight"), g["width"], n * g["streams"], g["streams"])
+        query = o.norm(self.residual, o.vector(p + "norm_query.weight"), g["width"], n * g["streams"], g["streams"])
+        value = self.mat(p + "value.weight", emb)
+        gate, gated = o.alloc(n * g["streams"]), o.alloc(n * hc)
+        b.run("strata_ple_gate", dict(Key=key, Query=query, Gate=gate, width=g["width"], streams=n * g["streams"]),
+              [n * g["streams"], 1, 1])
+        b.run("strata_ple_broadcast_batch", dict(Value=value, Gate=gate, Y=gated, width=g["width"], streams=g["streams"], tokens=n),
+              grid(n * hc))
+        norm = o.norm(gated, o.vector(p + "norm_conv.weight"), g["width"], n * g["streams"], g["streams"])
+        conv = o.alloc(n * hc)
+        b.run("strata_conv_batch", dict(History=e.ple_history, X=norm, W=o.vector(p + "conv1d.weight"), Y=conv, channels=hc,
+                                        taps=g["pleTaps"], dilation=g["pleDilation"], activation=1, tokens=n), grid(hc))
+        b.run("strata_ple_add", dict(Residual=self.residual, Gated=gated, Conv=conv, n=n * hc), grid(n * hc))
+
+    def gdn(self, layer: int, x):
+        g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
+        p, st = f"blk.{layer}.", e.states[layer]
+        qk, vn = g["ssmDim"] * g["keyHeads"], g["ssmDim"] * g["valueHeads"]
+        c = 2 * qk + vn
+        qkv = self.mat(p + "attn_qkv.weight", x)
+        convolved = o.alloc(n * c)
+        b.run("strata_conv_batch", dict(History=st["conv"], X=qkv, W=o.vector(p + "ssm_conv1d.weight"), Y=convolved, channels=c, taps=4,
+                                        dilation=1, activation=1, tokens=n), grid(c))
+        qr, kr, v = o.slice(convolved, qk, n, c), o.slice(convolved, qk, n, c, qk), o.slice(convolved, vn, n, c, 2 * qk)
+        q = o.norm(qr, qr, g["ssmDim"], n * g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
+        k = o.norm(kr, kr, g["ssmDim"], n * g["keyHeads"], 1, 1)
+        alpha, beta = self.mat(p + "ssm_alpha.weight", x), self.mat(p + "ssm_beta.weight", x)
+        decay, strength, y = o.alloc(n * g["valueHeads"]), o.alloc(n * g["valueHeads"]), o.alloc(n * vn)
+        b.run("strata_gdn_gates_batch", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
+                                             Strength=strength, heads=g["valueHeads"], tokens=n), grid(n * g["valueHeads"]))
+        b.run("strata_gdn_batch", dict(State=st["state"], Q=q, K=k, V=v, Decay=decay, Beta=strength, Y=y, dim=g["ssmDim"],
+                                       keyHeads=g["keyHeads"], valueHeads=g["valueHeads"], tokens=n), grid(vn))
+        z = self.mat(p + "attn_gate.weight", x)
+        norm = o.norm(y, o.vector(p + "ssm_norm.weight"), g["ssmDim"], n * g["valueHeads"])
+        return self.mat(p + "ssm_out.weight", o.elem(norm, z, 4))
+
+    def qsa(self, layer: int, x):
+        g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
+        p, st, hd = f"blk.{layer}.", e.states[layer], g["headDim"]
+        full = self.mat(p + "attn_q.weight", x)
+        qr = o.slice(full, hd, n * g["heads"], hd * 2)
+        q = o.rotate(o.norm(qr, o.vector(p + "attn_q_norm.weight"), hd, n * g["heads"]), g["heads"], self.position, n)
+        kr = self.mat(p + "attn_k.weight", x)
+        k = o.rotate(o.norm(kr, o.vector(p + "attn_k_norm.weight"), hd, n * g["kvHeads"]), g["kvHeads"], self.position, n)
+        v = self.mat(p + "attn_v.weight", x)
+        b.run("strata_kv_append_batch", dict(K=k, V=v, Keys=st["keys"], Values=st["values"], width=g["kvHeads"] * hd,
+                                             position=self.position, tokens=n), grid(n * g["kvHeads"] * hd))
+        attn = o.alloc(n * g["heads"] * hd)
+        gated = o.alloc(attn.length)
+        b.run("strata_attention_batch", dict(Q=q, Keys=st["keys"], Values=st["values"], Y=attn, dim=hd, heads=g["heads"],
+                                             kvHeads=g["kvHeads"], position=self.position, scale=_f32(1 / math.sqrt(hd))),
+              [g["heads"], (hd + 63) // 64, n])
+        b.run("strata_attention_gate_batch", dict(Attention=attn, FullQ=full, Y=gated, dim=hd, heads=g["heads"], tokens=n),
+              grid(attn.length))
+        return self.mat(p + "attn_output.weight", gated)
+
+    def moe(self, layer: int, x):
+        g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
+        p = f"blk.{layer}."
+        logits = self.mat(p + "ffn_gate_inp.weight", x)
+        ids, weights = o.alloc(n * g["topK"], "i32"), o.alloc(n * g["topK"])
+        b.run("strata_router_batch", dict(Logits=logits, Ids=ids, Weights=weights, experts=g["experts"], topK=g["topK"]), [n, 1, 1])
+        selected = [int(i) for i in b.read(ids, "i32")]
+        groups = {}
+        parts = o.alloc(n * g["topK"] * g["width"])
+        for t in range(n):
+            row = selected[t * g["topK"]:(t + 1) * g["topK"]]
+            e.check_route(row, "Invalid prompt expert routing")
+            e.stats["routes"].append(dict(position=self.position + t, layer=layer, ids=row))
+            for k, expert in enumerate(row):
+                groups.setdefault(expert, []).append((t, t * g["topK"] + k))
+        for expert, jobs in groups.items():
+            indices = o.alloc(np.array([t for t, _ in jobs], np.int32), "i32")
+            rows = o.alloc(len(jobs) * g["width"])
+            b.run("strata_gather_rows", dict(X=x, Indices=indices, Y=rows, width=g["width"], rows=len(jobs)), grid(rows.length))
+            output = e.expert(p + f"expert.{expert}.", rows, False, len(jobs))
+            destinations = o.alloc(np.array([part for _, part in jobs], np.int32), "i32")
+            b.run("strata_scatter_rows", dict(X=output, Indices=destinations, Y=parts, width=g["width"], rows=len(jobs)),
+                  grid(output.length))
+        shared = e.expert(p, x, True, n)
+        shared_gate = self.mat(p + "ffn_gate_inp_shexp.weight", x)
+        y = o.alloc(n * g["width"])
+        b.run("strata_moe_combine_batch", dict(Parts=parts, Weights=weights, Shared=shared, SharedGate=shared_gate, Y=y, width=g["width"],
+                                               count=g["topK"], tokens=n), grid(y.length))
+        return y
+
+    def run(self) -> None:
+        g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
+        hc = g["width"] * g["streams"]
+        self.residual = b.alloc(n * hc)
+        try:
+            for t, token in enumerate(self.tokens):
+                o.embedding(token, self.residual, t * hc)
+            for layer in range(g["layers"]):
+                e._layer(layer, self)
+            b.copy(self.residual, e.residual, hc, (n - 1) * hc, 0)
+            e.position += n
+            e.previous = (e.previous + self.tokens)[-2:]
+            e.stats["tokens"] += n
+        finally:
+            b.idle()
+            b.free(self.residual)
