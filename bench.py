@@ -476,6 +476,51 @@ def prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K):
             "phase_ms_per_step": {k: v / max(1, calls) for k, v in ph.items()}}
 
 
+def run_model_arm(args):
+    """The full-model workload on one GPU: the seeded 48-layer synthetic model
+    (stratacuda_b200.synthetic) resident in HBM, a prompt prefilled in chunks of 64, then greedy
+    decode at batch 1, all through StrataEngine (the reference host's call order). Timed end to
+    end by the host clock around each phase, which ends in the argmax read: the host dispatch
+    of every entry is inside the number. Prints its own JSON line (not the MoE-layer metric)."""
+    from stratacuda_b200.backend import CudaBackend
+    from stratacuda_b200.engine import StrataEngine
+    from stratacuda_b200.synthetic import MODEL_GEOMETRY, MOE_MODES, DeviceStore
+
+    b = CudaBackend(0)
+    g = dict(MODEL_GEOMETRY, layers=args.model_layers)
+    t0 = time.perf_counter()
+    store = DeviceStore(b, g, seed=1)
+    b.idle()
+    t_gen = time.perf_counter() - t0
+    engine = StrataEngine.create(store, b, MOE_MODES[args.mode], graph=not args.no_graph)
+    prompt = np.random.default_rng(7).integers(0, g["vocab"], args.prompt).tolist()
+    for _ in range(max(1, args.warmup // 3)):  # warm-up: pools, RoPE table, the decode graph's capture
+        engine.prefill(prompt[:64], chunk_size=64)
+        engine.step(1)
+        engine.step(2)
+        engine.reset()
+    t0 = time.perf_counter()
+    r = engine.prefill(prompt, chunk_size=64)
+    t_prefill = time.perf_counter() - t0
+    token, tokens = r["token"], []
+    t0 = time.perf_counter()
+    for _ in range(args.decode):
+        token = engine.step(token)["token"]
+        tokens.append(token)
+    t_decode = time.perf_counter() - t0
+    line = {"metric": "full-model tokens/s (prefill; greedy decode b=1)", "workload": "model48", "value": args.decode / t_decode,
+            "unit": "tokens/s", "n_gpus": 1, "prefill_tokens_per_s": args.prompt / t_prefill, "prefill_s": t_prefill,
+            "decode_ms_per_token": 1e3 * t_decode / args.decode, "higher_is_better": True, "dtype": "f32+q2", "data": "synthetic",
+            "moe_mode": args.mode, "decode_graph": not args.no_graph, "generate_s": t_gen, "resident_gb": store.bytes_resident() / 1e9,
+            "config": {"workload": f"{g['layers']}-layer synthetic model, hidden {g['width']}, vocab {g['vocab']}, prompt {args.prompt}, "
+                                   f"decode {args.decode}, chunk 64", "timing": "host clock, end to end"},
+            "first_tokens": tokens[:8]}
+    engine.dispose()
+    store.free()
+    b.dispose()
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -491,6 +536,10 @@ def main():
     ap.add_argument("--ep", action="store_true", help="expert-parallel layer over the ranks (BASELINE config 4)")
     ap.add_argument("--no-graph", action="store_true", help="time direct launches instead of a CUDA graph replay of the K steps")
     ap.add_argument("--ep-tokens", type=int, default=16384, help="tokens of the expert-parallel job (split over the ranks)")
+    ap.add_argument("--model", action="store_true", help="the full-model workload (48-layer synthetic model, 1 GPU)")
+    ap.add_argument("--model-layers", type=int, default=48)
+    ap.add_argument("--prompt", type=int, default=1920, help="--model: prompt tokens (context 2048 = prompt + decode)")
+    ap.add_argument("--decode", type=int, default=128, help="--model: greedy decode tokens")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -498,6 +547,9 @@ def main():
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
         run_reference_arm(args, world, rank)
+        return
+    if args.model:
+        run_model_arm(args)
         return
     world, rank, local = dist_setup(args.gpus)
     try:

@@ -309,6 +309,22 @@ int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params
     } else if (n == "strata_hc_mix" || n == "strata_hc_mix_batch") {
         ok = int_in(I("width")) && int_in(I("streams")) &&
              fits((n == "strata_hc_mix" ? 1 : I("tokens")) * I("streams") * I("width"), "Norm");
+    } else if (n == "strata_embed_token") {
+        ok = int_in(I("width")) && int_in(I("streams")) && int_in(I("vocab")) && fits(I("width") * I("streams"), "Residual") &&
+             fits(I("vocab") * I("width"), "Table") && fits(1, "Token");
+    } else if (n == "strata_rope_at") {
+        for (const char *p : {"rotary", "dim", "heads", "tokens"})
+            if (!int_in(I(p))) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p);
+        if (I("rotary") % 2 || I("rotary") > I("dim") || len("X") != I("dim") * I("heads") * I("tokens") || len("Y") != len("X"))
+            return fail(ctx, STRATA_ERR_LAYOUT, "Invalid RoPE layout");
+        ok = fits(1, "Position");
+    } else if (n == "strata_kv_append_at") {
+        ok = int_in(I("width")) && int_in(I("tokens")) && fits(1, "Position");
+    } else if (n == "strata_attention_at") {
+        for (const char *p : {"heads", "kvHeads", "dim"})
+            if (!int_in(I(p))) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p);
+        if (I("heads") % I("kvHeads")) return fail(ctx, STRATA_ERR_RANGE, "Attention heads must be divisible by KV heads");
+        ok = fits(I("heads") * I("dim"), "Q") && fits(1, "Position");
     }
     if (!ok) return fail(ctx, STRATA_ERR_LAYOUT, "%s: a loop extent exceeds its buffer layout", name);
     return STRATA_OK;

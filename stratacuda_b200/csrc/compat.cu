@@ -76,16 +76,21 @@ __global__ void k_scatter_rows(Grid g, FB X, IB Indices, FB Y, int width, int ro
 // kernels/strata.cu:156-165
 __global__ void k_project(Grid g, FB X, FB W, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset, unsigned *err) {
     unsigned row, token, z;
-    if (!my_group(g, row, token, z)) return;
+    if (!my_group_y_first(g, row, token, z)) return;
     if (!((int)row < rows && (int)token < tokens)) return;
     int t = threadIdx.x & 31;
-    float lo = 0.0f, hi = 0.0f;
-    for (int i = t; i < cols; i += STRATA_LANES) {
-        lo = __fadd_rn(lo, __fmul_rn(W.get((long long)row * cols + i, err), X.get((long long)token * cols + i, err)));
-        if (i + 32 < cols)
-            hi = __fadd_rn(hi, __fmul_rn(W.get((long long)row * cols + i + 32, err), X.get((long long)token * cols + i + 32, err)));
+    const long long wb = (long long)row * cols, xb = (long long)token * cols;
+    float r;
+    if (covers(W, wb, cols) && covers(X, xb, cols)) {
+        r = lane_dot(W.p + wb, X.p + xb, cols, t);
+    } else {  // some index falls outside a buffer: the checked loop reports it
+        float lo = 0.0f, hi = 0.0f;
+        for (int i = t; i < cols; i += STRATA_LANES) {
+            lo = __fadd_rn(lo, __fmul_rn(W.get(wb + i, err), X.get(xb + i, err)));
+            if (i + 32 < cols) hi = __fadd_rn(hi, __fmul_rn(W.get(wb + i + 32, err), X.get(xb + i + 32, err)));
+        }
+        r = tree64(lo, hi);
     }
-    float r = tree64(lo, hi);
     if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
 }
 

@@ -30,6 +30,41 @@ __device__ __forceinline__ int code_of(const UB &b, long long codeOffset, long l
     return (int)((b.get(codeOffset + index / 16, err) >> ((index % 16) * 2)) & 3u) - 1;
 }
 
+// Whether [start, start + count) lies inside the buffer (a warp checks once, then loads unchecked).
+template <typename T>
+__device__ __forceinline__ bool covers(const Buf<T> &b, long long start, long long count) {
+    return start >= 0 && count >= 0 && start + count <= b.n;
+}
+
+// One reference workgroup's strided sum of products over a row of `cols` (thread t of the warp
+// owns lanes t and t + 32), then the shared-memory tree: tree64's result. The pointers must
+// cover [0, cols). Loads are issued eight at a time ahead of the two rounded accumulation
+// chains, which keep the reference's order.
+__device__ __forceinline__ float lane_dot(const float *w, const float *x, int cols, int t) {
+    float lo = 0.0f, hi = 0.0f;
+    int i = t;
+    for (; i + 3 * STRATA_LANES + 32 < cols; i += 4 * STRATA_LANES) {
+        float wv[8], xv[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            wv[2 * k] = w[i + STRATA_LANES * k];
+            xv[2 * k] = x[i + STRATA_LANES * k];
+            wv[2 * k + 1] = w[i + STRATA_LANES * k + 32];
+            xv[2 * k + 1] = x[i + STRATA_LANES * k + 32];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            lo = __fadd_rn(lo, __fmul_rn(wv[2 * k], xv[2 * k]));
+            hi = __fadd_rn(hi, __fmul_rn(wv[2 * k + 1], xv[2 * k + 1]));
+        }
+    }
+    for (; i < cols; i += STRATA_LANES) {
+        lo = __fadd_rn(lo, __fmul_rn(w[i], x[i]));
+        if (i + 32 < cols) hi = __fadd_rn(hi, __fmul_rn(w[i + 32], x[i + 32]));
+    }
+    return tree64(lo, hi);
+}
+
 // kernels/strata.cu:22-31, the IQ4_NL codebook
 __device__ __forceinline__ float iq4(int c) {
     const float t[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f, 1.f, 13.f, 25.f, 38.f, 53.f, 69.f, 89.f, 113.f};
@@ -48,6 +83,18 @@ __device__ __forceinline__ bool my_group(const Grid g, unsigned &gx, unsigned &g
     if (w >= total) return false;
     gx = (unsigned)(w % g.x);
     gy = (unsigned)((w / g.x) % g.y);
+    gz = (unsigned)(w / ((unsigned long long)g.x * g.y));
+    return true;
+}
+
+// The same workgroups with y varying fastest: consecutive warps take consecutive tokens of one
+// weight row, so a prompt chunk reads each row from HBM once (the rest hit L1/L2).
+__device__ __forceinline__ bool my_group_y_first(const Grid g, unsigned &gx, unsigned &gy, unsigned &gz) {
+    unsigned long long w = (unsigned long long)blockIdx.x * kWarpsPerBlock + threadIdx.x / 32;
+    unsigned long long total = (unsigned long long)g.x * g.y * g.z;
+    if (w >= total) return false;
+    gy = (unsigned)(w % g.y);
+    gx = (unsigned)((w / g.y) % g.x);
     gz = (unsigned)(w / ((unsigned long long)g.x * g.y));
     return true;
 }

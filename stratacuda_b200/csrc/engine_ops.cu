@@ -17,6 +17,9 @@
 // against its buffer; an out-of-range index sets the device error word instead of faulting.
 #include "compat.cuh"
 
+#include <algorithm>
+#include <cstdint>
+
 namespace strata {
 namespace {
 
@@ -130,10 +133,11 @@ __global__ void k_rope_table(Grid g, FB High, FB Low, FB Cos, FB Sin, int rotary
 
 // kernels/strata.cu:113-120 (rope_position: table row position + token), :319-327 (rope: one
 // row of Cos / Sin) and :445-452 (rope_batch: table row = token). `mode` 0 / 1 / 2 picks which.
-__global__ void k_rope(Grid g, FB X, FB Cos, FB Sin, FB Y, int dim, int heads, int rotary, int position, int tokens, int mode,
+__global__ void k_rope(Grid g, FB X, FB Cos, FB Sin, FB Y, int dim, int heads, int rotary, int position, int tokens, int mode, IB Pos,
                        unsigned *err) {
     long long i = lane_index(g, (long long)dim * heads * tokens);
     if (i < 0) return;
+    if (Pos.n > 0) position = Pos.get(0, err);  // strata_rope_at: the position lives on the device
     const long long d = i % dim;
     if (d >= rotary) {
         Y.set(i, X.get(i, err), err);
@@ -153,13 +157,18 @@ __global__ void k_gemv(Grid g, FB X, FB W, FB Y, int cols, int rows, int tokens,
     unsigned row, token, z;
     if (!my_group(g, row, token, z) || (int)row >= rows || (int)token >= tokens) return;
     const int t = threadIdx.x & 31;
-    float lo = 0.0f, hi = 0.0f;
-    for (int i = t; i < cols; i += STRATA_LANES) {
-        lo = __fadd_rn(lo, __fmul_rn(W.get((long long)row * cols + i, err), X.get((long long)token * cols + i, err)));
-        if (i + 32 < cols)
-            hi = __fadd_rn(hi, __fmul_rn(W.get((long long)row * cols + i + 32, err), X.get((long long)token * cols + i + 32, err)));
+    const long long wb = (long long)row * cols, xb = (long long)token * cols;
+    float r;
+    if (covers(W, wb, cols) && covers(X, xb, cols)) {
+        r = lane_dot(W.p + wb, X.p + xb, cols, t);
+    } else {
+        float lo = 0.0f, hi = 0.0f;
+        for (int i = t; i < cols; i += STRATA_LANES) {
+            lo = __fadd_rn(lo, __fmul_rn(W.get(wb + i, err), X.get(xb + i, err)));
+            if (i + 32 < cols) hi = __fadd_rn(hi, __fmul_rn(W.get(wb + i + 32, err), X.get(xb + i + 32, err)));
+        }
+        r = tree64(lo, hi);
     }
-    const float r = tree64(lo, hi);
     if (t == 0) Y.set((long long)token * rows + row, r, err);
 }
 
@@ -193,19 +202,31 @@ __global__ void k_norm(Grid g, FB X, FB W, FB Y, int cols, int rows, int weightR
     unsigned row, y, z;
     if (!my_group(g, row, y, z) || (int)row >= rows) return;
     const int t = threadIdx.x & 31;
-    const long long base = (long long)row * cols;
-    float lo = 0.0f, hi = 0.0f;
-    for (int i = t; i < cols; i += STRATA_LANES) {
-        const float a = X.get(base + i, err);
-        lo = __fadd_rn(lo, __fmul_rn(a, a));
-        if (i + 32 < cols) {
-            const float b = X.get(base + i + 32, err);
-            hi = __fadd_rn(hi, __fmul_rn(b, b));
+    const long long base = (long long)row * cols, wbase = (long long)(row % weightRows) * cols;
+    const bool fast = covers(X, base, cols) && covers(Y, base, cols) && (mode != 0 || covers(W, wbase, cols));
+    float ss;
+    if (fast) {
+        ss = lane_dot(X.p + base, X.p + base, cols, t);
+    } else {
+        float lo = 0.0f, hi = 0.0f;
+        for (int i = t; i < cols; i += STRATA_LANES) {
+            const float a = X.get(base + i, err);
+            lo = __fadd_rn(lo, __fmul_rn(a, a));
+            if (i + 32 < cols) {
+                const float b = X.get(base + i + 32, err);
+                hi = __fadd_rn(hi, __fmul_rn(b, b));
+            }
         }
+        ss = tree64(lo, hi);
     }
-    const float ss = __shfl_sync(0xffffffffu, tree64(lo, hi), 0);
+    ss = __shfl_sync(0xffffffffu, ss, 0);
     const float inv = __fdiv_rn(scale, __fsqrt_rn(__fadd_rn(mode == 0 ? __fdiv_rn(ss, (float)cols) : ss, epsilon)));
-    const long long wbase = (long long)(row % weightRows) * cols;
+    if (fast) {
+        const float *x = X.p + base, *w = W.p + wbase;
+        float *y = Y.p + base;
+        for (int i = t; i < cols; i += 32) y[i] = __fmul_rn(__fmul_rn(x[i], inv), mode == 0 ? w[i] : 1.0f);
+        return;
+    }
     for (int i = t; i < cols; i += 32) {
         const float w = mode == 0 ? W.get(wbase + i, err) : 1.0f;
         Y.set(base + i, __fmul_rn(__fmul_rn(X.get(base + i, err), inv), w), err);
@@ -219,12 +240,17 @@ __global__ void k_ple_gate(Grid g, FB Key, FB Query, FB Gate, int width, int str
     if (!my_group(g, c, y, z) || (int)c >= streams) return;
     const int t = threadIdx.x & 31;
     const long long base = (long long)c * width;
-    float lo = 0.0f, hi = 0.0f;
-    for (int d = t; d < width; d += STRATA_LANES) {
-        lo = __fadd_rn(lo, __fmul_rn(Key.get(base + d, err), Query.get(base + d, err)));
-        if (d + 32 < width) hi = __fadd_rn(hi, __fmul_rn(Key.get(base + d + 32, err), Query.get(base + d + 32, err)));
+    float dot;
+    if (covers(Key, base, width) && covers(Query, base, width)) {
+        dot = lane_dot(Key.p + base, Query.p + base, width, t);
+    } else {
+        float lo = 0.0f, hi = 0.0f;
+        for (int d = t; d < width; d += STRATA_LANES) {
+            lo = __fadd_rn(lo, __fmul_rn(Key.get(base + d, err), Query.get(base + d, err)));
+            if (d + 32 < width) hi = __fadd_rn(hi, __fmul_rn(Key.get(base + d + 32, err), Query.get(base + d + 32, err)));
+        }
+        dot = tree64(lo, hi);
     }
-    const float dot = tree64(lo, hi);
     if (t == 0) {
         const float v = __fdiv_rn(dot, __fsqrt_rn((float)width));
         const float sign = v > 0.0f ? 1.0f : (v < 0.0f ? -1.0f : 0.0f);
@@ -273,62 +299,121 @@ __global__ void k_argmax(FB Logits, IB Token, int count, unsigned *err) {
 // ---------------------------------------------------------------- attention
 
 // kernels/strata.cu:334-356 (decode: the Cells list, count cells) and :512-534 (prompt: query
-// token = z, its causal prefix of position + token + 1 cells). One warp per (head, 64-wide
-// output tile); the tile's scores stay in shared memory.
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) k_attention(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads,
-                                                                   int kvHeads, int count, int position, float scale, int batch,
-                                                                   unsigned *err) {
-    __shared__ float scores_all[kWarpsPerBlock][kMaxCells];
-    unsigned h, tile, token;
-    if (!my_group(g, h, tile, token) || (int)h >= heads) return;
-    float *scores = scores_all[(threadIdx.x / 32) % kWarpsPerBlock];
-    const int t = threadIdx.x & 31;
-    const long long cells = batch ? (long long)position + token + 1 : count;
-    if (cells > kMaxCells || cells < 1) {
-        raise_error(err, kErrIndex);
+// token = y, its causal prefix of position + token + 1 cells). One CTA per (head, query token)
+// computes what the reference's (head, 64-wide tile) workgroups compute, each value by the same
+// operations in the same order, without their redundancy:
+//   A. the CTA's threads share out the cells; each score is one thread's in-order sum over the
+//      head dimension (16-byte loads, four in flight), times `scale`, into shared memory;
+//   B. one warp takes the maximum and the exponential sum in the reference's lane order and tree;
+//   C. each output dimension d is one thread's in-order sum over the cells, divided by the sum.
+// A key or value row outside its buffer reads as zeros and is reported.
+constexpr int kAttnThreads = 512;
+__global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads,
+                                                            int kvHeads, int count, int position, float scale, int batch, IB Pos,
+                                                            unsigned *err) {
+    __shared__ float scores[kMaxCells];
+    __shared__ long long value_row[kMaxCells];  // element offset of each cell's value row, or -1
+    __shared__ float total_s;
+    const unsigned h = blockIdx.x, token = blockIdx.y;
+    const int tid = threadIdx.x;
+    if ((int)h >= heads) return;
+    if (Pos.n > 0) position = Pos.get(0, err);  // strata_attention_at: the prefix of one query
+    const long long n = batch ? (long long)position + token + 1 : count;
+    if (n < 1 || n > kMaxCells) {
+        if (tid == 0) raise_error(err, kErrIndex);
         return;
     }
-    const int n = (int)cells;
     const int kh = (int)h / (heads / kvHeads);
     const long long qbase = batch ? ((long long)token * heads + h) * dim : (long long)h * dim;
-    auto cell = [&](int c) -> long long { return batch ? c : Cells.get(c, err); };
-    float mx[2] = {-3.402823e38f, -3.402823e38f};
+    const bool q_ok = covers(Q, qbase, dim);
+    const bool vec = q_ok && dim % 4 == 0 && ((reinterpret_cast<uintptr_t>(Q.p) | reinterpret_cast<uintptr_t>(Keys.p)) & 15) == 0;
+    for (int c = tid; c < n; c += kAttnThreads) {  // A
+        const long long cell = batch ? c : (long long)Cells.get(c, err);
+        const long long kb = (cell * kvHeads + kh) * dim;
+        const bool key_ok = cell >= 0 && covers(Keys, kb, dim), value_ok = cell >= 0 && covers(Values, kb, dim);
+        if (!key_ok || !value_ok) raise_error(err, kErrIndex);
+        float score = 0.0f;
+        if (key_ok && vec) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(Keys.p + kb), *q4 = reinterpret_cast<const float4 *>(Q.p + qbase);
+            const int d4 = dim / 4;
+            int j = 0;
+            for (; j + 4 <= d4; j += 4) {
+                float4 kv[4], qv[4];
 #pragma unroll
-    for (int half = 0; half < 2; ++half)
-        for (int c = t + 32 * half; c < n; c += STRATA_LANES) {
-            const long long kbase = (cell(c) * kvHeads + kh) * dim;
-            float score = 0.0f;
-            for (int j = 0; j < dim; ++j) score = __fadd_rn(score, __fmul_rn(Q.get(qbase + j, err), Keys.get(kbase + j, err)));
-            score = __fmul_rn(score, scale);
-            scores[c] = score;
-            mx[half] = fmaxf(mx[half], score);
+                for (int u = 0; u < 4; ++u) {
+                    kv[u] = k4[j + u];
+                    qv[u] = q4[j + u];
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    score = __fadd_rn(score, __fmul_rn(qv[u].x, kv[u].x));
+                    score = __fadd_rn(score, __fmul_rn(qv[u].y, kv[u].y));
+                    score = __fadd_rn(score, __fmul_rn(qv[u].z, kv[u].z));
+                    score = __fadd_rn(score, __fmul_rn(qv[u].w, kv[u].w));
+                }
+            }
+            for (; j < d4; ++j) {
+                const float4 kv = k4[j], qv = q4[j];
+                score = __fadd_rn(score, __fmul_rn(qv.x, kv.x));
+                score = __fadd_rn(score, __fmul_rn(qv.y, kv.y));
+                score = __fadd_rn(score, __fmul_rn(qv.z, kv.z));
+                score = __fadd_rn(score, __fmul_rn(qv.w, kv.w));
+            }
+        } else if (key_ok) {
+            for (int j = 0; j < dim; ++j) score = __fadd_rn(score, __fmul_rn(Q.get(qbase + j, err), Keys.p[kb + j]));
         }
-    const float m = __shfl_sync(0xffffffffu, max_tree64(mx[0], mx[1]), 0);
-    float sum[2] = {0.0f, 0.0f};
-#pragma unroll
-    for (int half = 0; half < 2; ++half)
-        for (int c = t + 32 * half; c < n; c += STRATA_LANES) {
+        scores[c] = __fmul_rn(score, scale);
+        value_row[c] = value_ok ? kb : -1;
+    }
+    __syncthreads();
+    if (tid < 32) {  // B
+        float mlo = -3.402823e38f, mhi = -3.402823e38f;
+        for (int c = tid; c < n; c += STRATA_LANES) mlo = fmaxf(mlo, scores[c]);
+        for (int c = tid + 32; c < n; c += STRATA_LANES) mhi = fmaxf(mhi, scores[c]);
+        const float m = __shfl_sync(0xffffffffu, max_tree64(mlo, mhi), 0);
+        float slo = 0.0f, shi = 0.0f;
+        for (int c = tid; c < n; c += STRATA_LANES) {
             const float p = ref_expf(__fsub_rn(scores[c], m));
             scores[c] = p;
-            sum[half] = __fadd_rn(sum[half], p);
+            slo = __fadd_rn(slo, p);
         }
-    const float total = __shfl_sync(0xffffffffu, tree64(sum[0], sum[1]), 0);
-    __syncwarp();
-    const long long ybase = batch ? ((long long)token * heads + h) * dim : (long long)h * dim;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        const int d = (int)tile * STRATA_LANES + t + 32 * half;
-        if (d >= dim) continue;
+        for (int c = tid + 32; c < n; c += STRATA_LANES) {
+            const float p = ref_expf(__fsub_rn(scores[c], m));
+            scores[c] = p;
+            shi = __fadd_rn(shi, p);
+        }
+        const float total = tree64(slo, shi);
+        if (tid == 0) total_s = total;
+    }
+    __syncthreads();
+    const float total = total_s;
+    const int dmax = (int)min((long long)dim, (long long)g.y * STRATA_LANES);  // the dispatched 64-wide tiles
+    for (int d = tid; d < dmax; d += kAttnThreads) {  // C
         float value = 0.0f;
-        for (int c = 0; c < n; ++c) value = __fadd_rn(value, __fmul_rn(scores[c], Values.get((cell(c) * kvHeads + kh) * dim + d, err)));
-        Y.set(ybase + d, __fdiv_rn(value, total), err);
+        int c = 0;
+        for (; c + 8 <= n; c += 8) {
+            float vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const long long r = value_row[c + u];
+                vv[u] = r >= 0 ? Values.p[r + d] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) value = __fadd_rn(value, __fmul_rn(scores[c + u], vv[u]));
+        }
+        for (; c < n; ++c) {
+            const long long r = value_row[c];
+            value = __fadd_rn(value, __fmul_rn(scores[c], r >= 0 ? Values.p[r + d] : 0.0f));
+        }
+        Y.set(qbase + d, __fdiv_rn(value, total), err);
     }
 }
 
 // kernels/strata.cu:328-330 and :453-456
-__global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, int position, int tokens, unsigned *err) {
+__global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, int position, int tokens, IB Pos, unsigned *err) {
     long long i = lane_index(g, (long long)width * tokens);
     if (i < 0) return;
+    if (Pos.n > 0) position = Pos.get(0, err);
     const long long at = (long long)position * width + i;
     Keys.set(at, K.get(i, err), err);
     Values.set(at, V.get(i, err), err);
@@ -450,6 +535,91 @@ __global__ void k_gdn(Grid g, FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB 
     }
 }
 
+// The same rule with a block's state tile in shared memory across the tokens (DIM known at compile
+// time, one block of DIM threads per value head): the tile is loaded and stored once per
+// dispatch instead of twice per token, and the head's key and query rows of each token are
+// staged once for all of its columns. Thread x owns column x of the tile (row i at i * DIM + x:
+// conflict-free). Launched only when the host has checked that every index lies in its buffer.
+template <int DIM>
+__global__ void __launch_bounds__(DIM) k_gdn_tile(FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int keyHeads, int valueHeads,
+                                                  int tokens, long long columns) {
+    extern __shared__ float tile[];  // [DIM][DIM]
+    __shared__ float ks[DIM], qs[DIM];
+    const long long stride = (long long)valueHeads * DIM;
+    const long long h = blockIdx.x, jh = h * DIM + threadIdx.x, kh = h % keyHeads;
+    const int x = threadIdx.x;
+    const bool active = jh < columns;
+    if (active)
+        for (int i = 0; i < DIM; ++i) tile[i * DIM + x] = State.p[i * stride + jh];
+    for (int token = 0; token < tokens; ++token) {
+        const long long kbase = ((long long)token * keyHeads + kh) * DIM, gh = (long long)token * valueHeads + h;
+        ks[x] = K.p[kbase + x];
+        qs[x] = Q.p[kbase + x];
+        __syncthreads();
+        if (active) {
+            const float decay = Decay.p[gh];
+            float prediction = 0.0f;
+#pragma unroll 8
+            for (int i = 0; i < DIM; ++i) {
+                const float v = __fmul_rn(tile[i * DIM + x], decay);
+                tile[i * DIM + x] = v;
+                prediction = __fadd_rn(prediction, __fmul_rn(v, ks[i]));
+            }
+            const float delta = __fmul_rn(__fsub_rn(V.p[token * stride + jh], prediction), Beta.p[gh]);
+            float result = 0.0f;
+#pragma unroll 8
+            for (int i = 0; i < DIM; ++i) {
+                const float v = __fadd_rn(tile[i * DIM + x], __fmul_rn(ks[i], delta));
+                tile[i * DIM + x] = v;
+                result = __fadd_rn(result, __fmul_rn(v, qs[i]));
+            }
+            Y.p[token * stride + jh] = result;
+        }
+        __syncthreads();
+    }
+    if (active)
+        for (int i = 0; i < DIM; ++i) State.p[i * stride + jh] = tile[i * DIM + x];
+}
+
+// The shared-memory tile form when dim is 128 and the buffers cover every index, else the checked kernel.
+cudaError_t launch_gdn(const Grid g, const KArg *a, int tokens, cudaStream_t s, unsigned *err) {
+    const int dim = a[7].i, kh = a[8].i, vh = a[9].i;
+    const long long stride = (long long)vh * dim, columns = std::min(stride, (long long)g.x * STRATA_LANES);
+    const bool covered = a[0].len >= (long long)dim * stride && a[1].len >= (long long)tokens * kh * dim &&
+                         a[2].len >= (long long)tokens * kh * dim && a[3].len >= tokens * stride && a[4].len >= (long long)tokens * vh &&
+                         a[5].len >= (long long)tokens * vh && a[6].len >= tokens * stride && kh >= 1 && vh >= 1;
+    if (dim == 128 && covered) {
+        constexpr int kTile = 128 * 128 * 4;
+        cudaError_t e = cudaFuncSetAttribute(k_gdn_tile<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTile);
+        if (e != cudaSuccess) return e;
+        k_gdn_tile<128><<<(unsigned)((columns + 127) / 128), 128, kTile, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), F(6), kh, vh, tokens,
+                                                                             columns);
+    } else {
+        k_gdn<<<(unsigned)(((unsigned long long)g.x * STRATA_LANES + 255) / 256), 256, 0, s>>>(g, F(0), F(1), F(2), F(3), F(4), F(5), F(6),
+                                                                                             dim, kh, vh, tokens, err);
+    }
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- device-position entries
+// No counterpart in the reference: the decode step's four token- or position-dependent
+// dispatches with that value read from a device scalar instead of a kernel argument, so one
+// captured CUDA graph replays every decode step. Each computes exactly what its reference entry
+// computes for the same value.
+
+// strata_embed_token: copy of row Token[0] of the table, then strata_embedding format 0.
+__global__ void k_embed_token(Grid g, FB Table, IB Token, FB Residual, int width, int streams, int vocab, unsigned *err) {
+    long long i = lane_index(g, width);
+    if (i < 0) return;
+    const int t = Token.get(0, err);
+    if (t < 0 || t >= vocab) {
+        raise_error(err, kErrIndex);
+        return;
+    }
+    const float v = Table.get((long long)t * width + i, err);
+    for (int stream = 0; stream < streams; ++stream) Residual.set((long long)stream * width + i, v, err);
+}
+
 // ---------------------------------------------------------------- launchers
 
 #define SCALAR_TOKENS 1
@@ -475,15 +645,32 @@ cudaError_t L_rope_table(const KArg *a, const unsigned g[3], cudaStream_t s, uns
     return cudaGetLastError();
 }
 cudaError_t L_rope_position(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, 0, err);
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, 0, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, SCALAR_TOKENS, 1, err);
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, SCALAR_TOKENS, 1, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i, 2, err);
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i, 2, IB{nullptr, 0}, err);
+    return cudaGetLastError();
+}
+cudaError_t L_embed_token(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_embed_token<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_rope_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[5].i, a[6].i, a[7].i, 0, a[8].i, 0, I(4), err);
+    return cudaGetLastError();
+}
+cudaError_t L_kv_append_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[5].i, 0, a[6].i, I(4), err);
+    return cudaGetLastError();
+}
+cudaError_t L_attention_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    k_attention<<<dim3(g[0], 1), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(4), a[5].i, a[6].i, a[7].i, 0, 0, a[8].f,
+                                                       1, I(3), err);
     return cudaGetLastError();
 }
 cudaError_t L_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -507,19 +694,21 @@ cudaError_t L_argmax(const KArg *a, const unsigned g[3], cudaStream_t s, unsigne
     return cudaGetLastError();
 }
 cudaError_t L_attention(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, 0, a[9].f, 0, err);
+    k_attention<<<dim3(g[0], 1), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, 0, a[9].f, 0,
+                                                       IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i, a[8].f, 1, err);
+    k_attention<<<dim3(g[0], g[2]), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i,
+                                                          a[8].f, 1, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_kv_append(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, SCALAR_TOKENS, err);
+    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, SCALAR_TOKENS, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_kv_append_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, err);
+    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -579,12 +768,10 @@ cudaError_t L_gdn_gates_batch(const KArg *a, const unsigned g[3], cudaStream_t s
     return cudaGetLastError();
 }
 cudaError_t L_gdn_step(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_gdn<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), F(6), a[7].i, a[8].i, a[9].i, SCALAR_TOKENS, err);
-    return cudaGetLastError();
+    return launch_gdn(grid_of(g), a, SCALAR_TOKENS, s, err);
 }
 cudaError_t L_gdn_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_gdn<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), F(6), a[7].i, a[8].i, a[9].i, a[10].i, err);
-    return cudaGetLastError();
+    return launch_gdn(grid_of(g), a, a[10].i, s, err);
 }
 
 }  // namespace
@@ -628,6 +815,11 @@ const KernelSpec kEngineKernels[] = {
     {"strata_gdn_gates_batch", "Alpha:f Beta:f A:f Dt:f Decay:f Strength:f heads:I tokens:I", L_gdn_gates_batch},
     {"strata_gdn_step", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I", L_gdn_step},
     {"strata_gdn_batch", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I tokens:I", L_gdn_batch},
+    // device-position entries (no reference counterpart)
+    {"strata_embed_token", "Table:f Token:i Residual:f width:I streams:I vocab:I", L_embed_token},
+    {"strata_rope_at", "X:f Cos:f Sin:f Y:f Position:i dim:I heads:I rotary:I tokens:I", L_rope_at},
+    {"strata_kv_append_at", "K:f V:f Keys:f Values:f Position:i width:I tokens:I", L_kv_append_at},
+    {"strata_attention_at", "Q:f Keys:f Values:f Position:i Y:f dim:I heads:I kvHeads:I scale:F", L_attention_at},
 };
 const int kNumEngineKernels = sizeof(kEngineKernels) / sizeof(kEngineKernels[0]);
 

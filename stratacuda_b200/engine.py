@@ -19,7 +19,16 @@ which changes a value:
   tiling never changed a result).
 * On-device gathers. The token embedding row is copied out of the resident table on the device,
   and the per-layer-embedding rows are gathered from the resident PLE table with
-  strata_gather_rows; only the n-gram row ids (src/model.js:22-34) come from the host.
+  strata_gather_rows (F32 table) or strata_ple_gather_decode (IQ4_NL table); only the n-gram row
+  ids (src/model.js:22-34) come from the host.
+* Pooled temporaries. A temporary returns to a free list keyed by (length, type) when the
+  reference would free it, and the next allocation of that shape reuses it; all work is ordered
+  on one stream, so reuse needs no synchronisation and a steady-state step allocates nothing.
+
+A store that keeps its weights on the device (stratacuda_b200.synthetic.DeviceStore) hands the
+engine its resident buffers and one fused Q2 mixture-of-experts layer per layer; the engine then
+runs each layer's experts as one strata_moe_forward call (src/engine.js:133-156 and
+src/prefill.js:52-78 collapsed into one dispatch, with no host read of the routed ids).
 
 The engine takes any backend with the reference protocol (src/backend.js:58-206): ``alloc``,
 ``write``, ``read``, ``copy``, ``zero``, ``free``, ``run``, ``idle``. On a B200 that is
@@ -52,29 +61,43 @@ class Ops:
         self.store = store
         self.g = store.config
         self.temporary = []
+        self.pool = {}
         self.resident = {}
         self.rope = None
 
-    # ---- buffers (src/ops.js:13-16)
+    # ---- buffers (src/ops.js:13-16), pooled by (length, type)
     def alloc(self, data_or_length, type: str = "f32"):
-        buf = self.b.alloc(data_or_length, type, zero=False)
+        n = int(data_or_length) if isinstance(data_or_length, (int, np.integer)) else int(np.asarray(data_or_length).size)
+        free = self.pool.get((n, type))
+        if free:
+            buf = free.pop()
+            if not isinstance(data_or_length, (int, np.integer)):
+                self.b.write(buf, np.asarray(data_or_length).ravel())
+        else:
+            buf = self.b.alloc(data_or_length, type, zero=False)
         self.temporary.append(buf)
         return buf
+
+    def _recycle(self, buf) -> None:
+        self.pool.setdefault((buf.length, buf.type), []).append(buf)
 
     def release(self, *buffers) -> None:
         for buf in buffers:
             if any(buf is t for t in self.temporary):
                 self.temporary = [t for t in self.temporary if t is not buf]
-                self.b.free(buf)
+                self._recycle(buf)
 
     def clear_temporary(self) -> None:
-        self.b.idle()
         for buf in self.temporary:
-            self.b.free(buf)
+            self._recycle(buf)
         self.temporary = []
 
     def weight(self, name: str):
-        """The whole tensor, resident in device memory after its first use."""
+        """The whole tensor, resident in device memory (the store's own buffer where it keeps one,
+        else uploaded once on first use)."""
+        on_device = getattr(self.store, "device_buffer", None)
+        if on_device is not None:
+            return on_device(name)
         buf = self.resident.get(name)
         if buf is None:
             t = self.store.describe(name)
@@ -125,9 +148,14 @@ class Ops:
         self.b.run("strata_slice", dict(X=x, Y=y, width=width, rows=rows, stride=stride, offset=offset), grid(width * rows))
         return y
 
-    def embedding(self, token: int, output, output_offset: int = 0) -> None:
-        """src/ops.js:76-81: the token's row of the resident table into every residual stream."""
+    def embedding(self, token: int, output, output_offset: int = 0, device_token=None) -> None:
+        """src/ops.js:76-81: the token's row of the resident table into every residual stream
+        (read from a device scalar with `device_token`: strata_embed_token)."""
         g = self.g
+        if device_token is not None:
+            self.b.run("strata_embed_token", dict(Table=self.weight("token_embd.weight"), Token=device_token, Residual=output,
+                                                  width=g["width"], streams=g["streams"], vocab=g["vocab"]), grid(g["width"]))
+            return
         row = self.alloc(g["width"])
         self.b.copy(self.weight("token_embd.weight"), row, g["width"], token * g["width"], 0)
         self.b.run("strata_embedding", dict(Values=row, Codes=row, Scales=row, Offsets=row, Residual=output, width=g["width"],
@@ -135,17 +163,23 @@ class Ops:
                                             codebook=0, hasOffset=0), grid(g["width"]))
         self.release(row)
 
-    def ple(self, token: int, previous):
-        """src/ops.js:82-86 / src/model.js:70: the token's pleHeads rows of the resident PLE table."""
+    def ple(self, token: int, previous, device_ids=None):
+        """src/ops.js:82-86 / src/model.js:70: the token's pleHeads rows of the resident PLE table
+        (row ids already on the device with `device_ids`)."""
         g = self.g
-        ids = self.alloc(self.store.ple_indices(token, previous).astype(np.int32), "i32")
+        ids = device_ids if device_ids is not None else self.alloc(self.store.ple_indices(token, previous).astype(np.int32), "i32")
         out = self.alloc(g["width"])
+        table = getattr(self.store, "ple_table", None)
+        if table is not None:  # IQ4_NL rows, decoded as they are gathered
+            self.b.ple_gather_decode(table, ids, g["pleHeads"], g["pleHeadDim"], out)
+            self.release(ids)
+            return out
         self.b.run("strata_gather_rows", dict(X=self.weight("per_layer_token_embd.weight"), Indices=ids, Y=out, width=g["pleHeadDim"],
                                               rows=g["pleHeads"]), grid(g["width"]))
         self.release(ids)
         return out
 
-    def rotate(self, x, heads: int, position: int, tokens: int = 1):
+    def rotate(self, x, heads: int, position: int, tokens: int = 1, device_position=None):
         """src/ops.js:87-97: the RoPE table is built once on the device, then rows rotate at `position`."""
         g = self.g
         if self.rope is None:
@@ -158,12 +192,21 @@ class Ops:
             self.release(hi, lo)
             self.rope = (cos, sin)
         y = self.alloc(x.length)
+        if device_position is not None:
+            self.b.run("strata_rope_at", dict(X=x, Cos=self.rope[0], Sin=self.rope[1], Y=y, Position=device_position, dim=g["headDim"],
+                                              heads=heads, rotary=g["rotary"], tokens=tokens), grid(x.length))
+            return y
         self.b.run("strata_rope_position", dict(X=x, Cos=self.rope[0], Sin=self.rope[1], Y=y, dim=g["headDim"], heads=heads,
                                                 rotary=g["rotary"], position=position, tokens=tokens), grid(x.length))
         return y
 
     def dispose(self) -> None:
         self.clear_temporary()
+        self.b.idle()
+        for bufs in self.pool.values():
+            for buf in bufs:
+                self.b.free(buf)
+        self.pool = {}
         for buf in self.resident.values():
             self.b.free(buf)
         self.resident = {}
@@ -176,7 +219,13 @@ class Ops:
 class StrataEngine:
     """src/engine.js:7-222 for one backend (no CPU expert lane: every expert runs on the device)."""
 
-    def __init__(self, store, backend):
+    def __init__(self, store, backend, moe_mode: int = 0, graph: bool = False):
+        self.moe_mode = moe_mode  # fused layers only: 0 exact (bit-identical), 1 fast (tensor cores)
+        # Decode steps replayed from one captured CUDA graph (needs a store with fused layers: a
+        # step then reads nothing back until its argmax).
+        self.use_graph = bool(graph)
+        self._graph = None
+        self._dev = None
         self.store = store
         self.g = validate_geometry(store.config)
         self.b = backend
@@ -191,8 +240,8 @@ class StrataEngine:
         self.stats = dict(tokens=0, routes=[])
 
     @classmethod
-    def create(cls, store, backend) -> "StrataEngine":
-        engine = cls(store, backend)
+    def create(cls, store, backend, moe_mode: int = 0, graph: bool = False) -> "StrataEngine":
+        engine = cls(store, backend, moe_mode, graph)
         try:
             engine.initialize()
         except Exception:
@@ -303,7 +352,7 @@ class StrataEngine:
     def ple(self, token: int) -> None:
         g, o, b = self.g, self.ops, self.b
         p, hc = f"blk.{g['pleLayer']}.ple_", g["width"] * g["streams"]
-        emb = o.ple(token, self.previous)
+        emb = o.ple(token, self.previous, self._dev["ple"] if self._dev_mode else None)
         key = o.norm(o.mat(p + "key.weight", emb), o.vector(p + "norm_key.weight"), g["width"], g["streams"], g["streams"])
         query = o.norm(self.residual, o.vector(p + "norm_query.weight"), g["width"], g["streams"], g["streams"])
         value = o.mat(p + "value.weight", emb)
@@ -342,12 +391,21 @@ class StrataEngine:
     def qsa(self, layer: int, x):
         g, o, b = self.g, self.ops, self.b
         p, st, hd = f"blk.{layer}.", self.states[layer], g["headDim"]
+        dpos = self._dev["position"] if self._dev_mode else None
         full = o.mat(p + "attn_q.weight", x)
         qr = o.slice(full, hd, g["heads"], hd * 2)
-        q = o.rotate(o.norm(qr, o.vector(p + "attn_q_norm.weight"), hd, g["heads"]), g["heads"], self.position)
+        q = o.rotate(o.norm(qr, o.vector(p + "attn_q_norm.weight"), hd, g["heads"]), g["heads"], self.position, device_position=dpos)
         kr = o.mat(p + "attn_k.weight", x)
-        k = o.rotate(o.norm(kr, o.vector(p + "attn_k_norm.weight"), hd, g["kvHeads"]), g["kvHeads"], self.position)
+        k = o.rotate(o.norm(kr, o.vector(p + "attn_k_norm.weight"), hd, g["kvHeads"]), g["kvHeads"], self.position, device_position=dpos)
         v = o.mat(p + "attn_v.weight", x)
+        if dpos is not None:  # the same three dispatches with the position read on the device
+            attn, gated = o.alloc(g["heads"] * hd), o.alloc(g["heads"] * hd)
+            b.run("strata_kv_append_at", dict(K=k, V=v, Keys=st["keys"], Values=st["values"], Position=dpos, width=g["kvHeads"] * hd,
+                                              tokens=1), grid(g["kvHeads"] * hd))
+            b.run("strata_attention_at", dict(Q=q, Keys=st["keys"], Values=st["values"], Position=dpos, Y=attn, dim=hd, heads=g["heads"],
+                                              kvHeads=g["kvHeads"], scale=_f32(1 / math.sqrt(hd))), [g["heads"], (hd + 63) // 64, 1])
+            b.run("strata_attention_gate", dict(Attention=attn, FullQ=full, Y=gated, dim=hd, heads=g["heads"]), grid(g["heads"] * hd))
+            return o.mat(p + "attn_output.weight", gated)
         b.run("strata_kv_append", dict(K=k, V=v, Keys=st["keys"], Values=st["values"], width=g["kvHeads"] * hd, position=self.position),
               grid(g["kvHeads"] * hd))
         cells = o.alloc(np.arange(self.position + 1, dtype=np.int32), "i32")
@@ -369,7 +427,21 @@ class StrataEngine:
         if any(i < 0 or i >= self.g["experts"] for i in ids) or len(set(ids)) != self.g["topK"]:
             raise RuntimeError(message)
 
+    def fused_moe(self, layer: int, x, tokens: int):
+        """The store's fused Q2 layer: router, top-k, routed and shared experts and the combine in
+        one strata_moe_forward call, or None when the store has no fused layers."""
+        fused = getattr(self.store, "moe_layer", None)
+        if fused is None:
+            return None
+        g, o = self.g, self.ops
+        y, ids, weights = o.alloc(tokens * g["width"]), o.alloc(tokens * g["topK"], "i32"), o.alloc(tokens * g["topK"])
+        fused(layer).forward(x, tokens, y, ids, weights, self.moe_mode)
+        return y
+
     def moe(self, layer: int, x):
+        y = self.fused_moe(layer, x, 1)
+        if y is not None:
+            return y
         g, o, b = self.g, self.ops, self.b
         p = f"blk.{layer}."
         logits = o.mat(p + "ffn_gate_inp.weight", x)
@@ -405,14 +477,20 @@ class StrataEngine:
         host.hc_write(host.moe(layer, mixed), inject)
         self.ops.clear_temporary()
 
-    def _predict(self, logits: bool) -> dict:
-        """src/engine.js:186-193 / src/prefill.js:103-108: output hyper-connection, vocabulary
-        projection and greedy argmax."""
-        g, o, b = self.g, self.ops, self.b
+    def _head(self):
+        """Output hyper-connection, vocabulary projection and greedy argmax, without a read."""
+        g, o = self.g, self.ops
         head, _ = self.hc("output_hc_", False)
         values = o.mat("output.weight", head)
         nxt = o.alloc(1, "i32")
-        b.run("strata_argmax", dict(Logits=values, Token=nxt, count=g["vocab"]), [1, 1, 1])
+        self.b.run("strata_argmax", dict(Logits=values, Token=nxt, count=g["vocab"]), [1, 1, 1])
+        return values, nxt
+
+    def _predict(self, logits: bool, head=None) -> dict:
+        """src/engine.js:186-193 / src/prefill.js:103-108: output hyper-connection, vocabulary
+        projection and greedy argmax, then the read of the token (and logits)."""
+        g, b = self.g, self.b
+        values, nxt = head if head is not None else self._head()
         result = dict(token=int(b.read(nxt, "i32")[0]))
         require_integer(result["token"], "generated token", 0, g["vocab"] - 1)
         if logits:
@@ -437,14 +515,17 @@ class StrataEngine:
             raise ValueError("Context capacity reached; reset or create a larger session")
         self.stats["routes"] = []
         try:
-            self.ops.embedding(token, self.residual)
-            self._token = token
-            for layer in range(self.g["layers"]):
-                self._layer(layer)
-            result = dict(position=self.position)
-            if predict:
-                result.update(self._predict(logits))
-            self.ops.clear_temporary()
+            if self.use_graph and predict and getattr(self.store, "moe_layer", None) is not None:
+                result = self._graph_step(token, logits)
+            else:
+                self.ops.embedding(token, self.residual)
+                self._token = token
+                for layer in range(self.g["layers"]):
+                    self._layer(layer)
+                result = dict(position=self.position)
+                if predict:
+                    result.update(self._predict(logits))
+                self.ops.clear_temporary()
         except Exception:
             self.failed = True
             raise
@@ -452,6 +533,45 @@ class StrataEngine:
         self.position += 1
         self.stats["tokens"] += 1
         return result
+
+    _dev_mode = False
+
+    def _device_body(self):
+        """One decode step with the token, position and PLE row ids read from device scalars;
+        returns the (logits, token) buffers of its head."""
+        self._dev_mode = True
+        try:
+            self.ops.embedding(0, self.residual, device_token=self._dev["token"])
+            self._token = None
+            for layer in range(self.g["layers"]):
+                self._layer(layer)
+            head = self._head()
+            self.ops.clear_temporary()
+            return head
+        finally:
+            self._dev_mode = False
+
+    def _graph_step(self, token: int, logits: bool) -> dict:
+        """A decode step replayed from the captured graph. The first one runs eagerly (which also
+        fills the buffer pools and sizes the fused layers' workspace), then the same body is
+        captured; each later step writes three small inputs, replays, and reads the result."""
+        b, g = self.b, self.g
+        if self._dev is None:
+            self._dev = dict(token=b.alloc(1, "i32"), position=b.alloc(1, "i32"), ple=b.alloc(g["pleHeads"], "i32"))
+        b.write(self._dev["token"], np.array([token], np.int32))
+        b.write(self._dev["position"], np.array([self.position], np.int32))
+        b.write(self._dev["ple"], self.store.ple_indices(token, self.previous).astype(np.int32))
+        if self._graph is None:
+            head = self._device_body()
+            result = dict(position=self.position, **self._predict(logits, head))
+            b.capture_begin()
+            try:
+                self._graph_head = self._device_body()
+            finally:
+                self._graph = b.capture_end()
+            return result
+        b.graph_launch(self._graph)
+        return dict(position=self.position, **self._predict(logits, self._graph_head))
 
     def prefill(self, tokens, chunk_size: int = 16, logits: bool = False, predict: bool = True) -> dict:
         """src/engine.js:161-168 and src/prefill.js:99-111: layer-major prompt chunks."""
@@ -509,11 +629,18 @@ class StrataEngine:
     def dispose(self) -> None:
         if self.disposed:
             return
+        if self._graph is not None:
+            self.b.graph_free(self._graph)
+            self._graph = None
+        for buf in (self._dev or {}).values():
+            self.b.free(buf)
+        self._dev = None
         self.ops.dispose()
         for buf in self.persistent:
             self.b.free(buf)
         self.persistent = []
         self.disposed = True
+        self.b.idle()
 
 
 class PromptBatch:
@@ -608,6 +735,9 @@ class PromptBatch:
         return self.mat(p + "attn_output.weight", gated)
 
     def moe(self, layer: int, x):
+        y = self.e.fused_moe(layer, x, self.n)
+        if y is not None:
+            return y
         g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
         p = f"blk.{layer}."
         logits = self.mat(p + "ffn_gate_inp.weight", x)

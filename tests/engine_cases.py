@@ -97,7 +97,7 @@ def cases():
         add("strata_argmax", (1, 1, 1), dict(Logits=logits, Token=np.full(1, -1, np.int32), count=count), ["Token"])
 
     # attention (kernels/strata.cu:328-359, :453-459, :512-534)
-    for dim, count in [(70, 65), (8, 3), (64, 200)]:
+    for dim, count in [(70, 65), (8, 3), (64, 200), (256, 2048)]:
         heads, kv = 4, 2
         total = count + 5
         cells = rng.permutation(total)[:count].astype(np.int32)
@@ -105,7 +105,7 @@ def cases():
             dict(Q=_f(rng, heads * dim, 0.2), Keys=_f(rng, total * kv * dim), Values=_f(rng, total * kv * dim), Cells=cells,
                  Y=np.zeros(heads * dim, np.float32), dim=dim, heads=heads, kvHeads=kv, count=count,
                  scale=float(np.float32(1 / np.sqrt(dim)))), ["Y"])
-    for dim, position, tokens in [(16, 3, 4), (72, 0, 2)]:
+    for dim, position, tokens in [(16, 3, 4), (72, 0, 2), (256, 300, 3)]:
         heads, kv = 4, 2
         add("strata_attention_batch", (heads, (dim + 63) // 64, tokens),
             dict(Q=_f(rng, tokens * heads * dim, 0.3), Keys=_f(rng, (position + tokens) * kv * dim),
@@ -157,7 +157,7 @@ def cases():
                                                          Dt=_f(rng, heads), Decay=np.zeros(3 * heads, np.float32),
                                                          Strength=np.zeros(3 * heads, np.float32), heads=heads, tokens=3),
         ["Decay", "Strength"], ulps=1)
-    for dim, kh, vh, tokens in [(8, 2, 4, 1), (32, 2, 6, 3)]:
+    for dim, kh, vh, tokens in [(8, 2, 4, 1), (32, 2, 6, 3), (128, 2, 4, 1), (128, 2, 4, 5)]:
         vn = dim * vh
         args = dict(State=_f(rng, dim * vn, 0.3), Q=_f(rng, tokens * kh * dim, 0.3), K=_f(rng, tokens * kh * dim, 0.3),
                     V=_f(rng, tokens * vn), Decay=rng.uniform(0.5, 1.0, tokens * vh).astype(np.float32),
