@@ -504,9 +504,17 @@ def run_model_arm(args):
     t_prefill = time.perf_counter() - t0
     token, tokens = r["token"], []
     t0 = time.perf_counter()
-    for _ in range(args.decode):
+    for k in range(args.decode):
+        last = args.profile_step and k == args.decode - 1
+        if last:  # only this step is inside an `ncu --profile-from-start off` capture
+            import torch
+            b.idle()
+            torch.cuda.cudart().cudaProfilerStart()
         token = engine.step(token)["token"]
         tokens.append(token)
+        if last:
+            b.idle()
+            torch.cuda.cudart().cudaProfilerStop()
     t_decode = time.perf_counter() - t0
     line = {"metric": "full-model tokens/s (prefill; greedy decode b=1)", "workload": "model48", "value": args.decode / t_decode,
             "unit": "tokens/s", "n_gpus": 1, "prefill_tokens_per_s": args.prompt / t_prefill, "prefill_s": t_prefill,
@@ -540,6 +548,8 @@ def main():
     ap.add_argument("--model-layers", type=int, default=48)
     ap.add_argument("--prompt", type=int, default=1920, help="--model: prompt tokens (context 2048 = prompt + decode)")
     ap.add_argument("--decode", type=int, default=128, help="--model: greedy decode tokens")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="--model: bracket the last decode step with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -1,4 +1,6 @@
-"""TEST INFRASTRUCTURE. The reference backend protocol (src/backend.js:58-206: alloc, write, read,
+"""TEST INFRASTRUCTURE (oracle). Only tests/ and __graft_entry__.smoke() use it, as the checker.
+
+The reference backend protocol (src/backend.js:58-206: alloc, write, read,
 copy, zero, free, run, idle) over host arrays, dispatching every entry to an Oracle: the C
 restatement or the reference's own compiled kernels. It lets the engine host
 (stratacuda_b200.engine) run a whole model on the CPU checker, as the reference runs on its
@@ -7,7 +9,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from oracle.oracle import SIGNATURES
+from .oracle import SIGNATURES
 
 _DT = {"f32": np.float32, "i32": np.int32, "u32": np.uint32}
 _VIEW = {"f*": np.float32, "u*": np.uint32, "i*": np.int32}

@@ -12,6 +12,8 @@
 #include "route.cuh"
 #include "compat.cuh"
 
+#include <algorithm>
+
 namespace strata {
 namespace {
 
@@ -92,6 +94,24 @@ __global__ void k_project(Grid g, FB X, FB W, FB Y, int cols, int rows, int toke
         r = tree64(lo, hi);
     }
     if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
+}
+
+// The same projection for dispatches with few (row, token) pairs: one block per pair stages the
+// weight row and the input row in shared memory with all its threads (every load in flight at
+// once), then one warp forms the reference's strided sums and tree from shared memory. The host
+// launches it only when the buffers cover every row it reads.
+constexpr int kStagedThreads = 256;
+__global__ void __launch_bounds__(kStagedThreads) k_project_staged(FB X, FB W, FB Y, int cols, int outputStride, int outputOffset,
+                                                                   unsigned *err) {
+    extern __shared__ float staged[];  // [cols] weights, then [cols] inputs
+    const long long row = blockIdx.x, token = blockIdx.y;
+    stage_row(staged, W.p + row * cols, cols);
+    stage_row(staged + cols, X.p + token * cols, cols);
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float r = lane_dot(staged, staged + cols, cols, threadIdx.x);
+        if (threadIdx.x == 0) Y.set(token * outputStride + outputOffset + row, r, err);
+    }
 }
 
 // kernels/strata.cu:168-176
@@ -296,6 +316,18 @@ cudaError_t L_q2_down(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
     return cudaGetLastError();
 }
 cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    // few (row, token) pairs of long rows: one staging block per pair (the pairs the dispatch
+    // names, rows < g[0] and tokens < g[1]; z repeats them)
+    const long long cols = a[3].i, rows = std::min<long long>(a[4].i, g[0]), tokens = std::min<long long>(a[5].i, g[1]);
+    const size_t bytes = (size_t)cols * 8;
+    if (rows * tokens <= 2048 && cols >= 512 && bytes <= 200 * 1024 && a[1].len >= rows * cols && a[0].len >= tokens * cols &&
+        rows > 0 && tokens > 0) {
+        cudaError_t e = cudaFuncSetAttribute(k_project_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return e;
+        k_project_staged<<<dim3((unsigned)rows, (unsigned)tokens), kStagedThreads, bytes, s>>>(F(0), F(1), F(2), a[3].i, a[6].i, a[7].i,
+                                                                                                err);
+        return cudaGetLastError();
+    }
     k_project<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);
     return cudaGetLastError();
 }

@@ -4,6 +4,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cstdint>
+
 namespace strata {
 
 template <typename T>
@@ -63,6 +65,20 @@ __device__ __forceinline__ float lane_dot(const float *w, const float *x, int co
         if (i + 32 < cols) hi = __fadd_rn(hi, __fmul_rn(w[i + 32], x[i + 32]));
     }
     return tree64(lo, hi);
+}
+
+// Copy n floats from global memory into shared memory with all threads of the block, 16 bytes
+// at a time where both sides allow it.
+__device__ __forceinline__ void stage_row(float *dst, const float *src, int n) {
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        const int n4 = n / 4;
+        const float4 *s4 = reinterpret_cast<const float4 *>(src);
+        float4 *d4 = reinterpret_cast<float4 *>(dst);
+        for (int k = threadIdx.x; k < n4; k += blockDim.x) d4[k] = s4[k];
+        for (int k = n4 * 4 + threadIdx.x; k < n; k += blockDim.x) dst[k] = src[k];
+    } else {
+        for (int k = threadIdx.x; k < n; k += blockDim.x) dst[k] = src[k];
+    }
 }
 
 // kernels/strata.cu:22-31, the IQ4_NL codebook

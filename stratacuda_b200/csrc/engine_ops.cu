@@ -224,13 +224,46 @@ __global__ void k_norm(Grid g, FB X, FB W, FB Y, int cols, int rows, int weightR
     if (fast) {
         const float *x = X.p + base, *w = W.p + wbase;
         float *y = Y.p + base;
-        for (int i = t; i < cols; i += 32) y[i] = __fmul_rn(__fmul_rn(x[i], inv), mode == 0 ? w[i] : 1.0f);
+        int i = t;
+        for (; i + 7 * 32 < cols; i += 8 * 32) {  // eight loads of each row in flight, then the stores
+            float xv[8], wv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                xv[u] = x[i + 32 * u];
+                wv[u] = mode == 0 ? w[i + 32 * u] : 1.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) y[i + 32 * u] = __fmul_rn(__fmul_rn(xv[u], inv), wv[u]);
+        }
+        for (; i < cols; i += 32) y[i] = __fmul_rn(__fmul_rn(x[i], inv), mode == 0 ? w[i] : 1.0f);
         return;
     }
     for (int i = t; i < cols; i += 32) {
         const float w = mode == 0 ? W.get(wbase + i, err) : 1.0f;
         Y.set(base + i, __fmul_rn(__fmul_rn(X.get(base + i, err), inv), w), err);
     }
+}
+
+// The same norm with one block per row for long rows: the block stages the row (and its gamma
+// row) in shared memory, one warp forms the sum of squares in the reference's order, and every
+// thread writes its share of the outputs. Launched only when the buffers cover every row.
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) k_norm_staged(FB X, FB W, FB Y, int cols, int weightRows, int mode, float epsilon,
+                                                              float scale) {
+    extern __shared__ float staged[];  // [cols] row, then [cols] gamma (mode 0)
+    __shared__ float inv_s;
+    const long long row = blockIdx.x, base = row * cols;
+    stage_row(staged, X.p + base, cols);
+    if (mode == 0) stage_row(staged + cols, W.p + (row % weightRows) * cols, cols);
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float ss = lane_dot(staged, staged, cols, threadIdx.x);
+        if (threadIdx.x == 0) inv_s = __fdiv_rn(scale, __fsqrt_rn(__fadd_rn(mode == 0 ? __fdiv_rn(ss, (float)cols) : ss, epsilon)));
+    }
+    __syncthreads();
+    const float inv = inv_s;
+    for (int i = threadIdx.x; i < cols; i += kNormThreads)
+        Y.p[base + i] = __fmul_rn(__fmul_rn(staged[i], inv), mode == 0 ? staged[cols + i] : 1.0f);
 }
 
 // kernels/strata.cu:367-377: per stream, gate = sigmoid(sign(v) sqrt(max(|v|, 1e-6))) with
@@ -258,42 +291,69 @@ __global__ void k_ple_gate(Grid g, FB Key, FB Query, FB Gate, int width, int str
     }
 }
 
-// kernels/strata.cu:386-397: greedy token, the lowest index wins a tie. Every workgroup of the
-// dispatch would write the same answer; one warp computes it.
-__global__ void k_argmax(FB Logits, IB Token, int count, unsigned *err) {
-    const int t = threadIdx.x & 31;
-    float best[2];
-    int id[2];
+// kernels/strata.cu:386-397: greedy token, the lowest index wins a tie. The reference's answer is
+// the element that is largest under (value, then lower index), among values that are not NaN and
+// not below -3.402823e38 (else `count`): a maximum under a total order, which any reduction order
+// reaches. One block of 1024 threads takes it with the reference's comparison (loads eight ahead),
+// then warp shuffles and a shared-memory round combine the threads' bests.
+constexpr int kArgmaxThreads = 1024;
+__device__ __forceinline__ bool takes(float v, int i, float best, int id) { return v > best || (v == best && i < id); }
+__global__ void __launch_bounds__(kArgmaxThreads) k_argmax(FB Logits, IB Token, int count, unsigned *err) {
+    __shared__ float wbest[kArgmaxThreads / 32];
+    __shared__ int wid[kArgmaxThreads / 32];
+    const int tid = threadIdx.x, t = tid & 31, w = tid / 32;
+    float best = -3.402823e38f;
+    int id = count;
+    const bool fast = covers(Logits, 0, count);
+    int i = tid;
+    if (fast) {
+        for (; i + 7 * kArgmaxThreads < count; i += 8 * kArgmaxThreads) {
+            float v[8];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        best[h] = -3.402823e38f;
-        id[h] = count;
-        for (int i = t + 32 * h; i < count; i += STRATA_LANES) {
-            const float v = Logits.get(i, err);
-            if (v > best[h] || (v == best[h] && i < id[h])) {
-                best[h] = v;
-                id[h] = i;
-            }
+            for (int u = 0; u < 8; ++u) v[u] = Logits.p[i + u * kArgmaxThreads];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (takes(v[u], i + u * kArgmaxThreads, best, id)) {
+                    best = v[u];
+                    id = i + u * kArgmaxThreads;
+                }
         }
     }
-    // The tree: lane l takes lane l + s when that holds a larger value, or an equal one with a
-    // lower index; s = 32 is in-thread, the rest are shuffles.
-    float b = best[0];
-    int k = id[0];
-    if (best[1] > b || (best[1] == b && id[1] < k)) {
-        b = best[1];
-        k = id[1];
+    for (; i < count; i += kArgmaxThreads) {
+        const float v = Logits.get(i, err);
+        if (takes(v, i, best, id)) {
+            best = v;
+            id = i;
+        }
     }
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) {
-        const float ob = __shfl_down_sync(0xffffffffu, b, s);
-        const int ok = __shfl_down_sync(0xffffffffu, k, s);
-        if (t < s && (ob > b || (ob == b && ok < k))) {
-            b = ob;
-            k = ok;
+        const float ob = __shfl_down_sync(0xffffffffu, best, s);
+        const int oi = __shfl_down_sync(0xffffffffu, id, s);
+        if (takes(ob, oi, best, id)) {
+            best = ob;
+            id = oi;
         }
     }
-    if (t == 0) Token.set(0, k, err);
+    if (t == 0) {
+        wbest[w] = best;
+        wid[w] = id;
+    }
+    __syncthreads();
+    if (w == 0) {
+        best = wbest[t];
+        id = wid[t];
+#pragma unroll
+        for (int s = 16; s > 0; s >>= 1) {
+            const float ob = __shfl_down_sync(0xffffffffu, best, s);
+            const int oi = __shfl_down_sync(0xffffffffu, id, s);
+            if (takes(ob, oi, best, id)) {
+                best = ob;
+                id = oi;
+            }
+        }
+        if (t == 0) Token.set(0, id, err);
+    }
 }
 
 // ---------------------------------------------------------------- attention
@@ -391,15 +451,15 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Key
     for (int d = tid; d < dmax; d += kAttnThreads) {  // C
         float value = 0.0f;
         int c = 0;
-        for (; c + 8 <= n; c += 8) {
-            float vv[8];
+        for (; c + 16 <= n; c += 16) {  // sixteen value loads in flight ahead of the ordered sum
+            float vv[16];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 16; ++u) {
                 const long long r = value_row[c + u];
                 vv[u] = r >= 0 ? Values.p[r + d] : 0.0f;
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) value = __fadd_rn(value, __fmul_rn(scores[c + u], vv[u]));
+            for (int u = 0; u < 16; ++u) value = __fadd_rn(value, __fmul_rn(scores[c + u], vv[u]));
         }
         for (; c < n; ++c) {
             const long long r = value_row[c];
@@ -682,6 +742,16 @@ cudaError_t L_quant_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, uns
     return cudaGetLastError();
 }
 cudaError_t L_norm(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const long long cols = a[3].i, rows = std::min<long long>(a[4].i, g[0]), wrows = a[5].i;
+    const int mode = a[6].i;
+    const size_t bytes = (size_t)cols * (mode == 0 ? 8 : 4);
+    if (cols >= 512 && bytes <= 200 * 1024 && rows > 0 && wrows > 0 && a[0].len >= rows * cols && a[2].len >= rows * cols &&
+        (mode != 0 || a[1].len >= std::min(rows, wrows) * cols)) {
+        cudaError_t e = cudaFuncSetAttribute(k_norm_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return e;
+        k_norm_staged<<<(unsigned)rows, kNormThreads, bytes, s>>>(F(0), F(1), F(2), a[3].i, a[5].i, mode, a[7].f, a[8].f);
+        return cudaGetLastError();
+    }
     k_norm<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].f, a[8].f, err);
     return cudaGetLastError();
 }
@@ -690,7 +760,7 @@ cudaError_t L_ple_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsig
     return cudaGetLastError();
 }
 cudaError_t L_argmax(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_argmax<<<1, 32, 0, s>>>(F(0), I(1), a[2].i, err);
+    k_argmax<<<1, kArgmaxThreads, 0, s>>>(F(0), I(1), a[2].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {

@@ -87,13 +87,25 @@ def cases():
     x = _f(rng, 4 * 8)
     add("strata_norm", (4, 1, 1), dict(X=x, W=x, Y=np.zeros(32, np.float32), cols=8, rows=4, weightRows=1, mode=1, epsilon=1e-6,
                                        scale=float(np.float32(1 / np.sqrt(8)))), ["Y"])
+    # long rows: one staging block per row (norms) or per (row, token) pair (projections)
+    x = _f(rng, 4 * 2048)
+    add("strata_norm", (4, 1, 1), dict(X=x, W=_f(rng, 2 * 2048), Y=np.zeros(4 * 2048, np.float32), cols=2048, rows=4, weightRows=2,
+                                       mode=0, epsilon=1e-6, scale=1.0), ["Y"])
+    x = _f(rng, 3 * 515)
+    add("strata_norm", (3, 1, 1), dict(X=x, W=x, Y=np.zeros(3 * 515, np.float32), cols=515, rows=3, weightRows=1, mode=1, epsilon=1e-6,
+                                       scale=float(np.float32(0.125))), ["Y"])
+    for cols, rows, tokens in [(2048, 7, 3), (8192, 4, 1), (600, 5, 2)]:
+        add("strata_project", (rows, tokens, 1), dict(X=_f(rng, cols * tokens), W=_f(rng, rows * cols), Y=np.zeros(rows * tokens + 3, np.float32),
+                                                      cols=cols, rows=rows, tokens=tokens, outputStride=rows + 1, outputOffset=1), ["Y"])
     key, query = _f(rng, 5 * 40), _f(rng, 5 * 40)
     key[40:80] = 0.0  # a zero dot product: sign 0, gate sigmoid(0)
     add("strata_ple_gate", (5, 1, 1), dict(Key=key, Query=query, Gate=np.zeros(5, np.float32), width=40, streams=5), ["Gate"])
-    for count in [1000, 40, 3]:
+    for count in [1000, 40, 3, 70000]:
         logits = _f(rng, count)
         if count > 3:
             logits[[7, count - 5, count // 2]] = logits.max() + 1.0  # a three-way tie at the top
+        if count > 1000:
+            logits[[3, 9000, 51234]] = np.nan  # never taken
         add("strata_argmax", (1, 1, 1), dict(Logits=logits, Token=np.full(1, -1, np.int32), count=count), ["Token"])
 
     # attention (kernels/strata.cu:328-359, :453-459, :512-534)

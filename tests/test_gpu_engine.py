@@ -9,7 +9,7 @@ import pytest
 from engine_conformance import run_conformance
 from oracle.engine_ref import compare
 from oracle.oracle import Oracle
-from oracle_backend import OracleBackend
+from oracle.backend import OracleBackend
 
 pytestmark = pytest.mark.gpu
 

@@ -7,7 +7,7 @@ import pytest
 
 from engine_conformance import run_conformance
 from oracle.oracle import Oracle
-from oracle_backend import OracleBackend
+from oracle.backend import OracleBackend
 from stratacuda_b200.model import PLE_CONSTANTS, create_fixture, ngram_rows, validate_geometry
 
 
