@@ -500,7 +500,16 @@ def run_model_arm(args):
         engine.step(2)
         engine.reset()
     t0 = time.perf_counter()
-    r = engine.prefill(prompt, chunk_size=64)
+    if args.profile_prefill and args.prompt > 64:  # only the last chunk is inside the capture
+        import torch
+        engine.prefill(prompt[:-64], chunk_size=64)
+        b.idle()
+        torch.cuda.cudart().cudaProfilerStart()
+        r = engine.prefill(prompt[-64:], chunk_size=64)
+        b.idle()
+        torch.cuda.cudart().cudaProfilerStop()
+    else:
+        r = engine.prefill(prompt, chunk_size=64)
     t_prefill = time.perf_counter() - t0
     token, tokens = r["token"], []
     t0 = time.perf_counter()
@@ -548,6 +557,8 @@ def main():
     ap.add_argument("--model-layers", type=int, default=48)
     ap.add_argument("--prompt", type=int, default=1920, help="--model: prompt tokens (context 2048 = prompt + decode)")
     ap.add_argument("--decode", type=int, default=128, help="--model: greedy decode tokens")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="--model: bracket the last 64-token prompt chunk with cudaProfilerStart/Stop")
     ap.add_argument("--profile-step", action="store_true",
                     help="--model: bracket the last decode step with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()

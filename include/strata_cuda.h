@@ -84,12 +84,24 @@ int strata_zero(strata_ctx *ctx, strata_buf buf);
 int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *type, void **device_ptr);
 
 /* ---- dispatch (run, src/backend.js:101-113; validateDispatch :10-56) ----
- * Runs one reference entry of kernels/strata.cu by name with the reference's grid of 64-lane
- * workgroups. Supported names: strata_unpack_half, strata_expert_scales, strata_ple_decode, strata_q2_gate_up,
- * strata_q2_down, strata_project, strata_bf16_project, strata_q2_project, strata_quant_project,
- * strata_elementwise, strata_router, strata_router_batch, strata_moe_combine,
- * strata_moe_combine_batch, strata_gather_rows, strata_scatter_rows. Results are bit-identical
- * to the reference's F32 CPU path. */
+ * Runs one reference entry of kernels/strata.cu by name, with the reference's parameter names and
+ * its grid of 64-lane workgroups: all 49 entries that src/engine.js, src/ops.js and src/prefill.js
+ * dispatch (mixture of experts, projections, norms, embeddings, RoPE, hyper-connections, the gated
+ * delta rule, convolution, attention, per-layer embeddings, argmax; their prompt-batch forms).
+ * Results are bit-identical to the reference's F32 CPU path; the RoPE table's cosf / sinf and the
+ * softplus's logf, which the reference leaves to its C library, agree with it within one ulp.
+ * Validation mirrors src/backend.js:10-56. It also rejects zero divisors and loop extents larger
+ * than their buffers, which the reference leaves unchecked.
+ *
+ * Four further names have no counterpart in the reference. They read a token list or a position
+ * from device memory instead of a kernel argument, so that one captured CUDA graph can replay
+ * every decode step or full prompt chunk:
+ *   strata_embed_token  (Table, Token, Residual, width, streams, vocab, tokens)
+ *   strata_rope_at      (X, Cos, Sin, Y, Position, dim, heads, rotary, tokens)
+ *   strata_kv_append_at (K, V, Keys, Values, Position, width, tokens)
+ *   strata_attention_at (Q, Keys, Values, Position, Y, dim, heads, kvHeads, scale; query tokens = groups[2])
+ * Each computes what strata_embedding, strata_rope_position, strata_kv_append_batch and
+ * strata_attention_batch compute for the same values. */
 int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int nargs, const uint32_t groups[3]);
 
 /* ---- synchronisation and introspection (idle, flush, info: src/backend.js:119-120) ---- */

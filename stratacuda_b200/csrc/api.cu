@@ -310,8 +310,8 @@ int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params
         ok = int_in(I("width")) && int_in(I("streams")) &&
              fits((n == "strata_hc_mix" ? 1 : I("tokens")) * I("streams") * I("width"), "Norm");
     } else if (n == "strata_embed_token") {
-        ok = int_in(I("width")) && int_in(I("streams")) && int_in(I("vocab")) && fits(I("width") * I("streams"), "Residual") &&
-             fits(I("vocab") * I("width"), "Table") && fits(1, "Token");
+        ok = int_in(I("width")) && int_in(I("streams")) && int_in(I("vocab")) && int_in(I("tokens")) &&
+             fits(I("tokens") * I("width") * I("streams"), "Residual") && fits(I("vocab") * I("width"), "Table") && fits(I("tokens"), "Token");
     } else if (n == "strata_rope_at") {
         for (const char *p : {"rotary", "dim", "heads", "tokens"})
             if (!int_in(I(p))) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p);

@@ -114,6 +114,85 @@ __global__ void __launch_bounds__(kStagedThreads) k_project_staged(FB X, FB W, F
     }
 }
 
+// The same projection for prompt chunks, register-tiled: each warp computes 4 rows x 8 tokens.
+// Lane l keeps, for every (row, token), the reference's two strided sums (elements l + 64k and
+// l + 32 + 64k, k ascending), so each weight value read feeds 8 sums and each input value 4. The
+// sums of two neighbouring tokens share one 64-bit register and advance with the paired F32
+// product (an FMA whose addend is a run-time -0: the rounded product) and the paired rounded add,
+// each element rounded exactly as the scalar __fmul_rn / __fadd_rn would. Each output then takes
+// the reference's tree over the 64 lanes. A block (8 warps: 2 row groups x 4 token groups) stages
+// 256-column chunks of its 8 weight rows and 32 input rows in shared memory with 16-byte
+// asynchronous copies, two chunks in flight. Used when cols is a multiple of 256, the rows are
+// 16-byte aligned, and the host has checked that W and X cover every row and token named.
+constexpr int kTileRows = 4, kTileTokens = 8, kTileWarps = 8, kTileK = 256;
+constexpr int kBlockRows = 2 * kTileRows, kBlockTokens = 4 * kTileTokens;
+constexpr size_t kTileSmem = 2 * (size_t)(kBlockRows + kBlockTokens) * kTileK * 4;  // 80 KB
+__global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, FB Y, int cols, int rows, int tokens, int outputStride,
+                                                                   int outputOffset, unsigned long long neg0, unsigned *err) {
+    extern __shared__ __align__(16) float tile_smem[];  // [2 stages][8 weight rows + 32 input rows][256]
+    const int warp = threadIdx.x / 32, t = threadIdx.x & 31;
+    const int rb = blockIdx.x * kBlockRows, tb = blockIdx.y * kBlockTokens;
+    const int wr = (warp / 4) * kTileRows, wt = (warp % 4) * kTileTokens;  // this warp's rows / tokens within the block
+    const int chunks = cols / kTileK;
+    auto stage = [&](int c, int st) {  // chunk c of every block row into stage st (rows past the end repeat the last)
+        float *base = tile_smem + (size_t)st * (kBlockRows + kBlockTokens) * kTileK;
+        for (int k = threadIdx.x; k < (kBlockRows + kBlockTokens) * (kTileK / 4); k += kTileWarps * 32) {
+            const int line = k / (kTileK / 4), q = k % (kTileK / 4);
+            const float *src = line < kBlockRows ? W.p + (long long)min(rb + line, rows - 1) * cols
+                                                 : X.p + (long long)min(tb + line - kBlockRows, tokens - 1) * cols;
+            copy16_async(base + (size_t)line * kTileK + q * 4, src + (long long)c * kTileK + q * 4);
+        }
+        copy_commit();
+    };
+    unsigned long long acc[kTileRows][kTileTokens / 2][2];
+#pragma unroll
+    for (int r = 0; r < kTileRows; ++r)
+#pragma unroll
+        for (int j = 0; j < kTileTokens / 2; ++j) acc[r][j][0] = acc[r][j][1] = 0ull;
+    stage(0, 0);
+    for (int c = 0; c < chunks; ++c) {
+        if (c + 1 < chunks) {
+            stage(c + 1, (c + 1) & 1);
+            copy_wait<1>();
+        } else {
+            copy_wait<0>();
+        }
+        __syncthreads();
+        const float *ws = tile_smem + (size_t)(c & 1) * (kBlockRows + kBlockTokens) * kTileK + (size_t)wr * kTileK;
+        const float *xs = tile_smem + (size_t)(c & 1) * (kBlockRows + kBlockTokens) * kTileK + (size_t)(kBlockRows + wt) * kTileK;
+#pragma unroll
+        for (int kk = 0; kk < kTileK / STRATA_LANES; ++kk)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int e = t + STRATA_LANES * kk + 32 * h;
+                unsigned long long xv[kTileTokens / 2];
+#pragma unroll
+                for (int j = 0; j < kTileTokens / 2; ++j)
+                    xv[j] = (unsigned long long)__float_as_uint(xs[(2 * j) * kTileK + e]) |
+                            ((unsigned long long)__float_as_uint(xs[(2 * j + 1) * kTileK + e]) << 32);
+#pragma unroll
+                for (int r = 0; r < kTileRows; ++r) {
+                    const unsigned long long ww = (unsigned long long)__float_as_uint(ws[r * kTileK + e]) * 0x100000001ull;
+#pragma unroll
+                    for (int j = 0; j < kTileTokens / 2; ++j) acc[r][j][h] = add2_rn(acc[r][j][h], mul_rn2(ww, xv[j], neg0));
+                }
+            }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int r = 0; r < kTileRows; ++r)
+#pragma unroll
+        for (int j = 0; j < kTileTokens / 2; ++j)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const float lo = __uint_as_float((unsigned)(acc[r][j][0] >> (32 * q)));
+                const float hi = __uint_as_float((unsigned)(acc[r][j][1] >> (32 * q)));
+                const float sum = tree64(lo, hi);
+                const int row = rb + wr + r, token = tb + wt + 2 * j + q;
+                if (t == 0 && row < rows && token < tokens) Y.set((long long)token * outputStride + outputOffset + row, sum, err);
+            }
+}
+
 // kernels/strata.cu:168-176
 __global__ void k_bf16_project(Grid g, FB X, UB Codes, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset,
                                unsigned *err) {
@@ -326,6 +405,16 @@ cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
         if (e != cudaSuccess) return e;
         k_project_staged<<<dim3((unsigned)rows, (unsigned)tokens), kStagedThreads, bytes, s>>>(F(0), F(1), F(2), a[3].i, a[6].i, a[7].i,
                                                                                                 err);
+        return cudaGetLastError();
+    }
+    const bool aligned = ((reinterpret_cast<uintptr_t>(a[0].ptr) | reinterpret_cast<uintptr_t>(a[1].ptr)) & 15) == 0;
+    if (tokens >= kTileTokens && rows >= kTileRows && cols % kTileK == 0 && aligned && a[1].len >= rows * cols &&
+        a[0].len >= tokens * cols && g[2] >= 1) {
+        cudaError_t e = cudaFuncSetAttribute(k_project_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTileSmem);
+        if (e != cudaSuccess) return e;
+        const dim3 blocks((unsigned)((rows + kBlockRows - 1) / kBlockRows), (unsigned)((tokens + kBlockTokens - 1) / kBlockTokens));
+        k_project_tiled<<<blocks, kTileWarps * 32, kTileSmem, s>>>(F(0), F(1), F(2), a[3].i, (int)rows, (int)tokens, a[6].i, a[7].i,
+                                                                   kNegZero2, err);
         return cudaGetLastError();
     }
     k_project<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);

@@ -81,6 +81,17 @@ __device__ __forceinline__ void stage_row(float *dst, const float *src, int n) {
     }
 }
 
+// 16-byte asynchronous global -> shared copies (cp.async, L2 only) and their group waits.
+__device__ __forceinline__ void copy16_async(void *dst, const void *src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void copy_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void copy_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // kernels/strata.cu:22-31, the IQ4_NL codebook
 __device__ __forceinline__ float iq4(int c) {
     const float t[16] = {-127.f, -104.f, -83.f, -65.f, -49.f, -35.f, -22.f, -10.f, 1.f, 13.f, 25.f, 38.f, 53.f, 69.f, 89.f, 113.f};

@@ -554,6 +554,50 @@ __global__ void k_conv(Grid g, FB History, FB X, FB W, FB Y, int channels, int t
     }
 }
 
+// The same convolution with the channel's history in registers across the tokens, for the tap
+// counts and dilations known at compile time (the model's 4 taps at dilations 1 and 3); loaded
+// and stored once per dispatch. Launched only when the host's layout checks cover every index.
+template <int TAPS, int DIL>
+__global__ void k_conv_reg(Grid g, FB History, FB X, FB W, FB Y, int channels, int activation, int tokens) {
+    constexpr int H = (TAPS - 1) * DIL;
+    const long long c = lane_index(g, channels);
+    if (c < 0) return;
+    float hist[H], w[TAPS];
+#pragma unroll
+    for (int k = 0; k < H; ++k) hist[k] = History.p[c * H + k];
+#pragma unroll
+    for (int k = 0; k < TAPS; ++k) w[k] = W.p[c * TAPS + k];
+    for (int token = 0; token < tokens; ++token) {
+        const long long at = (long long)token * channels + c;
+        const float x = X.p[at];
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < TAPS - 1; ++k) sum = __fadd_rn(sum, __fmul_rn(hist[k * DIL], w[k]));
+        sum = __fadd_rn(sum, __fmul_rn(x, w[TAPS - 1]));
+        Y.p[at] = activation == 1 ? ref_silu(sum) : sum;
+#pragma unroll
+        for (int k = 0; k + 1 < H; ++k) hist[k] = hist[k + 1];
+        hist[H - 1] = x;
+    }
+#pragma unroll
+    for (int k = 0; k < H; ++k) History.p[c * H + k] = hist[k];
+}
+
+cudaError_t launch_conv(const KArg *a, const unsigned g[3], int tokens, int batch, cudaStream_t s, unsigned *err) {
+    const int channels = a[4].i, taps = a[5].i, dil = a[6].i, act = a[7].i;
+    const long long c = channels;
+    const bool covered = c >= 1 && a[0].len >= c * (taps - 1) * dil && a[2].len >= c * taps && a[1].len >= tokens * c &&
+                         a[3].len >= tokens * c;
+    if (covered && taps == 4 && dil == 1) {
+        k_conv_reg<4, 1><<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
+    } else if (covered && taps == 4 && dil == 3) {
+        k_conv_reg<4, 3><<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
+    } else {
+        k_conv<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), channels, taps, dil, act, tokens, batch, err);
+    }
+    return cudaGetLastError();
+}
+
 // kernels/strata.cu:296-301 and :425-431: decay = exp(A softplus(alpha + dt)), strength = sigmoid(beta).
 __global__ void k_gdn_gates(Grid g, FB Alpha, FB Beta, FB A, FB Dt, FB Decay, FB Strength, int heads, int tokens, unsigned *err) {
     long long i = lane_index(g, (long long)heads * tokens);
@@ -662,22 +706,25 @@ cudaError_t launch_gdn(const Grid g, const KArg *a, int tokens, cudaStream_t s, 
 }
 
 // ---------------------------------------------------------------- device-position entries
-// No counterpart in the reference: the decode step's four token- or position-dependent
-// dispatches with that value read from a device scalar instead of a kernel argument, so one
-// captured CUDA graph replays every decode step. Each computes exactly what its reference entry
+// No counterpart in the reference: the four token- or position-dependent dispatches of a decode
+// step or prompt chunk with those values read from device memory instead of kernel arguments,
+// so one captured CUDA graph replays every decode step (or every full prompt chunk).
+// strata_attention_at takes its query tokens as the dispatch's z extent, like strata_attention_batch. Each computes exactly what its reference entry
 // computes for the same value.
 
-// strata_embed_token: copy of row Token[0] of the table, then strata_embedding format 0.
-__global__ void k_embed_token(Grid g, FB Table, IB Token, FB Residual, int width, int streams, int vocab, unsigned *err) {
-    long long i = lane_index(g, width);
+// strata_embed_token: for each of `tokens` ids in Token, that row of the table into every stream
+// of the token's residual (token k at k * width * streams): strata_embedding format 0 per token.
+__global__ void k_embed_token(Grid g, FB Table, IB Token, FB Residual, int width, int streams, int vocab, int tokens, unsigned *err) {
+    long long i = lane_index(g, (long long)width * tokens);
     if (i < 0) return;
-    const int t = Token.get(0, err);
+    const long long k = i / width, d = i % width;
+    const int t = Token.get(k, err);
     if (t < 0 || t >= vocab) {
         raise_error(err, kErrIndex);
         return;
     }
-    const float v = Table.get((long long)t * width + i, err);
-    for (int stream = 0; stream < streams; ++stream) Residual.set((long long)stream * width + i, v, err);
+    const float v = Table.get((long long)t * width + d, err);
+    for (int stream = 0; stream < streams; ++stream) Residual.set((k * streams + stream) * width + d, v, err);
 }
 
 // ---------------------------------------------------------------- launchers
@@ -717,7 +764,7 @@ cudaError_t L_rope_batch(const KArg *a, const unsigned g[3], cudaStream_t s, uns
     return cudaGetLastError();
 }
 cudaError_t L_embed_token(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_embed_token<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    k_embed_token<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -729,8 +776,8 @@ cudaError_t L_kv_append_at(const KArg *a, const unsigned g[3], cudaStream_t s, u
     return cudaGetLastError();
 }
 cudaError_t L_attention_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention<<<dim3(g[0], 1), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(4), a[5].i, a[6].i, a[7].i, 0, 0, a[8].f,
-                                                       1, I(3), err);
+    k_attention<<<dim3(g[0], g[2]), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(4), a[5].i, a[6].i, a[7].i, 0, 0,
+                                                          a[8].f, 1, I(3), err);
     return cudaGetLastError();
 }
 cudaError_t L_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -822,12 +869,10 @@ cudaError_t L_ple_add(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
     return cudaGetLastError();
 }
 cudaError_t L_conv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_conv<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, SCALAR_TOKENS, 0, err);
-    return cudaGetLastError();
+    return launch_conv(a, g, SCALAR_TOKENS, 0, s, err);
 }
 cudaError_t L_conv_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_conv<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, 1, err);
-    return cudaGetLastError();
+    return launch_conv(a, g, a[8].i, 1, s, err);
 }
 cudaError_t L_gdn_gates(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     k_gdn_gates<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, SCALAR_TOKENS, err);
@@ -886,7 +931,7 @@ const KernelSpec kEngineKernels[] = {
     {"strata_gdn_step", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I", L_gdn_step},
     {"strata_gdn_batch", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I tokens:I", L_gdn_batch},
     // device-position entries (no reference counterpart)
-    {"strata_embed_token", "Table:f Token:i Residual:f width:I streams:I vocab:I", L_embed_token},
+    {"strata_embed_token", "Table:f Token:i Residual:f width:I streams:I vocab:I tokens:I", L_embed_token},
     {"strata_rope_at", "X:f Cos:f Sin:f Y:f Position:i dim:I heads:I rotary:I tokens:I", L_rope_at},
     {"strata_kv_append_at", "K:f V:f Keys:f Values:f Position:i width:I tokens:I", L_kv_append_at},
     {"strata_attention_at", "Q:f Keys:f Values:f Position:i Y:f dim:I heads:I kvHeads:I scale:F", L_attention_at},

@@ -154,7 +154,7 @@ class Ops:
         g = self.g
         if device_token is not None:
             self.b.run("strata_embed_token", dict(Table=self.weight("token_embd.weight"), Token=device_token, Residual=output,
-                                                  width=g["width"], streams=g["streams"], vocab=g["vocab"]), grid(g["width"]))
+                                                  width=g["width"], streams=g["streams"], vocab=g["vocab"], tokens=1), grid(g["width"]))
             return
         row = self.alloc(g["width"])
         self.b.copy(self.weight("token_embd.weight"), row, g["width"], token * g["width"], 0)
@@ -226,6 +226,7 @@ class StrataEngine:
         self.use_graph = bool(graph)
         self._graph = None
         self._dev = None
+        self._chunks = {}  # prompt chunk size -> its device inputs and captured graph
         self.store = store
         self.g = validate_geometry(store.config)
         self.b = backend
@@ -551,13 +552,46 @@ class StrataEngine:
         finally:
             self._dev_mode = False
 
+    def _device_scalars(self):
+        if self._dev is None:
+            b, g = self.b, self.g
+            self._dev = dict(token=b.alloc(1, "i32"), position=b.alloc(1, "i32"), ple=b.alloc(g["pleHeads"], "i32"))
+        return self._dev
+
+    def _graph_chunk(self, chunk) -> None:
+        """A full prompt chunk replayed from the graph captured for its size: the chunk's token ids,
+        PLE row ids and starting position are written to device memory, the first chunk of a size
+        runs eagerly and is then captured, later ones replay it."""
+        b, g, n = self.b, self.g, len(chunk)
+        dev = self._chunks.get(n)
+        if dev is None:
+            dev = dict(tokens=b.alloc(n, "i32"), ple=b.alloc(n * g["pleHeads"], "i32"), residual=b.alloc(n * g["width"] * g["streams"]),
+                       graph=None)
+            self._chunks[n] = dev
+        ids, previous = [], list(self.previous)
+        for t in chunk:
+            ids.append(self.store.ple_indices(t, previous))
+            previous = (previous + [t])[-2:]
+        b.write(dev["tokens"], np.array(chunk, np.int32))
+        b.write(dev["ple"], np.concatenate(ids).astype(np.int32))
+        b.write(self._device_scalars()["position"], np.array([self.position], np.int32))
+        if dev["graph"] is None:
+            PromptBatch(self, chunk, dev).run()
+            b.capture_begin()
+            try:
+                PromptBatch(self, chunk, dev).run(bookkeeping=False)
+            finally:
+                dev["graph"] = b.capture_end()
+            return
+        b.graph_launch(dev["graph"])
+        PromptBatch(self, chunk, dev).bookkeep()
+
     def _graph_step(self, token: int, logits: bool) -> dict:
         """A decode step replayed from the captured graph. The first one runs eagerly (which also
         fills the buffer pools and sizes the fused layers' workspace), then the same body is
         captured; each later step writes three small inputs, replays, and reads the result."""
         b, g = self.b, self.g
-        if self._dev is None:
-            self._dev = dict(token=b.alloc(1, "i32"), position=b.alloc(1, "i32"), ple=b.alloc(g["pleHeads"], "i32"))
+        self._device_scalars()
         b.write(self._dev["token"], np.array([token], np.int32))
         b.write(self._dev["position"], np.array([self.position], np.int32))
         b.write(self._dev["ple"], self.store.ple_indices(token, self.previous).astype(np.int32))
@@ -588,8 +622,13 @@ class StrataEngine:
             raise ValueError("Logits require prediction")
         self.stats["routes"] = []
         try:
+            graphs = self.use_graph and getattr(self.store, "moe_layer", None) is not None
             for offset in range(0, len(tokens), chunk_size):
-                PromptBatch(self, tokens[offset:offset + chunk_size]).run()
+                chunk = tokens[offset:offset + chunk_size]
+                if graphs and len(chunk) == chunk_size:
+                    self._graph_chunk(chunk)
+                else:
+                    PromptBatch(self, chunk).run()
             result = dict(position=self.position - 1)
             if predict:
                 result.update(self._predict(logits))
@@ -632,6 +671,12 @@ class StrataEngine:
         if self._graph is not None:
             self.b.graph_free(self._graph)
             self._graph = None
+        for dev in self._chunks.values():
+            if dev["graph"] is not None:
+                self.b.graph_free(dev["graph"])
+            for key in ("tokens", "ple", "residual"):
+                self.b.free(dev[key])
+        self._chunks = {}
         for buf in (self._dev or {}).values():
             self.b.free(buf)
         self._dev = None
@@ -647,9 +692,12 @@ class PromptBatch:
     """src/prefill.js:5-97: one chunk of prompt tokens through every layer, layer by layer; each
     projection and each routed expert runs once over all of the chunk's tokens."""
 
-    def __init__(self, engine: StrataEngine, tokens):
+    def __init__(self, engine: StrataEngine, tokens, device=None):
         self.e, self.g, self.o, self.b = engine, engine.g, engine.ops, engine.b
         self.tokens, self.n, self.position = list(tokens), len(tokens), engine.position
+        # device inputs of a graph-replayed chunk: token ids, PLE row ids and a fixed residual
+        # buffer; the position is the engine's device scalar
+        self.device = device
 
     def mat(self, name, x):
         return self.o.mat(name, x, self.n)
@@ -673,7 +721,14 @@ class PromptBatch:
         g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
         p, hc = f"blk.{g['pleLayer']}.ple_", g["width"] * g["streams"]
         emb, previous = o.alloc(n * g["width"]), list(e.previous)
-        for i, t in enumerate(self.tokens):
+        if self.device is not None:  # every token's rows in one gather from the device row ids
+            table = getattr(e.store, "ple_table", None)
+            if table is not None:
+                b.ple_gather_decode(table, self.device["ple"], n * g["pleHeads"], g["pleHeadDim"], emb)
+            else:
+                b.run("strata_gather_rows", dict(X=o.weight("per_layer_token_embd.weight"), Indices=self.device["ple"], Y=emb,
+                                                 width=g["pleHeadDim"], rows=n * g["pleHeads"]), grid(n * g["width"]))
+        for i, t in enumerate(self.tokens if self.device is None else []):
             row = o.ple(t, previous)
             b.copy(row, emb, g["width"], 0, i * g["width"])
             o.release(row)
@@ -717,12 +772,23 @@ class PromptBatch:
     def qsa(self, layer: int, x):
         g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
         p, st, hd = f"blk.{layer}.", e.states[layer], g["headDim"]
+        dpos = e._dev["position"] if self.device is not None else None
         full = self.mat(p + "attn_q.weight", x)
         qr = o.slice(full, hd, n * g["heads"], hd * 2)
-        q = o.rotate(o.norm(qr, o.vector(p + "attn_q_norm.weight"), hd, n * g["heads"]), g["heads"], self.position, n)
+        q = o.rotate(o.norm(qr, o.vector(p + "attn_q_norm.weight"), hd, n * g["heads"]), g["heads"], self.position, n, dpos)
         kr = self.mat(p + "attn_k.weight", x)
-        k = o.rotate(o.norm(kr, o.vector(p + "attn_k_norm.weight"), hd, n * g["kvHeads"]), g["kvHeads"], self.position, n)
+        k = o.rotate(o.norm(kr, o.vector(p + "attn_k_norm.weight"), hd, n * g["kvHeads"]), g["kvHeads"], self.position, n, dpos)
         v = self.mat(p + "attn_v.weight", x)
+        if dpos is not None:  # the same dispatches with the position read on the device
+            attn = o.alloc(n * g["heads"] * hd)
+            gated = o.alloc(attn.length)
+            b.run("strata_kv_append_at", dict(K=k, V=v, Keys=st["keys"], Values=st["values"], Position=dpos, width=g["kvHeads"] * hd,
+                                              tokens=n), grid(n * g["kvHeads"] * hd))
+            b.run("strata_attention_at", dict(Q=q, Keys=st["keys"], Values=st["values"], Position=dpos, Y=attn, dim=hd, heads=g["heads"],
+                                              kvHeads=g["kvHeads"], scale=_f32(1 / math.sqrt(hd))), [g["heads"], (hd + 63) // 64, n])
+            b.run("strata_attention_gate_batch", dict(Attention=attn, FullQ=full, Y=gated, dim=hd, heads=g["heads"], tokens=n),
+                  grid(attn.length))
+            return self.mat(p + "attn_output.weight", gated)
         b.run("strata_kv_append_batch", dict(K=k, V=v, Keys=st["keys"], Values=st["values"], width=g["kvHeads"] * hd,
                                              position=self.position, tokens=n), grid(n * g["kvHeads"] * hd))
         attn = o.alloc(n * g["heads"] * hd)
@@ -767,19 +833,29 @@ class PromptBatch:
                                                count=g["topK"], tokens=n), grid(y.length))
         return y
 
-    def run(self) -> None:
+    def run(self, bookkeeping: bool = True) -> None:
         g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
         hc = g["width"] * g["streams"]
-        self.residual = b.alloc(n * hc)
+        self.residual = self.device["residual"] if self.device is not None else b.alloc(n * hc)
         try:
-            for t, token in enumerate(self.tokens):
-                o.embedding(token, self.residual, t * hc)
+            if self.device is not None:
+                b.run("strata_embed_token", dict(Table=o.weight("token_embd.weight"), Token=self.device["tokens"], Residual=self.residual,
+                                                 width=g["width"], streams=g["streams"], vocab=g["vocab"], tokens=n), grid(n * g["width"]))
+            else:
+                for t, token in enumerate(self.tokens):
+                    o.embedding(token, self.residual, t * hc)
             for layer in range(g["layers"]):
                 e._layer(layer, self)
             b.copy(self.residual, e.residual, hc, (n - 1) * hc, 0)
-            e.position += n
-            e.previous = (e.previous + self.tokens)[-2:]
-            e.stats["tokens"] += n
+            if bookkeeping:
+                self.bookkeep()
         finally:
-            b.idle()
-            b.free(self.residual)
+            if self.device is None:
+                b.idle()
+                b.free(self.residual)
+
+    def bookkeep(self) -> None:
+        e = self.e
+        e.position += self.n
+        e.previous = (e.previous + self.tokens)[-2:]
+        e.stats["tokens"] += self.n

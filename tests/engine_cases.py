@@ -94,8 +94,8 @@ def cases():
     x = _f(rng, 3 * 515)
     add("strata_norm", (3, 1, 1), dict(X=x, W=x, Y=np.zeros(3 * 515, np.float32), cols=515, rows=3, weightRows=1, mode=1, epsilon=1e-6,
                                        scale=float(np.float32(0.125))), ["Y"])
-    for cols, rows, tokens in [(2048, 7, 3), (8192, 4, 1), (600, 5, 2)]:
-        add("strata_project", (rows, tokens, 1), dict(X=_f(rng, cols * tokens), W=_f(rng, rows * cols), Y=np.zeros(rows * tokens + 3, np.float32),
+    for cols, rows, tokens in [(2048, 7, 3), (8192, 4, 1), (600, 5, 2), (2048, 37, 67), (256, 9, 13)]:
+        add("strata_project", (rows, tokens, 1), dict(X=_f(rng, cols * tokens), W=_f(rng, rows * cols), Y=np.zeros(tokens * (rows + 1) + 3, np.float32),
                                                       cols=cols, rows=rows, tokens=tokens, outputStride=rows + 1, outputOffset=1), ["Y"])
     key, query = _f(rng, 5 * 40), _f(rng, 5 * 40)
     key[40:80] = 0.0  # a zero dot product: sign 0, gate sigmoid(0)

@@ -4,8 +4,8 @@ workload's hidden size, every weight resident, run by the engine host.
 * The fused mixture-of-experts layer inside the engine (strata_moe_forward, exact mode) gives the
   same logits, bit for bit, as the reference's own per-expert order (router, host read of the ids,
   one packed-expert dispatch per routed expert: src/engine.js:133-156, src/prefill.js:52-78).
-* At 48 layers, a prompt prefilled in chunks gives the same logits, bit for bit, as the same
-  tokens stepped one at a time: the prompt entries compute each token's floats exactly as the
+* At 48 layers, a prompt prefilled in chunks (9, 9, 1 tokens) gives the same logits, bit for bit,
+  as the same tokens stepped one at a time (register-tiled, staged and per-warp projections alike): the prompt entries compute each token's floats exactly as the
   decode entries do, at any chunk size and starting position.
 * The fast (tensor-core) MoE mode stays within 2e-2 relative L2 of the exact logits over the
   whole model."""
@@ -66,10 +66,10 @@ def test_full_model_prefill_equals_stepwise_and_fast_mode_is_close(b):
     from stratacuda_b200.synthetic import MODEL_GEOMETRY, DeviceStore
     store = DeviceStore(b, MODEL_GEOMETRY, seed=1)
     try:
-        prompt = np.random.default_rng(5).integers(0, MODEL_GEOMETRY["vocab"], 12).tolist()
+        prompt = np.random.default_rng(5).integers(0, MODEL_GEOMETRY["vocab"], 20).tolist()
         chunked = StrataEngine.create(store, b, 0)
         chunked.step(prompt[0], predict=False)  # a nonzero starting position
-        a = chunked.prefill(prompt[1:], chunk_size=5, logits=True)
+        a = chunked.prefill(prompt[1:], chunk_size=9, logits=True)  # 9 + 9 + 1: tiled, tiled, decode-sized
         stepwise = StrataEngine.create(store, b, 0)
         for t in prompt[:-1]:
             stepwise.step(t, predict=False)
@@ -91,16 +91,18 @@ def test_full_model_prefill_equals_stepwise_and_fast_mode_is_close(b):
 
 
 def test_graph_decode_equals_eager(b):
-    """Decode steps replayed from one captured CUDA graph (token, position and PLE rows read from
-    device scalars) give the eager steps' logits bit for bit, across positions, two attention
-    layers, the PLE layer, and a reset."""
+    """Prompt chunks and decode steps replayed from captured CUDA graphs (token ids, position and PLE
+    rows read from device memory) give the eager engine's logits bit for bit, across positions,
+    two attention layers, the PLE layer, and a reset."""
     from stratacuda_b200.engine import StrataEngine
     from stratacuda_b200.synthetic import MODEL_GEOMETRY, DeviceStore
     store = DeviceStore(b, dict(MODEL_GEOMETRY, layers=8, vocab=4096, eos=4095), seed=4)
     try:
         eager, graph = StrataEngine.create(store, b, 0), StrataEngine.create(store, b, 0, graph=True)
         for _ in range(2):
-            a, c = eager.prefill([3, 99, 7], chunk_size=3), graph.prefill([3, 99, 7], chunk_size=3)
+            prompt = [3, 99, 7, 12, 500, 8, 41]  # chunks of 3, 3 (a replay at a new position) and 1
+            a, c = eager.prefill(prompt, chunk_size=3, logits=True), graph.prefill(prompt, chunk_size=3, logits=True)
+            assert np.array_equal(_bits(a["logits"]), _bits(c["logits"]))
             ta, tc = a["token"], c["token"]
             for _ in range(5):
                 ra, rc = eager.step(ta, logits=True), graph.step(tc, logits=True)
