@@ -639,53 +639,51 @@ __global__ void k_gdn(Grid g, FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB 
     }
 }
 
-// The same rule with a block's state tile in shared memory across the tokens (DIM known at compile
-// time, one block of DIM threads per value head): the tile is loaded and stored once per
-// dispatch instead of twice per token, and the head's key and query rows of each token are
-// staged once for all of its columns. Thread x owns column x of the tile (row i at i * DIM + x:
-// conflict-free). Launched only when the host has checked that every index lies in its buffer.
+// The same rule with the thread's state column in registers (DIM known at compile time), one
+// block of DIM threads per value head: the head's key and query rows of each token are staged in
+// shared memory and read through a volatile view, so the compiler issues them in order beside
+// the accumulation chains instead of holding all 2 x DIM of them in registers.
 template <int DIM>
-__global__ void __launch_bounds__(DIM) k_gdn_tile(FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int keyHeads, int valueHeads,
+__global__ void __launch_bounds__(DIM) k_gdn_regs(FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int keyHeads, int valueHeads,
                                                   int tokens, long long columns) {
-    extern __shared__ float tile[];  // [DIM][DIM]
     __shared__ float ks[DIM], qs[DIM];
+    const volatile float *kv = ks, *qv = qs;
     const long long stride = (long long)valueHeads * DIM;
     const long long h = blockIdx.x, jh = h * DIM + threadIdx.x, kh = h % keyHeads;
     const int x = threadIdx.x;
     const bool active = jh < columns;
-    if (active)
-        for (int i = 0; i < DIM; ++i) tile[i * DIM + x] = State.p[i * stride + jh];
+    float st[DIM];
+#pragma unroll
+    for (int i = 0; i < DIM; ++i) st[i] = active ? State.p[i * stride + jh] : 0.0f;
     for (int token = 0; token < tokens; ++token) {
         const long long kbase = ((long long)token * keyHeads + kh) * DIM, gh = (long long)token * valueHeads + h;
         ks[x] = K.p[kbase + x];
         qs[x] = Q.p[kbase + x];
         __syncthreads();
-        if (active) {
-            const float decay = Decay.p[gh];
-            float prediction = 0.0f;
-#pragma unroll 8
-            for (int i = 0; i < DIM; ++i) {
-                const float v = __fmul_rn(tile[i * DIM + x], decay);
-                tile[i * DIM + x] = v;
-                prediction = __fadd_rn(prediction, __fmul_rn(v, ks[i]));
-            }
-            const float delta = __fmul_rn(__fsub_rn(V.p[token * stride + jh], prediction), Beta.p[gh]);
-            float result = 0.0f;
-#pragma unroll 8
-            for (int i = 0; i < DIM; ++i) {
-                const float v = __fadd_rn(tile[i * DIM + x], __fmul_rn(ks[i], delta));
-                tile[i * DIM + x] = v;
-                result = __fadd_rn(result, __fmul_rn(v, qs[i]));
-            }
-            Y.p[token * stride + jh] = result;
+        const float decay = Decay.p[gh];
+        float prediction = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DIM; ++i) {
+            st[i] = __fmul_rn(st[i], decay);
+            prediction = __fadd_rn(prediction, __fmul_rn(st[i], kv[i]));
         }
+        const float delta = __fmul_rn(__fsub_rn(active ? V.p[token * stride + jh] : 0.0f, prediction), Beta.p[gh]);
+        float result = 0.0f;
+#pragma unroll
+        for (int i = 0; i < DIM; ++i) {
+            st[i] = __fadd_rn(st[i], __fmul_rn(kv[i], delta));
+            result = __fadd_rn(result, __fmul_rn(st[i], qv[i]));
+        }
+        if (active) Y.p[token * stride + jh] = result;
         __syncthreads();
     }
-    if (active)
-        for (int i = 0; i < DIM; ++i) State.p[i * stride + jh] = tile[i * DIM + x];
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < DIM; ++i) State.p[i * stride + jh] = st[i];
+    }
 }
 
-// The shared-memory tile form when dim is 128 and the buffers cover every index, else the checked kernel.
+// The register form when dim is 128 and the buffers cover every index, else the checked kernel.
 cudaError_t launch_gdn(const Grid g, const KArg *a, int tokens, cudaStream_t s, unsigned *err) {
     const int dim = a[7].i, kh = a[8].i, vh = a[9].i;
     const long long stride = (long long)vh * dim, columns = std::min(stride, (long long)g.x * STRATA_LANES);
@@ -693,11 +691,8 @@ cudaError_t launch_gdn(const Grid g, const KArg *a, int tokens, cudaStream_t s, 
                          a[2].len >= (long long)tokens * kh * dim && a[3].len >= tokens * stride && a[4].len >= (long long)tokens * vh &&
                          a[5].len >= (long long)tokens * vh && a[6].len >= tokens * stride && kh >= 1 && vh >= 1;
     if (dim == 128 && covered) {
-        constexpr int kTile = 128 * 128 * 4;
-        cudaError_t e = cudaFuncSetAttribute(k_gdn_tile<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTile);
-        if (e != cudaSuccess) return e;
-        k_gdn_tile<128><<<(unsigned)((columns + 127) / 128), 128, kTile, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), F(6), kh, vh, tokens,
-                                                                             columns);
+        k_gdn_regs<128><<<(unsigned)((columns + 127) / 128), 128, 0, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), F(6), kh, vh, tokens,
+                                                                          columns);
     } else {
         k_gdn<<<(unsigned)(((unsigned long long)g.x * STRATA_LANES + 255) / 256), 256, 0, s>>>(g, F(0), F(1), F(2), F(3), F(4), F(5), F(6),
                                                                                              dim, kh, vh, tokens, err);
