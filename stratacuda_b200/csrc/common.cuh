@@ -111,6 +111,13 @@ __device__ __forceinline__ unsigned long long mul_rn2(unsigned long long a, unsi
     return d;
 }
 constexpr unsigned long long kNegZero2 = 0x8000000080000000ull;  // the host passes this as neg0
+// Two floats as one 64-bit register pair (low = lo), and back: register moves, no arithmetic.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    unsigned long long d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float &lo, float &hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
 __device__ __forceinline__ unsigned xor3(unsigned a, unsigned b, unsigned c) {
     unsigned d;
     asm("lop3.b32 %0, %1, %2, %3, 0x96;" : "=r"(d) : "r"(a), "r"(b), "r"(c));

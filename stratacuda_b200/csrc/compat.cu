@@ -167,12 +167,11 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, F
                 const int e = t + STRATA_LANES * kk + 32 * h;
                 unsigned long long xv[kTileTokens / 2];
 #pragma unroll
-                for (int j = 0; j < kTileTokens / 2; ++j)
-                    xv[j] = (unsigned long long)__float_as_uint(xs[(2 * j) * kTileK + e]) |
-                            ((unsigned long long)__float_as_uint(xs[(2 * j + 1) * kTileK + e]) << 32);
+                for (int j = 0; j < kTileTokens / 2; ++j) xv[j] = pack2(xs[(2 * j) * kTileK + e], xs[(2 * j + 1) * kTileK + e]);
 #pragma unroll
                 for (int r = 0; r < kTileRows; ++r) {
-                    const unsigned long long ww = (unsigned long long)__float_as_uint(ws[r * kTileK + e]) * 0x100000001ull;
+                    const float wr = ws[r * kTileK + e];
+                    const unsigned long long ww = pack2(wr, wr);
 #pragma unroll
                     for (int j = 0; j < kTileTokens / 2; ++j) acc[r][j][h] = add2_rn(acc[r][j][h], mul_rn2(ww, xv[j], neg0));
                 }
@@ -185,9 +184,10 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, F
         for (int j = 0; j < kTileTokens / 2; ++j)
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-                const float lo = __uint_as_float((unsigned)(acc[r][j][0] >> (32 * q)));
-                const float hi = __uint_as_float((unsigned)(acc[r][j][1] >> (32 * q)));
-                const float sum = tree64(lo, hi);
+                float l0, l1, h0, h1;
+                unpack2(acc[r][j][0], l0, l1);
+                unpack2(acc[r][j][1], h0, h1);
+                const float sum = tree64(q ? l1 : l0, q ? h1 : h0);
                 const int row = rb + wr + r, token = tb + wt + 2 * j + q;
                 if (t == 0 && row < rows && token < tokens) Y.set((long long)token * outputStride + outputOffset + row, sum, err);
             }
