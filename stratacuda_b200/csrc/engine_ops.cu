@@ -469,6 +469,129 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Key
     }
 }
 
+// The prompt form for a group of query heads that share one KV head (GQA): one block per (KV
+// head, query token). Each key row is loaded once for the group's G scores (G independent
+// in-order sums), one warp per head takes the maximum and the exponential sum in the reference's
+// lane order, and each value is loaded once for four heads' in-order sums. Every value is formed
+// by the same operations in the same order as in k_attention. Cells are 0 .. position + token; a
+// key or value row outside its buffer reads as zeros and is reported.
+constexpr int kGroupThreads = 512, kMaxGroup = 8;
+__global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q, FB Keys, FB Values, FB Y, int dim, int heads, int kvHeads,
+                                                                   int position, float scale, IB Pos, unsigned *err) {
+    extern __shared__ __align__(16) float group_smem[];  // [G][dim] queries, then [G][kMaxCells] scores
+    __shared__ float totals[kMaxGroup];
+    const int G = heads / kvHeads, kh = blockIdx.x, token = blockIdx.y, tid = threadIdx.x;
+    if (Pos.n > 0) position = Pos.get(0, err);
+    const long long n = (long long)position + token + 1;
+    if (n < 1 || n > kMaxCells) {
+        if (tid == 0) raise_error(err, kErrIndex);
+        return;
+    }
+    float *qs = group_smem, *scores = group_smem + (size_t)G * dim;
+    const long long qbase = ((long long)token * heads + (long long)kh * G) * dim;  // the group's G query rows are consecutive
+    for (int k = tid; k < G * dim; k += kGroupThreads) qs[k] = Q.get(qbase + k, err);
+    __syncthreads();
+    for (int c = tid; c < n; c += kGroupThreads) {  // A
+        const long long kb = ((long long)c * kvHeads + kh) * dim;
+        float sc[kMaxGroup];
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) sc[h] = 0.0f;
+        if (covers(Keys, kb, dim)) {
+            const float4 *k4 = reinterpret_cast<const float4 *>(Keys.p + kb);
+#pragma unroll 4
+            for (int j4 = 0; j4 < dim / 4; ++j4) {
+                const float4 kv = k4[j4];
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h) {
+                    if (h >= G) break;
+                    const float *q = qs + h * dim + 4 * j4;
+                    sc[h] = __fadd_rn(sc[h], __fmul_rn(q[0], kv.x));
+                    sc[h] = __fadd_rn(sc[h], __fmul_rn(q[1], kv.y));
+                    sc[h] = __fadd_rn(sc[h], __fmul_rn(q[2], kv.z));
+                    sc[h] = __fadd_rn(sc[h], __fmul_rn(q[3], kv.w));
+                }
+            }
+        } else {
+            raise_error(err, kErrIndex);
+        }
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h)
+            if (h < G) scores[(size_t)h * kMaxCells + c] = __fmul_rn(sc[h], scale);
+    }
+    __syncthreads();
+    const int warp = tid / 32, t = tid & 31;
+    if (warp < G) {  // B: head `warp`
+        float *sh = scores + (size_t)warp * kMaxCells;
+        float mlo = -3.402823e38f, mhi = -3.402823e38f;
+        for (int c = t; c < n; c += STRATA_LANES) mlo = fmaxf(mlo, sh[c]);
+        for (int c = t + 32; c < n; c += STRATA_LANES) mhi = fmaxf(mhi, sh[c]);
+        const float m = __shfl_sync(0xffffffffu, max_tree64(mlo, mhi), 0);
+        float slo = 0.0f, shi = 0.0f;
+        for (int c = t; c < n; c += STRATA_LANES) {
+            const float p = ref_expf(__fsub_rn(sh[c], m));
+            sh[c] = p;
+            slo = __fadd_rn(slo, p);
+        }
+        for (int c = t + 32; c < n; c += STRATA_LANES) {
+            const float p = ref_expf(__fsub_rn(sh[c], m));
+            sh[c] = p;
+            shi = __fadd_rn(shi, p);
+        }
+        const float total = tree64(slo, shi);
+        if (t == 0) totals[warp] = total;
+    }
+    __syncthreads();
+    const int dmax = (int)min((long long)dim, (long long)g.y * STRATA_LANES);
+    constexpr int kHeadsPerThread = 4;
+    const int quads = (G + kHeadsPerThread - 1) / kHeadsPerThread;
+    for (int w = tid; w < dmax * quads; w += kGroupThreads) {  // C: dimension d of heads h0 .. h0 + 3
+        const int d = w % dmax, h0 = (w / dmax) * kHeadsPerThread;
+        float value[kHeadsPerThread] = {0.0f, 0.0f, 0.0f, 0.0f};
+        int c = 0;
+        for (; c + 8 <= n; c += 8) {  // eight value loads in flight ahead of the ordered sums
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const long long vb = ((long long)(c + u) * kvHeads + kh) * dim;
+                v[u] = covers(Values, vb, dim) ? Values.p[vb + d] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int q = 0; q < kHeadsPerThread; ++q)
+                    if (h0 + q < G) value[q] = __fadd_rn(value[q], __fmul_rn(scores[(size_t)(h0 + q) * kMaxCells + c + u], v[u]));
+        }
+        for (; c < n; ++c) {
+            const long long vb = ((long long)c * kvHeads + kh) * dim;
+            const float v = covers(Values, vb, dim) ? Values.p[vb + d] : 0.0f;
+#pragma unroll
+            for (int q = 0; q < kHeadsPerThread; ++q)
+                if (h0 + q < G) value[q] = __fadd_rn(value[q], __fmul_rn(scores[(size_t)(h0 + q) * kMaxCells + c], v));
+        }
+#pragma unroll
+        for (int u = 0; u < kHeadsPerThread; ++u)
+            if (h0 + u < G) Y.set(((long long)token * heads + (long long)kh * G + h0 + u) * dim + d, __fdiv_rn(value[u], totals[h0 + u]), err);
+    }
+}
+
+cudaError_t launch_attention_prompt(const KArg *a, int qi, int ki, int vi, int yi, int dim, int heads, int kvHeads, int position, float scale,
+                                    IB pos, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const int G = kvHeads > 0 ? heads / kvHeads : 0;
+    const size_t bytes = ((size_t)G * dim + (size_t)G * kMaxCells) * 4;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(a[ki].ptr)) & 15) == 0;
+    if (g[2] >= 8 && G >= 1 && G <= kMaxGroup && heads % kvHeads == 0 && dim % 4 == 0 && aligned && bytes <= 200 * 1024 &&
+        g[0] >= (unsigned)heads) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention_group, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return e;
+        k_attention_group<<<dim3(kvHeads, g[2]), kGroupThreads, bytes, s>>>(grid_of(g), F(qi), F(ki), F(vi), F(yi), dim, heads, kvHeads,
+                                                                           position, scale, pos, err);
+        return cudaGetLastError();
+    }
+    k_attention<<<dim3(g[0], g[2]), kAttnThreads, 0, s>>>(grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim, heads, kvHeads, 0,
+                                                          position, scale, 1, pos, err);
+    return cudaGetLastError();
+}
+
 // kernels/strata.cu:328-330 and :453-456
 __global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, int position, int tokens, IB Pos, unsigned *err) {
     long long i = lane_index(g, (long long)width * tokens);
@@ -771,9 +894,7 @@ cudaError_t L_kv_append_at(const KArg *a, const unsigned g[3], cudaStream_t s, u
     return cudaGetLastError();
 }
 cudaError_t L_attention_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention<<<dim3(g[0], g[2]), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(4), a[5].i, a[6].i, a[7].i, 0, 0,
-                                                          a[8].f, 1, I(3), err);
-    return cudaGetLastError();
+    return launch_attention_prompt(a, 0, 1, 2, 4, a[5].i, a[6].i, a[7].i, 0, a[8].f, I(3), g, s, err);
 }
 cudaError_t L_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     k_gemv<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
@@ -811,9 +932,7 @@ cudaError_t L_attention(const KArg *a, const unsigned g[3], cudaStream_t s, unsi
     return cudaGetLastError();
 }
 cudaError_t L_attention_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention<<<dim3(g[0], g[2]), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i,
-                                                          a[8].f, 1, IB{nullptr, 0}, err);
-    return cudaGetLastError();
+    return launch_attention_prompt(a, 0, 1, 2, 3, a[4].i, a[5].i, a[6].i, a[7].i, a[8].f, IB{nullptr, 0}, g, s, err);
 }
 cudaError_t L_kv_append(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, SCALAR_TOKENS, IB{nullptr, 0}, err);

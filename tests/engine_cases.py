@@ -123,6 +123,11 @@ def cases():
             dict(Q=_f(rng, tokens * heads * dim, 0.3), Keys=_f(rng, (position + tokens) * kv * dim),
                  Values=_f(rng, (position + tokens) * kv * dim), Y=np.zeros(tokens * heads * dim, np.float32), dim=dim, heads=heads,
                  kvHeads=kv, position=position, scale=float(np.float32(1 / np.sqrt(dim)))), ["Y"])
+    for dim, position, tokens, heads, kv in [(256, 100, 9, 4, 2), (64, 50, 8, 16, 2)]:  # 8+ query tokens: one block per KV group
+        add("strata_attention_batch", (heads, (dim + 63) // 64, tokens),
+            dict(Q=_f(rng, tokens * heads * dim, 0.3), Keys=_f(rng, (position + tokens) * kv * dim),
+                 Values=_f(rng, (position + tokens) * kv * dim), Y=np.zeros(tokens * heads * dim, np.float32), dim=dim, heads=heads,
+                 kvHeads=kv, position=position, scale=float(np.float32(1 / np.sqrt(dim)))), ["Y"])
     add("strata_kv_append", _grid(16), dict(K=_f(rng, 16), V=_f(rng, 16), Keys=_f(rng, 8 * 16), Values=_f(rng, 8 * 16), width=16,
                                             position=3), ["Keys", "Values"])
     add("strata_kv_append_batch", _grid(32), dict(K=_f(rng, 32), V=_f(rng, 32), Keys=_f(rng, 8 * 16), Values=_f(rng, 8 * 16), width=16,
