@@ -462,6 +462,8 @@ class StrataEngine:
                                          count=g["topK"]), grid(g["width"]))
         return y
 
+    _progress = None
+
     def _layer(self, layer: int, batch=None) -> None:
         """One layer: PLE (on its layer), token mixer through the attention hyper-connection, then
         the mixture of experts through the feed-forward one (src/engine.js:176-182)."""
@@ -477,6 +479,8 @@ class StrataEngine:
         mixed, inject = host.hc(f"blk.{layer}.hc_ffn_")
         host.hc_write(host.moe(layer, mixed), inject)
         self.ops.clear_temporary()
+        if self._progress is not None:  # src/engine.js:183 onProgress(layer + 1, layers); it may raise to abort
+            self._progress(layer + 1, self.g["layers"])
 
     def _head(self):
         """Output hyper-connection, vocabulary projection and greedy argmax, without a read."""
@@ -506,8 +510,11 @@ class StrataEngine:
         if self.failed:
             raise RuntimeError("Session failed; reset it before continuing")
 
-    def step(self, token: int, logits: bool = False, predict: bool = True) -> dict:
-        """src/engine.js:172-196: one decode step; returns {position, token[, logits]}."""
+    def step(self, token: int, logits: bool = False, predict: bool = True, on_progress=None) -> dict:
+        """src/engine.js:172-196: one decode step; returns {position, token[, logits]}.
+        `on_progress(layer, layers)` runs after each layer (src/engine.js:183); an exception it
+        raises aborts the step, leaves the session failed (reset() recovers it) and its position
+        unchanged. A step with a callback runs eagerly, never from a captured graph."""
         self._check_ready()
         if logits and not predict:
             raise ValueError("Logits require prediction")
@@ -515,8 +522,9 @@ class StrataEngine:
         if self.position >= self.g["context"]:
             raise ValueError("Context capacity reached; reset or create a larger session")
         self.stats["routes"] = []
+        self._progress = on_progress
         try:
-            if self.use_graph and predict and getattr(self.store, "moe_layer", None) is not None:
+            if self.use_graph and predict and on_progress is None and getattr(self.store, "moe_layer", None) is not None:
                 result = self._graph_step(token, logits)
             else:
                 self.ops.embedding(token, self.residual)
@@ -527,9 +535,11 @@ class StrataEngine:
                 if predict:
                     result.update(self._predict(logits))
                 self.ops.clear_temporary()
-        except Exception:
+        except BaseException:
             self.failed = True
             raise
+        finally:
+            self._progress = None
         self.previous = (self.previous + [token])[-2:]
         self.position += 1
         self.stats["tokens"] += 1
@@ -607,8 +617,11 @@ class StrataEngine:
         b.graph_launch(self._graph)
         return dict(position=self.position, **self._predict(logits, self._graph_head))
 
-    def prefill(self, tokens, chunk_size: int = 16, logits: bool = False, predict: bool = True) -> dict:
-        """src/engine.js:161-168 and src/prefill.js:99-111: layer-major prompt chunks."""
+    def prefill(self, tokens, chunk_size: int = 16, logits: bool = False, predict: bool = True, on_progress=None) -> dict:
+        """src/engine.js:161-168 and src/prefill.js:99-111: layer-major prompt chunks.
+        `on_progress(layer, layers, offset, chunk_tokens)` runs after each layer of each chunk
+        (src/prefill.js:102); an exception it raises aborts the prompt and leaves the session
+        failed. Chunks with a callback run eagerly."""
         self._check_ready()
         tokens = [int(t) for t in tokens]
         if not tokens:
@@ -622,9 +635,11 @@ class StrataEngine:
             raise ValueError("Logits require prediction")
         self.stats["routes"] = []
         try:
-            graphs = self.use_graph and getattr(self.store, "moe_layer", None) is not None
+            graphs = self.use_graph and on_progress is None and getattr(self.store, "moe_layer", None) is not None
             for offset in range(0, len(tokens), chunk_size):
                 chunk = tokens[offset:offset + chunk_size]
+                if on_progress is not None:
+                    self._progress = lambda layer, layers, o=offset, n=len(chunk): on_progress(layer, layers, o, n)
                 if graphs and len(chunk) == chunk_size:
                     self._graph_chunk(chunk)
                 else:
@@ -633,9 +648,11 @@ class StrataEngine:
             if predict:
                 result.update(self._predict(logits))
             self.ops.clear_temporary()
-        except Exception:
+        except BaseException:
             self.failed = True
             raise
+        finally:
+            self._progress = None
         return result
 
     # ---- session state (src/engine.js:197-222)
