@@ -101,7 +101,15 @@ int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *t
  *   strata_kv_append_at (K, V, Keys, Values, Position, width, tokens)
  *   strata_attention_at (Q, Keys, Values, Position, Y, dim, heads, kvHeads, scale; query tokens = groups[2])
  * Each computes what strata_embedding, strata_rope_position, strata_kv_append_batch and
- * strata_attention_batch compute for the same values. */
+ * strata_attention_batch compute for the same values.
+ *
+ * Two more have no counterpart either. They run the decode step's hyper-connection block
+ * (src/engine.js:78-84) in two launches instead of six, with each value formed by the same
+ * operations in the same order:
+ *   strata_hc_in  (Residual, NormW, DownW, InjectW, Norm, Down, Inject, width, streams, rank, epsilon):
+ *                 strata_norm of the streams rows, then the down and inject projections of the norm
+ *   strata_hc_out (Norm, Down, UpW, Mixed, width, streams, rank, scale):
+ *                 strata_elementwise mode 1, the up projection and strata_hc_mix */
 int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int nargs, const uint32_t groups[3]);
 
 /* ---- synchronisation and introspection (idle, flush, info: src/backend.js:119-120) ---- */

@@ -326,6 +326,16 @@ int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params
         if (I("heads") % I("kvHeads")) return fail(ctx, STRATA_ERR_RANGE, "Attention heads must be divisible by KV heads");
         ok = fits(I("heads") * I("dim"), "Q") && fits(1, "Position");
     }
+    if (n == "strata_hc_in" || n == "strata_hc_out") {  // every index the kernels read or write lies inside its buffer
+        const long long w = I("width"), st = I("streams"), r = I("rank"), hc = w * st;
+        if (!int_in(w) || !int_in(st, 1, 64) || !int_in(r))
+            return fail(ctx, STRATA_ERR_RANGE, "%s: width, rank >= 1 and streams in [1, 64] required", name);
+        if (n == "strata_hc_in")
+            ok = hc * 8 <= 200 * 1024 && fits(hc, "Residual") && fits(hc, "NormW") && fits(r * hc, "DownW") && fits(st * hc, "InjectW") &&
+                 fits(hc, "Norm") && fits(r, "Down") && fits(st, "Inject");
+        else
+            ok = r * 4 <= 48 * 1024 && fits(hc, "Norm") && fits(r, "Down") && fits(hc * r, "UpW") && fits(w, "Mixed");
+    }
     if (!ok) return fail(ctx, STRATA_ERR_LAYOUT, "%s: a loop extent exceeds its buffer layout", name);
     return STRATA_OK;
 }

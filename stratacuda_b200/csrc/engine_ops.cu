@@ -823,6 +823,66 @@ cudaError_t launch_gdn(const Grid g, const KArg *a, int tokens, cudaStream_t s, 
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- hyper-connection blocks
+// No counterpart in the reference: the decode step's hyper-connection sequence (src/engine.js:
+// 78-84: norm -> down projection -> SiLU(x / streams) -> up projection -> mix, and the inject
+// projection of the same norm) in two launches instead of six, each value formed by the same
+// operations in the same order as the reference entries (k_norm, k_project, k_elementwise,
+// k_hc_mix). Neither needs a grid-wide wait: each block recomputes the small shared inputs.
+constexpr int kHcThreads = 128;
+
+// strata_hc_in: Norm = RMSNorm of the `streams` residual rows (gamma row = stream), then
+// Down = down . Norm (rank rows of width*streams) and Inject = inject . Norm (streams rows). One
+// block per output row stages the residual and its weight row in shared memory together, forms the
+// norm there (one warp per stream row, as k_norm does) and one warp takes the row's ordered dot.
+// Block 0 also writes the norm.
+constexpr int kHcInThreads = 256;
+__global__ void __launch_bounds__(kHcInThreads) k_hc_in(FB Residual, FB NormW, FB DownW, FB InjectW, FB Norm, FB Down, FB Inject, int width,
+                                                        int streams, int rank, float epsilon) {
+    extern __shared__ __align__(16) float hc_in[];  // [hc] residual -> norm, then [hc] the weight row
+    __shared__ float inv_s[64];
+    const int warp = threadIdx.x / 32, t = threadIdx.x & 31, hc = width * streams, j = blockIdx.x;
+    float *x = hc_in, *w = hc_in + hc;
+    stage_row(x, Residual.p, hc);
+    stage_row(w, j < rank ? DownW.p + (long long)j * hc : InjectW.p + (long long)(j - rank) * hc, hc);
+    __syncthreads();
+    for (int c = warp; c < streams; c += kHcInThreads / 32) {
+        const float ss = lane_dot(x + (size_t)c * width, x + (size_t)c * width, width, t);
+        if (t == 0) inv_s[c] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)width), epsilon)));
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < hc; k += kHcInThreads) x[k] = __fmul_rn(__fmul_rn(x[k], inv_s[k / width]), NormW.p[k]);
+    __syncthreads();
+    if (j == 0)
+        for (int k = threadIdx.x; k < hc; k += kHcInThreads) Norm.p[k] = x[k];
+    if (warp == 0) {
+        const float r = lane_dot(w, x, hc, t);
+        if (t == 0) {
+            if (j < rank) Down.p[j] = r;
+            else Inject.p[j - rank] = r;
+        }
+    }
+}
+
+// strata_hc_out: Mixed[d] = sum_c Norm[c, d] * sigmoid(up[c, d] . lo) / streams with
+// lo = SiLU(Down / streams) (elementwise mode 1, scale = 1/streams). Every block forms lo in shared
+// memory; one warp per output column d computes its `streams` gate rows and the mix.
+__global__ void __launch_bounds__(kHcThreads) k_hc_out(FB Norm, FB Down, FB UpW, FB Mixed, int width, int streams, int rank, float scale) {
+    extern __shared__ __align__(16) float hc_lo[];  // [rank]
+    const int warp = threadIdx.x / 32, t = threadIdx.x & 31;
+    for (int k = threadIdx.x; k < rank; k += kHcThreads) hc_lo[k] = ref_silu(__fmul_rn(Down.p[k], scale));
+    __syncthreads();
+    const int d = blockIdx.x * (kHcThreads / 32) + warp;
+    if (d >= width) return;
+    float v = 0.0f;
+    for (int c = 0; c < streams; ++c) {
+        const long long row = (long long)c * width + d;
+        const float gate = __shfl_sync(0xffffffffu, lane_dot(UpW.p + row * rank, hc_lo, rank, t), 0);
+        v = __fadd_rn(v, __fmul_rn(Norm.p[row], ref_sigmoid(gate)));
+    }
+    if (t == 0) Mixed.p[d] = __fdiv_rn(v, (float)streams);
+}
+
 // ---------------------------------------------------------------- device-position entries
 // No counterpart in the reference: the four token- or position-dependent dispatches of a decode
 // step or prompt chunk with those values read from device memory instead of kernel arguments,
@@ -895,6 +955,20 @@ cudaError_t L_kv_append_at(const KArg *a, const unsigned g[3], cudaStream_t s, u
 }
 cudaError_t L_attention_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     return launch_attention_prompt(a, 0, 1, 2, 4, a[5].i, a[6].i, a[7].i, 0, a[8].f, I(3), g, s, err);
+}
+cudaError_t L_hc_in(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const int width = a[7].i, streams = a[8].i, rank = a[9].i;
+    const size_t bytes = (size_t)width * streams * 8;
+    cudaError_t e = cudaFuncSetAttribute(k_hc_in, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return e;
+    k_hc_in<<<(unsigned)(rank + streams), kHcInThreads, bytes, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), F(6), width, streams, rank, a[10].f);
+    return cudaGetLastError();
+}
+cudaError_t L_hc_out(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const int width = a[4].i, streams = a[5].i, rank = a[6].i;
+    k_hc_out<<<(unsigned)((width + kHcThreads / 32 - 1) / (kHcThreads / 32)), kHcThreads, (size_t)rank * 4, s>>>(
+        F(0), F(1), F(2), F(3), width, streams, rank, a[7].f);
+    return cudaGetLastError();
 }
 cudaError_t L_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     k_gemv<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
@@ -1049,6 +1123,9 @@ const KernelSpec kEngineKernels[] = {
     {"strata_rope_at", "X:f Cos:f Sin:f Y:f Position:i dim:I heads:I rotary:I tokens:I", L_rope_at},
     {"strata_kv_append_at", "K:f V:f Keys:f Values:f Position:i width:I tokens:I", L_kv_append_at},
     {"strata_attention_at", "Q:f Keys:f Values:f Position:i Y:f dim:I heads:I kvHeads:I scale:F", L_attention_at},
+    // hyper-connection blocks (no reference counterpart)
+    {"strata_hc_in", "Residual:f NormW:f DownW:f InjectW:f Norm:f Down:f Inject:f width:I streams:I rank:I epsilon:F", L_hc_in},
+    {"strata_hc_out", "Norm:f Down:f UpW:f Mixed:f width:I streams:I rank:I scale:F", L_hc_out},
 };
 const int kNumEngineKernels = sizeof(kEngineKernels) / sizeof(kEngineKernels[0]);
 

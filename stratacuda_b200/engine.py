@@ -337,6 +337,16 @@ class StrataEngine:
     # ---- one token (src/engine.js:73-156)
     def hc(self, prefix: str, inject: bool = True):
         g, o = self.g, self.ops
+        if inject and getattr(self.b, "kind", None) == "cuda" and g["streams"] <= 64:
+            # the same six dispatches' values in two launches (strata_hc_in / strata_hc_out)
+            hc = g["width"] * g["streams"]
+            norm, down, inj, mixed = o.alloc(hc), o.alloc(g["rank"]), o.alloc(g["streams"]), o.alloc(g["width"])
+            self.b.run("strata_hc_in", dict(Residual=self.residual, NormW=o.vector(prefix + "norm.weight"), DownW=o.weight(prefix + "down.weight"),
+                                            InjectW=o.weight(prefix + "inject.weight"), Norm=norm, Down=down, Inject=inj, width=g["width"],
+                                            streams=g["streams"], rank=g["rank"], epsilon=1e-6), [1, 1, 1])
+            self.b.run("strata_hc_out", dict(Norm=norm, Down=down, UpW=o.weight(prefix + "up.weight"), Mixed=mixed, width=g["width"],
+                                             streams=g["streams"], rank=g["rank"], scale=_f32(1 / g["streams"])), [1, 1, 1])
+            return mixed, inj
         norm = o.norm(self.residual, o.vector(prefix + "norm.weight"), g["width"], g["streams"], g["streams"])
         down = o.mat(prefix + "down.weight", norm)
         lo = o.elem(down, down, 1, 1 / g["streams"])
