@@ -907,14 +907,14 @@ __global__ void k_embed_token(Grid g, FB Table, IB Token, FB Residual, int width
 
 // ---------------------------------------------------------------- launchers
 
-#define SCALAR_TOKENS 1
+constexpr int kOneToken = 1;  // the decode entries: one token
 cudaError_t L_embedding(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     k_embedding<<<LANESL>>>(grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, a[12].i,
                             a[13].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_embed(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_embed<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, SCALAR_TOKENS, err);
+    k_embed<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_embed_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -934,7 +934,7 @@ cudaError_t L_rope_position(const KArg *a, const unsigned g[3], cudaStream_t s, 
     return cudaGetLastError();
 }
 cudaError_t L_rope(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, SCALAR_TOKENS, 1, IB{nullptr, 0}, err);
+    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, kOneToken, 1, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1009,7 +1009,7 @@ cudaError_t L_attention_batch(const KArg *a, const unsigned g[3], cudaStream_t s
     return launch_attention_prompt(a, 0, 1, 2, 3, a[4].i, a[5].i, a[6].i, a[7].i, a[8].f, IB{nullptr, 0}, g, s, err);
 }
 cudaError_t L_kv_append(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, SCALAR_TOKENS, IB{nullptr, 0}, err);
+    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, kOneToken, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_kv_append_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1017,7 +1017,7 @@ cudaError_t L_kv_append_batch(const KArg *a, const unsigned g[3], cudaStream_t s
     return cudaGetLastError();
 }
 cudaError_t L_attention_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention_gate<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    k_attention_gate<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_gate_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1029,7 +1029,7 @@ cudaError_t L_slice(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned
     return cudaGetLastError();
 }
 cudaError_t L_hc_mix(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_hc_mix<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    k_hc_mix<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_hc_mix_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1037,7 +1037,7 @@ cudaError_t L_hc_mix_batch(const KArg *a, const unsigned g[3], cudaStream_t s, u
     return cudaGetLastError();
 }
 cudaError_t L_hc_write(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_hc_write<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    k_hc_write<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_hc_write_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1045,7 +1045,7 @@ cudaError_t L_hc_write_batch(const KArg *a, const unsigned g[3], cudaStream_t s,
     return cudaGetLastError();
 }
 cudaError_t L_ple_broadcast(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_ple_broadcast<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, SCALAR_TOKENS, err);
+    k_ple_broadcast<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_ple_broadcast_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1057,13 +1057,13 @@ cudaError_t L_ple_add(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
     return cudaGetLastError();
 }
 cudaError_t L_conv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    return launch_conv(a, g, SCALAR_TOKENS, 0, s, err);
+    return launch_conv(a, g, kOneToken, 0, s, err);
 }
 cudaError_t L_conv_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     return launch_conv(a, g, a[8].i, 1, s, err);
 }
 cudaError_t L_gdn_gates(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_gdn_gates<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, SCALAR_TOKENS, err);
+    k_gdn_gates<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_gdn_gates_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1071,7 +1071,7 @@ cudaError_t L_gdn_gates_batch(const KArg *a, const unsigned g[3], cudaStream_t s
     return cudaGetLastError();
 }
 cudaError_t L_gdn_step(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    return launch_gdn(grid_of(g), a, SCALAR_TOKENS, s, err);
+    return launch_gdn(grid_of(g), a, kOneToken, s, err);
 }
 cudaError_t L_gdn_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     return launch_gdn(grid_of(g), a, a[10].i, s, err);
