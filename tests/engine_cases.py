@@ -184,6 +184,26 @@ def cases():
             add("strata_gdn_step", _grid(vn), args, ["State", "Y"])
         else:
             add("strata_gdn_batch", _grid(vn), dict(args, tokens=tokens), ["State", "Y"])
+    # edge values the reference's code paths branch on
+    q, keys = _f(rng, 2 * 8, 0.2), _f(rng, 6 * 1 * 8)
+    keys[8:16] = np.nan  # a NaN score: fmaxf passes it over, its exponential poisons only its own term
+    keys[16:24] = -np.inf
+    add("strata_attention", (2, 1, 1), dict(Q=q, Keys=keys, Values=_f(rng, 6 * 8), Cells=np.arange(6, dtype=np.int32),
+                                            Y=np.zeros(16, np.float32), dim=8, heads=2, kvHeads=1, count=6, scale=0.25), ["Y"])
+    add("strata_conv", _grid(12), dict(History=np.zeros(1, np.float32), X=_f(rng, 12), W=_f(rng, 12), Y=np.zeros(12, np.float32),
+                                       channels=12, taps=1, dilation=1, activation=1), ["Y"])  # one tap: no history
+    vn = 16 * 3
+    add("strata_gdn_step", _grid(vn), dict(State=_f(rng, 16 * vn, 0.3), Q=_f(rng, 3 * 16, 0.3), K=_f(rng, 3 * 16, 0.3), V=_f(rng, vn),
+                                          Decay=np.full(3, 0.9, np.float32), Beta=np.full(3, 0.5, np.float32), Y=np.zeros(vn, np.float32),
+                                          dim=16, keyHeads=3, valueHeads=3), ["State", "Y"])  # as many key heads as value heads
+    x = np.zeros(2 * 64, np.float32)
+    x[64:] = _f(rng, 64)
+    add("strata_norm", (2, 1, 1), dict(X=x, W=x, Y=np.full(128, -1.0, np.float32), cols=64, rows=2, weightRows=1, mode=1, epsilon=1e-6,
+                                       scale=1.0), ["Y"])  # an all-zero row under the L2 norm
+    add("strata_rope_table", _grid(4), dict(High=hi[:4], Low=lo[:4], Cos=np.full(4, -1.0, np.float32), Sin=np.full(4, -1.0, np.float32), rotary=8,
+                                            context=1), ["Cos", "Sin"], ulps=1)  # position 0 only
+    add("strata_argmax", (1, 1, 1), dict(Logits=np.full(70, np.nan, np.float32), Token=np.full(1, -1, np.int32), count=70),
+        ["Token"])  # nothing qualifies: the count itself
     return out
 
 
