@@ -168,6 +168,12 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
  *  - The first call on each device looks the array's address up, so make it before any
  *    stream capture.
  *  - Calls share the array: calls that overlap on the GPU race, so order them on one stream.
+ *  - The calling thread's current device must own `stream`, the pointers and the layer, in
+ *    the runtime's primary context (the array's address is cached per device ordinal); a
+ *    stream of another device is rejected with STRATA_ERR_RANGE.
+ *  - A token whose routing fails (NaN probabilities) gets id -1; that pair adds nothing to y.
+ *    strata_moe_forward reports it as an error at the next synchronising call; this entry
+ *    cannot without synchronising, so check `ids` for -1.
  *  - Never allocates or frees. `msg` (optional) receives the reason for a non-zero status. */
 #define STRATA_NOALLOC_SCRATCH_BYTES (8u << 20)
 typedef struct {
@@ -190,12 +196,29 @@ int strata_moe_forward_noalloc(const strata_moe_layer_dev *layer, const float *x
  * relative L2, the tensor-core path's tolerance).
  * Setup: rank 0 calls strata_ep_unique_id, the 128 bytes are shared by the caller (e.g. a
  * torch.distributed broadcast), every rank calls strata_ep_init. NCCL (libnccl.so.2) is bound
- * at run time. Each forward reads the per-peer row counts back to the host once. */
+ * at run time. Each forward reads the per-peer row counts back to the host once.
+ * Failure detection (no reference counterpart; the reference's nearest is its failed-session
+ * state, src/engine.js:147-151, and worker-crash rejection, src/backend.js:165-168): the
+ * communicator is non-blocking, and every host wait on the peers (the forward's count read,
+ * strata_sync/strata_read and friends, strata_destroy) is bounded by strata_ep_set_timeout
+ * (default 60 s). A wait that runs out, or an NCCL asynchronous error, aborts the communicator
+ * (ncclCommAbort) and returns STRATA_ERR_CUDA naming the cause; later expert-parallel calls
+ * fail until strata_ep_init is called again. The context itself stays usable. */
 #define STRATA_EP_ID_BYTES 128
 int strata_ep_unique_id(strata_ctx *ctx, uint8_t *id, size_t cap);
 int strata_ep_init(strata_ctx *ctx, int32_t rank, int32_t n_ranks, const uint8_t *id);
+int strata_ep_set_timeout(strata_ctx *ctx, int32_t milliseconds);
 int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                           strata_buf weights);
+/* Same-device loopback transport (no reference counterpart): n virtual ranks on ONE GPU, one
+ * context each, driven by n host threads; the exchanges become device-to-device copies
+ * between the ranks' buffers, ordered by stream events (no kernel waits on another rank).
+ * Tests the expert-parallel layer at 2, 4 or 8 ranks on a single GPU. The hub's creator calls
+ * strata_ep_loopback_create once, every rank's context strata_ep_init_loopback(rank, hub);
+ * strata_ep_loopback_release drops the creator's reference (the ranks keep theirs). */
+int strata_ep_loopback_create(strata_ctx *ctx, int32_t n_ranks, uint64_t *hub);
+int strata_ep_init_loopback(strata_ctx *ctx, int32_t rank, uint64_t hub);
+int strata_ep_loopback_release(strata_ctx *ctx, uint64_t hub);
 
 /* ---- per-layer embeddings (PLE) on the device ----
  * Replaces the host-side row gather of src/model.js:230-242 (plePackedRows) followed by the

@@ -60,6 +60,10 @@ SIGNATURES = {
     "strata_graph_free": ([_vp, _u64], _i),
     "strata_ep_unique_id": ([_vp, C.c_char_p, _sz], _i),
     "strata_ep_init": ([_vp, C.c_int32, C.c_int32, C.c_char_p], _i),
+    "strata_ep_set_timeout": ([_vp, C.c_int32], _i),
+    "strata_ep_loopback_create": ([_vp, C.c_int32, C.POINTER(_u64)], _i),
+    "strata_ep_init_loopback": ([_vp, C.c_int32, _u64], _i),
+    "strata_ep_loopback_release": ([_vp, _u64], _i),
     "strata_moe_ep_forward": ([_vp, C.POINTER(StrataMoeLayer), _u64, C.c_int32, _u64, _u64, _u64], _i),
     "strata_profile_read": ([_vp, C.POINTER(C.c_double), C.c_int32, C.POINTER(C.c_uint64)], _i),
     "strata_moe_forward": ([_vp, C.POINTER(StrataMoeLayer), _u64, C.c_int32, _u64, _u64, _u64, C.c_int32], _i),

@@ -45,7 +45,8 @@ struct strata_ctx {
     std::vector<Mark> marks;
     std::vector<cudaEvent_t> spare_events;
     uint64_t profiled_calls = 0;
-    EpComm *ep = nullptr;  // strata_ep_init
+    EpComm *ep = nullptr;  // strata_ep_init / strata_ep_init_loopback
+    long long ep_timeout_ms = 60000;  // strata_ep_set_timeout
     // strata_capture_*: the stream is being captured; instantiated graphs by handle
     bool capturing = false;
     struct Graph {
@@ -109,7 +110,12 @@ int sync(strata_ctx *ctx) {
     if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "synchronising calls are not allowed while the stream is captured");
     CUDA_OR_FAIL(ctx, cudaMemcpyAsync(ctx->err_host, ctx->err_dev, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx->stream),
                  "error word readback");
-    CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (ctx->ep) {  // the stream may hold exchanges with the peers: a bounded wait, never a hang
+        std::string msg;
+        if (ep_wait(ctx->ep, ctx->stream, &msg)) return fail(ctx, STRATA_ERR_CUDA, "expert-parallel peers: %s", msg.c_str());
+    } else {
+        CUDA_OR_FAIL(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    }
     return check_device_errors(ctx);
 }
 
@@ -377,6 +383,10 @@ int strata_create(int device, strata_ctx **out) {
 int strata_destroy(strata_ctx *ctx) {
     if (!ctx) return STRATA_OK;
     cudaSetDevice(ctx->device);
+    if (ctx->ep && ctx->stream) {  // a peer that is gone must not hang the teardown: bounded wait, abort on failure
+        std::string msg;
+        ep_wait(ctx->ep, ctx->stream, &msg);
+    }
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     for (auto &kv : ctx->buffers) cudaFree(kv.second.ptr);
     ctx->buffers.clear();
@@ -684,8 +694,46 @@ int strata_ep_init(strata_ctx *ctx, int32_t rank, int32_t n_ranks, const uint8_t
         ctx->ep = nullptr;
     }
     std::string err;
-    ctx->ep = ep_create(rank, n_ranks, reinterpret_cast<const char *>(id), &err);
+    ctx->ep = ep_create(rank, n_ranks, reinterpret_cast<const char *>(id), ctx->ep_timeout_ms, &err);
     if (!ctx->ep) return fail(ctx, STRATA_ERR_CUDA, "%s", err.c_str());
+    return STRATA_OK;
+}
+
+int strata_ep_loopback_create(strata_ctx *ctx, int32_t n_ranks, uint64_t *hub) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!hub) return fail(ctx, STRATA_ERR_RANGE, "null hub");
+    std::string err;
+    unsigned long long h = 0;
+    if (ep_loopback_hub_create(n_ranks, &h, &err)) return fail(ctx, STRATA_ERR_RANGE, "%s", err.c_str());
+    *hub = h;
+    return STRATA_OK;
+}
+
+int strata_ep_loopback_release(strata_ctx *ctx, uint64_t hub) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    std::string err;
+    if (ep_loopback_hub_release(hub, &err)) return fail(ctx, STRATA_ERR_HANDLE, "%s", err.c_str());
+    return STRATA_OK;
+}
+
+int strata_ep_init_loopback(strata_ctx *ctx, int32_t rank, uint64_t hub) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (int r = use_device(ctx)) return r;
+    if (ctx->ep) {
+        ep_destroy(ctx->ep);
+        ctx->ep = nullptr;
+    }
+    std::string err;
+    ctx->ep = ep_create_loopback(hub, rank, ctx->ep_timeout_ms, &err);
+    if (!ctx->ep) return fail(ctx, STRATA_ERR_RANGE, "%s", err.c_str());
+    return STRATA_OK;
+}
+
+int strata_ep_set_timeout(strata_ctx *ctx, int32_t milliseconds) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (milliseconds < 1) return fail(ctx, STRATA_ERR_RANGE, "timeout must be >= 1 ms");
+    ctx->ep_timeout_ms = milliseconds;
+    if (ctx->ep) ctx->ep->t->timeout_ms = milliseconds;
     return STRATA_OK;
 }
 

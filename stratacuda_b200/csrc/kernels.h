@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "ep_comm.h"
+
 namespace strata {
 
 // Device-side error word bits (set with atomicOr, read by the host at the next sync).
@@ -108,14 +110,9 @@ size_t moe_prefill_scratch_bytes(int tokens, int width, int ff, int experts, int
 cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
                                 int grid, cudaStream_t s, unsigned *err, cudaEvent_t *marks = nullptr);
 
-// Expert parallel over NCCL (csrc/prefill.cu): communicator from a unique id shared by the
-// ranks; forward of one layer whose L.blobs holds this rank's L.experts / n experts. Returns 0
-// or a nonzero code with `msg`.
-struct EpComm;
-int ep_unique_id(char *out128, std::string *err);
-EpComm *ep_create(int rank, int n_ranks, const char *id128, std::string *err);
-void ep_destroy(EpComm *c);
-int ep_ranks(const EpComm *c);
+// Expert parallel (csrc/prefill.cu, communicator and transports in csrc/ep_comm.h): forward of
+// one layer whose L.blobs holds this rank's L.experts / n experts. Returns 0 or a nonzero
+// code with `msg`; a failed exchange marks the communicator failed and aborts it.
 int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int tokens, float *y, int *ids, float *weights, int grid, cudaStream_t s,
                    unsigned *err, std::string *msg,
                    cudaEvent_t *marks = nullptr);

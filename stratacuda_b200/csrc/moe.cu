@@ -238,14 +238,19 @@ __global__ void __launch_bounds__(kThreads) k_down(MoeLayerDev L, int tokens, co
     }
 }
 
-__global__ void k_combine(const float *parts, const float *weights, const float *shared_out, const float *sg, float *y, int width,
-                          int topK, int tokens) {
+// A pair whose id is outside [0, experts) (a token whose probabilities are all NaN routes to
+// -1, which k_permute reports as kErrRouting, src/engine.js:138) has no parts row: it adds
+// nothing, so y never depends on what the scratch held before the call.
+__global__ void k_combine(const float *parts, const float *weights, const int *ids, const float *shared_out, const float *sg, float *y,
+                          int width, int topK, int experts, int tokens) {
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)width * tokens) return;
     long long token = i / width, d = i % width;
     float value = __fmul_rn(shared_out[i], ref_sigmoid(sg[token]));
-    for (int k = 0; k < topK; ++k)
+    for (int k = 0; k < topK; ++k) {
+        if ((unsigned)ids[token * topK + k] >= (unsigned)experts) continue;
         value = __fadd_rn(value, __fmul_rn(parts[(token * topK + k) * width + d], weights[token * topK + k]));
+    }
     y[i] = value;
 }
 
@@ -309,7 +314,8 @@ cudaError_t moe_forward_exact(const MoeLayerDev &L, const float *x, int tokens, 
                                                                       ws.hidden, ws.parts, ws.shared_out);
     STRATA_CUDA_TRY(cudaGetLastError());
     const long long n = (long long)tokens * L.width;
-    k_combine<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ws.parts, weights, ws.shared_out, ws.sg, y, L.width, L.topK, tokens);
+    k_combine<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ws.parts, weights, ids, ws.shared_out, ws.sg, y, L.width, L.topK, L.experts,
+                                                      tokens);
     return cudaGetLastError();
 }
 

@@ -16,8 +16,12 @@
 //   * A call whose scratch need exceeds it is rejected with STRATA_ERR_RANGE and a message.
 //     At H 2048 / E 512 / k 10 / F 512 that means up to 73 tokens.
 //   * Every call shares the one array, and it keeps the previous call's contents. Each call
-//     rewrites every scratch byte it later reads (the counting sort, hidden rows, parts and
-//     shared outputs are all written before use), so nothing has to start at zero.
+//     writes every scratch byte it later reads (the counting sort, hidden rows and shared
+//     outputs), so nothing has to start at zero. The one exception is a token whose routing
+//     failed (its probabilities are NaN, so an id is -1): that pair has no parts row, and the
+//     combine skips it rather than read an older call's row. The reference rejects such a
+//     routing ("Invalid expert routing result", src/engine.js:138); this entry cannot report
+//     it without synchronising, so the -1 in `ids` is the caller's signal.
 //     Two calls that overlap on the GPU (different streams, or different host threads
 //     without ordering) race on the array and produce wrong results. Order them on one
 //     stream.
@@ -25,6 +29,9 @@
 //     passing it to a kernel would fault. The device address is therefore looked up once per
 //     device, with that device current, by cudaGetSymbolAddress on the first call made on
 //     that device. Make that first call before starting any stream capture.
+//   * The calling thread's current device must be the device of `stream`, of every pointer
+//     and of the layer, in the runtime's primary context of that device (the address cache is
+//     keyed by device ordinal). A stream of another device is rejected.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -76,6 +83,17 @@ extern "C" int strata_moe_forward_noalloc(const strata_moe_layer_dev *layer, con
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return say(msg, msg_cap, STRATA_ERR_CUDA, cudaGetErrorString(e));
     if (device < 0 || device >= kMaxDevices) return say(msg, msg_cap, STRATA_ERR_RANGE, "device ordinal out of range");
+    if (stream) {
+        int stream_device = -1;
+        e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_device);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return say(msg, msg_cap, STRATA_ERR_CUDA, cudaGetErrorString(e));
+        }
+        if (stream_device != device)
+            return say(msg, msg_cap, STRATA_ERR_RANGE,
+                       "strata_moe_forward_noalloc: the stream belongs to another device than the calling thread's current device");
+    }
     void *scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_lookup_mutex);

@@ -20,7 +20,6 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <dlfcn.h>
-#include <nccl.h>
 
 #include <cstring>
 #include <mutex>
@@ -28,6 +27,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "ep_comm.h"
 #include "kernels.h"
 #include "pf_gemm.cuh"
 #include "route.cuh"
@@ -778,108 +778,6 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
 
 
 // ------------------------------------------------------------------ expert parallel (host)
-// NCCL is bound at run time (the process's loaded libnccl.so.2 first, e.g. the one torch
-// brought, else the system's): the library itself needs no NCCL link dependency.
-namespace {
-struct NcclApi {
-    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
-    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
-    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
-    ncclResult_t (*GroupStart)() = nullptr;
-    ncclResult_t (*GroupEnd)() = nullptr;
-    ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-    ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-    const char *(*GetErrorString)(ncclResult_t) = nullptr;
-    bool ok = false;
-};
-const NcclApi &nccl() {
-    static NcclApi a;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
-        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-        if (!h) return;
-        a.GetUniqueId = reinterpret_cast<decltype(a.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
-        a.CommInitRank = reinterpret_cast<decltype(a.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
-        a.CommDestroy = reinterpret_cast<decltype(a.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
-        a.GroupStart = reinterpret_cast<decltype(a.GroupStart)>(dlsym(h, "ncclGroupStart"));
-        a.GroupEnd = reinterpret_cast<decltype(a.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
-        a.Send = reinterpret_cast<decltype(a.Send)>(dlsym(h, "ncclSend"));
-        a.Recv = reinterpret_cast<decltype(a.Recv)>(dlsym(h, "ncclRecv"));
-        a.GetErrorString = reinterpret_cast<decltype(a.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
-        a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.GroupStart && a.GroupEnd && a.Send && a.Recv && a.GetErrorString;
-    });
-    return a;
-}
-}  // namespace
-
-struct EpComm {
-    ncclComm_t comm = nullptr;
-    int rank = 0, n = 1;
-    struct Buf {
-        void *p = nullptr;
-        size_t cap = 0;
-    };
-    Buf bufs[25];
-    int *h_off = nullptr;  // pinned: [0, n] send offsets, [n + 1, 2n] receive counts
-    ~EpComm() {
-        for (Buf &b : bufs)
-            if (b.p) cudaFree(b.p);
-        if (h_off) cudaFreeHost(h_off);
-        if (comm) nccl().CommDestroy(comm);
-    }
-    // grow-only device buffer i of at least `bytes`
-    void *get(int i, size_t bytes, cudaError_t &e) {
-        if (bufs[i].cap < bytes) {
-            if (bufs[i].p) cudaFree(bufs[i].p);
-            bufs[i].p = nullptr;
-            bufs[i].cap = 0;
-            const size_t want = (bytes + bytes / 4 + 255) & ~size_t(255);
-            e = cudaMalloc(&bufs[i].p, want);
-            if (e != cudaSuccess) return nullptr;
-            bufs[i].cap = want;
-        }
-        return bufs[i].p;
-    }
-};
-
-int ep_unique_id(char *out, std::string *err) {
-    if (!nccl().ok) {
-        *err = "libnccl.so.2 could not be loaded";
-        return 1;
-    }
-    ncclUniqueId id;
-    const ncclResult_t r = nccl().GetUniqueId(&id);
-    if (r != ncclSuccess) {
-        *err = std::string("ncclGetUniqueId: ") + nccl().GetErrorString(r);
-        return 1;
-    }
-    std::memcpy(out, id.internal, NCCL_UNIQUE_ID_BYTES);
-    return 0;
-}
-
-EpComm *ep_create(int rank, int n, const char *id_bytes, std::string *err) {
-    if (!nccl().ok) {
-        *err = "libnccl.so.2 could not be loaded";
-        return nullptr;
-    }
-    ncclUniqueId id;
-    std::memcpy(id.internal, id_bytes, NCCL_UNIQUE_ID_BYTES);
-    auto *c = new EpComm;
-    c->rank = rank;
-    c->n = n;
-    const ncclResult_t r = nccl().CommInitRank(&c->comm, n, id, rank);
-    if (r != ncclSuccess || cudaMallocHost(&c->h_off, sizeof(int) * (2 * n + 2)) != cudaSuccess) {
-        *err = std::string("ncclCommInitRank: ") + nccl().GetErrorString(r);
-        delete c;
-        return nullptr;
-    }
-    return c;
-}
-
-void ep_destroy(EpComm *c) { delete c; }
-int ep_ranks(const EpComm *c) { return c->n; }
-
 // One layer over the ranks of `c`: this rank's T tokens in, its y out; L.blobs holds this
 // rank's experts [rank El, (rank + 1) El), El = L.experts / n (L.experts is the layer's total).
 // Stages: exact routing; one row per (token, destination rank) bucketed by rank (stable,
@@ -895,23 +793,29 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
                    unsigned *err, std::string *msg, cudaEvent_t *marks) {
     const int H = L.width, F = L.ff, E = L.experts, K = L.topK, n = c->n, El = E / n;
     cudaError_t e = cudaSuccess;
+    if (c->failed) {
+        *msg = "the expert-parallel communicator failed earlier (" + c->failure + "); call strata_ep_init again";
+        return 3;
+    }
     auto fail_cuda = [&](cudaError_t ce, const char *what) {
         *msg = std::string(what) + ": " + cudaGetErrorString(ce);
         return 2;
     };
-    auto fail_nccl = [&](ncclResult_t r, const char *what) {
-        *msg = std::string(what) + ": " + nccl().GetErrorString(r);
+    // a failed exchange leaves the peers in an unknown state: the communicator is aborted
+    auto fail_ep = [&](const char *what) {
+        *msg = std::string(what) + ": " + *msg;
+        c->fail(*msg);
         return 3;
     };
+    EpTransport &tr = *c->t;
 #define EP_CUDA(x, what)                              \
     do {                                              \
         cudaError_t _c = (x);                         \
         if (_c != cudaSuccess) return fail_cuda(_c, what); \
     } while (0)
-#define EP_NCCL(x, what)                              \
-    do {                                              \
-        ncclResult_t _r = (x);                        \
-        if (_r != ncclSuccess) return fail_nccl(_r, what); \
+#define EP_XCHG(what)                                  \
+    do {                                               \
+        if (tr.group_end(s, msg)) return fail_ep(what); \
     } while (0)
 #define EP_GET(ptr, type, i, count)                                                   \
     type *ptr = static_cast<type *>(c->get(i, sizeof(type) * (size_t)(count) + 16, e)); \
@@ -954,15 +858,15 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     EP_GET(d_cnt, int, 10, 2 * n);
     pf::k_ep_send_counts<<<(n + 127) / 128, 128, 0, s>>>(off, n, d_cnt);
     EP_CUDA(cudaGetLastError(), "routing and packing kernels");
-    EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
+    tr.group_start();
     for (int p = 0; p < n; ++p) {
-        EP_NCCL(nccl().Send(d_cnt + p, 1, ncclInt32, p, c->comm, s), "ncclSend");
-        EP_NCCL(nccl().Recv(d_cnt + n + p, 1, ncclInt32, p, c->comm, s), "ncclRecv");
+        tr.send(d_cnt + p, sizeof(int), p);
+        tr.recv(d_cnt + n + p, sizeof(int), p);
     }
-    EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
+    EP_XCHG("counts exchange");
     EP_CUDA(cudaMemcpyAsync(c->h_off, off, sizeof(int) * (n + 1), cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
     EP_CUDA(cudaMemcpyAsync(c->h_off + n + 1, d_cnt + n, sizeof(int) * n, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync");
-    EP_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    if (tr.wait(s, msg)) return fail_ep("waiting for the receive counts");
     std::vector<int> soff(n + 1), sc(n), rc(n), roff(n + 1);
     for (int i = 0; i <= n; ++i) soff[i] = c->h_off[i];
     for (int i = 0; i < n; ++i) sc[i] = soff[i + 1] - soff[i];
@@ -975,18 +879,18 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     // 4. rows exchange
     EP_GET(recv_rows, __half, 11, (long long)max(R, 1) * H);
     EP_GET(recv_meta, int, 12, (long long)max(R, 1) * MS);
-    EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
+    tr.group_start();
     for (int p = 0; p < n; ++p) {
         if (sc[p]) {
-            EP_NCCL(nccl().Send(send_rows + (long long)soff[p] * H, (size_t)sc[p] * H, ncclFloat16, p, c->comm, s), "ncclSend");
-            EP_NCCL(nccl().Send(send_meta + (long long)soff[p] * MS, (size_t)sc[p] * MS, ncclInt32, p, c->comm, s), "ncclSend");
+            tr.send(send_rows + (long long)soff[p] * H, sizeof(__half) * sc[p] * H, p);
+            tr.send(send_meta + (long long)soff[p] * MS, sizeof(int) * sc[p] * MS, p);
         }
         if (rc[p]) {
-            EP_NCCL(nccl().Recv(recv_rows + (long long)roff[p] * H, (size_t)rc[p] * H, ncclFloat16, p, c->comm, s), "ncclRecv");
-            EP_NCCL(nccl().Recv(recv_meta + (long long)roff[p] * MS, (size_t)rc[p] * MS, ncclInt32, p, c->comm, s), "ncclRecv");
+            tr.recv(recv_rows + (long long)roff[p] * H, sizeof(__half) * rc[p] * H, p);
+            tr.recv(recv_meta + (long long)roff[p] * MS, sizeof(int) * rc[p] * MS, p);
         }
     }
-    EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
+    EP_XCHG("dispatch");
     // 5. the received rows' pairs grouped by local expert (pair slot i K + j of row i), this
     //    rank's shared-expert rows after them; the GEMMs add every pair of received row i into
     //    Y[i] (pre-combine) and token t's shared expert into Y[R + t]
@@ -1025,19 +929,19 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
                              marks ? marks + 3 : nullptr),
             "expert GEMMs");
     // 6. one pre-combined row per received row back to its token's rank
-    EP_NCCL(nccl().GroupStart(), "ncclGroupStart");
+    tr.group_start();
     for (int p = 0; p < n; ++p) {
-        if (rc[p]) EP_NCCL(nccl().Send(Y + (long long)roff[p] * H, (size_t)rc[p] * H, ncclFloat32, p, c->comm, s), "ncclSend");
-        if (sc[p]) EP_NCCL(nccl().Recv(ret + (long long)soff[p] * H, (size_t)sc[p] * H, ncclFloat32, p, c->comm, s), "ncclRecv");
+        if (rc[p]) tr.send(Y + (long long)roff[p] * H, sizeof(float) * rc[p] * H, p);
+        if (sc[p]) tr.recv(ret + (long long)soff[p] * H, sizeof(float) * sc[p] * H, p);
     }
-    EP_NCCL(nccl().GroupEnd(), "ncclGroupEnd");
+    EP_XCHG("return");
     // 7. combine: shared row + the returned rows in rank order
     pf::k_ep_combine<<<T, 128, 0, s>>>(ret, pos, n, H, Y + (long long)R * H, y);
     EP_CUDA(cudaGetLastError(), "combine");
     EP_MARK(5);
 #undef EP_MARK
 #undef EP_CUDA
-#undef EP_NCCL
+#undef EP_XCHG
 #undef EP_GET
     return 0;
 }

@@ -239,6 +239,15 @@ class StrataEngine:
         self.disposed = False
         self.owner = str(uuid.uuid4())
         self.stats = dict(tokens=0, routes=[])
+        # When a list: every MoE layer's output is read back and appended as
+        # {position, layer, y} (conformance checks; a read per layer, so off by default).
+        self.moe_trace = None
+
+    def _trace_moe(self, layer: int, y, position: int, tokens: int) -> None:
+        if self.moe_trace is not None:
+            v = np.array(self.b.read(y), np.float32).reshape(tokens, self.g["width"])
+            for t in range(tokens):
+                self.moe_trace.append(dict(position=position + t, layer=layer, y=v[t].copy()))
 
     @classmethod
     def create(cls, store, backend, moe_mode: int = 0, graph: bool = False) -> "StrataEngine":
@@ -447,11 +456,16 @@ class StrataEngine:
         g, o = self.g, self.ops
         y, ids, weights = o.alloc(tokens * g["width"]), o.alloc(tokens * g["topK"], "i32"), o.alloc(tokens * g["topK"])
         fused(layer).forward(x, tokens, y, ids, weights, self.moe_mode)
+        if self.moe_trace is not None:  # conformance checks: the routed ids as well
+            sel = self.b.read(ids, "i32").reshape(tokens, g["topK"])
+            for t in range(tokens):
+                self.stats["routes"].append(dict(layer=layer, ids=[int(v) for v in sel[t]]))
         return y
 
     def moe(self, layer: int, x):
         y = self.fused_moe(layer, x, 1)
         if y is not None:
+            self._trace_moe(layer, y, self.position, 1)
             return y
         g, o, b = self.g, self.ops, self.b
         p = f"blk.{layer}."
@@ -470,6 +484,7 @@ class StrataEngine:
         y = o.alloc(g["width"])
         b.run("strata_moe_combine", dict(Parts=parts, Weights=weights, Shared=shared, SharedGate=shared_gate, Y=y, width=g["width"],
                                          count=g["topK"]), grid(g["width"]))
+        self._trace_moe(layer, y, self.position, 1)
         return y
 
     _progress = None
@@ -830,6 +845,7 @@ class PromptBatch:
     def moe(self, layer: int, x):
         y = self.e.fused_moe(layer, x, self.n)
         if y is not None:
+            self.e._trace_moe(layer, y, self.position, self.n)
             return y
         g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
         p = f"blk.{layer}."
@@ -858,6 +874,7 @@ class PromptBatch:
         y = o.alloc(n * g["width"])
         b.run("strata_moe_combine_batch", dict(Parts=parts, Weights=weights, Shared=shared, SharedGate=shared_gate, Y=y, width=g["width"],
                                                count=g["topK"], tokens=n), grid(y.length))
+        e._trace_moe(layer, y, self.position, n)
         return y
 
     def run(self, bookkeeping: bool = True) -> None:

@@ -1,4 +1,5 @@
-"""Expert-parallel MoE layer over NCCL (strata_moe_ep_forward): one process per GPU.
+"""Expert-parallel MoE layer (strata_moe_ep_forward): one process per GPU over NCCL, or n
+virtual ranks on one GPU over the library's loopback transport (tests).
 
 The layer's routed experts are sharded evenly: rank r holds experts [r E/n, (r + 1) E/n) and
 runs them for every rank's tokens that route there; router, shared gate and shared expert are
@@ -8,10 +9,18 @@ bit-exact, y within 2e-3 relative L2).
 
 The NCCL communicator lives in the library (bound at run time to the process's libnccl.so.2);
 the ranks share its 128-byte unique id through torch.distributed (any backend).
+
+Failure detection has two layers. In the library, every host wait on the peers is bounded
+(strata_ep_set_timeout) and a lost peer aborts the communicator with an error status. On the
+host, ``EpHealth`` is a step rendezvous through the process group's store: before each step a
+rank announces it and waits, with a deadline, for every peer to announce the same step, so a
+rank that crashed or left between steps is reported by name before anyone launches the next
+exchange (the reference's analogue is its failed-session state, src/engine.js:147-151).
 """
 from __future__ import annotations
 
 import ctypes as C
+import time
 from dataclasses import dataclass
 
 import numpy as np
@@ -33,6 +42,76 @@ def ep_init(backend: CudaBackend, rank: int, n_ranks: int) -> None:
     if n_ranks > 1:
         dist.broadcast_object_list(ident, src=0)
     backend._check(backend.lib.strata_ep_init(backend.ctx, int(rank), int(n_ranks), C.c_char_p(ident[0])))
+
+
+def ep_init_loopback(backends: list[CudaBackend], timeout_ms: int | None = None) -> None:
+    """n virtual ranks on one GPU: backends[r] (one context each, same device) becomes rank r
+    of a loopback hub. Drive the ranks' forwards from n host threads (ctypes releases the GIL),
+    as separate processes would."""
+    b0 = backends[0]
+    hub = C.c_uint64()
+    b0._check(b0.lib.strata_ep_loopback_create(b0.ctx, len(backends), C.byref(hub)))
+    try:
+        for r, b in enumerate(backends):
+            if timeout_ms is not None:
+                b._check(b.lib.strata_ep_set_timeout(b.ctx, int(timeout_ms)))
+            b._check(b.lib.strata_ep_init_loopback(b.ctx, r, hub.value))
+    finally:
+        b0._check(b0.lib.strata_ep_loopback_release(b0.ctx, hub.value))
+
+
+def ep_set_timeout(backend: CudaBackend, timeout_ms: int) -> None:
+    """Bound of every host wait on the peers (default 60 s)."""
+    backend._check(backend.lib.strata_ep_set_timeout(backend.ctx, int(timeout_ms)))
+
+
+class EpPeerFailure(RuntimeError):
+    """A peer rank did not reach a step within the deadline, or announced that it left."""
+
+    def __init__(self, missing: list[int], step: int, left: list[int]):
+        what = []
+        if left:
+            what.append(f"rank(s) {left} left")
+        if missing:
+            what.append(f"rank(s) {missing} did not reach step {step}")
+        super().__init__("expert-parallel peers failed: " + "; ".join(what))
+        self.missing, self.left, self.step = missing, left, step
+
+
+class EpHealth:
+    """Host-side liveness of the expert-parallel ranks through a torch.distributed store.
+
+    ``arrive(step)`` publishes this rank's step and waits until every peer has published the
+    same step; it raises EpPeerFailure naming the ranks that announced ``leave()`` (at once) or
+    did not arrive within ``timeout_s``. Call it before each step's exchange: a peer that dies
+    between steps is then reported on the host, before any collective with it is launched."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 30.0, prefix: str = "strata_ep_health"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+
+    def _key(self, *parts) -> str:
+        return "/".join((self.prefix,) + tuple(str(p) for p in parts))
+
+    def leave(self) -> None:
+        self.store.set(self._key("left", self.rank), "1")
+
+    def _has(self, key: str) -> bool:
+        return bool(self.store.check([key]))
+
+    def arrive(self, step: int, poll_s: float = 0.005) -> None:
+        self.store.set(self._key("step", step, self.rank), "1")
+        deadline = time.monotonic() + self.timeout_s
+        pending = [r for r in range(self.world) if r != self.rank]
+        while True:
+            pending = [r for r in pending if not self._has(self._key("step", step, r))]
+            left = [r for r in range(self.world) if r != self.rank and self._has(self._key("left", r))]
+            left_pending = [r for r in left if r in pending]
+            if not pending:
+                return
+            if left_pending or time.monotonic() >= deadline:
+                raise EpPeerFailure([r for r in pending if r not in left_pending], step, left_pending)
+            time.sleep(poll_s)
 
 
 @dataclass

@@ -97,3 +97,41 @@ def test_prefill_samples_vs_oracle(b, port):
     for i, t in enumerate(sample):
         assert rel_l2(y[t], y_o[i]) <= TOL, (t, rel_l2(y[t], y_o[i]))
     layer.free()
+
+
+def test_prefill_4096_zipf_fast_path(b, port):
+    """BASELINE config 3 itself on the tensor-core path it benchmarks (T = 4096, Zipf(1.1)
+    router offsets, STRATA_MOE_FAST): every token's ids and weights bit-identical to the exact
+    layer and y within 2e-3 relative L2 per token; 16 sampled tokens against the oracle (the
+    reference's per-token layer, src/engine.js:133-156) for ids, weights and y."""
+    from oracle.oracle import moe_layer_port, route_port
+    from stratacuda_b200 import _lib as L
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import MoeLayer, synth_activations
+    T, E, K, H, F = 4096, 512, 10, 2048, 512
+    layer = MoeLayer.synthesize(b, seed=1, layer=0, zipf=1.1)
+    xb = synth_activations(b, 3, T, H)
+    yf, idf, wf = run(b, layer, xb, T, L.MOE_FAST)
+    ye, ide, we = run(b, layer, xb, T, L.MOE_EXACT)
+    b.free(xb)
+    assert np.array_equal(idf, ide)
+    assert np.array_equal(bits(wf), bits(we))
+    errs = np.array([rel_l2(yf[t], ye[t]) for t in range(T)])
+    assert errs.max() <= TOL, (int(errs.argmax()), float(errs.max()))
+    # the workload is the skewed one: the top expert holds many 128-row tiles
+    counts = np.bincount(idf.reshape(-1), minlength=E)
+    assert counts.max() > 8 * T * K / E
+    x = synth.activations(3, T, H)
+    router = synth.router_weights(1, 0, E, H)
+    bias = synth.zipf_bias(1, E, 1.1)
+    sample = sorted(np.random.default_rng(4096).choice(T, 16, replace=False).tolist())
+    _, ids_o, w_o = route_port(port, x[sample], router, K, bias)
+    assert np.array_equal(idf[sample], ids_o)
+    assert np.array_equal(bits(wf[sample]), bits(w_o))
+    blobs = np.zeros((E, layer.blob_words), np.uint32)
+    for e in sorted(set(ids_o.reshape(-1).tolist())):
+        blobs[e] = synth.expert_blob(1, 0, e, H, F)
+    y_o, _, _ = moe_layer_port(port, x[sample], router, synth.shared_gate(1, 0, H), blobs, synth.expert_blob(1, 0, 0, H, F, True), K, bias)
+    for i, t in enumerate(sample):
+        assert rel_l2(yf[t], y_o[i]) <= TOL, (t, rel_l2(yf[t], y_o[i]))
+    layer.free()

@@ -62,3 +62,28 @@ def test_reference_build_gives_the_same_logits():
     assert len(a["logits"]) == len(b["logits"])
     for x, y in zip(a["logits"], b["logits"]):
         assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
+
+
+def test_config1_reference_build_and_f64_engine():
+    """BASELINE config 1 on the CPU: the C restatement against the reference's own compiled
+    kernels (tokens, routes, MoE outputs, logits bit for bit) and against the F64 reference
+    engine (8e-5 relative on the logits, the same greedy tokens); the greedy run is not
+    degenerate."""
+    from config1_case import PROMPT_LEN, compare_runs, prompt_ids, run_config1
+    from oracle.engine_ref import ReferenceEngine, compare
+    try:
+        ref = Oracle("reference", threads=2)
+    except FileNotFoundError:
+        pytest.skip("oracle/_ref not built")
+    port = run_config1(OracleBackend(Oracle("port")))
+    assert compare_runs(port, run_config1(OracleBackend(ref))) == 0.0
+    f64 = ReferenceEngine(create_fixture())
+    for t in prompt_ids()[:-1]:
+        f64.step(t)
+    feed = [prompt_ids()[-1]] + port["tokens"][:-1]
+    for i, t in enumerate(feed):
+        want = f64.step(t)
+        assert want["token"] == port["tokens"][i]
+        compare(port["logits"][i], want["logits"], 8e-5)
+        assert len(port["routes"]) >= PROMPT_LEN * 4
+    assert len(set(port["tokens"])) > 1

@@ -62,3 +62,49 @@ def test_noalloc_matches_fused_layer_on_two_calls_in_a_row():
         layer.free()
     finally:
         b.dispose()
+
+
+def test_noalloc_failed_routing_does_not_read_an_older_call():
+    """A router bias of NaN on one expert makes every token's probabilities NaN, so every id
+    is -1 (the reference rejects that routing, src/engine.js:138). The first call leaves a
+    finite layer's parts rows in the shared scratch; the second call, with the NaN bias, must
+    give exactly the handle-based layer's y (the shared expert alone), not a mix with those
+    stale rows. The handle-based layer also reports the routing error at its next sync."""
+    from stratacuda_b200 import _lib as L
+    from stratacuda_b200.backend import CudaBackend, StrataError
+    from stratacuda_b200.moe import MoeLayer, synth_activations
+
+    b = CudaBackend(0)
+    try:
+        layer = MoeLayer.synthesize(b, seed=6, layer=0, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK)
+        stream = C.c_void_p(b.stream_handle)
+        T = 9
+        x = synth_activations(b, 31, T, WIDTH)
+        y, ids, w = b.alloc(T * WIDTH), b.alloc(T * TOPK, "i32"), b.alloc(T * TOPK)
+        msg = C.create_string_buffer(256)
+        dev = _dev_layer(layer)
+        assert b.lib.strata_moe_forward_noalloc(C.byref(dev), x.device_ptr, T, y.device_ptr, ids.device_ptr, w.device_ptr, stream, msg,
+                                                len(msg)) == L.OK, msg.value
+        b.idle()
+        assert (b.read(ids) >= 0).all()
+        bias = np.zeros(EXPERTS, np.float32)
+        bias[17] = np.nan
+        layer.router_bias = b.alloc(bias)
+        y_ref, ids_ref, w_ref = b.alloc(T * WIDTH), b.alloc(T * TOPK, "i32"), b.alloc(T * TOPK)
+        layer.forward(x, T, y_ref, ids_ref, w_ref)
+        with pytest.raises(StrataError, match="invalid expert routing"):
+            b.idle()
+        dev = _dev_layer(layer)
+        assert b.lib.strata_moe_forward_noalloc(C.byref(dev), x.device_ptr, T, y.device_ptr, ids.device_ptr, w.device_ptr, stream, msg,
+                                                len(msg)) == L.OK, msg.value
+        b.idle()
+        got_ids, want_ids = b.read(ids), b.read(ids_ref)
+        assert (want_ids == -1).all() and np.array_equal(got_ids, want_ids)
+        got_y, want_y = b.read(y), b.read(y_ref)
+        assert np.isfinite(want_y).all()
+        assert np.array_equal(got_y.view(np.uint32), want_y.view(np.uint32))
+        for buf in (x, y, ids, w, y_ref, ids_ref, w_ref):
+            b.free(buf)
+        layer.free()
+    finally:
+        b.dispose()
