@@ -26,10 +26,20 @@ fresh activation batch per step, so no step reads weights left in L2 by the prev
           (oracle/_ref, WASM-path host order, 8 threads) on a bounded sample of the same
           workload; falls back to the C restatement when the native build is absent.
 
-Multi-GPU: by default every rank runs its own replica of the layer stack (the reference has
-no multi-GPU path); scaling is weak. `--ep` runs BASELINE config 4 instead: 16384 tokens
-split over the ranks, the 512 experts sharded, Zipf(1.1) routing, NCCL dispatch and return
-inside the library; scaling is strong.
+Nested blocks (skipped with --headline-only): the line also carries the metric's other
+configurations, each timed the same way on the same GPU(s):
+  decode_b8, decode_b64   BASELINE config 2's other batch sizes: tokens/s and the HBM roofline
+          from the experts each step actually routed to;
+  prefill_4096            BASELINE config 3 (Zipf(1.1) router offsets): layer tokens/s, the
+          grouped GEMMs' TFLOP/s against the measured sustained dense BF16 peak, phase split;
+  ep                      BASELINE config 4 at this run's N: 16384 tokens split over the ranks,
+          the 512 experts sharded, NCCL dispatch and return between the ranks when N >= 2;
+          tokens/s (max over ranks), per-GPU TFLOP/s, rank 0's phase split, and
+          efficiency_vs_n1 when an N=1 run on the same host left its number in /tmp.
+
+Multi-GPU: the headline has every rank run its own replica of the layer stack (the reference
+has no multi-GPU path); scaling is weak. The `ep` block (and `--ep`, which times BASELINE
+config 4 alone) is strong scaling.
 """
 from __future__ import annotations
 
@@ -210,11 +220,125 @@ def peak_tflops():
 
 # ----------------------------------------------------------------------------- GPU arm
 
+class LayerSteps:
+    """Per-step device buffers of a batch size over a stack of layers: fresh activations every
+    step (a ring of 8 batches above 64 tokens), one dedicated y/ids/weights slot per batch."""
+
+    def __init__(self, b, B, n_x, seed):
+        from stratacuda_b200.moe import synth_activations
+        self.b, self.B, self.n_x = b, B, n_x
+        x_all = synth_activations(b, seed, n_x * B, WIDTH)
+        self.xs = [b.alloc(B * WIDTH, zero=False) for _ in range(n_x)]
+        for s in range(n_x):
+            b.copy(x_all, self.xs[s], B * WIDTH, s * B * WIDTH, 0)
+        self.x_all = x_all
+        self.ys = [b.alloc(B * WIDTH, zero=False) for _ in range(n_x)]
+        self.idss = [b.alloc(B * TOPK, "i32") for _ in range(n_x)]
+        self.wss = [b.alloc(B * TOPK, zero=False) for _ in range(n_x)]
+        b.idle()
+
+    def run(self, layers, s, mode):
+        i = s % self.n_x
+        layers[s % len(layers)].forward(self.xs[i], self.B, self.ys[i], self.idss[i], self.wss[i], mode=mode)
+
+    def free(self):
+        for buf in [self.x_all] + self.xs + self.ys + self.idss + self.wss:
+            self.b.free(buf)
+
+
+def time_layer_steps(b, layers, st, K, W, mode, world, local, graph=True, clocks=False):
+    """W warm-up steps, then K steps captured once as a CUDA graph and replayed between CUDA
+    events on the library's stream (K direct launches without `graph`); max over ranks."""
+    import torch
+    stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", local))
+    for s in range(W):
+        st.run(layers, s, mode)
+    b.idle()
+    g = None
+    if graph:
+        b.capture_begin()
+        for s in range(W, W + K):
+            st.run(layers, s, mode)
+        g = b.capture_end()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local) if clocks else None
+    if sampler:
+        sampler.__enter__()
+    start.record(stream)
+    if g is not None:
+        b.graph_launch(g)
+    else:
+        for s in range(W, W + K):
+            st.run(layers, s, mode)
+    end.record(stream)
+    b.idle()
+    if sampler:
+        sampler.__exit__(None, None, None)
+    if g is not None:
+        b.graph_free(g)
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    ms = dist_max(start.elapsed_time(end), world)
+    return ms, (sampler.summary() if sampler else None)
+
+
+def routed_bytes(b, st, B, K, W):
+    """Algorithmic bytes per step from the routing that actually happened (the last n_x steps):
+    the U + 1 distinct blobs read, router rows, shared gate, activations in and out."""
+    out = []
+    for s in range(max(W, W + K - st.n_x), W + K):
+        U = len(set(b.read(st.idss[s % st.n_x]).tolist()))
+        out.append((U + 1) * BLOB_BYTES + ROUTER_BYTES + GATE_BYTES + 2 * B * WIDTH * 4)
+    return float(np.mean(out))
+
+
+def decode_block(b, layers, B, K, W, mode, world, local):
+    """A decode batch (BASELINE config 2's 8 and 64): tokens/s and the HBM roofline."""
+    from stratacuda_b200 import _lib as LL
+    st = LayerSteps(b, B, K + W, seed=20 + B)
+    ms, _ = time_layer_steps(b, layers, st, K, W, mode, world, local)
+    alg = routed_bytes(b, st, B, K, W)
+    st.free()
+    hbm, kind = peaks()
+    step_s = ms / 1000.0 / K
+    kernel = ("k_moe_fast (one persistent launch per step)" if mode == LL.MOE_FAST and B <= 8 else
+              "k_moe_medium (after the exact router kernels: 4 launches per step)" if mode == LL.MOE_FAST else "fused exact layer")
+    return {"batch": B, "tokens_per_s": B * K * world / (ms / 1000.0), "ms_per_step": ms / K, "steps": K, "warmup": W,
+            "roofline": {"bound": "hbm", "achieved": alg / step_s / 1e9, "peak": hbm, "unit": "GB/s", "frac": alg / step_s / 1e9 / hbm,
+                         "peak_kind": kind, "algorithmic_bytes_per_step": alg, "kernel": kernel}}
+
+
+def prefill_block(b, layers, K, W, mode, world, local, T=4096, zipf=1.1):
+    """4096 tokens, Zipf(1.1) router offsets, tensor-core prefill path."""
+    from stratacuda_b200 import synth
+    bias = b.alloc(synth.zipf_bias(1, EXPERTS, zipf))
+    for L in layers:
+        L.router_bias = bias
+    try:
+        st = LayerSteps(b, T, 8, seed=40)
+        ms, _ = time_layer_steps(b, layers, st, K, W, mode, world, local)
+        roof = prefill_roofline(b, layers, st.xs, st.ys, st.idss, st.wss, T, len(layers), st.n_x, mode, K)
+        st.free()
+    finally:
+        for L in layers:
+            L.router_bias = None
+        b.free(bias)
+    flops = 2.0 * 3 * WIDTH * FF * (T * TOPK + T)
+    peak, kind = peak_tflops()
+    layer_tf = flops / (ms / 1000.0 / K) / 1e12
+    return {"tokens": T, "zipf": zipf, "tokens_per_s": T * K * world / (ms / 1000.0), "ms_per_step": ms / K, "steps": K, "warmup": W,
+            "layer_tflops": layer_tf, "layer_frac": layer_tf / peak, "gemm_tflops": roof["achieved"], "gemm_frac": roof["frac"],
+            "peak_tflops": peak, "peak_kind": kind, "phase_ms_per_step": roof["phase_ms_per_step"],
+            "kernel": roof["kernel"], "algorithmic_flops_per_step": flops}
+
+
 def run_gpu_arm(args, world, rank, local):
     import torch
 
     from stratacuda_b200.backend import CudaBackend
-    from stratacuda_b200.moe import MoeLayer, synth_activations
+    from stratacuda_b200.moe import MoeLayer
 
     torch.cuda.set_device(local)
     b = CudaBackend(local)
@@ -222,25 +346,7 @@ def run_gpu_arm(args, world, rank, local):
     zipf = args.zipf if args.zipf is not None else (1.1 if B > 64 else None)
     layers = [MoeLayer.synthesize(b, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf) for l in range(NL)]
     # distinct activation batches: every step for small batches, a ring of 8 for large ones
-    n_x = K + W if B <= 64 else min(K + W, 8)
-    x_all = synth_activations(b, 2 + rank, n_x * B, WIDTH)
-    y_all = b.alloc(n_x * B * WIDTH, zero=False)
-    ids_all = b.alloc(n_x * B * TOPK, "i32")
-    w_all = b.alloc(n_x * B * TOPK, zero=False)
-    b.idle()
-
-    # views into the per-step slices: the fused call takes whole buffers, so give it
-    # per-step buffers that alias nothing (copy-free: a dedicated buffer per step)
-    xs = [b.alloc(B * WIDTH, zero=False) for _ in range(n_x)]
-    for s in range(n_x):
-        b.copy(x_all, xs[s], B * WIDTH, s * B * WIDTH, 0)
-    ys = [b.alloc(B * WIDTH, zero=False) for _ in range(n_x)]
-    idss = [b.alloc(B * TOPK, "i32") for _ in range(n_x)]
-    wss = [b.alloc(B * TOPK, zero=False) for _ in range(n_x)]
-    b.idle()
-    slot = lambda s: s % n_x
-
-    stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", local))
+    st = LayerSteps(b, B, K + W if B <= 64 else min(K + W, 8), seed=2 + rank)
     from stratacuda_b200 import _lib as LL
     mode = LL.MOE_FAST if args.mode == "fast" else LL.MOE_EXACT
     medium = mode == LL.MOE_FAST and 8 < B <= 64
@@ -248,47 +354,13 @@ def run_gpu_arm(args, world, rank, local):
     # kernels per step: decode 1; medium 4 (router tail rows, exact logits, top-k, the layer);
     # prefill 9; exact 6
     launches = 1 if (mode == LL.MOE_FAST and B <= 8) else 4 if medium else 9 if prefill else 6
-    for s in range(W):
-        layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
-    b.idle()
-    # the K timed steps are captured once as a CUDA graph and replayed (the launches are the
-    # same kernels with the same arguments; replay removes the per-call host launch path)
-    graph = None
-    if not args.no_graph:
-        b.capture_begin()
-        for s in range(W, W + K):
-            layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
-        graph = b.capture_end()
-    dist_barrier(world)
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record(stream)
-        if graph is not None:
-            b.graph_launch(graph)
-        else:
-            for s in range(W, W + K):
-                layers[s % NL].forward(xs[slot(s)], B, ys[slot(s)], idss[slot(s)], wss[slot(s)], mode=mode)
-        end.record(stream)
-        b.idle()
-    if graph is not None:
-        b.graph_free(graph)
-    torch.cuda.synchronize()
-    dist_barrier(world)
-    ms = start.elapsed_time(end)
-    ms_max = dist_max(ms, world)
-    # algorithmic bytes per step from the routing that actually happened (the last n_x steps)
-    bytes_steps = []
-    for s in range(max(W, W + K - n_x), W + K):
-        ids = b.read(idss[slot(s)])
-        U = len(set(ids.tolist()))
-        bytes_steps.append((U + 1) * BLOB_BYTES + ROUTER_BYTES + GATE_BYTES + 2 * B * WIDTH * 4)
-    alg_bytes = float(np.mean(bytes_steps))
-    step_s = ms / 1000.0 / K
+    ms_max, clocks = time_layer_steps(b, layers, st, K, W, mode, world, local, graph=not args.no_graph, clocks=True)
+    alg_bytes = routed_bytes(b, st, B, K, W)
+    step_s = ms_max / 1000.0 / K
     hbm_peak, peak_kind = peaks()
     achieved = alg_bytes / step_s / 1e9
     if prefill:
-        roofline = prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K)
+        roofline = prefill_roofline(b, layers, st.xs, st.ys, st.idss, st.wss, B, NL, st.n_x, mode, K)
     else:
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
                     "peak_kind": peak_kind,
@@ -299,12 +371,13 @@ def run_gpu_arm(args, world, rank, local):
 
     # end to end through the C-ABI with host buffers (pinned), host-timed
     e2e_steps = min(K, max(20, K // 2)) if B <= 64 else min(K, 8)
+    e2e_steps = min(e2e_steps, st.n_x)
     hx = torch.empty(e2e_steps, B * WIDTH, dtype=torch.float32, pin_memory=True)
-    hx.copy_(torch.from_numpy(b.read(x_all, count=e2e_steps * B * WIDTH).reshape(e2e_steps, B * WIDTH)))
+    hx.copy_(torch.from_numpy(b.read(st.x_all, count=e2e_steps * B * WIDTH).reshape(e2e_steps, B * WIDTH)))
     hy = torch.empty(B * WIDTH, dtype=torch.float32, pin_memory=True)
     hx_np, hy_np = hx.numpy(), hy.numpy()
     lib, ctx = b.lib, b.ctx
-    xbuf, ybuf = xs[0], ys[0]
+    xbuf, ybuf = st.xs[0], st.ys[0]
     # Each layer's call is captured once (the decode-loop pattern of the graph API): a step is
     # strata_write of the batch from pinned memory, strata_graph_launch of that layer's call,
     # strata_read of y into pinned memory. --no-graph calls strata_moe_forward every step.
@@ -312,7 +385,7 @@ def run_gpu_arm(args, world, rank, local):
     if not args.no_graph:
         for l in range(min(NL, e2e_steps)):
             b.capture_begin()
-            layers[l].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
+            layers[l].forward(xbuf, B, ybuf, st.idss[0], st.wss[0], mode=mode)
             e2e_graphs.append(b.capture_end())
 
     def e2e_step(s):
@@ -320,7 +393,7 @@ def run_gpu_arm(args, world, rank, local):
         if e2e_graphs:
             b.graph_launch(e2e_graphs[s % len(e2e_graphs)])
         else:
-            layers[s % NL].forward(xbuf, B, ybuf, idss[0], wss[0], mode=mode)
+            layers[s % NL].forward(xbuf, B, ybuf, st.idss[0], st.wss[0], mode=mode)
         b._check(lib.strata_read(ctx, ybuf.handle, hy_np.ctypes.data, B * WIDTH, 0))
 
     for s in range(min(3, e2e_steps)):
@@ -333,6 +406,21 @@ def run_gpu_arm(args, world, rank, local):
     e2e_s = dist_max(e2e_s, world)
     for g in e2e_graphs:
         b.graph_free(g)
+    st.free()
+
+    # the metric's other configurations, nested in the same line (3, 4)
+    blocks = {}
+    if not args.headline_only:
+        kb, wb = min(K, 40), max(3, min(W, 5))
+        for bb in (8, 64):
+            if bb != B:
+                blocks[f"decode_b{bb}"] = decode_block(b, layers, bb, kb, wb, mode, world, local)
+        if B != 4096:
+            blocks["prefill_4096"] = prefill_block(b, layers, min(K, 10), 3, mode, world, local)
+    for L in layers:
+        L.free()
+    if not args.headline_only:
+        blocks["ep"] = ep_block(args, world, rank, local, b)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -357,14 +445,91 @@ def run_gpu_arm(args, world, rank, local):
                               "(pinned host, synchronising), host-timed" if e2e_graphs or not args.no_graph else
                               "strata_write (pinned host) + strata_moe_forward + strata_read (pinned host, synchronising), host-timed")},
             "gpu_launches": launches * K,
-            "clocks": clocks.summary()}
+            "clocks": clocks}
     if cpu:
         line["cpu_baseline"] = cpu
+    line.update(blocks)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    b.dispose()
+
+
+EP_N1_CACHE = pathlib.Path("/tmp/strata_bench_ep_n1.json")
+
+
+def ep_block(args, world, rank, local, b):
+    """BASELINE config 4 at this run's N: 16384 tokens split over the ranks, 512 experts sharded
+    E/N per GPU, Zipf(1.1) routing; at N >= 2 the library's NCCL dispatch and return run between
+    the ranks. Device time of K steps (CUDA events on the library's stream), max over ranks."""
+    import torch
+
+    from stratacuda_b200.ep import EpMoeLayer, ep_init
+    from stratacuda_b200.moe import synth_activations
+    total, K, W, NL = args.ep_tokens, min(args.steps, 10), 3, 4
+    if total % world or EXPERTS % world:
+        return {"skipped": f"{total} tokens and {EXPERTS} experts must divide over {world} ranks"}
+    T = total // world
+    zipf = 1.1
+    ep_init(b, rank, world)
+    layers = [EpMoeLayer.synthesize(b, rank, world, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf)
+              for l in range(NL)]
+    n_x = 2
+    xs = [synth_activations(b, 2 + s, T, WIDTH, start_token=rank * T) for s in range(n_x)]
+    ys = [b.alloc(T * WIDTH, zero=False) for _ in range(n_x)]
+    idss = [b.alloc(T * TOPK, "i32") for _ in range(n_x)]
+    wss = [b.alloc(T * TOPK, zero=False) for _ in range(n_x)]
+    b.idle()
+    stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", local))
+    step = lambda s: layers[s % NL].forward(xs[s % n_x], T, ys[s % n_x], idss[s % n_x], wss[s % n_x])
+    for s in range(W):
+        step(s)
+    b.idle()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(W, W + K):
+        step(s)
+    end.record(stream)
+    b.idle()
+    torch.cuda.synchronize()
+    dist_barrier(world)
+    ms_max = dist_max(start.elapsed_time(end), world)
+    b.profile(True)
+    for s in range(3):
+        step(s)
+    ph, calls = b.profile_read()
+    b.profile(False)
     for L in layers:
         L.free()
-    b.dispose()
+    for buf in xs + ys + idss + wss:
+        b.free(buf)
+    b.idle()
+    flops = 2.0 * 3 * WIDTH * FF * (total * TOPK + total)
+    peak, kind = peak_tflops()
+    per_gpu_tf = flops / (ms_max / 1000.0 / K) / world / 1e12
+    tps = total * K / (ms_max / 1000.0)
+    out = {"tokens": total, "tokens_per_rank": T, "experts_per_rank": EXPERTS // world, "zipf": zipf, "parallelism": f"ep{world}",
+           "exchange": "NCCL grouped send/recv inside strata_moe_ep_forward" if world > 1 else "none (one rank)",
+           "tokens_per_s": tps, "ms_per_step": ms_max / K, "steps": K, "warmup": W, "layers_cycled": NL,
+           "per_gpu_tflops": per_gpu_tf, "per_gpu_frac": per_gpu_tf / peak, "peak_tflops": peak, "peak_kind": kind,
+           "phase_ms_per_step_rank0": {k: v / max(1, calls) for k, v in ph.items() if k != "decode_kernel"},
+           "timing": "CUDA events around K direct calls (the layer reads the receive counts on the host), max over ranks"}
+    key = {"tokens": total, "zipf": zipf, "layers": NL}
+    if world == 1 and rank == 0:
+        try:
+            EP_N1_CACHE.write_text(json.dumps({"key": key, "tokens_per_s": tps}))
+        except OSError:
+            pass
+    elif world > 1:
+        try:
+            n1 = json.loads(EP_N1_CACHE.read_text())
+            if n1["key"] == key:
+                out["efficiency_vs_n1"] = tps / (world * n1["tokens_per_s"])
+                out["n1_tokens_per_s"] = n1["tokens_per_s"]
+        except (OSError, ValueError, KeyError):
+            pass
+    return out
 
 
 def run_ep_arm(args, world, rank, local):
@@ -551,6 +716,8 @@ def main():
     ap.add_argument("--mode", default="fast", choices=["fast", "exact"])
     ap.add_argument("--zipf", type=float, default=None, help="router bias skew (default: 1.1 for batches above 64 and --ep)")
     ap.add_argument("--ep", action="store_true", help="expert-parallel layer over the ranks (BASELINE config 4)")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="skip the nested blocks (decode_b8, decode_b64, prefill_4096, ep) of the default line")
     ap.add_argument("--no-graph", action="store_true", help="time direct launches instead of a CUDA graph replay of the K steps")
     ap.add_argument("--ep-tokens", type=int, default=16384, help="tokens of the expert-parallel job (split over the ranks)")
     ap.add_argument("--model", action="store_true", help="the full-model workload (48-layer synthetic model, 1 GPU)")

@@ -154,6 +154,13 @@ typedef struct {
 int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                        strata_buf weights, int32_t mode);
 
+/* Replaces the per-blob check of PackStore.readExpertBlob (src/model.js:160-167), which the
+ * whole-model upload skips: every FP16 scale of `count` consecutive Q2 blobs in `blobs` (gate/up
+ * and down scale planes) must be finite. Returns STRATA_ERR_LAYOUT "Non-finite expert scales
+ * (blob i)" naming the lowest offending blob. Synchronises. The fused kernels convert scales
+ * with the hardware FP16 conversion and rely on this check having passed on upload. */
+int strata_validate_experts(strata_ctx *ctx, strata_buf blobs, int32_t count, int32_t width, int32_t ff);
+
 /* ---- allocation-free fused layer ----
  * No counterpart in the reference. For callers that must not allocate device memory: a host
  * engine that has already carved HBM into its own arenas and forbids allocations behind its
@@ -260,7 +267,9 @@ int strata_profile(strata_ctx *ctx, int32_t enable);
 int strata_profile_read(strata_ctx *ctx, double *ms, int32_t n, uint64_t *calls);
 
 /* ---- seeded synthetic workload (device generator; same bytes as stratacuda_b200/synth.py) ---- */
-/* `count` expert blobs of one layer starting at `first_expert` into buf at element offset. */
+/* `count` expert blobs of one layer starting at `first_expert` into buf at element offset.
+ * `shared` is a flag word: 1 = the shared expert's random streams, 2 = signed FP16 scales
+ * N(0, 0.02) instead of |N(0, 0.02)|. */
 int strata_synth_blobs(strata_ctx *ctx, strata_buf buf, uint64_t offset, uint64_t seed, int32_t layer, int32_t first_expert,
                        int32_t count, int32_t width, int32_t ff, int32_t shared);
 /* `count` normals N(0,1)*scale of stream (seed, tag, sub) from draw `start` into buf at offset. */

@@ -67,6 +67,7 @@ SIGNATURES = {
     "strata_moe_ep_forward": ([_vp, C.POINTER(StrataMoeLayer), _u64, C.c_int32, _u64, _u64, _u64], _i),
     "strata_profile_read": ([_vp, C.POINTER(C.c_double), C.c_int32, C.POINTER(C.c_uint64)], _i),
     "strata_moe_forward": ([_vp, C.POINTER(StrataMoeLayer), _u64, C.c_int32, _u64, _u64, _u64, C.c_int32], _i),
+    "strata_validate_experts": ([_vp, _u64, C.c_int32, C.c_int32, C.c_int32], _i),
     "strata_moe_forward_noalloc": ([C.POINTER(StrataMoeLayerDev), _vp, C.c_int32, _vp, _vp, _vp, _vp, C.c_char_p, _sz], _i),
     "strata_synth_blobs": ([_vp, _u64, _u64, _u64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32], _i),
     "strata_synth_normals": ([_vp, _u64, _u64, _u64, _u64, _u64, _u64, _u64, _d], _i),

@@ -33,6 +33,7 @@ struct strata_ctx {
     unsigned *err_dev = nullptr;   // device error word (kErr* bits)
     unsigned *err_host = nullptr;  // pinned mirror
     unsigned *fast_sync = nullptr; // grid-arrival words of the fast fused kernel (self-resetting)
+    int *check_dev = nullptr;      // strata_validate_experts result
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
     uint64_t dispatches = 0, fused_calls = 0;
@@ -406,6 +407,7 @@ int strata_destroy(strata_ctx *ctx) {
     ctx->graphs.clear();
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->fast_sync) cudaFree(ctx->fast_sync);
+    if (ctx->check_dev) cudaFree(ctx->check_dev);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -807,6 +809,27 @@ int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata
     }
     if (rc) return fail(ctx, STRATA_ERR_CUDA, "strata_moe_ep_forward: %s", msg.c_str());
     ++ctx->fused_calls;
+    return STRATA_OK;
+}
+
+int strata_validate_experts(strata_ctx *ctx, strata_buf blobs, int32_t count, int32_t width, int32_t ff) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!blob_geometry_ok(width, ff)) return fail(ctx, STRATA_ERR_LAYOUT, "Packed expert dimensions must contain complete groups");
+    if (count < 1) return fail(ctx, STRATA_ERR_RANGE, "count must be an integer >= 1");
+    Buffer *b = find(ctx, blobs);
+    if (!b) return fail(ctx, STRATA_ERR_HANDLE, "validate experts: not a live buffer");
+    const long long bw = blob_words_of(width, ff);
+    if ((long long)b->length < bw * count)
+        return fail(ctx, STRATA_ERR_LAYOUT, "validate experts: the buffer holds %llu words, %d blobs need %lld", (unsigned long long)b->length,
+                    count, bw * count);
+    if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "synchronising calls are not allowed while the stream is captured");
+    if (int r = use_device(ctx)) return r;
+    if (!ctx->check_dev) CUDA_OR_FAIL(ctx, cudaMalloc(&ctx->check_dev, sizeof(int)), "cudaMalloc");
+    CUDA_OR_FAIL(ctx, check_expert_scales((const unsigned *)b->ptr, count, width, ff, ctx->check_dev, ctx->stream), "scale check");
+    int first_bad = 0;
+    CUDA_OR_FAIL(ctx, cudaMemcpyAsync(&first_bad, ctx->check_dev, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream), "readback");
+    if (int r = sync(ctx)) return r;
+    if (first_bad != 0x7f7f7f7f) return fail(ctx, STRATA_ERR_LAYOUT, "Non-finite expert scales (blob %d)", first_bad);
     return STRATA_OK;
 }
 

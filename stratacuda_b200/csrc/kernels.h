@@ -100,6 +100,10 @@ size_t moe_logits_tail_bytes(int width);
 cudaError_t moe_route_exact(const MoeLayerDev &L, const float *x, int T, float *logits, float *sg, float *tail, int *ids, float *weights,
                             int grid, cudaStream_t s, unsigned *err);
 
+// src/model.js:164: the lowest index of `count` blobs holding a non-finite FP16 scale into
+// *first_bad (device int), or 0x7f7f7f7f when every scale is finite.
+cudaError_t check_expert_scales(const unsigned *blobs, long long count, int width, int ff, int *first_bad, cudaStream_t s);
+
 // Prompt / large-batch layer (csrc/prefill.cu): exact routing, expert products on tcgen05
 // tensor cores from Q2 weights dequantised to FP16 (y within 2e-3 relative L2). `grid` is
 // the GEMMs' persistent grid (one CTA per SM).

@@ -16,6 +16,8 @@
 //   k_combine  : y = shared * sigmoid(sg) + sum_k parts[k] * w[k]   (kernels/strata.cu:470-476)
 // Slot 0 of the expert grids is the shared expert (all tokens), slot s > 0 the s-th active
 // routed expert; grids are sized for the worst case and slots past the active count exit.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "route.cuh"
@@ -256,7 +258,28 @@ __global__ void k_combine(const float *parts, const float *weights, const int *i
 
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
+// src/model.js:164 (readExpertBlob): every FP16 scale of a blob, from the gate/up scale plane to
+// the end of the down scale plane, must be finite (its exponent bits 0x7c00 not all set). Each
+// thread checks one word (two scales); the lowest offending blob index is kept.
+__global__ void k_check_scales(const unsigned *blobs, long long blob_words, long long first_word, long long count, int *first_bad) {
+    const long long per = blob_words - first_word, n = count * per;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long e = i / per;
+        const unsigned v = __ldg(blobs + e * blob_words + first_word + i % per);
+        if ((v & 0x7c00u) == 0x7c00u || (v & 0x7c000000u) == 0x7c000000u) atomicMin(first_bad, (int)e);
+    }
+}
+
 }  // namespace
+
+cudaError_t check_expert_scales(const unsigned *blobs, long long count, int width, int ff, int *first_bad, cudaStream_t s) {
+    const long long blob_words = 27LL * ff * width / 128, first_word = 3LL * ff * width / 16;
+    STRATA_CUDA_TRY(cudaMemsetAsync(first_bad, 0x7f, sizeof(int), s));  // 0x7f7f7f7f: no blob failed
+    const long long n = count * (blob_words - first_word);
+    const unsigned blocks = (unsigned)std::min<long long>((n + 255) / 256, 148LL * 16);
+    if (n > 0) k_check_scales<<<blocks, 256, 0, s>>>(blobs, blob_words, first_word, count, first_bad);
+    return cudaGetLastError();
+}
 
 size_t moe_scratch_bytes(int tokens, int width, int ff, int experts, int topK) {
     size_t P = (size_t)tokens * topK;

@@ -62,8 +62,10 @@ __host__ __device__ inline unsigned long long key_of(unsigned long long seed, un
     return mix(mix(seed + tag * kGamma) + sub * kSub);
 }
 
+// flags: 1 = the shared expert's streams, 2 = signed scales N(0, 0.02) instead of |N(0, 0.02)|
 __global__ void k_blobs(unsigned *out, unsigned long long seed, int layer, int first, int count, long long code_words, long long words,
-                        int shared) {
+                        int flags) {
+    const bool shared = flags & 1, sign = flags & 2;
     long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)count * words) return;
     int e = first + (int)(idx / words);
@@ -73,8 +75,9 @@ __global__ void k_blobs(unsigned *out, unsigned long long seed, int layer, int f
         out[idx] = (unsigned)(draw(key_of(seed, shared ? 6 : 3, sub), (unsigned long long)w) & 0xFFFFFFFFull);
     } else {
         unsigned long long hp = (unsigned long long)(w - code_words), sk = key_of(seed, shared ? 7 : 4, sub);
-        __half h0 = __double2half(fabs(__dmul_rn(normal_at(sk, 2 * hp), 0.02)));
-        __half h1 = __double2half(fabs(__dmul_rn(normal_at(sk, 2 * hp + 1), 0.02)));
+        const double z0 = __dmul_rn(normal_at(sk, 2 * hp), 0.02), z1 = __dmul_rn(normal_at(sk, 2 * hp + 1), 0.02);
+        __half h0 = __double2half(sign ? z0 : fabs(z0));
+        __half h1 = __double2half(sign ? z1 : fabs(z1));
         out[idx] = (unsigned)__half_as_ushort(h0) | ((unsigned)__half_as_ushort(h1) << 16);
     }
 }

@@ -64,6 +64,13 @@ class MoeLayer:
         b._check(b.lib.strata_moe_forward(b.ctx, C.byref(st), x.handle, int(tokens), y.handle, ids.handle, weights.handle,
                                           int(mode)))
 
+    def validate(self) -> None:
+        """Every expert's and the shared expert's FP16 scales are finite, or StrataError
+        'Non-finite expert scales' (src/model.js:164, checked on the resident blobs)."""
+        b = self.backend
+        b._check(b.lib.strata_validate_experts(b.ctx, self.experts_blob.handle, self.experts, self.width, self.ff))
+        b._check(b.lib.strata_validate_experts(b.ctx, self.shared_blob.handle, 1, self.width, self.ff))
+
     def free(self) -> None:
         for buf in (self.router, self.experts_blob, self.shared_blob, self.shared_gate, self.router_bias):
             if buf is not None:
@@ -78,15 +85,22 @@ class MoeLayer:
         ff = blobs.shape[1] * 4 * 32 // (27 * width)
         if blob_layout(width, ff)["blob_bytes"] != blobs.shape[1] * 4:
             raise StrataError(L.ERR_LAYOUT, "expert blob size does not match the geometry")
-        return cls(backend, width, ff, experts, top_k, backend.alloc(router.reshape(-1)), backend.alloc(blobs.reshape(-1), "u32"),
-                   backend.alloc(np.ascontiguousarray(shared_blob, np.uint32), "u32"),
-                   backend.alloc(np.ascontiguousarray(shared_gate, np.float32)),
-                   None if bias is None else backend.alloc(np.ascontiguousarray(bias, np.float32)))
+        layer = cls(backend, width, ff, experts, top_k, backend.alloc(router.reshape(-1)), backend.alloc(blobs.reshape(-1), "u32"),
+                    backend.alloc(np.ascontiguousarray(shared_blob, np.uint32), "u32"),
+                    backend.alloc(np.ascontiguousarray(shared_gate, np.float32)),
+                    None if bias is None else backend.alloc(np.ascontiguousarray(bias, np.float32)))
+        try:
+            layer.validate()
+        except Exception:
+            layer.free()
+            raise
+        return layer
 
     @classmethod
     def synthesize(cls, backend: CudaBackend, seed: int, layer: int, width: int = 2048, ff: int = 512, experts: int = 512,
-                   top_k: int = 10, zipf: float | None = None) -> "MoeLayer":
-        """The seeded synthetic layer, generated on the device (same bytes as synth.py)."""
+                   top_k: int = 10, zipf: float | None = None, signed_scales: bool = False) -> "MoeLayer":
+        """The seeded synthetic layer, generated on the device (same bytes as synth.py); FP16
+        group scales |N(0, 0.02)|, or N(0, 0.02) with `signed_scales`."""
         words = blob_layout(width, ff)["blob_bytes"] // 4
         lib, ctx = backend.lib, backend.ctx
         router = backend.alloc(experts * width, zero=False)
@@ -94,9 +108,10 @@ class MoeLayer:
         gate = backend.alloc(width, zero=False)
         backend._check(lib.strata_synth_normals(ctx, gate.handle, 0, seed, synth.TAG_SHARED_GATE, layer, 0, width, 0.02))
         blobs = backend.alloc(experts * words, "u32", zero=False)
-        backend._check(lib.strata_synth_blobs(ctx, blobs.handle, 0, seed, layer, 0, experts, width, ff, 0))
+        sign = 2 if signed_scales else 0
+        backend._check(lib.strata_synth_blobs(ctx, blobs.handle, 0, seed, layer, 0, experts, width, ff, sign))
         shared = backend.alloc(words, "u32", zero=False)
-        backend._check(lib.strata_synth_blobs(ctx, shared.handle, 0, seed, layer, 0, 1, width, ff, 1))
+        backend._check(lib.strata_synth_blobs(ctx, shared.handle, 0, seed, layer, 0, 1, width, ff, 1 | sign))
         bias = None if zipf is None else backend.alloc(synth.zipf_bias(seed, experts, zipf))
         return cls(backend, width, ff, experts, top_k, router, blobs, shared, gate, bias)
 

@@ -107,15 +107,17 @@ def normals(key: int, start: int, count: int) -> np.ndarray:
     return np.sqrt(-2.0 * det_log(u1)) * det_cos_turns(u2)
 
 
-def expert_blob(seed: int, layer: int, expert: int, width: int, ff: int, shared: bool = False) -> np.ndarray:
-    """One Q2 expert blob (u32 words): uniform code words, then |N(0,0.02)| FP16 scales."""
+def expert_blob(seed: int, layer: int, expert: int, width: int, ff: int, shared: bool = False, signed: bool = False) -> np.ndarray:
+    """One Q2 expert blob (u32 words): uniform code words, then |N(0,0.02)| FP16 scales
+    (N(0,0.02) with `signed`)."""
     code_words = 3 * ff * width // 16
     halves = 3 * ff * width // 64
     sub = (layer << 20) | expert
     ck = stream_key(seed, TAG_SHARED_CODES if shared else TAG_CODES, sub)
     sk = stream_key(seed, TAG_SHARED_SCALES if shared else TAG_SCALES, sub)
     codes = (draws(ck, 0, code_words) & np.uint64(0xFFFFFFFF)).astype(np.uint32)
-    scales = np.abs(normals(sk, 0, halves) * 0.02).astype(np.float16)
+    z = normals(sk, 0, halves) * 0.02
+    scales = (z if signed else np.abs(z)).astype(np.float16)
     return np.concatenate([codes, scales.view(np.uint16).view(np.uint32)])
 
 

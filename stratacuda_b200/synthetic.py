@@ -21,8 +21,12 @@ Values:
 * token embeddings are N(0, 0.16);
 * norm gammas are 1 + N(0, 0.0025);
 * ssm_a is -0.1 - |N(0, 1)| and ssm_dt.bias is N(0, 0.01);
-* the mixture-of-experts layers are those of the single-layer workload (MoeLayer.synthesize:
-  router N(0, 0.0004), uniform 2-bit codes, FP16 group scales |N(0, 0.0004)|);
+* the mixture-of-experts layers are the single-layer workload's (MoeLayer.synthesize: router
+  N(0, 0.02), uniform 2-bit codes) except that the FP16 group scales are signed, N(0, 0.02)
+  rather than |N(0, 0.02)|. Uniform codes give the weight values (code - 1) a mean of 0.5, so
+  with positive scales every expert output carries a component along one fixed direction; over
+  48 layers it swamps the residual, and greedy decode returned one token for every prompt.
+  Signed scales make every weight zero-mean;
 * the PLE table has random codes and FP16 scales |N(0, 1e-4)|.
 """
 from __future__ import annotations
@@ -139,7 +143,8 @@ class DeviceStore:
                 self.buffers[name] = self._normals(name, n, 1.0 / np.sqrt(shape[0]))
         for layer in range(g["layers"]):
             self.layers.append(MoeLayer.synthesize(self.b, self.seed, layer, width=g["width"], ff=g["ff"], experts=g["experts"],
-                                                   top_k=g["topK"]))
+                                                   top_k=g["topK"], signed_scales=True))
+            self.layers[-1].validate()  # the upload-time scale check of src/model.js:164
         rows = sum(self.constants["vocab"])
         blocks = rows * g["pleHeadDim"] // 32
         raw = rng.integers(0, 256, blocks * 18, dtype=np.uint8)

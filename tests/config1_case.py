@@ -43,12 +43,20 @@ def run_config1(backend) -> dict:
                 moe={key(d): d["y"] for d in trace})
 
 
-def compare_runs(a: dict, b: dict) -> float:
-    """Same tokens, routes and MoE outputs bit for bit; returns the largest |logit difference|."""
+def compare_runs(a: dict, b: dict, moe_tol: float = 0.0) -> dict:
+    """Same tokens and routes; every MoE output bit for bit (moe_tol 0) or within moe_tol
+    relative L2. Returns the largest |logit difference|, the largest MoE relative L2 and the
+    number of MoE outputs that are not bit-identical."""
     assert a["tokens"] == b["tokens"], (a["tokens"], b["tokens"])
     assert a["routes"] == b["routes"]
     assert a["moe"].keys() == b["moe"].keys() and len(a["moe"]) == (PROMPT_LEN + DECODE_STEPS) * 4
+    worst_moe, differ = 0.0, 0
     for k in a["moe"]:
-        assert np.array_equal(a["moe"][k].view(np.uint32), b["moe"][k].view(np.uint32)), k
+        x, y = a["moe"][k].astype(np.float64), b["moe"][k].astype(np.float64)
+        if not np.array_equal(a["moe"][k].view(np.uint32), b["moe"][k].view(np.uint32)):
+            differ += 1
+            worst_moe = max(worst_moe, float(np.linalg.norm(x - y) / max(np.linalg.norm(y), 1e-30)))
+    assert worst_moe <= moe_tol, (worst_moe, moe_tol)
     assert len(a["logits"]) == len(b["logits"]) == DECODE_STEPS + 1
-    return max(float(np.abs(x.astype(np.float64) - y).max()) for x, y in zip(a["logits"], b["logits"]))
+    logits = max(float(np.abs(x.astype(np.float64) - y).max()) for x, y in zip(a["logits"], b["logits"]))
+    return dict(logits=logits, moe=worst_moe, moe_differ=differ)

@@ -190,3 +190,71 @@ def test_fused_rejects_bad_layouts(b, layer):
     for buf in (x, y, ids, w):
         b.free(buf)
     b.idle()
+
+
+def test_upload_rejects_non_finite_expert_scales(b, golden):
+    """src/model.js:164: a blob holding an FP16 scale with exponent 0x1f (inf or NaN) is
+    rejected with 'Non-finite expert scales' on upload; the clean layer passes."""
+    from stratacuda_b200.backend import StrataError
+    from stratacuda_b200.moe import MoeLayer, blob_layout
+    g = golden["moe_small"]
+    L = MoeLayer.upload(b, g["router"], g["blobs"], g["shared_blob"], g["shared_gate"], int(g["top_k"]), g["bias"])
+    L.free()
+    width, ff = g["router"].shape[1], None
+    lay = None
+    for bad_expert, plane, value in ((3, "gate_up_scales", 0x7c00), (0, "down_scales", 0xfe00)):
+        blobs = np.array(g["blobs"], np.uint32).copy()
+        E = blobs.shape[0]
+        ff = blobs.shape[1] * 4 * 32 // (27 * width)
+        lay = blob_layout(width, ff)
+        raw = blobs.view(np.uint8).reshape(E, -1)
+        off = lay[plane] + 2 * 5
+        raw[bad_expert, off:off + 2] = np.array([value], np.uint16).view(np.uint8)
+        with pytest.raises(StrataError, match=f"Non-finite expert scales \\(blob {bad_expert}\\)"):
+            MoeLayer.upload(b, g["router"], blobs, g["shared_blob"], g["shared_gate"], int(g["top_k"]), g["bias"])
+    shared = np.array(g["shared_blob"], np.uint32).copy()
+    shared.view(np.uint8)[lay["blob_bytes"] - 2:] = np.array([0x7fff], np.uint16).view(np.uint8)  # last scale of the down plane
+    with pytest.raises(StrataError, match="Non-finite expert scales"):
+        MoeLayer.upload(b, g["router"], g["blobs"], shared, g["shared_gate"], int(g["top_k"]), g["bias"])
+    b.idle()
+
+
+def test_device_generator_signed_scales_match_numpy(b):
+    """The full model's layers: the same codes, FP16 scales N(0, 0.02) with their signs."""
+    from stratacuda_b200 import synth
+    from stratacuda_b200.moe import MoeLayer, blob_layout
+    L = MoeLayer.synthesize(b, seed=1, layer=7, signed_scales=True)
+    words = L.blob_words
+    for e in (0, 200):
+        got = b.read(L.experts_blob, count=words, offset=e * words)
+        want = synth.expert_blob(1, 7, e, WIDTH, FF, signed=True)
+        assert np.array_equal(got, want), e
+        assert np.array_equal(got, synth.expert_blob(1, 7, e, WIDTH, FF) | (want & np.uint32(0x80008000)))  # only the signs differ
+    assert np.array_equal(b.read(L.shared_blob), synth.expert_blob(1, 7, 0, WIDTH, FF, shared=True, signed=True))
+    scales = b.read(L.experts_blob, count=words)[blob_layout(WIDTH, FF)["gate_up_scales"] // 4:].view(np.float16)
+    assert 0.4 < (scales < 0).mean() < 0.6
+    L.free()
+
+
+def test_model_greedy_decode_is_not_degenerate(b):
+    """The seeded 48-layer model: 16 greedy tokens after a 4-token prompt are not all one token
+    (with the single-layer workload's positive scales they were, for any prompt)."""
+    from stratacuda_b200.engine import StrataEngine
+    from stratacuda_b200.synthetic import MODEL_GEOMETRY, MOE_MODES, DeviceStore
+    store = DeviceStore(b, dict(MODEL_GEOMETRY), seed=1)
+    try:
+        e = StrataEngine.create(store, b, MOE_MODES["fast"], graph=True)
+        outs = []
+        for prompt in ([151, 90210, 7, 151000], [5, 6, 7, 8]):
+            e.reset()
+            r = e.prefill(prompt, chunk_size=4)
+            toks = [r["token"]]
+            for _ in range(15):
+                r = e.step(r["token"])
+                toks.append(r["token"])
+            outs.append(toks)
+        e.dispose()
+    finally:
+        store.free()
+    print("greedy tokens:", outs)
+    assert all(len(set(t)) > 1 for t in outs) and outs[0] != outs[1]
