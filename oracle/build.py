@@ -20,7 +20,7 @@ HERE = pathlib.Path(__file__).resolve().parent
 ORACLE_SO = HERE / "libstrata_oracle.so"
 REF_DIR = HERE / "_ref"
 REF_SO = REF_DIR / "libstrata_ref.so"
-REFERENCE_ROOT = pathlib.Path(os.environ.get("STRATA_REFERENCE_ROOT", "/root/reference"))
+REFERENCE_ROOT = pathlib.Path(os.environ.get("STRATA_REFERENCE_ROOT", str(pathlib.Path(__file__).resolve().parents[2] / "reference")))
 REF_SOURCE = REFERENCE_ROOT / "kernels" / "strata.cu"
 FP_FLAGS = ["-ffp-contract=off", "-fno-fast-math"]
 

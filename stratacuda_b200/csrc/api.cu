@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -17,6 +18,8 @@
 #include "kernels.h"
 
 using namespace strata;
+
+constexpr int kFastSyncWords = 4 + kDecode1SyncWords;
 
 struct Buffer {
     void *ptr;
@@ -32,8 +35,10 @@ struct strata_ctx {
     uint64_t bytes_resident = 0;
     unsigned *err_dev = nullptr;   // device error word (kErr* bits)
     unsigned *err_host = nullptr;  // pinned mirror
-    unsigned *fast_sync = nullptr; // grid-arrival words of the fast fused kernel (self-resetting)
+    unsigned *fast_sync = nullptr; // grid-arrival words of the fast kernels (self-resetting): [0, 4) batch decode and
+                                   // medium layers, [4, 4 + kDecode1SyncWords) the one-token decode layer
     int *check_dev = nullptr;      // strata_validate_experts result
+    void *decode1_xchg = nullptr;  // the one-token decode layer's exchange words (zeroed at creation)
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
     uint64_t dispatches = 0, fused_calls = 0;
@@ -366,8 +371,10 @@ int strata_create(int device, strata_ctx **out) {
     if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&ctx->err_dev, sizeof(unsigned)) != cudaSuccess ||
         cudaHostAlloc(&ctx->err_host, sizeof(unsigned), cudaHostAllocDefault) != cudaSuccess ||
-        cudaMemset(ctx->err_dev, 0, sizeof(unsigned)) != cudaSuccess || cudaMalloc(&ctx->fast_sync, 4 * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(ctx->fast_sync, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
+        cudaMemset(ctx->err_dev, 0, sizeof(unsigned)) != cudaSuccess || cudaMalloc(&ctx->fast_sync, kFastSyncWords * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(ctx->fast_sync, 0, kFastSyncWords * sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&ctx->decode1_xchg, moe_decode1_xchg_bytes()) != cudaSuccess ||
+        cudaMemset(ctx->decode1_xchg, 0, moe_decode1_xchg_bytes()) != cudaSuccess) {
         strata_destroy(ctx);
         return STRATA_ERR_CUDA;
     }
@@ -408,6 +415,7 @@ int strata_destroy(strata_ctx *ctx) {
     if (ctx->err_dev) cudaFree(ctx->err_dev);
     if (ctx->fast_sync) cudaFree(ctx->fast_sync);
     if (ctx->check_dev) cudaFree(ctx->check_dev);
+    if (ctx->decode1_xchg) cudaFree(ctx->decode1_xchg);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -846,6 +854,12 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     // FAST: the fused decode kernel up to 8 tokens, the medium-batch layer up to 64, the
     // tensor-core prefill path above
     const bool fast = mode == STRATA_MOE_FAST && moe_fast_supported(tokens, l.width, l.ff, l.top_k, ctx->sms);
+    // one token: the one-arrival layer (STRATA_DECODE1=0 keeps the batch decode kernel, for comparisons)
+    static const bool decode1_on = [] {
+        const char *v = std::getenv("STRATA_DECODE1");
+        return !(v && v[0] == '0');
+    }();
+    const bool decode1 = fast && decode1_on && moe_decode1_supported(tokens, l.width, l.ff, l.experts, l.top_k, ctx->sms);
     const bool medium = mode == STRATA_MOE_FAST && !fast && moe_medium_supported(tokens, l.width, l.ff, l.experts, l.top_k, ctx->sms);
     const bool prefill = mode == STRATA_MOE_FAST && !fast && !medium && moe_prefill_supported(l.width, l.ff, l.experts, l.top_k);
     const long long bw = blob_words_of(l.width, l.ff);
@@ -910,9 +924,11 @@ int strata_moe_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_bu
     cudaError_t e;
     if (fast || medium) {
         if (ev[0]) CUDA_OR_FAIL(ctx, cudaEventRecord(ev[0], ctx->stream), "cudaEventRecord");
-        e = fast ? moe_forward_fast(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
-                                    ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev)
-                 : moe_forward_medium(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
+        e = fast && decode1 ? moe_forward_decode1(L, (const float *)ptr[5], (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->decode1_xchg,
+                                                  ctx->fast_sync + 4, ctx->sms, ctx->stream, ctx->err_dev)
+            : fast ? moe_forward_fast(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
+                                      ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev)
+                   : moe_forward_medium(L, (const float *)ptr[5], tokens, (float *)ptr[6], (int *)ptr[7], (float *)ptr[8], ctx->workspace,
                                       ctx->fast_sync, ctx->sms, ctx->stream, ctx->err_dev);
         if (ev[0]) {
             CUDA_OR_FAIL(ctx, cudaEventRecord(ev[1], ctx->stream), "cudaEventRecord");

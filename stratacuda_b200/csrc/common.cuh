@@ -49,7 +49,8 @@ static __device__ const unsigned long long c_exp2_tab[32] = {
     0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
 };
 
-__device__ __forceinline__ float ref_expf(float x) {
+// `tab`: the table's 32 words where the caller staged them (shared memory), else the global copy.
+__device__ __forceinline__ float ref_expf(float x, const unsigned long long *tab = nullptr) {
     const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
     const double shift = 0x1.8p+52;
     const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0;
@@ -66,7 +67,7 @@ __device__ __forceinline__ float ref_expf(float x) {
     const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
     kd = __dsub_rn(kd, shift);
     const double r = __dsub_rn(z, kd);
-    const unsigned long long t = __ldg(&c_exp2_tab[ki & 31ull]) + (ki << 47);
+    const unsigned long long t = (tab ? tab[ki & 31ull] : __ldg(&c_exp2_tab[ki & 31ull])) + (ki << 47);
     const double s = __longlong_as_double((long long)t);
     const double p = __dadd_rn(__dmul_rn(c0, r), c1);
     const double r2 = __dmul_rn(r, r);
@@ -84,8 +85,10 @@ __device__ __forceinline__ float ref_expf(float x) {
 }
 
 // kernels/strata.cu:7-8
-__device__ __forceinline__ float ref_sigmoid(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, ref_expf(-x))); }
-__device__ __forceinline__ float ref_silu(float x) { return __fmul_rn(x, ref_sigmoid(x)); }
+__device__ __forceinline__ float ref_sigmoid(float x, const unsigned long long *tab = nullptr) {
+    return __fdiv_rn(1.0f, __fadd_rn(1.0f, ref_expf(-x, tab)));
+}
+__device__ __forceinline__ float ref_silu(float x, const unsigned long long *tab = nullptr) { return __fmul_rn(x, ref_sigmoid(x, tab)); }
 
 // Paired F32 arithmetic (sm_100): each element of the pair is rounded to nearest exactly as
 // the scalar __fmul_rn / __fadd_rn would round it (measured bit for bit). The compiler turns a

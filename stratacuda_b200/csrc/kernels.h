@@ -77,14 +77,28 @@ int moe_fast_pdl_state();  // 1: launched with programmatic dependent launch, 0:
 cudaError_t moe_forward_fast(const MoeLayerDev &L, const float *x, int tokens, float *y, int *ids, float *weights, void *scratch,
                              unsigned *sync, int grid, cudaStream_t s, unsigned *err);
 
+// One-token decode layer (csrc/moe_decode1.cu): one cooperative launch of `grid` CTAs. `xchg`
+// (moe_decode1_xchg_bytes, zeroed once) and `sync` (kDecode1SyncWords words, zeroed once) belong
+// to this kernel alone: they carry its tagged cross-CTA exchange and launch count between calls.
+constexpr int kDecode1SyncWords = 2;
+bool moe_decode1_supported(int tokens, int width, int ff, int experts, int topK, int grid);
+size_t moe_decode1_xchg_bytes();
+cudaError_t moe_forward_decode1(const MoeLayerDev &L, const float *x, float *y, int *ids, float *weights, void *xchg, unsigned *sync,
+                                int grid, cudaStream_t s, unsigned *err);
+
 // TMA maps of the medium-batch layer for a layer's routed experts [0] and shared expert [1],
 // cached by blob address (csrc/moe_fast.cu), all boxes of 128 rows: gate/up codes (128 bytes,
 // 128-byte swizzle), gate/up scales (8 groups) and down codes (full rows; 128-byte swizzle for
 // 128-byte rows).
 struct MoeMaps {
     CUtensorMap gu[2], gs[2], dc[2];
+    CUtensorMap dn16[2];  // down codes, boxes of 16 full rows (the one-token decode layer)
+    CUtensorMap gu16r[2]; // gate/up codes, boxes of 16 full rows in one request (chunk-major, swizzled)
+    CUtensorMap dn64[2];  // down codes, boxes of 64 full rows (8 KB, contiguous)
 };
 bool moe_tensor_maps(const MoeLayerDev &L, MoeMaps *maps);
+// the same plus the gate/up code maps in boxes of 16 rows ([0] routed, [1] shared)
+bool moe_decode_maps(const MoeLayerDev &L, CUtensorMap *gu16, MoeMaps *maps);
 
 // Medium-batch layer (csrc/moe_medium.cu), 9 .. 64 tokens: the exact router kernels, then one
 // cooperative launch of integer tensor-core units on the 2-bit codes (y within 1e-5 relative

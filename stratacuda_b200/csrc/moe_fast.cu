@@ -894,6 +894,21 @@ bool map3d(CUtensorMap *m, const void *base, unsigned long long d0, unsigned lon
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Gate/up codes as {128-byte chunk, rows, chunks, experts} (strides: row H/4, chunk 128, blob):
+// one box {128, 16, CH, 1} copies 16 whole rows in one request and lays them out chunk-major,
+// [chunk][row][128 B] with the 128-byte swizzle, as CH separate {128, 16} boxes would. Measured
+// on B200 (all SMs streaming 8 KB tiles): 60 GB/s per SM, against 24 GB/s for four {128, 16}
+// boxes of the same rows.
+bool map_gu_rows(CUtensorMap *m, const void *base, unsigned long long H, unsigned long long F, unsigned long long ne,
+                 unsigned long long blob_bytes) {
+    auto fn = encoder();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {128, 2 * F, H / 512, ne}, strides[3] = {H / 4, 128, blob_bytes};
+    cuuint32_t box[4] = {128, 16, (cuuint32_t)(H / 512), 1}, es[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Encoded maps of the last layers used, keyed by their blob addresses.
 struct MapSet {
     const void *blobs, *shared;
@@ -940,6 +955,14 @@ bool layer_maps(const MoeLayerDev &L, CUtensorMap *gu2, MoeMaps *all) {
         if (!map3d(&m.all.dc[i], base + 2 * F * H / 4, F / 4, H, ne, F / 4, bb, F / 4, 128,
                    F / 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return false;
+        if (!map_gu_rows(&m.all.gu16r[i], base, H, F, ne, bb)) return false;
+        if (!map3d(&m.all.dn64[i], base + 2 * F * H / 4, F / 4, H, ne, F / 4, bb, F / 4, 64,
+                   F / 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return false;
+        // the same in boxes of 16 rows (one-token decode: a CTA's 16 output rows of one expert)
+        if (!map3d(&m.all.dn16[i], base + 2 * F * H / 4, F / 4, H, ne, F / 4, bb, F / 4, 16,
+                   F / 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return false;
     }
     g_maps[g_map_next] = m;
     g_map_next = (g_map_next + 1) % 64;
@@ -953,6 +976,8 @@ bool moe_tensor_maps(const MoeLayerDev &L, MoeMaps *maps) {
     CUtensorMap gu[2];
     return layer_maps(L, gu, maps);
 }
+
+bool moe_decode_maps(const MoeLayerDev &L, CUtensorMap *gu16, MoeMaps *maps) { return layer_maps(L, gu16, maps); }
 
 namespace {
 

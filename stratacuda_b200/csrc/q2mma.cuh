@@ -43,6 +43,13 @@ __device__ __forceinline__ void tma_3d(void *dst, const CUtensorMap *map, int x,
         "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
 }
+__device__ __forceinline__ void tma_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w, unsigned long long *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+        : "memory");
+}
 // L2 prefetches by the bulk-copy engine: a contiguous range (16-byte aligned, a multiple of 16
 // bytes), or one box of a tensor map.
 __device__ __forceinline__ void prefetch_l2_bulk(const void *src, unsigned bytes) {

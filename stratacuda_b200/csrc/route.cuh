@@ -8,8 +8,9 @@ namespace strata {
 // 64-lane sum, multiply by 1/sum), then k rounds of lane-strided argmax with the lower ID
 // winning ties, then weights = sel_k / max(sum_k sel_k, 2^-14). Thread t owns virtual lanes
 // t (experts t + 64m) and t + 32 (experts t + 32 + 64m), m < 8. `sel` is 32 floats of
-// scratch for this warp.
-__device__ __forceinline__ void route_warp(const float *logits, int experts, int topK, int *ids, float *weights, float *sel) {
+// scratch for this warp; `exp_tab` (optional) the expf table staged in shared memory.
+__device__ __forceinline__ void route_warp(const float *logits, int experts, int topK, int *ids, float *weights, float *sel,
+                                           const unsigned long long *exp_tab = nullptr) {
     // `logits` must hold 512 readable floats (entries past `experts` may be anything): every
     // lane evaluates all 16 of its slots without branches and masks the unused ones, which
     // lets the 16 exp evaluations interleave. Masked slots contribute exactly nothing:
@@ -31,7 +32,7 @@ __device__ __forceinline__ void route_warp(const float *logits, int experts, int
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
         const int ea = t + 64 * m, eb = ea + 32;
-        const float xa = ref_expf(__fsub_rn(logits[ea], mx)), xb = ref_expf(__fsub_rn(logits[eb], mx));
+        const float xa = ref_expf(__fsub_rn(logits[ea], mx), exp_tab), xb = ref_expf(__fsub_rn(logits[eb], mx), exp_tab);
         pa[m] = ea < experts ? xa : 0.0f;
         pb[m] = eb < experts ? xb : 0.0f;
         sa = __fadd_rn(sa, pa[m]);
@@ -108,7 +109,8 @@ __device__ __forceinline__ void route_warp(const float *logits, int experts, int
 // `lg` holds the token's logits (512 floats; entries past `experts` are ignored) and is
 // overwritten. `red` holds W floats, `cand` 8*topK keys (16-byte aligned), `nzc` one int
 // that the caller zeroes before the call; ids/sel/weights receive topK entries. Group
-// synchronisation uses named barrier `bar_id` (W > 1).
+// synchronisation uses named barrier `bar_id` (W > 1). `exp_tab` (optional): the expf table
+// staged in shared memory by the caller.
 template <int W>
 __device__ __forceinline__ void group_sync(int bar_id) {
     if (W == 1) __syncwarp();
@@ -144,7 +146,7 @@ static __device__ __forceinline__ ulonglong2 warp_sort64_desc(ulonglong2 k, int 
 
 template <int W>
 __device__ __forceinline__ void route_group(float *lg, int experts, int topK, float *red, unsigned long long *cand, int *nzc,
-                                            int *ids, float *sel, float *weights, int bar_id) {
+                                            int *ids, float *sel, float *weights, int bar_id, const unsigned long long *exp_tab = nullptr) {
     constexpr int T = 32 * W, NPT = 512 / T;
     const int i = threadIdx.x % T, lane = threadIdx.x & 31, wg = i >> 5;
     float v[NPT];
@@ -167,7 +169,7 @@ __device__ __forceinline__ void route_group(float *lg, int experts, int topK, fl
 #pragma unroll
     for (int m = 0; m < NPT; ++m) {
         const int e = i + T * m;
-        const float ex = ref_expf(__fsub_rn(v[m], mx));
+        const float ex = ref_expf(__fsub_rn(v[m], mx), exp_tab);
         v[m] = e < experts ? ex : 0.0f;
         lg[e] = v[m];
     }

@@ -23,6 +23,7 @@ Sources of truth, per fixture:
 from __future__ import annotations
 
 import math
+import os
 import pathlib
 import subprocess
 import sys
@@ -37,7 +38,7 @@ from oracle.oracle import Oracle, grid, moe_layer_wasm_path  # noqa: E402
 from stratacuda_b200 import synth  # noqa: E402
 
 OUT = pathlib.Path(__file__).resolve().parent
-REFERENCE = pathlib.Path("/root/reference")
+REFERENCE = pathlib.Path(os.environ.get("STRATA_REFERENCE_ROOT", str(ROOT.parent / "reference")))  # the reference tree (read-only)
 
 
 def half_to_float(h: int) -> float:
