@@ -69,9 +69,10 @@ struct Params {
     float *y;
     int *ids;
     float *weights;
-    unsigned long long *lgx;   // [experts + 1] tagged router logits, the shared-gate logit last
+    unsigned long long *lgx;   // [513] tagged router logits (the shared-gate logit at [experts]), then [kPresence]
+                               // presence words: one per CTA, stored as soon as it holds the tag
     unsigned long long *part;  // [kMaxSlots - 1][H] tagged down rows of the routed slots
-    unsigned *sync;            // [0] launch count (tag = count + 1), [1] exits
+    unsigned *sync;            // [0] launch count (tag = count + 1)
     unsigned *err;
     unsigned long long spin_limit;
     CUtensorMap tm_gu[2];  // gate/up codes {128, 2F rows, H/512 chunks, experts}, box {128, 16, H/512, 1}; [0] routed, [1] shared
@@ -149,6 +150,11 @@ __device__ __forceinline__ unsigned cluster_id() {
 }
 __device__ __forceinline__ void cluster_sync_all() {  // every thread of every CTA of the cluster
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Execution-only cluster barrier: every thread has arrived, nothing ordered (the peers' reads of
+// this CTA's shared memory have completed: their values were used before the arrival).
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 __device__ __forceinline__ float ld_peer(const float *local, unsigned rank) {  // the same variable in CTA `rank`'s shared memory
     unsigned remote;
@@ -258,6 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
         for (int i = tid; i < kH; i += kThreads) S.u.x[i] = __ldg(P.x + i);
     }
     __syncthreads();
+    if (tid == 0) st_tagged(&P.lgx[513 + blockIdx.x], 0.0f, S.tag);  // this CTA holds the tag
     {  // largest |x| (NaN ignored, as fmaxf; order-free)
         float mx = 0.0f;
         for (int i = tid; i < kH; i += kThreads) mx = fmaxf(mx, fabsf(S.u.x[i]));
@@ -396,6 +403,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
             if (e < 512) lg[e] = e < E ? v : 0.0f;
         }
         if (tid == 0) S.nzc = 0;
+        if (cl == 0 && j == 0)  // every CTA of the grid holds this launch's tag (see the exit)
+            for (int b = tid; b < G; b += kThreads) {
+                float v;
+                if (!poll_tagged(&P.lgx[513 + b], S.tag, P.spin_limit, v)) atomicOr(&S.abort_flag, 1);
+            }
         __syncthreads();
         if (!S.abort_flag) {
             route_group<8>(S.u.r.lg, E, K, S.u.r.red, S.u.r.cand, &S.nzc, S.ids, S.u.r.sel, S.wts, 1, S.exp_tab);
@@ -413,13 +425,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
                     }
                 }
                 S.n_slots = n;
-                S.sgw = ref_sigmoid(S.sg_raw, S.exp_tab);
-                if (cl >= 1 && cl < n) {  // this cluster's slot: its tiles (stages held router rows) and down scales
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    for (int w = 0; w < kWarps; ++w) issue_tile(w, cl);
-                    issue_down_scales(cl);
-                }
             }
+            __syncthreads();
+            // this cluster's slot: lane 0 of warp w requests tile w (its stage held a router row,
+            // read through the generic proxy), the last warp also the down scales (one thread
+            // issuing all of them took 1.5 us)
+            if (cl >= 1 && cl < S.n_slots && lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_tile(warp, cl);
+                if (warp == kWarps - 1) issue_down_scales(cl);
+            }
+            if (tid == 32) S.sgw = ref_sigmoid(S.sg_raw, S.exp_tab);
             if (cl == 0 && j == 0)
                 for (int k = tid; k < K; k += kThreads) {
                     P.ids[k] = S.ids[k];
@@ -437,6 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
     // ------------------------------------------------------------------ phase 4: down rows of the slot
     if (slot_cluster) cluster_sync_all();  // A: every CTA of the cluster has its 64 hidden values in hloc
     if (active) {
+        // the slot's hidden values from the cluster's CTAs (two loads per thread; every warp reading
+        // all 512 for itself from the peers was 6 us slower), then warp 0 forms their digits
         for (int i = tid; i < kF; i += kThreads) S.u.d.h[i] = ld_peer(&S.hloc[i % 64], (unsigned)(i / 64));
         __syncthreads();
         if (warp == 0) {  // digits of the slot's hidden values: lane = block (group lane / 4, q) of 16
@@ -516,22 +534,42 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
         __syncthreads();
         // cluster 0: y rows DROWS j .. in the reference's combine order (kernels/strata.cu:360-365)
         if (cl == 0 && !S.abort_flag) {
+            // every routed slot's word of this row requested at once, then re-read only while some
+            // lack the tag (one L2 round trip per pass instead of one per slot)
             const int row = tid;  // kThreads == DROWS
-            float v = __fmul_rn(S.res[row], S.sgw);
-            for (int k = 0; k < K; ++k) {
-                const int s = S.slot_of_k[k];
-                if (s <= 0) continue;
-                float p = 0.0f;
-                if (!poll_tagged(P.part + (long long)(s - 1) * kH + DROWS * j + row, S.tag, P.spin_limit, p)) {
+            const unsigned long long *src = P.part + DROWS * j + row;
+            float pv[kMaxSlots - 1];
+            unsigned missing = 0;
+            for (int s = 1; s < S.n_slots; ++s) missing |= 1u << s;
+            for (unsigned long long i = 0; missing; ++i) {
+                unsigned long long w[kMaxSlots - 1];
+#pragma unroll
+                for (int s = 1; s < kMaxSlots; ++s)
+                    if (missing >> s & 1u) w[s - 1] = ld_relaxed64(src + (long long)(s - 1) * kH);
+#pragma unroll
+                for (int s = 1; s < kMaxSlots; ++s)
+                    if ((missing >> s & 1u) && (unsigned)(w[s - 1] >> 32) == S.tag) {
+                        pv[s - 1] = __uint_as_float((unsigned)w[s - 1]);
+                        missing &= ~(1u << s);
+                    }
+                if (!missing) break;
+                if (i > P.spin_limit) {
                     atomicOr(&S.abort_flag, 1);
                     break;
                 }
-                v = __fadd_rn(v, __fmul_rn(p, S.wts[k]));
+                __nanosleep(64);
             }
-            P.y[DROWS * j + row] = v;
+            if (!missing) {  // kernels/strata.cu:360-365
+                float v = __fmul_rn(S.res[row], S.sgw);
+                for (int k = 0; k < K; ++k) {
+                    const int s = S.slot_of_k[k];
+                    if (s > 0) v = __fadd_rn(v, __fmul_rn(pv[s - 1], S.wts[k]));
+                }
+                P.y[DROWS * j + row] = v;
+            }
         }
     }
-    if (slot_cluster) cluster_sync_all();  // B: no CTA leaves while a peer may still read its hloc
+    if (slot_cluster) cluster_sync_relaxed();  // B: no CTA leaves while a peer may still read its hloc
 
     // ------------------------------------------------------------------ exit
     __syncthreads();
@@ -547,12 +585,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
             if (a >> 14 & 1u) wait_bar(&S.bar_x);
             raise_error(P.err, kErrWaitTimeout);
         }
-        __threadfence();
-        const unsigned prev = atomicAdd(&P.sync[1], 1u);
-        if (prev == (unsigned)G - 1) {  // last CTA out: the launch count moves on (the next launch's tag)
-            P.sync[0] = S.tag;
-            P.sync[1] = 0;
-        }
+        // The launch count moves on (the next launch's tag) once no CTA can still need the old
+        // count: CTA 0 of cluster 0 has seen every CTA's presence word carry this launch's tag.
+        // The next launch reads the count after griddepcontrol.wait, i.e. after every CTA of this
+        // one is gone. Should the presence wait have run out, a late CTA of this launch may read
+        // the new count and store words with tag + 1: the count then skips that tag.
+        if (cl == 0 && j == 0) P.sync[0] = S.abort_flag ? S.tag + 1u : S.tag;
     }
 }
 
@@ -567,7 +605,8 @@ bool moe_decode1_supported(int tokens, int width, int ff, int experts, int topK,
            experts + 1 <= (d1::kClusters - 1) * d1::kCluster * d1::kRowWarps && grid >= d1::kClusters * d1::kCluster;
 }
 
-static size_t lgx_words() { return (513 + 31) & ~size_t(31); }
+constexpr int kPresence = d1::kClusters * d1::kCluster;  // one presence word per CTA
+static size_t lgx_words() { return (513 + kPresence + 31) & ~size_t(31); }
 size_t moe_decode1_xchg_bytes() { return sizeof(unsigned long long) * (lgx_words() + (size_t)(d1::kMaxSlots - 1) * d1::kH); }
 
 namespace {
