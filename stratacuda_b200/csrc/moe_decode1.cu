@@ -61,6 +61,7 @@ struct Geo {
     static_assert(TILE == kH * 4, "a router row fills one gate/up stage");
     static_assert(DROWS == 4 * 64, "the CTA's down rows are four 64-row boxes");
     static_assert(DROWS == kThreads, "the collector takes one row per thread");
+    static_assert(NG * 4 == 128 && kThreads == 256, "the x digits' 128 blocks on the upper half of the threads");
 };
 
 struct Params {
@@ -287,8 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
             if (lane == 0) st_tagged(&P.lgx[r], r < E && L.bias ? __fadd_rn(v, L.bias[r]) : v, S.tag);
         }
     }
-    if (slot_cluster)  // x digits: block b = (group, q) of 16 elements, one per thread
-        for (int b = tid; b < NG * 4; b += kThreads) {
+    if (slot_cluster)  // x digits: block b = (group, q) of 16 elements, one per thread of warps 4..7 (0.. compute router rows)
+        for (int b = tid ^ 128; b < NG * 4; b += kThreads) {
             const int grp = b >> 2, qq = b & 3;
             const int k = scale_exp(__uint_as_float(S.xmax));
             const float mul = pow2f(k);
@@ -411,7 +412,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
         __syncthreads();
         if (!S.abort_flag) {
             route_group<8>(S.u.r.lg, E, K, S.u.r.red, S.u.r.cand, &S.nzc, S.ids, S.u.r.sel, S.wts, 1, S.exp_tab);
-            __syncthreads();
+            // (route_group ends with a barrier of all eight warps: every thread sees the ids.)
+            // This cluster's slot is the cl-th valid selection: lane 0 of every warp finds it and
+            // requests the warp's tile at once (its stage held a router row, read through the
+            // generic proxy); the last warp also the down scales.
+            if (cl >= 1 && lane == 0) {
+                int n = 0, e_cl = -1;
+                for (int k = 0; k < K; ++k) {
+                    const int e = S.ids[k];
+                    if (e >= 0 && e < E && ++n == cl) e_cl = e;
+                }
+                if (e_cl >= 0) {
+                    S.slot_expert[cl] = (short)e_cl;  // the same value from every warp
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue_tile(warp, cl);
+                    if (warp == kWarps - 1) issue_down_scales(cl);
+                }
+            }
             if (tid == 0) {  // slot s >= 1: the s-th valid selection (ids of one token are distinct)
                 int n = 1;
                 for (int k = 0; k < K; ++k) {
@@ -425,15 +442,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_consta
                     }
                 }
                 S.n_slots = n;
-            }
-            __syncthreads();
-            // this cluster's slot: lane 0 of warp w requests tile w (its stage held a router row,
-            // read through the generic proxy), the last warp also the down scales (one thread
-            // issuing all of them took 1.5 us)
-            if (cl >= 1 && cl < S.n_slots && lane == 0) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                issue_tile(warp, cl);
-                if (warp == kWarps - 1) issue_down_scales(cl);
             }
             if (tid == 32) S.sgw = ref_sigmoid(S.sg_raw, S.exp_tab);
             if (cl == 0 && j == 0)
