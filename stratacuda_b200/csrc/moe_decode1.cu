@@ -165,7 +165,22 @@ __device__ __forceinline__ float ld_peer(const float *local, unsigned rank) {  /
     return v;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_constant__ Params P) {
+__device__ __forceinline__ unsigned cluster_size() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+
+// The cluster shape is part of the kernel (not of a launch attribute), so that every launch of
+// it, including a replay by a profiler, has 8-CTA clusters: the distributed-shared-memory reads
+// name ranks 0..7.
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) k_moe_decode1(const __grid_constant__ Params P) {
+    // a launch of another shape would make the peers' ranks, the slots and the router rows
+    // wrong: report it and touch nothing
+    if (cluster_size() != (unsigned)kCluster || gridDim.x != (unsigned)(kClusters * kCluster) || blockDim.x != (unsigned)kThreads) {
+        if (threadIdx.x == 0) raise_error(P.err, kErrIndex);
+        return;
+    }
     using G1 = Geo;
     constexpr int NG = G1::NG, CH = G1::CH, DG = G1::DG, DROWS = G1::DROWS;
     extern __shared__ unsigned char smem_raw[];
@@ -634,18 +649,14 @@ cudaError_t launch_d1(const d1::Params &p, cudaStream_t s) {
     cfg.blockDim = dim3(q2::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[3];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = d1::kCluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    attr[2].id = cudaLaunchAttributeCooperative;  // the grid-wide exchange needs every CTA resident
-    attr[2].val.cooperative = 1;
+    cudaLaunchAttribute attr[2];  // the 8-CTA clusters come from the kernel's __cluster_dims__
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;  // the grid-wide exchange needs every CTA resident
+    attr[1].val.cooperative = 1;
     cfg.attrs = attr;
     if (g_d1_coop != 0) {
-        cfg.numAttrs = 3;
+        cfg.numAttrs = 2;
         const cudaError_t e = cudaLaunchKernelEx(&cfg, d1::k_moe_decode1, p);
         if (e == cudaSuccess || g_d1_coop == 1) {
             g_d1_coop = e == cudaSuccess ? 1 : g_d1_coop;
@@ -654,7 +665,7 @@ cudaError_t launch_d1(const d1::Params &p, cudaStream_t s) {
         cudaGetLastError();  // refused with clusters: the grid (one CTA per SM, under the co-resident
         g_d1_coop = 0;       // cluster count) is resident without the guarantee
     }
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, d1::k_moe_decode1, p);
 }
 }  // namespace
