@@ -303,7 +303,8 @@ def decode_block(b, layers, B, K, W, mode, world, local):
     st.free()
     hbm, kind = peaks()
     step_s = ms / 1000.0 / K
-    kernel = ("k_moe_fast (one persistent launch per step)" if mode == LL.MOE_FAST and B <= 8 else
+    kernel = ("k_moe_decode1 (one launch of 8-CTA clusters per step)" if mode == LL.MOE_FAST and B == 1 else
+              "k_moe_fast (one persistent launch per step)" if mode == LL.MOE_FAST and B <= 8 else
               "k_moe_medium (after the exact router kernels: 4 launches per step)" if mode == LL.MOE_FAST else "fused exact layer")
     return {"batch": B, "tokens_per_s": B * K * world / (ms / 1000.0), "ms_per_step": ms / K, "steps": K, "warmup": W,
             "roofline": {"bound": "hbm", "achieved": alg / step_s / 1e9, "peak": hbm, "unit": "GB/s", "frac": alg / step_s / 1e9 / hbm,
@@ -364,7 +365,8 @@ def run_gpu_arm(args, world, rank, local):
     else:
         roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
                     "peak_kind": peak_kind,
-                    "kernel": ("k_moe_fast (one persistent launch per step)" if launches == 1
+                    "kernel": ("k_moe_decode1 (one launch of 8-CTA clusters per step)" if launches == 1 and B == 1
+                               else "k_moe_fast (one persistent launch per step)" if launches == 1
                                else "k_moe_medium (after the exact router kernels: 4 launches per step)" if medium
                                else "fused exact MoE layer (6 launches per step)"),
                     "algorithmic_bytes_per_step": alg_bytes}
