@@ -136,3 +136,43 @@ def test_ep_loopback_ranks(R, T):
     ids = run_loopback(R, T, seed=6, zipf=1.1)
     owners = np.bincount((ids // (512 // R)).reshape(-1), minlength=R)
     assert (owners > 0).sum() >= min(R, 2)  # rows really cross between ranks
+
+
+@pytest.mark.timeout(300)
+def test_ep_loopback_peer_never_arrives():
+    """Failure detection without a GPU fault: rank 1 of a two-rank loopback group never calls
+    the layer. Rank 0's bounded host wait at the first exchange runs out (1 s), its forward
+    fails naming the cause, later expert-parallel calls fail at once, and the same context
+    still runs the single-GPU layer with the same routing as an untouched context."""
+    import time
+
+    from stratacuda_b200 import _lib as L
+    from stratacuda_b200.backend import CudaBackend
+    from stratacuda_b200.ep import EpMoeLayer, ep_init_loopback
+    from stratacuda_b200.moe import MoeLayer, synth_activations
+    H, K, T = 2048, 10, 4
+    bs = [CudaBackend(0) for _ in range(2)]
+    try:
+        ep_init_loopback(bs, timeout_ms=1000)
+        layer = EpMoeLayer.synthesize(bs[0], 0, 2, seed=3, layer=0)
+        x = synth_activations(bs[0], 92, T, H)
+        y, ids, w = bs[0].alloc(T * H), bs[0].alloc(T * K, "i32"), bs[0].alloc(T * K)
+        t0 = time.monotonic()
+        with pytest.raises(Exception, match="did not reach the exchange"):
+            layer.forward(x, T, y, ids, w)
+        assert time.monotonic() - t0 < 30
+        with pytest.raises(Exception):
+            layer.forward(x, T, y, ids, w)
+        got = []
+        for b in bs:
+            full = MoeLayer.synthesize(b, seed=3, layer=0)
+            xb = synth_activations(b, 92, T, H)
+            yb, idb, wb = b.alloc(T * H), b.alloc(T * K, "i32"), b.alloc(T * K)
+            full.forward(xb, T, yb, idb, wb, mode=L.MOE_EXACT)
+            got.append((b.read(yb), b.read(idb), b.read(wb)))
+        assert np.array_equal(got[0][1], got[1][1])
+        assert np.array_equal(bits(got[0][2]), bits(got[1][2]))
+        assert np.array_equal(bits(got[0][0]), bits(got[1][0]))
+    finally:
+        for b in bs:
+            b.dispose()
