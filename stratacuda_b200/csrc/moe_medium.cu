@@ -30,14 +30,16 @@
 //   C. After a second arrival every CTA sums a slice of y from the partial rows in a fixed
 //      order (the shared expert, then the routed pairs in selection order): the same bits
 //      every run.
-// Whole experts per unit keep every copy a TMA box of full rows (splitting an expert by hidden
-// columns left 16 bytes of each 128-byte down row per unit: 2,048 small requests per unit,
-// measured 307 us per 64-token layer). The copies run through one CTA-wide ring of NST
-// stages: a step is 128 rows (the 8 warps' 16-row slices side by side), one TMA box of codes
-// (gate/up: 128 bytes of columns, 128-byte swizzle; down: full rows) plus one copy of their
-// scales; thread 0 produces, every warp consumes its slice and frees the stage (per-warp boxes
-// of 16 rows capped the copies near 2 TB/s). Every wait is bounded: past the limit the kernel
-// records kErrWaitTimeout and leaves.
+// Whole experts per unit keep every copy a TMA box of full rows, and every box one contiguous
+// range of the blob: a step is one warp's work, either a gate/up tile (16 interleaved rows,
+// full width: one 4D box laid out chunk-major, 128-byte swizzle) or a down block (64 full
+// rows), plus one bulk copy of the step's scales. Measured on B200 with all SMs streaming,
+// boxes of contiguous rows moved 60 GB/s per SM, boxes of 128-byte pieces of strided rows
+// (a 128-row x 128-byte gate/up box, the earlier step of this kernel) 18-24 GB/s per SM.
+// Step c of the CTA belongs to warp c % 8 and lands in stage c % NST of one shared ring; the
+// warp that consumed step c issues step c + NST into the same stage at once (the stage has no
+// other reader), so no warp waits for another to refill and no copy waits behind compute.
+// Every wait is bounded: past the limit the kernel records kErrWaitTimeout and leaves.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -73,21 +75,26 @@ struct Rec {
     static_assert(BYTES % 16 == 0 && STRIDE % 128 == 96, "record layout");
 };
 
-// A step is 128 rows: the 8 warps' 16-row tiles side by side, one TMA box of codes and one
-// copy of their scales per step.
+// A step: one warp's gate/up tile (16 rows x H/4 bytes) or down block (64 rows x F/4 bytes)
+// with its scales; both are STAGE bytes of codes at the supported shapes.
 template <int H, int F>
 struct MGeo {
     static constexpr int NG = H / 64;                // gate/up scale groups per row
     static constexpr int NJ = F / 64;                // down scale groups per row
     static constexpr int CPT = NG / 8;               // gate/up column chunks (128 bytes) per row
-    static constexpr int GU_STEPS = (2 * F / 128) * CPT;  // per unit: 128-row blocks x column chunks
-    static constexpr int DN_STEPS = H / 128;         // per unit: 128-row blocks of full down rows
+    static constexpr int GU_STEPS = 2 * F / 16;      // per unit: 16-row gate/up tiles
+    static constexpr int DN_STEPS = H / 64;          // per unit: 64-row down blocks
     static constexpr int STEPS = GU_STEPS + DN_STEPS;
     static constexpr int DROW = F / 4;               // bytes of a down row
-    static constexpr int STAGE = 128 * DROW > 16384 ? 128 * DROW : 16384;  // codes of a step (1024-aligned)
-    static constexpr int SSTAGE = 128 * (NJ > 8 ? NJ : 8) * 2;            // scales of a step
-    static constexpr int NST = F == 512 ? 6 : 4;     // stages (shared-memory budget)
-    static_assert(NG % 8 == 0 && H % 128 == 0 && STAGE % 1024 == 0 && SSTAGE % 128 == 0, "geometry");
+    static constexpr int GU_BYTES = 16 * (H / 4), DN_BYTES = 64 * DROW;
+    static constexpr int GU_SBYTES = 16 * NG * 2, DN_SBYTES = 64 * NJ * 2;
+    static constexpr int STAGE = GU_BYTES > DN_BYTES ? GU_BYTES : DN_BYTES;          // codes of a step (1024-aligned)
+    static constexpr int SSTAGE = GU_SBYTES > DN_SBYTES ? GU_SBYTES : DN_SBYTES;     // scales of a step
+    static constexpr int NST = F == 512 ? 12 : 8;    // stages (shared-memory budget)
+    static_assert(NG % 8 == 0 && H % 512 == 0 && STAGE % 1024 == 0 && SSTAGE % 128 == 0, "geometry");
+    // steps go round-robin to the warps in every phase of a unit, and a stage's use v - 2 was
+    // consumed by the warp that consumes its use v (the parity waits below rely on it)
+    static_assert(GU_STEPS % kWarps == 0 && DN_STEPS % kWarps == 0 && (2 * NST) % kWarps == 0, "step ownership");
 };
 
 struct Params {
@@ -126,6 +133,7 @@ struct Smem {
     float uw[2][kMaxTokens];  // unit token slot -> weight
     unsigned xmax;
     unsigned long long full[G::NST], empty[G::NST];
+    int issued[G::NST];  // uses of each stage issued so far
     unsigned long long bar_x;
     int abort_flag;
 };
@@ -242,20 +250,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
     const int G = gridDim.x, cta = blockIdx.x;
     const int B = P.tokens, K = L.topK, E = L.experts, P2 = B * K, SG = (B + kSharedGroup - 1) / kSharedGroup;
-    const long long d_scales_b = 3LL * F * H / 4 + 2LL * F * (H / 64) * 2;
+    const long long gu_scales_b = 3LL * F * H / 4, d_scales_b = gu_scales_b + 2LL * F * (H / 64) * 2;
 
     if (tid == 0) {
         for (int s = 0; s < NST; ++s) {
             mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], kWarps);
+            mbar_init(&S.empty[s], 1);
+            S.issued[s] = 0;
         }
         mbar_init(&S.bar_x, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.abort_flag = 0;
         for (int i = 0; i < 2; ++i) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.gu[i])) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.gs[i])) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.dc[i])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.gu16r[i])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.dn64[i])) : "memory");
         }
     }
     for (int e = tid; e < E; e += kThreads) S.run[e] = 0;
@@ -349,13 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     const int NU = S.gstart[E];
     const int n_units = cta < NU ? (NU - 1 - cta) / G + 1 : 0;
 
-    // ------------------------------------------------------------------ copy pipeline (CTA-wide ring)
-    // Step c of this CTA: unit c / STEPS; within it the gate/up steps (128-row block, column
-    // chunk) first, then the down steps. Thread 0 produces (one TMA box of codes + one copy of
-    // scales per step); every warp consumes every step (its 16-row slice) and arrives on the
-    // stage's empty barrier.
+    // ------------------------------------------------------------------ copy pipeline
+    // Step c of this CTA: unit c / STEPS; within it the gate/up tiles first, then the down
+    // blocks. Warp c % 8 consumes it from stage c % NST and then issues step c + NST there.
     const int total = n_units * STEPS;
-    int produced = 0, done = 0;    // produced: thread 0's count; done: steps consumed (every warp)
     bool stalled = false;          // this warp saw a wait time out
     int memo_gi = -1, memo_e = 0;  // the last routed group looked up
     // unit ui -> token group gi, map m (1: shared expert), expert e, group index tg within it
@@ -394,43 +399,41 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         stalled = true;
         atomicOr(&S.abort_flag, 1);
     };
-    auto produce = [&]() {  // thread 0: the next step into its stage, once every warp has freed it
-        const int c = produced, st = c % NST;
-        if (c >= NST && !wait_bar(&S.empty[st], ((c / NST) - 1) & 1)) {
-            S.abort_flag = 1;
-            return false;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the stage was read through the generic proxy
-        const int ui = c / STEPS, idx = c % STEPS;
+    auto produce = [&](int c) {  // one thread: step c into its stage, whose last use has been consumed
+        const int st = c % NST, ui = c / STEPS, idx = c % STEPS;
         int gi, m, e, tg;
         unit_of(ui, gi, m, e, tg);
-        if (idx < GU_STEPS) {
-            const int blk = idx / CPT, sub = idx % CPT;
-            mbar_expect(&S.full[st], 16384 + 128 * 16);
-            tma_3d(S.codes[st], &P.maps.gu[m], 128 * sub, 128 * blk, e, &S.full[st]);
-            tma_3d(S.scl[st], &P.maps.gs[m], 16 * sub, 128 * blk, e, &S.full[st]);  // [128 rows][8 groups]
-        } else {
-            const int row0 = 128 * (idx - GU_STEPS);
-            mbar_expect(&S.full[st], 128 * Gm::DROW + 128 * NJ * 2);
-            tma_3d(S.codes[st], &P.maps.dc[m], 0, row0, e, &S.full[st]);
-            bulk_copy(S.scl[st], blob_of(m, e) + d_scales_b + (long long)row0 * NJ * 2, 128 * NJ * 2, &S.full[st]);  // [128 rows][NJ]
+        if (idx < GU_STEPS) {  // gate/up tile idx: blob rows 16 idx .. 16 idx + 15, [chunk][row][128 B]
+            mbar_expect(&S.full[st], Gm::GU_BYTES + Gm::GU_SBYTES);
+            tma_4d(S.codes[st], &P.maps.gu16r[m], 0, 16 * idx, 0, e, &S.full[st]);
+            bulk_copy(S.scl[st], blob_of(m, e) + gu_scales_b + (long long)16 * idx * NG * 2, Gm::GU_SBYTES, &S.full[st]);
+        } else {  // down block d: rows 64 d .. 64 d + 63
+            const int row0 = 64 * (idx - GU_STEPS);
+            mbar_expect(&S.full[st], Gm::DN_BYTES + Gm::DN_SBYTES);
+            tma_3d(S.codes[st], &P.maps.dn64[m], 0, row0, e, &S.full[st]);
+            bulk_copy(S.scl[st], blob_of(m, e) + d_scales_b + (long long)row0 * NJ * 2, Gm::DN_SBYTES, &S.full[st]);
         }
-        ++produced;
-        return true;
+        S.issued[st] = c / NST + 1;
     };
-    auto take = [&]() -> int {  // the next step's stage once it has landed, -1 after a timeout
-        const int c = done, st = c % NST;
-        if (!stalled && !__all_sync(0xffffffffu, wait_bar(&S.full[st], (c / NST) & 1))) fail_wait();
+    // This warp's step c once it has landed (-1 after a timeout). The stage's previous use was
+    // consumed first (the empty barrier): only then is the full barrier's parity unambiguous.
+    auto take = [&](int c) -> int {
+        const int st = c % NST, v = c / NST;
+        if (!stalled && !__all_sync(0xffffffffu, (v == 0 || wait_bar(&S.empty[st], (v - 1) & 1)) && wait_bar(&S.full[st], v & 1)))
+            fail_wait();
         return stalled ? -1 : st;
     };
-    // this warp is done with step `done`; thread 0 then refills the stage freed two steps ago
-    // (waiting there for the slowest warp, not for the step just read)
-    auto release = [&]() {
+    // this warp is done reading step c: free its stage and refill it with step c + NST (the stage
+    // was read through the generic proxy)
+    auto release = [&](int c) {
         __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&S.empty[done % NST])) : "memory");
-        ++done;
-        if (tid == 0 && !stalled && done >= 2 && produced < total && produced < done + NST - 2 + 1) {
-            if (!produce()) stalled = true;
+        if (lane == 0) {
+            const int st = c % NST;
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&S.empty[st])) : "memory");
+            if (!stalled && c + NST < total) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                produce(c + NST);
+            }
         }
         __syncwarp();
     };
@@ -465,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     };
 
     if (tid == 0)  // weights need no digits: the first steps' copies start now
-        for (int i = 0; i < NST && i < total; ++i) produce();
+        for (int c = 0; c < NST && c < total; ++c) produce(c);
 
     // ------------------------------------------------------------------ arrival: digit records
     if (tid == 0) {
@@ -507,18 +510,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         float hmax[NCG];
 #pragma unroll
         for (int cg = 0; cg < NCG; ++cg) hmax[cg] = 0.0f;
-        for (int i = 0; i < 2 * F / 128; ++i) {
-            const int tile = warp + kWarps * i;  // rows 16 tile .. 16 tile + 15: this warp's slice of block i
+        const int c0 = ui * STEPS;  // this unit's first step
+        for (int tile = warp; tile < GU_STEPS; tile += kWarps) {  // rows 16 tile .. 16 tile + 15
             float acc[NCG][2];
 #pragma unroll
             for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
-            for (int sub = 0; sub < CPT; ++sub) {
-                const int st = take();
-                if (st >= 0)
-                    mma_chunk<8, true, 128, 8, RX::STRIDE>(smem_u32(S.codes[st]) + 2048 * warp, S.scl[st] + 16 * 8 * warp, &S.xrec[0][0],
-                                                           RX::SUM, 8 * sub, tsB, tsC, ncg, acc);
-                release();
-            }
+            const int st = take(c0 + tile);
+            if (st >= 0)
+#pragma unroll 1
+                for (int sub = 0; sub < CPT; ++sub)
+                    mma_chunk<8, true, 128, NG, RX::STRIDE>(smem_u32(S.codes[st]) + 2048 * sub, S.scl[st] + 8 * sub, &S.xrec[0][0], RX::SUM,
+                                                            8 * sub, tsB, tsC, ncg, acc);
+            release(c0 + tile);
             // lanes with even q hold token slot 2cg + q/2; row g (gate when g is even) pairs with
             // row g+1 (up) four lanes down: hidden 8 tile + g/2 (+4 for row g+8)
 #pragma unroll
@@ -579,7 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         }
         __syncthreads();
 
-        // down: rows 128 dt + 16 warp (+ g, + g + 8); lanes with even q hold token slot 2cg + q/2
+        // down: warp w takes the 64-row blocks w, w + 8, ... (tiles of 16 rows: + g, + g + 8); lanes
+        // with even q hold token slot 2cg + q/2
         float wsc[NCG];
         int prow[NCG];
 #pragma unroll
@@ -587,74 +591,69 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
             wsc[cg] = tsC[cg] >= 0 ? *reinterpret_cast<const float *>(S.hrec[tsC[cg]] + RH::SCALE) * S.uw[buf][tsC[cg]] : 0.0f;
             prow[cg] = tsC[cg] >= 0 ? S.urow[buf][tsC[cg]] : 0;
         }
-        for (int dt = 0; dt < DN_STEPS; ++dt) {
-            float acc[NCG][2];
+        for (int blk = warp; blk < DN_STEPS; blk += kWarps) {  // rows 64 blk .. 64 blk + 63, 16 per tile
+            const int st = take(c0 + GU_STEPS + blk);
+#pragma unroll 1
+            for (int tt = 0; tt < 4; ++tt) {
+                float acc[NCG][2];
 #pragma unroll
-            for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
-            const int st = take();
-            if (st >= 0)
-                mma_chunk<NJ, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(smem_u32(S.codes[st]) + 16 * Gm::DROW * warp, S.scl[st] + 16 * NJ * warp,
-                                                                         &S.hrec[0][0], RH::SUM, 0, tsB, tsC, ncg, acc);
-            release();
-            const int row = 128 * dt + 16 * warp + g;
+                for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
+                if (st >= 0)
+                    mma_chunk<NJ, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(smem_u32(S.codes[st]) + 16 * Gm::DROW * tt, S.scl[st] + 16 * NJ * tt,
+                                                                             &S.hrec[0][0], RH::SUM, 0, tsB, tsC, ncg, acc);
+                const int row = 64 * blk + 16 * tt + g;
 #pragma unroll
-            for (int cg = 0; cg < NCG; ++cg) {
-                if (cg >= ncg) break;
-                if (!(q & 1) && tsC[cg] >= 0) {
-                    float *pr = P.part + (long long)prow[cg] * H + row;
-                    __stcg(pr, acc[cg][0] * wsc[cg]);
-                    __stcg(pr + 8, acc[cg][1] * wsc[cg]);
+                for (int cg = 0; cg < NCG; ++cg) {
+                    if (cg >= ncg) break;
+                    if (st >= 0 && !(q & 1) && tsC[cg] >= 0) {
+                        float *pr = P.part + (long long)prow[cg] * H + row;
+                        __stcg(pr, acc[cg][0] * wsc[cg]);
+                        __stcg(pr + 8, acc[cg][1] * wsc[cg]);
+                    }
                 }
             }
+            release(c0 + GU_STEPS + blk);
         }
     }
 
     // ------------------------------------------------------------------ second arrival: y
-    if (tid == 0)  // no copy may be in flight at exit
-        for (int c = done; c < produced; ++c) wait_bar(&S.full[c % NST], (c / NST) & 1);
+    __syncthreads();
+    if (tid < NST && S.issued[tid] > 0)  // no copy may be in flight at exit: each stage's last use has landed
+        wait_bar(&S.full[tid], (S.issued[tid] - 1) & 1);
     if (x_staged >= 0) wait_bar(&S.bar_x, x_staged & 1);  // no copy may be in flight at exit
     if (stalled) atomicOr(&S.abort_flag, 1);
     __syncthreads();
     if (tid == 0 && !grid_arrive_wait(&P.sync[1], (unsigned)G, P.spin_limit)) S.abort_flag = 1;
     __syncthreads();
     if (!S.abort_flag) {
-        // y[t][r]: the K + 1 terms of one float4 column (the shared expert, then the routed pairs
-        // in selection order; a pair without an expert adds zero): lane l adds terms l and l + 32,
-        // then a fixed shuffle tree. Eight items of a warp at once: their loads are all in flight.
-        const int H4 = H / 4, NT = K + 1;
+        // y[t][4c .. 4c + 3], one thread each: the shared expert's term, then the routed pairs'
+        // terms in selection order (kernels/strata.cu:360-365 adds them in that order; a pair
+        // without an expert adds nothing). Eight terms' loads are in flight at once.
+        const int H4 = H / 4;
         const float4 *part4 = reinterpret_cast<const float4 *>(P.part);
-        constexpr int NB = 8;
-        const int stride = G * kWarps;
-        auto term = [&](int t, int mm, int c, bool in) -> float4 {
-            const int row = mm == 0 ? P2 + t : t * K + mm - 1;
-            const bool ok = in && mm < NT && (mm == 0 || (unsigned)S.ids[t * K + mm - 1] < (unsigned)E);
-            return ok ? __ldcg(part4 + (long long)row * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        };
-        for (int item0 = cta * kWarps + warp; item0 < B * H4; item0 += NB * stride) {
-            float4 u[NB][2];
+        for (int item = cta * kThreads + tid; item < B * H4; item += G * kThreads) {
+            const int t = item / H4, c = item % H4;
+            float4 v = __ldcg(part4 + (long long)(P2 + t) * H4 + c);
+            for (int k0 = 0; k0 < K; k0 += 8) {
+                float4 u[8];
 #pragma unroll
-            for (int n = 0; n < NB; ++n) {
-                const int item = item0 + n * stride, t = min(item / H4, B - 1), c = item % H4;  // t clamped: past the end, nothing is read
-                u[n][0] = term(t, lane, c, item < B * H4);
-                u[n][1] = term(t, lane + 32, c, item < B * H4);
-            }
-#pragma unroll
-            for (int n = 0; n < NB; ++n) {
-                float4 a = u[n][0];
-                a.x += u[n][1].x;
-                a.y += u[n][1].y;
-                a.z += u[n][1].z;
-                a.w += u[n][1].w;
-#pragma unroll
-                for (int sft = 16; sft > 0; sft >>= 1) {
-                    a.x += __shfl_xor_sync(0xffffffffu, a.x, sft);
-                    a.y += __shfl_xor_sync(0xffffffffu, a.y, sft);
-                    a.z += __shfl_xor_sync(0xffffffffu, a.z, sft);
-                    a.w += __shfl_xor_sync(0xffffffffu, a.w, sft);
+                for (int n = 0; n < 8; ++n) {
+                    const int k = k0 + n;
+                    const bool ok = k < K && (unsigned)S.ids[t * K + k] < (unsigned)E;
+                    u[n] = ok ? __ldcg(part4 + (long long)(t * K + k) * H4 + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 }
-                const int item = item0 + n * stride;
-                if (lane == 0 && item < B * H4) reinterpret_cast<float4 *>(P.y)[item] = a;
+#pragma unroll
+                for (int n = 0; n < 8; ++n) {
+                    const int k = k0 + n;
+                    if (k < K && (unsigned)S.ids[t * K + k] < (unsigned)E) {
+                        v.x = __fadd_rn(v.x, u[n].x);
+                        v.y = __fadd_rn(v.y, u[n].y);
+                        v.z = __fadd_rn(v.z, u[n].z);
+                        v.w = __fadd_rn(v.w, u[n].w);
+                    }
+                }
             }
+            reinterpret_cast<float4 *>(P.y)[item] = v;
         }
     }
 
@@ -672,6 +671,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         }
     }
 }
+
+static_assert(sizeof(Smem<2048, 512>) + 1024 <= 227 * 1024 && sizeof(Smem<2560, 640>) + 1024 <= 227 * 1024, "shared memory per CTA");
 
 }  // namespace medium
 
