@@ -181,16 +181,45 @@ __device__ __forceinline__ void scan2(Smem<H, F> &S, const int (&a)[2], const in
     }
 }
 
+// GPC values of 16 bits from shared memory into floats (FP16 -> F32, exact), vector loads
+// where the row allows them.
+template <int GPC, int SCLN>
+__device__ __forceinline__ void load_scales(const unsigned short *row, float (&s)[GPC]) {
+    if constexpr (GPC % 8 == 0 && SCLN % 8 == 0) {
+#pragma unroll
+        for (int i = 0; i < GPC / 8; ++i) {
+            const uint4 v = reinterpret_cast<const uint4 *>(row)[i];
+            const unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[j]));
+                s[8 * i + 2 * j] = f.x;
+                s[8 * i + 2 * j + 1] = f.y;
+            }
+        }
+    } else {
+        static_assert(GPC % 2 == 0 && SCLN % 2 == 0, "scale pairs");
+#pragma unroll
+        for (int i = 0; i < GPC / 2; ++i) {
+            const float2 f = __half22float2(reinterpret_cast<const __half2 *>(row)[i]);
+            s[2 * i] = f.x;
+            s[2 * i + 1] = f.y;
+        }
+    }
+}
+
 // 16 rows x GPC groups of one chunk against the digit records of the unit's token slots (MMA
 // columns: token slot 2 cg + g / 4, digit g % 4, the fourth digit zero). `code` is the chunk's
 // codes in shared memory (SWZ: 128-byte rows with the 128-byte swizzle; else ROWB-byte rows),
 // `scl` its scales [16 rows][SCLN] (the chunk's groups from column 0), `g0` the chunk's first
 // group in the records (RSTRIDE bytes apart, group sums at byte `sum_off`). Adds
-// scale * sum((c - 1) v) per group into acc.
+// scale * sum((c - 1) v) per group into acc[cg] of row g (even q) or g + 8 (odd q), token slot
+// 2 cg + q / 2: the two lanes of a pair swap the partial digit sums the other one's row needs.
 template <int GPC, bool SWZ, int ROWB, int SCLN, int RSTRIDE>
 __device__ __forceinline__ void mma_chunk(unsigned code, const unsigned short *scl, const unsigned char *recs, int sum_off, int g0,
-                                          const int (&tsB)[4], const int (&tsC)[4], int ncg, float (&acc)[4][2]) {
+                                          const int (&tsB)[4], const int (&tsC)[4], int ncg, float (&acc)[4]) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3, d = g & 3;
+    const bool odd = q & 1;
     const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
     unsigned w[GPC / 2][4];
 #pragma unroll
@@ -199,13 +228,9 @@ __device__ __forceinline__ void mma_chunk(unsigned code, const unsigned short *s
         const unsigned addr = SWZ ? code + r * 128 + ((c ^ (r & 7)) << 4) : code + r * ROWB + (c << 4);
         ldsm_x4(addr, w[gp][0], w[gp][1], w[gp][2], w[gp][3]);
     }
-    // expert scales are finite FP16 (rejected on load otherwise, src/model.js:164): exact conversion
-    float s_lo[GPC], s_hi[GPC];
-#pragma unroll
-    for (int gl = 0; gl < GPC; ++gl) {
-        s_lo[gl] = __half2float(__ushort_as_half(scl[g * SCLN + gl]));
-        s_hi[gl] = __half2float(__ushort_as_half(scl[(g + 8) * SCLN + gl]));
-    }
+    // expert scales are finite FP16 (checked on upload, src/model.js:164): exact conversion
+    float s_row[GPC];
+    load_scales<GPC, SCLN>(scl + (g + (odd ? 8 : 0)) * SCLN, s_row);
 #pragma unroll
     for (int cg = 0; cg < 4; ++cg) {
         if (cg >= ncg) break;
@@ -226,13 +251,16 @@ __device__ __forceinline__ void mma_chunk(unsigned code, const unsigned short *s
                 imma(c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                      (wh >> (4 * h + 2)) & 0x03030303u, bf[gl][h].x, bf[gl][h].y);
             }
+        // lane (g, q) holds rows g and g + 8 at columns 2q, 2q + 1: digits 0, 1 (even q) or 2 and
+        // the zero column (odd q). Even q keeps row g, odd q row g + 8; each sends its partner the
+        // piece of the other row: digits 0 + 256 * 1 of row g + 8, or digit 2 of row g.
         const int *xsr = reinterpret_cast<const int *>(recs + (tsC[cg] >= 0 ? tsC[cg] : 0) * RSTRIDE + sum_off) + g0;
 #pragma unroll
         for (int gl = 0; gl < GPC; ++gl) {
-            const int d2lo = __shfl_down_sync(0xffffffffu, c4[gl][0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[gl][2], 1);
-            const int xs = xsr[gl];
-            acc[cg][0] = fmaf(s_lo[gl], (float)(c4[gl][0] + 256 * c4[gl][1] + 65536 * d2lo - xs), acc[cg][0]);
-            acc[cg][1] = fmaf(s_hi[gl], (float)(c4[gl][2] + 256 * c4[gl][3] + 65536 * d2hi - xs), acc[cg][1]);
+            const int send = odd ? c4[gl][0] : c4[gl][2] + 256 * c4[gl][3];
+            const int recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            const int v = odd ? recv + 65536 * c4[gl][2] : c4[gl][0] + 256 * c4[gl][1] + 65536 * recv;
+            acc[cg] = fmaf(s_row[gl], (float)(v - xsr[gl]), acc[cg]);
         }
     }
 }
@@ -512,9 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         for (int cg = 0; cg < NCG; ++cg) hmax[cg] = 0.0f;
         const int c0 = ui * STEPS;  // this unit's first step
         for (int tile = warp; tile < GU_STEPS; tile += kWarps) {  // rows 16 tile .. 16 tile + 15
-            float acc[NCG][2];
+            float acc[NCG];
 #pragma unroll
-            for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
+            for (int cg = 0; cg < NCG; ++cg) acc[cg] = 0.0f;
             const int st = take(c0 + tile);
             if (st >= 0)
 #pragma unroll 1
@@ -522,19 +550,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
                     mma_chunk<8, true, 128, NG, RX::STRIDE>(smem_u32(S.codes[st]) + 2048 * sub, S.scl[st] + 8 * sub, &S.xrec[0][0], RX::SUM,
                                                             8 * sub, tsB, tsC, ncg, acc);
             release(c0 + tile);
-            // lanes with even q hold token slot 2cg + q/2; row g (gate when g is even) pairs with
-            // row g+1 (up) four lanes down: hidden 8 tile + g/2 (+4 for row g+8)
+            // lane (g, q) holds row g (even q) or g + 8 (odd q) for token slot 2cg + q/2; row g
+            // (gate when g is even) pairs with row g + 1 (up) four lanes down: hidden 8 tile + g/2
+            // (+ 4 for rows g + 8)
 #pragma unroll
             for (int cg = 0; cg < NCG; ++cg) {
                 if (cg >= ncg) break;
                 const float sc = tsC[cg] >= 0 ? *reinterpret_cast<const float *>(S.xrec[tsC[cg]] + RX::SCALE) : 0.0f;
-                const float gv0 = acc[cg][0] * sc, gv1 = acc[cg][1] * sc;
-                const float up0 = __shfl_down_sync(0xffffffffu, gv0, 4), up1 = __shfl_down_sync(0xffffffffu, gv1, 4);
-                if (!(q & 1) && !(g & 1) && tsC[cg] >= 0) {
-                    const float h0 = __fmul_rn(ref_silu(gv0), up0), h1 = __fmul_rn(ref_silu(gv1), up1);
-                    S.hid[tsC[cg]][8 * tile + (g >> 1)] = h0;
-                    S.hid[tsC[cg]][8 * tile + 4 + (g >> 1)] = h1;
-                    hmax[cg] = fmaxf(hmax[cg], fmaxf(fabsf(h0), fabsf(h1)));  // NaN ignored, as fmaxf
+                const float gv = acc[cg] * sc;
+                const float up = __shfl_down_sync(0xffffffffu, gv, 4);
+                if (!(g & 1) && tsC[cg] >= 0) {
+                    const float hv = __fmul_rn(ref_silu(gv), up);
+                    S.hid[tsC[cg]][8 * tile + ((q & 1) ? 4 : 0) + (g >> 1)] = hv;
+                    hmax[cg] = fmaxf(hmax[cg], fabsf(hv));  // NaN ignored, as fmaxf
                 }
             }
         }
@@ -542,6 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         for (int cg = 0; cg < NCG; ++cg) {
             if (cg >= ncg) break;
             float mh = hmax[cg];
+            mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 1));
             mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 4));
             mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 8));
             mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, 16));
@@ -582,8 +611,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         }
         __syncthreads();
 
-        // down: warp w takes the 64-row blocks w, w + 8, ... (tiles of 16 rows: + g, + g + 8); lanes
-        // with even q hold token slot 2cg + q/2
+        // down: warp w takes the 64-row blocks w, w + 8, ... (tiles of 16 rows: row g for even q,
+        // g + 8 for odd q; token slot 2cg + q/2)
         float wsc[NCG];
         int prow[NCG];
 #pragma unroll
@@ -595,21 +624,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
             const int st = take(c0 + GU_STEPS + blk);
 #pragma unroll 1
             for (int tt = 0; tt < 4; ++tt) {
-                float acc[NCG][2];
+                float acc[NCG];
 #pragma unroll
-                for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
+                for (int cg = 0; cg < NCG; ++cg) acc[cg] = 0.0f;
                 if (st >= 0)
                     mma_chunk<NJ, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(smem_u32(S.codes[st]) + 16 * Gm::DROW * tt, S.scl[st] + 16 * NJ * tt,
                                                                              &S.hrec[0][0], RH::SUM, 0, tsB, tsC, ncg, acc);
-                const int row = 64 * blk + 16 * tt + g;
+                const int row = 64 * blk + 16 * tt + g + ((q & 1) ? 8 : 0);
 #pragma unroll
                 for (int cg = 0; cg < NCG; ++cg) {
                     if (cg >= ncg) break;
-                    if (st >= 0 && !(q & 1) && tsC[cg] >= 0) {
-                        float *pr = P.part + (long long)prow[cg] * H + row;
-                        __stcg(pr, acc[cg][0] * wsc[cg]);
-                        __stcg(pr + 8, acc[cg][1] * wsc[cg]);
-                    }
+                    if (st >= 0 && tsC[cg] >= 0) __stcg(P.part + (long long)prow[cg] * H + row, acc[cg] * wsc[cg]);
                 }
             }
             release(c0 + GU_STEPS + blk);
