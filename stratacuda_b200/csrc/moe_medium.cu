@@ -59,6 +59,10 @@ constexpr int kMaxTopK = 32;
 constexpr int kMaxPairs = kMaxBatch * kMaxTopK;
 constexpr int kMaxExperts = 512;
 constexpr int kSharedGroup = 2;  // tokens per shared-expert unit (its weights are read once per unit, from L2 after the first)
+constexpr int kMWarps = 16;      // warps of a CTA: four per scheduler, to hide the MMA and load latencies
+constexpr int kMThreads = kMWarps * 32;
+constexpr int kUnitTokens = 4;   // token slots of a unit (MMA column pairs: kUnitTokens / 2)
+constexpr int kUnitCG = kUnitTokens / 2;
 
 // Digit record of one vector of N elements: digits uint2[N/64][2][4][3] (group, MMA half,
 // 16-element block q, digit), int sum[N/64], float scale (2^-k). In shared memory, slots are
@@ -90,11 +94,11 @@ struct MGeo {
     static constexpr int GU_SBYTES = 16 * NG * 2, DN_SBYTES = 64 * NJ * 2;
     static constexpr int STAGE = GU_BYTES > DN_BYTES ? GU_BYTES : DN_BYTES;          // codes of a step (1024-aligned)
     static constexpr int SSTAGE = GU_SBYTES > DN_SBYTES ? GU_SBYTES : DN_SBYTES;     // scales of a step
-    static constexpr int NST = F == 512 ? 12 : 8;    // stages (shared-memory budget)
+    static constexpr int NST = F == 512 ? 16 : 8;    // stages (shared-memory budget)
     static_assert(NG % 8 == 0 && H % 512 == 0 && STAGE % 1024 == 0 && SSTAGE % 128 == 0, "geometry");
-    // steps go round-robin to the warps in every phase of a unit, and a stage's use v - 2 was
-    // consumed by the warp that consumes its use v (the parity waits below rely on it)
-    static_assert(GU_STEPS % kWarps == 0 && DN_STEPS % kWarps == 0 && (2 * NST) % kWarps == 0, "step ownership");
+    // step c of a CTA belongs to warp c % kMWarps, and a stage's use v - 2 was consumed by the
+    // warp that consumes its use v (the parity waits below rely on it)
+    static_assert((2 * NST) % kMWarps == 0, "step ownership");
 };
 
 struct Params {
@@ -118,19 +122,19 @@ struct Smem {
     using G = MGeo<H, F>;
     unsigned char codes[G::NST][G::STAGE];  // 1024-aligned
     alignas(128) unsigned short scl[G::NST][G::SSTAGE / 2];
-    alignas(128) unsigned char xrec[kMaxTokens][Rec<H>::STRIDE];  // the unit's tokens: x digits
-    alignas(128) unsigned char hrec[kMaxTokens][Rec<F>::STRIDE];  // the unit's tokens: hidden digits
-    float hid[kMaxTokens][F];
-    float hmaxw[kWarps][kMaxTokens];  // per-warp max |hidden| of each token slot
+    alignas(128) unsigned char xrec[kUnitTokens][Rec<H>::STRIDE];  // the unit's tokens: x digits
+    alignas(128) unsigned char hrec[kUnitTokens][Rec<F>::STRIDE];  // the unit's tokens: hidden digits
+    float hid[kUnitTokens][F];
+    float hmaxw[kMWarps][kUnitTokens];  // per-warp max |hidden| of each token slot
     short pairs[kMaxPairs];           // pairs ordered by expert, token-major within one
     int off[kMaxExperts + 1];         // expert e's pairs: pairs[off[e] .. off[e+1])
     int gstart[kMaxExperts + 1];      // expert e's token groups: [gstart[e], gstart[e+1])
     int run[kMaxExperts];             // pair counts, then placement cursors
     int ids[kMaxPairs];               // the routed ids
-    int scan_w[2][kWarps];
+    int scan_w[2][kMWarps];
     float sgw[kMaxBatch];     // sigmoid(shared-gate logit) per token
-    int urow[2][kMaxTokens];  // unit token slot -> partial row (by unit parity)
-    float uw[2][kMaxTokens];  // unit token slot -> weight
+    int urow[2][kUnitTokens];  // unit token slot -> partial row (by unit parity)
+    float uw[2][kUnitTokens];  // unit token slot -> weight
     unsigned xmax;
     unsigned long long full[G::NST], empty[G::NST];
     int issued[G::NST];  // uses of each stage issued so far
@@ -138,8 +142,8 @@ struct Smem {
     int abort_flag;
 };
 
-// Block-wide exclusive scan of two sequences over [0, n) (n <= 512, 256 threads: thread i
-// holds entries 2i and 2i+1); out[n] receives each total.
+// Block-wide exclusive scan of two sequences over [0, n) (n <= 2 kMThreads: thread i holds
+// entries 2i and 2i+1); out[n] receives each total.
 template <int H, int F>
 __device__ __forceinline__ void scan2(Smem<H, F> &S, const int (&a)[2], const int (&b)[2], int n, int *out_a, int *out_b, int base_b) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -158,7 +162,7 @@ __device__ __forceinline__ void scan2(Smem<H, F> &S, const int (&a)[2], const in
     }
     __syncthreads();
     int wa = 0, wb = 0, ta = 0, tb = 0;
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < kMWarps; ++w) {
         if (w < warp) {
             wa += S.scan_w[0][w];
             wb += S.scan_w[1][w];
@@ -209,22 +213,23 @@ __device__ __forceinline__ void load_scales(const unsigned short *row, float (&s
 }
 
 // 16 rows x GPC groups of one chunk against the digit records of the unit's token slots (MMA
-// columns: token slot 2 cg + g / 4, digit g % 4, the fourth digit zero). `code` is the chunk's
+// columns: token slot 2 cg + g / 4, digit g % 4, the fourth digit zero). `code` is the rows'
 // codes in shared memory (SWZ: 128-byte rows with the 128-byte swizzle; else ROWB-byte rows),
-// `scl` its scales [16 rows][SCLN] (the chunk's groups from column 0), `g0` the chunk's first
+// the groups starting at 16-byte column `col0`, `scl` their scales [16 rows][SCLN] (from the
+// first group), `g0` the first
 // group in the records (RSTRIDE bytes apart, group sums at byte `sum_off`). Adds
 // scale * sum((c - 1) v) per group into acc[cg] of row g (even q) or g + 8 (odd q), token slot
 // 2 cg + q / 2: the two lanes of a pair swap the partial digit sums the other one's row needs.
 template <int GPC, bool SWZ, int ROWB, int SCLN, int RSTRIDE>
-__device__ __forceinline__ void mma_chunk(unsigned code, const unsigned short *scl, const unsigned char *recs, int sum_off, int g0,
-                                          const int (&tsB)[4], const int (&tsC)[4], int ncg, float (&acc)[4]) {
+__device__ __forceinline__ void mma_chunk(unsigned code, int col0, const unsigned short *scl, const unsigned char *recs, int sum_off, int g0,
+                                          const int (&tsB)[kUnitCG], const int (&tsC)[kUnitCG], int ncg, float (&acc)[kUnitCG]) {
     const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3, d = g & 3;
     const bool odd = q & 1;
     const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
     unsigned w[GPC / 2][4];
 #pragma unroll
     for (int gp = 0; gp < GPC / 2; ++gp) {
-        const int c = 2 * gp + (lane >> 4);
+        const int c = col0 + 2 * gp + (lane >> 4);
         const unsigned addr = SWZ ? code + r * 128 + ((c ^ (r & 7)) << 4) : code + r * ROWB + (c << 4);
         ldsm_x4(addr, w[gp][0], w[gp][1], w[gp][2], w[gp][3]);
     }
@@ -232,7 +237,7 @@ __device__ __forceinline__ void mma_chunk(unsigned code, const unsigned short *s
     float s_row[GPC];
     load_scales<GPC, SCLN>(scl + (g + (odd ? 8 : 0)) * SCLN, s_row);
 #pragma unroll
-    for (int cg = 0; cg < 4; ++cg) {
+    for (int cg = 0; cg < kUnitCG; ++cg) {
         if (cg >= ncg) break;
         const uint2 *dg = reinterpret_cast<const uint2 *>(recs + (tsB[cg] >= 0 ? tsB[cg] : 0) * RSTRIDE);
         uint2 bf[GPC][2];
@@ -266,7 +271,7 @@ __device__ __forceinline__ void mma_chunk(unsigned code, const unsigned short *s
 }
 
 template <int H, int F>
-__global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kMThreads, 1) k_moe_medium(const __grid_constant__ Params P) {
     using Gm = MGeo<H, F>;
     using RX = Rec<H>;
     using RH = Rec<F>;
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<unsigned long long>(&P.maps.dn64[i])) : "memory");
         }
     }
-    for (int e = tid; e < E; e += kThreads) S.run[e] = 0;
+    for (int e = tid; e < E; e += kMThreads) S.run[e] = 0;
     __syncthreads();
 
     // ------------------------------------------------------------------ A1: digit records of tokens cta, cta + G, ...
@@ -304,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         if (tid == 0) S.xmax = 0u;
         __syncthreads();
         float mx = 0.0f;  // largest |x| (NaN ignored, as fmaxf; max is order-free)
-        for (int i = tid; i < H / 4; i += kThreads) {
+        for (int i = tid; i < H / 4; i += kMThreads) {
             const float4 v = __ldg(reinterpret_cast<const float4 *>(xt) + i);
             mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
@@ -316,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         const float mul = pow2f(k);  // exact power of two
         // blocks of 16 elements (group, q), one per thread; NG * 4 is a multiple of 32, so whole
         // warps take part and the group-sum shuffles see all four blocks of a group
-        for (int b = tid; b < NG * 4; b += kThreads) {
+        for (int b = tid; b < NG * 4; b += kMThreads) {
             const int grp = b >> 2, qq = b & 3;
             const float4 *src = reinterpret_cast<const float4 *>(xt + 64 * grp + 16 * qq);
             int v[16];
@@ -348,12 +353,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     }
 
     // ------------------------------------------------------------------ A2: pair table, token groups
-    for (int p = tid; p < P2; p += kThreads) {
+    for (int p = tid; p < P2; p += kMThreads) {
         const int e = __ldg(P.ids + p);
         S.ids[p] = e;
         if (e >= 0 && e < E) atomicAdd(&S.run[e], 1);
     }
-    for (int t = tid; t < B; t += kThreads) S.sgw[t] = ref_sigmoid(__ldg(P.sg + t));
+    for (int t = tid; t < B; t += kMThreads) S.sgw[t] = ref_sigmoid(__ldg(P.sg + t));
     __syncthreads();
     {
         int c[2], ng[2];
@@ -361,12 +366,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         for (int i = 0; i < 2; ++i) {
             const int e = 2 * tid + i;
             c[i] = e < E ? S.run[e] : 0;
-            ng[i] = (c[i] + kMaxTokens - 1) / kMaxTokens;
+            ng[i] = (c[i] + kUnitTokens - 1) / kUnitTokens;
         }
         scan2(S, c, ng, E, S.off, S.gstart, SG);
     }
     __syncthreads();
-    for (int e = tid; e < E; e += kThreads) S.run[e] = S.off[e];  // placement cursors
+    for (int e = tid; e < E; e += kMThreads) S.run[e] = S.off[e];  // placement cursors
     __syncthreads();
     if (warp == 0) {  // stable placement, 32 pairs at a time in pair order
         for (int base = 0; base < P2; base += 32) {
@@ -471,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     auto stage_unit = [&](int ui) {
         int gi, m, e, tg;
         unit_of(ui, gi, m, e, tg);
-        const int n = m ? min(kSharedGroup, B - kSharedGroup * tg) : min(kMaxTokens, S.off[e + 1] - S.off[e] - kMaxTokens * tg);
+        const int n = m ? min(kSharedGroup, B - kSharedGroup * tg) : min(kUnitTokens, S.off[e + 1] - S.off[e] - kUnitTokens * tg);
         const int buf = ui & 1;
         int tok = 0;
         if (lane < n) {
@@ -480,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
                 S.urow[buf][lane] = P2 + tok;
                 S.uw[buf][lane] = S.sgw[tok];
             } else {
-                const int pr = S.pairs[S.off[e] + kMaxTokens * tg + lane];
+                const int pr = S.pairs[S.off[e] + kUnitTokens * tg + lane];
                 tok = pr / K;
                 S.urow[buf][lane] = pr;
                 S.uw[buf][lane] = __ldg(P.weights + pr);
@@ -519,11 +524,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
     }
 
     // ------------------------------------------------------------------ units
-    constexpr int NCG = 4;
+    constexpr int NCG = kUnitCG;
     for (int ui = 0; ui < n_units; ++ui) {
         int gi, m, e, tg;
         unit_of(ui, gi, m, e, tg);
-        const int n_cur = m ? min(kSharedGroup, B - kSharedGroup * tg) : min(kMaxTokens, S.off[e + 1] - S.off[e] - kMaxTokens * tg);
+        const int n_cur = m ? min(kSharedGroup, B - kSharedGroup * tg) : min(kUnitTokens, S.off[e + 1] - S.off[e] - kUnitTokens * tg);
         const int ncg = (n_cur + 1) / 2, buf = ui & 1;
         int tsB[NCG], tsC[NCG];
 #pragma unroll
@@ -538,17 +543,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         float hmax[NCG];
 #pragma unroll
         for (int cg = 0; cg < NCG; ++cg) hmax[cg] = 0.0f;
-        const int c0 = ui * STEPS;  // this unit's first step
-        for (int tile = warp; tile < GU_STEPS; tile += kWarps) {  // rows 16 tile .. 16 tile + 15
+        const int c0 = ui * STEPS;  // this unit's first step; step c belongs to warp c % kMWarps
+        const int first = ((warp - c0) % kMWarps + kMWarps) % kMWarps;
+        for (int tile = first; tile < GU_STEPS; tile += kMWarps) {  // rows 16 tile .. 16 tile + 15
             float acc[NCG];
 #pragma unroll
             for (int cg = 0; cg < NCG; ++cg) acc[cg] = 0.0f;
             const int st = take(c0 + tile);
             if (st >= 0)
 #pragma unroll 1
-                for (int sub = 0; sub < CPT; ++sub)
-                    mma_chunk<8, true, 128, NG, RX::STRIDE>(smem_u32(S.codes[st]) + 2048 * sub, S.scl[st] + 8 * sub, &S.xrec[0][0], RX::SUM,
-                                                            8 * sub, tsB, tsC, ncg, acc);
+                for (int hc = 0; hc < 2 * CPT; ++hc) {  // half chunks: 4 scale groups of one 128-byte column chunk
+                    const int sub = hc >> 1, half = hc & 1;
+                    mma_chunk<4, true, 128, NG, RX::STRIDE>(smem_u32(S.codes[st]) + 2048 * sub, 4 * half, S.scl[st] + 8 * sub + 4 * half,
+                                                            &S.xrec[0][0], RX::SUM, 8 * sub + 4 * half, tsB, tsC, ncg, acc);
+                }
             release(c0 + tile);
             // lane (g, q) holds row g (even q) or g + 8 (odd q) for token slot 2cg + q/2; row g
             // (gate when g is even) pairs with row g + 1 (up) four lanes down: hidden 8 tile + g/2
@@ -583,13 +591,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         }
 
         // hidden -> digit records: blocks of 16 values (slot, group, q), 32 per warp iteration
-        for (int b0 = warp * 32; b0 < n_cur * NJ * 4; b0 += kThreads) {
+        for (int b0 = warp * 32; b0 < n_cur * NJ * 4; b0 += kMThreads) {
             const int b = b0 + lane;
             const bool live = b < n_cur * NJ * 4;
             const int ts = live ? b / (NJ * 4) : 0, grp = (b >> 2) % NJ, qq = b & 3;
             float mx = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, S.hmaxw[w][ts]);
+            for (int w = 0; w < kMWarps; ++w) mx = fmaxf(mx, S.hmaxw[w][ts]);
             const int k = scale_exp(mx);
             const float mul = pow2f(k);
             int v[16];
@@ -620,16 +628,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
             wsc[cg] = tsC[cg] >= 0 ? *reinterpret_cast<const float *>(S.hrec[tsC[cg]] + RH::SCALE) * S.uw[buf][tsC[cg]] : 0.0f;
             prow[cg] = tsC[cg] >= 0 ? S.urow[buf][tsC[cg]] : 0;
         }
-        for (int blk = warp; blk < DN_STEPS; blk += kWarps) {  // rows 64 blk .. 64 blk + 63, 16 per tile
+        const int first_dn = ((warp - c0 - GU_STEPS) % kMWarps + kMWarps) % kMWarps;
+        for (int blk = first_dn; blk < DN_STEPS; blk += kMWarps) {  // rows 64 blk .. 64 blk + 63, 16 per tile
             const int st = take(c0 + GU_STEPS + blk);
 #pragma unroll 1
             for (int tt = 0; tt < 4; ++tt) {
                 float acc[NCG];
 #pragma unroll
                 for (int cg = 0; cg < NCG; ++cg) acc[cg] = 0.0f;
-                if (st >= 0)
-                    mma_chunk<NJ, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(smem_u32(S.codes[st]) + 16 * Gm::DROW * tt, S.scl[st] + 16 * NJ * tt,
-                                                                             &S.hrec[0][0], RH::SUM, 0, tsB, tsC, ncg, acc);
+                if (st >= 0) {
+                    const unsigned cb = smem_u32(S.codes[st]) + 16 * Gm::DROW * tt;
+                    const unsigned short *sb = S.scl[st] + 16 * NJ * tt;
+#pragma unroll 1
+                    for (int g4 = 0; g4 < NJ / 4; ++g4)
+                        mma_chunk<4, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(cb, 4 * g4, sb + 4 * g4, &S.hrec[0][0], RH::SUM, 4 * g4, tsB, tsC,
+                                                                                ncg, acc);
+                    if constexpr (NJ % 4 != 0)
+                        mma_chunk<NJ % 4, Gm::DROW == 128, Gm::DROW, NJ, RH::STRIDE>(cb, NJ / 4 * 4, sb + NJ / 4 * 4, &S.hrec[0][0], RH::SUM,
+                                                                                     NJ / 4 * 4, tsB, tsC, ncg, acc);
+                }
                 const int row = 64 * blk + 16 * tt + g + ((q & 1) ? 8 : 0);
 #pragma unroll
                 for (int cg = 0; cg < NCG; ++cg) {
@@ -656,7 +673,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_medium(const __grid_constan
         // without an expert adds nothing). Eight terms' loads are in flight at once.
         const int H4 = H / 4;
         const float4 *part4 = reinterpret_cast<const float4 *>(P.part);
-        for (int item = cta * kThreads + tid; item < B * H4; item += G * kThreads) {
+        for (int item = cta * kMThreads + tid; item < B * H4; item += G * kMThreads) {
             const int t = item / H4, c = item % H4;
             float4 v = __ldcg(part4 + (long long)(P2 + t) * H4 + c);
             for (int k0 = 0; k0 < K; k0 += 8) {
@@ -727,7 +744,7 @@ cudaError_t launch_medium(const medium::Params &p, int grid, cudaStream_t s) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(q2::kThreads);
+    cfg.blockDim = dim3(medium::kMThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
