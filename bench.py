@@ -459,22 +459,46 @@ def run_gpu_arm(args, world, rank, local):
 EP_N1_CACHE = pathlib.Path("/tmp/strata_bench_ep_n1.json")
 
 
+def ep_placement(world, layers, zipf, calib_tokens=2048):
+    """Owner rank per expert for the expert-parallel runs, balanced by the routed rows of a
+    calibration sample (tokens that are not in the timed batches) over the cycled layers, from
+    the seeded synthetic router on the host (every rank computes the same placement). None on
+    one rank."""
+    if world == 1:
+        return None
+    import numpy as np
+
+    from stratacuda_b200 import synth
+    from stratacuda_b200.ep import balanced_placement
+    x = synth.activations(7, calib_tokens, WIDTH, start_token=1 << 30).reshape(calib_tokens, WIDTH)
+    bias = synth.zipf_bias(1, EXPERTS, zipf) if zipf is not None else np.zeros(EXPERTS, np.float32)
+    rows = np.zeros(EXPERTS)
+    for layer in range(layers):
+        W = synth.router_weights(1, layer, EXPERTS, WIDTH).reshape(EXPERTS, WIDTH)
+        top = np.argpartition(-(x @ W.T + bias), TOPK - 1, axis=1)[:, :TOPK]
+        rows += np.bincount(top.reshape(-1), minlength=EXPERTS)
+    return balanced_placement(rows, world)
+
+
 def ep_block(args, world, rank, local, b):
     """BASELINE config 4 at this run's N: 16384 tokens split over the ranks, 512 experts sharded
     E/N per GPU, Zipf(1.1) routing; at N >= 2 the library's NCCL dispatch and return run between
     the ranks. Device time of K steps (CUDA events on the library's stream), max over ranks."""
     import torch
 
-    from stratacuda_b200.ep import EpMoeLayer, ep_init
+    from stratacuda_b200.ep import EpMoeLayer, ep_init, ep_set_placement
     from stratacuda_b200.moe import synth_activations
     total, K, W, NL = args.ep_tokens, min(args.steps, 10), 3, 4
-    if total % world or EXPERTS % world:
-        return {"skipped": f"{total} tokens and {EXPERTS} experts must divide over {world} ranks"}
+    if total % world:
+        return {"skipped": f"{total} tokens must divide over {world} ranks"}
     T = total // world
     zipf = 1.1
     ep_init(b, rank, world)
-    layers = [EpMoeLayer.synthesize(b, rank, world, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf)
-              for l in range(NL)]
+    owner = ep_placement(world, NL, zipf)
+    ep_set_placement(b, owner)
+    layers = [EpMoeLayer.synthesize(b, rank, world, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf,
+                                    owner=owner) for l in range(NL)]
+    n_local = layers[0].local_experts
     n_x = 2
     xs = [synth_activations(b, 2 + s, T, WIDTH, start_token=rank * T) for s in range(n_x)]
     ys = [b.alloc(T * WIDTH, zero=False) for _ in range(n_x)]
@@ -512,6 +536,8 @@ def ep_block(args, world, rank, local, b):
     per_gpu_tf = flops / (ms_max / 1000.0 / K) / world / 1e12
     tps = total * K / (ms_max / 1000.0)
     out = {"tokens": total, "tokens_per_rank": T, "experts_per_rank": EXPERTS // world, "zipf": zipf, "parallelism": f"ep{world}",
+           "placement": "contiguous (one rank)" if owner is None else "balanced by a calibration sample's routed rows",
+           "experts_on_rank0": n_local,
            "exchange": "NCCL grouped send/recv inside strata_moe_ep_forward" if world > 1 else "none (one rank)",
            "tokens_per_s": tps, "ms_per_step": ms_max / K, "steps": K, "warmup": W, "layers_cycled": NL,
            "per_gpu_tflops": per_gpu_tf, "per_gpu_frac": per_gpu_tf / peak, "peak_tflops": peak, "peak_kind": kind,
@@ -542,19 +568,21 @@ def run_ep_arm(args, world, rank, local):
     import torch
 
     from stratacuda_b200.backend import CudaBackend
-    from stratacuda_b200.ep import EpMoeLayer, ep_init
+    from stratacuda_b200.ep import EpMoeLayer, ep_init, ep_set_placement
     from stratacuda_b200.moe import synth_activations
 
     torch.cuda.set_device(local)
     b = CudaBackend(local)
     total, K, W, NL = args.ep_tokens, args.steps, args.warmup, args.layers
-    if total % world or EXPERTS % world:
-        raise SystemExit("--ep-tokens and the 512 experts must divide over the ranks")
+    if total % world:
+        raise SystemExit("--ep-tokens must divide over the ranks")
     T = total // world
     zipf = args.zipf if args.zipf is not None else 1.1
     ep_init(b, rank, world)
-    layers = [EpMoeLayer.synthesize(b, rank, world, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf)
-              for l in range(NL)]
+    owner = ep_placement(world, NL, zipf)
+    ep_set_placement(b, owner)
+    layers = [EpMoeLayer.synthesize(b, rank, world, seed=1, layer=l, width=WIDTH, ff=FF, experts=EXPERTS, top_k=TOPK, zipf=zipf,
+                                    owner=owner) for l in range(NL)]
     n_x = 4
     xs = [synth_activations(b, 2 + s, T, WIDTH, start_token=rank * T) for s in range(n_x)]
     ys = [b.alloc(T * WIDTH, zero=False) for _ in range(n_x)]
@@ -605,9 +633,10 @@ def run_ep_arm(args, world, rank, local):
     line = {"metric": METRIC, "value": total * K / (ms_max / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded SplitMix64; BASELINE config 4 distributions)",
-            "config": {"workload": f"expert-parallel MoE layer, {total} tokens over {world} GPU(s), E512 sharded {EXPERTS // world} per GPU, "
+            "config": {"workload": f"expert-parallel MoE layer, {total} tokens over {world} GPU(s), E512 sharded over the GPUs, "
                                    f"top-10, H2048, F512, Q2 experts + shared expert, Zipf({zipf}) router bias",
                        "tokens": total, "tokens_per_rank": T, "experts_per_rank": EXPERTS // world, "hidden": WIDTH, "ff": FF, "top_k": TOPK,
+                       "placement": "contiguous (one rank)" if owner is None else "balanced by a calibration sample's routed rows",
                        "layers_cycled": NL, "zipf": zipf, "l2": "inputs larger than L2: distinct layer replicas cycled",
                        "parallelism": f"ep{world}"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,

@@ -197,8 +197,9 @@ int strata_moe_forward_noalloc(const strata_moe_layer_dev *layer, const float *x
 /* ---- expert-parallel layer over NCCL (one process per GPU) ----
  * The fused entry point strata_moe_ep (the expert-parallel path of BASELINE's north star; the
  * reference has no multi-GPU path). The 512 (layer.experts) routed experts are sharded evenly:
- * rank r owns experts [r E/n, (r + 1) E/n), and its layer.experts_blob holds exactly those E/n
- * blobs; router, shared gate and shared expert are replicated. A rank passes its own tokens and
+ * rank r owns the experts its placement gives it (strata_ep_set_placement; by default
+ * [r E/n, (r + 1) E/n)), and its layer.experts_blob holds exactly those blobs in ascending id;
+ * router, shared gate and shared expert are replicated. A rank passes its own tokens and
  * receives their y, ids and weights (routing over all E experts, bit-exact; y within 2e-3
  * relative L2, the tensor-core path's tolerance).
  * Setup: rank 0 calls strata_ep_unique_id, the 128 bytes are shared by the caller (e.g. a
@@ -215,6 +216,15 @@ int strata_moe_forward_noalloc(const strata_moe_layer_dev *layer, const float *x
 int strata_ep_unique_id(strata_ctx *ctx, uint8_t *id, size_t cap);
 int strata_ep_init(strata_ctx *ctx, int32_t rank, int32_t n_ranks, const uint8_t *id);
 int strata_ep_set_timeout(strata_ctx *ctx, int32_t milliseconds);
+/* Expert placement (no reference counterpart): owner[e] is the rank that holds expert e, for
+ * e < experts; every rank must own at least one expert, and every rank must set the same
+ * placement. A rank's layer.experts_blob then holds the experts it owns in ascending id order.
+ * Without a call (or with owner = NULL) rank r owns experts [r E/n, (r + 1) E/n). A placement
+ * balanced by the experts' routed rows keeps a skewed router from loading one rank with the
+ * popular experts. Synchronises. strata_ep_local_experts gives this rank's blob count under
+ * the placement in force for `experts` (setting the contiguous one if none is). */
+int strata_ep_set_placement(strata_ctx *ctx, int32_t experts, const int32_t *owner);
+int strata_ep_local_experts(strata_ctx *ctx, int32_t experts, int32_t *count);
 int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                           strata_buf weights);
 /* Same-device loopback transport (no reference counterpart): n virtual ranks on ONE GPU, one

@@ -61,6 +61,8 @@ SIGNATURES = {
     "strata_ep_unique_id": ([_vp, C.c_char_p, _sz], _i),
     "strata_ep_init": ([_vp, C.c_int32, C.c_int32, C.c_char_p], _i),
     "strata_ep_set_timeout": ([_vp, C.c_int32], _i),
+    "strata_ep_set_placement": ([_vp, C.c_int32, C.POINTER(C.c_int32)], _i),
+    "strata_ep_local_experts": ([_vp, C.c_int32, C.POINTER(C.c_int32)], _i),
     "strata_ep_loopback_create": ([_vp, C.c_int32, C.POINTER(_u64)], _i),
     "strata_ep_init_loopback": ([_vp, C.c_int32, _u64], _i),
     "strata_ep_loopback_release": ([_vp, _u64], _i),

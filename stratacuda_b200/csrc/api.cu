@@ -747,17 +747,71 @@ int strata_ep_set_timeout(strata_ctx *ctx, int32_t milliseconds) {
     return STRATA_OK;
 }
 
+namespace {
+// Expert placement of the context's communicator: owner[e] (nullptr: contiguous, experts / n
+// per rank); every rank must own at least one expert. Synchronises.
+int set_placement(strata_ctx *ctx, int experts, const int32_t *owner) {
+    EpComm &c = *ctx->ep;
+    const int n = c.n;
+    if (experts < 1 || experts > 512) return fail(ctx, STRATA_ERR_RANGE, "placement: experts must be 1 .. 512");
+    if (!owner && experts % n) return fail(ctx, STRATA_ERR_RANGE, "experts must be a multiple of the %d ranks", n);
+    std::vector<int> h(2 * (size_t)experts), cnt(n, 0);
+    for (int e = 0; e < experts; ++e) {
+        const int o = owner ? owner[e] : e / (experts / n);
+        if (o < 0 || o >= n) return fail(ctx, STRATA_ERR_RANGE, "placement: expert %d on rank %d, outside 0 .. %d", e, o, n - 1);
+        h[e] = o;
+        h[experts + e] = cnt[o]++;
+    }
+    for (int r = 0; r < n; ++r)
+        if (!cnt[r]) return fail(ctx, STRATA_ERR_RANGE, "placement: rank %d owns no expert", r);
+    if (int r = use_device(ctx)) return r;
+    const size_t bytes = sizeof(int) * h.size();
+    if (c.place_cap < bytes) {
+        if (c.d_place) cudaFree(c.d_place);
+        c.d_place = nullptr;
+        c.place_cap = 0;
+        CUDA_OR_FAIL(ctx, cudaMalloc(&c.d_place, bytes), "cudaMalloc");
+        c.place_cap = bytes;
+    }
+    CUDA_OR_FAIL(ctx, cudaMemcpy(c.d_place, h.data(), bytes, cudaMemcpyHostToDevice), "cudaMemcpy");
+    c.placed_experts = experts;
+    c.n_local = cnt[c.rank];
+    return STRATA_OK;
+}
+}  // namespace
+
+int strata_ep_set_placement(strata_ctx *ctx, int32_t experts, const int32_t *owner) {
+    if (!ctx) return STRATA_ERR_RANGE;
+    if (!ctx->ep) return fail(ctx, STRATA_ERR_RANGE, "strata_ep_init has not been called");
+    if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "synchronising calls are not allowed while the stream is captured");
+    return set_placement(ctx, experts, owner);
+}
+
+int strata_ep_local_experts(strata_ctx *ctx, int32_t experts, int32_t *count) {
+    if (!ctx || !count) return STRATA_ERR_RANGE;
+    if (!ctx->ep) return fail(ctx, STRATA_ERR_RANGE, "strata_ep_init has not been called");
+    if (ctx->ep->placed_experts != experts) {
+        if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "synchronising calls are not allowed while the stream is captured");
+        if (int r = set_placement(ctx, experts, nullptr)) return r;
+    }
+    *count = ctx->ep->n_local;
+    return STRATA_OK;
+}
+
 int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata_buf x, int32_t tokens, strata_buf y, strata_buf ids,
                           strata_buf weights) {
     if (!ctx) return STRATA_ERR_RANGE;
     if (!ctx->ep) return fail(ctx, STRATA_ERR_RANGE, "strata_ep_init has not been called");
     if (!layer) return fail(ctx, STRATA_ERR_RANGE, "null layer");
     const strata_moe_layer &l = *layer;
-    const int n = ep_ranks(ctx->ep);
     if (!moe_prefill_supported(l.width, l.ff, l.experts, l.top_k))
         return fail(ctx, STRATA_ERR_RANGE, "expert-parallel layer supports H 2048/F 512 and H 2560/F 640, <= 512 experts, topK <= 32");
-    if (l.top_k < 1 || l.top_k > l.experts || l.experts % n) return fail(ctx, STRATA_ERR_RANGE, "experts must be a multiple of the %d ranks", n);
+    if (l.top_k < 1 || l.top_k > l.experts) return fail(ctx, STRATA_ERR_RANGE, "topK must be 1 .. experts");
     if (tokens < 1) return fail(ctx, STRATA_ERR_RANGE, "tokens must be an integer >= 1");
+    if (ctx->ep->placed_experts != l.experts) {  // no placement for this expert count: contiguous
+        if (ctx->capturing) return fail(ctx, STRATA_ERR_RANGE, "synchronising calls are not allowed while the stream is captured");
+        if (int r = set_placement(ctx, l.experts, nullptr)) return r;
+    }
     const long long bw = blob_words_of(l.width, l.ff);
     struct Need {
         strata_buf h;
@@ -766,7 +820,7 @@ int strata_moe_ep_forward(strata_ctx *ctx, const strata_moe_layer *layer, strata
         bool optional;
     } need[] = {{l.router, (long long)l.experts * l.width, "router", false},
                 {l.router_bias, l.experts, "router_bias", true},
-                {l.experts_blob, bw * (l.experts / n), "experts_blob (this rank's experts)", false},
+                {l.experts_blob, bw * ctx->ep->n_local, "experts_blob (this rank's experts)", false},
                 {l.shared_blob, bw, "shared_blob", false},
                 {l.shared_gate, l.width, "shared_gate", false},
                 {x, (long long)tokens * l.width, "x", false},

@@ -364,6 +364,7 @@ EpComm::~EpComm() {
     for (Buf &b : bufs)
         if (b.p) cudaFree(b.p);
     if (h_off) cudaFreeHost(h_off);
+    if (d_place) cudaFree(d_place);
     if (t && failed) t->abort();
     t.reset();
 }

@@ -40,6 +40,12 @@ struct EpComm {
     };
     Buf bufs[25];
     int *h_off = nullptr;  // pinned: [0, n] send offsets, [n + 1, 2n] receive counts
+    // Expert placement: d_place = [owner rank of expert e][local blob index of expert e] over
+    // placed_experts experts; this rank holds n_local blobs, the experts it owns in ascending id.
+    int placed_experts = 0;
+    int n_local = 0;
+    int *d_place = nullptr;
+    size_t place_cap = 0;
     ~EpComm();
     // grow-only device buffer i of at least `bytes`
     void *get(int i, size_t bytes, cudaError_t &e);

@@ -430,21 +430,21 @@ __host__ __device__ inline int ep_meta_ints(int K) { return kEpMetaFixed + 2 * K
 
 // dst[t n + p] = p when token t has an expert on rank p (experts sharded evenly: rank p owns
 // [p El, (p + 1) El)), else -1. n <= 32.
-__global__ void k_ep_dest_rows(const int *ids, int T, int K, int E, int El, int n, int *dst) {
+__global__ void k_ep_dest_rows(const int *ids, int T, int K, int E, const int *owner, int n, int *dst) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
     unsigned mask = 0u;
     for (int kk = 0; kk < K; ++kk) {
         const int e = ids[(long long)t * K + kk];
-        if (e >= 0 && e < E) mask |= 1u << (e / El);
+        if (e >= 0 && e < E) mask |= 1u << owner[e];
     }
     for (int p = 0; p < n; ++p) dst[(long long)t * n + p] = (mask >> p) & 1u ? p : -1;
 }
 
 // One block per token: the token's FP16 row (times 2^k, largest |x| < 2^15) at each of its
 // send rows, and each row's metadata (the token's pairs on that rank, in k order).
-__global__ void __launch_bounds__(256) k_ep_pack(const float *__restrict__ x, int H, int K, const int *ids, const float *weights, int El,
-                                                 int n, const int *pos, __half *send_rows, int *send_meta) {
+__global__ void __launch_bounds__(256) k_ep_pack(const float *__restrict__ x, int H, int K, const int *ids, const float *weights, int E,
+                                                 const int *owner, const int *lidx, int n, const int *pos, __half *send_rows, int *send_meta) {
     const int t = blockIdx.x, tid = threadIdx.x, nch = H / 8, MS = ep_meta_ints(K);
     __shared__ float red[8];
     float4 v[2][2];
@@ -492,8 +492,8 @@ __global__ void __launch_bounds__(256) k_ep_pack(const float *__restrict__ x, in
             int np = 0;
             for (int kk = 0; kk < K; ++kk) {
                 const int e = ids[(long long)t * K + kk];
-                if (e >= 0 && e / El == p) {
-                    m[kEpMetaFixed + 2 * np] = e % El;
+                if (e >= 0 && e < E && owner[e] == p) {
+                    m[kEpMetaFixed + 2 * np] = lidx[e];
                     m[kEpMetaFixed + 2 * np + 1] = __float_as_int(weights[(long long)t * K + kk]);
                     ++np;
                 }
@@ -778,8 +778,9 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
 
 
 // ------------------------------------------------------------------ expert parallel (host)
-// One layer over the ranks of `c`: this rank's T tokens in, its y out; L.blobs holds this
-// rank's experts [rank El, (rank + 1) El), El = L.experts / n (L.experts is the layer's total).
+// One layer over the ranks of `c`: this rank's T tokens in, its y out; L.blobs holds the
+// c->n_local experts this rank owns under the communicator's placement, in ascending id
+// (L.experts is the layer's total).
 // Stages: exact routing; one row per (token, destination rank) bucketed by rank (stable,
 // token-major), packed as an FP16 row with its pair list {local expert, weight} and 2^-k;
 // counts, then rows, exchanged by grouped ncclSend/ncclRecv; the received rows' pairs grouped
@@ -791,8 +792,13 @@ cudaError_t moe_forward_prefill(const MoeLayerDev &L, const float *x, int T, flo
 // before the GEMMs, after gate/up, after down, after the combine.
 int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float *y, int *ids, float *weights, int grid, cudaStream_t s,
                    unsigned *err, std::string *msg, cudaEvent_t *marks) {
-    const int H = L.width, F = L.ff, E = L.experts, K = L.topK, n = c->n, El = E / n;
+    const int H = L.width, F = L.ff, E = L.experts, K = L.topK, n = c->n, El = c->n_local;
     cudaError_t e = cudaSuccess;
+    if (c->placed_experts != E || El < 1) {
+        *msg = "no expert placement for this layer's expert count";
+        return 2;
+    }
+    const int *owner = c->d_place, *lidx = c->d_place + E;
     if (c->failed) {
         *msg = "the expert-parallel communicator failed earlier (" + c->failure + "); call strata_ep_init again";
         return 3;
@@ -846,13 +852,13 @@ int moe_forward_ep(const MoeLayerDev &L, EpComm *c, const float *x, int T, float
     EP_GET(pos, int, 5, TN);
     EP_GET(dchunks, pf::Chunk, 6, TN / pf::kMaxN + n + 2);
     EP_GET(dn, int, 7, 1);
-    pf::k_ep_dest_rows<<<(T + 255) / 256, 256, 0, s>>>(ids, T, K, E, El, n, dest);
+    pf::k_ep_dest_rows<<<(T + 255) / 256, 256, 0, s>>>(ids, T, K, E, owner, n, dest);
     pf::k_pf_count<<<n_tc, 256, 0, s>>>(dest, T, n, n, cc);
     pf::k_pf_scan<<<1, 512, 0, s>>>(cc, n_tc, 0, 0, n, off, dchunks, dn);
     pf::k_pf_place<<<n_tc, 256, 0, s>>>(dest, T, n, n, cc, off, pos);
     EP_GET(send_rows, __half, 8, TN * H);
     EP_GET(send_meta, int, 9, TN * MS);
-    pf::k_ep_pack<<<T, 256, 0, s>>>(x, H, K, ids, weights, El, n, pos, send_rows, send_meta);
+    pf::k_ep_pack<<<T, 256, 0, s>>>(x, H, K, ids, weights, E, owner, lidx, n, pos, send_rows, send_meta);
     EP_MARK(1);
     // 3. counts exchange; one host read of the send offsets and the receive counts
     EP_GET(d_cnt, int, 10, 2 * n);

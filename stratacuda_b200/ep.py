@@ -1,9 +1,11 @@
 """Expert-parallel MoE layer (strata_moe_ep_forward): one process per GPU over NCCL, or n
 virtual ranks on one GPU over the library's loopback transport (tests).
 
-The layer's routed experts are sharded evenly: rank r holds experts [r E/n, (r + 1) E/n) and
-runs them for every rank's tokens that route there; router, shared gate and shared expert are
-replicated. Each rank passes its own tokens and gets back their y, ids and weights. The
+The layer's routed experts are sharded: by default rank r holds experts [r E/n, (r + 1) E/n);
+``ep_set_placement`` gives any other owner per expert, e.g. ``balanced_placement`` of the
+experts' routed rows, so that a skewed router does not load one rank with the popular
+experts. A rank runs its experts for every rank's tokens that route there; router, shared gate
+and shared expert are replicated. Each rank passes its own tokens and gets back their y, ids and weights. The
 reference has no multi-GPU path; the layer's arithmetic is the tensor-core path's (routing
 bit-exact, y within 2e-3 relative L2).
 
@@ -63,6 +65,45 @@ def ep_init_loopback(backends: list[CudaBackend], timeout_ms: int | None = None)
 def ep_set_timeout(backend: CudaBackend, timeout_ms: int) -> None:
     """Bound of every host wait on the peers (default 60 s)."""
     backend._check(backend.lib.strata_ep_set_timeout(backend.ctx, int(timeout_ms)))
+
+
+def ep_set_placement(backend: CudaBackend, owner) -> None:
+    """strata_ep_set_placement: owner[e] = the rank holding expert e (the same on every rank);
+    None restores the contiguous placement."""
+    if owner is None:
+        return
+    own = np.ascontiguousarray(owner, dtype=np.int32)
+    backend._check(backend.lib.strata_ep_set_placement(backend.ctx, int(own.size), own.ctypes.data_as(C.POINTER(C.c_int32))))
+
+
+def balanced_placement(rows: np.ndarray, n_ranks: int, expert_cost: float = 64.0) -> np.ndarray:
+    """Owner rank per expert from the experts' routed rows (longest processing time first: the
+    expert with the most rows goes to the least loaded rank). An expert costs its rows plus
+    ``expert_cost`` rows' worth for its weights, which a rank reads once however few rows it has.
+    Every rank gets at least one expert."""
+    rows = np.asarray(rows, dtype=np.float64)
+    E = rows.size
+    if E < n_ranks:
+        raise ValueError("fewer experts than ranks")
+    cost = rows + expert_cost
+    owner = np.empty(E, np.int32)
+    load = np.zeros(n_ranks)
+    count = np.zeros(n_ranks, np.int64)
+    for e in np.argsort(-cost, kind="stable"):
+        empty = np.flatnonzero(count == 0)
+        r = int(empty[0]) if empty.size and (E - count.sum()) <= empty.size else int(np.argmin(load))
+        owner[e] = r
+        load[r] += cost[e]
+        count[r] += 1
+    return owner
+
+
+def owned_experts(owner, rank: int, experts: int, n_ranks: int) -> np.ndarray:
+    """The experts rank `rank` holds, in blob order (ascending id)."""
+    if owner is None:
+        el = experts // n_ranks
+        return np.arange(rank * el, (rank + 1) * el)
+    return np.flatnonzero(np.asarray(owner) == rank)
 
 
 class EpPeerFailure(RuntimeError):
@@ -128,14 +169,15 @@ class EpMoeLayer:
     shared_blob: Buffer
     shared_gate: Buffer
     router_bias: Buffer | None = None
+    owner: np.ndarray | None = None  # owner rank per expert (None: contiguous)
+
+    @property
+    def local_ids(self) -> np.ndarray:
+        return owned_experts(self.owner, self.rank, self.experts, self.n_ranks)
 
     @property
     def local_experts(self) -> int:
-        return self.experts // self.n_ranks
-
-    @property
-    def first_expert(self) -> int:
-        return self.rank * self.local_experts
+        return int(self.local_ids.size)
 
     def forward(self, x: Buffer, tokens: int, y: Buffer, ids: Buffer, weights: Buffer) -> None:
         b = self.backend
@@ -151,34 +193,47 @@ class EpMoeLayer:
 
     @classmethod
     def synthesize(cls, backend: CudaBackend, rank: int, n_ranks: int, seed: int, layer: int, width: int = 2048, ff: int = 512,
-                   experts: int = 512, top_k: int = 10, zipf: float | None = None) -> "EpMoeLayer":
-        """The seeded synthetic layer of stratacuda_b200.moe.MoeLayer.synthesize, this rank's expert slice only."""
-        if experts % n_ranks:
+                   experts: int = 512, top_k: int = 10, zipf: float | None = None, owner=None) -> "EpMoeLayer":
+        """The seeded synthetic layer of stratacuda_b200.moe.MoeLayer.synthesize, this rank's
+        experts only (``owner``: the placement set with ep_set_placement; None: contiguous)."""
+        if owner is None and experts % n_ranks:
             raise ValueError("experts must be a multiple of the ranks")
         words = blob_layout(width, ff)["blob_bytes"] // 4
         lib, ctx = backend.lib, backend.ctx
-        el = experts // n_ranks
+        mine = owned_experts(owner, rank, experts, n_ranks)
+        el = int(mine.size)
         router = backend.alloc(experts * width, zero=False)
         backend._check(lib.strata_synth_normals(ctx, router.handle, 0, seed, synth.TAG_ROUTER, layer, 0, experts * width, 0.02))
         gate = backend.alloc(width, zero=False)
         backend._check(lib.strata_synth_normals(ctx, gate.handle, 0, seed, synth.TAG_SHARED_GATE, layer, 0, width, 0.02))
         blobs = backend.alloc(el * words, "u32", zero=False)
-        backend._check(lib.strata_synth_blobs(ctx, blobs.handle, 0, seed, layer, rank * el, el, width, ff, 0))
+        i = 0
+        while i < el:  # runs of consecutive ids in one call
+            j = i + 1
+            while j < el and mine[j] == mine[j - 1] + 1:
+                j += 1
+            backend._check(lib.strata_synth_blobs(ctx, blobs.handle, i * words, seed, layer, int(mine[i]), j - i, width, ff, 0))
+            i = j
         shared = backend.alloc(words, "u32", zero=False)
         backend._check(lib.strata_synth_blobs(ctx, shared.handle, 0, seed, layer, 0, 1, width, ff, 1))
         bias = None if zipf is None else backend.alloc(synth.zipf_bias(seed, experts, zipf))
-        return cls(backend, rank, n_ranks, width, ff, experts, top_k, router, blobs, shared, gate, bias)
+        return cls(backend, rank, n_ranks, width, ff, experts, top_k, router, blobs, shared, gate, bias,
+                   None if owner is None else np.asarray(owner, np.int32))
 
 
-def plan_dispatch(ids: np.ndarray, experts: int, n_ranks: int):
+def plan_dispatch(ids: np.ndarray, experts: int, n_ranks: int, placement=None):
     """Host restatement of the dispatch plan the library computes on the device (used by the
     CPU tests). One row per (token, destination rank) that owns at least one of the token's
-    experts (rank r owns [r E/n, (r + 1) E/n)), bucketed by rank, token-major inside a bucket.
-    Returns (row of every (token, rank) in the send order or -1 [T, n], rows per rank [n],
-    pairs: for every send row the token's (k, expert) pairs on that rank in k order)."""
-    el = experts // n_ranks
+    experts (placement[e], by default rank r owns [r E/n, (r + 1) E/n)), bucketed by rank,
+    token-major inside a bucket. Returns (row of every (token, rank) in the send order or -1
+    [T, n], rows per rank [n], pairs: for every send row the token's (k, expert) pairs on that
+    rank in k order)."""
+    if placement is None:
+        placement = np.arange(experts) // (experts // n_ranks)
+    placement = np.asarray(placement)
     T, K = ids.shape
-    owner = np.where((ids >= 0) & (ids < experts), ids // el, -1)
+    valid = (ids >= 0) & (ids < experts)
+    owner = np.where(valid, placement[np.where(valid, ids, 0)], -1)
     has = np.zeros((T, n_ranks), bool)
     for t in range(T):
         for k in range(K):

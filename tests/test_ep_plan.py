@@ -107,3 +107,41 @@ def test_plan_dispatch_is_stable_and_complete():
     assert pos.tolist() == [[0, 4], [1, 5], [2, 6], [3, -1]]
     assert pairs[0] == [(0, 5), (2, 1)] and pairs[4] == [(1, 300)]
     assert pairs[5] == [(0, 300), (2, 511)] and pairs[6] == [(1, 256)] and pairs[3] == [(0, 7), (1, 8), (2, 9)]
+
+
+def test_plan_dispatch_with_a_placement():
+    """Experts on the ranks of an explicit placement (owner per expert) instead of contiguous
+    slices: the rows go where the experts live."""
+    from stratacuda_b200.ep import owned_experts, plan_dispatch
+    owner = np.zeros(512, np.int64)
+    owner[1::2] = 1  # odd experts on rank 1
+    ids = np.array([[5, 300, 1], [300, 2, 511], [-1, 256, 4]])
+    pos, counts, pairs = plan_dispatch(ids, 512, 2, owner)
+    # rank 0 (even): t0 (300), t1 (300, 2), t2 (256, 4); rank 1 (odd): t0 (5, 1), t1 (511)
+    assert counts.tolist() == [3, 2]
+    assert pos.tolist() == [[0, 3], [1, 4], [2, -1]]
+    assert pairs[0] == [(1, 300)] and pairs[3] == [(0, 5), (2, 1)] and pairs[2] == [(1, 256), (2, 4)]
+    assert owned_experts(owner, 1, 512, 2).tolist() == list(range(1, 512, 2))
+
+
+def test_balanced_placement_evens_skewed_rows():
+    """Zipf-skewed rows over 512 experts: the placement's heaviest rank is within a few percent
+    of the mean (contiguous slices put whole hot runs on one rank), every rank owns an expert,
+    and the placement is a function of the rows alone (every rank computes the same)."""
+    from stratacuda_b200.ep import balanced_placement
+    rng = np.random.default_rng(3)
+    bias = np.log(1.0 / np.arange(1, 513) ** 1.1)[rng.permutation(512)]
+    # 4096 tokens, top-10 of Gumbel-perturbed biases: an expert takes at most one row per token
+    ids = np.argsort(-(bias + rng.gumbel(size=(4096, 512))), axis=1)[:, :10]
+    rows = np.bincount(ids.reshape(-1), minlength=512).astype(np.float64)
+    for n in (2, 4, 8):
+        owner = balanced_placement(rows, n)
+        load = np.bincount(owner, weights=rows + 64.0, minlength=n)
+        # no better than the heaviest single expert allows, else within 3% of the mean
+        assert load.max() <= max(1.03 * load.mean(), (rows + 64.0).max() + 1e-9), (n, load)
+        contiguous = np.bincount(np.arange(512) // (512 // n), weights=rows + 64.0, minlength=n)
+        assert load.max() <= contiguous.max()
+        assert np.bincount(owner, minlength=n).min() >= 1
+        assert np.array_equal(owner, balanced_placement(rows.copy(), n))
+    tiny = balanced_placement(np.array([100.0, 0, 0, 0]), 4)
+    assert sorted(tiny.tolist()) == [0, 1, 2, 3]

@@ -80,21 +80,23 @@ def test_ep_two_ranks(T):
         assert err <= TOL, (r, err)
 
 
-def run_loopback(R, T, seed, zipf, timeout_ms=120000):
+def run_loopback(R, T, seed, zipf, timeout_ms=120000, owner=None):
     """R virtual ranks of the expert-parallel layer on GPU 0 (one context and host thread
     each, the library's loopback transport for the exchanges) against the exact single-GPU
-    layer over all R * T tokens."""
+    layer over all R * T tokens. `owner`: an expert placement (None: contiguous slices)."""
     from concurrent.futures import ThreadPoolExecutor
 
     from stratacuda_b200 import _lib as L
     from stratacuda_b200.backend import CudaBackend
-    from stratacuda_b200.ep import EpMoeLayer, ep_init_loopback
+    from stratacuda_b200.ep import EpMoeLayer, ep_init_loopback, ep_set_placement
     from stratacuda_b200.moe import MoeLayer, synth_activations
     H, K = 2048, 10
     bs = [CudaBackend(0) for _ in range(R)]
     try:
         ep_init_loopback(bs, timeout_ms=timeout_ms)
-        layers = [EpMoeLayer.synthesize(b, r, R, seed=seed, layer=0, zipf=zipf) for r, b in enumerate(bs)]
+        for b in bs:
+            ep_set_placement(b, owner)
+        layers = [EpMoeLayer.synthesize(b, r, R, seed=seed, layer=0, zipf=zipf, owner=owner) for r, b in enumerate(bs)]
         xs = [synth_activations(b, 91, T, H, start_token=r * T) for r, b in enumerate(bs)]
         outs = [(b.alloc(T * H), b.alloc(T * K, "i32"), b.alloc(T * K)) for b in bs]
         for b in bs:
@@ -136,6 +138,36 @@ def test_ep_loopback_ranks(R, T):
     ids = run_loopback(R, T, seed=6, zipf=1.1)
     owners = np.bincount((ids // (512 // R)).reshape(-1), minlength=R)
     assert (owners > 0).sum() >= min(R, 2)  # rows really cross between ranks
+
+
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("R,T", [(4, 200), (8, 64)])
+def test_ep_loopback_balanced_placement(R, T):
+    """An explicit placement (balanced by routed rows, so ranks hold different numbers of
+    experts, scattered over the id range): the rows go to the experts' owners, routing stays
+    bit-exact and y within 2e-3 per token."""
+    from stratacuda_b200 import synth
+    from stratacuda_b200.ep import balanced_placement
+    bias = synth.zipf_bias(6, 512, 1.1)
+    rows = np.exp(bias - bias.max()) * 1000.0  # expected rows follow the bias
+    owner = balanced_placement(rows, R)
+    assert len(set(np.bincount(owner, minlength=R).tolist())) > 1  # uneven expert counts
+    run_loopback(R, T, seed=6, zipf=1.1, owner=owner)
+
+
+def test_ep_placement_rejects_bad_owners():
+    from stratacuda_b200.backend import CudaBackend
+    from stratacuda_b200.ep import ep_init_loopback, ep_set_placement
+    bs = [CudaBackend(0) for _ in range(2)]
+    try:
+        ep_init_loopback(bs)
+        with pytest.raises(Exception, match="outside"):
+            ep_set_placement(bs[0], np.full(512, 2))
+        with pytest.raises(Exception, match="owns no expert"):
+            ep_set_placement(bs[0], np.zeros(512, np.int32))
+    finally:
+        for b in bs:
+            b.dispose()
 
 
 @pytest.mark.timeout(300)
