@@ -281,6 +281,32 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
     }
     __syncthreads();
     if (tid == 0) st_tagged(&P.lgx[513 + blockIdx.x], 0.0f, S.tag);  // this CTA holds the tag
+    // The router rows first (they are on the critical path; the x digits are not). Thread t of
+    // warp w holds the reference's lanes 2t and 2t + 1 of row rc + R w (kernels/strata.cu:156-165:
+    // lane l adds x[k] w[k] over k = l mod 64 in increasing k, then the tree partial[l] +=
+    // partial[l + s], s = 32 .. 1): one 8-byte load of each operand per step; the tree's level s
+    // is a shuffle by s / 2 threads, the last level joins the two lanes of thread 0.
+    if (warp < nrows) {
+        const int r = rc + R * warp;
+        if (warp_wait(&S.bar_rows)) {
+            const float2 *W2 = reinterpret_cast<const float2 *>(S.gu[warp]);
+            const float2 *X2 = reinterpret_cast<const float2 *>(S.u.x);
+            float ev = 0.0f, od = 0.0f;
+#pragma unroll 8
+            for (int c = 0; c < NG; ++c) {
+                const float2 w = W2[32 * c + lane], xv = X2[32 * c + lane];
+                ev = __fadd_rn(ev, __fmul_rn(w.x, xv.x));
+                od = __fadd_rn(od, __fmul_rn(w.y, xv.y));
+            }
+#pragma unroll
+            for (int s = 16; s > 0; s >>= 1) {
+                ev = __fadd_rn(ev, __shfl_down_sync(0xffffffffu, ev, s));
+                od = __fadd_rn(od, __shfl_down_sync(0xffffffffu, od, s));
+            }
+            const float v = __fadd_rn(ev, od);
+            if (lane == 0) st_tagged(&P.lgx[r], r < E && L.bias ? __fadd_rn(v, L.bias[r]) : v, S.tag);
+        }
+    }
     {  // largest |x| (NaN ignored, as fmaxf; order-free)
         float mx = 0.0f;
         for (int i = tid; i < kH; i += kThreads) mx = fmaxf(mx, fabsf(S.u.x[i]));
@@ -289,20 +315,6 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
         if (lane == 0) atomicMax(&S.xmax, __float_as_uint(mx));
     }
     __syncthreads();
-    if (warp < nrows) {
-        const int r = rc + R * warp;
-        if (warp_wait(&S.bar_rows)) {
-            const float *W = reinterpret_cast<const float *>(S.gu[warp]);
-            float lo = 0.0f, hi = 0.0f;
-#pragma unroll 8
-            for (int c = 0; c < NG; ++c) {
-                lo = __fadd_rn(lo, __fmul_rn(W[64 * c + lane], S.u.x[64 * c + lane]));
-                hi = __fadd_rn(hi, __fmul_rn(W[64 * c + 32 + lane], S.u.x[64 * c + 32 + lane]));
-            }
-            const float v = tree64(lo, hi);
-            if (lane == 0) st_tagged(&P.lgx[r], r < E && L.bias ? __fadd_rn(v, L.bias[r]) : v, S.tag);
-        }
-    }
     if (slot_cluster)  // x digits: block b = (group, q) of 16 elements, one per thread of warps 4..7 (0.. compute router rows)
         for (int b = tid ^ 128; b < NG * 4; b += kThreads) {
             const int grp = b >> 2, qq = b & 3;
@@ -330,10 +342,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
     __syncthreads();  // logits stored, x digits complete
 
     // ------------------------------------------------------------------ gate/up of warp w's tile
-    // One 128-byte chunk (8 scale groups) of the tile's 16 rows: the partial sums of rows g and
-    // g + 8 (lanes with q = 0 hold them).
-    auto gu_chunk = [&](int w, int c, float &acc0, float &acc1) {
-        acc0 = acc1 = 0.0f;
+    // One 128-byte chunk (8 scale groups) of the tile's 16 rows: the partial sum of row g (lane
+    // q = 0) or row g + 8 (lane q = 1); lanes q = 2, 3 hold nothing of use. The MMA leaves digits
+    // 0 and 1 of rows g and g + 8 in lane q = 0 and digit 2 in lane q = 1: the pair swaps the
+    // pieces of the other one's row (one shuffle), then each lane finishes one row.
+    auto gu_chunk = [&](int w, int c, float &acc) {
+        acc = 0.0f;
         const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
         const bool live = g < 3;  // B columns 0..2: the token's three digits; 3..7 zero
         const unsigned base = smem_u32(S.gu[w] + 2048 * c);
@@ -344,11 +358,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
             const int cc = 2 * gp + (lane >> 4);
             ldsm_x4(base + r * 128 + ((cc ^ (r & 7)) << 4), wd[gp][0], wd[gp][1], wd[gp][2], wd[gp][3]);
         }
-        float s_lo[8], s_hi[8];
+        const bool odd = q & 1;
+        float s_row[8];  // this lane's row: 8 FP16 scales, one 16-byte load
+        {
+            const uint4 v = *reinterpret_cast<const uint4 *>(scl + (g + (odd ? 8 : 0)) * NG);
+            const unsigned wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int gl = 0; gl < 8; ++gl) {
-            s_lo[gl] = __half2float(__ushort_as_half(scl[g * NG + gl]));
-            s_hi[gl] = __half2float(__ushort_as_half(scl[(g + 8) * NG + gl]));
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wv[i]));
+                s_row[2 * i] = f.x;
+                s_row[2 * i + 1] = f.y;
+            }
         }
         uint2 bf[8][2];
 #pragma unroll
@@ -368,32 +388,28 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
             }
 #pragma unroll
         for (int gl = 0; gl < 8; ++gl) {
-            const int d2lo = __shfl_down_sync(0xffffffffu, c4[gl][0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[gl][2], 1);
-            const int xs = S.xsum[8 * c + gl];
-            acc0 = fmaf(s_lo[gl], (float)(c4[gl][0] + 256 * c4[gl][1] + 65536 * d2lo - xs), acc0);
-            acc1 = fmaf(s_hi[gl], (float)(c4[gl][2] + 256 * c4[gl][3] + 65536 * d2hi - xs), acc1);
+            const int send = odd ? c4[gl][0] : c4[gl][2] + 256 * c4[gl][3];
+            const int recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            const int v = odd ? recv + 65536 * c4[gl][2] : c4[gl][0] + 256 * c4[gl][1] + 65536 * recv;
+            acc = fmaf(s_row[gl], (float)(v - S.xsum[8 * c + gl]), acc);
         }
     };
-    // Warp w's tile: chunk sums added in chunk order; lane (g, q = 0) holds rows g and g + 8, gate
-    // row g (even) pairs with up row g + 1 four lanes down. Hidden value of row g: 8 w + g / 2
-    // (+ 4 for row g + 8) of this CTA's 64. Then the stage is free: warps 0..3 fetch the CTA's
-    // down rows into theirs.
+    // Warp w's tile: chunk sums added in chunk order; lane (g, q = 0) holds row g, lane (g, q = 1)
+    // row g + 8; gate row g (even) pairs with up row g + 1 four lanes down. Hidden value of row g:
+    // 8 w + g / 2 (+ 4 for row g + 8) of this CTA's 64. Then the stage is free: warps 0..3 fetch
+    // the CTA's down rows into theirs.
     auto gate_up = [&](int w, int slot) {
         if (warp_wait(&S.bar_gu[w])) {
-            float acc0 = 0.0f, acc1 = 0.0f;
+            float acc = 0.0f;
 #pragma unroll 1
             for (int c = 0; c < CH; ++c) {
-                float p0, p1;
-                gu_chunk(w, c, p0, p1);
-                acc0 = __fadd_rn(acc0, p0);
-                acc1 = __fadd_rn(acc1, p1);
+                float pc;
+                gu_chunk(w, c, pc);
+                acc = __fadd_rn(acc, pc);
             }
-            const float gv0 = acc0 * S.xscale, gv1 = acc1 * S.xscale;
-            const float up0 = __shfl_down_sync(0xffffffffu, gv0, 4), up1 = __shfl_down_sync(0xffffffffu, gv1, 4);
-            if (q == 0 && !(g & 1)) {
-                S.hloc[8 * w + (g >> 1)] = __fmul_rn(ref_silu(gv0, S.exp_tab), up0);
-                S.hloc[8 * w + 4 + (g >> 1)] = __fmul_rn(ref_silu(gv1, S.exp_tab), up1);
-            }
+            const float gv = acc * S.xscale;
+            const float up = __shfl_down_sync(0xffffffffu, gv, 4);
+            if (q < 2 && !(g & 1)) S.hloc[8 * w + 4 * q + (g >> 1)] = __fmul_rn(ref_silu(gv, S.exp_tab), up);
         }
         __syncwarp();
         if (w < 4 && lane == 0) {  // the stage was last read through the generic proxy (ldmatrix)
@@ -410,13 +426,39 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
     // ------------------------------------------------------------------ phase 2: routing (clusters 0..10)
     if (slot_cluster) {
         // the grid-wide exchange: every CTA polls the 513 tagged logit words until each carries
-        // this launch's tag (one L2 round trip once they are there; no arrival counter)
+        // this launch's tag; a thread requests all of its words at once and re-reads only those
+        // still without the tag (one L2 round trip once they are there; no arrival counter)
         float *lg = S.u.r.lg;
-        for (int e = tid; e <= 512; e += kThreads) {
-            float v = 0.0f;
-            if (e <= E && !poll_tagged(&P.lgx[e], S.tag, P.spin_limit, v)) atomicOr(&S.abort_flag, 1);
-            if (e == E) S.sg_raw = v;
-            if (e < 512) lg[e] = e < E ? v : 0.0f;
+        {
+            constexpr int NW = (513 + kThreads - 1) / kThreads;
+            unsigned miss = 0u;
+#pragma unroll
+            for (int i = 0; i < NW; ++i) {
+                const int e = tid + kThreads * i;
+                if (e <= E) miss |= 1u << i;
+                else if (e < 512) lg[e] = 0.0f;
+            }
+            for (unsigned long long it = 0; miss; ++it) {
+                unsigned long long w[NW];
+#pragma unroll
+                for (int i = 0; i < NW; ++i)
+                    if (miss >> i & 1u) w[i] = ld_relaxed64(&P.lgx[tid + kThreads * i]);
+#pragma unroll
+                for (int i = 0; i < NW; ++i)
+                    if ((miss >> i & 1u) && (unsigned)(w[i] >> 32) == S.tag) {
+                        const int e = tid + kThreads * i;
+                        const float v = __uint_as_float((unsigned)w[i]);
+                        if (e == E) S.sg_raw = v;
+                        if (e < 512) lg[e] = e < E ? v : 0.0f;
+                        miss &= ~(1u << i);
+                    }
+                if (!miss) break;
+                if (it > P.spin_limit) {
+                    atomicOr(&S.abort_flag, 1);
+                    break;
+                }
+                if (it > 16) __nanosleep(64);
+            }
         }
         if (tid == 0) S.nzc = 0;
         if (cl == 0 && j == 0)  // every CTA of the grid holds this launch's tag (see the exit)
@@ -426,24 +468,30 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
             }
         __syncthreads();
         if (!S.abort_flag) {
-            route_group<8>(S.u.r.lg, E, K, S.u.r.red, S.u.r.cand, &S.nzc, S.ids, S.u.r.sel, S.wts, 1, S.exp_tab);
-            // (route_group ends with a barrier of all eight warps: every thread sees the ids.)
-            // This cluster's slot is the cl-th valid selection: lane 0 of every warp finds it and
-            // requests the warp's tile at once (its stage held a router row, read through the
-            // generic proxy); the last warp also the down scales.
-            if (cl >= 1 && lane == 0) {
-                int n = 0, e_cl = -1;
-                for (int k = 0; k < K; ++k) {
-                    const int e = S.ids[k];
-                    if (e >= 0 && e < E && ++n == cl) e_cl = e;
+            // This cluster's slot is the cl-th valid selection: as soon as the ids are final (before
+            // the weights), lane 0 of every warp finds it and requests the warp's tile (its stage
+            // held a router row, read through the generic proxy); the last warp also the down scales.
+            route_group<8>(S.u.r.lg, E, K, S.u.r.red, S.u.r.cand, &S.nzc, S.ids, S.u.r.sel, S.wts, 1, S.exp_tab, [&] {
+                if (cl >= 1 && lane == 0) {
+                    int e_cl = -1;
+                    if (S.nzc >= K) {  // every selection valid: slot cl is selection cl - 1
+                        if (cl <= K) e_cl = S.ids[cl - 1];
+                    } else {
+                        int n = 0;
+                        for (int k = 0; k < K; ++k) {
+                            const int e = S.ids[k];
+                            if (e >= 0 && e < E && ++n == cl) e_cl = e;
+                        }
+                    }
+                    if (e_cl >= 0) {
+                        S.slot_expert[cl] = (short)e_cl;  // the same value from every warp
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        issue_tile(warp, cl);
+                        if (warp == kWarps - 1) issue_down_scales(cl);
+                    }
                 }
-                if (e_cl >= 0) {
-                    S.slot_expert[cl] = (short)e_cl;  // the same value from every warp
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    issue_tile(warp, cl);
-                    if (warp == kWarps - 1) issue_down_scales(cl);
-                }
-            }
+            });
+            // (route_group ends with a barrier of all eight warps: every thread sees ids and weights.)
             if (tid == 0) {  // slot s >= 1: the s-th valid selection (ids of one token are distinct)
                 int n = 1;
                 for (int k = 0; k < K; ++k) {
@@ -516,7 +564,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
             for (int t = 0; t < 2; ++t) {
                 const int row0 = 32 * warp + 16 * t;  // the CTA's row of this tile's first row
                 const int brow = row0 - 64 * st + r16;  // row in the stage's box
-                float acc_lo = 0.0f, acc_hi = 0.0f;
+                // lane q = 0: row row0 + g, lane q = 1: row row0 + g + 8 (the digit pieces swapped as in
+                // the gate/up chunks)
+                const bool odd = q & 1;
+                const int myrow = row0 + g + (odd ? 8 : 0);
+                float acc = 0.0f;
 #pragma unroll
                 for (int gp = 0; gp < DG / 2; ++gp) {
                     unsigned w0, w1, w2, w3;
@@ -533,24 +585,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
                             imma(c4, (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                                  (wh >> (4 * h + 2)) & 0x03030303u, b.x, b.y);
                         }
-                        const int d2lo = __shfl_down_sync(0xffffffffu, c4[0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[2], 1);
-                        const int hs = S.u.d.hsum[gl];
-                        const float s_lo = __half2float(__ushort_as_half(S.dns[(row0 + g) * DG + gl]));
-                        const float s_hi = __half2float(__ushort_as_half(S.dns[(row0 + g + 8) * DG + gl]));
-                        acc_lo = fmaf(s_lo, (float)(c4[0] + 256 * c4[1] + 65536 * d2lo - hs), acc_lo);
-                        acc_hi = fmaf(s_hi, (float)(c4[2] + 256 * c4[3] + 65536 * d2hi - hs), acc_hi);
+                        const int send = odd ? c4[0] : c4[2] + 256 * c4[3];
+                        const int recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const int v = odd ? recv + 65536 * c4[2] : c4[0] + 256 * c4[1] + 65536 * recv;
+                        const float sc = __half2float(__ushort_as_half(S.dns[myrow * DG + gl]));
+                        acc = fmaf(sc, (float)(v - S.u.d.hsum[gl]), acc);
                     }
                 }
-                if (q == 0) {
-                    const float lo = acc_lo * S.u.d.hinv, hi = acc_hi * S.u.d.hinv;
-                    if (cl == 0) {
-                        S.res[row0 + g] = lo;
-                        S.res[row0 + g + 8] = hi;
-                    } else {  // the routed slot's rows, tagged, for cluster 0
-                        unsigned long long *dst = P.part + (long long)(cl - 1) * kH + DROWS * j + row0;
-                        st_tagged(dst + g, lo, S.tag);
-                        st_tagged(dst + g + 8, hi, S.tag);
-                    }
+                if (q < 2) {
+                    const float val = acc * S.u.d.hinv;
+                    if (cl == 0) S.res[myrow] = val;
+                    else st_tagged(P.part + (long long)(cl - 1) * kH + DROWS * j + myrow, val, S.tag);  // tagged, for cluster 0
                 }
             }
         }

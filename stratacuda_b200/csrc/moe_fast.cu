@@ -475,9 +475,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
             tokB[cg] = d < 3 && tsB < n_cur ? tok_of(tsB) : -1;
             tokC[cg] = tsC < n_cur ? tok_of(tsC) : -1;
         }
-        float acc[NCG][2];
+        // lane (g, q) finishes row g (even q) or row g + 8 (odd q) of token slot 2 cg + q / 2: the
+        // lane pair swaps the digit pieces of the other one's row (one shuffle per group)
+        float acc[NCG];
 #pragma unroll
-        for (int cg = 0; cg < NCG; ++cg) acc[cg][0] = acc[cg][1] = 0.0f;
+        for (int cg = 0; cg < NCG; ++cg) acc[cg] = 0.0f;
+        const bool odd = q & 1;
         const int r = (lane & 7) + ((lane >> 3) & 1) * 8;
         for (int sub = 0; sub < CPT; ++sub) {
             const int k = ui * CPT + sub, st = k % SGU;
@@ -493,11 +496,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
                 }
                 // expert scales are finite FP16 (rejected on load otherwise, src/model.js:164): the
                 // hardware conversion is exact for them
-                float s_lo[8], s_hi[8];
+                float s_row[8];  // this lane's row: one 16-byte load of 8 FP16 scales
+                {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(scl + (g + (odd ? 8 : 0)) * NG);
+                    const unsigned wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int gl = 0; gl < 8; ++gl) {
-                    s_lo[gl] = __half2float(__ushort_as_half(scl[g * NG + gl]));
-                    s_hi[gl] = __half2float(__ushort_as_half(scl[(g + 8) * NG + gl]));
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wv[i]));
+                        s_row[2 * i] = f.x;
+                        s_row[2 * i + 1] = f.y;
+                    }
                 }
                 // issue order matters (the MMA and ldmatrix statements keep their order): all
                 // operands, then 16 independent MMAs, then the combines
@@ -524,36 +532,35 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
                     const int* xsr = S.xsum[tokC[cg] >= 0 ? tokC[cg] : 0] + sub * 8;
 #pragma unroll
                     for (int gl = 0; gl < 8; ++gl) {
-                        const int d2lo = __shfl_down_sync(0xffffffffu, c4[gl][0], 1), d2hi = __shfl_down_sync(0xffffffffu, c4[gl][2], 1);
-                        const int xs = xsr[gl];
-                        acc[cg][0] = fmaf(s_lo[gl], (float)(c4[gl][0] + 256 * c4[gl][1] + 65536 * d2lo - xs), acc[cg][0]);
-                        acc[cg][1] = fmaf(s_hi[gl], (float)(c4[gl][2] + 256 * c4[gl][3] + 65536 * d2hi - xs), acc[cg][1]);
+                        const int send = odd ? c4[gl][0] : c4[gl][2] + 256 * c4[gl][3];
+                        const int recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const int v = odd ? recv + 65536 * c4[gl][2] : c4[gl][0] + 256 * c4[gl][1] + 65536 * recv;
+                        acc[cg] = fmaf(s_row[gl], (float)(v - xsr[gl]), acc[cg]);
                     }
                 }
             }
             ++gu_done;
             pump();
         }
-        // lanes with even q hold token slot 2cg + q/2; row g (gate when g is even) pairs with
-        // row g+1 (up) four lanes down. Hidden index of row g: 8 warp + g/2 (+4 for row g+8).
-        // Each warp also records its largest |hidden| per token slot (NaN ignored, as fmaxf).
+        // lane (g, q) holds row g (even q) or g + 8 (odd q) of token slot 2cg + q/2; row g (gate
+        // when g is even) pairs with row g+1 (up) four lanes down. Hidden index of row g:
+        // 8 warp + g/2 (+4 for row g+8). Each warp also records its largest |hidden| per token
+        // slot (NaN ignored, as fmaxf).
         const int buf = ui & 1;
 #pragma unroll
         for (int cg = 0; cg < NCG; ++cg) {
             if (cg >= ncg) break;
             const float sc = tokC[cg] >= 0 ? S.xscale[tokC[cg]] : 0.0f;
-            const float gv0 = acc[cg][0] * sc, gv1 = acc[cg][1] * sc;
-            const float up0 = __shfl_down_sync(0xffffffffu, gv0, 4), up1 = __shfl_down_sync(0xffffffffu, gv1, 4);
-            const bool own = !(q & 1) && !(g & 1) && tokC[cg] >= 0;
-            float h0 = 0.0f, h1 = 0.0f;
+            const float gv = acc[cg] * sc;
+            const float up = __shfl_down_sync(0xffffffffu, gv, 4);
+            const bool own = !(g & 1) && tokC[cg] >= 0;
+            float hv = 0.0f;
             if (own) {
-                h0 = __fmul_rn(ref_silu(gv0), up0);
-                h1 = __fmul_rn(ref_silu(gv1), up1);
-                float *hrow = S.hid[buf][2 * cg + (q >> 1)];
-                hrow[8 * warp + (g >> 1)] = h0;
-                hrow[8 * warp + 4 + (g >> 1)] = h1;
+                hv = __fmul_rn(ref_silu(gv), up);
+                S.hid[buf][2 * cg + (q >> 1)][8 * warp + (odd ? 4 : 0) + (g >> 1)] = hv;
             }
-            float m = fmaxf(fmaxf(0.0f, fabsf(h0)), fabsf(h1));
+            float m = fmaxf(0.0f, fabsf(hv));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));

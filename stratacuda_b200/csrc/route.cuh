@@ -144,9 +144,12 @@ static __device__ __forceinline__ ulonglong2 warp_sort64_desc(ulonglong2 k, int 
     return make_ulonglong2(k0, k1);
 }
 
-template <int W>
+// `after_ids` runs on every thread of the group once the ids are final, before the weights
+// (the one-token decode layer requests its expert's tiles there).
+template <int W, class AfterIds>
 __device__ __forceinline__ void route_group(float *lg, int experts, int topK, float *red, unsigned long long *cand, int *nzc,
-                                            int *ids, float *sel, float *weights, int bar_id, const unsigned long long *exp_tab = nullptr) {
+                                            int *ids, float *sel, float *weights, int bar_id, const unsigned long long *exp_tab,
+                                            AfterIds &&after_ids) {
     constexpr int T = 32 * W, NPT = 512 / T;
     const int i = threadIdx.x % T, lane = threadIdx.x & 31, wg = i >> 5;
     float v[NPT];
@@ -221,6 +224,7 @@ __device__ __forceinline__ void route_group(float *lg, int experts, int topK, fl
         sel[i] = -1.0f;
     }
     group_sync<W>(bar_id);
+    after_ids();
     if (i < topK) {
         float denom = 0.0f;  // sequential, in selection order
         for (int k = 0; k < topK; ++k) denom = __fadd_rn(denom, sel[k]);
@@ -228,6 +232,11 @@ __device__ __forceinline__ void route_group(float *lg, int experts, int topK, fl
         weights[i] = __fdiv_rn(sel[i], denom);
     }
     group_sync<W>(bar_id);
+}
+template <int W>
+__device__ __forceinline__ void route_group(float *lg, int experts, int topK, float *red, unsigned long long *cand, int *nzc,
+                                            int *ids, float *sel, float *weights, int bar_id, const unsigned long long *exp_tab = nullptr) {
+    route_group<W>(lg, experts, topK, red, cand, nzc, ids, sel, weights, bar_id, exp_tab, [] {});
 }
 
 }  // namespace strata
