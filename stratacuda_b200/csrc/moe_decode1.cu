@@ -377,13 +377,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
             for (int h = 0; h < 2; ++h) bf[gl][h] = live ? S.xf[(((8 * c + gl) * 2 + h) * 4 + q) * 3 + g] : make_uint2(0u, 0u);
         int c4[8][4];
 #pragma unroll
-        for (int gl = 0; gl < 8; ++gl) c4[gl][0] = c4[gl][1] = c4[gl][2] = c4[gl][3] = 0;
-#pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int gl = 0; gl < 8; ++gl) {
                 const unsigned wl = wd[gl >> 1][(gl & 1) ? 2 : 0], wh = wd[gl >> 1][(gl & 1) ? 3 : 1];
-                imma(c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                imma_acc(h > 0, c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                      (wh >> (4 * h + 2)) & 0x03030303u, bf[gl][h].x, bf[gl][h].y);
             }
 #pragma unroll
@@ -578,11 +576,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
                     for (int hh = 0; hh < 2; ++hh) {
                         const int gl = 2 * gp + hh;
                         const unsigned wl = hh ? w2 : w0, wh = hh ? w3 : w1;
-                        int c4[4] = {0, 0, 0, 0};
+                        int c4[4];
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const uint2 b = live ? S.u.d.hf[((gl * 2 + h) * 4 + q) * 3 + g] : make_uint2(0u, 0u);
-                            imma(c4, (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                            imma_acc(h > 0, c4, (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                                  (wh >> (4 * h + 2)) & 0x03030303u, b.x, b.y);
                         }
                         const int send = odd ? c4[0] : c4[2] + 256 * c4[3];

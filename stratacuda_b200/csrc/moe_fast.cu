@@ -520,13 +520,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
                             bf[gl][h] = tokB[cg] >= 0 ? S.xf[((((sub * 8 + gl) * 2 + h) * kMaxTokens + tokB[cg]) * 4 + q) * 3 + d] : make_uint2(0u, 0u);
                     int c4[8][4];
 #pragma unroll
-                    for (int gl = 0; gl < 8; ++gl) c4[gl][0] = c4[gl][1] = c4[gl][2] = c4[gl][3] = 0;
-#pragma unroll
                     for (int h = 0; h < 2; ++h)
 #pragma unroll
                         for (int gl = 0; gl < 8; ++gl) {
                             const unsigned wl = w[gl >> 1][(gl & 1) ? 2 : 0], wh = w[gl >> 1][(gl & 1) ? 3 : 1];
-                            imma(c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                            imma_acc(h > 0, c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                                  (wh >> (4 * h + 2)) & 0x03030303u, bf[gl][h].x, bf[gl][h].y);
                         }
                     const int* xsr = S.xsum[tokC[cg] >= 0 ? tokC[cg] : 0] + sub * 8;
@@ -639,13 +637,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_fast(const __grid_constant_
                     if (cg >= ncg) break;
                     int c4[MB][4];
 #pragma unroll
-                    for (int m = 0; m < MB; ++m) c4[m][0] = c4[m][1] = c4[m][2] = c4[m][3] = 0;
-#pragma unroll
                     for (int h = 0; h < 2; ++h)
 #pragma unroll
                         for (int m = 0; m < MB; ++m) {
                             const unsigned wl = wt[m][0], wh = wt[m][1];
-                            imma(c4[m], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                            imma_acc(h > 0, c4[m], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                                  (wh >> (4 * h + 2)) & 0x03030303u, hb[cg][h].x, hb[cg][h].y);
                         }
                     float *pr = P.part + ((long long)j * PP + prow[cg]) * H + RW * warp + 16 * mb + g;

@@ -247,13 +247,11 @@ __device__ __forceinline__ void mma_chunk(unsigned code, int col0, const unsigne
             for (int h = 0; h < 2; ++h) bf[gl][h] = tsB[cg] >= 0 ? dg[(((g0 + gl) * 2 + h) * 4 + q) * 3 + d] : make_uint2(0u, 0u);
         int c4[GPC][4];
 #pragma unroll
-        for (int gl = 0; gl < GPC; ++gl) c4[gl][0] = c4[gl][1] = c4[gl][2] = c4[gl][3] = 0;
-#pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int gl = 0; gl < GPC; ++gl) {
                 const unsigned wl = w[gl >> 1][(gl & 1) ? 2 : 0], wh = w[gl >> 1][(gl & 1) ? 3 : 1];
-                imma(c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
+                imma_acc(h > 0, c4[gl], (wl >> (4 * h)) & 0x03030303u, (wh >> (4 * h)) & 0x03030303u, (wl >> (4 * h + 2)) & 0x03030303u,
                      (wh >> (4 * h + 2)) & 0x03030303u, bf[gl][h].x, bf[gl][h].y);
             }
         // lane (g, q) holds rows g and g + 8 at columns 2q, 2q + 1: digits 0, 1 (even q) or 2 and
