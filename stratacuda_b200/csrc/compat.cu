@@ -96,6 +96,61 @@ __global__ void k_project(Grid g, FB X, FB W, FB Y, int cols, int rows, int toke
     if (t == 0) Y.set((long long)token * outputStride + outputOffset + row, r, err);
 }
 
+// The same projection for one token (decode), bandwidth-shaped: a half-warp per output row, 16
+// rows per block. Thread u of a half-warp holds the reference's lanes 4u .. 4u + 3 (elements
+// 4u + 64k .. 4u + 64k + 3 of round k: one 16-byte load of the weights and one of the input
+// per round, eight rounds in flight), each lane's products added in round order from 0. The
+// tree partial[l] += partial[l + s] (s = 32 .. 4) is a shuffle by s / 4 threads within the
+// half-warp; s = 2 and 1 join the lanes of thread 0. Same sums and roundings as k_project.
+// The host launches it when cols is a multiple of 64, both rows are 16-byte aligned and the
+// buffers cover every row read.
+constexpr int kGemvThreads = 256, kGemvRows = kGemvThreads / 16;
+__global__ void __launch_bounds__(kGemvThreads) k_project_gemv(FB X, FB W, FB Y, int cols, int rows, int outputOffset, unsigned *err) {
+    const int hw = threadIdx.x >> 4, u = threadIdx.x & 15;
+    const int row = blockIdx.x * kGemvRows + hw;
+    if (row >= rows) return;  // whole half-warps leave together (the shuffles use 16-lane masks)
+    const unsigned mask = 0xffffu << (threadIdx.x & 16);
+    const float4 *w4 = reinterpret_cast<const float4 *>(W.p + (long long)row * cols) + u;
+    const float4 *x4 = reinterpret_cast<const float4 *>(X.p) + u;
+    const int R = cols / 64;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    int k = 0;
+    for (; k + 8 <= R; k += 8) {
+        float4 wv[8], xv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            wv[i] = __ldcs(w4 + 16 * (k + i));  // streamed once: no reuse in the caches
+            xv[i] = __ldg(x4 + 16 * (k + i));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            a0 = __fadd_rn(a0, __fmul_rn(wv[i].x, xv[i].x));
+            a1 = __fadd_rn(a1, __fmul_rn(wv[i].y, xv[i].y));
+            a2 = __fadd_rn(a2, __fmul_rn(wv[i].z, xv[i].z));
+            a3 = __fadd_rn(a3, __fmul_rn(wv[i].w, xv[i].w));
+        }
+    }
+    for (; k < R; ++k) {
+        const float4 wv = __ldcs(w4 + 16 * k), xv = __ldg(x4 + 16 * k);
+        a0 = __fadd_rn(a0, __fmul_rn(wv.x, xv.x));
+        a1 = __fadd_rn(a1, __fmul_rn(wv.y, xv.y));
+        a2 = __fadd_rn(a2, __fmul_rn(wv.z, xv.z));
+        a3 = __fadd_rn(a3, __fmul_rn(wv.w, xv.w));
+    }
+#pragma unroll
+    for (int s = 8; s > 0; s >>= 1) {  // reference levels 32, 16, 8, 4
+        a0 = __fadd_rn(a0, __shfl_down_sync(mask, a0, s, 16));
+        a1 = __fadd_rn(a1, __shfl_down_sync(mask, a1, s, 16));
+        a2 = __fadd_rn(a2, __shfl_down_sync(mask, a2, s, 16));
+        a3 = __fadd_rn(a3, __shfl_down_sync(mask, a3, s, 16));
+    }
+    if (u == 0) {
+        a0 = __fadd_rn(a0, a2);  // level 2
+        a1 = __fadd_rn(a1, a3);
+        Y.set((long long)outputOffset + row, __fadd_rn(a0, a1), err);  // level 1
+    }
+}
+
 // The same projection for dispatches with few (row, token) pairs: one block per pair stages the
 // weight row and the input row in shared memory with all its threads (every load in flight at
 // once), then one warp forms the reference's strided sums and tree from shared memory. The host
@@ -398,6 +453,15 @@ cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
     // few (row, token) pairs of long rows: one staging block per pair (the pairs the dispatch
     // names, rows < g[0] and tokens < g[1]; z repeats them)
     const long long cols = a[3].i, rows = std::min<long long>(a[4].i, g[0]), tokens = std::min<long long>(a[5].i, g[1]);
+    const bool aligned16 = ((reinterpret_cast<uintptr_t>(a[0].ptr) | reinterpret_cast<uintptr_t>(a[1].ptr)) & 15) == 0;
+    // one token, many rows: a half-warp per row, 16-byte streaming loads (fewer rows: the
+    // staging blocks below have every load of a row in flight at once)
+    if (tokens == 1 && rows > 2048 && cols >= 64 && cols % 64 == 0 && aligned16 && a[1].len >= rows * cols && a[0].len >= cols &&
+        (long long)a[7].i + rows <= a[2].len && a[7].i >= 0) {
+        k_project_gemv<<<(unsigned)((rows + kGemvRows - 1) / kGemvRows), kGemvThreads, 0, s>>>(F(0), F(1), F(2), (int)cols, (int)rows,
+                                                                                                 a[7].i, err);
+        return cudaGetLastError();
+    }
     const size_t bytes = (size_t)cols * 8;
     if (rows * tokens <= 2048 && cols >= 512 && bytes <= 200 * 1024 && a[1].len >= rows * cols && a[0].len >= tokens * cols &&
         rows > 0 && tokens > 0) {

@@ -71,11 +71,21 @@ __device__ __forceinline__ float lane_dot(const float *w, const float *x, int co
 // at a time where both sides allow it.
 __device__ __forceinline__ void stage_row(float *dst, const float *src, int n) {
     if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
-        const int n4 = n / 4;
+        const int n4 = n / 4, bd = blockDim.x;
         const float4 *s4 = reinterpret_cast<const float4 *>(src);
         float4 *d4 = reinterpret_cast<float4 *>(dst);
-        for (int k = threadIdx.x; k < n4; k += blockDim.x) d4[k] = s4[k];
-        for (int k = n4 * 4 + threadIdx.x; k < n; k += blockDim.x) dst[k] = src[k];
+        // eight 16-byte loads of a thread in flight before their stores (one round trip for
+        // rows up to 8 * 16 * blockDim bytes)
+        for (int k0 = threadIdx.x; k0 < n4; k0 += 8 * bd) {
+            float4 v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (k0 + i * bd < n4) v[i] = s4[k0 + i * bd];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (k0 + i * bd < n4) d4[k0 + i * bd] = v[i];
+        }
+        for (int k = n4 * 4 + threadIdx.x; k < n; k += bd) dst[k] = src[k];
     } else {
         for (int k = threadIdx.x; k < n; k += blockDim.x) dst[k] = src[k];
     }

@@ -833,25 +833,39 @@ constexpr int kHcThreads = 128;
 
 // strata_hc_in: Norm = RMSNorm of the `streams` residual rows (gamma row = stream), then
 // Down = down . Norm (rank rows of width*streams) and Inject = inject . Norm (streams rows). One
-// block per output row stages the residual and its weight row in shared memory together, forms the
-// norm there (one warp per stream row, as k_norm does) and one warp takes the row's ordered dot.
-// Block 0 also writes the norm.
+// block per output row copies the residual, its weight row and the gammas into shared memory
+// with asynchronous 16-byte copies (all in flight at once), forms the norm there (one warp per
+// stream row, as k_norm does) and one warp takes the row's ordered dot. Block 0 also writes the
+// norm.
 constexpr int kHcInThreads = 256;
 __global__ void __launch_bounds__(kHcInThreads) k_hc_in(FB Residual, FB NormW, FB DownW, FB InjectW, FB Norm, FB Down, FB Inject, int width,
                                                         int streams, int rank, float epsilon) {
-    extern __shared__ __align__(16) float hc_in[];  // [hc] residual -> norm, then [hc] the weight row
+    extern __shared__ __align__(16) float hc_in[];  // [hc] residual -> norm, [hc] the weight row, [hc] the gammas
     __shared__ float inv_s[64];
     const int warp = threadIdx.x / 32, t = threadIdx.x & 31, hc = width * streams, j = blockIdx.x;
-    float *x = hc_in, *w = hc_in + hc;
-    stage_row(x, Residual.p, hc);
-    stage_row(w, j < rank ? DownW.p + (long long)j * hc : InjectW.p + (long long)(j - rank) * hc, hc);
+    float *x = hc_in, *w = hc_in + hc, *gam = hc_in + 2 * (size_t)hc;
+    const float *wsrc = j < rank ? DownW.p + (long long)j * hc : InjectW.p + (long long)(j - rank) * hc;
+    if (((reinterpret_cast<uintptr_t>(Residual.p) | reinterpret_cast<uintptr_t>(wsrc) | reinterpret_cast<uintptr_t>(NormW.p)) & 15) == 0 &&
+        hc % 4 == 0) {
+        for (int k = 4 * threadIdx.x; k < hc; k += 4 * kHcInThreads) {
+            copy16_async(x + k, Residual.p + k);
+            copy16_async(w + k, wsrc + k);
+            copy16_async(gam + k, NormW.p + k);
+        }
+        copy_commit();
+        copy_wait<0>();
+    } else {
+        stage_row(x, Residual.p, hc);
+        stage_row(w, wsrc, hc);
+        stage_row(gam, NormW.p, hc);
+    }
     __syncthreads();
     for (int c = warp; c < streams; c += kHcInThreads / 32) {
         const float ss = lane_dot(x + (size_t)c * width, x + (size_t)c * width, width, t);
         if (t == 0) inv_s[c] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)width), epsilon)));
     }
     __syncthreads();
-    for (int k = threadIdx.x; k < hc; k += kHcInThreads) x[k] = __fmul_rn(__fmul_rn(x[k], inv_s[k / width]), NormW.p[k]);
+    for (int k = threadIdx.x; k < hc; k += kHcInThreads) x[k] = __fmul_rn(__fmul_rn(x[k], inv_s[k / width]), gam[k]);
     __syncthreads();
     if (j == 0)
         for (int k = threadIdx.x; k < hc; k += kHcInThreads) Norm.p[k] = x[k];
@@ -866,7 +880,9 @@ __global__ void __launch_bounds__(kHcInThreads) k_hc_in(FB Residual, FB NormW, F
 
 // strata_hc_out: Mixed[d] = sum_c Norm[c, d] * sigmoid(up[c, d] . lo) / streams with
 // lo = SiLU(Down / streams) (elementwise mode 1, scale = 1/streams). Every block forms lo in shared
-// memory; one warp per output column d computes its `streams` gate rows and the mix.
+// memory; one warp per output column d computes its `streams` gate rows and the mix. With rank
+// 256 and at most 4 streams a lane loads its elements of every gate row first (one round trip),
+// then each row's two reference-lane sums run in order, as lane_dot's.
 __global__ void __launch_bounds__(kHcThreads) k_hc_out(FB Norm, FB Down, FB UpW, FB Mixed, int width, int streams, int rank, float scale) {
     extern __shared__ __align__(16) float hc_lo[];  // [rank]
     const int warp = threadIdx.x / 32, t = threadIdx.x & 31;
@@ -875,10 +891,38 @@ __global__ void __launch_bounds__(kHcThreads) k_hc_out(FB Norm, FB Down, FB UpW,
     const int d = blockIdx.x * (kHcThreads / 32) + warp;
     if (d >= width) return;
     float v = 0.0f;
-    for (int c = 0; c < streams; ++c) {
-        const long long row = (long long)c * width + d;
-        const float gate = __shfl_sync(0xffffffffu, lane_dot(UpW.p + row * rank, hc_lo, rank, t), 0);
-        v = __fadd_rn(v, __fmul_rn(Norm.p[row], ref_sigmoid(gate)));
+    if (rank == 256 && streams <= 4) {
+        float wv[4][8], nv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if (c >= streams) break;
+            const long long row = (long long)c * width + d;
+            const float *wr = UpW.p + row * rank;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                wv[c][2 * k] = __ldg(wr + t + 64 * k);
+                wv[c][2 * k + 1] = __ldg(wr + t + 32 + 64 * k);
+            }
+            nv[c] = __ldg(Norm.p + row);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if (c >= streams) break;
+            float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                lo = __fadd_rn(lo, __fmul_rn(wv[c][2 * k], hc_lo[t + 64 * k]));
+                hi = __fadd_rn(hi, __fmul_rn(wv[c][2 * k + 1], hc_lo[t + 32 + 64 * k]));
+            }
+            const float gate = __shfl_sync(0xffffffffu, tree64(lo, hi), 0);
+            v = __fadd_rn(v, __fmul_rn(nv[c], ref_sigmoid(gate)));
+        }
+    } else {
+        for (int c = 0; c < streams; ++c) {
+            const long long row = (long long)c * width + d;
+            const float gate = __shfl_sync(0xffffffffu, lane_dot(UpW.p + row * rank, hc_lo, rank, t), 0);
+            v = __fadd_rn(v, __fmul_rn(Norm.p[row], ref_sigmoid(gate)));
+        }
     }
     if (t == 0) Mixed.p[d] = __fdiv_rn(v, (float)streams);
 }
@@ -958,7 +1002,8 @@ cudaError_t L_attention_at(const KArg *a, const unsigned g[3], cudaStream_t s, u
 }
 cudaError_t L_hc_in(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     const int width = a[7].i, streams = a[8].i, rank = a[9].i;
-    const size_t bytes = (size_t)width * streams * 8;
+    const size_t bytes = (size_t)width * streams * 12;  // residual, weight row and gammas staged
+    if (streams < 1 || streams > 64 || bytes > 227 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(k_hc_in, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return e;
     k_hc_in<<<(unsigned)(rank + streams), kHcInThreads, bytes, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), F(6), width, streams, rank, a[10].f);

@@ -347,7 +347,7 @@ class StrataEngine:
     def hc(self, prefix: str, inject: bool = True):
         g, o = self.g, self.ops
         hc_cols = g["width"] * g["streams"]
-        if (inject and getattr(self.b, "kind", None) == "cuda" and g["streams"] <= 64 and hc_cols * 8 <= 200 * 1024
+        if (inject and getattr(self.b, "kind", None) == "cuda" and g["streams"] <= 64 and hc_cols * 12 <= 200 * 1024
                 and g["rank"] * 4 <= 48 * 1024):  # the fused entries' staging limits; the six dispatches below otherwise
             # the same six dispatches' values in two launches (strata_hc_in / strata_hc_out)
             hc = g["width"] * g["streams"]
