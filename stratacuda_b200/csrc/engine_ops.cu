@@ -358,6 +358,30 @@ __global__ void __launch_bounds__(kArgmaxThreads) k_argmax(FB Logits, IB Token, 
 
 // ---------------------------------------------------------------- attention
 
+// Sixteen 16-byte loads (p[0 .. 15]) issued back to back, one statement: all in flight at once.
+__device__ __forceinline__ void ld16_v4(const float4 *p, float4 (&v)[16]) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+        asm volatile(
+            "ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%16];\n\t"
+            "ld.global.nc.v4.f32 {%4, %5, %6, %7}, [%16 + 16];\n\t"
+            "ld.global.nc.v4.f32 {%8, %9, %10, %11}, [%16 + 32];\n\t"
+            "ld.global.nc.v4.f32 {%12, %13, %14, %15}, [%16 + 48];"
+            : "=f"(v[4 * g].x), "=f"(v[4 * g].y), "=f"(v[4 * g].z), "=f"(v[4 * g].w), "=f"(v[4 * g + 1].x), "=f"(v[4 * g + 1].y),
+              "=f"(v[4 * g + 1].z), "=f"(v[4 * g + 1].w), "=f"(v[4 * g + 2].x), "=f"(v[4 * g + 2].y), "=f"(v[4 * g + 2].z),
+              "=f"(v[4 * g + 2].w), "=f"(v[4 * g + 3].x), "=f"(v[4 * g + 3].y), "=f"(v[4 * g + 3].z), "=f"(v[4 * g + 3].w)
+            : "l"(p + 4 * g)
+            : "memory");
+}
+// Sixteen 4-byte loads at p[i] (p[i] null: 0), issued back to back.
+__device__ __forceinline__ void ld16_f(const float *const (&p)[16], float (&v)[16]) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        if (p[i]) asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v[i]) : "l"(p[i]) : "memory");
+        else v[i] = 0.0f;
+    }
+}
+
 // kernels/strata.cu:334-356 (decode: the Cells list, count cells) and :512-534 (prompt: query
 // token = y, its causal prefix of position + token + 1 cells). One CTA per (head, query token)
 // computes what the reference's (head, 64-wide tile) workgroups compute, each value by the same
@@ -397,6 +421,18 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Key
             const float4 *k4 = reinterpret_cast<const float4 *>(Keys.p + kb), *q4 = reinterpret_cast<const float4 *>(Q.p + qbase);
             const int d4 = dim / 4;
             int j = 0;
+            for (; j + 16 <= d4; j += 16) {  // sixteen key loads in flight (one round trip for a 256-wide head)
+                float4 kv[16];
+                ld16_v4(k4 + j, kv);
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const float4 qv = q4[j + u];
+                    score = __fadd_rn(score, __fmul_rn(qv.x, kv[u].x));
+                    score = __fadd_rn(score, __fmul_rn(qv.y, kv[u].y));
+                    score = __fadd_rn(score, __fmul_rn(qv.z, kv[u].z));
+                    score = __fadd_rn(score, __fmul_rn(qv.w, kv[u].w));
+                }
+            }
             for (; j + 4 <= d4; j += 4) {
                 float4 kv[4], qv[4];
 #pragma unroll
@@ -451,6 +487,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Key
     for (int d = tid; d < dmax; d += kAttnThreads) {  // C
         float value = 0.0f;
         int c = 0;
+        for (; c + 64 <= n; c += 64) {  // 64 value loads in flight ahead of the ordered sum
+            float vv[4][16];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+                const float *ptr[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const long long r = value_row[c + 16 * q4 + u];
+                    ptr[u] = r >= 0 ? Values.p + r + d : nullptr;
+                }
+                ld16_f(ptr, vv[q4]);
+            }
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+                for (int u = 0; u < 16; ++u) value = __fadd_rn(value, __fmul_rn(scores[c + 16 * q4 + u], vv[q4][u]));
+        }
         for (; c + 16 <= n; c += 16) {  // sixteen value loads in flight ahead of the ordered sum
             float vv[16];
 #pragma unroll
@@ -467,6 +520,144 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Key
         }
         Y.set(qbase + d, __fdiv_rn(value, total), err);
     }
+}
+
+// The same attention for a few query tokens, split over an 8-CTA cluster per (head, query
+// token) so that every SM streams a share of the keys and values (one CTA per head left 16 SMs
+// reading the whole cache). Same values, same order:
+//   A. CTA r scores cells [r m, r m + m) (m = n / 8 rounded up), each one thread's in-order sum
+//      over the head dimension, times `scale`;
+//   the cluster's CTAs then copy each other's scores from distributed shared memory;
+//   B. one warp per CTA takes the maximum and the exponential sum in the reference's lane order
+//      and tree (every CTA the same values);
+//   C. CTA r forms output dimensions [r dim / 8, (r + 1) dim / 8): each one thread's in-order sum
+//      over all cells, from value rows staged in shared memory by the whole CTA (64 cells at a
+//      time, double-buffered), divided by the sum.
+// Requires dim a multiple of 64 and at most 256, 16-byte aligned keys and values. A key or value
+// row outside its buffer reads as zeros and is reported.
+constexpr int kAcThreads = 256, kAcCluster = 8, kAcChunk = 64;
+__device__ __forceinline__ unsigned ac_rank() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void ac_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ac_ld_peer(const float *local, unsigned rank) {
+    unsigned remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"((unsigned)__cvta_generic_to_shared(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+__global__ void __cluster_dims__(kAcCluster, 1, 1) __launch_bounds__(kAcThreads)
+    k_attention_cl(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads, int kvHeads, int count, int position, float scale,
+                   int batch, IB Pos, unsigned *err) {
+    __shared__ float scores[kMaxCells];
+    __shared__ long long value_row[kMaxCells];
+    __shared__ __align__(16) float vst[2][kAcChunk][32];  // value rows' slices of this CTA's dimensions
+    __shared__ float total_s;
+    const unsigned rank = ac_rank(), h = blockIdx.x / kAcCluster, token = blockIdx.y;
+    const int tid = threadIdx.x;
+    if (Pos.n > 0) position = Pos.get(0, err);
+    const long long n = batch ? (long long)position + token + 1 : count;
+    // every CTA of the cluster takes the same branch: the cluster barriers below are reached by all
+    const bool run = (int)h < heads && n >= 1 && n <= kMaxCells;
+    if (!run && tid == 0 && (int)h < heads) raise_error(err, kErrIndex);
+    const int kh = run ? (int)h / (heads / kvHeads) : 0;
+    const long long qbase = batch ? ((long long)token * heads + h) * dim : (long long)h * dim;
+    const bool q_ok = covers(Q, qbase, dim);
+    const int m = run ? (int)((n + kAcCluster - 1) / kAcCluster) : 0;
+    const int c0 = (int)rank * m, c1 = run ? (int)min(n, (long long)c0 + m) : 0;
+    if (run) {
+        for (int c = tid; c < n; c += kAcThreads) {  // every cell's value row (and its checks, once: by its scorer)
+            const long long cell = batch ? c : (long long)Cells.get(c, err);
+            const long long kb = (cell * kvHeads + kh) * dim;
+            const bool key_ok = cell >= 0 && covers(Keys, kb, dim), value_ok = cell >= 0 && covers(Values, kb, dim);
+            value_row[c] = value_ok ? kb : -1;
+            if (c >= c0 && c < c1) {  // A
+                if (!key_ok || !value_ok || !q_ok) raise_error(err, kErrIndex);
+                float score = 0.0f;
+                if (key_ok && q_ok) {
+                    const float4 *k4 = reinterpret_cast<const float4 *>(Keys.p + kb), *q4 = reinterpret_cast<const float4 *>(Q.p + qbase);
+                    for (int j = 0; j < dim / 4; j += 16) {
+                        float4 kv[16];
+                        ld16_v4(k4 + j, kv);
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) {
+                            const float4 qv = q4[j + u];
+                            score = __fadd_rn(score, __fmul_rn(qv.x, kv[u].x));
+                            score = __fadd_rn(score, __fmul_rn(qv.y, kv[u].y));
+                            score = __fadd_rn(score, __fmul_rn(qv.z, kv[u].z));
+                            score = __fadd_rn(score, __fmul_rn(qv.w, kv[u].w));
+                        }
+                    }
+                }
+                scores[c] = __fmul_rn(score, scale);
+            }
+        }
+    }
+    ac_cluster_sync();  // every CTA's scores are in its shared memory
+    if (run)
+        for (int c = tid; c < n; c += kAcThreads)
+            if (c < c0 || c >= c1) scores[c] = ac_ld_peer(&scores[c], (unsigned)(c / m));
+    ac_cluster_sync();  // every peer read done: the scores may be overwritten
+    if (!run) return;
+    if (tid < 32) {  // B
+        float mlo = -3.402823e38f, mhi = -3.402823e38f;
+        for (int c = tid; c < n; c += STRATA_LANES) mlo = fmaxf(mlo, scores[c]);
+        for (int c = tid + 32; c < n; c += STRATA_LANES) mhi = fmaxf(mhi, scores[c]);
+        const float mx = __shfl_sync(0xffffffffu, max_tree64(mlo, mhi), 0);
+        float slo = 0.0f, shi = 0.0f;
+        for (int c = tid; c < n; c += STRATA_LANES) {
+            const float p = ref_expf(__fsub_rn(scores[c], mx));
+            scores[c] = p;
+            slo = __fadd_rn(slo, p);
+        }
+        for (int c = tid + 32; c < n; c += STRATA_LANES) {
+            const float p = ref_expf(__fsub_rn(scores[c], mx));
+            scores[c] = p;
+            shi = __fadd_rn(shi, p);
+        }
+        const float total = tree64(slo, shi);
+        if (tid == 0) total_s = total;
+    }
+    __syncthreads();
+    // C: dimensions [d0, d0 + dp) of this CTA, 64 cells' slices staged per step
+    const int dp = dim / kAcCluster, d0 = (int)rank * dp;
+    const int dmax = (int)min((long long)dim, (long long)g.y * STRATA_LANES);  // the dispatched 64-wide tiles
+    const int nv = dp / 4;  // 16-byte pieces of a row's slice
+    auto stage = [&](int step, int buf) {
+        for (int i = tid; i < kAcChunk * nv; i += kAcThreads) {
+            const int cc = i / nv, piece = i % nv, c = step * kAcChunk + cc;
+            float *dst = &vst[buf][cc][4 * piece];
+            const long long r = c < n ? value_row[c] : -1;
+            if (r >= 0) copy16_async(dst, Values.p + r + d0 + 4 * piece);
+            else *reinterpret_cast<float4 *>(dst) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        copy_commit();
+    };
+    const int steps = (int)((n + kAcChunk - 1) / kAcChunk);
+    const float total = total_s;
+    float value = 0.0f;
+    stage(0, 0);
+    for (int st = 0; st < steps; ++st) {
+        if (st + 1 < steps) {
+            stage(st + 1, (st + 1) & 1);
+            copy_wait<1>();
+        } else {
+            copy_wait<0>();
+        }
+        __syncthreads();
+        if (tid < dp) {
+            const int cend = (int)min((long long)kAcChunk, n - (long long)st * kAcChunk);
+            const float *sc = scores + st * kAcChunk;
+            for (int cc = 0; cc < cend; ++cc) value = __fadd_rn(value, __fmul_rn(sc[cc], vst[st & 1][cc][tid]));
+        }
+        __syncthreads();  // the buffer is refilled two steps on
+    }
+    if (tid < dp && d0 + tid < dmax) Y.set(qbase + d0 + tid, __fdiv_rn(value, total), err);
 }
 
 // The prompt form for a group of query heads that share one KV head (GQA): one block per (KV
@@ -574,6 +765,12 @@ __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q,
     }
 }
 
+// The cluster form's conditions: a head dimension of whole 64-element key loads, at most 256 (eight
+// slices of at most 32), 16-byte aligned key and value buffers, whole KV groups.
+static bool attention_cl_ok(const KArg &k, const KArg &v, int dim, int heads, int kvHeads, const unsigned g[3]) {
+    return dim >= 64 && dim <= 256 && dim % 64 == 0 && kvHeads >= 1 && heads % kvHeads == 0 && g[0] >= 1 &&
+           ((reinterpret_cast<uintptr_t>(k.ptr) | reinterpret_cast<uintptr_t>(v.ptr)) & 15) == 0;
+}
 cudaError_t launch_attention_prompt(const KArg *a, int qi, int ki, int vi, int yi, int dim, int heads, int kvHeads, int position, float scale,
                                     IB pos, const unsigned g[3], cudaStream_t s, unsigned *err) {
     const int G = kvHeads > 0 ? heads / kvHeads : 0;
@@ -585,6 +782,11 @@ cudaError_t launch_attention_prompt(const KArg *a, int qi, int ki, int vi, int y
         if (e != cudaSuccess) return e;
         k_attention_group<<<dim3(kvHeads, g[2]), kGroupThreads, bytes, s>>>(grid_of(g), F(qi), F(ki), F(vi), F(yi), dim, heads, kvHeads,
                                                                            position, scale, pos, err);
+        return cudaGetLastError();
+    }
+    if (attention_cl_ok(a[ki], a[vi], dim, heads, kvHeads, g)) {
+        k_attention_cl<<<dim3(g[0] * kAcCluster, g[2]), kAcThreads, 0, s>>>(grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim,
+                                                                            heads, kvHeads, 0, position, scale, 1, pos, err);
         return cudaGetLastError();
     }
     k_attention<<<dim3(g[0], g[2]), kAttnThreads, 0, s>>>(grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim, heads, kvHeads, 0,
@@ -1046,6 +1248,11 @@ cudaError_t L_argmax(const KArg *a, const unsigned g[3], cudaStream_t s, unsigne
     return cudaGetLastError();
 }
 cudaError_t L_attention(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    if (attention_cl_ok(a[1], a[2], a[5].i, a[6].i, a[7].i, g)) {
+        k_attention_cl<<<dim3(g[0] * kAcCluster, 1), kAcThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i,
+                                                                         a[8].i, 0, a[9].f, 0, IB{nullptr, 0}, err);
+        return cudaGetLastError();
+    }
     k_attention<<<dim3(g[0], 1), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, 0, a[9].f, 0,
                                                        IB{nullptr, 0}, err);
     return cudaGetLastError();

@@ -227,3 +227,45 @@ def test_out_of_range_index_is_reported_not_faulted(b):
           [4, 1, 1])
     b.idle()
     assert np.array_equal(b.read(Y), np.ones(4 * width, np.float32))
+
+
+@pytest.mark.parametrize("dim,heads,kv,count", [(256, 16, 2, 1500), (64, 4, 4, 3), (128, 8, 2, 2048), (256, 16, 2, 9)])
+def test_attention_split_over_clusters_bit_exact(b, port, dim, heads, kv, count):
+    """Decode attention (one query, a list of cells) at head sizes the 8-CTA cluster form takes:
+    the scores split over the cluster and gathered through distributed shared memory, the value
+    columns split over it; bit-identical to the oracle, also with repeated and shuffled cells."""
+    rng = np.random.default_rng(dim + count)
+    cells_total = count + 7
+    q = rng.normal(0, 1, heads * dim).astype(np.float32)
+    keys = rng.normal(0, 1, cells_total * kv * dim).astype(np.float32)
+    vals = rng.normal(0, 1, cells_total * kv * dim).astype(np.float32)
+    cells = rng.permutation(cells_total)[:count].astype(np.int32)
+    if count > 4:
+        cells[3] = cells[1]  # a repeated cell
+    scale = 1.0 / math.sqrt(dim)
+    want = np.zeros(heads * dim, np.float32)
+    port.run("strata_attention", (heads, dim // 64, 1), Q=q, Keys=keys, Values=vals, Cells=cells, Y=want, dim=dim, heads=heads,
+             kvHeads=kv, count=count, scale=scale)
+    y = b.alloc(heads * dim)
+    b.run("strata_attention", dict(Q=b.alloc(q), Keys=b.alloc(keys), Values=b.alloc(vals), Cells=b.alloc(cells, "i32"), Y=y, dim=dim,
+                                   heads=heads, kvHeads=kv, count=count, scale=float(np.float32(scale))), [heads, dim // 64, 1])
+    assert np.array_equal(bits(b.read(y)), bits(want))
+
+
+@pytest.mark.parametrize("position", [0, 700, 2047])
+def test_attention_at_device_position_bit_exact(b, port, position):
+    """strata_attention_at (the decode step's form: the causal prefix of the position held in device
+    memory) against the oracle's strata_attention_batch for one query token."""
+    rng = np.random.default_rng(position + 5)
+    dim, heads, kv = 256, 16, 2
+    q = rng.normal(0, 1, heads * dim).astype(np.float32)
+    keys = rng.normal(0, 1, 2048 * kv * dim).astype(np.float32)
+    vals = rng.normal(0, 1, 2048 * kv * dim).astype(np.float32)
+    want = np.zeros(heads * dim, np.float32)
+    port.run("strata_attention_batch", (heads, dim // 64, 1), Q=q, Keys=keys, Values=vals, Y=want, dim=dim, heads=heads, kvHeads=kv,
+             position=position, scale=0.0625)
+    y = b.alloc(heads * dim)
+    pos = b.alloc(np.array([position], np.int32), "i32")
+    b.run("strata_attention_at", dict(Q=b.alloc(q), Keys=b.alloc(keys), Values=b.alloc(vals), Position=pos, Y=y, dim=dim, heads=heads,
+                                      kvHeads=kv, scale=0.0625), [heads, dim // 64, 1])
+    assert np.array_equal(bits(b.read(y)), bits(want))
