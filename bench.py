@@ -35,7 +35,10 @@ configurations, each timed the same way on the same GPU(s):
   ep                      BASELINE config 4 at this run's N: 16384 tokens split over the ranks,
           the 512 experts sharded, NCCL dispatch and return between the ranks when N >= 2;
           tokens/s (max over ranks), per-GPU TFLOP/s, rank 0's phase split, and
-          efficiency_vs_n1 when an N=1 run on the same host left its number in /tmp.
+          efficiency_vs_n1 when an N=1 run on the same host left its number in /tmp;
+  model48                 BASELINE config 5 at batch 1 (one GPU only): the 48-layer synthetic
+          model through the whole engine, prompt 1920 prefilled in chunks of 64, 128 greedy
+          decode tokens; decode ms per token and prefill tokens/s by the host clock.
 
 Multi-GPU: the headline has every rank run its own replica of the layer stack (the reference
 has no multi-GPU path); scaling is weak. The `ep` block (and `--ep`, which times BASELINE
@@ -423,6 +426,8 @@ def run_gpu_arm(args, world, rank, local):
         L.free()
     if not args.headline_only:
         blocks["ep"] = ep_block(args, world, rank, local, b)
+    if not args.headline_only and world == 1:
+        blocks["model48"] = model_block(b)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -672,31 +677,28 @@ def prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K):
             "phase_ms_per_step": {k: v / max(1, calls) for k, v in ph.items()}}
 
 
-def run_model_arm(args):
-    """The full-model workload on one GPU: the seeded 48-layer synthetic model
-    (stratacuda_b200.synthetic) resident in HBM, a prompt prefilled in chunks of 64, then greedy
-    decode at batch 1, all through StrataEngine (the reference host's call order). Timed end to
-    end by the host clock around each phase, which ends in the argmax read: the host dispatch
-    of every entry is inside the number. Prints its own JSON line (not the MoE-layer metric)."""
-    from stratacuda_b200.backend import CudaBackend
+def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_prefill=False, profile_step=False):
+    """The full-model workload on backend b: the seeded synthetic model (stratacuda_b200.synthetic)
+    resident in HBM, a prompt prefilled in chunks of 64, then greedy decode at batch 1, all through
+    StrataEngine (the reference host's call order). Timed by the host clock around each phase,
+    which ends in the argmax read: the host dispatch of every entry is inside the numbers."""
     from stratacuda_b200.engine import StrataEngine
     from stratacuda_b200.synthetic import MODEL_GEOMETRY, MOE_MODES, DeviceStore
 
-    b = CudaBackend(0)
-    g = dict(MODEL_GEOMETRY, layers=args.model_layers)
+    g = dict(MODEL_GEOMETRY, layers=layers)
     t0 = time.perf_counter()
     store = DeviceStore(b, g, seed=1)
     b.idle()
     t_gen = time.perf_counter() - t0
-    engine = StrataEngine.create(store, b, MOE_MODES[args.mode], graph=not args.no_graph)
-    prompt = np.random.default_rng(7).integers(0, g["vocab"], args.prompt).tolist()
-    for _ in range(max(1, args.warmup // 3)):  # warm-up: pools, RoPE table, the decode graph's capture
+    engine = StrataEngine.create(store, b, MOE_MODES[mode], graph=graph)
+    prompt = np.random.default_rng(7).integers(0, g["vocab"], prompt_len).tolist()
+    for _ in range(max(1, warmup // 3)):  # warm-up: pools, RoPE table, the decode graph's capture
         engine.prefill(prompt[:64], chunk_size=64)
         engine.step(1)
         engine.step(2)
         engine.reset()
     t0 = time.perf_counter()
-    if args.profile_prefill and args.prompt > 64:  # only the last chunk is inside the capture
+    if profile_prefill and prompt_len > 64:  # only the last chunk is inside the capture
         import torch
         engine.prefill(prompt[:-64], chunk_size=64)
         b.idle()
@@ -709,8 +711,8 @@ def run_model_arm(args):
     t_prefill = time.perf_counter() - t0
     token, tokens = r["token"], []
     t0 = time.perf_counter()
-    for k in range(args.decode):
-        last = args.profile_step and k == args.decode - 1
+    for k in range(decode):
+        last = profile_step and k == decode - 1
         if last:  # only this step is inside an `ncu --profile-from-start off` capture
             import torch
             b.idle()
@@ -721,15 +723,34 @@ def run_model_arm(args):
             b.idle()
             torch.cuda.cudart().cudaProfilerStop()
     t_decode = time.perf_counter() - t0
-    line = {"metric": "full-model tokens/s (prefill; greedy decode b=1)", "workload": "model48", "value": args.decode / t_decode,
-            "unit": "tokens/s", "n_gpus": 1, "prefill_tokens_per_s": args.prompt / t_prefill, "prefill_s": t_prefill,
-            "decode_ms_per_token": 1e3 * t_decode / args.decode, "higher_is_better": True, "dtype": "f32+q2", "data": "synthetic",
-            "moe_mode": args.mode, "decode_graph": not args.no_graph, "generate_s": t_gen, "resident_gb": store.bytes_resident() / 1e9,
-            "config": {"workload": f"{g['layers']}-layer synthetic model, hidden {g['width']}, vocab {g['vocab']}, prompt {args.prompt}, "
-                                   f"decode {args.decode}, chunk 64", "timing": "host clock, end to end"},
-            "first_tokens": tokens[:8]}
+    out = {"decode_tokens_per_s": decode / t_decode, "decode_ms_per_token": 1e3 * t_decode / decode,
+           "prefill_tokens_per_s": prompt_len / t_prefill, "prefill_s": t_prefill, "generate_s": t_gen,
+           "resident_gb": store.bytes_resident() / 1e9,
+           "config": {"workload": f"{g['layers']}-layer synthetic model, hidden {g['width']}, vocab {g['vocab']}, prompt {prompt_len}, "
+                                  f"decode {decode}, chunk 64", "moe_mode": mode, "decode_graph": graph,
+                      "timing": "host clock, end to end"},
+           "first_tokens": tokens[:8]}
     engine.dispose()
     store.free()
+    return out
+
+
+def model_block(b):
+    """BASELINE config 5 at batch 1 (one GPU): the 48-layer synthetic model, prompt 1920, 128
+    greedy decode tokens (context 2048)."""
+    return model_run(b, 48, 1920, 128, 3, "fast")
+
+
+def run_model_arm(args):
+    """The full-model workload on one GPU (model_run); prints its own JSON line (not the MoE-layer
+    metric)."""
+    from stratacuda_b200.backend import CudaBackend
+
+    b = CudaBackend(0)
+    r = model_run(b, args.model_layers, args.prompt, args.decode, args.warmup, args.mode, graph=not args.no_graph,
+                  profile_prefill=args.profile_prefill, profile_step=args.profile_step)
+    line = {"metric": "full-model tokens/s (prefill; greedy decode b=1)", "workload": "model48", "value": r["decode_tokens_per_s"],
+            "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "dtype": "f32+q2", "data": "synthetic", **r}
     b.dispose()
     print(json.dumps(line), flush=True)
 
@@ -748,7 +769,7 @@ def main():
     ap.add_argument("--zipf", type=float, default=None, help="router bias skew (default: 1.1 for batches above 64 and --ep)")
     ap.add_argument("--ep", action="store_true", help="expert-parallel layer over the ranks (BASELINE config 4)")
     ap.add_argument("--headline-only", action="store_true",
-                    help="skip the nested blocks (decode_b8, decode_b64, prefill_4096, ep) of the default line")
+                    help="skip the nested blocks (decode_b8, decode_b64, prefill_4096, ep, model48) of the default line")
     ap.add_argument("--no-graph", action="store_true", help="time direct launches instead of a CUDA graph replay of the K steps")
     ap.add_argument("--ep-tokens", type=int, default=16384, help="tokens of the expert-parallel job (split over the ranks)")
     ap.add_argument("--model", action="store_true", help="the full-model workload (48-layer synthetic model, 1 GPU)")

@@ -923,6 +923,61 @@ cudaError_t launch_conv(const KArg *a, const unsigned g[3], int tokens, int batc
     return cudaGetLastError();
 }
 
+// strata_gdn_prep (no counterpart in the reference): the delta-rule layer's input sequence of one
+// token (src/engine.js's strata_conv (4 taps, dilation 1, SiLU) over the [q | k | v] projection,
+// three strata_slice, then the L2 norms of the q heads (times qScale) and of the k heads,
+// strata_norm mode 1) in one launch, each value by the same operations in the same order. Block
+// b takes channels [2 hd b, 2 hd b + 2 hd): two heads' worth of q, k or v channels (keyDim and
+// valueDim are multiples of 2 hd): the conv per channel, as k_conv_reg, into shared memory and
+// the history; then two warps norm the block's two q or k heads as k_norm does (lane_dot, tree),
+// or the v channels are copied out.
+constexpr int kPrepThreads = 256;
+__global__ void __launch_bounds__(kPrepThreads) k_gdn_prep(FB History, FB X, FB W, FB Q, FB K, FB V, int keyDim, int valueDim, int hd,
+                                                           float qScale, float epsilon) {
+    extern __shared__ float prep[];  // [2 hd] the block's convolved channels
+    const int tid = threadIdx.x, warp = tid >> 5, t = tid & 31, span = 2 * hd;
+    const long long c0 = (long long)blockIdx.x * span;
+    for (int i = tid; i < span; i += kPrepThreads) {  // k_conv_reg<4, 1>, one token
+        const long long c = c0 + i;
+        float hist[3], w[4];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) hist[k] = History.p[c * 3 + k];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[k] = W.p[c * 4 + k];
+        const float x = X.p[c];
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) sum = __fadd_rn(sum, __fmul_rn(hist[k], w[k]));
+        sum = __fadd_rn(sum, __fmul_rn(x, w[3]));
+        prep[i] = ref_silu(sum);
+        History.p[c * 3 + 0] = hist[1];
+        History.p[c * 3 + 1] = hist[2];
+        History.p[c * 3 + 2] = x;
+    }
+    __syncthreads();
+    if (c0 >= 2LL * keyDim) {  // v channels: the slice
+        for (int i = tid; i < span; i += kPrepThreads) V.p[c0 - 2LL * keyDim + i] = prep[i];
+        return;
+    }
+    if (warp >= 2) return;
+    const bool is_q = c0 < keyDim;
+    const float scale = is_q ? qScale : 1.0f;
+    const float *x = prep + warp * hd;
+    float *y = (is_q ? Q.p + c0 : K.p + (c0 - keyDim)) + warp * hd;
+    const float ss = __shfl_sync(0xffffffffu, lane_dot(x, x, hd, t), 0);
+    const float inv = __fdiv_rn(scale, __fsqrt_rn(__fadd_rn(ss, epsilon)));  // k_norm, mode 1
+    for (int i = t; i < hd; i += 32) y[i] = __fmul_rn(__fmul_rn(x[i], inv), 1.0f);
+}
+cudaError_t L_gdn_prep(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const long long kd = a[6].i, vd = a[7].i, hd = a[8].i, c = 2 * kd + vd;
+    if (hd < 32 || hd > 1024 || kd < 2 * hd || kd % (2 * hd) != 0 || vd % (2 * hd) != 0 || a[0].len < 3 * c || a[1].len < c ||
+        a[2].len < 4 * c || a[3].len < kd || a[4].len < kd || a[5].len < vd)
+        return cudaErrorInvalidValue;
+    k_gdn_prep<<<(unsigned)(c / (2 * hd)), kPrepThreads, (size_t)(2 * hd) * 4, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), (int)kd, (int)vd,
+                                                                                   (int)hd, a[9].f, a[10].f);
+    return cudaGetLastError();
+}
+
 // kernels/strata.cu:296-301 and :425-431: decay = exp(A softplus(alpha + dt)), strength = sigmoid(beta).
 __global__ void k_gdn_gates(Grid g, FB Alpha, FB Beta, FB A, FB Dt, FB Decay, FB Strength, int heads, int tokens, unsigned *err) {
     long long i = lane_index(g, (long long)heads * tokens);
@@ -1378,6 +1433,7 @@ const KernelSpec kEngineKernels[] = {
     // hyper-connection blocks (no reference counterpart)
     {"strata_hc_in", "Residual:f NormW:f DownW:f InjectW:f Norm:f Down:f Inject:f width:I streams:I rank:I epsilon:F", L_hc_in},
     {"strata_hc_out", "Norm:f Down:f UpW:f Mixed:f width:I streams:I rank:I scale:F", L_hc_out},
+    {"strata_gdn_prep", "History:f X:f W:f Q:f K:f V:f keyDim:I valueDim:I headDim:I qScale:F epsilon:F", L_gdn_prep},
 };
 const int kNumEngineKernels = sizeof(kEngineKernels) / sizeof(kEngineKernels[0]);
 

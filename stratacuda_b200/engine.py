@@ -393,12 +393,19 @@ class StrataEngine:
         qk, vn = g["ssmDim"] * g["keyHeads"], g["ssmDim"] * g["valueHeads"]
         c = 2 * qk + vn
         qkv = o.mat(p + "attn_qkv.weight", x)
-        convolved = o.alloc(c)
-        b.run("strata_conv", dict(History=st["conv"], X=qkv, W=o.vector(p + "ssm_conv1d.weight"), Y=convolved, channels=c, taps=4,
-                                  dilation=1, activation=1), grid(c))
-        qr, kr, v = o.slice(convolved, qk), o.slice(convolved, qk, 1, qk, qk), o.slice(convolved, vn, 1, vn, 2 * qk)
-        q = o.norm(qr, qr, g["ssmDim"], g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
-        k = o.norm(kr, kr, g["ssmDim"], g["keyHeads"], 1, 1)
+        hd = g["ssmDim"]
+        if getattr(b, "kind", None) == "cuda" and 32 <= hd <= 1024 and qk % (2 * hd) == 0 and vn % (2 * hd) == 0:
+            # the six dispatches below in one launch, the same values (strata_gdn_prep)
+            q, k, v = o.alloc(qk), o.alloc(qk), o.alloc(vn)
+            b.run("strata_gdn_prep", dict(History=st["conv"], X=qkv, W=o.vector(p + "ssm_conv1d.weight"), Q=q, K=k, V=v, keyDim=qk,
+                                          valueDim=vn, headDim=hd, qScale=_f32(1 / math.sqrt(hd)), epsilon=1e-6), [1, 1, 1])
+        else:
+            convolved = o.alloc(c)
+            b.run("strata_conv", dict(History=st["conv"], X=qkv, W=o.vector(p + "ssm_conv1d.weight"), Y=convolved, channels=c, taps=4,
+                                      dilation=1, activation=1), grid(c))
+            qr, kr, v = o.slice(convolved, qk), o.slice(convolved, qk, 1, qk, qk), o.slice(convolved, vn, 1, vn, 2 * qk)
+            q = o.norm(qr, qr, g["ssmDim"], g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
+            k = o.norm(kr, kr, g["ssmDim"], g["keyHeads"], 1, 1)
         alpha, beta = o.mat(p + "ssm_alpha.weight", x), o.mat(p + "ssm_beta.weight", x)
         decay, strength = o.alloc(g["valueHeads"]), o.alloc(g["valueHeads"])
         b.run("strata_gdn_gates", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
