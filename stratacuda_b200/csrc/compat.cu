@@ -11,6 +11,7 @@
 #include "kernels.h"
 #include "route.cuh"
 #include "compat.cuh"
+#include "q2mma.cuh"
 
 #include <algorithm>
 
@@ -21,16 +22,19 @@ namespace {
 // (one reference lane per thread: i = blockIdx.x * 64 + threadIdx.x over the x extent)
 
 __global__ void k_unpack_half(Grid g, UB Packed, FB Values, int count, unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < (long long)g.x * STRATA_LANES && i < count) Values.set(i, half_of(Packed, i, err), err);
 }
 
 __global__ void k_expert_scales(Grid g, UB Blob, FB Scales, int offset, int count, unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < (long long)g.x * STRATA_LANES && i < count) Scales.set(i, half_of(Blob, offset + i, err), err);
 }
 
 __global__ void k_elementwise(Grid g, FB A, FB B, FB Y, int n, int mode, float scale, unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)g.x * STRATA_LANES || i >= n) return;
     float a = __fmul_rn(A.get(i, err), scale), v = a;
@@ -43,6 +47,7 @@ __global__ void k_elementwise(Grid g, FB A, FB B, FB Y, int n, int mode, float s
 }
 
 __global__ void k_moe_combine(Grid g, FB Parts, FB Weights, FB Shared, FB SharedGate, FB Y, int width, int count, unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)g.x * STRATA_LANES || i >= width) return;
     float value = __fmul_rn(Shared.get(i, err), ref_sigmoid(SharedGate.get(0, err)));
@@ -52,6 +57,7 @@ __global__ void k_moe_combine(Grid g, FB Parts, FB Weights, FB Shared, FB Shared
 
 __global__ void k_moe_combine_batch(Grid g, FB Parts, FB Weights, FB Shared, FB SharedGate, FB Y, int width, int count, int tokens,
                                     unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)g.x * STRATA_LANES || i >= (long long)width * tokens) return;
     long long token = i / width, d = i % width;
@@ -62,12 +68,14 @@ __global__ void k_moe_combine_batch(Grid g, FB Parts, FB Weights, FB Shared, FB 
 }
 
 __global__ void k_gather_rows(Grid g, FB X, IB Indices, FB Y, int width, int rows, unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)g.x * STRATA_LANES || i >= (long long)width * rows) return;
     Y.set(i, X.get((long long)Indices.get(i / width, err) * width + i % width, err), err);
 }
 
 __global__ void k_scatter_rows(Grid g, FB X, IB Indices, FB Y, int width, int rows, unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)g.x * STRATA_LANES || i >= (long long)width * rows) return;
     Y.set((long long)Indices.get(i / width, err) * width + i % width, X.get(i, err), err);
@@ -77,6 +85,7 @@ __global__ void k_scatter_rows(Grid g, FB X, IB Indices, FB Y, int width, int ro
 
 // kernels/strata.cu:156-165
 __global__ void k_project(Grid g, FB X, FB W, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset, unsigned *err) {
+    dep_enter();
     unsigned row, token, z;
     if (!my_group_y_first(g, row, token, z)) return;
     if (!((int)row < rows && (int)token < tokens)) return;
@@ -106,6 +115,11 @@ __global__ void k_project(Grid g, FB X, FB W, FB Y, int cols, int rows, int toke
 // buffers cover every row read.
 constexpr int kGemvThreads = 256, kGemvRows = kGemvThreads / 16;
 __global__ void __launch_bounds__(kGemvThreads) k_project_gemv(FB X, FB W, FB Y, int cols, int rows, int outputOffset, unsigned *err) {
+    if (threadIdx.x == 0) {  // the block's weight rows, while the previous kernel finishes
+        const int r0 = blockIdx.x * kGemvRows, nr = min(kGemvRows, rows - r0);
+        if (nr > 0) prefetch_l2(W.p + (long long)r0 * cols, (unsigned long long)nr * cols * 4);
+    }
+    dep_enter();
     const int hw = threadIdx.x >> 4, u = threadIdx.x & 15;
     const int row = blockIdx.x * kGemvRows + hw;
     if (row >= rows) return;  // whole half-warps leave together (the shuffles use 16-lane masks)
@@ -151,6 +165,112 @@ __global__ void __launch_bounds__(kGemvThreads) k_project_gemv(FB X, FB W, FB Y,
     }
 }
 
+// The same one-token projection as a weight stream, for matrices of at least 512 rows. Block b
+// owns the contiguous rows [b n, b n + n) and pulls them, one bulk copy (cp.async.bulk) per row,
+// through row slots in shared memory: up to about 200 KB in flight per SM, independent of
+// registers. The first copies are requested before dep_enter() (kernels never write weights), so
+// they stream while the previous kernel finishes. Each of the first `halves` half-warps owns
+// `depth` slots and the block rows h, h + halves, ... (its k-th row in slot h depth + k % depth);
+// it forms each row exactly as k_project_gemv does (thread u holds the reference's lanes
+// 4u .. 4u + 3, the same chains and tree), reading the row from its slot and the input from a
+// copy staged once per block, then refills the slot with its row k + depth. A slot is only ever
+// waited on and refilled by its own half-warp, in order, so the full barrier's parity is never
+// ambiguous. Every wait is bounded: past the limit the block records kErrWaitTimeout, stops, and
+// thread 0 waits (bounded) for the copies that were issued before the block exits.
+constexpr int kStreamThreads = 256, kStreamHalves = kStreamThreads / 16, kStreamMaxSlots = 64, kStreamMaxDepth = 4;
+constexpr size_t kStreamSmem = 200 * 1024;
+constexpr unsigned long long kStreamSpin = 1ull << 20;
+__global__ void __launch_bounds__(kStreamThreads, 1) k_project_stream(FB X, FB W, FB Y, int cols, int rows, int rows_per_block, int halves,
+                                                                      int depth, int outputOffset, unsigned *err) {
+    extern __shared__ __align__(128) float stream_smem[];  // [cols] input, then [halves * depth][cols] weight rows
+    __shared__ __align__(8) unsigned long long full[kStreamMaxSlots];
+    __shared__ int issued[kStreamMaxSlots];  // copies issued into each slot
+    __shared__ int failed;
+    const int r0 = blockIdx.x * rows_per_block, n = max(0, min(rows_per_block, rows - r0));
+    const int slots = halves * depth, stride = halves * depth;  // a half-warp's row k + depth is block row i + stride
+    const unsigned row_bytes = (unsigned)cols * 4;
+    float *xs = stream_smem, *ring = stream_smem + cols;
+    const float *wrow0 = W.p + (long long)r0 * cols;
+    if (threadIdx.x == 0) {
+        failed = 0;
+        for (int sl = 0; sl < slots; ++sl) {
+            q2::mbar_init(&full[sl], 1);
+            issued[sl] = 0;
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int h = 0; h < halves; ++h)  // weights only: before the dependency wait
+            for (int k = 0; k < depth && h + k * halves < n; ++k) {
+                const int sl = h * depth + k;
+                q2::mbar_expect(&full[sl], row_bytes);
+                q2::bulk_copy(ring + (size_t)sl * cols, wrow0 + (long long)(h + k * halves) * cols, row_bytes, &full[sl]);
+                issued[sl] = 1;
+            }
+    }
+    dep_enter();
+    {
+        const float4 *x4 = reinterpret_cast<const float4 *>(X.p);
+        float4 *xs4 = reinterpret_cast<float4 *>(xs);
+        for (int k = threadIdx.x; k < cols / 4; k += kStreamThreads) xs4[k] = x4[k];
+    }
+    __syncthreads();
+    auto wait_bar = [&](unsigned long long *bar, unsigned parity) -> bool {
+        for (unsigned long long i = 0;; ++i) {
+            if (q2::mbar_try(bar, parity)) return true;
+            if (i > kStreamSpin || *(volatile int *)&failed) return false;
+        }
+    };
+    const int hw = threadIdx.x >> 4, u = threadIdx.x & 15;
+    const unsigned mask = 0xffffu << (threadIdx.x & 16);
+    const int R = cols / 64;
+    if (hw < halves)
+        for (int k = 0, i = hw; i < n; ++k, i += halves) {
+            const int sl = hw * depth + k % depth;
+            if (__any_sync(mask, !wait_bar(&full[sl], (k / depth) & 1))) {
+                if (u == 0) {
+                    failed = 1;
+                    raise_error(err, kErrWaitTimeout);
+                }
+                break;
+            }
+            const float4 *w4 = reinterpret_cast<const float4 *>(ring + (size_t)sl * cols) + u;
+            const float4 *x4 = reinterpret_cast<const float4 *>(xs) + u;
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 8
+            for (int r = 0; r < R; ++r) {
+                const float4 wv = w4[16 * r], xv = x4[16 * r];
+                a0 = __fadd_rn(a0, __fmul_rn(wv.x, xv.x));
+                a1 = __fadd_rn(a1, __fmul_rn(wv.y, xv.y));
+                a2 = __fadd_rn(a2, __fmul_rn(wv.z, xv.z));
+                a3 = __fadd_rn(a3, __fmul_rn(wv.w, xv.w));
+            }
+            __syncwarp(mask);  // the slot has been read by all 16 threads
+            if (u == 0 && i + stride < n) {  // refill it (it was read through the generic proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                q2::mbar_expect(&full[sl], row_bytes);
+                q2::bulk_copy(ring + (size_t)sl * cols, wrow0 + (long long)(i + stride) * cols, row_bytes, &full[sl]);
+                issued[sl] = k / depth + 2;
+            }
+#pragma unroll
+            for (int sh = 8; sh > 0; sh >>= 1) {  // reference levels 32, 16, 8, 4
+                a0 = __fadd_rn(a0, __shfl_down_sync(mask, a0, sh, 16));
+                a1 = __fadd_rn(a1, __shfl_down_sync(mask, a1, sh, 16));
+                a2 = __fadd_rn(a2, __shfl_down_sync(mask, a2, sh, 16));
+                a3 = __fadd_rn(a3, __shfl_down_sync(mask, a3, sh, 16));
+            }
+            if (u == 0) {
+                a0 = __fadd_rn(a0, a2);  // level 2
+                a1 = __fadd_rn(a1, a3);
+                Y.p[(long long)outputOffset + r0 + i] = __fadd_rn(a0, a1);  // level 1
+            }
+        }
+    __syncthreads();
+    if (threadIdx.x == 0 && failed)  // copies still in flight must land before the block exits
+        for (int sl = 0; sl < slots; ++sl)
+            for (unsigned long long k = 0; issued[sl] > 0 && !q2::mbar_try(&full[sl], (issued[sl] - 1) & 1) && k <= kStreamSpin; ++k) {
+            }
+}
+
 // The same projection for dispatches with few (row, token) pairs: one block per pair stages the
 // weight row and the input row in shared memory with all its threads (every load in flight at
 // once), then one warp forms the reference's strided sums and tree from shared memory. The host
@@ -158,6 +278,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_project_gemv(FB X, FB W, FB Y,
 constexpr int kStagedThreads = 256;
 __global__ void __launch_bounds__(kStagedThreads) k_project_staged(FB X, FB W, FB Y, int cols, int outputStride, int outputOffset,
                                                                    unsigned *err) {
+    if (threadIdx.x == 0 && blockIdx.y == 0) prefetch_l2(W.p + (long long)blockIdx.x * cols, (unsigned long long)cols * 4);
+    dep_enter();
     extern __shared__ float staged[];  // [cols] weights, then [cols] inputs
     const long long row = blockIdx.x, token = blockIdx.y;
     stage_row(staged, W.p + row * cols, cols);
@@ -184,6 +306,7 @@ constexpr int kBlockRows = 2 * kTileRows, kBlockTokens = 4 * kTileTokens;
 constexpr size_t kTileSmem = 2 * (size_t)(kBlockRows + kBlockTokens) * kTileK * 4;  // 80 KB
 __global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, FB Y, int cols, int rows, int tokens, int outputStride,
                                                                    int outputOffset, unsigned long long neg0, unsigned *err) {
+    dep_enter();
     extern __shared__ __align__(16) float tile_smem[];  // [2 stages][8 weight rows + 32 input rows][256]
     const int warp = threadIdx.x / 32, t = threadIdx.x & 31;
     const int rb = blockIdx.x * kBlockRows, tb = blockIdx.y * kBlockTokens;
@@ -251,6 +374,7 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, F
 // kernels/strata.cu:168-176
 __global__ void k_bf16_project(Grid g, FB X, UB Codes, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset,
                                unsigned *err) {
+    dep_enter();
     unsigned row, token, z;
     if (!my_group(g, row, token, z)) return;
     if (!((int)row < rows && (int)token < tokens)) return;
@@ -272,6 +396,7 @@ __global__ void k_bf16_project(Grid g, FB X, UB Codes, FB Y, int cols, int rows,
 // kernels/strata.cu:179-192
 __global__ void k_q2_project(Grid g, FB X, UB Blob, FB Y, int cols, int rows, int tokens, int outputStride, int outputOffset,
                              int codeOffset, int scaleOffset, int weightRow, int rowStride, unsigned *err) {
+    dep_enter();
     unsigned row, token, z;
     if (!my_group(g, row, token, z)) return;
     if (!((int)row < rows && (int)token < tokens)) return;
@@ -300,6 +425,7 @@ __device__ __forceinline__ float ple_value(const UB &Packed, long long byte0, in
     return __fmul_rn(half_bits(half), iq4(code));
 }
 __global__ void k_ple_decode(Grid g, UB Packed, FB Values, int count, unsigned *err) {
+    dep_enter();
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < (long long)g.x * STRATA_LANES && i < count) Values.set(i, ple_value(Packed, 0, (int)i, err), err);
 }
@@ -309,6 +435,7 @@ __global__ void k_ple_decode(Grid g, UB Packed, FB Values, int count, unsigned *
 // outside the table reads zeros and sets kErrIndex; a non-finite scale sets kErrPleScale
 // (src/model.js:241 rejects those rows).
 __global__ void k_ple_gather_decode(UB Table, IB Ids, FB Values, int rows, int head_dim, unsigned *err) {
+    dep_enter();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)rows * head_dim) return;
     const int h = (int)(i / head_dim), j = (int)(i % head_dim);
@@ -328,6 +455,7 @@ __device__ __forceinline__ long long group_of(long long index, int size) {
 // kernels/strata.cu:193-211
 __global__ void k_quant_project(Grid g, FB X, UB Codes, FB Scales, FB Offsets, FB Y, int cols, int rows, int tokens, int outputStride,
                                 int outputOffset, int bits, int groupSize, int bias, int codebook, int hasOffset, unsigned *err) {
+    dep_enter();
     unsigned row, token, z;
     if (!my_group(g, row, token, z)) return;
     if (!((int)row < rows && (int)token < tokens)) return;
@@ -353,6 +481,7 @@ __global__ void k_quant_project(Grid g, FB X, UB Codes, FB Scales, FB Offsets, F
 // kernels/strata.cu:38-55
 __global__ void k_q2_gate_up(Grid g, FB X, UB Blob, FB Scales, IB Mapping, FB Hidden, int width, int ff, int tokens, int mapped,
                              int expanded, int codeOffset, int scaleOffset, unsigned *err) {
+    dep_enter();
     unsigned row, token, z;
     if (!my_group(g, row, token, z)) return;
     if (!((int)row < ff && (int)token < tokens)) return;
@@ -381,6 +510,7 @@ __global__ void k_q2_gate_up(Grid g, FB X, UB Blob, FB Scales, IB Mapping, FB Hi
 // kernels/strata.cu:56-69
 __global__ void k_q2_down(Grid g, FB Hidden, UB Blob, FB Scales, IB Mapping, FB Y, int width, int ff, int tokens, int mapped,
                           int expanded, int outputOffset, int codeOffset, int scaleOffset, unsigned *err) {
+    dep_enter();
     unsigned row, token, z;
     if (!my_group(g, row, token, z)) return;
     if (!((int)row < width && (int)token < tokens)) return;
@@ -407,6 +537,7 @@ __global__ void k_q2_down(Grid g, FB Hidden, UB Blob, FB Scales, IB Mapping, FB 
 namespace {
 // kernels/strata.cu:238-270 and :478-509. Logits are staged in shared memory per warp.
 __global__ void k_router_batch(Grid g, FB Logits, IB Ids, FB Weights, int experts, int topK, int batch, unsigned *err) {
+    dep_enter();
     __shared__ float lg[kWarpsPerBlock][512];
     __shared__ float sel[kWarpsPerBlock][32];
     __shared__ int ids[kWarpsPerBlock][32];
@@ -429,23 +560,23 @@ __global__ void k_router_batch(Grid g, FB Logits, IB Ids, FB Weights, int expert
 
 
 cudaError_t L_unpack_half(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_unpack_half<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, err);
+    launch_k(true, k_unpack_half, LANESL, grid_of(g), U(0), F(1), a[2].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_ple_decode(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_ple_decode<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, err);
+    launch_k(true, k_ple_decode, LANESL, grid_of(g), U(0), F(1), a[2].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_expert_scales(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_expert_scales<<<LANESL>>>(grid_of(g), U(0), F(1), a[2].i, a[3].i, err);
+    launch_k(true, k_expert_scales, LANESL, grid_of(g), U(0), F(1), a[2].i, a[3].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_q2_gate_up(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_q2_gate_up<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, err);
+    launch_k(true, k_q2_gate_up, GROUPS, grid_of(g), F(0), U(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_q2_down(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_q2_down<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, a[12].i,
+    launch_k(true, k_q2_down, GROUPS, grid_of(g), F(0), U(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, a[12].i,
                           err);
     return cudaGetLastError();
 }
@@ -454,11 +585,35 @@ cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
     // names, rows < g[0] and tokens < g[1]; z repeats them)
     const long long cols = a[3].i, rows = std::min<long long>(a[4].i, g[0]), tokens = std::min<long long>(a[5].i, g[1]);
     const bool aligned16 = ((reinterpret_cast<uintptr_t>(a[0].ptr) | reinterpret_cast<uintptr_t>(a[1].ptr)) & 15) == 0;
+    // one token, at least 512 rows: the weight stream (one block per SM, rows through a ring of
+    // bulk-copied slots)
+    if (tokens == 1 && rows >= 512 && cols >= 64 && cols % 64 == 0 && (size_t)cols * 8 <= kStreamSmem && aligned16 &&
+        a[1].len >= rows * cols && a[0].len >= cols && (long long)a[7].i + rows <= a[2].len && a[7].i >= 0 && rows <= INT32_MAX) {
+        static int sms = 0;
+        if (!sms) {
+            int dev = 0;
+            cudaError_t e = cudaGetDevice(&dev);
+            if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess || sms <= 0) return e != cudaSuccess ? e : cudaErrorInvalidValue;
+        }
+        const long long blocks = std::min<long long>(rows, sms), per = (rows + blocks - 1) / blocks;
+        // slots that fit beside the input row; half-warps that own them, and slots per half-warp
+        const long long fit = std::min<long long>(kStreamMaxSlots, (long long)(kStreamSmem / ((size_t)cols * 4)) - 1);
+        const long long halves = std::min<long long>({(long long)kStreamHalves, fit, per});
+        const long long depth = std::max<long long>(
+            1, std::min<long long>({(long long)kStreamMaxDepth, fit / halves, (per + halves - 1) / halves}));
+        const size_t bytes = (size_t)(halves * depth + 1) * cols * 4;
+        cudaError_t e = cudaFuncSetAttribute(k_project_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return e;
+        launch_k(true, k_project_stream, (unsigned)((rows + per - 1) / per), kStreamThreads, bytes, s, F(0), F(1), F(2), (int)cols, (int)rows,
+                 (int)per, (int)halves, (int)depth, a[7].i, err);
+        return cudaGetLastError();
+    }
     // one token, many rows: a half-warp per row, 16-byte streaming loads (fewer rows: the
     // staging blocks below have every load of a row in flight at once)
     if (tokens == 1 && rows > 2048 && cols >= 64 && cols % 64 == 0 && aligned16 && a[1].len >= rows * cols && a[0].len >= cols &&
         (long long)a[7].i + rows <= a[2].len && a[7].i >= 0) {
-        k_project_gemv<<<(unsigned)((rows + kGemvRows - 1) / kGemvRows), kGemvThreads, 0, s>>>(F(0), F(1), F(2), (int)cols, (int)rows,
+        launch_k(true, k_project_gemv, (unsigned)((rows + kGemvRows - 1) / kGemvRows), kGemvThreads, 0, s, F(0), F(1), F(2), (int)cols, (int)rows,
                                                                                                  a[7].i, err);
         return cudaGetLastError();
     }
@@ -467,7 +622,7 @@ cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
         rows > 0 && tokens > 0) {
         cudaError_t e = cudaFuncSetAttribute(k_project_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
         if (e != cudaSuccess) return e;
-        k_project_staged<<<dim3((unsigned)rows, (unsigned)tokens), kStagedThreads, bytes, s>>>(F(0), F(1), F(2), a[3].i, a[6].i, a[7].i,
+        launch_k(tokens == 1, k_project_staged, dim3((unsigned)rows, (unsigned)tokens), kStagedThreads, bytes, s, F(0), F(1), F(2), a[3].i, a[6].i, a[7].i,
                                                                                                 err);
         return cudaGetLastError();
     }
@@ -477,53 +632,53 @@ cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
         cudaError_t e = cudaFuncSetAttribute(k_project_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTileSmem);
         if (e != cudaSuccess) return e;
         const dim3 blocks((unsigned)((rows + kBlockRows - 1) / kBlockRows), (unsigned)((tokens + kBlockTokens - 1) / kBlockTokens));
-        k_project_tiled<<<blocks, kTileWarps * 32, kTileSmem, s>>>(F(0), F(1), F(2), a[3].i, (int)rows, (int)tokens, a[6].i, a[7].i,
+        launch_k(false, k_project_tiled, blocks, kTileWarps * 32, kTileSmem, s, F(0), F(1), F(2), a[3].i, (int)rows, (int)tokens, a[6].i, a[7].i,
                                                                    kNegZero2, err);
         return cudaGetLastError();
     }
-    k_project<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);
+    launch_k(tokens == 1, k_project, GROUPS, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_bf16_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_bf16_project<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);
+    launch_k(true, k_bf16_project, GROUPS, grid_of(g), F(0), U(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_q2_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_q2_project<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i,
+    launch_k(true, k_q2_project, GROUPS, grid_of(g), F(0), U(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i,
                              err);
     return cudaGetLastError();
 }
 cudaError_t L_quant_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_quant_project<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i,
+    launch_k(true, k_quant_project, GROUPS, grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i,
                                 a[12].i, a[13].i, a[14].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_elementwise(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_elementwise<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].f, err);
+    launch_k(a[3].i <= 16384, k_elementwise, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].f, err);
     return cudaGetLastError();
 }
 cudaError_t L_router(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_router_batch<<<1, kWarpsPerBlock * 32, 0, s>>>(Grid{1, 1, 1}, F(0), I(1), F(2), a[3].i, a[4].i, 0, err);
+    launch_k(true, k_router_batch, 1, kWarpsPerBlock * 32, 0, s, Grid{1, 1, 1}, F(0), I(1), F(2), a[3].i, a[4].i, 0, err);
     return cudaGetLastError();
 }
 cudaError_t L_router_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_router_batch<<<GROUPS>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, 1, err);
+    launch_k(false, k_router_batch, GROUPS, grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, 1, err);
     return cudaGetLastError();
 }
 cudaError_t L_moe_combine(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_moe_combine<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), a[5].i, a[6].i, err);
+    launch_k(true, k_moe_combine, LANESL, grid_of(g), F(0), F(1), F(2), F(3), F(4), a[5].i, a[6].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_moe_combine_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_moe_combine_batch<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, err);
+    launch_k(false, k_moe_combine_batch, LANESL, grid_of(g), F(0), F(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_gather_rows(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_gather_rows<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, err);
+    launch_k(true, k_gather_rows, LANESL, grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_scatter_rows(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_scatter_rows<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, err);
+    launch_k(true, k_scatter_rows, LANESL, grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, err);
     return cudaGetLastError();
 }
 }  // namespace
@@ -531,7 +686,7 @@ cudaError_t L_scatter_rows(const KArg *a, const unsigned g[3], cudaStream_t s, u
 cudaError_t ple_gather_decode(const unsigned *table, long long table_words, const int *ids, long long ids_len, int rows, int head_dim,
                               float *values, long long values_len, cudaStream_t s, unsigned *err) {
     const long long n = (long long)rows * head_dim;
-    k_ple_gather_decode<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(UB{const_cast<unsigned *>(table), table_words},
+    launch_k(true, k_ple_gather_decode, (unsigned)((n + 255) / 256), 256, 0, s, UB{const_cast<unsigned *>(table), table_words},
                                                                       IB{const_cast<int *>(ids), ids_len}, FB{values, values_len}, rows,
                                                                       head_dim, err);
     return cudaGetLastError();

@@ -91,6 +91,47 @@ __device__ __forceinline__ void stage_row(float *dst, const float *src, int n) {
     }
 }
 
+// Programmatic dependent launch of the engine entries. A kernel launched by launch_dep may be
+// scheduled while the previous kernel of its stream is still running. Its first statement is
+// dep_enter(): wait until that kernel has finished and its writes are visible, then let the next
+// kernel of the stream be scheduled. So at most one kernel runs ahead of its predecessor's end,
+// and it touches no memory before dep_enter() except L2 prefetches of weights (which no kernel
+// writes). Launched without the attribute (STRATA_ENGINE_PDL=0), dep_enter() returns at once.
+__device__ __forceinline__ void dep_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// A hint that [p, p + bytes) will be read soon: one bulk L2 prefetch (16-byte aligned start, the
+// size rounded down to 16 bytes; nothing is issued for an unaligned start).
+__device__ __forceinline__ void prefetch_l2(const void *p, unsigned long long bytes) {
+    bytes &= ~15ull;
+    if ((reinterpret_cast<uintptr_t>(p) & 15) != 0 || bytes == 0) return;
+    while (bytes > 0) {
+        const unsigned n = bytes > (1ull << 30) ? (1u << 30) : (unsigned)bytes;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
+        p = static_cast<const char *>(p) + n;
+        bytes -= n;
+    }
+}
+bool engine_pdl();  // STRATA_ENGINE_PDL is not "0" (read once)
+// `dep`: launch with the attribute. The one-token (decode) dispatches take it; prompt-chunk
+// dispatches run long enough that an early launch gains nothing, and their blocks are then placed
+// wherever the previous kernel has freed room instead of evenly over the SMs.
+template <typename... KT, typename... AT>
+inline cudaError_t launch_k(bool dep, void (*k)(KT...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, AT &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dep && engine_pdl() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<AT &&>(args)...);
+}
+
 // 16-byte asynchronous global -> shared copies (cp.async, L2 only) and their group waits.
 __device__ __forceinline__ void copy16_async(void *dst, const void *src) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(dst);

@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 
 namespace strata {
 namespace {
@@ -56,6 +57,7 @@ __device__ __forceinline__ float rotate(float a, float b, float c, float s, bool
 // stream of the residual.
 __global__ void k_embedding(Grid g, FB Values, UB Codes, FB Scales, FB Offsets, FB Residual, int width, int streams, int outputOffset,
                             int format, int bits, int groupSize, int bias, int codebook, int hasOffset, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, width);
     if (i < 0) return;
     float value = 0.0f;
@@ -75,6 +77,7 @@ __global__ void k_embedding(Grid g, FB Values, UB Codes, FB Scales, FB Offsets, 
 
 // kernels/strata.cu:282-284 and :399-402
 __global__ void k_embed(Grid g, FB Row, FB Residual, int width, int streams, int tokens, unsigned *err) {
+    dep_enter();
     const long long hc = (long long)width * streams;
     long long i = lane_index(g, hc * tokens);
     if (i >= 0) Residual.set(i, Row.get((i / hc) * width + i % width, err), err);
@@ -86,6 +89,7 @@ __global__ void k_embed(Grid g, FB Row, FB Residual, int width, int streams, int
 // series and an exp series, in double arithmetic with every operation rounded on its own (the
 // reference's CPU target has no fused multiply-add), split into a float and its remainder.
 __global__ void k_rope_frequencies(Grid g, FB High, FB Low, int rotary, float base, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, rotary / 2);
     if (i < 0) return;
     double value = (double)base;
@@ -119,6 +123,7 @@ __global__ void k_rope_frequencies(Grid g, FB High, FB Low, int rotary, float ba
 
 // kernels/strata.cu:105-111: cos / sin of position * frequency, reduced by whole turns in double.
 __global__ void k_rope_table(Grid g, FB High, FB Low, FB Cos, FB Sin, int rotary, int context, unsigned *err) {
+    dep_enter();
     const int half = rotary / 2;
     long long i = lane_index(g, (long long)context * half);
     if (i < 0) return;
@@ -135,6 +140,7 @@ __global__ void k_rope_table(Grid g, FB High, FB Low, FB Cos, FB Sin, int rotary
 // row of Cos / Sin) and :445-452 (rope_batch: table row = token). `mode` 0 / 1 / 2 picks which.
 __global__ void k_rope(Grid g, FB X, FB Cos, FB Sin, FB Y, int dim, int heads, int rotary, int position, int tokens, int mode, IB Pos,
                        unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, (long long)dim * heads * tokens);
     if (i < 0) return;
     if (Pos.n > 0) position = Pos.get(0, err);  // strata_rope_at: the position lives on the device
@@ -154,6 +160,7 @@ __global__ void k_rope(Grid g, FB X, FB Cos, FB Sin, FB Y, int dim, int heads, i
 
 // kernels/strata.cu:121-131: Y[token, row] = W[row] . X[token], 64-lane stride then the tree.
 __global__ void k_gemv(Grid g, FB X, FB W, FB Y, int cols, int rows, int tokens, unsigned *err) {
+    dep_enter();
     unsigned row, token, z;
     if (!my_group(g, row, token, z) || (int)row >= rows || (int)token >= tokens) return;
     const int t = threadIdx.x & 31;
@@ -176,6 +183,7 @@ __global__ void k_gemv(Grid g, FB X, FB W, FB Y, int cols, int rows, int tokens,
 // scale and optional offset per group) against one input vector.
 __global__ void k_quant_gemv(Grid g, FB X, UB Codes, FB Scales, FB Offsets, FB Y, int cols, int rows, int bits, int groupSize, int bias,
                              int codebook, int hasOffset, unsigned *err) {
+    dep_enter();
     unsigned row, y, z;
     if (!my_group(g, row, y, z) || (int)row >= rows) return;
     const int t = threadIdx.x & 31;
@@ -199,6 +207,7 @@ __global__ void k_quant_gemv(Grid g, FB X, UB Codes, FB Scales, FB Offsets, FB Y
 
 // kernels/strata.cu:214-227: mode 0 weighted RMSNorm (gamma row `row % weightRows`), mode 1 L2 norm.
 __global__ void k_norm(Grid g, FB X, FB W, FB Y, int cols, int rows, int weightRows, int mode, float epsilon, float scale, unsigned *err) {
+    dep_enter();
     unsigned row, y, z;
     if (!my_group(g, row, y, z) || (int)row >= rows) return;
     const int t = threadIdx.x & 31;
@@ -250,6 +259,7 @@ __global__ void k_norm(Grid g, FB X, FB W, FB Y, int cols, int rows, int weightR
 constexpr int kNormThreads = 256;
 __global__ void __launch_bounds__(kNormThreads) k_norm_staged(FB X, FB W, FB Y, int cols, int weightRows, int mode, float epsilon,
                                                               float scale) {
+    dep_enter();
     extern __shared__ float staged[];  // [cols] row, then [cols] gamma (mode 0)
     __shared__ float inv_s;
     const long long row = blockIdx.x, base = row * cols;
@@ -269,6 +279,7 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_staged(FB X, FB W, FB Y, 
 // kernels/strata.cu:367-377: per stream, gate = sigmoid(sign(v) sqrt(max(|v|, 1e-6))) with
 // v = key . query / sqrt(width).
 __global__ void k_ple_gate(Grid g, FB Key, FB Query, FB Gate, int width, int streams, unsigned *err) {
+    dep_enter();
     unsigned c, y, z;
     if (!my_group(g, c, y, z) || (int)c >= streams) return;
     const int t = threadIdx.x & 31;
@@ -299,6 +310,7 @@ __global__ void k_ple_gate(Grid g, FB Key, FB Query, FB Gate, int width, int str
 constexpr int kArgmaxThreads = 1024;
 __device__ __forceinline__ bool takes(float v, int i, float best, int id) { return v > best || (v == best && i < id); }
 __global__ void __launch_bounds__(kArgmaxThreads) k_argmax(FB Logits, IB Token, int count, unsigned *err) {
+    dep_enter();
     __shared__ float wbest[kArgmaxThreads / 32];
     __shared__ int wid[kArgmaxThreads / 32];
     const int tid = threadIdx.x, t = tid & 31, w = tid / 32;
@@ -395,6 +407,7 @@ constexpr int kAttnThreads = 512;
 __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads,
                                                             int kvHeads, int count, int position, float scale, int batch, IB Pos,
                                                             unsigned *err) {
+    dep_enter();
     __shared__ float scores[kMaxCells];
     __shared__ long long value_row[kMaxCells];  // element offset of each cell's value row, or -1
     __shared__ float total_s;
@@ -554,6 +567,7 @@ __device__ __forceinline__ float ac_ld_peer(const float *local, unsigned rank) {
 __global__ void __cluster_dims__(kAcCluster, 1, 1) __launch_bounds__(kAcThreads)
     k_attention_cl(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads, int kvHeads, int count, int position, float scale,
                    int batch, IB Pos, unsigned *err) {
+    dep_enter();
     __shared__ float scores[kMaxCells];
     __shared__ long long value_row[kMaxCells];
     __shared__ __align__(16) float vst[2][kAcChunk][32];  // value rows' slices of this CTA's dimensions
@@ -669,6 +683,7 @@ __global__ void __cluster_dims__(kAcCluster, 1, 1) __launch_bounds__(kAcThreads)
 constexpr int kGroupThreads = 512, kMaxGroup = 8;
 __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q, FB Keys, FB Values, FB Y, int dim, int heads, int kvHeads,
                                                                    int position, float scale, IB Pos, unsigned *err) {
+    dep_enter();
     extern __shared__ __align__(16) float group_smem[];  // [G][dim] queries, then [G][kMaxCells] scores
     __shared__ float totals[kMaxGroup];
     const int G = heads / kvHeads, kh = blockIdx.x, token = blockIdx.y, tid = threadIdx.x;
@@ -780,22 +795,23 @@ cudaError_t launch_attention_prompt(const KArg *a, int qi, int ki, int vi, int y
         g[0] >= (unsigned)heads) {
         cudaError_t e = cudaFuncSetAttribute(k_attention_group, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
         if (e != cudaSuccess) return e;
-        k_attention_group<<<dim3(kvHeads, g[2]), kGroupThreads, bytes, s>>>(grid_of(g), F(qi), F(ki), F(vi), F(yi), dim, heads, kvHeads,
+        launch_k(false, k_attention_group, dim3(kvHeads, g[2]), kGroupThreads, bytes, s, grid_of(g), F(qi), F(ki), F(vi), F(yi), dim, heads, kvHeads,
                                                                            position, scale, pos, err);
         return cudaGetLastError();
     }
     if (attention_cl_ok(a[ki], a[vi], dim, heads, kvHeads, g)) {
-        k_attention_cl<<<dim3(g[0] * kAcCluster, g[2]), kAcThreads, 0, s>>>(grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim,
+        launch_k(g[2] == 1, k_attention_cl, dim3(g[0] * kAcCluster, g[2]), kAcThreads, 0, s, grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim,
                                                                             heads, kvHeads, 0, position, scale, 1, pos, err);
         return cudaGetLastError();
     }
-    k_attention<<<dim3(g[0], g[2]), kAttnThreads, 0, s>>>(grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim, heads, kvHeads, 0,
+    launch_k(g[2] == 1, k_attention, dim3(g[0], g[2]), kAttnThreads, 0, s, grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim, heads, kvHeads, 0,
                                                           position, scale, 1, pos, err);
     return cudaGetLastError();
 }
 
 // kernels/strata.cu:328-330 and :453-456
 __global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, int position, int tokens, IB Pos, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, (long long)width * tokens);
     if (i < 0) return;
     if (Pos.n > 0) position = Pos.get(0, err);
@@ -807,12 +823,14 @@ __global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, i
 // kernels/strata.cu:357-359 and :457-459: attention output times sigmoid of the gate half of
 // each head's [query | gate] row.
 __global__ void k_attention_gate(Grid g, FB Attention, FB FullQ, FB Y, int dim, int heads, int tokens, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, (long long)dim * heads * tokens);
     if (i >= 0) Y.set(i, __fmul_rn(Attention.get(i, err), ref_sigmoid(FullQ.get((i / dim) * dim * 2 + dim + i % dim, err))), err);
 }
 
 // kernels/strata.cu:314-316
 __global__ void k_slice(Grid g, FB X, FB Y, int width, int rows, int stride, int offset, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, (long long)width * rows);
     if (i >= 0) Y.set(i, X.get((i / width) * stride + offset + i % width, err), err);
 }
@@ -821,6 +839,7 @@ __global__ void k_slice(Grid g, FB X, FB Y, int width, int rows, int stride, int
 
 // kernels/strata.cu:273-277 and :403-408: mean over streams of norm * sigmoid(gate).
 __global__ void k_hc_mix(Grid g, FB Norm, FB Gate, FB Mixed, int width, int streams, int tokens, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, (long long)width * tokens);
     if (i < 0) return;
     const long long token = i / width, d = i % width;
@@ -834,6 +853,7 @@ __global__ void k_hc_mix(Grid g, FB Norm, FB Gate, FB Mixed, int width, int stre
 
 // kernels/strata.cu:278-281 and :409-412: residual += output * 2 sigmoid(inject / streams).
 __global__ void k_hc_write(Grid g, FB Residual, FB Output, FB Inject, int width, int streams, int tokens, unsigned *err) {
+    dep_enter();
     const long long hc = (long long)width * streams;
     long long i = lane_index(g, hc * tokens);
     if (i < 0) return;
@@ -845,6 +865,7 @@ __global__ void k_hc_write(Grid g, FB Residual, FB Output, FB Inject, int width,
 
 // kernels/strata.cu:378-380 and :460-463
 __global__ void k_ple_broadcast(Grid g, FB Value, FB Gate, FB Y, int width, int streams, int tokens, unsigned *err) {
+    dep_enter();
     const long long hc = (long long)width * streams;
     long long i = lane_index(g, hc * tokens);
     if (i >= 0) Y.set(i, __fmul_rn(Value.get((i / hc) * width + i % width, err), Gate.get(i / width, err)), err);
@@ -852,6 +873,7 @@ __global__ void k_ple_broadcast(Grid g, FB Value, FB Gate, FB Y, int width, int 
 
 // kernels/strata.cu:381-383
 __global__ void k_ple_add(Grid g, FB Residual, FB Gated, FB Conv, int n, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, n);
     if (i >= 0) Residual.set(i, __fadd_rn(Residual.get(i, err), __fadd_rn(Gated.get(i, err), Conv.get(i, err))), err);
 }
@@ -863,6 +885,7 @@ __global__ void k_ple_add(Grid g, FB Residual, FB Gated, FB Conv, int n, unsigne
 // the tokens in order; neighbouring channels are neighbouring threads.
 __global__ void k_conv(Grid g, FB History, FB X, FB W, FB Y, int channels, int taps, int dilation, int activation, int tokens, int batch,
                        unsigned *err) {
+    dep_enter();
     long long c = lane_index(g, channels);
     if (c < 0) return;
     const long long history = (long long)(taps - 1) * dilation, hbase = c * history;
@@ -884,6 +907,7 @@ __global__ void k_conv(Grid g, FB History, FB X, FB W, FB Y, int channels, int t
 // and stored once per dispatch. Launched only when the host's layout checks cover every index.
 template <int TAPS, int DIL>
 __global__ void k_conv_reg(Grid g, FB History, FB X, FB W, FB Y, int channels, int activation, int tokens) {
+    dep_enter();
     constexpr int H = (TAPS - 1) * DIL;
     const long long c = lane_index(g, channels);
     if (c < 0) return;
@@ -914,11 +938,11 @@ cudaError_t launch_conv(const KArg *a, const unsigned g[3], int tokens, int batc
     const bool covered = c >= 1 && a[0].len >= c * (taps - 1) * dil && a[2].len >= c * taps && a[1].len >= tokens * c &&
                          a[3].len >= tokens * c;
     if (covered && taps == 4 && dil == 1) {
-        k_conv_reg<4, 1><<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
+        launch_k(tokens == 1, k_conv_reg<4, 1>, LANESL, grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
     } else if (covered && taps == 4 && dil == 3) {
-        k_conv_reg<4, 3><<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
+        launch_k(tokens == 1, k_conv_reg<4, 3>, LANESL, grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
     } else {
-        k_conv<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), channels, taps, dil, act, tokens, batch, err);
+        launch_k(tokens == 1, k_conv, LANESL, grid_of(g), F(0), F(1), F(2), F(3), channels, taps, dil, act, tokens, batch, err);
     }
     return cudaGetLastError();
 }
@@ -934,6 +958,7 @@ cudaError_t launch_conv(const KArg *a, const unsigned g[3], int tokens, int batc
 constexpr int kPrepThreads = 256;
 __global__ void __launch_bounds__(kPrepThreads) k_gdn_prep(FB History, FB X, FB W, FB Q, FB K, FB V, int keyDim, int valueDim, int hd,
                                                            float qScale, float epsilon) {
+    dep_enter();
     extern __shared__ float prep[];  // [2 hd] the block's convolved channels
     const int tid = threadIdx.x, warp = tid >> 5, t = tid & 31, span = 2 * hd;
     const long long c0 = (long long)blockIdx.x * span;
@@ -973,13 +998,14 @@ cudaError_t L_gdn_prep(const KArg *a, const unsigned g[3], cudaStream_t s, unsig
     if (hd < 32 || hd > 1024 || kd < 2 * hd || kd % (2 * hd) != 0 || vd % (2 * hd) != 0 || a[0].len < 3 * c || a[1].len < c ||
         a[2].len < 4 * c || a[3].len < kd || a[4].len < kd || a[5].len < vd)
         return cudaErrorInvalidValue;
-    k_gdn_prep<<<(unsigned)(c / (2 * hd)), kPrepThreads, (size_t)(2 * hd) * 4, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), (int)kd, (int)vd,
+    launch_k(true, k_gdn_prep, (unsigned)(c / (2 * hd)), kPrepThreads, (size_t)(2 * hd) * 4, s, F(0), F(1), F(2), F(3), F(4), F(5), (int)kd, (int)vd,
                                                                                    (int)hd, a[9].f, a[10].f);
     return cudaGetLastError();
 }
 
 // kernels/strata.cu:296-301 and :425-431: decay = exp(A softplus(alpha + dt)), strength = sigmoid(beta).
 __global__ void k_gdn_gates(Grid g, FB Alpha, FB Beta, FB A, FB Dt, FB Decay, FB Strength, int heads, int tokens, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, (long long)heads * tokens);
     if (i < 0) return;
     const float x = __fadd_rn(Alpha.get(i, err), Dt.get(i % heads, err));
@@ -993,6 +1019,7 @@ __global__ void k_gdn_gates(Grid g, FB Alpha, FB Beta, FB A, FB Dt, FB Decay, FB
 // Value head h reads key head h % keyHeads.
 __global__ void k_gdn(Grid g, FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int dim, int keyHeads, int valueHeads, int tokens,
                       unsigned *err) {
+    dep_enter();
     const long long stride = (long long)valueHeads * dim;
     long long jh = lane_index(g, stride);
     if (jh < 0) return;
@@ -1026,6 +1053,7 @@ __global__ void k_gdn(Grid g, FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB 
 template <int DIM>
 __global__ void __launch_bounds__(DIM) k_gdn_regs(FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int keyHeads, int valueHeads,
                                                   int tokens, long long columns) {
+    dep_enter();
     __shared__ float ks[DIM], qs[DIM];
     const volatile float *kv = ks, *qv = qs;
     const long long stride = (long long)valueHeads * DIM;
@@ -1071,10 +1099,10 @@ cudaError_t launch_gdn(const Grid g, const KArg *a, int tokens, cudaStream_t s, 
                          a[2].len >= (long long)tokens * kh * dim && a[3].len >= tokens * stride && a[4].len >= (long long)tokens * vh &&
                          a[5].len >= (long long)tokens * vh && a[6].len >= tokens * stride && kh >= 1 && vh >= 1;
     if (dim == 128 && covered) {
-        k_gdn_regs<128><<<(unsigned)((columns + 127) / 128), 128, 0, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), F(6), kh, vh, tokens,
+        launch_k(tokens == 1, k_gdn_regs<128>, (unsigned)((columns + 127) / 128), 128, 0, s, F(0), F(1), F(2), F(3), F(4), F(5), F(6), kh, vh, tokens,
                                                                           columns);
     } else {
-        k_gdn<<<(unsigned)(((unsigned long long)g.x * STRATA_LANES + 255) / 256), 256, 0, s>>>(g, F(0), F(1), F(2), F(3), F(4), F(5), F(6),
+        launch_k(tokens == 1, k_gdn, (unsigned)(((unsigned long long)g.x * STRATA_LANES + 255) / 256), 256, 0, s, g, F(0), F(1), F(2), F(3), F(4), F(5), F(6),
                                                                                              dim, kh, vh, tokens, err);
     }
     return cudaGetLastError();
@@ -1102,6 +1130,8 @@ __global__ void __launch_bounds__(kHcInThreads) k_hc_in(FB Residual, FB NormW, F
     const int warp = threadIdx.x / 32, t = threadIdx.x & 31, hc = width * streams, j = blockIdx.x;
     float *x = hc_in, *w = hc_in + hc, *gam = hc_in + 2 * (size_t)hc;
     const float *wsrc = j < rank ? DownW.p + (long long)j * hc : InjectW.p + (long long)(j - rank) * hc;
+    if (threadIdx.x == 0) prefetch_l2(wsrc, (unsigned long long)hc * 4);  // weights: before the previous kernel ends
+    dep_enter();
     if (((reinterpret_cast<uintptr_t>(Residual.p) | reinterpret_cast<uintptr_t>(wsrc) | reinterpret_cast<uintptr_t>(NormW.p)) & 15) == 0 &&
         hc % 4 == 0) {
         for (int k = 4 * threadIdx.x; k < hc; k += 4 * kHcInThreads) {
@@ -1143,6 +1173,9 @@ __global__ void __launch_bounds__(kHcInThreads) k_hc_in(FB Residual, FB NormW, F
 __global__ void __launch_bounds__(kHcThreads) k_hc_out(FB Norm, FB Down, FB UpW, FB Mixed, int width, int streams, int rank, float scale) {
     extern __shared__ __align__(16) float hc_lo[];  // [rank]
     const int warp = threadIdx.x / 32, t = threadIdx.x & 31;
+    if (t < streams && blockIdx.x * (kHcThreads / 32) + warp < width)  // this warp's gate rows, before the previous kernel ends
+        prefetch_l2(UpW.p + ((long long)t * width + blockIdx.x * (kHcThreads / 32) + warp) * rank, (unsigned long long)rank * 4);
+    dep_enter();
     for (int k = threadIdx.x; k < rank; k += kHcThreads) hc_lo[k] = ref_silu(__fmul_rn(Down.p[k], scale));
     __syncthreads();
     const int d = blockIdx.x * (kHcThreads / 32) + warp;
@@ -1194,6 +1227,7 @@ __global__ void __launch_bounds__(kHcThreads) k_hc_out(FB Norm, FB Down, FB UpW,
 // strata_embed_token: for each of `tokens` ids in Token, that row of the table into every stream
 // of the token's residual (token k at k * width * streams): strata_embedding format 0 per token.
 __global__ void k_embed_token(Grid g, FB Table, IB Token, FB Residual, int width, int streams, int vocab, int tokens, unsigned *err) {
+    dep_enter();
     long long i = lane_index(g, (long long)width * tokens);
     if (i < 0) return;
     const long long k = i / width, d = i % width;
@@ -1207,51 +1241,62 @@ __global__ void k_embed_token(Grid g, FB Table, IB Token, FB Residual, int width
 }
 
 // ---------------------------------------------------------------- launchers
+}  // namespace
+
+bool engine_pdl() {
+    static const bool on = [] {
+        const char *v = std::getenv("STRATA_ENGINE_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+namespace {
 
 constexpr int kOneToken = 1;  // the decode entries: one token
 cudaError_t L_embedding(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_embedding<<<LANESL>>>(grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, a[12].i,
+    launch_k(true, k_embedding, LANESL, grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, a[12].i,
                             a[13].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_embed(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_embed<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, kOneToken, err);
+    launch_k(true, k_embed, LANESL, grid_of(g), F(0), F(1), a[2].i, a[3].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_embed_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_embed<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, a[4].i, err);
+    launch_k(false, k_embed, LANESL, grid_of(g), F(0), F(1), a[2].i, a[3].i, a[4].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_frequencies(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope_frequencies<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].f, err);
+    launch_k(true, k_rope_frequencies, LANESL, grid_of(g), F(0), F(1), a[2].i, a[3].f, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_table(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope_table<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, err);
+    launch_k(true, k_rope_table, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_position(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, 0, IB{nullptr, 0}, err);
+    launch_k(true, k_rope, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, 0, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, kOneToken, 1, IB{nullptr, 0}, err);
+    launch_k(true, k_rope, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, kOneToken, 1, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i, 2, IB{nullptr, 0}, err);
+    launch_k(false, k_rope, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, 0, a[7].i, 2, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_embed_token(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_embed_token<<<LANESL>>>(grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, err);
+    launch_k(a[6].i == 1, k_embed_token, LANESL, grid_of(g), F(0), I(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_rope_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_rope<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[5].i, a[6].i, a[7].i, 0, a[8].i, 0, I(4), err);
+    launch_k(a[8].i == 1, k_rope, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[5].i, a[6].i, a[7].i, 0, a[8].i, 0, I(4), err);
     return cudaGetLastError();
 }
 cudaError_t L_kv_append_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[5].i, 0, a[6].i, I(4), err);
+    launch_k(a[6].i == 1, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[5].i, 0, a[6].i, I(4), err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1263,21 +1308,21 @@ cudaError_t L_hc_in(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned
     if (streams < 1 || streams > 64 || bytes > 227 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(k_hc_in, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e != cudaSuccess) return e;
-    k_hc_in<<<(unsigned)(rank + streams), kHcInThreads, bytes, s>>>(F(0), F(1), F(2), F(3), F(4), F(5), F(6), width, streams, rank, a[10].f);
+    launch_k(true, k_hc_in, (unsigned)(rank + streams), kHcInThreads, bytes, s, F(0), F(1), F(2), F(3), F(4), F(5), F(6), width, streams, rank, a[10].f);
     return cudaGetLastError();
 }
 cudaError_t L_hc_out(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     const int width = a[4].i, streams = a[5].i, rank = a[6].i;
-    k_hc_out<<<(unsigned)((width + kHcThreads / 32 - 1) / (kHcThreads / 32)), kHcThreads, (size_t)rank * 4, s>>>(
+    launch_k(true, k_hc_out, (unsigned)((width + kHcThreads / 32 - 1) / (kHcThreads / 32)), kHcThreads, (size_t)rank * 4, s, 
         F(0), F(1), F(2), F(3), width, streams, rank, a[7].f);
     return cudaGetLastError();
 }
 cudaError_t L_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_gemv<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    launch_k(true, k_gemv, GROUPS, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_quant_gemv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_quant_gemv<<<GROUPS>>>(grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, err);
+    launch_k(true, k_quant_gemv, GROUPS, grid_of(g), F(0), U(1), F(2), F(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, a[9].i, a[10].i, a[11].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_norm(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1288,27 +1333,27 @@ cudaError_t L_norm(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned 
         (mode != 0 || a[1].len >= std::min(rows, wrows) * cols)) {
         cudaError_t e = cudaFuncSetAttribute(k_norm_staged, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
         if (e != cudaSuccess) return e;
-        k_norm_staged<<<(unsigned)rows, kNormThreads, bytes, s>>>(F(0), F(1), F(2), a[3].i, a[5].i, mode, a[7].f, a[8].f);
+        launch_k(rows <= 64, k_norm_staged, (unsigned)rows, kNormThreads, bytes, s, F(0), F(1), F(2), a[3].i, a[5].i, mode, a[7].f, a[8].f);
         return cudaGetLastError();
     }
-    k_norm<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].f, a[8].f, err);
+    launch_k(a[4].i <= 64, k_norm, GROUPS, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, a[6].i, a[7].f, a[8].f, err);
     return cudaGetLastError();
 }
 cudaError_t L_ple_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_ple_gate<<<GROUPS>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, err);
+    launch_k(true, k_ple_gate, GROUPS, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_argmax(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_argmax<<<1, kArgmaxThreads, 0, s>>>(F(0), I(1), a[2].i, err);
+    launch_k(true, k_argmax, 1, kArgmaxThreads, 0, s, F(0), I(1), a[2].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     if (attention_cl_ok(a[1], a[2], a[5].i, a[6].i, a[7].i, g)) {
-        k_attention_cl<<<dim3(g[0] * kAcCluster, 1), kAcThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i,
+        launch_k(true, k_attention_cl, dim3(g[0] * kAcCluster, 1), kAcThreads, 0, s, grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i,
                                                                          a[8].i, 0, a[9].f, 0, IB{nullptr, 0}, err);
         return cudaGetLastError();
     }
-    k_attention<<<dim3(g[0], 1), kAttnThreads, 0, s>>>(grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, 0, a[9].f, 0,
+    launch_k(true, k_attention, dim3(g[0], 1), kAttnThreads, 0, s, grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, 0, a[9].f, 0,
                                                        IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
@@ -1316,51 +1361,51 @@ cudaError_t L_attention_batch(const KArg *a, const unsigned g[3], cudaStream_t s
     return launch_attention_prompt(a, 0, 1, 2, 3, a[4].i, a[5].i, a[6].i, a[7].i, a[8].f, IB{nullptr, 0}, g, s, err);
 }
 cudaError_t L_kv_append(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, kOneToken, IB{nullptr, 0}, err);
+    launch_k(true, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, kOneToken, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_kv_append_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_kv_append<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, IB{nullptr, 0}, err);
+    launch_k(false, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, IB{nullptr, 0}, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention_gate<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
+    launch_k(true, k_attention_gate, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_gate_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_attention_gate<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    launch_k(false, k_attention_gate, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_slice(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_slice<<<LANESL>>>(grid_of(g), F(0), F(1), a[2].i, a[3].i, a[4].i, a[5].i, err);
+    launch_k((long long)a[2].i * a[3].i <= 16384, k_slice, LANESL, grid_of(g), F(0), F(1), a[2].i, a[3].i, a[4].i, a[5].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_hc_mix(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_hc_mix<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
+    launch_k(true, k_hc_mix, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_hc_mix_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_hc_mix<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    launch_k(false, k_hc_mix, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_hc_write(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_hc_write<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
+    launch_k(true, k_hc_write, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_hc_write_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_hc_write<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    launch_k(false, k_hc_write, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_ple_broadcast(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_ple_broadcast<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
+    launch_k(true, k_ple_broadcast, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_ple_broadcast_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_ple_broadcast<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
+    launch_k(false, k_ple_broadcast, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, a[4].i, a[5].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_ple_add(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_ple_add<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), a[3].i, err);
+    launch_k(true, k_ple_add, LANESL, grid_of(g), F(0), F(1), F(2), a[3].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_conv(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1370,11 +1415,11 @@ cudaError_t L_conv_batch(const KArg *a, const unsigned g[3], cudaStream_t s, uns
     return launch_conv(a, g, a[8].i, 1, s, err);
 }
 cudaError_t L_gdn_gates(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_gdn_gates<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, kOneToken, err);
+    launch_k(true, k_gdn_gates, LANESL, grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, kOneToken, err);
     return cudaGetLastError();
 }
 cudaError_t L_gdn_gates_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    k_gdn_gates<<<LANESL>>>(grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, a[7].i, err);
+    launch_k(false, k_gdn_gates, LANESL, grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), a[6].i, a[7].i, err);
     return cudaGetLastError();
 }
 cudaError_t L_gdn_step(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {

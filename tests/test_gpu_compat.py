@@ -118,6 +118,25 @@ def test_random_kernels_bit_exact_vs_oracle(b, port):
     assert np.array_equal(bits(b.read(y)), bits(want))
 
 
+@pytest.mark.parametrize("rows,cols,offset", [(512, 64, 0), (2048, 4096, 0), (8192, 2048, 3), (1000, 8192, 1), (600, 25600, 0),
+                                             (70001, 128, 5), (300, 2048, 0), (4100, 2048, 2), (700, 2112, 0)])
+def test_project_one_token_bit_exact(b, port, rows, cols, offset):
+    """One-token strata_project over the weight-stream kernel (at least 512 rows: a ring of
+    bulk-copied row slots, from one slot per block at 25600 columns to refills of a 64-slot ring
+    at 473 rows per block), the staging blocks (fewer rows) and the half-warp form: bit-identical
+    to the oracle."""
+    rng = np.random.default_rng(rows + cols)
+    X = rng.normal(0, 1, (1, cols)).astype(np.float32)
+    W = rng.normal(0, 0.03, (rows, cols)).astype(np.float32)
+    want = np.full(rows + offset + 4, -7, np.float32)
+    port.run("strata_project", (rows, 1, 1), X=X, W=W, Y=want, cols=cols, rows=rows, tokens=1, outputStride=rows + offset,
+             outputOffset=offset)
+    y = b.alloc(np.full(rows + offset + 4, -7, np.float32))
+    b.run("strata_project", dict(X=b.alloc(X), W=b.alloc(W), Y=y, cols=cols, rows=rows, tokens=1, outputStride=rows + offset,
+                                 outputOffset=offset), [rows, 1, 1])
+    assert np.array_equal(bits(b.read(y)), bits(want))
+
+
 def test_elementwise_modes_cover_expf_range(b, port):
     """SiLU / sigmoid exercise the device expf on 4M inputs spanning its whole range."""
     rng = np.random.default_rng(3)
