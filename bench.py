@@ -36,9 +36,10 @@ configurations, each timed the same way on the same GPU(s):
           the 512 experts sharded, NCCL dispatch and return between the ranks when N >= 2;
           tokens/s (max over ranks), per-GPU TFLOP/s, rank 0's phase split, and
           efficiency_vs_n1 when an N=1 run on the same host left its number in /tmp;
-  model48                 BASELINE config 5 at batch 1 (one GPU only): the 48-layer synthetic
-          model through the whole engine, prompt 1920 prefilled in chunks of 64, 128 greedy
-          decode tokens; decode ms per token and prefill tokens/s by the host clock.
+  model48                 BASELINE config 5 (one GPU only): the 48-layer synthetic model through
+          the whole engine, prompt 1920 prefilled in chunks of 64, 128 greedy decode tokens at
+          batch 1 and at batch 64 (64 sequences from the prompt's state, each with its own
+          seeded first token); decode ms per token or step and prefill tokens/s by the host clock.
 
 Multi-GPU: the headline has every rank run its own replica of the layer stack (the reference
 has no multi-GPU path); scaling is weak. The `ep` block (and `--ep`, which times BASELINE
@@ -677,12 +678,15 @@ def prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K):
             "phase_ms_per_step": {k: v / max(1, calls) for k, v in ph.items()}}
 
 
-def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_prefill=False, profile_step=False):
+def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_prefill=False, profile_step=False, batch=64):
     """The full-model workload on backend b: the seeded synthetic model (stratacuda_b200.synthetic)
     resident in HBM, a prompt prefilled in chunks of 64, then greedy decode at batch 1, all through
     StrataEngine (the reference host's call order). Timed by the host clock around each phase,
-    which ends in the argmax read: the host dispatch of every entry is inside the numbers."""
-    from stratacuda_b200.engine import StrataEngine
+    which ends in the argmax read: the host dispatch of every entry is inside the numbers.
+    With `batch` > 1, greedy decode of `batch` sequences together (SequenceBatch) is timed too:
+    every sequence starts from the prefilled prompt's state and takes its own seeded first token,
+    then `decode` steps of all sequences (each step reads the batch's tokens back)."""
+    from stratacuda_b200.engine import SequenceBatch, StrataEngine
     from stratacuda_b200.synthetic import MODEL_GEOMETRY, MOE_MODES, DeviceStore
 
     g = dict(MODEL_GEOMETRY, layers=layers)
@@ -692,8 +696,14 @@ def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_p
     t_gen = time.perf_counter() - t0
     engine = StrataEngine.create(store, b, MOE_MODES[mode], graph=graph)
     prompt = np.random.default_rng(7).integers(0, g["vocab"], prompt_len).tolist()
-    for _ in range(max(1, warmup // 3)):  # warm-up: pools, RoPE table, the decode graph's capture
+    seqs = SequenceBatch(engine, batch, graph=graph) if batch > 1 else None
+    for _ in range(max(1, warmup // 3)):  # warm-up: pools, RoPE table, the decode graphs' capture
         engine.prefill(prompt[:64], chunk_size=64)
+        if seqs is not None:
+            for s in range(batch):
+                seqs.admit(s, engine)
+            seqs.step(list(range(batch)))
+            seqs.step(list(range(batch)))
         engine.step(1)
         engine.step(2)
         engine.reset()
@@ -709,6 +719,19 @@ def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_p
     else:
         r = engine.prefill(prompt, chunk_size=64)
     t_prefill = time.perf_counter() - t0
+    batch_out = {}
+    if seqs is not None:
+        for s in range(batch):
+            seqs.admit(s, engine)
+        step_tokens = np.random.default_rng(8).integers(0, g["vocab"], batch).tolist()
+        b.idle()
+        t0 = time.perf_counter()
+        for _ in range(decode):
+            step_tokens = seqs.step(step_tokens)["tokens"]
+        t_batch = time.perf_counter() - t0
+        batch_out = {f"decode_b{batch}_tokens_per_s": batch * decode / t_batch, f"decode_b{batch}_ms_per_step": 1e3 * t_batch / decode,
+                     f"decode_b{batch}_last_tokens": step_tokens[:8]}
+        seqs.dispose()
     token, tokens = r["token"], []
     t0 = time.perf_counter()
     for k in range(decode):
@@ -724,10 +747,11 @@ def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_p
             torch.cuda.cudart().cudaProfilerStop()
     t_decode = time.perf_counter() - t0
     out = {"decode_tokens_per_s": decode / t_decode, "decode_ms_per_token": 1e3 * t_decode / decode,
-           "prefill_tokens_per_s": prompt_len / t_prefill, "prefill_s": t_prefill, "generate_s": t_gen,
+           "prefill_tokens_per_s": prompt_len / t_prefill, "prefill_s": t_prefill, "generate_s": t_gen, **batch_out,
            "resident_gb": store.bytes_resident() / 1e9,
            "config": {"workload": f"{g['layers']}-layer synthetic model, hidden {g['width']}, vocab {g['vocab']}, prompt {prompt_len}, "
-                                  f"decode {decode}, chunk 64", "moe_mode": mode, "decode_graph": graph,
+                                  f"decode {decode}, chunk 64" + (f"; decode batch {batch} from the prompt's state, seeded first tokens"
+                                                                  if batch > 1 else ""), "moe_mode": mode, "decode_graph": graph,
                       "timing": "host clock, end to end"},
            "first_tokens": tokens[:8]}
     engine.dispose()
@@ -748,7 +772,7 @@ def run_model_arm(args):
 
     b = CudaBackend(0)
     r = model_run(b, args.model_layers, args.prompt, args.decode, args.warmup, args.mode, graph=not args.no_graph,
-                  profile_prefill=args.profile_prefill, profile_step=args.profile_step)
+                  profile_prefill=args.profile_prefill, profile_step=args.profile_step, batch=args.model_batch)
     line = {"metric": "full-model tokens/s (prefill; greedy decode b=1)", "workload": "model48", "value": r["decode_tokens_per_s"],
             "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "dtype": "f32+q2", "data": "synthetic", **r}
     b.dispose()
@@ -774,6 +798,7 @@ def main():
     ap.add_argument("--ep-tokens", type=int, default=16384, help="tokens of the expert-parallel job (split over the ranks)")
     ap.add_argument("--model", action="store_true", help="the full-model workload (48-layer synthetic model, 1 GPU)")
     ap.add_argument("--model-layers", type=int, default=48)
+    ap.add_argument("--model-batch", type=int, default=64, help="--model: sequences decoded together after the batch-1 decode (1: none)")
     ap.add_argument("--prompt", type=int, default=1920, help="--model: prompt tokens (context 2048 = prompt + decode)")
     ap.add_argument("--decode", type=int, default=128, help="--model: greedy decode tokens")
     ap.add_argument("--profile-prefill", action="store_true",

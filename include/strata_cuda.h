@@ -109,7 +109,21 @@ int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *t
  *   strata_hc_in  (Residual, NormW, DownW, InjectW, Norm, Down, Inject, width, streams, rank, epsilon):
  *                 strata_norm of the streams rows, then the down and inject projections of the norm
  *   strata_hc_out (Norm, Down, UpW, Mixed, width, streams, rank, scale):
- *                 strata_elementwise mode 1, the up projection and strata_hc_mix */
+ *                 strata_elementwise mode 1, the up projection and strata_hc_mix
+ *
+ * Six more serve decode of many independent sequences at once (a serving batch; the reference
+ * holds one session per engine, src/engine.js:53-72). Token t of a dispatch belongs to sequence t,
+ * which has its own position Positions[t] and its own slice of the cache, history or state
+ * buffer; each gives sequence t what the one-sequence entry in brackets gives it alone:
+ *   strata_rope_seqs      (X, Cos, Sin, Y, Positions, dim, heads, rotary, tokens)   [strata_rope_position]
+ *   strata_kv_append_seqs (K, V, Keys, Values, Positions, width, cells, tokens)     [strata_kv_append;
+ *                          sequence t's cache is cells [t cells, (t + 1) cells) of Keys / Values]
+ *   strata_attention_seqs (Q, Keys, Values, Positions, Y, dim, heads, kvHeads, cells, scale;
+ *                          sequences = groups[2])                                   [strata_attention_batch]
+ *   strata_conv_seqs      (History, X, W, Y, channels, taps, dilation, activation, tokens)  [strata_conv]
+ *   strata_gdn_seqs       (State, Q, K, V, Decay, Beta, Y, dim, keyHeads, valueHeads, tokens) [strata_gdn_step]
+ *   strata_argmax_rows    (Logits, Tokens, count, rows)                             [strata_argmax per row]
+ * A position outside [0, cells) is reported as an index error, never written. */
 int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int nargs, const uint32_t groups[3]);
 
 /* ---- synchronisation and introspection (idle, flush, info: src/backend.js:119-120) ---- */

@@ -161,7 +161,7 @@ std::vector<Entry> &entries() {
 bool int_in(long long v, long long lo = 1, long long hi = 0x7fffffff) { return v >= lo && v <= hi; }
 
 // src/backend.js:10-56 for the entries this library serves. Returns 0 or an error code.
-int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params, const std::vector<KArg> &a) {
+int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params, const std::vector<KArg> &a, const uint32_t groups[3]) {
     auto idx = [&](const char *p) {
         for (size_t i = 0; i < params.size(); ++i)
             if (params[i].name == p) return (int)i;
@@ -337,6 +337,55 @@ int validate(strata_ctx *ctx, const char *name, const std::vector<Param> &params
             if (!int_in(I(p))) return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p);
         if (I("heads") % I("kvHeads")) return fail(ctx, STRATA_ERR_RANGE, "Attention heads must be divisible by KV heads");
         ok = fits(I("heads") * I("dim"), "Q") && fits(1, "Position");
+    }
+    // Sequence-batch decode entries: one token per sequence, each sequence with its own position,
+    // cache, history or state; every per-sequence region must lie inside its buffer.
+    if (n == "strata_rope_seqs" || n == "strata_kv_append_seqs" || n == "strata_attention_seqs" || n == "strata_conv_seqs" ||
+        n == "strata_gdn_seqs" || n == "strata_argmax_rows") {
+        static const struct {
+            const char *entry, *params;
+        } kPositive[] = {
+            {"strata_rope_seqs", "dim heads rotary tokens"},     {"strata_kv_append_seqs", "width cells tokens"},
+            {"strata_attention_seqs", "dim heads kvHeads cells"}, {"strata_conv_seqs", "channels taps dilation tokens"},
+            {"strata_gdn_seqs", "dim keyHeads valueHeads tokens"}, {"strata_argmax_rows", "count rows"},
+        };
+        for (const auto &d : kPositive) {
+            if (n != d.entry) continue;
+            std::string list(d.params), p;
+            for (size_t at = 0; at <= list.size(); ++at) {
+                if (at < list.size() && list[at] != ' ') {
+                    p += list[at];
+                    continue;
+                }
+                if (!p.empty() && !int_in(I(p.c_str())))
+                    return fail(ctx, STRATA_ERR_RANGE, "%s.%s must be an integer in [1, 2147483647]", name, p.c_str());
+                p.clear();
+            }
+        }
+        if (n == "strata_rope_seqs") {
+            if (I("rotary") % 2 || I("rotary") > I("dim") || len("X") != I("dim") * I("heads") * I("tokens") || len("Y") != len("X"))
+                return fail(ctx, STRATA_ERR_LAYOUT, "Invalid RoPE layout");
+            ok = fits(I("tokens"), "Positions");
+        } else if (n == "strata_kv_append_seqs") {
+            const long long t = I("tokens"), w = I("width"), cache = t * I("cells") * w;
+            ok = fits(t * w, "K") && fits(t * w, "V") && fits(cache, "Keys") && fits(cache, "Values") && fits(t, "Positions");
+        } else if (n == "strata_attention_seqs") {
+            if (I("heads") % I("kvHeads")) return fail(ctx, STRATA_ERR_RANGE, "Attention heads must be divisible by KV heads");
+            if (I("cells") > 2048) return fail(ctx, STRATA_ERR_RANGE, "attention cells must be an integer in [1, 2048]");
+            const long long t = groups[2], cache = t * I("cells") * I("kvHeads") * I("dim");
+            ok = fits(t * I("heads") * I("dim"), "Q") && fits(t * I("heads") * I("dim"), "Y") && fits(cache, "Keys") &&
+                 fits(cache, "Values") && fits(t, "Positions");
+        } else if (n == "strata_conv_seqs") {
+            const long long c = I("channels"), t = I("tokens");
+            ok = fits(t * c * (I("taps") - 1) * I("dilation"), "History") && fits(c * I("taps"), "W") && fits(t * c, "X") &&
+                 fits(t * c, "Y");
+        } else if (n == "strata_gdn_seqs") {
+            const long long d = I("dim"), vh = I("valueHeads"), kh = I("keyHeads"), t = I("tokens");
+            ok = fits(t * d * vh * d, "State") && fits(t * kh * d, "Q") && fits(t * kh * d, "K") && fits(t * vh * d, "V") &&
+                 fits(t * vh * d, "Y") && fits(t * vh, "Decay") && fits(t * vh, "Beta");
+        } else {
+            ok = fits(I("rows") * I("count"), "Logits") && fits(I("rows"), "Tokens");
+        }
     }
     if (n == "strata_hc_in" || n == "strata_hc_out") {  // every index the kernels read or write lies inside its buffer
         const long long w = I("width"), st = I("streams"), r = I("rank"), hc = w * st;
@@ -564,7 +613,7 @@ int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int na
         }
         vals[i] = v;
     }
-    if (int r = validate(ctx, name, entry->params, vals)) return r;
+    if (int r = validate(ctx, name, entry->params, vals, groups)) return r;
     if (int r = use_device(ctx)) return r;
     const unsigned g[3] = {groups[0], groups[1], groups[2]};
     cudaError_t e = entry->spec->launch(vals.data(), g, ctx->stream, ctx->err_dev);

@@ -137,21 +137,23 @@ __global__ void k_rope_table(Grid g, FB High, FB Low, FB Cos, FB Sin, int rotary
 }
 
 // kernels/strata.cu:113-120 (rope_position: table row position + token), :319-327 (rope: one
-// row of Cos / Sin) and :445-452 (rope_batch: table row = token). `mode` 0 / 1 / 2 picks which.
+// row of Cos / Sin) and :445-452 (rope_batch: table row = token). `mode` 0 / 1 / 2 picks which;
+// mode 3 (strata_rope_seqs, no reference counterpart) rotates token t's rows at Pos[t], the
+// position of the sequence that token t belongs to.
 __global__ void k_rope(Grid g, FB X, FB Cos, FB Sin, FB Y, int dim, int heads, int rotary, int position, int tokens, int mode, IB Pos,
                        unsigned *err) {
     dep_enter();
     long long i = lane_index(g, (long long)dim * heads * tokens);
     if (i < 0) return;
-    if (Pos.n > 0) position = Pos.get(0, err);  // strata_rope_at: the position lives on the device
-    const long long d = i % dim;
+    const long long d = i % dim, token = i / ((long long)dim * heads);
+    if (Pos.n > 0) position = Pos.get(mode == 3 ? token : 0, err);  // strata_rope_at / _seqs: positions live on the device
     if (d >= rotary) {
         Y.set(i, X.get(i, err), err);
         return;
     }
     const int half = rotary / 2;
-    const long long pair = d % half, row = i - d, token = i / ((long long)dim * heads);
-    const long long angle = mode == 1 ? pair : (mode == 0 ? (position + token) : token) * half + pair;
+    const long long pair = d % half, row = i - d;
+    const long long angle = mode == 1 ? pair : (mode == 0 ? (position + token) : mode == 3 ? position : token) * half + pair;
     const float a = X.get(row + pair, err), b = X.get(row + pair + half, err);
     Y.set(i, rotate(a, b, Cos.get(angle, err), Sin.get(angle, err), d < half), err);
 }
@@ -309,20 +311,23 @@ __global__ void k_ple_gate(Grid g, FB Key, FB Query, FB Gate, int width, int str
 // then warp shuffles and a shared-memory round combine the threads' bests.
 constexpr int kArgmaxThreads = 1024;
 __device__ __forceinline__ bool takes(float v, int i, float best, int id) { return v > best || (v == best && i < id); }
+// Block r takes row r of Logits (strata_argmax_rows, no reference counterpart: one greedy token per
+// sequence of a decode batch); strata_argmax is the one-block case.
 __global__ void __launch_bounds__(kArgmaxThreads) k_argmax(FB Logits, IB Token, int count, unsigned *err) {
     dep_enter();
     __shared__ float wbest[kArgmaxThreads / 32];
     __shared__ int wid[kArgmaxThreads / 32];
     const int tid = threadIdx.x, t = tid & 31, w = tid / 32;
+    const long long base = (long long)blockIdx.x * count;
     float best = -3.402823e38f;
     int id = count;
-    const bool fast = covers(Logits, 0, count);
+    const bool fast = covers(Logits, base, count);
     int i = tid;
     if (fast) {
         for (; i + 7 * kArgmaxThreads < count; i += 8 * kArgmaxThreads) {
             float v[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = Logits.p[i + u * kArgmaxThreads];
+            for (int u = 0; u < 8; ++u) v[u] = Logits.p[base + i + u * kArgmaxThreads];
 #pragma unroll
             for (int u = 0; u < 8; ++u)
                 if (takes(v[u], i + u * kArgmaxThreads, best, id)) {
@@ -332,7 +337,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) k_argmax(FB Logits, IB Token, 
         }
     }
     for (; i < count; i += kArgmaxThreads) {
-        const float v = Logits.get(i, err);
+        const float v = Logits.get(base + i, err);
         if (takes(v, i, best, id)) {
             best = v;
             id = i;
@@ -364,7 +369,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) k_argmax(FB Logits, IB Token, 
                 id = oi;
             }
         }
-        if (t == 0) Token.set(0, id, err);
+        if (t == 0) Token.set(blockIdx.x, id, err);
     }
 }
 
@@ -406,7 +411,7 @@ __device__ __forceinline__ void ld16_f(const float *const (&p)[16], float (&v)[1
 constexpr int kAttnThreads = 512;
 __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads,
                                                             int kvHeads, int count, int position, float scale, int batch, IB Pos,
-                                                            unsigned *err) {
+                                                            int seqCells, unsigned *err) {
     dep_enter();
     __shared__ float scores[kMaxCells];
     __shared__ long long value_row[kMaxCells];  // element offset of each cell's value row, or -1
@@ -414,9 +419,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Key
     const unsigned h = blockIdx.x, token = blockIdx.y;
     const int tid = threadIdx.x;
     if ((int)h >= heads) return;
-    if (Pos.n > 0) position = Pos.get(0, err);  // strata_attention_at: the prefix of one query
-    const long long n = batch ? (long long)position + token + 1 : count;
-    if (n < 1 || n > kMaxCells) {
+    // strata_attention_at: the prefix of one query; strata_attention_seqs (seqCells > 0): query
+    // token t is sequence t's, over cells 0 .. Pos[t] of its own cache of seqCells cells
+    if (Pos.n > 0) position = Pos.get(seqCells > 0 ? (long long)token : 0, err);
+    const long long n = seqCells > 0 ? (long long)position + 1 : batch ? (long long)position + token + 1 : count;
+    const long long cell0 = seqCells > 0 ? (long long)token * seqCells : 0;
+    if (n < 1 || n > kMaxCells || (seqCells > 0 && n > seqCells)) {
         if (tid == 0) raise_error(err, kErrIndex);
         return;
     }
@@ -426,7 +434,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(Grid g, FB Q, FB Key
     const bool vec = q_ok && dim % 4 == 0 && ((reinterpret_cast<uintptr_t>(Q.p) | reinterpret_cast<uintptr_t>(Keys.p)) & 15) == 0;
     for (int c = tid; c < n; c += kAttnThreads) {  // A
         const long long cell = batch ? c : (long long)Cells.get(c, err);
-        const long long kb = (cell * kvHeads + kh) * dim;
+        const long long kb = ((cell0 + cell) * kvHeads + kh) * dim;
         const bool key_ok = cell >= 0 && covers(Keys, kb, dim), value_ok = cell >= 0 && covers(Values, kb, dim);
         if (!key_ok || !value_ok) raise_error(err, kErrIndex);
         float score = 0.0f;
@@ -566,7 +574,7 @@ __device__ __forceinline__ float ac_ld_peer(const float *local, unsigned rank) {
 }
 __global__ void __cluster_dims__(kAcCluster, 1, 1) __launch_bounds__(kAcThreads)
     k_attention_cl(Grid g, FB Q, FB Keys, FB Values, IB Cells, FB Y, int dim, int heads, int kvHeads, int count, int position, float scale,
-                   int batch, IB Pos, unsigned *err) {
+                   int batch, IB Pos, int seqCells, unsigned *err) {
     dep_enter();
     __shared__ float scores[kMaxCells];
     __shared__ long long value_row[kMaxCells];
@@ -574,10 +582,11 @@ __global__ void __cluster_dims__(kAcCluster, 1, 1) __launch_bounds__(kAcThreads)
     __shared__ float total_s;
     const unsigned rank = ac_rank(), h = blockIdx.x / kAcCluster, token = blockIdx.y;
     const int tid = threadIdx.x;
-    if (Pos.n > 0) position = Pos.get(0, err);
-    const long long n = batch ? (long long)position + token + 1 : count;
+    if (Pos.n > 0) position = Pos.get(seqCells > 0 ? (long long)token : 0, err);  // as in k_attention
+    const long long n = seqCells > 0 ? (long long)position + 1 : batch ? (long long)position + token + 1 : count;
+    const long long cell0 = seqCells > 0 ? (long long)token * seqCells : 0;
     // every CTA of the cluster takes the same branch: the cluster barriers below are reached by all
-    const bool run = (int)h < heads && n >= 1 && n <= kMaxCells;
+    const bool run = (int)h < heads && n >= 1 && n <= kMaxCells && (seqCells <= 0 || n <= seqCells);
     if (!run && tid == 0 && (int)h < heads) raise_error(err, kErrIndex);
     const int kh = run ? (int)h / (heads / kvHeads) : 0;
     const long long qbase = batch ? ((long long)token * heads + h) * dim : (long long)h * dim;
@@ -587,7 +596,7 @@ __global__ void __cluster_dims__(kAcCluster, 1, 1) __launch_bounds__(kAcThreads)
     if (run) {
         for (int c = tid; c < n; c += kAcThreads) {  // every cell's value row (and its checks, once: by its scorer)
             const long long cell = batch ? c : (long long)Cells.get(c, err);
-            const long long kb = (cell * kvHeads + kh) * dim;
+            const long long kb = ((cell0 + cell) * kvHeads + kh) * dim;
             const bool key_ok = cell >= 0 && covers(Keys, kb, dim), value_ok = cell >= 0 && covers(Values, kb, dim);
             value_row[c] = value_ok ? kb : -1;
             if (c >= c0 && c < c1) {  // A
@@ -801,21 +810,29 @@ cudaError_t launch_attention_prompt(const KArg *a, int qi, int ki, int vi, int y
     }
     if (attention_cl_ok(a[ki], a[vi], dim, heads, kvHeads, g)) {
         launch_k(g[2] == 1, k_attention_cl, dim3(g[0] * kAcCluster, g[2]), kAcThreads, 0, s, grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim,
-                                                                            heads, kvHeads, 0, position, scale, 1, pos, err);
+                                                                            heads, kvHeads, 0, position, scale, 1, pos, 0, err);
         return cudaGetLastError();
     }
     launch_k(g[2] == 1, k_attention, dim3(g[0], g[2]), kAttnThreads, 0, s, grid_of(g), F(qi), F(ki), F(vi), IB{nullptr, 0}, F(yi), dim, heads, kvHeads, 0,
-                                                          position, scale, 1, pos, err);
+                                                          position, scale, 1, pos, 0, err);
     return cudaGetLastError();
 }
 
 // kernels/strata.cu:328-330 and :453-456
-__global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, int position, int tokens, IB Pos, unsigned *err) {
+// With seqCells > 0 (strata_kv_append_seqs, no reference counterpart) token t's row goes to cell
+// Pos[t] of sequence t's own cache, cells [t seqCells, (t + 1) seqCells) of Keys and Values.
+__global__ void k_kv_append(Grid g, FB K, FB V, FB Keys, FB Values, int width, int position, int tokens, IB Pos, int seqCells,
+                            unsigned *err) {
     dep_enter();
     long long i = lane_index(g, (long long)width * tokens);
     if (i < 0) return;
-    if (Pos.n > 0) position = Pos.get(0, err);
-    const long long at = (long long)position * width + i;
+    const long long token = i / width;
+    if (Pos.n > 0) position = Pos.get(seqCells > 0 ? token : 0, err);
+    if (seqCells > 0 && (position < 0 || position >= seqCells)) {
+        raise_error(err, kErrIndex);
+        return;
+    }
+    const long long at = seqCells > 0 ? (token * seqCells + position) * width + i % width : (long long)position * width + i;
     Keys.set(at, K.get(i, err), err);
     Values.set(at, V.get(i, err), err);
 }
@@ -947,6 +964,25 @@ cudaError_t launch_conv(const KArg *a, const unsigned g[3], int tokens, int batc
     return cudaGetLastError();
 }
 
+// strata_conv_seqs (no counterpart in the reference): one token of each of `tokens` independent
+// sequences, token t with its own history [t channels (taps - 1) dilation, ...), each channel's
+// value by strata_conv's operations in its order. One thread per (token, channel).
+__global__ void k_conv_seqs(Grid g, FB History, FB X, FB W, FB Y, int channels, int taps, int dilation, int activation, int tokens,
+                            unsigned *err) {
+    dep_enter();
+    const long long i = lane_index(g, (long long)channels * tokens);
+    if (i < 0) return;
+    const long long c = i % channels, history = (long long)(taps - 1) * dilation, hbase = i * history;
+    float sum = 0.0f;
+    for (int t = 0; t < taps - 1; ++t)
+        sum = __fadd_rn(sum, __fmul_rn(History.get(hbase + (long long)t * dilation, err), W.get(c * taps + t, err)));
+    const float x = X.get(i, err);
+    sum = __fadd_rn(sum, __fmul_rn(x, W.get(c * taps + taps - 1, err)));
+    Y.set(i, activation == 1 ? ref_silu(sum) : sum, err);
+    for (long long t = 0; t < history - 1; ++t) History.set(hbase + t, History.get(hbase + t + 1, err), err);
+    if (history > 0) History.set(hbase + history - 1, x, err);
+}
+
 // strata_gdn_prep (no counterpart in the reference): the delta-rule layer's input sequence of one
 // token (src/engine.js's strata_conv (4 taps, dilation 1, SiLU) over the [q | k | v] projection,
 // three strata_slice, then the L2 norms of the q heads (times qScale) and of the k heads,
@@ -1050,7 +1086,9 @@ __global__ void k_gdn(Grid g, FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB 
 // block of DIM threads per value head: the head's key and query rows of each token are staged in
 // shared memory and read through a volatile view, so the compiler issues them in order beside
 // the accumulation chains instead of holding all 2 x DIM of them in registers.
-template <int DIM>
+// SEQS (strata_gdn_seqs, no reference counterpart): block (h, t) runs token t alone on sequence
+// t's own state, [t DIM stride, (t + 1) DIM stride) of State.
+template <int DIM, bool SEQS>
 __global__ void __launch_bounds__(DIM) k_gdn_regs(FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int keyHeads, int valueHeads,
                                                   int tokens, long long columns) {
     dep_enter();
@@ -1060,10 +1098,12 @@ __global__ void __launch_bounds__(DIM) k_gdn_regs(FB State, FB Q, FB K, FB V, FB
     const long long h = blockIdx.x, jh = h * DIM + threadIdx.x, kh = h % keyHeads;
     const int x = threadIdx.x;
     const bool active = jh < columns;
+    if (SEQS) State.p += (long long)blockIdx.y * DIM * stride;
+    const int first = SEQS ? (int)blockIdx.y : 0, end = SEQS ? first + 1 : tokens;
     float st[DIM];
 #pragma unroll
     for (int i = 0; i < DIM; ++i) st[i] = active ? State.p[i * stride + jh] : 0.0f;
-    for (int token = 0; token < tokens; ++token) {
+    for (int token = first; token < end; ++token) {
         const long long kbase = ((long long)token * keyHeads + kh) * DIM, gh = (long long)token * valueHeads + h;
         ks[x] = K.p[kbase + x];
         qs[x] = Q.p[kbase + x];
@@ -1099,13 +1139,43 @@ cudaError_t launch_gdn(const Grid g, const KArg *a, int tokens, cudaStream_t s, 
                          a[2].len >= (long long)tokens * kh * dim && a[3].len >= tokens * stride && a[4].len >= (long long)tokens * vh &&
                          a[5].len >= (long long)tokens * vh && a[6].len >= tokens * stride && kh >= 1 && vh >= 1;
     if (dim == 128 && covered) {
-        launch_k(tokens == 1, k_gdn_regs<128>, (unsigned)((columns + 127) / 128), 128, 0, s, F(0), F(1), F(2), F(3), F(4), F(5), F(6), kh, vh, tokens,
+        launch_k(tokens == 1, k_gdn_regs<128, false>, (unsigned)((columns + 127) / 128), 128, 0, s, F(0), F(1), F(2), F(3), F(4), F(5), F(6), kh, vh, tokens,
                                                                           columns);
     } else {
         launch_k(tokens == 1, k_gdn, (unsigned)(((unsigned long long)g.x * STRATA_LANES + 255) / 256), 256, 0, s, g, F(0), F(1), F(2), F(3), F(4), F(5), F(6),
                                                                                              dim, kh, vh, tokens, err);
     }
     return cudaGetLastError();
+}
+
+// strata_gdn_seqs (no counterpart in the reference), the checked form: one token of each of
+// `tokens` independent sequences, token t on its own state [t dim stride, (t + 1) dim stride),
+// each value by strata_gdn_step's operations in its order. One thread per (token, column).
+__global__ void k_gdn_seqs(Grid g, FB State, FB Q, FB K, FB V, FB Decay, FB Beta, FB Y, int dim, int keyHeads, int valueHeads, int tokens,
+                           unsigned *err) {
+    dep_enter();
+    const long long stride = (long long)valueHeads * dim;
+    const long long i = lane_index(g, stride * tokens);
+    if (i < 0) return;
+    const long long token = i / stride, jh = i % stride, h = jh / dim, kh = h % keyHeads;
+    const long long sbase = token * dim * stride, kbase = (token * keyHeads + kh) * dim, gh = token * valueHeads + h;
+    const float decay = Decay.get(gh, err);
+    float prediction = 0.0f;
+    for (int k = 0; k < dim; ++k) {
+        const long long ix = sbase + k * stride + jh;
+        const float s = __fmul_rn(State.get(ix, err), decay);
+        State.set(ix, s, err);
+        prediction = __fadd_rn(prediction, __fmul_rn(s, K.get(kbase + k, err)));
+    }
+    const float delta = __fmul_rn(__fsub_rn(V.get(i, err), prediction), Beta.get(gh, err));
+    float result = 0.0f;
+    for (int k = 0; k < dim; ++k) {
+        const long long ix = sbase + k * stride + jh;
+        const float s = __fadd_rn(State.get(ix, err), __fmul_rn(K.get(kbase + k, err), delta));
+        State.set(ix, s, err);
+        result = __fadd_rn(result, __fmul_rn(s, Q.get(kbase + k, err)));
+    }
+    Y.set(i, result, err);
 }
 
 // ---------------------------------------------------------------- hyper-connection blocks
@@ -1296,7 +1366,7 @@ cudaError_t L_rope_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
     return cudaGetLastError();
 }
 cudaError_t L_kv_append_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    launch_k(a[6].i == 1, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[5].i, 0, a[6].i, I(4), err);
+    launch_k(a[6].i == 1, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[5].i, 0, a[6].i, I(4), 0, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_at(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1350,22 +1420,22 @@ cudaError_t L_argmax(const KArg *a, const unsigned g[3], cudaStream_t s, unsigne
 cudaError_t L_attention(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     if (attention_cl_ok(a[1], a[2], a[5].i, a[6].i, a[7].i, g)) {
         launch_k(true, k_attention_cl, dim3(g[0] * kAcCluster, 1), kAcThreads, 0, s, grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i,
-                                                                         a[8].i, 0, a[9].f, 0, IB{nullptr, 0}, err);
+                                                                         a[8].i, 0, a[9].f, 0, IB{nullptr, 0}, 0, err);
         return cudaGetLastError();
     }
     launch_k(true, k_attention, dim3(g[0], 1), kAttnThreads, 0, s, grid_of(g), F(0), F(1), F(2), I(3), F(4), a[5].i, a[6].i, a[7].i, a[8].i, 0, a[9].f, 0,
-                                                       IB{nullptr, 0}, err);
+                                                       IB{nullptr, 0}, 0, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     return launch_attention_prompt(a, 0, 1, 2, 3, a[4].i, a[5].i, a[6].i, a[7].i, a[8].f, IB{nullptr, 0}, g, s, err);
 }
 cudaError_t L_kv_append(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    launch_k(true, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, kOneToken, IB{nullptr, 0}, err);
+    launch_k(true, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, kOneToken, IB{nullptr, 0}, 0, err);
     return cudaGetLastError();
 }
 cudaError_t L_kv_append_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    launch_k(false, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, IB{nullptr, 0}, err);
+    launch_k(false, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, IB{nullptr, 0}, 0, err);
     return cudaGetLastError();
 }
 cudaError_t L_attention_gate(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
@@ -1429,6 +1499,53 @@ cudaError_t L_gdn_batch(const KArg *a, const unsigned g[3], cudaStream_t s, unsi
     return launch_gdn(grid_of(g), a, a[10].i, s, err);
 }
 
+// ---- sequence-batch entries (no reference counterpart): one decode token for each of `tokens`
+// independent sequences, each with its own position, cache, history or state. Each value is formed
+// by the same operations in the same order as the one-sequence entry it batches.
+cudaError_t L_rope_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    launch_k(true, k_rope, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[5].i, a[6].i, a[7].i, 0, a[8].i, 3, I(4), err);
+    return cudaGetLastError();
+}
+cudaError_t L_kv_append_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    launch_k(true, k_kv_append, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[5].i, 0, a[7].i, I(4), a[6].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_attention_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const int dim = a[5].i, heads = a[6].i, kvHeads = a[7].i, cells = a[8].i;
+    const float scale = a[9].f;
+    if (attention_cl_ok(a[1], a[2], dim, heads, kvHeads, g)) {
+        launch_k(false, k_attention_cl, dim3(g[0] * kAcCluster, g[2]), kAcThreads, 0, s, grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(4), dim,
+                 heads, kvHeads, 0, 0, scale, 1, I(3), cells, err);
+        return cudaGetLastError();
+    }
+    launch_k(false, k_attention, dim3(g[0], g[2]), kAttnThreads, 0, s, grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(4), dim, heads, kvHeads, 0, 0,
+             scale, 1, I(3), cells, err);
+    return cudaGetLastError();
+}
+cudaError_t L_conv_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    launch_k(true, k_conv_seqs, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, err);
+    return cudaGetLastError();
+}
+cudaError_t L_gdn_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const int dim = a[7].i, kh = a[8].i, vh = a[9].i, tokens = a[10].i;
+    const long long stride = (long long)vh * dim;
+    const bool covered = kh >= 1 && vh >= 1 && tokens >= 1 && (long long)g[0] * STRATA_LANES >= stride * tokens &&
+                         a[0].len >= (long long)tokens * dim * stride && a[1].len >= (long long)tokens * kh * dim &&
+                         a[2].len >= (long long)tokens * kh * dim && a[3].len >= tokens * stride && a[4].len >= (long long)tokens * vh &&
+                         a[5].len >= (long long)tokens * vh && a[6].len >= tokens * stride;
+    if (dim == 128 && covered && tokens <= 65535) {
+        launch_k(false, k_gdn_regs<128, true>, dim3((unsigned)((stride + 127) / 128), (unsigned)tokens), 128, 0, s, F(0), F(1), F(2), F(3), F(4),
+                 F(5), F(6), kh, vh, tokens, stride);
+    } else {
+        launch_k(false, k_gdn_seqs, lane_blocks(g), 256, 0, s, grid_of(g), F(0), F(1), F(2), F(3), F(4), F(5), F(6), dim, kh, vh, tokens, err);
+    }
+    return cudaGetLastError();
+}
+cudaError_t L_argmax_rows(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    launch_k(true, k_argmax, (unsigned)a[3].i, kArgmaxThreads, 0, s, F(0), I(1), a[2].i, err);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 // Parameter lists in kernels/strata.cu order and spelling (kinds as in compat.cu's table).
@@ -1479,6 +1596,13 @@ const KernelSpec kEngineKernels[] = {
     {"strata_hc_in", "Residual:f NormW:f DownW:f InjectW:f Norm:f Down:f Inject:f width:I streams:I rank:I epsilon:F", L_hc_in},
     {"strata_hc_out", "Norm:f Down:f UpW:f Mixed:f width:I streams:I rank:I scale:F", L_hc_out},
     {"strata_gdn_prep", "History:f X:f W:f Q:f K:f V:f keyDim:I valueDim:I headDim:I qScale:F epsilon:F", L_gdn_prep},
+    // sequence-batch decode entries (no reference counterpart)
+    {"strata_rope_seqs", "X:f Cos:f Sin:f Y:f Positions:i dim:I heads:I rotary:I tokens:I", L_rope_seqs},
+    {"strata_kv_append_seqs", "K:f V:f Keys:f Values:f Positions:i width:I cells:I tokens:I", L_kv_append_seqs},
+    {"strata_attention_seqs", "Q:f Keys:f Values:f Positions:i Y:f dim:I heads:I kvHeads:I cells:I scale:F", L_attention_seqs},
+    {"strata_conv_seqs", "History:f X:f W:f Y:f channels:I taps:I dilation:I activation:I tokens:I", L_conv_seqs},
+    {"strata_gdn_seqs", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I tokens:I", L_gdn_seqs},
+    {"strata_argmax_rows", "Logits:f Tokens:i count:I rows:I", L_argmax_rows},
 };
 const int kNumEngineKernels = sizeof(kEngineKernels) / sizeof(kEngineKernels[0]);
 

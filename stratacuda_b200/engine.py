@@ -179,8 +179,8 @@ class Ops:
         self.release(ids)
         return out
 
-    def rotate(self, x, heads: int, position: int, tokens: int = 1, device_position=None):
-        """src/ops.js:87-97: the RoPE table is built once on the device, then rows rotate at `position`."""
+    def rope_tables(self):
+        """The RoPE cos / sin tables (src/ops.js:87-92), built on the device on first use."""
         g = self.g
         if self.rope is None:
             half = g["rotary"] // 2
@@ -191,6 +191,12 @@ class Ops:
                        grid(g["context"] * half))
             self.release(hi, lo)
             self.rope = (cos, sin)
+        return self.rope
+
+    def rotate(self, x, heads: int, position: int, tokens: int = 1, device_position=None):
+        """src/ops.js:87-97: the RoPE table is built once on the device, then rows rotate at `position`."""
+        g = self.g
+        self.rope_tables()
         y = self.alloc(x.length)
         if device_position is not None:
             self.b.run("strata_rope_at", dict(X=x, Cos=self.rope[0], Sin=self.rope[1], Y=y, Position=device_position, dim=g["headDim"],
@@ -912,3 +918,246 @@ class PromptBatch:
         e.position += self.n
         e.previous = (e.previous + self.tokens)[-2:]
         e.stats["tokens"] += self.n
+
+
+class SequenceBatch(PromptBatch):
+    """Greedy decode of many independent sequences (sessions) of one engine's model at once: each
+    step runs one token of every sequence through every layer. Projections, norms, the
+    hyper-connection blocks and the mixture of experts run once over all of the step's tokens, as
+    for a prompt chunk (src/prefill.js:5-97); what belongs to one sequence (its position, KV cache,
+    convolution histories, delta-rule state and n-gram history) is held per sequence and handled by
+    the sequence-batch entries (strata_rope_seqs, strata_kv_append_seqs, strata_attention_seqs,
+    strata_conv_seqs, strata_gdn_seqs, strata_argmax_rows). The reference holds one session per
+    engine (src/engine.js:53-72); each sequence here gets the values StrataEngine.step would give
+    it alone, bit for bit in the exact mixture-of-experts mode.
+
+    Slots are filled from single-sequence engines of the same store (``admit``: a prompt is
+    prefilled there, then its state is copied into the slot) and can be copied back (``export``).
+    With ``graph`` the step body is captured once and replayed; each later step writes the
+    tokens, positions and PLE row ids (4 + 4 + 4 pleHeads bytes per sequence) and reads the
+    next tokens back."""
+
+    def __init__(self, engine: StrataEngine, capacity: int, graph: bool = False):
+        require_integer(capacity, "batch capacity", 1, 1024)
+        engine._check_ready()
+        super().__init__(engine, [0] * capacity)
+        g, b = self.g, self.b
+        self.capacity = capacity
+        self.use_graph = bool(graph) and getattr(engine.store, "moe_layer", None) is not None
+        self.persistent = []
+        self.disposed = False
+        hc, c = g["width"] * g["streams"], (2 * g["keyHeads"] + g["valueHeads"]) * g["ssmDim"]
+        try:
+            self.residual = self._keep(capacity * hc)
+            self.ple_history = self._keep(capacity * (g["pleTaps"] - 1) * g["pleDilation"] * hc)
+            self.states = []
+            for layer in range(g["layers"]):
+                if engine.is_attention(layer):
+                    kv = capacity * g["context"] * g["kvHeads"] * g["headDim"]
+                    self.states.append(dict(keys=self._keep(kv), values=self._keep(kv)))
+                else:
+                    self.states.append(dict(state=self._keep(capacity * g["ssmDim"] * g["valueHeads"] * g["ssmDim"]),
+                                            conv=self._keep(capacity * c * 3)))
+            self.dev = dict(tokens=self._keep(capacity, "i32"), positions=self._keep(capacity, "i32"),
+                            ple=self._keep(capacity * g["pleHeads"], "i32"))
+        except Exception:
+            self.dispose()
+            raise
+        self.positions = [None] * capacity  # None: an empty slot
+        self.previous = [[] for _ in range(capacity)]
+        self._graph = None
+        self._graph_head = None
+        self.failed = False
+
+    def _keep(self, n: int, type: str = "f32"):
+        buf = self.b.alloc(n, type, zero=True)
+        self.persistent.append(buf)
+        return buf
+
+    def _regions(self, engine: StrataEngine):
+        """(engine buffer, batch buffer, elements per sequence) for every piece of sequence state."""
+        out = [(engine.ple_history, self.ple_history, engine.ple_history.length)]
+        for mine, theirs in zip(self.states, engine.states):
+            for key, buf in theirs.items():
+                out.append((buf, mine[key], buf.length))
+        return out
+
+    def _check_engine(self, slot: int, engine: StrataEngine) -> None:
+        require_integer(slot, "slot", 0, self.capacity - 1)
+        if self.disposed:
+            raise RuntimeError("Batch is disposed")
+        if engine.store is not self.e.store or engine.b is not self.b:
+            raise ValueError("The engine serves another model or backend")
+
+    def admit(self, slot: int, engine: StrataEngine) -> None:
+        """Copy a single-sequence engine's state (its prompt already prefilled, or none) into `slot`."""
+        self._check_engine(slot, engine)
+        engine._check_ready()
+        for src, dst, n in self._regions(engine):
+            self.b.copy(src, dst, n, 0, slot * n)
+        self.positions[slot] = engine.position
+        self.previous[slot] = list(engine.previous)
+
+    def export(self, slot: int, engine: StrataEngine) -> None:
+        """Copy the sequence in `slot` back into a single-sequence engine, which continues it."""
+        self._check_engine(slot, engine)
+        if self.positions[slot] is None:
+            raise ValueError("Slot is empty")
+        for dst, src, n in self._regions(engine):
+            self.b.copy(src, dst, n, slot * n, 0)
+        engine.position, engine.previous, engine.failed = self.positions[slot], list(self.previous[slot]), False
+
+    # ---- the per-sequence parts of a layer (the rest is PromptBatch's, over all tokens)
+    def ple(self) -> None:
+        g, o, b, n = self.g, self.o, self.b, self.n
+        p, hc = f"blk.{g['pleLayer']}.ple_", g["width"] * g["streams"]
+        emb = o.alloc(n * g["width"])
+        table = getattr(self.e.store, "ple_table", None)
+        if table is not None:
+            b.ple_gather_decode(table, self.dev["ple"], n * g["pleHeads"], g["pleHeadDim"], emb)
+        else:
+            b.run("strata_gather_rows", dict(X=o.weight("per_layer_token_embd.weight"), Indices=self.dev["ple"], Y=emb,
+                                             width=g["pleHeadDim"], rows=n * g["pleHeads"]), grid(n * g["width"]))
+        key = o.norm(self.mat(p + "key.weight", emb), o.vector(p + "norm_key.weight"), g["width"], n * g["streams"], g["streams"])
+        query = o.norm(self.residual, o.vector(p + "norm_query.weight"), g["width"], n * g["streams"], g["streams"])
+        value = self.mat(p + "value.weight", emb)
+        gate, gated = o.alloc(n * g["streams"]), o.alloc(n * hc)
+        b.run("strata_ple_gate", dict(Key=key, Query=query, Gate=gate, width=g["width"], streams=n * g["streams"]),
+              [n * g["streams"], 1, 1])
+        b.run("strata_ple_broadcast_batch", dict(Value=value, Gate=gate, Y=gated, width=g["width"], streams=g["streams"], tokens=n),
+              grid(n * hc))
+        norm = o.norm(gated, o.vector(p + "norm_conv.weight"), g["width"], n * g["streams"], g["streams"])
+        conv = o.alloc(n * hc)
+        b.run("strata_conv_seqs", dict(History=self.ple_history, X=norm, W=o.vector(p + "conv1d.weight"), Y=conv, channels=hc,
+                                       taps=g["pleTaps"], dilation=g["pleDilation"], activation=1, tokens=n), grid(n * hc))
+        b.run("strata_ple_add", dict(Residual=self.residual, Gated=gated, Conv=conv, n=n * hc), grid(n * hc))
+
+    def gdn(self, layer: int, x):
+        g, o, b, n = self.g, self.o, self.b, self.n
+        p, st = f"blk.{layer}.", self.states[layer]
+        qk, vn = g["ssmDim"] * g["keyHeads"], g["ssmDim"] * g["valueHeads"]
+        c = 2 * qk + vn
+        qkv = self.mat(p + "attn_qkv.weight", x)
+        convolved = o.alloc(n * c)
+        b.run("strata_conv_seqs", dict(History=st["conv"], X=qkv, W=o.vector(p + "ssm_conv1d.weight"), Y=convolved, channels=c, taps=4,
+                                       dilation=1, activation=1, tokens=n), grid(n * c))
+        qr, kr, v = o.slice(convolved, qk, n, c), o.slice(convolved, qk, n, c, qk), o.slice(convolved, vn, n, c, 2 * qk)
+        q = o.norm(qr, qr, g["ssmDim"], n * g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
+        k = o.norm(kr, kr, g["ssmDim"], n * g["keyHeads"], 1, 1)
+        alpha, beta = self.mat(p + "ssm_alpha.weight", x), self.mat(p + "ssm_beta.weight", x)
+        decay, strength, y = o.alloc(n * g["valueHeads"]), o.alloc(n * g["valueHeads"]), o.alloc(n * vn)
+        b.run("strata_gdn_gates_batch", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
+                                             Strength=strength, heads=g["valueHeads"], tokens=n), grid(n * g["valueHeads"]))
+        b.run("strata_gdn_seqs", dict(State=st["state"], Q=q, K=k, V=v, Decay=decay, Beta=strength, Y=y, dim=g["ssmDim"],
+                                      keyHeads=g["keyHeads"], valueHeads=g["valueHeads"], tokens=n), grid(n * vn))
+        z = self.mat(p + "attn_gate.weight", x)
+        norm = o.norm(y, o.vector(p + "ssm_norm.weight"), g["ssmDim"], n * g["valueHeads"])
+        return self.mat(p + "ssm_out.weight", o.elem(norm, z, 4))
+
+    def qsa(self, layer: int, x):
+        g, o, b, n = self.g, self.o, self.b, self.n
+        p, st, hd = f"blk.{layer}.", self.states[layer], g["headDim"]
+        cos, sin = o.rope_tables()
+        pos = self.dev["positions"]
+
+        def rotate(rows, heads):
+            y = o.alloc(rows.length)
+            b.run("strata_rope_seqs", dict(X=rows, Cos=cos, Sin=sin, Y=y, Positions=pos, dim=hd, heads=heads, rotary=g["rotary"], tokens=n),
+                  grid(rows.length))
+            return y
+
+        full = self.mat(p + "attn_q.weight", x)
+        qr = o.slice(full, hd, n * g["heads"], hd * 2)
+        q = rotate(o.norm(qr, o.vector(p + "attn_q_norm.weight"), hd, n * g["heads"]), g["heads"])
+        kr = self.mat(p + "attn_k.weight", x)
+        k = rotate(o.norm(kr, o.vector(p + "attn_k_norm.weight"), hd, n * g["kvHeads"]), g["kvHeads"])
+        v = self.mat(p + "attn_v.weight", x)
+        b.run("strata_kv_append_seqs", dict(K=k, V=v, Keys=st["keys"], Values=st["values"], Positions=pos, width=g["kvHeads"] * hd,
+                                            cells=g["context"], tokens=n), grid(n * g["kvHeads"] * hd))
+        attn = o.alloc(n * g["heads"] * hd)
+        gated = o.alloc(attn.length)
+        b.run("strata_attention_seqs", dict(Q=q, Keys=st["keys"], Values=st["values"], Positions=pos, Y=attn, dim=hd, heads=g["heads"],
+                                            kvHeads=g["kvHeads"], cells=g["context"], scale=_f32(1 / math.sqrt(hd))),
+              [g["heads"], (hd + 63) // 64, n])
+        b.run("strata_attention_gate_batch", dict(Attention=attn, FullQ=full, Y=gated, dim=hd, heads=g["heads"], tokens=n),
+              grid(attn.length))
+        return self.mat(p + "attn_output.weight", gated)
+
+    # ---- the step
+    def _body(self):
+        """Embedding, every layer and the head of one step; returns the (logits, tokens) buffers."""
+        g, o, b, n, e = self.g, self.o, self.b, self.n, self.e
+        b.run("strata_embed_token", dict(Table=o.weight("token_embd.weight"), Token=self.dev["tokens"], Residual=self.residual,
+                                         width=g["width"], streams=g["streams"], vocab=g["vocab"], tokens=n), grid(n * g["width"]))
+        for layer in range(g["layers"]):
+            e._layer(layer, self)
+        head, _ = self.hc("output_hc_", False)
+        values = self.mat("output.weight", head)
+        nxt = o.alloc(n, "i32")
+        b.run("strata_argmax_rows", dict(Logits=values, Tokens=nxt, count=g["vocab"], rows=n), [n, 1, 1])
+        o.clear_temporary()
+        return values, nxt
+
+    def step(self, tokens, logits: bool = False) -> dict:
+        """One greedy decode step of every sequence: `tokens[s]` is sequence s's next input token.
+        Returns {positions, tokens[, logits]} (logits as [capacity, vocab])."""
+        if self.disposed:
+            raise RuntimeError("Batch is disposed")
+        if self.failed:
+            raise RuntimeError("Batch failed; dispose it and admit the sequences again")
+        g, b = self.g, self.b
+        tokens = [int(t) for t in tokens]
+        if len(tokens) != self.capacity:
+            raise ValueError(f"expected {self.capacity} tokens, got {len(tokens)}")
+        for s, t in enumerate(tokens):
+            require_integer(t, "token", 0, g["vocab"] - 1)
+            if self.positions[s] is None:
+                raise ValueError(f"slot {s} is empty")
+            if self.positions[s] >= g["context"]:
+                raise ValueError("Context capacity reached; reset or create a larger session")
+        ple = [self.e.store.ple_indices(t, self.previous[s]) for s, t in enumerate(tokens)]
+        e = self.e
+        try:
+            b.write(self.dev["tokens"], np.array(tokens, np.int32))
+            b.write(self.dev["positions"], np.array(self.positions, np.int32))
+            b.write(self.dev["ple"], np.concatenate(ple).astype(np.int32))
+            if self.use_graph and self._graph is not None:
+                b.graph_launch(self._graph)
+                values, nxt = self._graph_head
+            else:
+                values, nxt = self._body()
+                if self.use_graph:
+                    b.capture_begin()
+                    try:
+                        self._graph_head = self._body()
+                    finally:
+                        self._graph = b.capture_end()
+                    # the captured body ran nothing: the eager body's results stand
+            out = np.array(b.read(nxt, "i32"), np.int64)
+            result = dict(positions=list(self.positions), tokens=[int(t) for t in out])
+            for t in result["tokens"]:
+                require_integer(t, "generated token", 0, g["vocab"] - 1)
+            if logits:
+                result["logits"] = np.array(b.read(values), np.float32).reshape(self.capacity, g["vocab"])
+                if not np.all(np.isfinite(result["logits"])):
+                    raise RuntimeError("Non-finite logits")
+        except BaseException:
+            self.failed = True
+            raise
+        for s, t in enumerate(tokens):
+            self.previous[s] = (self.previous[s] + [t])[-2:]
+            self.positions[s] += 1
+        e.stats["tokens"] += self.capacity
+        return result
+
+    def dispose(self) -> None:
+        if self.disposed:
+            return
+        if self._graph is not None:
+            self.b.graph_free(self._graph)
+            self._graph = None
+        self.b.idle()
+        for buf in self.persistent:
+            self.b.free(buf)
+        self.persistent = []
+        self.disposed = True
