@@ -678,7 +678,8 @@ def prefill_roofline(b, layers, xs, ys, idss, wss, B, NL, n_x, mode, K):
             "phase_ms_per_step": {k: v / max(1, calls) for k, v in ph.items()}}
 
 
-def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_prefill=False, profile_step=False, batch=64):
+def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_prefill=False, profile_step=False, batch=64,
+              profile_batch_step=False):
     """The full-model workload on backend b: the seeded synthetic model (stratacuda_b200.synthetic)
     resident in HBM, a prompt prefilled in chunks of 64, then greedy decode at batch 1, all through
     StrataEngine (the reference host's call order). Timed by the host clock around each phase,
@@ -726,8 +727,16 @@ def model_run(b, layers, prompt_len, decode, warmup, mode, graph=True, profile_p
         step_tokens = np.random.default_rng(8).integers(0, g["vocab"], batch).tolist()
         b.idle()
         t0 = time.perf_counter()
-        for _ in range(decode):
+        for k in range(decode):
+            last = profile_batch_step and k == decode - 1
+            if last:  # only this batch step is inside an `ncu --profile-from-start off` capture
+                import torch
+                b.idle()
+                torch.cuda.cudart().cudaProfilerStart()
             step_tokens = seqs.step(step_tokens)["tokens"]
+            if last:
+                b.idle()
+                torch.cuda.cudart().cudaProfilerStop()
         t_batch = time.perf_counter() - t0
         batch_out = {f"decode_b{batch}_tokens_per_s": batch * decode / t_batch, f"decode_b{batch}_ms_per_step": 1e3 * t_batch / decode,
                      f"decode_b{batch}_last_tokens": step_tokens[:8]}
@@ -772,7 +781,8 @@ def run_model_arm(args):
 
     b = CudaBackend(0)
     r = model_run(b, args.model_layers, args.prompt, args.decode, args.warmup, args.mode, graph=not args.no_graph,
-                  profile_prefill=args.profile_prefill, profile_step=args.profile_step, batch=args.model_batch)
+                  profile_prefill=args.profile_prefill, profile_step=args.profile_step, batch=args.model_batch,
+                  profile_batch_step=args.profile_batch_step)
     line = {"metric": "full-model tokens/s (prefill; greedy decode b=1)", "workload": "model48", "value": r["decode_tokens_per_s"],
             "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "dtype": "f32+q2", "data": "synthetic", **r}
     b.dispose()
@@ -805,6 +815,8 @@ def main():
                     help="--model: bracket the last 64-token prompt chunk with cudaProfilerStart/Stop")
     ap.add_argument("--profile-step", action="store_true",
                     help="--model: bracket the last decode step with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--profile-batch-step", action="store_true",
+                    help="--model: bracket the last batch decode step with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -688,17 +688,19 @@ __global__ void __cluster_dims__(kAcCluster, 1, 1) __launch_bounds__(kAcThreads)
 // in-order sums), one warp per head takes the maximum and the exponential sum in the reference's
 // lane order, and each value is loaded once for four heads' in-order sums. Every value is formed
 // by the same operations in the same order as in k_attention. Cells are 0 .. position + token; a
-// key or value row outside its buffer reads as zeros and is reported.
+// key or value row outside its buffer reads as zeros and is reported. With seqCells > 0
+// (strata_attention_seqs) query token t is sequence t's, over cells 0 .. Pos[t] of its own cache.
 constexpr int kGroupThreads = 512, kMaxGroup = 8;
 __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q, FB Keys, FB Values, FB Y, int dim, int heads, int kvHeads,
-                                                                   int position, float scale, IB Pos, unsigned *err) {
+                                                                   int position, float scale, IB Pos, int seqCells, unsigned *err) {
     dep_enter();
     extern __shared__ __align__(16) float group_smem[];  // [G][dim] queries, then [G][kMaxCells] scores
     __shared__ float totals[kMaxGroup];
     const int G = heads / kvHeads, kh = blockIdx.x, token = blockIdx.y, tid = threadIdx.x;
-    if (Pos.n > 0) position = Pos.get(0, err);
-    const long long n = (long long)position + token + 1;
-    if (n < 1 || n > kMaxCells) {
+    if (Pos.n > 0) position = Pos.get(seqCells > 0 ? token : 0, err);
+    const long long n = seqCells > 0 ? (long long)position + 1 : (long long)position + token + 1;
+    const long long cell0 = seqCells > 0 ? (long long)token * seqCells : 0;
+    if (n < 1 || n > kMaxCells || (seqCells > 0 && n > seqCells)) {
         if (tid == 0) raise_error(err, kErrIndex);
         return;
     }
@@ -707,7 +709,7 @@ __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q,
     for (int k = tid; k < G * dim; k += kGroupThreads) qs[k] = Q.get(qbase + k, err);
     __syncthreads();
     for (int c = tid; c < n; c += kGroupThreads) {  // A
-        const long long kb = ((long long)c * kvHeads + kh) * dim;
+        const long long kb = ((cell0 + c) * kvHeads + kh) * dim;
         float sc[kMaxGroup];
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) sc[h] = 0.0f;
@@ -767,7 +769,7 @@ __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q,
             float v[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
-                const long long vb = ((long long)(c + u) * kvHeads + kh) * dim;
+                const long long vb = ((cell0 + c + u) * kvHeads + kh) * dim;
                 v[u] = covers(Values, vb, dim) ? Values.p[vb + d] : 0.0f;
             }
 #pragma unroll
@@ -777,7 +779,7 @@ __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q,
                     if (h0 + q < G) value[q] = __fadd_rn(value[q], __fmul_rn(scores[(size_t)(h0 + q) * kMaxCells + c + u], v[u]));
         }
         for (; c < n; ++c) {
-            const long long vb = ((long long)c * kvHeads + kh) * dim;
+            const long long vb = ((cell0 + c) * kvHeads + kh) * dim;
             const float v = covers(Values, vb, dim) ? Values.p[vb + d] : 0.0f;
 #pragma unroll
             for (int q = 0; q < kHeadsPerThread; ++q)
@@ -805,7 +807,7 @@ cudaError_t launch_attention_prompt(const KArg *a, int qi, int ki, int vi, int y
         cudaError_t e = cudaFuncSetAttribute(k_attention_group, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
         if (e != cudaSuccess) return e;
         launch_k(false, k_attention_group, dim3(kvHeads, g[2]), kGroupThreads, bytes, s, grid_of(g), F(qi), F(ki), F(vi), F(yi), dim, heads, kvHeads,
-                                                                           position, scale, pos, err);
+                                                                           position, scale, pos, 0, err);
         return cudaGetLastError();
     }
     if (attention_cl_ok(a[ki], a[vi], dim, heads, kvHeads, g)) {
@@ -1513,6 +1515,19 @@ cudaError_t L_kv_append_seqs(const KArg *a, const unsigned g[3], cudaStream_t s,
 cudaError_t L_attention_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     const int dim = a[5].i, heads = a[6].i, kvHeads = a[7].i, cells = a[8].i;
     const float scale = a[9].f;
+    // the grouped-query form (each key and value row loaded once for the group's heads) when there
+    // are enough sequences to fill the SMs with (KV head, sequence) blocks
+    const int G = kvHeads > 0 ? heads / kvHeads : 0;
+    const size_t bytes = ((size_t)G * dim + (size_t)G * kMaxCells) * 4;
+    const bool aligned = (reinterpret_cast<uintptr_t>(a[1].ptr) & 15) == 0;
+    if ((long long)g[2] * kvHeads >= 64 && G >= 1 && G <= kMaxGroup && heads % kvHeads == 0 && dim % 4 == 0 && aligned &&
+        bytes <= 200 * 1024 && g[0] >= (unsigned)heads) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention_group, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) return e;
+        launch_k(false, k_attention_group, dim3(kvHeads, g[2]), kGroupThreads, bytes, s, grid_of(g), F(0), F(1), F(2), F(4), dim, heads, kvHeads, 0,
+                 scale, I(3), cells, err);
+        return cudaGetLastError();
+    }
     if (attention_cl_ok(a[1], a[2], dim, heads, kvHeads, g)) {
         launch_k(false, k_attention_cl, dim3(g[0] * kAcCluster, g[2]), kAcThreads, 0, s, grid_of(g), F(0), F(1), F(2), IB{nullptr, 0}, F(4), dim,
                  heads, kvHeads, 0, 0, scale, 1, I(3), cells, err);

@@ -56,14 +56,16 @@ def test_rope_seqs(b, port, dim, heads, rotary):
         assert np.array_equal(bits(got[s]), bits(want))
 
 
-@pytest.mark.parametrize("dim,heads,kv,cells", [(256, 16, 2, 2048), (64, 4, 4, 100), (8, 4, 2, 32)])
-def test_kv_append_and_attention_seqs(b, port, dim, heads, kv, cells):
+@pytest.mark.parametrize("dim,heads,kv,cells,seqs", [(256, 16, 2, 2048, 4), (64, 4, 4, 100, 4), (8, 4, 2, 32, 4), (256, 16, 2, 2048, 40),
+                                                     (8, 4, 2, 32, 33)])
+def test_kv_append_and_attention_seqs(b, port, dim, heads, kv, cells, seqs):
     """Every sequence appends its key and value row at its own position of its own cache, then
-    attends over cells 0 .. position of that cache (the 8-CTA cluster form at head sizes 64-256,
-    the one-CTA form below)."""
-    rng = np.random.default_rng(dim * 7 + cells)
-    seqs, width = 4, kv * dim
-    positions = np.array([cells - 1, 0, cells // 2, 3], np.int32)
+    attends over cells 0 .. position of that cache (few sequences: the 8-CTA cluster form at head
+    sizes 64-256, the one-CTA form below; 64 or more (KV head, sequence) pairs: the grouped-query
+    form)."""
+    rng = np.random.default_rng(dim * 7 + cells + seqs)
+    width = kv * dim
+    positions = np.concatenate([[cells - 1, 0, cells // 2, 3], rng.integers(0, cells, seqs - 4)]).astype(np.int32)
     keys = rng.normal(0, 1, seqs * cells * width).astype(np.float32)
     vals = rng.normal(0, 1, seqs * cells * width).astype(np.float32)
     k = rng.normal(0, 1, seqs * width).astype(np.float32)
