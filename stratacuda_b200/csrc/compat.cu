@@ -291,26 +291,30 @@ __global__ void __launch_bounds__(kStagedThreads) k_project_staged(FB X, FB W, F
     }
 }
 
-// The same projection for prompt chunks, register-tiled: each warp computes 4 rows x 8 tokens.
-// Lane l keeps, for every (row, token), the reference's two strided sums (elements l + 64k and
-// l + 32 + 64k, k ascending), so each weight value read feeds 8 sums and each input value 4. The
-// sums of two neighbouring tokens share one 64-bit register and advance with the paired F32
-// product (an FMA whose addend is a run-time -0: the rounded product) and the paired rounded add,
-// each element rounded exactly as the scalar __fmul_rn / __fadd_rn would. Each output then takes
-// the reference's tree over the 64 lanes. A block (8 warps: 2 row groups x 4 token groups) stages
-// 256-column chunks of its 8 weight rows and 32 input rows in shared memory with 16-byte
-// asynchronous copies, two chunks in flight. Used when cols is a multiple of 256, the rows are
-// 16-byte aligned, and the host has checked that W and X cover every row and token named.
-constexpr int kTileRows = 4, kTileTokens = 8, kTileWarps = 8, kTileK = 256;
-constexpr int kBlockRows = 2 * kTileRows, kBlockTokens = 4 * kTileTokens;
+// The same projection for prompt chunks and decode batches (8 or more tokens), register-tiled
+// with four reference lanes per thread. A half-warp computes 4 rows x 4 tokens; its thread u
+// holds lanes 4u .. 4u + 3 of each of those 16 sums (elements 4u + 64k .. 4u + 64k + 3, k
+// ascending) as two register pairs that advance with the paired rounded product (an FMA whose
+// addend is a run-time -0) and the paired rounded add, each element rounded exactly as the scalar
+// __fmul_rn / __fadd_rn would: the 16 bytes a thread needs of a staged weight or input row per
+// step come in one shared load, already paired. Each output then takes the
+// reference's tree over its 64 lanes: the levels 32, 16, 8 and 4 are exchanges between
+// half-warp threads 8, 4, 2 and 1 apart, in which each thread keeps (and adds) half of the
+// outputs it holds, so that thread u ends with output u; levels 2 and 1 are in the thread. A
+// block (16 half-warps: 2 row groups x 8 token groups) stages 256-column chunks of its 8 weight
+// rows and 32 input rows in shared memory with 16-byte asynchronous copies, two chunks in flight.
+// Used when cols is a multiple of 256, the rows are 16-byte aligned, and the host has checked
+// that W and X cover every row and token named.
+constexpr int kTileRows = 4, kTileTokens = 8, kTileWarps = 8, kTileK = 256;  // minimum rows and tokens; warps; chunk columns
+constexpr int kBlockRows = 2 * kTileRows, kBlockTokens = 8 * 4;
 constexpr size_t kTileSmem = 2 * (size_t)(kBlockRows + kBlockTokens) * kTileK * 4;  // 80 KB
-__global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, FB Y, int cols, int rows, int tokens, int outputStride,
-                                                                   int outputOffset, unsigned long long neg0, unsigned *err) {
+__global__ void __launch_bounds__(kTileWarps * 32) k_project_quad(FB X, FB W, FB Y, int cols, int rows, int tokens, int outputStride,
+                                                                  int outputOffset, unsigned long long neg0, unsigned *err) {
     dep_enter();
     extern __shared__ __align__(16) float tile_smem[];  // [2 stages][8 weight rows + 32 input rows][256]
-    const int warp = threadIdx.x / 32, t = threadIdx.x & 31;
+    const int hw = threadIdx.x / 16, u = threadIdx.x & 15;
     const int rb = blockIdx.x * kBlockRows, tb = blockIdx.y * kBlockTokens;
-    const int wr = (warp / 4) * kTileRows, wt = (warp % 4) * kTileTokens;  // this warp's rows / tokens within the block
+    const int rg = (hw / 8) * 4, tg = (hw % 8) * 4;  // this half-warp's rows / tokens within the block
     const int chunks = cols / kTileK;
     auto stage = [&](int c, int st) {  // chunk c of every block row into stage st (rows past the end repeat the last)
         float *base = tile_smem + (size_t)st * (kBlockRows + kBlockTokens) * kTileK;
@@ -322,11 +326,11 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, F
         }
         copy_commit();
     };
-    unsigned long long acc[kTileRows][kTileTokens / 2][2];
+    unsigned long long acc[4][4][2];  // [row][token][lanes (4u, 4u + 1) | (4u + 2, 4u + 3)]
 #pragma unroll
-    for (int r = 0; r < kTileRows; ++r)
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int j = 0; j < kTileTokens / 2; ++j) acc[r][j][0] = acc[r][j][1] = 0ull;
+        for (int j = 0; j < 4; ++j) acc[r][j][0] = acc[r][j][1] = 0ull;
     stage(0, 0);
     for (int c = 0; c < chunks; ++c) {
         if (c + 1 < chunks) {
@@ -336,39 +340,50 @@ __global__ void __launch_bounds__(kTileWarps * 32) k_project_tiled(FB X, FB W, F
             copy_wait<0>();
         }
         __syncthreads();
-        const float *ws = tile_smem + (size_t)(c & 1) * (kBlockRows + kBlockTokens) * kTileK + (size_t)wr * kTileK;
-        const float *xs = tile_smem + (size_t)(c & 1) * (kBlockRows + kBlockTokens) * kTileK + (size_t)(kBlockRows + wt) * kTileK;
+        const float *sbase = tile_smem + (size_t)(c & 1) * (kBlockRows + kBlockTokens) * kTileK;
+        const unsigned ws = (unsigned)__cvta_generic_to_shared(sbase + (size_t)rg * kTileK + 4 * u);
+        const unsigned xs = (unsigned)__cvta_generic_to_shared(sbase + (size_t)(kBlockRows + tg) * kTileK + 4 * u);
 #pragma unroll
-        for (int kk = 0; kk < kTileK / STRATA_LANES; ++kk)
+        for (int k = 0; k < kTileK / STRATA_LANES; ++k) {
+            unsigned long long w[4][2], x[4][2];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int e = t + STRATA_LANES * kk + 32 * h;
-                unsigned long long xv[kTileTokens / 2];
+            for (int r = 0; r < 4; ++r)
+                asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(w[r][0]), "=l"(w[r][1]) : "r"(ws + (unsigned)(r * kTileK + 64 * k) * 4));
 #pragma unroll
-                for (int j = 0; j < kTileTokens / 2; ++j) xv[j] = pack2(xs[(2 * j) * kTileK + e], xs[(2 * j + 1) * kTileK + e]);
+            for (int j = 0; j < 4; ++j)
+                asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(x[j][0]), "=l"(x[j][1]) : "r"(xs + (unsigned)(j * kTileK + 64 * k) * 4));
 #pragma unroll
-                for (int r = 0; r < kTileRows; ++r) {
-                    const float wr = ws[r * kTileK + e];
-                    const unsigned long long ww = pack2(wr, wr);
+            for (int r = 0; r < 4; ++r)
 #pragma unroll
-                    for (int j = 0; j < kTileTokens / 2; ++j) acc[r][j][h] = add2_rn(acc[r][j][h], mul_rn2(ww, xv[j], neg0));
-                }
-            }
+                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) acc[r][j][h] = add2_rn(acc[r][j][h], mul_rn2(w[r][h], x[j][h], neg0));
+        }
         __syncthreads();
     }
+    // the tree: v[o][i] = lane 4u + i of output o = 4 r + j
+    float v[16][4];
 #pragma unroll
-    for (int r = 0; r < kTileRows; ++r)
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int j = 0; j < kTileTokens / 2; ++j)
+        for (int j = 0; j < 4; ++j) {
+            unpack2(acc[r][j][0], v[4 * r + j][0], v[4 * r + j][1]);
+            unpack2(acc[r][j][1], v[4 * r + j][2], v[4 * r + j][3]);
+        }
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                float l0, l1, h0, h1;
-                unpack2(acc[r][j][0], l0, l1);
-                unpack2(acc[r][j][1], h0, h1);
-                const float sum = tree64(q ? l1 : l0, q ? h1 : h0);
-                const int row = rb + wr + r, token = tb + wt + 2 * j + q;
-                if (t == 0 && row < rows && token < tokens) Y.set((long long)token * outputStride + outputOffset + row, sum, err);
+    for (int m = 8, n = 16; m >= 1; m >>= 1, n >>= 1) {  // levels 32, 16, 8, 4: partner u ^ m; keep half of n outputs
+        const bool upper = (u & m) != 0;
+#pragma unroll
+        for (int o = 0; o < n / 2; ++o)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float give = upper ? v[o][i] : v[o + n / 2][i], keep = upper ? v[o + n / 2][i] : v[o][i];
+                v[o][i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, give, m));
             }
+    }
+    const float sum = __fadd_rn(__fadd_rn(v[0][0], v[0][2]), __fadd_rn(v[0][1], v[0][3]));  // levels 2 and 1
+    const int row = rb + rg + u / 4, token = tb + tg + u % 4;
+    if (row < rows && token < tokens) Y.set((long long)token * outputStride + outputOffset + row, sum, err);
 }
 
 // kernels/strata.cu:168-176
@@ -629,10 +644,10 @@ cudaError_t L_project(const KArg *a, const unsigned g[3], cudaStream_t s, unsign
     const bool aligned = ((reinterpret_cast<uintptr_t>(a[0].ptr) | reinterpret_cast<uintptr_t>(a[1].ptr)) & 15) == 0;
     if (tokens >= kTileTokens && rows >= kTileRows && cols % kTileK == 0 && aligned && a[1].len >= rows * cols &&
         a[0].len >= tokens * cols && g[2] >= 1) {
-        cudaError_t e = cudaFuncSetAttribute(k_project_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTileSmem);
+        cudaError_t e = cudaFuncSetAttribute(k_project_quad, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTileSmem);
         if (e != cudaSuccess) return e;
         const dim3 blocks((unsigned)((rows + kBlockRows - 1) / kBlockRows), (unsigned)((tokens + kBlockTokens - 1) / kBlockTokens));
-        launch_k(false, k_project_tiled, blocks, kTileWarps * 32, kTileSmem, s, F(0), F(1), F(2), a[3].i, (int)rows, (int)tokens, a[6].i, a[7].i,
+        launch_k(false, k_project_quad, blocks, kTileWarps * 32, kTileSmem, s, F(0), F(1), F(2), a[3].i, (int)rows, (int)tokens, a[6].i, a[7].i,
                                                                    kNegZero2, err);
         return cudaGetLastError();
     }

@@ -78,6 +78,23 @@ def test_all_fp16_patterns(b, golden):
     assert np.array_equal(b.read(vals).view(np.uint32), golden["conformance"]["half_ref_bits"])
 
 
+@pytest.mark.parametrize("cols,rows,tokens", [(2048, 37, 9), (256, 8192, 64), (4096, 100, 64), (512, 13, 33), (8192, 4, 8),
+                                              (2048, 151, 70)])
+def test_prompt_projection_tiles_bit_exact(b, port, cols, rows, tokens):
+    """strata_project over 8 or more tokens with 256-column chunks (the register-tiled prompt
+    form: 4 rows x 4 tokens per half-warp, ragged row and token tails) against the oracle."""
+    rng = np.random.default_rng(cols + rows + tokens)
+    X = rng.normal(0, 1, (tokens, cols)).astype(np.float32)
+    W = rng.normal(0, 0.03, (rows, cols)).astype(np.float32)
+    want = np.zeros(tokens * (rows + 3), np.float32)
+    port.run("strata_project", (rows, tokens, 1), X=X, W=W, Y=want, cols=cols, rows=rows, tokens=tokens, outputStride=rows + 3,
+             outputOffset=1)
+    y = b.alloc(tokens * (rows + 3))
+    b.run("strata_project", dict(X=b.alloc(X), W=b.alloc(W), Y=y, cols=cols, rows=rows, tokens=tokens, outputStride=rows + 3,
+                                 outputOffset=1), [rows, tokens, 1])
+    assert np.array_equal(bits(b.read(y)), bits(want))
+
+
 def test_random_kernels_bit_exact_vs_oracle(b, port):
     rng = np.random.default_rng(11)
     # strata_project with ragged sizes (cols not a multiple of 64, rows tail)
