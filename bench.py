@@ -789,6 +789,36 @@ def run_model_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def run_project_shape(args):
+    """One exact-order projection (strata_project) of the given shape, timed alone: W warm-up
+    launches, then K launches between CUDA events on the library's stream; prints its own line."""
+    import torch
+    from stratacuda_b200.backend import CudaBackend
+
+    cols, rows, tokens = (int(v) for v in args.project_shape.split(","))
+    b = CudaBackend(0)
+    rng = np.random.default_rng(1)
+    x = b.alloc(rng.normal(0, 1, tokens * cols).astype(np.float32))
+    w = b.alloc(rng.normal(0, 0.03, rows * cols).astype(np.float32))
+    y = b.alloc(rows * tokens)
+    call = dict(X=x, W=w, Y=y, cols=cols, rows=rows, tokens=tokens, outputStride=rows, outputOffset=0)
+    for _ in range(args.warmup):
+        b.run("strata_project", call, [rows, tokens, 1])
+    b.idle()
+    stream = torch.cuda.ExternalStream(b.stream_handle, device=torch.device("cuda", 0))
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        b.run("strata_project", call, [rows, tokens, 1])
+    t1.record(stream)
+    t1.synchronize()
+    us = t0.elapsed_time(t1) * 1e3 / args.steps
+    print(json.dumps({"metric": "strata_project multiply-adds/s", "shape": {"cols": cols, "rows": rows, "tokens": tokens},
+                      "us_per_launch": us, "tmac_per_s": cols * rows * tokens / us / 1e6, "steps": args.steps,
+                      "warmup": args.warmup}), flush=True)
+    b.dispose()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -817,6 +847,8 @@ def main():
                     help="--model: bracket the last decode step with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--profile-batch-step", action="store_true",
                     help="--model: bracket the last batch decode step with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--project-shape", default=None, metavar="COLS,ROWS,TOKENS",
+                    help="time one strata_project shape alone (seeded inputs, CUDA events) and print its own JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -827,6 +859,9 @@ def main():
         return
     if args.model:
         run_model_arm(args)
+        return
+    if args.project_shape:
+        run_project_shape(args)
         return
     world, rank, local = dist_setup(args.gpus)
     try:
