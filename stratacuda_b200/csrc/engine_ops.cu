@@ -715,9 +715,7 @@ __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q,
         for (int h = 0; h < kMaxGroup; ++h) sc[h] = 0.0f;
         if (covers(Keys, kb, dim)) {
             const float4 *k4 = reinterpret_cast<const float4 *>(Keys.p + kb);
-#pragma unroll 4
-            for (int j4 = 0; j4 < dim / 4; ++j4) {
-                const float4 kv = k4[j4];
+            auto step = [&](const float4 kv, int j4) {
 #pragma unroll
                 for (int h = 0; h < kMaxGroup; ++h) {
                     if (h >= G) break;
@@ -727,7 +725,16 @@ __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q,
                     sc[h] = __fadd_rn(sc[h], __fmul_rn(q[2], kv.z));
                     sc[h] = __fadd_rn(sc[h], __fmul_rn(q[3], kv.w));
                 }
+            };
+            int j4 = 0;
+            for (; j4 + 8 <= dim / 4; j4 += 8) {  // eight 16-byte key loads in flight ahead of the ordered sums
+                float4 kv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) kv[u] = k4[j4 + u];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) step(kv[u], j4 + u);
             }
+            for (; j4 < dim / 4; ++j4) step(k4[j4], j4);
         } else {
             raise_error(err, kErrIndex);
         }
@@ -765,15 +772,15 @@ __global__ void __launch_bounds__(kGroupThreads) k_attention_group(Grid g, FB Q,
         const int d = w % dmax, h0 = (w / dmax) * kHeadsPerThread;
         float value[kHeadsPerThread] = {0.0f, 0.0f, 0.0f, 0.0f};
         int c = 0;
-        for (; c + 8 <= n; c += 8) {  // eight value loads in flight ahead of the ordered sums
-            float v[8];
+        for (; c + 32 <= n; c += 32) {  // 32 value loads in flight ahead of the ordered sums
+            float v[32];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 32; ++u) {
                 const long long vb = ((cell0 + c + u) * kvHeads + kh) * dim;
                 v[u] = covers(Values, vb, dim) ? Values.p[vb + d] : 0.0f;
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < 32; ++u)
 #pragma unroll
                 for (int q = 0; q < kHeadsPerThread; ++q)
                     if (h0 + q < G) value[q] = __fadd_rn(value[q], __fmul_rn(scores[(size_t)(h0 + q) * kMaxCells + c + u], v[u]));
