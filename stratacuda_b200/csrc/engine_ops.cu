@@ -992,6 +992,32 @@ __global__ void k_conv_seqs(Grid g, FB History, FB X, FB W, FB Y, int channels, 
     if (history > 0) History.set(hbase + history - 1, x, err);
 }
 
+// The same with the tap count and dilation known at compile time (the model's 4 taps at dilations
+// 1 and 3): the thread's history and weights in registers, loaded and stored once. Launched only
+// when the host's layout checks cover every index.
+template <int TAPS, int DIL>
+__global__ void k_conv_seqs_reg(Grid g, FB History, FB X, FB W, FB Y, int channels, int activation, int tokens) {
+    dep_enter();
+    constexpr int H = (TAPS - 1) * DIL;
+    const long long i = lane_index(g, (long long)channels * tokens);
+    if (i < 0) return;
+    const long long c = i % channels;
+    float hist[H], w[TAPS];
+#pragma unroll
+    for (int k = 0; k < H; ++k) hist[k] = History.p[i * H + k];
+#pragma unroll
+    for (int k = 0; k < TAPS; ++k) w[k] = W.p[c * TAPS + k];
+    const float x = X.p[i];
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < TAPS - 1; ++k) sum = __fadd_rn(sum, __fmul_rn(hist[k * DIL], w[k]));
+    sum = __fadd_rn(sum, __fmul_rn(x, w[TAPS - 1]));
+    Y.p[i] = activation == 1 ? ref_silu(sum) : sum;
+#pragma unroll
+    for (int k = 0; k + 1 < H; ++k) History.p[i * H + k] = hist[k + 1];
+    History.p[i * H + H - 1] = x;
+}
+
 // strata_gdn_prep (no counterpart in the reference): the delta-rule layer's input sequence of one
 // token (src/engine.js's strata_conv (4 taps, dilation 1, SiLU) over the [q | k | v] projection,
 // three strata_slice, then the L2 norms of the q heads (times qScale) and of the k heads,
@@ -1545,7 +1571,17 @@ cudaError_t L_attention_seqs(const KArg *a, const unsigned g[3], cudaStream_t s,
     return cudaGetLastError();
 }
 cudaError_t L_conv_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
-    launch_k(true, k_conv_seqs, LANESL, grid_of(g), F(0), F(1), F(2), F(3), a[4].i, a[5].i, a[6].i, a[7].i, a[8].i, err);
+    const int channels = a[4].i, taps = a[5].i, dil = a[6].i, act = a[7].i, tokens = a[8].i;
+    const long long n = (long long)channels * tokens;
+    const bool covered = channels >= 1 && tokens >= 1 && (long long)g[0] * STRATA_LANES >= n && a[0].len >= n * (taps - 1) * dil &&
+                         a[2].len >= (long long)channels * taps && a[1].len >= n && a[3].len >= n;
+    if (covered && taps == 4 && dil == 1) {
+        launch_k(true, k_conv_seqs_reg<4, 1>, LANESL, grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
+    } else if (covered && taps == 4 && dil == 3) {
+        launch_k(true, k_conv_seqs_reg<4, 3>, LANESL, grid_of(g), F(0), F(1), F(2), F(3), channels, act, tokens);
+    } else {
+        launch_k(true, k_conv_seqs, LANESL, grid_of(g), F(0), F(1), F(2), F(3), channels, taps, dil, act, tokens, err);
+    }
     return cudaGetLastError();
 }
 cudaError_t L_gdn_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
