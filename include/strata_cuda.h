@@ -123,7 +123,11 @@ int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *t
  *   strata_conv_seqs      (History, X, W, Y, channels, taps, dilation, activation, tokens)  [strata_conv]
  *   strata_gdn_seqs       (State, Q, K, V, Decay, Beta, Y, dim, keyHeads, valueHeads, tokens) [strata_gdn_step]
  *   strata_argmax_rows    (Logits, Tokens, count, rows)                             [strata_argmax per row]
- * A position outside [0, cells) is reported as an index error, never written. */
+ * A position outside [0, cells) is reported as an index error, never written.
+ *
+ * One more runs the delta-rule layer's gate inputs (src/engine.js's alpha and beta projections,
+ * then strata_gdn_gates; src/prefill.js's batch forms) in one launch, with the same values:
+ *   strata_gdn_gates_fused (X, AlphaW, BetaW, A, Dt, Decay, Strength, width, heads, tokens) */
 int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int nargs, const uint32_t groups[3]);
 
 /* ---- synchronisation and introspection (idle, flush, info: src/backend.js:119-120) ---- */

@@ -1085,6 +1085,28 @@ __global__ void k_gdn_gates(Grid g, FB Alpha, FB Beta, FB A, FB Dt, FB Decay, FB
     Strength.set(i, ref_sigmoid(Beta.get(i, err)), err);
 }
 
+// strata_gdn_gates_fused (no counterpart in the reference): the delta-rule layer's alpha and beta
+// projections of each token (strata_project: rows h of AlphaW and BetaW dotted with the token's
+// row of X, the reference's 64-lane order and tree) and then strata_gdn_gates, in one launch, each
+// value by the same operations in the same order. Block (h, t): warp 0 forms alpha, warp 1 beta,
+// thread 0 the gates. The host checks that every row read lies inside its buffer.
+__global__ void __launch_bounds__(64) k_gdn_gates_fused(FB X, FB AlphaW, FB BetaW, FB A, FB Dt, FB Decay, FB Strength, int width, int heads) {
+    dep_enter();
+    __shared__ float ab[2];
+    const int h = blockIdx.x, t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *w = (warp == 0 ? AlphaW.p : BetaW.p) + (long long)h * width;
+    const float r = lane_dot(w, X.p + (long long)t * width, width, lane);
+    if (lane == 0) ab[warp] = r;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const long long i = (long long)t * heads + h;
+        const float x = __fadd_rn(ab[0], Dt.p[h]);
+        const float sp = x > 20.0f ? x : log_f(__fadd_rn(1.0f, ref_expf(x)));
+        Decay.p[i] = ref_expf(__fmul_rn(A.p[h], sp));
+        Strength.p[i] = ref_sigmoid(ab[1]);
+    }
+}
+
 // kernels/strata.cu:304-313 and :432-444: the gated delta rule. State is [dim_k][valueHeads][dim_v];
 // thread jh owns column jh of every key row, so each of its dim loads is one coalesced row.
 // Value head h reads key head h % keyHeads.
@@ -1599,6 +1621,15 @@ cudaError_t L_gdn_seqs(const KArg *a, const unsigned g[3], cudaStream_t s, unsig
     }
     return cudaGetLastError();
 }
+cudaError_t L_gdn_gates_fused(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
+    const long long width = a[7].i, heads = a[8].i, tokens = a[9].i;
+    if (width < 1 || heads < 1 || tokens < 1 || tokens > 65535 || a[0].len < tokens * width || a[1].len < heads * width ||
+        a[2].len < heads * width || a[3].len < heads || a[4].len < heads || a[5].len < tokens * heads || a[6].len < tokens * heads)
+        return cudaErrorInvalidValue;
+    launch_k(tokens == 1, k_gdn_gates_fused, dim3((unsigned)heads, (unsigned)tokens), 64, 0, s, F(0), F(1), F(2), F(3), F(4), F(5), F(6),
+             (int)width, (int)heads);
+    return cudaGetLastError();
+}
 cudaError_t L_argmax_rows(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
     launch_k(true, k_argmax, (unsigned)a[3].i, kArgmaxThreads, 0, s, F(0), I(1), a[2].i, err);
     return cudaGetLastError();
@@ -1661,6 +1692,8 @@ const KernelSpec kEngineKernels[] = {
     {"strata_conv_seqs", "History:f X:f W:f Y:f channels:I taps:I dilation:I activation:I tokens:I", L_conv_seqs},
     {"strata_gdn_seqs", "State:f Q:f K:f V:f Decay:f Beta:f Y:f dim:I keyHeads:I valueHeads:I tokens:I", L_gdn_seqs},
     {"strata_argmax_rows", "Logits:f Tokens:i count:I rows:I", L_argmax_rows},
+    // the delta-rule gate inputs in one launch (no reference counterpart)
+    {"strata_gdn_gates_fused", "X:f AlphaW:f BetaW:f A:f Dt:f Decay:f Strength:f width:I heads:I tokens:I", L_gdn_gates_fused},
 };
 const int kNumEngineKernels = sizeof(kEngineKernels) / sizeof(kEngineKernels[0]);
 

@@ -53,6 +53,27 @@ def _f32(x: float) -> float:
     return float(np.float32(x))
 
 
+def gdn_gates(o, b, g, p: str, x, tokens: int):
+    """The delta-rule layer's decay and strength of `tokens` tokens (src/engine.js's alpha and beta
+    projections, then strata_gdn_gates / strata_gdn_gates_batch). On the CUDA backend the three
+    dispatches run as one, strata_gdn_gates_fused, with the same values."""
+    heads = g["valueHeads"]
+    decay, strength = o.alloc(tokens * heads), o.alloc(tokens * heads)
+    if getattr(b, "kind", None) == "cuda":
+        b.run("strata_gdn_gates_fused", dict(X=x, AlphaW=o.weight(p + "ssm_alpha.weight"), BetaW=o.weight(p + "ssm_beta.weight"),
+                                             A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay, Strength=strength,
+                                             width=g["width"], heads=heads, tokens=tokens), [heads, tokens, 1])
+        return decay, strength
+    alpha, beta = o.mat(p + "ssm_alpha.weight", x, tokens), o.mat(p + "ssm_beta.weight", x, tokens)
+    if tokens == 1:
+        b.run("strata_gdn_gates", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
+                                       Strength=strength, heads=heads), grid(heads))
+    else:
+        b.run("strata_gdn_gates_batch", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
+                                             Strength=strength, heads=heads, tokens=tokens), grid(tokens * heads))
+    return decay, strength
+
+
 class Ops:
     """src/ops.js:5-126 with whole-model residency."""
 
@@ -412,10 +433,7 @@ class StrataEngine:
             qr, kr, v = o.slice(convolved, qk), o.slice(convolved, qk, 1, qk, qk), o.slice(convolved, vn, 1, vn, 2 * qk)
             q = o.norm(qr, qr, g["ssmDim"], g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
             k = o.norm(kr, kr, g["ssmDim"], g["keyHeads"], 1, 1)
-        alpha, beta = o.mat(p + "ssm_alpha.weight", x), o.mat(p + "ssm_beta.weight", x)
-        decay, strength = o.alloc(g["valueHeads"]), o.alloc(g["valueHeads"])
-        b.run("strata_gdn_gates", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
-                                       Strength=strength, heads=g["valueHeads"]), grid(g["valueHeads"]))
+        decay, strength = gdn_gates(o, b, g, p, x, 1)
         y = o.alloc(vn)
         b.run("strata_gdn_step", dict(State=st["state"], Q=q, K=k, V=v, Decay=decay, Beta=strength, Y=y, dim=g["ssmDim"],
                                       keyHeads=g["keyHeads"], valueHeads=g["valueHeads"]), grid(vn))
@@ -816,10 +834,8 @@ class PromptBatch:
         qr, kr, v = o.slice(convolved, qk, n, c), o.slice(convolved, qk, n, c, qk), o.slice(convolved, vn, n, c, 2 * qk)
         q = o.norm(qr, qr, g["ssmDim"], n * g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
         k = o.norm(kr, kr, g["ssmDim"], n * g["keyHeads"], 1, 1)
-        alpha, beta = self.mat(p + "ssm_alpha.weight", x), self.mat(p + "ssm_beta.weight", x)
-        decay, strength, y = o.alloc(n * g["valueHeads"]), o.alloc(n * g["valueHeads"]), o.alloc(n * vn)
-        b.run("strata_gdn_gates_batch", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
-                                             Strength=strength, heads=g["valueHeads"], tokens=n), grid(n * g["valueHeads"]))
+        decay, strength = gdn_gates(o, b, g, p, x, n)
+        y = o.alloc(n * vn)
         b.run("strata_gdn_batch", dict(State=st["state"], Q=q, K=k, V=v, Decay=decay, Beta=strength, Y=y, dim=g["ssmDim"],
                                        keyHeads=g["keyHeads"], valueHeads=g["valueHeads"], tokens=n), grid(vn))
         z = self.mat(p + "attn_gate.weight", x)
@@ -1044,10 +1060,8 @@ class SequenceBatch(PromptBatch):
         qr, kr, v = o.slice(convolved, qk, n, c), o.slice(convolved, qk, n, c, qk), o.slice(convolved, vn, n, c, 2 * qk)
         q = o.norm(qr, qr, g["ssmDim"], n * g["keyHeads"], 1, 1, 1 / math.sqrt(g["ssmDim"]))
         k = o.norm(kr, kr, g["ssmDim"], n * g["keyHeads"], 1, 1)
-        alpha, beta = self.mat(p + "ssm_alpha.weight", x), self.mat(p + "ssm_beta.weight", x)
-        decay, strength, y = o.alloc(n * g["valueHeads"]), o.alloc(n * g["valueHeads"]), o.alloc(n * vn)
-        b.run("strata_gdn_gates_batch", dict(Alpha=alpha, Beta=beta, A=o.vector(p + "ssm_a"), Dt=o.vector(p + "ssm_dt.bias"), Decay=decay,
-                                             Strength=strength, heads=g["valueHeads"], tokens=n), grid(n * g["valueHeads"]))
+        decay, strength = gdn_gates(o, b, g, p, x, n)
+        y = o.alloc(n * vn)
         b.run("strata_gdn_seqs", dict(State=st["state"], Q=q, K=k, V=v, Decay=decay, Beta=strength, Y=y, dim=g["ssmDim"],
                                       keyHeads=g["keyHeads"], valueHeads=g["valueHeads"], tokens=n), grid(n * vn))
         z = self.mat(p + "attn_gate.weight", x)

@@ -51,3 +51,33 @@ def test_gdn_prep_matches_six_dispatches(b, hd, kh, vh):
                                   epsilon=1e-6), [1, 1, 1])
     for ref, got in ((q1, q2), (k1, k2), (v1, v2), (H1, H2)):
         assert np.array_equal(bits(b.read(ref)), bits(b.read(got)))
+
+
+@pytest.mark.parametrize("width,heads,tokens", [(2048, 32, 1), (2048, 32, 64), (96, 4, 5), (2560, 48, 3)])
+def test_gdn_gates_fused_matches_three_dispatches(b, width, heads, tokens):
+    """strata_gdn_gates_fused against the alpha and beta projections (strata_project) followed by
+    strata_gdn_gates (one token) or strata_gdn_gates_batch: decay and strength bit-identical,
+    including softplus inputs past its cut-over at 20."""
+    rng = np.random.default_rng(width + heads + tokens)
+    x = rng.standard_normal(tokens * width).astype(np.float32)
+    aw = (rng.standard_normal(heads * width) / math.sqrt(width)).astype(np.float32)
+    bw = (rng.standard_normal(heads * width) / math.sqrt(width)).astype(np.float32)
+    a = (-np.abs(rng.standard_normal(heads))).astype(np.float32)
+    dt = rng.standard_normal(heads).astype(np.float32)
+    dt[0] = 25.0  # alpha + dt above 20: softplus passes it through
+    X, AW, BW, A, DT = (b.alloc(v) for v in (x, aw, bw, a, dt))
+    alpha, beta = b.alloc(tokens * heads), b.alloc(tokens * heads)
+    for W, out in ((AW, alpha), (BW, beta)):
+        b.run("strata_project", dict(X=X, W=W, Y=out, cols=width, rows=heads, tokens=tokens, outputStride=heads, outputOffset=0),
+              [heads, tokens, 1])
+    d1, s1 = b.alloc(tokens * heads), b.alloc(tokens * heads)
+    if tokens == 1:
+        b.run("strata_gdn_gates", dict(Alpha=alpha, Beta=beta, A=A, Dt=DT, Decay=d1, Strength=s1, heads=heads), grid(heads))
+    else:
+        b.run("strata_gdn_gates_batch", dict(Alpha=alpha, Beta=beta, A=A, Dt=DT, Decay=d1, Strength=s1, heads=heads, tokens=tokens),
+              grid(tokens * heads))
+    d2, s2 = b.alloc(tokens * heads), b.alloc(tokens * heads)
+    b.run("strata_gdn_gates_fused", dict(X=X, AlphaW=AW, BetaW=BW, A=A, Dt=DT, Decay=d2, Strength=s2, width=width, heads=heads,
+                                         tokens=tokens), [heads, tokens, 1])
+    assert np.array_equal(bits(b.read(d1)), bits(b.read(d2)))
+    assert np.array_equal(bits(b.read(s1)), bits(b.read(s2)))
