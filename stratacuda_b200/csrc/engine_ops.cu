@@ -1088,15 +1088,30 @@ __global__ void k_gdn_gates(Grid g, FB Alpha, FB Beta, FB A, FB Dt, FB Decay, FB
 // strata_gdn_gates_fused (no counterpart in the reference): the delta-rule layer's alpha and beta
 // projections of each token (strata_project: rows h of AlphaW and BetaW dotted with the token's
 // row of X, the reference's 64-lane order and tree) and then strata_gdn_gates, in one launch, each
-// value by the same operations in the same order. Block (h, t): warp 0 forms alpha, warp 1 beta,
-// thread 0 the gates. The host checks that every row read lies inside its buffer.
-__global__ void __launch_bounds__(64) k_gdn_gates_fused(FB X, FB AlphaW, FB BetaW, FB A, FB Dt, FB Decay, FB Strength, int width, int heads) {
-    dep_enter();
-    __shared__ float ab[2];
+// value by the same operations in the same order. Block (h, t) stages the two weight rows (L2
+// prefetch before the wait on the previous kernel) and the token's input row in shared memory
+// with 16-byte loads; warp 0 forms alpha, warp 1 beta, thread 0 the gates. The host checks that
+// every row read lies inside its buffer.
+constexpr int kGatesThreads = 128;
+__global__ void __launch_bounds__(kGatesThreads) k_gdn_gates_fused(FB X, FB AlphaW, FB BetaW, FB A, FB Dt, FB Decay, FB Strength, int width,
+                                                                   int heads) {
     const int h = blockIdx.x, t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float *w = (warp == 0 ? AlphaW.p : BetaW.p) + (long long)h * width;
-    const float r = lane_dot(w, X.p + (long long)t * width, width, lane);
-    if (lane == 0) ab[warp] = r;
+    const float *aw = AlphaW.p + (long long)h * width, *bw = BetaW.p + (long long)h * width;
+    if (threadIdx.x == 0) {  // weights: no kernel writes them
+        prefetch_l2(aw, (unsigned long long)width * 4);
+        prefetch_l2(bw, (unsigned long long)width * 4);
+    }
+    dep_enter();
+    extern __shared__ __align__(16) float gates_smem[];  // [3][width]: alpha row, beta row, input row
+    __shared__ float ab[2];
+    stage_row(gates_smem, aw, width);
+    stage_row(gates_smem + width, bw, width);
+    stage_row(gates_smem + 2 * width, X.p + (long long)t * width, width);
+    __syncthreads();
+    if (warp < 2) {
+        const float r = lane_dot(gates_smem + warp * width, gates_smem + 2 * width, width, lane);
+        if (lane == 0) ab[warp] = r;
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
         const long long i = (long long)t * heads + h;
@@ -1626,8 +1641,12 @@ cudaError_t L_gdn_gates_fused(const KArg *a, const unsigned g[3], cudaStream_t s
     if (width < 1 || heads < 1 || tokens < 1 || tokens > 65535 || a[0].len < tokens * width || a[1].len < heads * width ||
         a[2].len < heads * width || a[3].len < heads || a[4].len < heads || a[5].len < tokens * heads || a[6].len < tokens * heads)
         return cudaErrorInvalidValue;
-    launch_k(tokens == 1, k_gdn_gates_fused, dim3((unsigned)heads, (unsigned)tokens), 64, 0, s, F(0), F(1), F(2), F(3), F(4), F(5), F(6),
-             (int)width, (int)heads);
+    const size_t bytes = (size_t)width * 12;  // the two weight rows and the input row
+    if (bytes > 200 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(k_gdn_gates_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return e;
+    launch_k(tokens == 1, k_gdn_gates_fused, dim3((unsigned)heads, (unsigned)tokens), kGatesThreads, bytes, s, F(0), F(1), F(2), F(3), F(4),
+             F(5), F(6), (int)width, (int)heads);
     return cudaGetLastError();
 }
 cudaError_t L_argmax_rows(const KArg *a, const unsigned g[3], cudaStream_t s, unsigned *err) {
