@@ -125,9 +125,14 @@ int strata_buffer_info(strata_ctx *ctx, strata_buf buf, uint64_t *length, int *t
  *   strata_argmax_rows    (Logits, Tokens, count, rows)                             [strata_argmax per row]
  * A position outside [0, cells) is reported as an index error, never written.
  *
- * One more runs the delta-rule layer's gate inputs (src/engine.js's alpha and beta projections,
- * then strata_gdn_gates; src/prefill.js's batch forms) in one launch, with the same values:
- *   strata_gdn_gates_fused (X, AlphaW, BetaW, A, Dt, Decay, Strength, width, heads, tokens) */
+ * Two more run parts of the delta-rule layer in one launch each, with the same values as the
+ * dispatches they replace:
+ *   strata_gdn_prep (History, X, W, Q, K, V, keyDim, valueDim, headDim, qScale, epsilon): one
+ *     token's strata_conv (4 taps, dilation 1, SiLU) over the [q | k | v] projection, the three
+ *     strata_slice and the two strata_norm mode 1 (q heads times qScale, k heads);
+ *   strata_gdn_gates_fused (X, AlphaW, BetaW, A, Dt, Decay, Strength, width, heads, tokens): the
+ *     alpha and beta projections of each token, then strata_gdn_gates (src/engine.js; the batch
+ *     forms of src/prefill.js for tokens > 1). */
 int strata_run(strata_ctx *ctx, const char *name, const strata_arg *args, int nargs, const uint32_t groups[3]);
 
 /* ---- synchronisation and introspection (idle, flush, info: src/backend.js:119-120) ---- */

@@ -40,3 +40,18 @@ def test_null_context_is_rejected():
     assert lib.strata_idle(None) == L.ERR_RANGE
     assert lib.strata_alloc(None, 4, 0, 1, None) == L.ERR_RANGE
     assert lib.strata_destroy(None) == L.OK
+
+
+def test_every_by_name_entry_is_documented():
+    """Every name strata_run serves is either one of the reference's kernel entries (the oracle's
+    signature table, kernels/strata.cu) or documented in include/strata_cuda.h as an entry with no
+    reference counterpart."""
+    from oracle.oracle import SIGNATURES
+    header = (ROOT / "include" / "strata_cuda.h").read_text()
+    served = set()
+    for src in ("compat.cu", "engine_ops.cu"):
+        text = (ROOT / "stratacuda_b200" / "csrc" / src).read_text()
+        served |= set(re.findall(r'^\s*\{"(strata_\w+)",', text, re.M))
+    assert len(served) >= 49
+    undocumented = sorted(n for n in served if n not in SIGNATURES and n not in header)
+    assert not undocumented, undocumented
